@@ -1,0 +1,327 @@
+"""Throughput benchmark: batched streaming ASR (encoder chunk step + greedy RNNT) on B200s.
+
+Workload (BASELINE config #4): 256 independent streams per GPU at 560 ms latency, 30 s of seeded
+synthetic audio each (three 100->4000 Hz chirps + noise, random 200-600 ms pauses, per-stream
+seed), a random language prompt per stream among 128, full Nemotron-ASR-streaming-0.6B shape
+with random-init bf16 weights (the checkpoint is not used). One step = one 560 ms chunk of every
+stream: subsampling, 24 conformer blocks, prompt, joint projection and the greedy decode.
+
+  value : audio-sec/sec over all GPUs with the log-mel features already in HBM (CUDA-event time
+          on the engine's stream, max over ranks);
+  e2e   : the same metric through the public API (nemoasr_batch_feed) from host audio: host
+          resampling/mel, H2D window copies and D2H token reads inside the timed region.
+
+Streams shard across GPUs with no collective (one process per GPU); torch.distributed is used
+only for the start barrier and the max-over-ranks of the timings.
+
+  python bench.py [--gpus N --steps K --warmup W] [--impl reference]
+"""
+import argparse
+import json
+import os
+import subprocess
+import sys
+import tempfile
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "nemo-c_b200"))
+sys.path.insert(0, os.path.join(ROOT, "tests"))
+
+METRIC = "audio-sec/sec (RTFx) at N streams on 1/2/4/8 B200"
+UNIT = "audio-sec/sec"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--streams", type=int, default=256)
+    ap.add_argument("--latency", type=int, default=560)
+    ap.add_argument("--seconds", type=float, default=30.0)
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--single", action="store_true", help="also time the single-stream config #1 chunk latency")
+    return ap.parse_args()
+
+
+def config_dict(a, world):
+    return {"workload": f"BASELINE config #4: {a.streams} streams/GPU, {a.latency} ms chunks, {a.seconds:g} s synthetic audio per stream",
+            "streams_per_gpu": a.streams, "latency_ms": a.latency, "audio_s_per_stream": a.seconds, "parallelism": f"streams sharded over {world} GPU(s), no collective",
+            "l2": "inputs > L2: 1.2 GB of weights streamed per step (126 MB L2)", "model": "nemotron-asr-streaming-0.6b shape, random-init bf16"}
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+
+    Q = "clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap"
+
+    def __init__(self, index):
+        self.index, self.lines, self.p = index, [], None
+
+    def start(self):
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "-i", str(self.index), "--format=csv,noheader,nounits", "-lms", "200"],
+                                      stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            threading.Thread(target=lambda: [self.lines.append(l.strip()) for l in self.p.stdout], daemon=True).start()
+        except OSError:
+            self.p = None
+
+    def stop(self):
+        if self.p:
+            self.p.terminate()
+            try:
+                self.p.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.p.kill()
+        rows = []
+        for l in self.lines:
+            f = [x.strip() for x in l.split(",")]
+            if len(f) >= 8:
+                try:
+                    rows.append((float(f[0]), float(f[1]), f[4:8]))
+                except ValueError:
+                    pass
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unavailable"]}
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for _, _, fl in rows for i, v in enumerate(fl) if v.lower() == "active"})
+        return {"sm_mhz": float(np.median([r[0] for r in rows])), "sm_max_mhz": max(r[1] for r in rows), "reasons": reasons, "samples": len(rows)}
+
+
+def make_inputs(nb, a, rank):
+    """Per-stream audio (host) and its log-mel features, generated in parallel threads."""
+    from concurrent.futures import ThreadPoolExecutor
+    n = int(round(a.seconds * 16000))
+    audio = np.zeros((a.streams, n), np.float32)
+    seeds = [100000 * (rank + 1) + s for s in range(a.streams)]
+    with ThreadPoolExecutor(min(32, os.cpu_count() or 8)) as ex:
+        for s, x in enumerate(ex.map(lambda sd: nb.synth_audio(sd, 16000, n=n, pauses=True), seeds)):
+            audio[s] = x
+        mels = list(ex.map(lambda s: nb.mel(audio[s]), range(a.streams)))
+    T = min(m.shape[0] for m in mels)
+    mel = np.stack([m[:T] for m in mels])
+    return audio, mel
+
+
+def languages(a, rank):
+    rng = np.random.default_rng(777 + rank)
+    keys = ["auto", "en-US"] + [f"lang{i}" for i in range(2, 128)]
+    return [keys[i] for i in rng.integers(0, 128, size=a.streams)]
+
+
+def dominant_gemm(nb, torch, a, B, c):
+    """CUDA-event time of the FF-in GEMM of one step (M = streams x rows, N = 4096, K = 1024),
+    launched through the C-ABI on a torch stream, averaged over 20 launches of 24 distinct weights
+    (more than L2 holds)."""
+    import ctypes as C
+    M, N, K = B * c, 4096, 1024
+    A = torch.randn(M, K, device="cuda", dtype=torch.float32)
+    Ws = [torch.randint(0, 1 << 15, (N, K), device="cuda", dtype=torch.int16) & 0x3C7F for _ in range(24)]
+    Cm = torch.empty(M, N, device="cuda", dtype=torch.float32)
+    args = nb.GemmArgs()
+    args.A, args.lda, args.a_fmt = A.data_ptr(), K, 0
+    args.ldw, args.C, args.ldc, args.M, args.N, args.K, args.act, args.alpha = K, Cm.data_ptr(), N, M, N, K, 1, 1.0
+    st = torch.cuda.current_stream()
+    for w in Ws[:3]:
+        args.W = w.data_ptr()
+        nb.check(nb.api().nemo_gemm(C.byref(args), C.c_void_p(st.cuda_stream)))
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record(st)
+    for i in range(20):
+        args.W = Ws[i % 24].data_ptr()
+        nb.check(nb.api().nemo_gemm(C.byref(args), C.c_void_p(st.cuda_stream)))
+    e1.record(st)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / 20
+    return ms, 2.0 * M * N * K
+
+
+def cpu_baseline(nb, a, audio0, budget_s=25.0):
+    """The oracle (plain-C fp32 restatement, OpenMP) on one stream of this workload."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as orc
+    with tempfile.TemporaryDirectory() as d:
+        nb.synth_write(d, nb.synth_default())
+        m = orc.Model(d)
+        secs = 4.0
+        t0 = time.time()
+        orc.run_stream(m, audio0[: int(secs * 16000)], 16000, a.latency)
+        dt = time.time() - t0
+        more = min(a.seconds, max(secs, secs * budget_s / max(dt, 1e-3) * 0.5))
+        if more > secs:
+            t0 = time.time()
+            orc.run_stream(m, audio0[: int(more * 16000)], 16000, a.latency)
+            dt, secs = time.time() - t0, more
+        del m
+    return {"value": secs / dt, "unit": UNIT, "cores": orc.num_threads(), "kind": "port",
+            "sample": f"1 stream x {secs:.1f} s of the config #4 audio through the oracle (full model, {a.latency} ms chunks)"}
+
+
+def run_reference(a):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    import nemoasr_b200 as nb
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as orc
+    audio = nb.synth_audio(100001, 16000, seconds=max(a.seconds, (a.warmup + a.steps + 2) * a.latency / 1000))
+    block = a.latency * 16
+    times = []
+    with tempfile.TemporaryDirectory() as d:
+        nb.synth_write(d, nb.synth_default())
+        if orc.ref_available():
+            import ctypes as C
+            R = orc.ref()
+            err = C.create_string_buffer(512)
+            s = R.nemoasr_open(d.encode(), b"auto", a.latency, 16000, err, 512)
+            if not s:
+                raise RuntimeError(err.value.decode())
+            kind = "reference"
+            for i in range(a.warmup + a.steps):
+                x = np.ascontiguousarray(audio[i * block:(i + 1) * block])
+                t0 = time.perf_counter()
+                t = R.nemoasr_feed(s, x.ctypes.data_as(orc.f32p), x.size, 0, err, 512)
+                dt = time.perf_counter() - t0
+                if t:
+                    R.nemoasr_free(t)
+                if i >= a.warmup:
+                    times.append(dt)
+            R.nemoasr_close(s)
+        else:
+            kind = "port"
+            m = orc.Model(d)
+            sess = orc.Session(m, a.latency, 16000)
+            for i in range(a.warmup + a.steps):
+                t0 = time.perf_counter()
+                sess.feed(audio[i * block:(i + 1) * block])
+                if i >= a.warmup:
+                    times.append(time.perf_counter() - t0)
+            sess.close()
+    # the first timed feeds may include a partial chunk; each feed of one chunk of audio yields one step
+    ms = float(np.mean(times)) * 1000
+    val = (a.latency / 1000) / (ms / 1000)
+    threads = orc.num_threads()
+    line = {"impl": "reference", "metric": METRIC, "value": val, "unit": UNIT, "n_gpus": a.gpus, "steps": a.steps, "warmup": a.warmup,
+            "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": config_dict(a, a.gpus),
+            "cpu_baseline": {"value": val, "unit": UNIT, "cores": threads, "kind": kind,
+                             "sample": f"1 stream, {a.steps} chunks of {a.latency} ms through the reference's own host C (nemoasr_feed) "
+                                       f"with the restated CPU kernels, {threads} threads"},
+            "e2e": {"value": val, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    a = parse()
+    if a.impl == "reference":
+        return run_reference(a)
+    a.seconds = max(a.seconds, (a.warmup + a.steps + 3) * a.latency / 1000.0)
+    import torch
+    import nemoasr_b200 as nb
+    rank, world, local = int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=torch.device("cuda", local))
+
+    def barrier():
+        if dist:
+            dist.barrier()
+
+    def max_over_ranks(x):
+        if not dist:
+            return x
+        t = torch.tensor([x], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    launches0 = nb.api().nemo_gpu_launch_count()
+    audio, mel = make_inputs(nb, a, rank)
+    B, T = a.streams, mel.shape[1]
+    chunk_s = a.latency / 1000.0
+    batch = nb.Batch(B, spec=nb.synth_default(), languages=languages(a, rank), latency_ms=a.latency)
+
+    # ---- value: features resident in HBM --------------------------------------------------
+    d_mel = torch.from_numpy(mel).cuda()
+    batch.attach_mel(d_mel.data_ptr(), T * 128, T)
+    for _ in range(a.warmup):
+        batch.step()
+    torch.cuda.synchronize()
+    barrier()
+    clocks = ClockSampler(local)
+    clocks.start()
+    g0, l0 = batch.gpu_ms(), nb.api().nemo_gpu_launch_count()
+    toks = 0
+    for _ in range(a.steps):
+        rc, rows, out = batch.step()
+        if rc != 1 or rows == 0:
+            raise RuntimeError("stream ran out of audio inside the timed region")
+        toks += sum(len(t) for t in out)
+    torch.cuda.synchronize()
+    gpu_ms = batch.gpu_ms() - g0
+    launches = nb.api().nemo_gpu_launch_count() - l0
+    clk = clocks.stop()
+    gpu_ms = max_over_ranks(gpu_ms)
+    value = a.steps * chunk_s * B * world / (gpu_ms / 1000.0)
+
+    # ---- e2e: host audio through nemoasr_batch_feed -----------------------------------------
+    e2e = None
+    if not a.no_e2e:
+        batch.reset()
+        blk = int(a.latency * 16)
+        for i in range(a.warmup + 1):
+            batch.feed(audio[:, i * blk:(i + 1) * blk])
+        torch.cuda.synchronize()
+        barrier()
+        t0 = time.perf_counter()
+        for i in range(a.warmup + 1, a.warmup + 1 + a.steps):
+            batch.feed(audio[:, i * blk:(i + 1) * blk])
+        torch.cuda.synchronize()
+        wall = max_over_ranks(time.perf_counter() - t0)
+        nwin = 16 + a.latency // 10 + 1
+        e2e = {"value": a.steps * chunk_s * B * world / wall, "unit": UNIT,
+               "h2d_bytes_per_step": B * nwin * 128 * 4 + 12,
+               "d2h_bytes_per_step": B * 4 + B * 16 * 10 * 4,
+               "note": "host audio -> host resample/log-mel (OpenMP) -> H2D window -> GPU step -> D2H tokens, wall clock"}
+    batch.close()
+
+    # ---- dominant kernel roofline ------------------------------------------------------------
+    c = a.latency // 80
+    ms, flops = dominant_gemm(nb, torch, a, B, c)
+    peaks = {}
+    try:
+        peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+    except (OSError, ValueError):
+        pass
+    peak = peaks.get("bf16_tflops", 1590.0)
+    ach = flops / (ms / 1e3) / 1e12
+    roof = {"bound": "tensor", "kernel": "nemo_gemm FF-in (M=%d N=4096 K=1024, SiLU)" % (B * c), "achieved": ach, "peak": peak, "unit": "TFLOP/s",
+            "frac": ach / peak, "traffic": None, "peak_source": "MEASURED_PEAKS.json bf16_tflops (burst)" if peaks else "fallback 1.59 PFLOP/s"}
+
+    cpu = None
+    if rank == 0 and world == 1 and not a.no_cpu:
+        cpu = cpu_baseline(nb, a, audio[0])
+
+    if rank == 0:
+        line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": a.steps, "warmup": a.warmup,
+                "ms_per_step": gpu_ms / a.steps, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+                "data": "synthetic (seeded chirps + noise + pauses; random-init bf16 weights of the published shape)",
+                "config": config_dict(a, world), "e2e": e2e, "gpu_launches": int(launches), "tokens_in_timed_region": toks,
+                "roofline": roof, "cpu_baseline": cpu, "clocks": clk}
+        print(json.dumps(line), flush=True)
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

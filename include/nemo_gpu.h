@@ -1,0 +1,109 @@
+/* nemo_gpu: C-ABI of the B200 kernels (sm_100a). Plain pointers and sizes; device pointers
+   unless stated; `stream` is a cudaStream_t (NULL = legacy default stream). Every entry point
+   returns 0 on success or -1 after recording a message retrievable with nemo_gpu_last_error().
+
+   These replace the reference's string-keyed Metal dispatch (src/gpu.h:20-41, src/gpu.m) and the
+   kernel launchers of src/model.h:71-76 plus the direct dispatches in src/encoder.c and
+   src/decoder.c. The math of each entry point is that of the Metal kernel it cites. */
+#ifndef NEMO_GPU_H
+#define NEMO_GPU_H
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum { NEMO_ACT_NONE = 0, NEMO_ACT_SILU = 1, NEMO_ACT_RELU = 2, NEMO_ACT_GLU = 3 };
+enum { NEMO_FMT_F32 = 0, NEMO_FMT_BF16X2 = 1 };
+
+/* C[row(m)][n] (= or +=) alpha * act(sum_k A[m][k] * W[n][k] + bias[g][n]).
+   Replaces k_gemm (src/model.h:71, src/model.c:70-99) and its kernels gemm_bf16 / gemm_spec /
+   gemm_mma (src/kernels.metal:12-208); like k_gemm it picks the kernel by row count:
+   M <= 16 streams the weights through CUDA cores; larger M runs tcgen05 tensor-core tiles.
+   Row mapping (new: lets one launch cover many streams and write into per-stream caches):
+   m -> group g = m / rpg, r = m % rpg; C element at C + g*gstride + (rowoff + r)*ldc + n,
+   bias at bias + g*bias_gstride + n. rowoff is read from device memory (NULL = 0).
+   A formats: NEMO_FMT_F32 (fp32 [M][lda]) or NEMO_FMT_BF16X2 (two bf16 planes, hi at A and
+   lo = A - hi at A + a_plane elements; hi + lo carries 16 mantissa bits). The C output may
+   also be written as NEMO_FMT_BF16X2 planes (c_plane apart) for a following tensor-core GEMM. */
+typedef struct {
+    const void *A;
+    int64_t lda, a_plane;
+    int a_fmt;
+    const uint16_t *W;
+    int64_t ldw;
+    const float *bias;
+    int64_t bias_gstride;
+    void *C;
+    int64_t ldc, c_plane;
+    int c_fmt;
+    int rpg;
+    int64_t gstride;
+    const int *rowoff;
+    const int *dynM; /* if non-NULL: rows actually processed = min(M, *dynM), read on the device */
+    int M, N, K;
+    int act, accumulate;
+    float alpha;
+} nemo_gemm_args_t;
+int nemo_gemm(const nemo_gemm_args_t *a, void *stream);
+/* Force a kernel family for tests and the kernel sweep: 0 = by row count (default),
+   1 = CUDA-core weight streaming, 2 = tcgen05 tensor cores. */
+int nemo_gemm_forced(const nemo_gemm_args_t *a, int kind, void *stream);
+
+/* Row LayerNorm. Replaces k_layernorm (src/model.h:73; kernel src/kernels.metal:258-288).
+   Y may be written as NEMO_FMT_BF16X2 planes (y_plane apart) for a tensor-core consumer. */
+int nemo_layernorm(const float *X, const float *g, const float *b, void *Y, int y_fmt, int64_t y_plane,
+                   int M, int D, float eps, void *stream);
+/* Y1 = LN(X; g1, b1), Y2 = LN(Y1; g2, b2). Replaces k_layernorm2 (src/model.h:72; kernel
+   src/kernels.metal:212-255). Y1 is fp32; Y2 may be BF16X2 planes. */
+int nemo_layernorm2(const float *X, const float *g1, const float *b1, const float *g2, const float *b2,
+                    float *Y1, void *Y2, int y2_fmt, int64_t y2_plane, int M, int D, float eps, void *stream);
+
+/* Relative-position attention over a K/V cache window for `streams` independent streams.
+   Replaces the attention_rel dispatch (src/encoder.c:161-165; kernel src/kernels.metal:293-348).
+   Per stream s: queries are rows [*pos, *pos + c) of Q + s*q_sstride ([.][ldq]); keys/values
+   rows [*pos - *cache_len, *pos + c) of K + s*kv_sstride / V + s*kv_sstride ([.][ldk]), so
+   L = *cache_len + c (<= Lmax); pos and cache_len are read from device ints. P: [2*Lmax-1][D] position table. Output
+   O + s*o_sstride ([c][D]) as fp32 or BF16X2 planes (o_plane apart). */
+int nemo_attention_rel(const float *Q, int64_t ldq, int64_t q_sstride, const float *K, const float *V, int64_t ldk,
+                       int64_t kv_sstride, const int *pos, const int *cache_len, const float *P, const float *bias_u,
+                       const float *bias_v, void *O, int o_fmt, int64_t o_plane, int64_t o_sstride,
+                       int streams, int c, int Lmax, int H, int dh, int D, float scale, void *stream);
+
+/* Causal depthwise conv (taps rows, history in place) + LayerNorm + SiLU, `streams` streams.
+   Replaces the dwconv_ln_silu dispatch (src/encoder.c:172-174; kernel src/kernels.metal:361-409).
+   din rows for stream s start at din + s*din_sstride + (*pos - (taps-1))*D. */
+int nemo_dwconv_ln_silu(const float *din, int64_t din_sstride, const int *pos, const float *W, const float *g,
+                        const float *b, void *Y, int y_fmt, int64_t y_plane, int streams, int c, int D, int taps,
+                        float eps, void *stream);
+
+/* 1 -> C channel 3x3 stride-2 conv + ReLU, causal padding, `streams` windows of [T][F] each
+   (x_sstride apart). Replaces conv2d_c1_s2_relu (src/kernels.metal:413-432). Y: [s][T1][F1][C]. */
+int nemo_conv2d_c1_s2_relu(const float *X, int64_t x_sstride, const float *W, const float *bias, float *Y,
+                           int streams, int T, int F, int T1, int F1, int C, void *stream);
+/* Depthwise 3x3 stride-2 conv. Replaces dwconv2d_s2 (src/kernels.metal:435-454). X [s][T][F][C]. */
+int nemo_dwconv2d_s2(const float *X, const float *W, const float *bias, float *Y, int streams, int T, int F,
+                     int T1, int F1, int C, void *stream);
+/* Gather rows [*lo, *lo + c) of each stream's [T][F][C] map and flatten them channel-major into
+   [s*c][C*F] fp32 (flatten_cf, src/kernels.metal:457-462, restricted to the rows the chunk keeps
+   at src/encoder.c:258). */
+int nemo_flatten_rows(const float *X, float *Y, const int *lo, int streams, int T, int F, int C, int c, void *stream);
+
+/* LSTM cell on gates [rows][4H] (i, f, g, o). Replaces lstm_cell (src/kernels.metal:475-486). */
+int nemo_lstm_cell(const float *gates, const float *c_in, float *c_out, float *h_out, int rows, int H, void *stream);
+/* Joint + argmax per row: logits = W . relu(enc[r] + pred[r]) + b (W bf16 [V][H]); ties ->
+   lowest index. out_idx[r], out_val[r]. Replaces joint_partial + argmax_reduce
+   (src/kernels.metal:490-550, dispatched at src/decoder.c:81-90). enc row r at enc + r*enc_ld,
+   pred row r at pred + r*pred_ld (pred_ld 0 = one shared prediction vector). */
+int nemo_joint_argmax(const float *enc, int64_t enc_ld, const float *pred, int64_t pred_ld, const uint16_t *W,
+                      const float *bias, int V, int H, int rows, int *out_idx, float *out_val, void *stream);
+
+const char *nemo_gpu_last_error(void);
+/* Number of CUDA kernels this library has launched (directly or by graph launch) since load. */
+uint64_t nemo_gpu_launch_count(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

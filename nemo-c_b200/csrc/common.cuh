@@ -1,0 +1,71 @@
+// Shared device helpers for the sm_100a kernels.
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include "../../include/nemo_gpu.h"
+
+namespace nb {
+
+__device__ __forceinline__ float bf16lo(uint32_t w) { return __uint_as_float(w << 16); }
+__device__ __forceinline__ float bf16hi(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
+__device__ __forceinline__ float bf2f(uint16_t v) { return __uint_as_float((uint32_t)v << 16); }
+
+// round-to-nearest-even fp32 -> bf16 bits (inputs here are finite)
+__device__ __forceinline__ uint16_t f2bf(float f) {
+    uint32_t u = __float_as_uint(f);
+    u += 0x7fffu + ((u >> 16) & 1u);
+    return (uint16_t)(u >> 16);
+}
+
+// Metal-equivalent activations (src/kernels.metal:6-7), IEEE expf / division
+__device__ __forceinline__ float sigmoid_f(float v) { return 1.0f / (1.0f + expf(-v)); }
+__device__ __forceinline__ float silu_f(float v) { return v / (1.0f + expf(-v)); }
+
+// Store one activation either as fp32 or as a bf16 hi/lo pair (hi + lo == v to ~2^-17 relative).
+__device__ __forceinline__ void store_act(void *base, int fmt, int64_t plane, int64_t idx, float v) {
+    if (fmt == NEMO_FMT_F32) {
+        ((float *)base)[idx] = v;
+    } else {
+        const uint16_t hi = f2bf(v);
+        const uint16_t lo = f2bf(v - bf2f(hi));
+        ((uint16_t *)base)[idx] = hi;
+        ((uint16_t *)base)[idx + plane] = lo;
+    }
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+// Block-wide sum for blockDim.x == NT (multiple of 32); red must hold NT/32 floats.
+template <int NT>
+__device__ __forceinline__ float block_sum(float v, float *red) {
+    v = warp_sum(v);
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    __syncthreads();
+    if (lane == 0) red[w] = v;
+    __syncthreads();
+    float t = 0.0f;
+#pragma unroll
+    for (int i = 0; i < NT / 32; ++i) t += red[i];
+    return t;
+}
+
+// Wait for the previous kernel in the stream when launched with programmatic dependent launch
+// (a no-op otherwise), and allow the next one to start its prologue.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" :::); }
+
+}  // namespace nb
+
+// host side
+extern "C" int nb_set_error(const char *fmt, ...);
+extern "C" void nb_count_launches(uint64_t n);
+int nb_check_launch(const char *what);

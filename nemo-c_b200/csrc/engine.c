@@ -1,0 +1,480 @@
+/* Streaming engine: host bookkeeping of src/encoder.c / src/decoder.c for B lockstep streams,
+   device buffers laid out [stream][row][...], and the per-chunk launch sequence. */
+#include "engine.h"
+#include "engine_dev.h"
+#include <cuda_runtime_api.h>
+#include <math.h>
+#include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
+
+#define CK(x) do { cudaError_t e_ = (x); if (e_ != cudaSuccess) { snprintf(err, errlen, "%s: %s", #x, cudaGetErrorString(e_)); goto fail; } } while (0)
+#define KL(x) do { if ((x) != 0) { snprintf(err, errlen, "%s", nemo_gpu_last_error()); return -1; } } while (0)
+
+struct nb_engine {
+    nb_model_t *m;
+    int B, right, chunk_frames, chunk_mel, cmax, left, conv_left, Lmax, cap_rows, nwin_max;
+    int fmt_layer, fmt_conv;   /* activation format feeding the GEMMs (fp32 or bf16 hi/lo planes) */
+    cudaStream_t st;
+    /* host bookkeeping (identical for every stream: they are fed in lockstep) */
+    float **pending;
+    size_t pending_n, pending_cap;
+    float *mel_cache;          /* [B][16][128] */
+    int mel_cache_n;
+    size_t consumed, emitted;
+    int closed, pos, cache_len;
+    /* optional device-resident mel source [B][sstride] (frames of 128 floats), replacing the
+       host queue: the window of every step is then a device-to-device 2D copy */
+    const float *dev_mel;
+    int64_t dev_mel_sstride;
+    size_t dev_mel_frames;
+    /* device */
+    float *d_win, *h_win;      /* [B][nwin_max][128]; h_win pinned */
+    float *c0, *c1, *c2, *c3, *c4, *flat;
+    float *hbuf[2], *xin, *ff, *att, *y, *ph, *prompted, *joint_enc;
+    float *kv, *din;           /* [layers][B][cap_rows][3D] and [layers][B][cap_rows][D] */
+    float *b_eff;              /* [B][PH] */
+    int *d_params, *h_params;  /* pos, cache_len, lo */
+    DecState dec;
+    int *h_cnt, *h_ntok, *h_tokens;
+    int *prompt_idx;
+    /* taps */
+    float *tap_prompted, *tap_joint;
+    size_t tap_cap, tap_rows;
+    int *tap_chunk_rows;
+    size_t tap_chunk_cap, tap_chunks;
+    double enc_ms, dec_ms, gpu_ms;
+    size_t chunks;
+    cudaEvent_t ev0, ev1;
+};
+
+double nb_engine_gpu_ms(const nb_engine_t *e) { return e->gpu_ms; }
+
+static int sub_len(int n) { return n / 2 + 1; }
+
+static void *dalloc(size_t bytes, int *fail) {
+    void *p = NULL;
+    if (*fail) return NULL;
+    if (cudaMalloc(&p, bytes ? bytes : 16) != cudaSuccess) { *fail = 1; return NULL; }
+    cudaMemset(p, 0, bytes ? bytes : 16);
+    return p;
+}
+
+nb_engine_t *nb_engine_create(nb_model_t *m, int B, int right, char *err, size_t errlen) {
+    if (B <= 0) { snprintf(err, errlen, "stream count must be positive"); return NULL; }
+    nb_engine_t *e = calloc(1, sizeof *e);
+    const nb_config_t *g = &m->g;
+    e->m = m;
+    e->B = B;
+    e->right = right;
+    e->chunk_frames = right + 1;
+    e->chunk_mel = e->chunk_frames * g->subsampling;
+    e->cmax = e->chunk_frames + 2;                  /* final boundary window (src/encoder.c:45) */
+    if (e->cmax < NB_MIN_CMAX) e->cmax = NB_MIN_CMAX;
+    e->left = g->att_left;
+    e->Lmax = g->Lmax;
+    e->conv_left = g->conv_kernel - 1;
+    e->cap_rows = e->left + NB_EPOCH_CHUNKS * e->cmax; /* src/encoder.c:73 */
+    e->nwin_max = NB_MEL_CACHE + e->chunk_mel + 1;
+    e->fmt_layer = NEMO_FMT_F32;
+    e->fmt_conv = NEMO_FMT_F32;
+    if (e->left + e->cmax > 96) { snprintf(err, errlen, "attention window %d exceeds 96 rows", e->left + e->cmax); free(e); return NULL; }
+    int fail = 0;
+    const size_t D = (size_t)g->d_model, CH = (size_t)g->sub_channels, FF = (size_t)g->d_ff, PH = (size_t)g->pred_hidden;
+    const size_t JH = (size_t)g->joint_hidden, PRH = (size_t)g->prompt_hidden, Bz = (size_t)B, cm = (size_t)e->cmax;
+    const size_t T1 = (size_t)sub_len(e->nwin_max), F1 = 128 / 2 + 1, T2 = T1 / 2 + 1, F2 = F1 / 2 + 1, T3 = T2 / 2 + 1, F3 = F2 / 2 + 1;
+    CK(cudaStreamCreateWithFlags(&e->st, cudaStreamNonBlocking));
+    CK(cudaEventCreate(&e->ev0));
+    CK(cudaEventCreate(&e->ev1));
+    e->d_win = dalloc(Bz * (size_t)e->nwin_max * 128 * 4, &fail);
+    CK(cudaMallocHost((void **)&e->h_win, Bz * (size_t)e->nwin_max * 128 * 4));
+    e->c0 = dalloc(Bz * T1 * F1 * CH * 4, &fail);
+    e->c1 = dalloc(Bz * T2 * F2 * CH * 4, &fail);
+    e->c2 = dalloc(Bz * T2 * F2 * CH * 4, &fail);
+    e->c3 = dalloc(Bz * T3 * F3 * CH * 4, &fail);
+    e->c4 = dalloc(Bz * T3 * F3 * CH * 4, &fail);
+    e->flat = dalloc(Bz * cm * CH * F3 * 4, &fail);
+    e->hbuf[0] = dalloc(Bz * cm * D * 4, &fail);
+    e->hbuf[1] = dalloc(Bz * cm * D * 4, &fail);
+    e->xin = dalloc(Bz * cm * D * 4, &fail);
+    e->ff = dalloc(Bz * cm * FF * 4, &fail);
+    e->att = dalloc(Bz * cm * D * 4, &fail);
+    e->y = dalloc(Bz * cm * D * 4, &fail);
+    e->ph = dalloc(Bz * cm * PRH * 4, &fail);
+    e->prompted = dalloc(Bz * cm * D * 4, &fail);
+    e->joint_enc = dalloc(Bz * cm * JH * 4, &fail);
+    e->kv = dalloc((size_t)g->n_layers * Bz * (size_t)e->cap_rows * 3 * D * 4, &fail);
+    e->din = dalloc((size_t)g->n_layers * Bz * (size_t)e->cap_rows * D * 4, &fail);
+    e->b_eff = dalloc(Bz * PRH * 4, &fail);
+    e->d_params = dalloc(8 * sizeof(int), &fail);
+    CK(cudaMallocHost((void **)&e->h_params, 8 * sizeof(int)));
+    /* decoder state */
+    DecState *d = &e->dec;
+    d->streams = B;
+    d->tok_cap = e->cmax * g->max_symbols;
+    int **ints[] = { &d->t, &d->symbols, &d->active, &d->pred_valid, &d->last_token, &d->ntok, &d->need_idx, &d->erow, &d->idx };
+    for (size_t i = 0; i < sizeof ints / sizeof *ints; ++i) *ints[i] = dalloc(Bz * sizeof(int), &fail);
+    d->tokens = dalloc(Bz * (size_t)d->tok_cap * sizeof(int), &fail);
+    d->cnt = dalloc(8 * sizeof(int), &fail);
+    d->h = dalloc(2 * Bz * PH * 4, &fail);
+    d->c = dalloc(2 * Bz * PH * 4, &fail);
+    d->hp = dalloc(2 * Bz * PH * 4, &fail);
+    d->cp = dalloc(2 * Bz * PH * 4, &fail);
+    d->pred = dalloc(Bz * JH * 4, &fail);
+    d->A0 = dalloc(Bz * 2 * PH * 4, &fail);
+    d->A1 = dalloc(Bz * 2 * PH * 4, &fail);
+    d->gates = dalloc(Bz * 4 * PH * 4, &fail);
+    d->hp1c = dalloc(Bz * PH * 4, &fail);
+    d->predc = dalloc(Bz * JH * 4, &fail);
+    if (fail) { snprintf(err, errlen, "out of device memory for %d streams", B); goto fail; }
+    CK(cudaMallocHost((void **)&e->h_cnt, 8 * sizeof(int)));
+    CK(cudaMallocHost((void **)&e->h_ntok, Bz * sizeof(int)));
+    CK(cudaMallocHost((void **)&e->h_tokens, Bz * (size_t)d->tok_cap * sizeof(int)));
+    e->pending = calloc(Bz, sizeof *e->pending);
+    e->mel_cache = calloc(Bz * NB_MEL_CACHE * 128, sizeof(float));
+    e->prompt_idx = calloc(Bz, sizeof(int));
+    {
+        float *be = malloc(PRH * 4);
+        nb_model_prompt_bias(m, 0, be);
+        for (int s = 0; s < B; ++s) CK(cudaMemcpy(e->b_eff + (size_t)s * PRH, be, PRH * 4, cudaMemcpyHostToDevice));
+        free(be);
+    }
+    if (nb_engine_reset(e, err, errlen)) goto fail;
+    return e;
+fail:
+    nb_engine_destroy(e);
+    return NULL;
+}
+
+void nb_engine_destroy(nb_engine_t *e) {
+    if (!e) return;
+    if (e->st) cudaStreamSynchronize(e->st);
+    float *f[] = { e->d_win, e->c0, e->c1, e->c2, e->c3, e->c4, e->flat, e->hbuf[0], e->hbuf[1], e->xin, e->ff, e->att, e->y, e->ph,
+                   e->prompted, e->joint_enc, e->kv, e->din, e->b_eff, e->dec.h, e->dec.c, e->dec.hp, e->dec.cp, e->dec.pred, e->dec.A0,
+                   e->dec.A1, e->dec.gates, e->dec.hp1c, e->dec.predc };
+    for (size_t i = 0; i < sizeof f / sizeof *f; ++i) if (f[i]) cudaFree(f[i]);
+    int *n[] = { e->d_params, e->dec.t, e->dec.symbols, e->dec.active, e->dec.pred_valid, e->dec.last_token, e->dec.ntok, e->dec.need_idx,
+                 e->dec.erow, e->dec.idx, e->dec.tokens, e->dec.cnt };
+    for (size_t i = 0; i < sizeof n / sizeof *n; ++i) if (n[i]) cudaFree(n[i]);
+    if (e->h_win) cudaFreeHost(e->h_win);
+    if (e->h_params) cudaFreeHost(e->h_params);
+    if (e->h_cnt) cudaFreeHost(e->h_cnt);
+    if (e->h_ntok) cudaFreeHost(e->h_ntok);
+    if (e->h_tokens) cudaFreeHost(e->h_tokens);
+    if (e->st) cudaStreamDestroy(e->st);
+    if (e->ev0) cudaEventDestroy(e->ev0);
+    if (e->ev1) cudaEventDestroy(e->ev1);
+    if (e->pending) for (int s = 0; s < e->B; ++s) free(e->pending[s]);
+    free(e->pending);
+    free(e->mel_cache);
+    free(e->prompt_idx);
+    free(e);
+}
+
+int nb_engine_reset(nb_engine_t *e, char *err, size_t errlen) {
+    e->pending_n = 0;
+    e->dev_mel = NULL;
+    e->dev_mel_frames = 0;
+    e->mel_cache_n = 0;
+    e->consumed = e->emitted = 0;
+    e->closed = 0;
+    e->cache_len = 0;
+    e->pos = e->conv_left;
+    /* conv history rows [0, conv_left) of every layer and stream read as zeros again */
+    const size_t D = (size_t)e->m->g.d_model, rowb = D * 4;
+    for (int l = 0; l < e->m->g.n_layers; ++l)
+        for (int s = 0; s < e->B; ++s) {
+            float *base = e->din + ((size_t)l * e->B + s) * (size_t)e->cap_rows * D;
+            if (cudaMemsetAsync(base, 0, (size_t)e->conv_left * rowb, e->st) != cudaSuccess) { snprintf(err, errlen, "reset failed"); return -1; }
+        }
+    if (nb_dec_reset(&e->dec, e->m->g.pred_hidden, e->m->g.blank_id, e->st)) { snprintf(err, errlen, "%s", nemo_gpu_last_error()); return -1; }
+    if (cudaStreamSynchronize(e->st) != cudaSuccess) { snprintf(err, errlen, "reset: %s", cudaGetErrorString(cudaGetLastError())); return -1; }
+    return 0;
+}
+
+int nb_engine_right(const nb_engine_t *e) { return e->right; }
+int nb_engine_streams(const nb_engine_t *e) { return e->B; }
+
+int nb_engine_set_prompt(nb_engine_t *e, int s, int idx, char *err, size_t errlen) {
+    if (s < 0 || s >= e->B || idx < 0 || idx >= e->m->g.num_prompts) { snprintf(err, errlen, "bad stream %d / prompt %d", s, idx); return -1; }
+    const size_t PRH = (size_t)e->m->g.prompt_hidden;
+    float *be = malloc(PRH * 4);
+    nb_model_prompt_bias(e->m, idx, be);
+    cudaError_t rc = cudaMemcpy(e->b_eff + (size_t)s * PRH, be, PRH * 4, cudaMemcpyHostToDevice);
+    free(be);
+    if (rc != cudaSuccess) { snprintf(err, errlen, "set prompt: %s", cudaGetErrorString(rc)); return -1; }
+    e->prompt_idx[s] = idx;
+    return 0;
+}
+
+int nb_engine_attach_device_mel(nb_engine_t *e, const float *d_mel, int64_t sstride_floats, size_t frames, char *err, size_t errlen) {
+    if (e->consumed || e->pending_n) { snprintf(err, errlen, "attach a device mel source right after reset"); return -1; }
+    e->dev_mel = d_mel;
+    e->dev_mel_sstride = sstride_floats;
+    e->dev_mel_frames = frames;
+    e->pending_n = frames;
+    return 0;
+}
+
+int nb_engine_push(nb_engine_t *e, const float *const *mel, size_t nframes, char *err, size_t errlen) {
+    if (e->dev_mel) { snprintf(err, errlen, "engine reads a device mel source"); return -1; }
+    if (!nframes) return 0;
+    if (e->pending_n + nframes > e->pending_cap) {
+        e->pending_cap = (e->pending_n + nframes) * 2;
+        for (int s = 0; s < e->B; ++s) e->pending[s] = realloc(e->pending[s], e->pending_cap * 128 * sizeof(float));
+    }
+    for (int s = 0; s < e->B; ++s) memcpy(e->pending[s] + e->pending_n * 128, mel[s], nframes * 128 * sizeof(float));
+    e->pending_n += nframes;
+    return 0;
+}
+
+void nb_engine_set_taps(nb_engine_t *e, float *prompted, float *joint_enc, size_t cap_rows, int *chunk_rows, size_t cap_chunks) {
+    e->tap_prompted = prompted;
+    e->tap_joint = joint_enc;
+    e->tap_cap = cap_rows;
+    e->tap_rows = 0;
+    e->tap_chunk_rows = chunk_rows;
+    e->tap_chunk_cap = cap_chunks;
+    e->tap_chunks = 0;
+}
+void nb_engine_tap_counts(const nb_engine_t *e, size_t *rows, size_t *chunks) { *rows = e->tap_rows; *chunks = e->tap_chunks; }
+void nb_engine_times(const nb_engine_t *e, double *enc_ms, double *dec_ms, size_t *chunks) { *enc_ms = e->enc_ms; *dec_ms = e->dec_ms; *chunks = e->chunks; }
+
+/* ---- device launch sequence of one encoder step ------------------------------------------ */
+static nemo_gemm_args_t gemm_args(const void *A, int64_t lda, int a_fmt, int64_t a_plane, const uint16_t *W, int64_t ldw, const float *bias, void *C,
+                                  int64_t ldc, int M, int N, int K, int act, int acc, float alpha) {
+    nemo_gemm_args_t a;
+    memset(&a, 0, sizeof a);
+    a.A = A; a.lda = lda; a.a_fmt = a_fmt; a.a_plane = a_plane;
+    a.W = W; a.ldw = ldw; a.bias = bias;
+    a.C = C; a.ldc = ldc; a.c_fmt = NEMO_FMT_F32;
+    a.M = M; a.N = N; a.K = K; a.act = act; a.accumulate = acc; a.alpha = alpha;
+    return a;
+}
+
+static int launch_encoder(nb_engine_t *e, int nwin, int c) {
+    const nb_model_t *m = e->m;
+    const nb_config_t *g = &m->g;
+    const int B = e->B, D = g->d_model, CH = g->sub_channels, FF = g->d_ff, PRH = g->prompt_hidden, JH = g->joint_hidden, NP = g->num_prompts;
+    const int T1 = sub_len(nwin), F1 = 65, T2 = T1 / 2 + 1, F2 = F1 / 2 + 1, T3 = T2 / 2 + 1, F3 = F2 / 2 + 1;
+    const int M = B * c;
+    const float eps = g->ln_eps;
+    cudaStream_t st = e->st;
+    int *d_pos = e->d_params, *d_cache_len = e->d_params + 1, *d_lo = e->d_params + 2;
+    const int fl = e->fmt_layer, fc = e->fmt_conv;
+    /* plane offsets (elements) for buffers written as bf16 hi/lo */
+    const int64_t pl_c1 = (int64_t)B * T2 * F2 * CH, pl_c3 = (int64_t)B * T3 * F3 * CH, pl_row = (int64_t)B * e->cmax;
+    nemo_gemm_args_t a;
+
+    /* subsampling (src/encoder.c:121-142); the flatten keeps only rows [lo, lo + c) (:258) */
+    if (nemo_conv2d_c1_s2_relu(e->d_win, (int64_t)e->nwin_max * 128, m->conv0_w, m->conv0_b, e->c0, B, nwin, 128, T1, F1, CH, st)) return -1;
+    if (nb_dwconv2d_s2_fmt(e->c0, m->conv2_w, m->conv2_b, e->c1, fc, pl_c1, B, T1, F1, T2, F2, CH, st)) return -1;
+    a = gemm_args(e->c1, CH, fc, pl_c1, m->conv3_w, CH, m->conv3_b, e->c2, CH, B * T2 * F2, CH, CH, NEMO_ACT_RELU, 0, 1.0f);
+    if (nemo_gemm(&a, st)) return -1;
+    if (nb_dwconv2d_s2_fmt(e->c2, m->conv5_w, m->conv5_b, e->c3, fc, pl_c3, B, T2, F2, T3, F3, CH, st)) return -1;
+    a = gemm_args(e->c3, CH, fc, pl_c3, m->conv6_w, CH, m->conv6_b, e->c4, CH, B * T3 * F3, CH, CH, NEMO_ACT_RELU, 0, 1.0f);
+    if (nemo_gemm(&a, st)) return -1;
+    if (nb_flatten_rows_fmt(e->c4, e->flat, fl, pl_row * CH * F3, d_lo, B, T3, F3, CH, c, st)) return -1;
+    float *h = e->hbuf[0], *hn = e->hbuf[1];
+    a = gemm_args(e->flat, CH * F3, fl, pl_row * CH * F3, m->pre_out_w, CH * F3, m->pre_out_b, h, D, M, D, CH * F3, 0, 0, 1.0f);
+    if (nemo_gemm(&a, st)) return -1;
+
+    /* 24 conformer blocks (src/encoder.c:145-188) */
+    const int64_t plD = pl_row * D, plFF = pl_row * FF;
+    const int64_t kv_s = (int64_t)e->cap_rows * 3 * D, din_s = (int64_t)e->cap_rows * D;
+    for (int l = 0; l < g->n_layers; ++l) {
+        const nb_layer_t *W = &m->L[l];
+        float *kv = e->kv + (size_t)l * B * kv_s, *din = e->din + (size_t)l * B * din_s;
+        if (l == 0 && nemo_layernorm(h, W->ln_ff1_g, W->ln_ff1_b, e->xin, fl, plD, M, D, eps, st)) return -1;
+        a = gemm_args(e->xin, D, fl, plD, W->ff1_w1, D, NULL, e->ff, FF, M, FF, D, NEMO_ACT_SILU, 0, 1.0f);
+        a.c_fmt = fl; a.c_plane = plFF;
+        if (nemo_gemm(&a, st)) return -1;
+        a = gemm_args(e->ff, FF, fl, plFF, W->ff1_w2, FF, NULL, h, D, M, D, FF, 0, 1, 0.5f);
+        if (nemo_gemm(&a, st)) return -1;
+        /* attention: q|k|v appended to the per-stream cache rows [pos, pos + c) */
+        if (nemo_layernorm(h, W->ln_att_g, W->ln_att_b, e->xin, fl, plD, M, D, eps, st)) return -1;
+        a = gemm_args(e->xin, D, fl, plD, W->wqkv, D, NULL, kv, 3 * D, M, 3 * D, D, 0, 0, 1.0f);
+        a.rpg = c; a.gstride = kv_s; a.rowoff = d_pos;
+        if (nemo_gemm(&a, st)) return -1;
+        if (nemo_attention_rel(kv, 3 * D, kv_s, kv + D, kv + 2 * D, 3 * D, kv_s, d_pos, d_cache_len, W->ptab, W->bias_u, W->bias_v, e->att, fl, plD,
+                               (int64_t)c * D, B, c, e->Lmax, g->n_heads, 128, D, 1.0f / sqrtf(128.0f), st))
+            return -1;
+        a = gemm_args(e->att, D, fl, plD, W->wo, D, NULL, h, D, M, D, D, 0, 1, 1.0f);
+        if (nemo_gemm(&a, st)) return -1;
+        /* conv module: GLU output appended to the conv history at rows [pos, pos + c) */
+        if (nemo_layernorm(h, W->ln_conv_g, W->ln_conv_b, e->xin, fl, plD, M, D, eps, st)) return -1;
+        a = gemm_args(e->xin, D, fl, plD, W->pw1, D, NULL, din, D, M, 2 * D, D, NEMO_ACT_GLU, 0, 1.0f);
+        a.rpg = c; a.gstride = din_s; a.rowoff = d_pos;
+        if (nemo_gemm(&a, st)) return -1;
+        if (nemo_dwconv_ln_silu(din, din_s, d_pos, W->dw_w, W->bn_g, W->bn_b, e->y, fl, plD, B, c, D, g->conv_kernel, eps, st)) return -1;
+        a = gemm_args(e->y, D, fl, plD, W->pw2, D, NULL, h, D, M, D, D, 0, 1, 1.0f);
+        if (nemo_gemm(&a, st)) return -1;
+        /* FF2 half step, then the output norm fused with the next block's FF1 norm */
+        if (nemo_layernorm(h, W->ln_ff2_g, W->ln_ff2_b, e->xin, fl, plD, M, D, eps, st)) return -1;
+        a = gemm_args(e->xin, D, fl, plD, W->ff2_w1, D, NULL, e->ff, FF, M, FF, D, NEMO_ACT_SILU, 0, 1.0f);
+        a.c_fmt = fl; a.c_plane = plFF;
+        if (nemo_gemm(&a, st)) return -1;
+        a = gemm_args(e->ff, FF, fl, plFF, W->ff2_w2, FF, NULL, h, D, M, D, FF, 0, 1, 0.5f);
+        if (nemo_gemm(&a, st)) return -1;
+        if (l + 1 < g->n_layers) {
+            const nb_layer_t *Wn = &m->L[l + 1];
+            if (nemo_layernorm2(h, W->ln_out_g, W->ln_out_b, Wn->ln_ff1_g, Wn->ln_ff1_b, hn, e->xin, fl, plD, M, D, eps, st)) return -1;
+            float *sw = h; h = hn; hn = sw;
+        } else {
+            if (nemo_layernorm(h, W->ln_out_g, W->ln_out_b, e->xin, fl, plD, M, D, eps, st)) return -1;
+        }
+    }
+    /* language prompt (per-stream one-hot folded into the bias) and joint encoder projection
+       (src/encoder.c:189-194) */
+    a = gemm_args(e->xin, D, fl, plD, m->prompt_w0, D + NP, e->b_eff, e->ph, PRH, M, PRH, D, NEMO_ACT_RELU, 0, 1.0f);
+    a.rpg = c; a.bias_gstride = PRH; a.c_fmt = fl; a.c_plane = pl_row * PRH;
+    if (nemo_gemm(&a, st)) return -1;
+    a = gemm_args(e->ph, PRH, fl, pl_row * PRH, m->prompt_w2, PRH, m->prompt_b2, e->prompted, D, M, D, PRH, 0, 0, 1.0f);
+    if (nemo_gemm(&a, st)) return -1;
+    a = gemm_args(e->prompted, D, NEMO_FMT_F32, 0, m->joint_enc_w, D, m->joint_enc_b, e->joint_enc, JH, M, JH, D, 0, 0, 1.0f);
+    if (nemo_gemm(&a, st)) return -1;
+    return 0;
+}
+
+/* ---- greedy RNNT decode of the chunk's c frames for every stream (src/decoder.c:92-127) --- */
+static int run_decoder(nb_engine_t *e, int c, char *err, size_t errlen) {
+    const nb_model_t *m = e->m;
+    const nb_config_t *g = &m->g;
+    const int B = e->B, PH = g->pred_hidden, JH = g->joint_hidden;
+    DecState *d = &e->dec;
+    cudaStream_t st = e->st;
+    KL(nb_dec_chunk_init(d, c, st));
+    const int max_it = c * (g->max_symbols + 1) + 2;
+    int it;
+    for (it = 0; it < max_it; ++it) {
+        KL(nb_dec_plan(d, c, st));
+        KL(nb_dec_gather(d, m->embed, PH, g->blank_id, st));
+        nemo_gemm_args_t a = gemm_args(d->A0, 2 * PH, NEMO_FMT_F32, 0, m->lstm_w[0], 2 * PH, m->lstm_b[0], d->gates, 4 * PH, B, 4 * PH, 2 * PH, 0, 0, 1.0f);
+        a.dynM = d->cnt;
+        KL(nemo_gemm(&a, st));
+        KL(nb_dec_cell(d, 0, PH, d->A1, 2 * PH, st));
+        a = gemm_args(d->A1, 2 * PH, NEMO_FMT_F32, 0, m->lstm_w[1], 2 * PH, m->lstm_b[1], d->gates, 4 * PH, B, 4 * PH, 2 * PH, 0, 0, 1.0f);
+        a.dynM = d->cnt;
+        KL(nemo_gemm(&a, st));
+        KL(nb_dec_cell(d, 1, PH, d->hp1c, PH, st));
+        a = gemm_args(d->hp1c, PH, NEMO_FMT_F32, 0, m->joint_pred_w, PH, m->joint_pred_b, d->predc, JH, B, JH, PH, 0, 0, 1.0f);
+        a.dynM = d->cnt;
+        KL(nemo_gemm(&a, st));
+        KL(nb_dec_scatter_pred(d, JH, st));
+        KL(nb_joint_argmax_rows(e->joint_enc, JH, d->pred, JH, 1, m->joint_out_w, m->joint_out_b, g->num_classes, JH, B, d->erow, d->idx, NULL, st));
+        KL(nb_dec_update(d, c, PH, g->blank_id, g->max_symbols, st));
+        if (cudaMemcpyAsync(e->h_cnt, d->cnt, 2 * sizeof(int), cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+            cudaStreamSynchronize(st) != cudaSuccess) {
+            snprintf(err, errlen, "decoder: %s", cudaGetErrorString(cudaGetLastError()));
+            return -1;
+        }
+        if (e->h_cnt[1] == 0) break;
+    }
+    if (it == max_it) { snprintf(err, errlen, "decoder did not finish the chunk in %d iterations", max_it); return -1; }
+    return 0;
+}
+
+int nb_engine_step(nb_engine_t *e, int final, int *tokens, int max_tokens, int *counts, int *frames, char *err, size_t errlen) {
+    *frames = 0;
+    if (e->closed) return 0;
+    if (e->pending_n == 0) { if (final) e->closed = 1; return 0; }
+    if ((int)e->pending_n < e->chunk_mel && !final) return 0;
+    const double t0 = nb_now_ms();
+    size_t take = (size_t)e->chunk_mel < e->pending_n ? (size_t)e->chunk_mel : e->pending_n;
+    if (final && e->pending_n <= (size_t)e->chunk_mel) take = e->pending_n;
+    const int include_boundary = final && e->pending_n == take;
+    /* window = mel cache ++ take rows, per stream */
+    const int nwin = e->mel_cache_n + (int)take;
+    const size_t wstride = (size_t)e->nwin_max * 128;
+    const size_t win_first = e->consumed - (size_t)e->mel_cache_n; /* window = frames [win_first, consumed + take) */
+    if (!e->dev_mel) {
+        for (int s = 0; s < e->B; ++s) {
+            float *w = e->h_win + (size_t)s * wstride;
+            memcpy(w, e->mel_cache + (size_t)s * NB_MEL_CACHE * 128, (size_t)e->mel_cache_n * 128 * sizeof(float));
+            memcpy(w + (size_t)e->mel_cache_n * 128, e->pending[s], take * 128 * sizeof(float));
+        }
+    }
+    /* bookkeeping of src/encoder.c:229-249 */
+    const size_t end = e->consumed + take;
+    const size_t base = (e->consumed - (size_t)e->mel_cache_n) / 8;
+    const size_t lo = e->emitted - base;
+    const int T3 = sub_len(sub_len(sub_len(nwin)));
+    const size_t hi = include_boundary ? (size_t)T3 : end / 8 - base;
+    e->consumed = end;
+    const int keep = nwin < NB_MEL_CACHE ? nwin : NB_MEL_CACHE;
+    if (!e->dev_mel) {
+        for (int s = 0; s < e->B; ++s)
+            memcpy(e->mel_cache + (size_t)s * NB_MEL_CACHE * 128, e->h_win + (size_t)s * wstride + (size_t)(nwin - keep) * 128,
+                   (size_t)keep * 128 * sizeof(float));
+        for (int s = 0; s < e->B; ++s) memmove(e->pending[s], e->pending[s] + take * 128, (e->pending_n - take) * 128 * sizeof(float));
+    }
+    e->mel_cache_n = keep;
+    e->pending_n -= take;
+    if (final && e->pending_n == 0) e->closed = 1;
+    if (hi <= lo) { e->emitted = base + (lo > hi ? lo : hi); return 1; }
+    e->emitted = base + hi;
+    const int c = (int)(hi - lo);
+    if (c > e->cmax) { snprintf(err, errlen, "chunk of %d rows exceeds buffer %d", c, e->cmax); return -1; }
+
+    cudaStream_t st = e->st;
+    const nb_config_t *g = &e->m->g;
+    const size_t D = (size_t)g->d_model;
+    cudaEventRecord(e->ev0, st);
+    if (e->pos + c > e->cap_rows) {
+        if (nb_compact(e->kv, e->din, g->n_layers, e->B, e->cap_rows, (int)D, e->pos - e->cache_len, e->cache_len, e->pos - e->conv_left,
+                       e->cache_len - e->conv_left, e->conv_left, st)) {
+            snprintf(err, errlen, "%s", nemo_gpu_last_error());
+            return -1;
+        }
+        e->pos = e->cache_len;
+    }
+    e->h_params[0] = e->pos;
+    e->h_params[1] = e->cache_len;
+    e->h_params[2] = (int)lo;
+    cudaError_t wrc;
+    if (e->dev_mel)
+        wrc = cudaMemcpy2DAsync(e->d_win, wstride * sizeof(float), e->dev_mel + win_first * 128, (size_t)e->dev_mel_sstride * sizeof(float),
+                                (size_t)nwin * 128 * sizeof(float), (size_t)e->B, cudaMemcpyDeviceToDevice, st);
+    else
+        wrc = cudaMemcpyAsync(e->d_win, e->h_win, (size_t)e->B * wstride * sizeof(float), cudaMemcpyHostToDevice, st);
+    if (wrc != cudaSuccess || cudaMemcpyAsync(e->d_params, e->h_params, 3 * sizeof(int), cudaMemcpyHostToDevice, st) != cudaSuccess) {
+        snprintf(err, errlen, "upload: %s", cudaGetErrorString(cudaGetLastError()));
+        return -1;
+    }
+    if (launch_encoder(e, nwin, c)) { snprintf(err, errlen, "encoder: %s", nemo_gpu_last_error()); return -1; }
+    if (cudaStreamSynchronize(st) != cudaSuccess) { snprintf(err, errlen, "encoder: %s", cudaGetErrorString(cudaGetLastError())); return -1; }
+    const double t1 = nb_now_ms();
+    e->pos += c;
+    const int L = e->cache_len + c;
+    e->cache_len = L < e->left ? L : e->left;
+    if (e->tap_prompted) {
+        const size_t rows = (size_t)e->B * c;
+        if (e->tap_rows + rows <= e->tap_cap) {
+            cudaMemcpy(e->tap_prompted + e->tap_rows * D, e->prompted, rows * D * 4, cudaMemcpyDeviceToHost);
+            cudaMemcpy(e->tap_joint + e->tap_rows * (size_t)g->joint_hidden, e->joint_enc, rows * (size_t)g->joint_hidden * 4, cudaMemcpyDeviceToHost);
+            e->tap_rows += rows;
+        }
+        if (e->tap_chunks < e->tap_chunk_cap) e->tap_chunk_rows[e->tap_chunks] = c;
+        e->tap_chunks++;
+    }
+    if (run_decoder(e, c, err, errlen)) return -1;
+    const DecState *d = &e->dec;
+    if (cudaMemcpyAsync(e->h_ntok, d->ntok, (size_t)e->B * sizeof(int), cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+        cudaMemcpyAsync(e->h_tokens, d->tokens, (size_t)e->B * (size_t)d->tok_cap * sizeof(int), cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+        cudaEventRecord(e->ev1, st) != cudaSuccess || cudaStreamSynchronize(st) != cudaSuccess) {
+        snprintf(err, errlen, "tokens: %s", cudaGetErrorString(cudaGetLastError()));
+        return -1;
+    }
+    float step_ms = 0.0f;
+    if (cudaEventElapsedTime(&step_ms, e->ev0, e->ev1) == cudaSuccess) e->gpu_ms += step_ms;
+    for (int s = 0; s < e->B; ++s) {
+        const int n = e->h_ntok[s] < d->tok_cap ? e->h_ntok[s] : d->tok_cap;
+        for (int i = 0; i < n; ++i)
+            if (counts[s] < max_tokens) tokens[(size_t)s * max_tokens + counts[s]++] = e->h_tokens[(size_t)s * d->tok_cap + i];
+    }
+    e->enc_ms += t1 - t0;
+    e->dec_ms += nb_now_ms() - t1;
+    e->chunks++;
+    *frames = c;
+    return 1;
+}

@@ -1,0 +1,38 @@
+/* Device-side decoder state of the streaming engine (structure of arrays over streams). Shared by
+   engine.c (host) and k_engine.cu (kernels). */
+#ifndef NB_ENGINE_DEV_H
+#define NB_ENGINE_DEV_H
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct {
+    int streams, tok_cap;
+    int *t, *symbols, *active, *pred_valid, *last_token, *ntok, *tokens;
+    int *need_idx, *erow, *idx, *cnt; /* cnt[0] streams needing the prediction net, cnt[1] still active */
+    float *h, *c, *hp, *cp;           /* [2][streams][PH] committed / provisional LSTM state */
+    float *pred;                      /* [streams][JH] joint prediction projection */
+    float *A0, *A1, *gates, *hp1c, *predc; /* compact per-iteration work rows */
+} DecState;
+
+int nb_compact(float *kv, float *din, int layers, int streams, int64_t cap, int D, int src_kv, int cache_len, int src_din, int dst_din,
+               int conv_left, void *stream);
+int nb_dec_chunk_init(const DecState *d, int c, void *stream);
+int nb_dec_plan(const DecState *d, int c, void *stream);
+int nb_dec_gather(const DecState *d, const uint16_t *embed, int PH, int blank, void *stream);
+int nb_dec_cell(const DecState *d, int layer, int PH, float *next, int64_t next_ld, void *stream);
+int nb_dec_scatter_pred(const DecState *d, int JH, void *stream);
+int nb_dec_update(const DecState *d, int c, int PH, int blank, int max_symbols, void *stream);
+int nb_dec_reset(const DecState *d, int PH, int blank, void *stream);
+int nb_joint_argmax_rows(const float *enc, int64_t enc_ld, const float *pred, int64_t pred_ld, int pred_rpg, const uint16_t *W,
+                         const float *bias, int V, int H, int rows, const int *enc_row_of, int *out_idx, float *out_val, void *stream);
+int nb_dwconv2d_s2_fmt(const float *X, const float *W, const float *bias, void *Y, int y_fmt, int64_t y_plane, int streams, int T, int F,
+                       int T1, int F1, int C, void *stream);
+int nb_flatten_rows_fmt(const float *X, void *Y, int y_fmt, int64_t y_plane, const int *lo, int streams, int T, int F, int C, int c, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,218 @@
+/* Host audio front end of the streaming API: log-mel features and sample-rate conversion.
+   Same definitions as the reference's src/mel.c and src/resample.c:
+   - log-mel: preemphasis 0.97, symmetric Hann(400) centred in a 512-point frame, 10 ms hop,
+     centred frames with reflect padding (no edge repeat), power spectrum from a double-precision
+     radix-2 FFT, 128 Slaney-normalised mel filters, log(x + 2^-24);
+   - resampler: Blackman-windowed sinc with 16 zero crossings, cutoff at the lower Nyquist,
+     weight-normalised, streaming with zero extension at the stream edges. */
+#include "nb.h"
+#include <math.h>
+#include <stdlib.h>
+#include <string.h>
+
+#define LOOKAHEAD (NB_MEL_NFFT / 2)
+#define LOG_GUARD 5.960464477539063e-08f
+
+struct nb_mel {
+    float *y;
+    size_t y_len, y_cap, y_start, total, next_frame;
+    float last_x;
+    int have_last, closed;
+    float window[NB_MEL_NFFT];
+    float fb[NB_MEL_NMEL * NB_MEL_NFREQ];
+    double wr[NB_MEL_NFFT / 2], wi[NB_MEL_NFFT / 2];
+    int rev[NB_MEL_NFFT];
+    float *out;
+    size_t out_cap;
+};
+
+/* Slaney scale: linear below 1 kHz (200/3 Hz per mel), logarithmic above (27 mels per ln 6.4) */
+static double slaney_mel(double hz) {
+    const double fsp = 200.0 / 3.0, brk = 1000.0, brk_mel = brk / fsp, step = log(6.4) / 27.0;
+    return hz < brk ? hz / fsp : brk_mel + log(hz / brk) / step;
+}
+static double slaney_hz(double mel) {
+    const double fsp = 200.0 / 3.0, brk = 1000.0, brk_mel = brk / fsp, step = log(6.4) / 27.0;
+    return mel < brk_mel ? fsp * mel : brk * exp(step * (mel - brk_mel));
+}
+
+nb_mel_t *nb_mel_create(void) {
+    nb_mel_t *m = calloc(1, sizeof *m);
+    m->y_cap = NB_MEL_SR * 4;
+    m->y = malloc(m->y_cap * sizeof(float));
+    const int off = (NB_MEL_NFFT - NB_MEL_WIN) / 2;
+    for (int n = 0; n < NB_MEL_WIN; ++n) m->window[off + n] = (float)(0.5 * (1.0 - cos(2.0 * M_PI * n / (NB_MEL_WIN - 1))));
+    double hz[NB_MEL_NFREQ], edge[NB_MEL_NMEL + 2];
+    for (int k = 0; k < NB_MEL_NFREQ; ++k) hz[k] = (NB_MEL_SR / 2) * (double)k / (NB_MEL_NFREQ - 1);
+    const double lo = slaney_mel(0.0), hi = slaney_mel(NB_MEL_SR / 2.0);
+    for (int i = 0; i < NB_MEL_NMEL + 2; ++i) edge[i] = slaney_hz(lo + (hi - lo) * (double)i / (NB_MEL_NMEL + 1));
+    for (int b = 0; b < NB_MEL_NMEL; ++b) {
+        const double norm = 2.0 / (edge[b + 2] - edge[b]);
+        for (int k = 0; k < NB_MEL_NFREQ; ++k) {
+            const double rise = (hz[k] - edge[b]) / (edge[b + 1] - edge[b]);
+            const double fall = (edge[b + 2] - hz[k]) / (edge[b + 2] - edge[b + 1]);
+            const double tri = fmax(0.0, fmin(rise, fall));
+            m->fb[b * NB_MEL_NFREQ + k] = (float)(tri * norm);
+        }
+    }
+    for (int i = 0; i < NB_MEL_NFFT / 2; ++i) { m->wr[i] = cos(-2.0 * M_PI * i / NB_MEL_NFFT); m->wi[i] = sin(-2.0 * M_PI * i / NB_MEL_NFFT); }
+    for (int i = 0; i < NB_MEL_NFFT; ++i) {
+        int r = 0;
+        for (int b = 0; b < 9; ++b) r |= ((i >> b) & 1) << (8 - b);
+        m->rev[i] = r;
+    }
+    return m;
+}
+void nb_mel_destroy(nb_mel_t *m) { if (m) { free(m->y); free(m->out); free(m); } }
+size_t nb_mel_total_samples(const nb_mel_t *m) { return m->total; }
+
+/* iterative radix-2 Cooley-Tukey, bit-reversed input order, butterflies by stage */
+static void fft(const nb_mel_t *m, double *re, double *im) {
+    for (int i = 0; i < NB_MEL_NFFT; ++i) {
+        const int j = m->rev[i];
+        if (j > i) { double t = re[i]; re[i] = re[j]; re[j] = t; t = im[i]; im[i] = im[j]; im[j] = t; }
+    }
+    for (int span = 2; span <= NB_MEL_NFFT; span <<= 1) {
+        const int half = span >> 1, tstep = NB_MEL_NFFT / span;
+        for (int base = 0; base < NB_MEL_NFFT; base += span)
+            for (int k = 0; k < half; ++k) {
+                const double c = m->wr[k * tstep], s = m->wi[k * tstep];
+                const int p = base + k, q = p + half;
+                const double xr = re[q] * c - im[q] * s, xi = re[q] * s + im[q] * c;
+                const double ar = re[p], ai = im[p];
+                re[p] = ar + xr; im[p] = ai + xi;
+                re[q] = ar - xr; im[q] = ai - xi;
+            }
+    }
+}
+
+static float sample_at(const nb_mel_t *m, long g) {
+    const long N = (long)m->total;
+    if (g < 0) g = -g;                 /* reflect without repeating the edge sample */
+    if (g >= N) g = 2 * N - 2 - g;
+    if (g < 0 || g >= N) return 0.0f;
+    const long i = g - (long)m->y_start;
+    return (i < 0 || i >= (long)m->y_len) ? 0.0f : m->y[i];
+}
+
+void nb_mel_push(nb_mel_t *m, const float *samples, size_t n, int final, const float **frames, size_t *nframes) {
+    *frames = NULL;
+    *nframes = 0;
+    if (m->closed) return;
+    if (m->y_len + n > m->y_cap) {
+        while (m->y_len + n > m->y_cap) m->y_cap *= 2;
+        m->y = realloc(m->y, m->y_cap * sizeof(float));
+    }
+    for (size_t i = 0; i < n; ++i) {
+        const float x = samples[i];
+        m->y[m->y_len++] = m->have_last ? x - 0.97f * m->last_x : x;
+        m->last_x = x;
+        m->have_last = 1;
+    }
+    m->total += n;
+    /* a frame is complete once its right half is present; the final call also emits the
+       frames whose right half is reflected */
+    const size_t end = final ? m->total / NB_MEL_HOP + 1 : (m->total >= LOOKAHEAD ? (m->total - LOOKAHEAD) / NB_MEL_HOP + 1 : 0);
+    if (final) m->closed = 1;
+    if (end <= m->next_frame) return;
+    const size_t count = end - m->next_frame;
+    if (count * NB_MEL_NMEL > m->out_cap) { m->out_cap = count * NB_MEL_NMEL; m->out = realloc(m->out, m->out_cap * sizeof(float)); }
+    double re[NB_MEL_NFFT], im[NB_MEL_NFFT];
+    float pw[NB_MEL_NFREQ];
+    for (size_t t = m->next_frame; t < end; ++t) {
+        const long start = (long)t * NB_MEL_HOP - LOOKAHEAD;
+        for (int k = 0; k < NB_MEL_NFFT; ++k) { re[k] = (double)(sample_at(m, start + k) * m->window[k]); im[k] = 0.0; }
+        fft(m, re, im);
+        for (int k = 0; k < NB_MEL_NFREQ; ++k) pw[k] = (float)(re[k] * re[k] + im[k] * im[k]);
+        float *row = m->out + (t - m->next_frame) * NB_MEL_NMEL;
+        for (int b = 0; b < NB_MEL_NMEL; ++b) {
+            const float *f = m->fb + b * NB_MEL_NFREQ;
+            float acc = 0.0f;
+            for (int k = 0; k < NB_MEL_NFREQ; ++k) acc += f[k] * pw[k];
+            row[b] = logf(acc + LOG_GUARD);
+        }
+    }
+    *frames = m->out;
+    *nframes = count;
+    m->next_frame = end;
+    const long keep = (long)m->next_frame * NB_MEL_HOP - NB_MEL_NFFT - 2;
+    if (keep > (long)m->y_start) {
+        size_t drop = (size_t)keep - m->y_start;
+        if (drop > m->y_len) drop = m->y_len;
+        memmove(m->y, m->y + drop, (m->y_len - drop) * sizeof(float));
+        m->y_len -= drop;
+        m->y_start += drop;
+    }
+}
+
+/* ---- resampler --------------------------------------------------------------------------- */
+struct nb_resampler {
+    double ratio, half, fc2;
+    float *buf;
+    size_t len, cap;
+    unsigned long long start, nin, nout;
+    int same;
+};
+
+nb_resampler_t *nb_resampler_create(int in_rate, int out_rate) {
+    nb_resampler_t *r = calloc(1, sizeof *r);
+    r->same = in_rate == out_rate;
+    r->ratio = (double)in_rate / (double)out_rate;
+    r->half = 16.0 * fmax(r->ratio, 1.0);
+    r->fc2 = fmin(1.0, 1.0 / r->ratio);
+    r->cap = 8192;
+    r->buf = malloc(r->cap * sizeof(float));
+    return r;
+}
+void nb_resampler_destroy(nb_resampler_t *r) { if (r) { free(r->buf); free(r); } }
+
+static double taper(const nb_resampler_t *r, double u) {
+    const double x = u / r->half;
+    if (x <= -1.0 || x >= 1.0) return 0.0;
+    const double blackman = 0.42 + 0.5 * cos(M_PI * x) + 0.08 * cos(2.0 * M_PI * x);
+    const double a = M_PI * r->fc2 * u;
+    return r->fc2 * (fabs(a) < 1e-9 ? 1.0 : sin(a) / a) * blackman;
+}
+
+static size_t produce(nb_resampler_t *r, float *out, size_t out_max, int final) {
+    size_t k = 0;
+    while (k < out_max) {
+        const double t = (double)r->nout * r->ratio;
+        const long a = (long)ceil(t - r->half), b = (long)floor(t + r->half);
+        if (!final && (unsigned long long)(b + 1) > r->nin) break;
+        if (final && (unsigned long long)a >= r->nin) break;
+        double acc = 0.0, wsum = 0.0;
+        for (long i = a; i <= b; ++i) {
+            const double h = taper(r, (double)i - t);
+            wsum += h;
+            if (i < 0 || (unsigned long long)i >= r->nin) continue;
+            const long j = i - (long)r->start;
+            if (j < 0 || (size_t)j >= r->len) continue;
+            acc += h * r->buf[j];
+        }
+        out[k++] = (float)(wsum > 0 ? acc / wsum : 0.0);
+        r->nout++;
+    }
+    const long keep = (long)floor((double)r->nout * r->ratio - r->half) - 2;
+    if (keep > (long)r->start) {
+        size_t drop = (size_t)keep - (size_t)r->start;
+        if (drop > r->len) drop = r->len;
+        memmove(r->buf, r->buf + drop, (r->len - drop) * sizeof(float));
+        r->len -= drop;
+        r->start += drop;
+    }
+    return k;
+}
+
+size_t nb_resampler_process(nb_resampler_t *r, const float *in, size_t n, float *out, size_t out_max) {
+    if (r->same) { const size_t k = n < out_max ? n : out_max; memcpy(out, in, k * sizeof(float)); return k; }
+    if (r->len + n > r->cap) {
+        while (r->len + n > r->cap) r->cap *= 2;
+        r->buf = realloc(r->buf, r->cap * sizeof(float));
+    }
+    memcpy(r->buf + r->len, in, n * sizeof(float));
+    r->len += n;
+    r->nin += n;
+    return produce(r, out, out_max, 0);
+}
+size_t nb_resampler_flush(nb_resampler_t *r, float *out, size_t out_max) { return r->same ? 0 : produce(r, out, out_max, 1); }

@@ -1,0 +1,170 @@
+// Kernels private to the streaming engine: per-epoch cache compaction (src/encoder.c:201-211)
+// and the batched greedy RNNT loop bookkeeping (src/decoder.c:92-127), one frame per stream per
+// iteration, every stream advancing independently.
+#include "common.cuh"
+#include "engine_dev.h"
+
+namespace {
+
+// Move kv rows [src_kv, src_kv + cache_len) to [0, cache_len) and din rows
+// [src_din, src_din + conv_left) to [dst_din, dst_din + conv_left), every layer and stream.
+// Source and destination never overlap (cap_rows >= 2 * att_left + cmax).
+__global__ void compact_kernel(float *kv, float *din, int layers, int streams, int64_t cap, int D, int src_kv, int cache_len, int src_din,
+                               int dst_din, int conv_left) {
+    const int64_t kv_row = 3LL * D, per_kv = (int64_t)cache_len * kv_row, per_din = (int64_t)conv_left * D;
+    const int64_t total = (int64_t)layers * streams * (per_kv + per_din);
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t ls = i / (per_kv + per_din), r = i - ls * (per_kv + per_din);
+        if (r < per_kv) {
+            float *base = kv + ls * cap * kv_row;
+            base[r] = base[(int64_t)src_kv * kv_row + r];
+        } else {
+            const int64_t q = r - per_kv;
+            float *base = din + ls * cap * D;
+            base[(int64_t)dst_din * D + q] = base[(int64_t)src_din * D + q];
+        }
+    }
+}
+
+__global__ void dec_chunk_init_kernel(DecState d, int streams, int c) {
+    const int b = blockIdx.x * blockDim.x + threadIdx.x;
+    if (b >= streams) return;
+    d.t[b] = 0;
+    d.symbols[b] = 0;
+    d.active[b] = c > 0;
+    d.ntok[b] = 0;
+}
+
+// Streams that still have frames and whose prediction vector is stale get the prediction
+// network this iteration (src/decoder.c:101); every active stream scores its current frame.
+__global__ void dec_plan_kernel(DecState d, int streams, int c) {
+    __shared__ int n_need;
+    if (threadIdx.x == 0) n_need = 0;
+    __syncthreads();
+    for (int b = threadIdx.x; b < streams; b += blockDim.x) {
+        const bool act = d.active[b];
+        d.erow[b] = act ? b * c + d.t[b] : -1;
+        if (act && !d.pred_valid[b]) d.need_idx[atomicAdd(&n_need, 1)] = b;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) { d.cnt[0] = n_need; d.cnt[1] = 0; }
+}
+
+// Prediction-network input for each listed stream: [embed(last token) (zeros for blank) | h0]
+// for layer 0 and [. | h1] for layer 1 (src/decoder.c:61-70).
+__global__ void dec_gather_kernel(DecState d, const uint16_t *__restrict__ embed, int PH, int blank) {
+    const int i = blockIdx.x;
+    if (i >= d.cnt[0]) return;
+    const int b = d.need_idx[i];
+    const int tok = d.last_token[b];
+    float *a0 = d.A0 + (int64_t)i * 2 * PH, *a1 = d.A1 + (int64_t)i * 2 * PH;
+    const float *h0 = d.h + (int64_t)b * PH, *h1 = d.h + ((int64_t)d.streams + b) * PH;
+    for (int j = threadIdx.x; j < PH; j += blockDim.x) {
+        a0[j] = tok == blank ? 0.0f : nb::bf2f(embed[(int64_t)tok * PH + j]);
+        a0[PH + j] = h0[j];
+        a1[PH + j] = h1[j];
+    }
+}
+
+// LSTM cell (src/kernels.metal:475-486) from the committed cell state into the provisional
+// state of each listed stream; h' also goes to `next` (the following GEMM's input row).
+__global__ void dec_cell_kernel(DecState d, int layer, int PH, float *next, int64_t next_ld) {
+    const int i = blockIdx.x;
+    if (i >= d.cnt[0]) return;
+    const int b = d.need_idx[i];
+    const float *g = d.gates + (int64_t)i * 4 * PH;
+    const int64_t sb = ((int64_t)layer * d.streams + b) * PH;
+    for (int j = threadIdx.x; j < PH; j += blockDim.x) {
+        const float ig = nb::sigmoid_f(g[j]), fg = nb::sigmoid_f(g[PH + j]), gg = tanhf(g[2 * PH + j]), og = nb::sigmoid_f(g[3 * PH + j]);
+        const float cc = fg * d.c[sb + j] + ig * gg;
+        const float hh = og * tanhf(cc);
+        d.cp[sb + j] = cc;
+        d.hp[sb + j] = hh;
+        next[(int64_t)i * next_ld + j] = hh;
+    }
+}
+
+__global__ void dec_scatter_pred_kernel(DecState d, int JH) {
+    const int i = blockIdx.x;
+    if (i >= d.cnt[0]) return;
+    const int b = d.need_idx[i];
+    for (int j = threadIdx.x; j < JH; j += blockDim.x) d.pred[(int64_t)b * JH + j] = d.predc[(int64_t)i * JH + j];
+    if (threadIdx.x == 0) d.pred_valid[b] = 1;
+}
+
+// One decision per active stream (src/decoder.c:106-121): blank -> next frame, symbols = 0;
+// token -> emit, commit the provisional LSTM state, re-score the same frame unless max_symbols
+// tokens came from it.
+__global__ void dec_update_kernel(DecState d, int c, int PH, int blank, int max_symbols) {
+    const int b = blockIdx.x;
+    if (!d.active[b]) return;
+    const int k = d.idx[b];
+    if (k != blank) {
+        for (int l = 0; l < 2; ++l) {
+            const int64_t sb = ((int64_t)l * d.streams + b) * PH;
+            for (int j = threadIdx.x; j < PH; j += blockDim.x) { d.h[sb + j] = d.hp[sb + j]; d.c[sb + j] = d.cp[sb + j]; }
+        }
+    }
+    if (threadIdx.x != 0) return;
+    int t = d.t[b], sym = d.symbols[b];
+    if (k == blank) {
+        sym = 0;
+        ++t;
+    } else {
+        if (d.ntok[b] < d.tok_cap) d.tokens[(int64_t)b * d.tok_cap + d.ntok[b]] = k;
+        d.ntok[b]++;
+        d.last_token[b] = k;
+        d.pred_valid[b] = 0;
+        if (++sym >= max_symbols) { sym = 0; ++t; }
+    }
+    d.t[b] = t;
+    d.symbols[b] = sym;
+    const int act = t < c;
+    d.active[b] = act;
+    if (act) atomicAdd(&d.cnt[1], 1);
+}
+
+__global__ void dec_reset_kernel(DecState d, int PH, int blank) {
+    const int b = blockIdx.x;
+    for (int l = 0; l < 2; ++l) {
+        const int64_t sb = ((int64_t)l * d.streams + b) * PH;
+        for (int j = threadIdx.x; j < PH; j += blockDim.x) d.h[sb + j] = d.c[sb + j] = 0.0f;
+    }
+    if (threadIdx.x == 0) { d.last_token[b] = blank; d.pred_valid[b] = 0; d.active[b] = 0; d.ntok[b] = 0; }
+}
+
+}  // namespace
+
+extern "C" int nb_compact(float *kv, float *din, int layers, int streams, int64_t cap, int D, int src_kv, int cache_len, int src_din, int dst_din,
+                          int conv_left, void *stream) {
+    compact_kernel<<<148 * 8, 256, 0, (cudaStream_t)stream>>>(kv, din, layers, streams, cap, D, src_kv, cache_len, src_din, dst_din, conv_left);
+    return nb_check_launch("compact_kernel");
+}
+extern "C" int nb_dec_chunk_init(const DecState *d, int c, void *stream) {
+    dec_chunk_init_kernel<<<(d->streams + 255) / 256, 256, 0, (cudaStream_t)stream>>>(*d, d->streams, c);
+    return nb_check_launch("dec_chunk_init_kernel");
+}
+extern "C" int nb_dec_plan(const DecState *d, int c, void *stream) {
+    dec_plan_kernel<<<1, 1024, 0, (cudaStream_t)stream>>>(*d, d->streams, c);
+    return nb_check_launch("dec_plan_kernel");
+}
+extern "C" int nb_dec_gather(const DecState *d, const uint16_t *embed, int PH, int blank, void *stream) {
+    dec_gather_kernel<<<d->streams, 128, 0, (cudaStream_t)stream>>>(*d, embed, PH, blank);
+    return nb_check_launch("dec_gather_kernel");
+}
+extern "C" int nb_dec_cell(const DecState *d, int layer, int PH, float *next, int64_t next_ld, void *stream) {
+    dec_cell_kernel<<<d->streams, 128, 0, (cudaStream_t)stream>>>(*d, layer, PH, next, next_ld);
+    return nb_check_launch("dec_cell_kernel");
+}
+extern "C" int nb_dec_scatter_pred(const DecState *d, int JH, void *stream) {
+    dec_scatter_pred_kernel<<<d->streams, 128, 0, (cudaStream_t)stream>>>(*d, JH);
+    return nb_check_launch("dec_scatter_pred_kernel");
+}
+extern "C" int nb_dec_update(const DecState *d, int c, int PH, int blank, int max_symbols, void *stream) {
+    dec_update_kernel<<<d->streams, 128, 0, (cudaStream_t)stream>>>(*d, c, PH, blank, max_symbols);
+    return nb_check_launch("dec_update_kernel");
+}
+extern "C" int nb_dec_reset(const DecState *d, int PH, int blank, void *stream) {
+    dec_reset_kernel<<<d->streams, 128, 0, (cudaStream_t)stream>>>(*d, PH, blank);
+    return nb_check_launch("dec_reset_kernel");
+}
