@@ -45,6 +45,8 @@ typedef struct {
     int M, N, K;
     int act, accumulate;
     float alpha;
+    float *c32;      /* optional: also write the fp32 value at c32[m * ldc32 + n] (dense rows) */
+    int64_t ldc32;
 } nemo_gemm_args_t;
 int nemo_gemm(const nemo_gemm_args_t *a, void *stream);
 /* Force a kernel family for tests and the kernel sweep: 0 = by row count (default),
@@ -100,6 +102,9 @@ int nemo_joint_argmax(const float *enc, int64_t enc_ld, const float *pred, int64
                       const float *bias, int V, int H, int rows, int *out_idx, float *out_val, void *stream);
 
 const char *nemo_gpu_last_error(void);
+/* 0 if no kernel has reported a device-side failure (a bounded wait that gave up instead of
+   hanging); otherwise -1 with the message in nemo_gpu_last_error(). Synchronous (reads a flag). */
+int nemo_gpu_check_device_errors(void);
 /* Number of CUDA kernels this library has launched (directly or by graph launch) since load. */
 uint64_t nemo_gpu_launch_count(void);
 

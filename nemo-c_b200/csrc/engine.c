@@ -31,7 +31,7 @@ struct nb_engine {
     /* device */
     float *d_win, *h_win;      /* [B][nwin_max][128]; h_win pinned */
     float *c0, *c1, *c2, *c3, *c4, *flat;
-    float *hbuf[2], *xin, *ff, *att, *y, *ph, *prompted, *joint_enc;
+    float *hbuf[2], *xin, *ff, *att, *y, *ph, *prompted, *prompted_x, *joint_enc;
     float *kv, *din;           /* [layers][B][cap_rows][3D] and [layers][B][cap_rows][D] */
     float *b_eff;              /* [B][PH] */
     int *d_params, *h_params;  /* pos, cache_len, lo */
@@ -76,8 +76,12 @@ nb_engine_t *nb_engine_create(nb_model_t *m, int B, int right, char *err, size_t
     e->conv_left = g->conv_kernel - 1;
     e->cap_rows = e->left + NB_EPOCH_CHUNKS * e->cmax; /* src/encoder.c:73 */
     e->nwin_max = NB_MEL_CACHE + e->chunk_mel + 1;
-    e->fmt_layer = NEMO_FMT_F32;
-    e->fmt_conv = NEMO_FMT_F32;
+    /* GEMM inputs travel as bf16 hi/lo planes into the tensor-core kernel; NEMO_GEMM=cuda keeps
+       them fp32 and routes every GEMM through the CUDA-core kernels instead */
+    const char *gm = getenv("NEMO_GEMM");
+    const int fmt = (gm && !strcmp(gm, "cuda")) ? NEMO_FMT_F32 : NEMO_FMT_BF16X2;
+    e->fmt_layer = fmt;
+    e->fmt_conv = fmt;
     if (e->left + e->cmax > 96) { snprintf(err, errlen, "attention window %d exceeds 96 rows", e->left + e->cmax); free(e); return NULL; }
     int fail = 0;
     const size_t D = (size_t)g->d_model, CH = (size_t)g->sub_channels, FF = (size_t)g->d_ff, PH = (size_t)g->pred_hidden;
@@ -102,6 +106,7 @@ nb_engine_t *nb_engine_create(nb_model_t *m, int B, int right, char *err, size_t
     e->y = dalloc(Bz * cm * D * 4, &fail);
     e->ph = dalloc(Bz * cm * PRH * 4, &fail);
     e->prompted = dalloc(Bz * cm * D * 4, &fail);
+    e->prompted_x = fmt == NEMO_FMT_F32 ? e->prompted : dalloc(Bz * cm * D * 4, &fail);
     e->joint_enc = dalloc(Bz * cm * JH * 4, &fail);
     e->kv = dalloc((size_t)g->n_layers * Bz * (size_t)e->cap_rows * 3 * D * 4, &fail);
     e->din = dalloc((size_t)g->n_layers * Bz * (size_t)e->cap_rows * D * 4, &fail);
@@ -126,6 +131,9 @@ nb_engine_t *nb_engine_create(nb_model_t *m, int B, int right, char *err, size_t
     d->gates = dalloc(Bz * 4 * PH * 4, &fail);
     d->hp1c = dalloc(Bz * PH * 4, &fail);
     d->predc = dalloc(Bz * JH * 4, &fail);
+    d->fmt = fmt;
+    d->a_plane = (int64_t)Bz * 2 * PH;
+    d->h_plane = (int64_t)Bz * PH;
     if (fail) { snprintf(err, errlen, "out of device memory for %d streams", B); goto fail; }
     CK(cudaMallocHost((void **)&e->h_cnt, 8 * sizeof(int)));
     CK(cudaMallocHost((void **)&e->h_ntok, Bz * sizeof(int)));
@@ -153,6 +161,7 @@ void nb_engine_destroy(nb_engine_t *e) {
                    e->prompted, e->joint_enc, e->kv, e->din, e->b_eff, e->dec.h, e->dec.c, e->dec.hp, e->dec.cp, e->dec.pred, e->dec.A0,
                    e->dec.A1, e->dec.gates, e->dec.hp1c, e->dec.predc };
     for (size_t i = 0; i < sizeof f / sizeof *f; ++i) if (f[i]) cudaFree(f[i]);
+    if (e->prompted_x && e->prompted_x != e->prompted) cudaFree(e->prompted_x);
     int *n[] = { e->d_params, e->dec.t, e->dec.symbols, e->dec.active, e->dec.pred_valid, e->dec.last_token, e->dec.ntok, e->dec.need_idx,
                  e->dec.erow, e->dec.idx, e->dec.tokens, e->dec.cnt };
     for (size_t i = 0; i < sizeof n / sizeof *n; ++i) if (n[i]) cudaFree(n[i]);
@@ -327,11 +336,13 @@ static int launch_encoder(nb_engine_t *e, int nwin, int c) {
     /* language prompt (per-stream one-hot folded into the bias) and joint encoder projection
        (src/encoder.c:189-194) */
     a = gemm_args(e->xin, D, fl, plD, m->prompt_w0, D + NP, e->b_eff, e->ph, PRH, M, PRH, D, NEMO_ACT_RELU, 0, 1.0f);
-    a.rpg = c; a.bias_gstride = PRH; a.c_fmt = fl; a.c_plane = pl_row * PRH;
+    a.rpg = c; a.gstride = (int64_t)c * PRH; a.bias_gstride = PRH; a.c_fmt = fl; a.c_plane = pl_row * PRH;
     if (nemo_gemm(&a, st)) return -1;
-    a = gemm_args(e->ph, PRH, fl, pl_row * PRH, m->prompt_w2, PRH, m->prompt_b2, e->prompted, D, M, D, PRH, 0, 0, 1.0f);
+    /* post-prompt encoder output: fp32 for the caller, plus bf16 planes for the next GEMM */
+    a = gemm_args(e->ph, PRH, fl, pl_row * PRH, m->prompt_w2, PRH, m->prompt_b2, e->prompted_x, D, M, D, PRH, 0, 0, 1.0f);
+    if (fl != NEMO_FMT_F32) { a.c_fmt = fl; a.c_plane = plD; a.c32 = e->prompted; a.ldc32 = D; }
     if (nemo_gemm(&a, st)) return -1;
-    a = gemm_args(e->prompted, D, NEMO_FMT_F32, 0, m->joint_enc_w, D, m->joint_enc_b, e->joint_enc, JH, M, JH, D, 0, 0, 1.0f);
+    a = gemm_args(e->prompted_x, D, fl, plD, m->joint_enc_w, D, m->joint_enc_b, e->joint_enc, JH, M, JH, D, 0, 0, 1.0f);
     if (nemo_gemm(&a, st)) return -1;
     return 0;
 }
@@ -349,15 +360,15 @@ static int run_decoder(nb_engine_t *e, int c, char *err, size_t errlen) {
     for (it = 0; it < max_it; ++it) {
         KL(nb_dec_plan(d, c, st));
         KL(nb_dec_gather(d, m->embed, PH, g->blank_id, st));
-        nemo_gemm_args_t a = gemm_args(d->A0, 2 * PH, NEMO_FMT_F32, 0, m->lstm_w[0], 2 * PH, m->lstm_b[0], d->gates, 4 * PH, B, 4 * PH, 2 * PH, 0, 0, 1.0f);
+        nemo_gemm_args_t a = gemm_args(d->A0, 2 * PH, d->fmt, d->a_plane, m->lstm_w[0], 2 * PH, m->lstm_b[0], d->gates, 4 * PH, B, 4 * PH, 2 * PH, 0, 0, 1.0f);
         a.dynM = d->cnt;
         KL(nemo_gemm(&a, st));
-        KL(nb_dec_cell(d, 0, PH, d->A1, 2 * PH, st));
-        a = gemm_args(d->A1, 2 * PH, NEMO_FMT_F32, 0, m->lstm_w[1], 2 * PH, m->lstm_b[1], d->gates, 4 * PH, B, 4 * PH, 2 * PH, 0, 0, 1.0f);
+        KL(nb_dec_cell(d, 0, PH, d->A1, 2 * PH, d->a_plane, st));
+        a = gemm_args(d->A1, 2 * PH, d->fmt, d->a_plane, m->lstm_w[1], 2 * PH, m->lstm_b[1], d->gates, 4 * PH, B, 4 * PH, 2 * PH, 0, 0, 1.0f);
         a.dynM = d->cnt;
         KL(nemo_gemm(&a, st));
-        KL(nb_dec_cell(d, 1, PH, d->hp1c, PH, st));
-        a = gemm_args(d->hp1c, PH, NEMO_FMT_F32, 0, m->joint_pred_w, PH, m->joint_pred_b, d->predc, JH, B, JH, PH, 0, 0, 1.0f);
+        KL(nb_dec_cell(d, 1, PH, d->hp1c, PH, d->h_plane, st));
+        a = gemm_args(d->hp1c, PH, d->fmt, d->h_plane, m->joint_pred_w, PH, m->joint_pred_b, d->predc, JH, B, JH, PH, 0, 0, 1.0f);
         a.dynM = d->cnt;
         KL(nemo_gemm(&a, st));
         KL(nb_dec_scatter_pred(d, JH, st));
@@ -443,6 +454,7 @@ int nb_engine_step(nb_engine_t *e, int final, int *tokens, int max_tokens, int *
     }
     if (launch_encoder(e, nwin, c)) { snprintf(err, errlen, "encoder: %s", nemo_gpu_last_error()); return -1; }
     if (cudaStreamSynchronize(st) != cudaSuccess) { snprintf(err, errlen, "encoder: %s", cudaGetErrorString(cudaGetLastError())); return -1; }
+    if (nemo_gpu_check_device_errors()) { snprintf(err, errlen, "encoder: %s", nemo_gpu_last_error()); return -1; }
     const double t1 = nb_now_ms();
     e->pos += c;
     const int L = e->cache_len + c;

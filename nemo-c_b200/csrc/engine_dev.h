@@ -15,6 +15,8 @@ typedef struct {
     float *h, *c, *hp, *cp;           /* [2][streams][PH] committed / provisional LSTM state */
     float *pred;                      /* [streams][JH] joint prediction projection */
     float *A0, *A1, *gates, *hp1c, *predc; /* compact per-iteration work rows */
+    int fmt;                          /* format of A0 / A1 / hp1c (GEMM inputs): fp32 or bf16 hi/lo planes */
+    int64_t a_plane, h_plane;         /* plane offsets (elements) of A0/A1 and of hp1c */
 } DecState;
 
 int nb_compact(float *kv, float *din, int layers, int streams, int64_t cap, int D, int src_kv, int cache_len, int src_din, int dst_din,
@@ -22,7 +24,7 @@ int nb_compact(float *kv, float *din, int layers, int streams, int64_t cap, int 
 int nb_dec_chunk_init(const DecState *d, int c, void *stream);
 int nb_dec_plan(const DecState *d, int c, void *stream);
 int nb_dec_gather(const DecState *d, const uint16_t *embed, int PH, int blank, void *stream);
-int nb_dec_cell(const DecState *d, int layer, int PH, float *next, int64_t next_ld, void *stream);
+int nb_dec_cell(const DecState *d, int layer, int PH, float *next, int64_t next_ld, int64_t next_plane, void *stream);
 int nb_dec_scatter_pred(const DecState *d, int JH, void *stream);
 int nb_dec_update(const DecState *d, int c, int PH, int blank, int max_symbols, void *stream);
 int nb_dec_reset(const DecState *d, int PH, int blank, void *stream);

@@ -57,18 +57,18 @@ __global__ void dec_gather_kernel(DecState d, const uint16_t *__restrict__ embed
     if (i >= d.cnt[0]) return;
     const int b = d.need_idx[i];
     const int tok = d.last_token[b];
-    float *a0 = d.A0 + (int64_t)i * 2 * PH, *a1 = d.A1 + (int64_t)i * 2 * PH;
     const float *h0 = d.h + (int64_t)b * PH, *h1 = d.h + ((int64_t)d.streams + b) * PH;
+    const int64_t r0 = (int64_t)i * 2 * PH;
     for (int j = threadIdx.x; j < PH; j += blockDim.x) {
-        a0[j] = tok == blank ? 0.0f : nb::bf2f(embed[(int64_t)tok * PH + j]);
-        a0[PH + j] = h0[j];
-        a1[PH + j] = h1[j];
+        nb::store_act(d.A0, d.fmt, d.a_plane, r0 + j, tok == blank ? 0.0f : nb::bf2f(embed[(int64_t)tok * PH + j]));
+        nb::store_act(d.A0, d.fmt, d.a_plane, r0 + PH + j, h0[j]);
+        nb::store_act(d.A1, d.fmt, d.a_plane, r0 + PH + j, h1[j]);
     }
 }
 
 // LSTM cell (src/kernels.metal:475-486) from the committed cell state into the provisional
 // state of each listed stream; h' also goes to `next` (the following GEMM's input row).
-__global__ void dec_cell_kernel(DecState d, int layer, int PH, float *next, int64_t next_ld) {
+__global__ void dec_cell_kernel(DecState d, int layer, int PH, float *next, int64_t next_ld, int64_t next_plane) {
     const int i = blockIdx.x;
     if (i >= d.cnt[0]) return;
     const int b = d.need_idx[i];
@@ -80,7 +80,7 @@ __global__ void dec_cell_kernel(DecState d, int layer, int PH, float *next, int6
         const float hh = og * tanhf(cc);
         d.cp[sb + j] = cc;
         d.hp[sb + j] = hh;
-        next[(int64_t)i * next_ld + j] = hh;
+        nb::store_act(next, d.fmt, next_plane, (int64_t)i * next_ld + j, hh);
     }
 }
 
@@ -152,8 +152,8 @@ extern "C" int nb_dec_gather(const DecState *d, const uint16_t *embed, int PH, i
     dec_gather_kernel<<<d->streams, 128, 0, (cudaStream_t)stream>>>(*d, embed, PH, blank);
     return nb_check_launch("dec_gather_kernel");
 }
-extern "C" int nb_dec_cell(const DecState *d, int layer, int PH, float *next, int64_t next_ld, void *stream) {
-    dec_cell_kernel<<<d->streams, 128, 0, (cudaStream_t)stream>>>(*d, layer, PH, next, next_ld);
+extern "C" int nb_dec_cell(const DecState *d, int layer, int PH, float *next, int64_t next_ld, int64_t next_plane, void *stream) {
+    dec_cell_kernel<<<d->streams, 128, 0, (cudaStream_t)stream>>>(*d, layer, PH, next, next_ld, next_plane);
     return nb_check_launch("dec_cell_kernel");
 }
 extern "C" int nb_dec_scatter_pred(const DecState *d, int JH, void *stream) {

@@ -6,41 +6,15 @@
 //   M  > 16 : tensor-core tiles (k_gemm_tc.cu) when A is in bf16 hi/lo planes, else a shared-
 //             memory tiled CUDA-core kernel.
 #include <cstdio>
-#include "common.cuh"
+#include "gemm_epi.cuh"
 
 int nb_gemm_tc(const nemo_gemm_args_t *a, void *stream);  // k_gemm_tc.cu
-int nb_gemm_tc_supported(const nemo_gemm_args_t *a);
 
 namespace {
 
-struct Epi {
-    const float *bias;
-    int64_t bias_gstride;
-    void *C;
-    int64_t ldc, c_plane, gstride;
-    int c_fmt, rpg, act, accumulate;
-    float alpha;
-};
-
-// Epilogue order bias -> act -> *alpha -> store/accumulate (src/kernels.metal:39-44, 106-114);
-// GLU takes a * sigmoid(b) (src/kernels.metal:96-104).
-__device__ __forceinline__ void epilogue(const Epi &e, int rowoff, int m, int n, int nb, float va, float vb) {
-    const int g = m / e.rpg, r = m - g * e.rpg;
-    const float *bias = e.bias ? e.bias + (int64_t)g * e.bias_gstride : nullptr;
-    float v;
-    if (e.act == NEMO_ACT_GLU) {
-        if (bias) { va += bias[n]; vb += bias[nb]; }
-        v = va * nb::sigmoid_f(vb) * e.alpha;
-    } else {
-        v = va + (bias ? bias[n] : 0.0f);
-        if (e.act == NEMO_ACT_SILU) v = nb::silu_f(v);
-        else if (e.act == NEMO_ACT_RELU) v = fmaxf(v, 0.0f);
-        v *= e.alpha;
-    }
-    const int64_t idx = (int64_t)g * e.gstride + (int64_t)(rowoff + r) * e.ldc + n;
-    if (e.accumulate) v += ((const float *)e.C)[idx];
-    nb::store_act(e.C, e.c_fmt, e.c_plane, idx, v);
-}
+using nb::Epi;
+using nb::epilogue;
+using nb::make_epi;
 
 // ---- M <= 16: weight streaming, one warp per output column (pair for GLU) ----------------
 template <int MB>
@@ -150,22 +124,6 @@ static int validate(const nemo_gemm_args_t *a) {
     if (a->act == NEMO_ACT_GLU && (a->N & 1)) return nb_set_error("nemo_gemm: GLU needs an even N");
     if (a->accumulate && a->c_fmt != NEMO_FMT_F32) return nb_set_error("nemo_gemm: accumulate needs an fp32 output");
     return 0;
-}
-
-static Epi make_epi(const nemo_gemm_args_t *a) {
-    Epi e;
-    e.bias = a->bias;
-    e.bias_gstride = a->bias_gstride;
-    e.C = a->C;
-    e.ldc = a->ldc;
-    e.c_plane = a->c_plane;
-    e.gstride = a->gstride;
-    e.c_fmt = a->c_fmt;
-    e.rpg = a->rpg > 0 ? a->rpg : (a->M > 0 ? a->M : 1);
-    e.act = a->act;
-    e.accumulate = a->accumulate;
-    e.alpha = a->alpha;
-    return e;
 }
 
 static int launch_ws(const nemo_gemm_args_t *a, cudaStream_t st) {

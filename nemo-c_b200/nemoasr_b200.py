@@ -33,9 +33,9 @@ class GemmArgs(C.Structure):  # nemo_gemm_args_t
     _fields_ = [("A", C.c_void_p), ("lda", C.c_int64), ("a_plane", C.c_int64), ("a_fmt", C.c_int),
                 ("W", C.c_void_p), ("ldw", C.c_int64), ("bias", C.c_void_p), ("bias_gstride", C.c_int64),
                 ("C", C.c_void_p), ("ldc", C.c_int64), ("c_plane", C.c_int64), ("c_fmt", C.c_int),
-                ("rpg", C.c_int), ("gstride", C.c_int64), ("rowoff", C.c_void_p),
+                ("rpg", C.c_int), ("gstride", C.c_int64), ("rowoff", C.c_void_p), ("dynM", C.c_void_p),
                 ("M", C.c_int), ("N", C.c_int), ("K", C.c_int), ("act", C.c_int), ("accumulate", C.c_int),
-                ("alpha", C.c_float)]
+                ("alpha", C.c_float), ("c32", C.c_void_p), ("ldc32", C.c_int64)]
 
 
 def lib():

@@ -1,0 +1,67 @@
+"""The tcgen05 tensor-core GEMM (activations as bf16 hi/lo planes) against the oracle GEMM, for
+row counts from a single stream (split-K weight streaming) to large batches, every epilogue."""
+import numpy as np
+import pytest
+
+import oracle as orc
+from parity import rel_err
+from test_gpu_kernels import BF16X2_TOL, bf16, run_gemm
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("M", [1, 7, 16, 17, 40, 64, 100, 128, 200, 600])
+@pytest.mark.parametrize("act", [0, 1, 2, 3])
+def test_tc_gemm_epilogues(M, act):
+    rng = np.random.default_rng(1000 + M * 4 + act)
+    N, K = 256, 320
+    A = rng.standard_normal((M, K)).astype(np.float32)
+    W = bf16(rng, (N, K))
+    b = (rng.standard_normal(N) * 0.1).astype(np.float32)
+    C0 = rng.standard_normal((M, N // 2 if act == 3 else N)).astype(np.float32)
+    got = run_gemm(A, W, b, C0, act=act, acc=1, alpha=0.5, kind=2, a_fmt=1)
+    ref = orc.gemm(A, W, b, C0=C0, act=act, accumulate=True, alpha=0.5)
+    assert rel_err(got, ref) < BF16X2_TOL
+
+
+@pytest.mark.parametrize("M", [7, 14, 1792])
+@pytest.mark.parametrize("shape", [(3072, 1024), (4096, 1024), (1024, 4096), (2048, 1024), (640, 1024), (2560, 1280), (1024, 4352)])
+def test_tc_gemm_model_shapes(M, shape):
+    rng = np.random.default_rng(M + sum(shape))
+    N, K = shape
+    A = rng.standard_normal((M, K)).astype(np.float32)
+    W = bf16(rng, (N, K), 0.02)
+    got = run_gemm(A, W, kind=2, a_fmt=1)
+    assert rel_err(got, orc.gemm(A, W)) < BF16X2_TOL
+
+
+def test_tc_gemm_glu_model_shape():
+    rng = np.random.default_rng(77)
+    A = rng.standard_normal((7, 1024)).astype(np.float32)
+    W = bf16(rng, (2048, 1024), 0.02)
+    got = run_gemm(A, W, act=3, kind=2, a_fmt=1)
+    assert rel_err(got, orc.gemm(A, W, act=3)) < BF16X2_TOL
+
+
+def test_tc_gemm_row_mapping_dynamic_rows():
+    rng = np.random.default_rng(19)
+    streams, c, N, K, cap, off = 6, 7, 256, 256, 30, 9
+    A = rng.standard_normal((streams * c, K)).astype(np.float32)
+    W = bf16(rng, (N, K))
+    bias = rng.standard_normal((streams, N)).astype(np.float32)
+    got = run_gemm(A, W, bias.ravel(), kind=2, a_fmt=1, rpg=c, gstride=cap * N, rowoff=off, crows=streams * cap, bias_gstride=N)
+    got = got.reshape(streams, cap, N)
+    for s in range(streams):
+        assert rel_err(got[s, off:off + c], orc.gemm(A[s * c:(s + 1) * c], W, bias[s])) < BF16X2_TOL
+        assert np.all(got[s, :off] == 0) and np.all(got[s, off + c:] == 0)
+    got = run_gemm(A[:20], W, kind=2, a_fmt=1, dynM=5)
+    assert rel_err(got[:5], orc.gemm(A[:5], W)) < BF16X2_TOL and np.all(got[5:] == 0)
+
+
+def test_tc_gemm_is_deterministic():
+    rng = np.random.default_rng(5)
+    A = rng.standard_normal((7, 4096)).astype(np.float32)
+    W = bf16(rng, (1024, 4096), 0.02)
+    a = run_gemm(A, W, kind=2, a_fmt=1)
+    b = run_gemm(A, W, kind=2, a_fmt=1)
+    assert np.array_equal(a, b)

@@ -25,8 +25,23 @@ def host(t):
     return t.cpu().numpy()
 
 
+_keep = []
+
+
 def p(t):
-    return C.c_void_p(t.data_ptr()) if t is not None else None
+    """Device pointer of t; t stays referenced until the test ends (a temporary tensor would be
+    freed, and its memory reused, before the kernel runs)."""
+    if t is None:
+        return None
+    _keep.append(t)
+    return C.c_void_p(t.data_ptr())
+
+
+@pytest.fixture(autouse=True)
+def _release_buffers():
+    yield
+    torch.cuda.synchronize()
+    _keep.clear()
 
 
 def bf16(rng, shape, std=0.05):
