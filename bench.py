@@ -121,11 +121,11 @@ def dominant_gemm(nb, torch, a, B, c):
     (more than L2 holds)."""
     import ctypes as C
     M, N, K = B * c, 4096, 1024
-    A = torch.randn(M, K, device="cuda", dtype=torch.float32)
+    A = torch.randn(2 * M, K, device="cuda", dtype=torch.float32).to(torch.bfloat16)  # hi and lo planes
     Ws = [torch.randint(0, 1 << 15, (N, K), device="cuda", dtype=torch.int16) & 0x3C7F for _ in range(24)]
     Cm = torch.empty(M, N, device="cuda", dtype=torch.float32)
     args = nb.GemmArgs()
-    args.A, args.lda, args.a_fmt = A.data_ptr(), K, 0
+    args.A, args.lda, args.a_fmt, args.a_plane = A.data_ptr(), K, 1, M * K
     args.ldw, args.C, args.ldc, args.M, args.N, args.K, args.act, args.alpha = K, Cm.data_ptr(), N, M, N, K, 1, 1.0
     st = torch.cuda.current_stream()
     for w in Ws[:3]:

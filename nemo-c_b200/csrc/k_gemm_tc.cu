@@ -11,8 +11,11 @@
 // the fp32 activations (bf16 weights are exact). Split-K partial tiles are reduced by the last
 // CTA of each tile in a fixed order, so results do not depend on scheduling.
 //
-// Warp roles (192 threads): warp 0 issues TMA loads, warp 1 owns TMEM and issues the MMAs,
-// warps 2-5 run the epilogue (warp w reads TMEM lanes 32*(w%4) .. +31). Every wait is bounded.
+// Persistent: one CTA per SM walks a strided list of work units (tile, k-split). The TMEM
+// accumulator is double-buffered, so the epilogue of one unit runs while the MMAs of the next
+// proceed. Warp roles (320 threads): warp 0 issues TMA loads, warp 1 owns TMEM and issues the
+// MMAs, warps 2-9 run the epilogue (warp w reads TMEM lanes 32*(w%4) .. +31; warps w and w+4
+// split the columns). Every wait is bounded: on a timeout the CTA records an error and unwinds.
 #include <cuda.h>
 #include <cstdio>
 #include <cstring>
@@ -25,12 +28,13 @@ namespace {
 constexpr int BM = 128;  // weight rows per tile (MMA M)
 constexpr int BK = 64;   // k per stage: 128 bytes of bf16 = one swizzle span
 constexpr int W_STAGE = BM * BK * 2;
-constexpr int THREADS = 192;
+constexpr int EPI_WARPS = 8;
+constexpr int THREADS = 64 + 32 * EPI_WARPS;
 
 __device__ int g_tc_error;  // set when a bounded wait gave up (host reads it back)
 
 struct TcArgs {
-    int M, N, K, kblocks, splits, kb_per_split, n_wtiles, n_mtiles, glu;
+    int M, N, K, kblocks, splits, kb_per_split, n_wtiles, n_mtiles, units, glu;
     const int *dynM, *rowoff;
     nb::Epi e;
     float *ws;     // split-K partial tiles
@@ -42,40 +46,83 @@ struct Cfg {
     static constexpr int A_STAGE = BN * BK * 2;                 // one activation plane
     static constexpr int STAGE = W_STAGE + 2 * A_STAGE;
     static constexpr int STAGES = BN <= 32 ? 8 : BN <= 64 ? 6 : BN <= 128 ? 4 : 2;
-    static constexpr int TMEM_COLS = BN < 32 ? 32 : BN;
-    static constexpr int SMEM = 1024 + STAGES * STAGE + 1024 + 64 * 16 * 4;
+    static constexpr int TMEM_COLS = 2 * BN < 32 ? 32 : 2 * BN; // two accumulator buffers
+    static constexpr int HALF = BN >= 32 ? BN / 2 : BN;        // columns per epilogue warp
+    static constexpr int XCH = 2 * 16 * 64;                     // GLU exchange, two halves [16][64]
+    // stages | barriers (1 KB) | GLU exchange | per-row output offsets | per-row bias offsets
+    static constexpr int SMEM = 1024 + STAGES * STAGE + 1024 + XCH * 4 + BN * 12;
 };
+
+__device__ __forceinline__ float fast_sigmoid(float x) { return __frcp_rn(1.0f + __expf(-x)); }
+
+// Epilogue for one 16-row chunk of one weight row: va[jj] belongs to activation row m0+j0+jj and
+// output column n. Row offsets (group stride, in-group row offset, ldc) were precomputed once
+// per unit; branches are uniform across the warp.
+__device__ __forceinline__ void epi_chunk(const nb::Epi &e, const int64_t *__restrict__ rowbase, const int *__restrict__ brow, int m0, int j0,
+                                          int mcount, int n, int nb_, const float (&va)[16], const float *vb, float bias_a, float bias_b,
+                                          bool row_bias) {
+    float *__restrict__ C32 = (float *)e.C;
+    uint16_t *__restrict__ C16 = (uint16_t *)e.C;
+#pragma unroll
+    for (int jj = 0; jj < 16; ++jj) {
+        const int ml = j0 + jj;
+        if (ml >= mcount) break;
+        float ba = bias_a, bb = bias_b;
+        if (row_bias) {
+            ba = e.bias[brow[ml] + n];
+            if (vb) bb = e.bias[brow[ml] + nb_];
+        }
+        float v;
+        if (vb) {
+            v = (va[jj] + ba) * fast_sigmoid(vb[jj] + bb) * e.alpha;
+        } else {
+            v = va[jj] + ba;
+            if (e.act == NEMO_ACT_SILU) v = v * fast_sigmoid(v);
+            else if (e.act == NEMO_ACT_RELU) v = fmaxf(v, 0.0f);
+            v *= e.alpha;
+        }
+        const int64_t idx = rowbase[ml] + n;
+        if (e.accumulate) v += C32[idx];
+        if (e.c_fmt == NEMO_FMT_F32) {
+            C32[idx] = v;
+        } else {
+            const uint16_t hi = nb::f2bf(v);
+            C16[idx] = hi;
+            C16[idx + e.c_plane] = nb::f2bf(v - nb::bf2f(hi));
+        }
+        if (e.c32) e.c32[(int64_t)(m0 + ml) * e.ldc32 + n] = v;
+    }
+}
 
 template <int BN>
 __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmAh,
-                                                           const __grid_constant__ CUtensorMap tmAl, const TcArgs p) {
+                                                           const __grid_constant__ CUtensorMap tmAl, const __grid_constant__ TcArgs p) {
     using C = Cfg<BN>;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     uint8_t *stages = smem;
     uint64_t *full = (uint64_t *)(smem + C::STAGES * C::STAGE);
     uint64_t *empty = full + C::STAGES;
-    uint64_t *done = empty + C::STAGES;
-    uint32_t *tmem_holder = (uint32_t *)(done + 1);
-    volatile int *flags = (volatile int *)(tmem_holder + 1); // [0] abort, [1] last-split
-    float *xch = (float *)(smem + C::STAGES * C::STAGE + 1024); // GLU exchange [16][64]
+    uint64_t *acc_full = empty + C::STAGES;  // [2] MMA -> epilogue: accumulator buffer ready
+    uint64_t *acc_empty = acc_full + 2;      // [2] epilogue -> MMA: accumulator buffer drained
+    uint32_t *tmem_holder = (uint32_t *)(acc_empty + 2);
+    volatile int *flags = (volatile int *)(tmem_holder + 1); // [0] abort, [1] last split of the unit, [2] epilogue abort
+    float *xch = (float *)(smem + C::STAGES * C::STAGE + 1024);
+    int64_t *rowbase = (int64_t *)(xch + C::XCH);
+    int *brow = (int *)(rowbase + BN);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int split = blockIdx.x % p.splits, tile = blockIdx.x / p.splits;
-    const int wt = tile % p.n_wtiles, mt = tile / p.n_wtiles;
-    const int kb0 = split * p.kb_per_split;
-    const int kb1 = min(p.kblocks, kb0 + p.kb_per_split);
-    const int nk = kb1 - kb0;
-
     nb::pdl_wait();
     const int M = p.dynM ? min(p.M, *p.dynM) : p.M;
-    if (mt * BN >= M || nk <= 0) return; // whole CTA leaves before touching TMEM or barriers
+    const int live_mtiles = (M + BN - 1) / BN;            // row tiles that hold real rows
+    const int units = live_mtiles * p.n_wtiles * p.splits;
+    if ((int)blockIdx.x >= units) return;                  // nothing for this CTA
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < C::STAGES; ++s) { sm100::mbar_init(&full[s], 1); sm100::mbar_init(&empty[s], 1); }
-        sm100::mbar_init(done, 1);
+        for (int b = 0; b < 2; ++b) { sm100::mbar_init(&acc_full[b], 1); sm100::mbar_init(&acc_empty[b], 1); }
         flags[0] = 0;
-        flags[1] = 0;
+        flags[2] = 0;
         sm100::fence_mbar_init();
         sm100::tma_prefetch_desc(&tmW);
         sm100::tma_prefetch_desc(&tmAh);
@@ -92,102 +139,146 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
 
     if (warp == 0 && lane == 0) {
         // ---- producer: weight tile (two 64-row halves for GLU) + activation hi/lo tiles ----
-        for (int i = 0; i < nk; ++i) {
-            const int s = i % C::STAGES;
-            if (i >= C::STAGES && !sm100::mbar_wait(&empty[s], ((i / C::STAGES) - 1) & 1)) { flags[0] = 1; atomicExch(&g_tc_error, 1); break; }
-            if (flags[0]) break;
-            uint8_t *st = stages + s * C::STAGE;
-            const int k0 = (kb0 + i) * BK;
-            sm100::mbar_arrive_expect_tx(&full[s], C::STAGE);
-            if (p.glu) {
-                sm100::tma_load_2d(st, &tmW, &full[s], k0, wt * 64);
-                sm100::tma_load_2d(st + W_STAGE / 2, &tmW, &full[s], k0, p.N / 2 + wt * 64);
-            } else {
-                sm100::tma_load_2d(st, &tmW, &full[s], k0, wt * BM);
+        int i = 0; // k-blocks issued by this CTA (ring position)
+        for (int u = blockIdx.x; u < units && !flags[0]; u += gridDim.x) {
+            const int split = u % p.splits, tile = u / p.splits, wt = tile % p.n_wtiles, mt = tile / p.n_wtiles;
+            const int kb0 = split * p.kb_per_split, kb1 = min(p.kblocks, kb0 + p.kb_per_split);
+            for (int kb = kb0; kb < kb1; ++kb, ++i) {
+                const int s = i % C::STAGES;
+                if (i >= C::STAGES && !sm100::mbar_wait(&empty[s], ((i / C::STAGES) - 1) & 1)) { flags[0] = 1; atomicExch(&g_tc_error, 1); break; }
+                if (flags[0]) break;
+                uint8_t *st = stages + s * C::STAGE;
+                const int k0 = kb * BK;
+                sm100::mbar_arrive_expect_tx(&full[s], C::STAGE);
+                if (p.glu) {
+                    sm100::tma_load_2d(st, &tmW, &full[s], k0, wt * 64);
+                    sm100::tma_load_2d(st + W_STAGE / 2, &tmW, &full[s], k0, p.N / 2 + wt * 64);
+                } else {
+                    sm100::tma_load_2d(st, &tmW, &full[s], k0, wt * BM);
+                }
+                sm100::tma_load_2d(st + W_STAGE, &tmAh, &full[s], k0, mt * BN);
+                sm100::tma_load_2d(st + W_STAGE + C::A_STAGE, &tmAl, &full[s], k0, mt * BN);
             }
-            sm100::tma_load_2d(st + W_STAGE, &tmAh, &full[s], k0, mt * BN);
-            sm100::tma_load_2d(st + W_STAGE + C::A_STAGE, &tmAl, &full[s], k0, mt * BN);
         }
     } else if (warp == 1 && lane == 0) {
-        // ---- MMA issuer ----
+        // ---- MMA issuer: one accumulator buffer per unit, alternating ----
         constexpr uint32_t idesc = sm100::idesc_bf16_f32(BM, BN);
-        for (int i = 0; i < nk; ++i) {
-            const int s = i % C::STAGES;
-            if (!sm100::mbar_wait(&full[s], (i / C::STAGES) & 1)) { flags[0] = 1; atomicExch(&g_tc_error, 2); break; }
+        int i = 0, t = 0;
+        for (int u = blockIdx.x; u < units && !flags[0]; u += gridDim.x, ++t) {
+            const int split = u % p.splits;
+            const int kb0 = split * p.kb_per_split, kb1 = min(p.kblocks, kb0 + p.kb_per_split);
+            const int b = t & 1;
+            if (t >= 2 && !sm100::mbar_wait(&acc_empty[b], ((t >> 1) - 1) & 1)) { flags[0] = 1; atomicExch(&g_tc_error, 4); break; }
             sm100::tc_fence_after();
-            const uint32_t w_addr = sm100::smem_u32(stages + s * C::STAGE);
-            const uint32_t h_addr = w_addr + W_STAGE, l_addr = h_addr + C::A_STAGE;
+            const uint32_t dacc = tmem + (uint32_t)(b * BN);
+            for (int kb = kb0; kb < kb1; ++kb, ++i) {
+                const int s = i % C::STAGES;
+                if (!sm100::mbar_wait(&full[s], (i / C::STAGES) & 1)) { flags[0] = 1; atomicExch(&g_tc_error, 2); break; }
+                sm100::tc_fence_after();
+                const uint32_t w_addr = sm100::smem_u32(stages + s * C::STAGE);
+                const uint32_t h_addr = w_addr + W_STAGE, l_addr = h_addr + C::A_STAGE;
 #pragma unroll
-            for (int kk = 0; kk < BK / 16; ++kk) {
-                const uint64_t ad = sm100::desc_k_sw128(w_addr + kk * 32);
-                sm100::mma_bf16(tmem, ad, sm100::desc_k_sw128(h_addr + kk * 32), idesc, (i | kk) != 0);
-                sm100::mma_bf16(tmem, ad, sm100::desc_k_sw128(l_addr + kk * 32), idesc, 1);
+                for (int kk = 0; kk < BK / 16; ++kk) {
+                    const uint64_t ad = sm100::desc_k_sw128(w_addr + kk * 32);
+                    sm100::mma_bf16(dacc, ad, sm100::desc_k_sw128(h_addr + kk * 32), idesc, (kb != kb0 || kk != 0) ? 1u : 0u);
+                    sm100::mma_bf16(dacc, ad, sm100::desc_k_sw128(l_addr + kk * 32), idesc, 1u);
+                }
+                sm100::mma_commit(&empty[s]);
             }
-            sm100::mma_commit(&empty[s]);
+            sm100::mma_commit(&acc_full[b]);
         }
-        sm100::mma_commit(done);
     } else if (warp >= 2) {
         // ---- epilogue: TMEM -> registers -> (split-K reduce) -> fused epilogue -> global ----
-        const int q = warp & 3;               // TMEM lane quarter this warp may access
-        const int row = q * 32 + lane;        // weight row inside the tile
-        const int etid = threadIdx.x - 64;    // 0..127
-        const bool ok = sm100::mbar_wait(done, 0);
-        if (!ok) { flags[0] = 1; atomicExch(&g_tc_error, 3); }
-        sm100::tc_fence_after();
-        const int rowoff = p.rowoff ? *p.rowoff : 0;
+        const int ew = warp - 2;                 // 0..7
+        const int q = warp & 3;                  // TMEM lane quarter this warp may access
+        const int half = ew >> 2;                // which half of the columns
+        const int row = q * 32 + lane;           // weight row inside the tile
+        const int etid = threadIdx.x - 64;       // 0..255
         const int nout = p.glu ? p.N / 2 : p.N;
-        float *wsb = p.ws + (int64_t)tile * p.splits * BN * BM;
-        if (ok && p.splits > 1) {
-            for (int j0 = 0; j0 < BN; j0 += 16) {
-                float v[16];
-                sm100::tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + j0, v);
-#pragma unroll
-                for (int jj = 0; jj < 16; ++jj) wsb[((int64_t)split * BN + j0 + jj) * BM + row] = v[jj];
+        const bool has_half = half * C::HALF < BN;
+        const int jbeg = half * C::HALF, jend = has_half ? jbeg + C::HALF : jbeg;
+        float *xh = xch + half * 16 * 64;
+        const bool row_bias = p.e.bias && p.e.bias_gstride != 0;
+        const int rowoff = p.rowoff ? *p.rowoff : 0;
+        int t = 0;
+        for (int u = blockIdx.x; u < units; u += gridDim.x, ++t) {
+            const int split = u % p.splits, tile = u / p.splits, wt = tile % p.n_wtiles, mt = tile / p.n_wtiles;
+            const int b = t & 1;
+            const int m0 = mt * BN, mcount = min(BN, M - m0);
+            // output row offsets of this unit (computed while its MMAs run)
+            sm100::named_barrier(1, 256);        // the previous unit is done with rowbase/brow
+            for (int ml = etid; ml < BN; ml += 256) {
+                const int m = m0 + ml, g = m / p.e.rpg, r = m - g * p.e.rpg;
+                rowbase[ml] = (int64_t)g * p.e.gstride + (int64_t)(rowoff + r) * p.e.ldc;
+                brow[ml] = (int)((int64_t)g * p.e.bias_gstride);
             }
-            __threadfence();
-            sm100::named_barrier(1, 128);
-            if (etid == 0) flags[1] = atomicAdd(&p.counters[tile], 1) == p.splits - 1;
-            sm100::named_barrier(1, 128);
-        }
-        const bool finish = ok && (p.splits == 1 || flags[1]);
-        if (finish) {
-            if (p.splits > 1) __threadfence();
-            for (int j0 = 0; j0 < BN; j0 += 16) {
-                float v[16];
-                if (p.splits == 1) {
-                    sm100::tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + j0, v);
-                } else {
+            const int ncol = p.glu ? wt * 64 + row : wt * BM + row;
+            const bool col_ok = ncol < nout && (!p.glu || row < 64);
+            float bias_a = 0.0f, bias_b = 0.0f;
+            if (p.e.bias && !row_bias && col_ok) {
+                bias_a = p.e.bias[ncol];
+                if (p.glu) bias_b = p.e.bias[ncol + p.N / 2];
+            }
+            if (!sm100::mbar_wait(&acc_full[b], (t >> 1) & 1)) { flags[2] = 1; flags[0] = 1; atomicExch(&g_tc_error, 3); }
+            // flags[2] is written only by epilogue threads before this barrier: every epilogue
+            // thread takes the same decision (a divergent exit would strand the others)
+            sm100::named_barrier(1, 256);
+            const bool ok = !flags[2];
+            sm100::tc_fence_after();
+            const uint32_t tacc = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(b * BN);
+            float *wsb = p.ws + (int64_t)tile * p.splits * BN * BM;
+            bool finish = ok;
+            if (ok && p.splits > 1) {
+                for (int j0 = jbeg; j0 < jend; j0 += 16) {
+                    float v[16];
+                    sm100::tmem_ld16(tacc + j0, v);
 #pragma unroll
-                    for (int jj = 0; jj < 16; ++jj) v[jj] = 0.0f;
-                    for (int s = 0; s < p.splits; ++s)
-#pragma unroll
-                        for (int jj = 0; jj < 16; ++jj) v[jj] += __ldcg(&wsb[((int64_t)s * BN + j0 + jj) * BM + row]);
+                    for (int jj = 0; jj < 16; ++jj) wsb[((int64_t)split * BN + j0 + jj) * BM + row] = v[jj];
                 }
-                if (p.glu) {
-                    // rows 64..127 hold the gate halves (columns n + N/2): hand them over
-                    if (row >= 64)
+                __threadfence();
+                sm100::named_barrier(1, 256);
+                if (etid == 0) flags[1] = atomicAdd(&p.counters[tile], 1) == p.splits - 1;
+                sm100::named_barrier(1, 256);
+                finish = flags[1];
+                if (finish) __threadfence();
+            }
+            if (finish) {
+                for (int j0 = jbeg; j0 < jend; j0 += 16) {
+                    if (j0 >= mcount) break;
+                    float v[16];
+                    if (p.splits == 1) {
+                        sm100::tmem_ld16(tacc + j0, v);
+                    } else {
 #pragma unroll
-                        for (int jj = 0; jj < 16; ++jj) xch[jj * 64 + row - 64] = v[jj];
-                    sm100::named_barrier(1, 128);
-                    if (row < 64) {
-                        const int n = wt * 64 + row;
+                        for (int jj = 0; jj < 16; ++jj) v[jj] = 0.0f;
+                        for (int s = 0; s < p.splits; ++s)
 #pragma unroll
-                        for (int jj = 0; jj < 16; ++jj) {
-                            const int m = mt * BN + j0 + jj;
-                            if (m < M && n < nout) nb::epilogue(p.e, rowoff, m, n, n + p.N / 2, v[jj], xch[jj * 64 + row]);
+                            for (int jj = 0; jj < 16; ++jj) v[jj] += __ldcg(&wsb[((int64_t)s * BN + j0 + jj) * BM + row]);
+                    }
+                    if (p.glu) {
+                        // rows 64..127 hold the gate halves (columns n + N/2): hand them over
+                        if (row >= 64)
+#pragma unroll
+                            for (int jj = 0; jj < 16; ++jj) xh[jj * 64 + row - 64] = v[jj];
+                        sm100::named_barrier(2 + half, 128);
+                        if (col_ok) {
+                            float vb[16];
+#pragma unroll
+                            for (int jj = 0; jj < 16; ++jj) vb[jj] = xh[jj * 64 + row];
+                            epi_chunk(p.e, rowbase, brow, m0, j0, mcount, ncol, ncol + p.N / 2, v, vb, bias_a, bias_b, row_bias);
                         }
-                    }
-                    sm100::named_barrier(1, 128);
-                } else {
-                    const int n = wt * BM + row;
-#pragma unroll
-                    for (int jj = 0; jj < 16; ++jj) {
-                        const int m = mt * BN + j0 + jj;
-                        if (m < M && n < nout) nb::epilogue(p.e, rowoff, m, n, 0, v[jj], 0.0f);
+                        sm100::named_barrier(2 + half, 128);
+                    } else if (col_ok) {
+                        epi_chunk(p.e, rowbase, brow, m0, j0, mcount, ncol, 0, v, nullptr, bias_a, 0.0f, row_bias);
                     }
                 }
+                if (p.splits > 1 && etid == 0) p.counters[tile] = 0; // ready for the next launch
             }
-            if (p.splits > 1 && etid == 0) p.counters[tile] = 0; // ready for the next launch
+            // this accumulator buffer may be overwritten by the unit after next
+            sm100::tc_fence_before();
+            sm100::named_barrier(1, 256);
+            if (etid == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(sm100::smem_u32(&acc_empty[b])) : "memory");
+            if (!ok) break;
         }
     }
     sm100::tc_fence_before();
@@ -272,12 +363,14 @@ int launch(const nemo_gemm_args_t *a, cudaStream_t st) {
     }
     p.kb_per_split = (p.kblocks + splits - 1) / splits;
     p.splits = (p.kblocks + p.kb_per_split - 1) / p.kb_per_split; // every split non-empty
+    p.units = tiles * p.splits;
     p.dynM = a->dynM;
     p.rowoff = a->rowoff;
     p.e = nb::make_epi(a);
     p.ws = g_ws;
     p.counters = g_counters;
-    gemm_tc_kernel<BN><<<tiles * p.splits, THREADS, Cfg<BN>::SMEM, st>>>(mw, mh, ml, p);
+    const int grid = p.units < g_sms ? p.units : g_sms;
+    gemm_tc_kernel<BN><<<grid, THREADS, Cfg<BN>::SMEM, st>>>(mw, mh, ml, p);
     return nb_check_launch("gemm_tc_kernel");
 }
 
