@@ -134,6 +134,8 @@ nb_engine_t *nb_engine_create(nb_model_t *m, int B, int right, char *err, size_t
     d->fmt = fmt;
     d->a_plane = (int64_t)Bz * 2 * PH;
     d->h_plane = (int64_t)Bz * PH;
+    d->jx = dalloc(Bz * JH * 4, &fail);
+    d->logits = dalloc(Bz * (size_t)g->num_classes * 4, &fail);
     if (fail) { snprintf(err, errlen, "out of device memory for %d streams", B); goto fail; }
     CK(cudaMallocHost((void **)&e->h_cnt, 8 * sizeof(int)));
     CK(cudaMallocHost((void **)&e->h_ntok, Bz * sizeof(int)));
@@ -162,6 +164,8 @@ void nb_engine_destroy(nb_engine_t *e) {
                    e->dec.A1, e->dec.gates, e->dec.hp1c, e->dec.predc };
     for (size_t i = 0; i < sizeof f / sizeof *f; ++i) if (f[i]) cudaFree(f[i]);
     if (e->prompted_x && e->prompted_x != e->prompted) cudaFree(e->prompted_x);
+    if (e->dec.jx) cudaFree(e->dec.jx);
+    if (e->dec.logits) cudaFree(e->dec.logits);
     int *n[] = { e->d_params, e->dec.t, e->dec.symbols, e->dec.active, e->dec.pred_valid, e->dec.last_token, e->dec.ntok, e->dec.need_idx,
                  e->dec.erow, e->dec.idx, e->dec.tokens, e->dec.cnt };
     for (size_t i = 0; i < sizeof n / sizeof *n; ++i) if (n[i]) cudaFree(n[i]);
@@ -372,7 +376,11 @@ static int run_decoder(nb_engine_t *e, int c, char *err, size_t errlen) {
         a.dynM = d->cnt;
         KL(nemo_gemm(&a, st));
         KL(nb_dec_scatter_pred(d, JH, st));
-        KL(nb_joint_argmax_rows(e->joint_enc, JH, d->pred, JH, 1, m->joint_out_w, m->joint_out_b, g->num_classes, JH, B, d->erow, d->idx, NULL, st));
+        if (d->fmt == NEMO_FMT_BF16X2)
+            KL(nb_joint_argmax_gemm(e->joint_enc, JH, d->pred, JH, m->joint_out_w, m->joint_out_b, g->num_classes, JH, B, d->erow, d->jx, d->logits,
+                                    g->num_classes, d->idx, NULL, st));
+        else
+            KL(nb_joint_argmax_rows(e->joint_enc, JH, d->pred, JH, 1, m->joint_out_w, m->joint_out_b, g->num_classes, JH, B, d->erow, d->idx, NULL, st));
         KL(nb_dec_update(d, c, PH, g->blank_id, g->max_symbols, st));
         if (cudaMemcpyAsync(e->h_cnt, d->cnt, 2 * sizeof(int), cudaMemcpyDeviceToHost, st) != cudaSuccess ||
             cudaStreamSynchronize(st) != cudaSuccess) {

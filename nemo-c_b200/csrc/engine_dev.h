@@ -17,6 +17,8 @@ typedef struct {
     float *A0, *A1, *gates, *hp1c, *predc; /* compact per-iteration work rows */
     int fmt;                          /* format of A0 / A1 / hp1c (GEMM inputs): fp32 or bf16 hi/lo planes */
     int64_t a_plane, h_plane;         /* plane offsets (elements) of A0/A1 and of hp1c */
+    uint16_t *jx;                     /* joint GEMM input planes [streams][JH] */
+    float *logits;                    /* [streams][num_classes] */
 } DecState;
 
 int nb_compact(float *kv, float *din, int layers, int streams, int64_t cap, int D, int src_kv, int cache_len, int src_din, int dst_din,
@@ -30,6 +32,8 @@ int nb_dec_update(const DecState *d, int c, int PH, int blank, int max_symbols, 
 int nb_dec_reset(const DecState *d, int PH, int blank, void *stream);
 int nb_joint_argmax_rows(const float *enc, int64_t enc_ld, const float *pred, int64_t pred_ld, int pred_rpg, const uint16_t *W,
                          const float *bias, int V, int H, int rows, const int *enc_row_of, int *out_idx, float *out_val, void *stream);
+int nb_joint_argmax_gemm(const float *enc, int64_t enc_ld, const float *pred, int64_t pred_ld, const uint16_t *W, const float *bias, int V, int H,
+                         int rows, const int *enc_row_of, uint16_t *X, float *logits, int64_t ldl, int *out_idx, float *out_val, void *stream);
 int nb_dwconv2d_s2_fmt(const float *X, const float *W, const float *bias, void *Y, int y_fmt, int64_t y_plane, int streams, int T, int F,
                        int T1, int F1, int C, void *stream);
 int nb_flatten_rows_fmt(const float *X, void *Y, int y_fmt, int64_t y_plane, const int *lo, int streams, int T, int F, int C, int c, void *stream);
