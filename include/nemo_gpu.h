@@ -84,6 +84,11 @@ int nemo_dwconv_ln_silu(const float *din, int64_t din_sstride, const int *pos, c
    (x_sstride apart). Replaces conv2d_c1_s2_relu (src/kernels.metal:413-432). Y: [s][T1][F1][C]. */
 int nemo_conv2d_c1_s2_relu(const float *X, int64_t x_sstride, const float *W, const float *bias, float *Y,
                            int streams, int T, int F, int T1, int F1, int C, void *stream);
+/* The first two subsampling stages in one pass: conv2d_c1_s2_relu followed by dwconv2d_s2
+   (src/encoder.c:125-130), without the intermediate [T1][F1][C] map. X: `streams` windows of
+   [T][F] (x_sstride apart); Y: [s][T2][F2][C] as fp32 or bf16 planes (y_plane apart). */
+int nemo_subsample_front(const float *X, int64_t x_sstride, const float *W0, const float *b0, const float *W2, const float *b2, void *Y,
+                         int y_fmt, int64_t y_plane, int streams, int T, int F, int C, void *stream);
 /* Depthwise 3x3 stride-2 conv. Replaces dwconv2d_s2 (src/kernels.metal:435-454). X [s][T][F][C]. */
 int nemo_dwconv2d_s2(const float *X, const float *W, const float *bias, float *Y, int streams, int T, int F,
                      int T1, int F1, int C, void *stream);

@@ -92,7 +92,8 @@ nb_engine_t *nb_engine_create(nb_model_t *m, int B, int right, char *err, size_t
     CK(cudaEventCreate(&e->ev1));
     e->d_win = dalloc(Bz * (size_t)e->nwin_max * 128 * 4, &fail);
     CK(cudaMallocHost((void **)&e->h_win, Bz * (size_t)e->nwin_max * 128 * 4));
-    e->c0 = dalloc(Bz * T1 * F1 * CH * 4, &fail);
+    e->c0 = NULL; /* the first subsampling stage is fused into the second (no [T1][F1][C] map) */
+    (void)T1; (void)F1;
     e->c1 = dalloc(Bz * T2 * F2 * CH * 4, &fail);
     e->c2 = dalloc(Bz * T2 * F2 * CH * 4, &fail);
     e->c3 = dalloc(Bz * T3 * F3 * CH * 4, &fail);
@@ -280,8 +281,8 @@ static int launch_encoder(nb_engine_t *e, int nwin, int c) {
     nemo_gemm_args_t a;
 
     /* subsampling (src/encoder.c:121-142); the flatten keeps only rows [lo, lo + c) (:258) */
-    if (nemo_conv2d_c1_s2_relu(e->d_win, (int64_t)e->nwin_max * 128, m->conv0_w, m->conv0_b, e->c0, B, nwin, 128, T1, F1, CH, st)) return -1;
-    if (nb_dwconv2d_s2_fmt(e->c0, m->conv2_w, m->conv2_b, e->c1, fc, pl_c1, B, T1, F1, T2, F2, CH, st)) return -1;
+    if (nemo_subsample_front(e->d_win, (int64_t)e->nwin_max * 128, m->conv0_w, m->conv0_b, m->conv2_w, m->conv2_b, e->c1, fc, pl_c1, B, nwin, 128, CH, st))
+        return -1;
     a = gemm_args(e->c1, CH, fc, pl_c1, m->conv3_w, CH, m->conv3_b, e->c2, CH, B * T2 * F2, CH, CH, NEMO_ACT_RELU, 0, 1.0f);
     if (nemo_gemm(&a, st)) return -1;
     if (nb_dwconv2d_s2_fmt(e->c2, m->conv5_w, m->conv5_b, e->c3, fc, pl_c3, B, T2, F2, T3, F3, CH, st)) return -1;

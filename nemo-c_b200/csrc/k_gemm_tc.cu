@@ -63,15 +63,26 @@ __device__ __forceinline__ void epi_chunk(const nb::Epi &e, const int64_t *__res
                                           bool row_bias) {
     float *__restrict__ C32 = (float *)e.C;
     uint16_t *__restrict__ C16 = (uint16_t *)e.C;
+    // every global load of the chunk (accumulated output, per-row bias) is issued before the
+    // first store, so their latencies overlap instead of queueing behind the stores
+    float cin[16], rba[16], rbb[16];
+#pragma unroll
+    for (int jj = 0; jj < 16; ++jj) {
+        const int ml = j0 + jj;
+        cin[jj] = rba[jj] = rbb[jj] = 0.0f;
+        if (ml < mcount) {
+            if (e.accumulate) cin[jj] = C32[rowbase[ml] + n];
+            if (row_bias) {
+                rba[jj] = e.bias[brow[ml] + n];
+                if (vb) rbb[jj] = e.bias[brow[ml] + nb_];
+            }
+        }
+    }
 #pragma unroll
     for (int jj = 0; jj < 16; ++jj) {
         const int ml = j0 + jj;
         if (ml >= mcount) break;
-        float ba = bias_a, bb = bias_b;
-        if (row_bias) {
-            ba = e.bias[brow[ml] + n];
-            if (vb) bb = e.bias[brow[ml] + nb_];
-        }
+        const float ba = row_bias ? rba[jj] : bias_a, bb = row_bias ? rbb[jj] : bias_b;
         float v;
         if (vb) {
             v = (va[jj] + ba) * fast_sigmoid(vb[jj] + bb) * e.alpha;
@@ -82,7 +93,7 @@ __device__ __forceinline__ void epi_chunk(const nb::Epi &e, const int64_t *__res
             v *= e.alpha;
         }
         const int64_t idx = rowbase[ml] + n;
-        if (e.accumulate) v += C32[idx];
+        v += cin[jj];
         if (e.c_fmt == NEMO_FMT_F32) {
             C32[idx] = v;
         } else {
@@ -229,7 +240,7 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
             float *wsb = p.ws + (int64_t)tile * p.splits * BN * BM;
             bool finish = ok;
             if (ok && p.splits > 1) {
-                for (int j0 = jbeg; j0 < jend; j0 += 16) {
+                for (int j0 = jbeg; j0 < jend && j0 < mcount; j0 += 16) {
                     float v[16];
                     sm100::tmem_ld16(tacc + j0, v);
 #pragma unroll

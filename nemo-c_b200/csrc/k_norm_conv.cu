@@ -136,6 +136,60 @@ __global__ void dwconv2d_s2_kernel(const float *__restrict__ X, const float *__r
     }
 }
 
+// The first two subsampling stages fused: conv2d_c1_s2_relu (src/kernels.metal:413-432) then
+// dwconv2d_s2 (src/kernels.metal:435-454), without materialising the first stage's output.
+// Output (t2, f2) needs first-stage outputs t1 = 2*t2-2+kh, f1 = 2*f2-2+kw (zero when outside
+// [0,T1) x [0,F1): the depthwise conv's padding), which need input rows 2*t1-2..2*t1 and columns
+// 2*f1-2..2*f1: a 7x7 input patch starting at (4*t2-6, 4*f2-6). One warp per output position;
+// the patch sits in shared memory; lanes take channels ch = lane, lane+32, ...
+__global__ void __launch_bounds__(256) subsample_front_kernel(const float *__restrict__ X, int64_t x_sstride, const float *__restrict__ W0,
+                                                              const float *__restrict__ b0, const float *__restrict__ W2, const float *__restrict__ b2,
+                                                              void *Y, int y_fmt, int64_t y_plane, int T, int F, int T1, int F1, int T2, int F2, int C,
+                                                              int64_t positions) {
+    __shared__ float patch[8][49];
+    nb::pdl_wait();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t pidx = (int64_t)blockIdx.x * 8 + warp;
+    if (pidx >= positions) return;
+    const int f2 = (int)(pidx % F2);
+    const int64_t r = pidx / F2;
+    const int t2 = (int)(r % T2), s = (int)(r / T2);
+    const float *x = X + (int64_t)s * x_sstride;
+    const int tx0 = 4 * t2 - 6, fx0 = 4 * f2 - 6;
+    for (int e = lane; e < 49; e += 32) {
+        const int ti = tx0 + e / 7, fi = fx0 + e % 7;
+        patch[warp][e] = (ti >= 0 && ti < T && fi >= 0 && fi < F) ? x[(int64_t)ti * F + fi] : 0.0f;
+    }
+    __syncwarp();
+    const float *pt = patch[warp];
+    for (int ch = lane; ch < C; ch += 32) {
+        float w0[9], w2[9];
+#pragma unroll
+        for (int k = 0; k < 9; ++k) { w0[k] = W0[ch * 9 + k]; w2[k] = W2[ch * 9 + k]; }
+        const float bb0 = b0[ch];
+        float acc = b2[ch];
+#pragma unroll
+        for (int kh = 0; kh < 3; ++kh) {
+            const int t1 = 2 * t2 - 2 + kh;
+            if (t1 < 0 || t1 >= T1) continue;
+#pragma unroll
+            for (int kw = 0; kw < 3; ++kw) {
+                const int f1 = 2 * f2 - 2 + kw;
+                if (f1 < 0 || f1 >= F1) continue;
+                // first-stage output at (t1, f1): input rows 2*t1-2+a, columns 2*f1-2+b, i.e.
+                // patch rows 2*kh + a and columns 2*kw + b
+                float c0 = bb0;
+#pragma unroll
+                for (int a = 0; a < 3; ++a)
+#pragma unroll
+                    for (int b = 0; b < 3; ++b) c0 += w0[a * 3 + b] * pt[(2 * kh + a) * 7 + 2 * kw + b];
+                acc += w2[kh * 3 + kw] * fmaxf(c0, 0.0f);
+            }
+        }
+        nb::store_act(Y, y_fmt, y_plane, pidx * C + ch, acc);
+    }
+}
+
 // flatten_cf (src/kernels.metal:457-462) of rows [lo, lo + c) only: Y[s*c + i][ch*F + f] =
 // X[s][lo + i][f][ch]. Thread per output element (f fastest within a channel).
 __global__ void flatten_rows_kernel(const float *__restrict__ X, void *Y, int y_fmt, int64_t y_plane, const int *lo_p, int T, int F, int C, int c,
@@ -199,6 +253,16 @@ extern "C" int nb_dwconv2d_s2_fmt(const float *X, const float *W, const float *b
 
 extern "C" int nemo_dwconv2d_s2(const float *X, const float *W, const float *bias, float *Y, int streams, int T, int F, int T1, int F1, int C, void *stream) {
     return nb_dwconv2d_s2_fmt(X, W, bias, Y, NEMO_FMT_F32, 0, streams, T, F, T1, F1, C, stream);
+}
+
+extern "C" int nemo_subsample_front(const float *X, int64_t x_sstride, const float *W0, const float *b0, const float *W2, const float *b2, void *Y,
+                                    int y_fmt, int64_t y_plane, int streams, int T, int F, int C, void *stream) {
+    const int T1 = T / 2 + 1, F1 = F / 2 + 1, T2 = T1 / 2 + 1, F2 = F1 / 2 + 1;
+    const int64_t positions = (int64_t)streams * T2 * F2;
+    if (positions <= 0) return 0;
+    subsample_front_kernel<<<(unsigned)((positions + 7) / 8), 256, 0, (cudaStream_t)stream>>>(X, x_sstride, W0, b0, W2, b2, Y, y_fmt, y_plane, T, F, T1,
+                                                                                              F1, T2, F2, C, positions);
+    return nb_check_launch("subsample_front_kernel");
 }
 
 extern "C" int nb_flatten_rows_fmt(const float *X, void *Y, int y_fmt, int64_t y_plane, const int *lo, int streams, int T, int F, int C, int c, void *stream) {

@@ -122,6 +122,7 @@ def _setup_api(L):
     L.nemo_dwconv_ln_silu.argtypes = [vp, i64, vp, vp, vp, vp, vp, C.c_int, i64, C.c_int, C.c_int, C.c_int, C.c_int, C.c_float, vp]
     L.nemo_conv2d_c1_s2_relu.argtypes = [vp, i64, vp, vp, vp] + [C.c_int] * 6 + [vp]
     L.nemo_dwconv2d_s2.argtypes = [vp, vp, vp, vp] + [C.c_int] * 6 + [vp]
+    L.nemo_subsample_front.argtypes = [vp, i64, vp, vp, vp, vp, vp, C.c_int, i64] + [C.c_int] * 4 + [vp]
     L.nemo_flatten_rows.argtypes = [vp, vp, vp] + [C.c_int] * 5 + [vp]
     L.nemo_lstm_cell.argtypes = [vp, vp, vp, vp, C.c_int, C.c_int, vp]
     L.nemo_joint_argmax.argtypes = [vp, i64, vp, i64, vp, vp, C.c_int, C.c_int, C.c_int, vp, vp, vp]

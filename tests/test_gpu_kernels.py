@@ -247,3 +247,21 @@ def test_lstm_cell_and_joint_argmax():
     for r in range(rows):
         assert gi[r] == ri[r] or rm[r] < 1e-3
         assert abs(gv[r] - rv[r]) < 1e-4 * max(1.0, abs(rv[r]))
+
+
+@pytest.mark.parametrize("T,C", [(72, 64), (56, 256), (17, 32)])
+def test_subsample_front_fused(T, C):
+    rng = np.random.default_rng(T + C)
+    streams, F = 2, 128
+    X = rng.standard_normal((streams, T + 3, F)).astype(np.float32)  # padded stride like the engine window
+    W0, b0 = rng.standard_normal(C * 9).astype(np.float32), rng.standard_normal(C).astype(np.float32)
+    W2, b2 = rng.standard_normal(C * 9).astype(np.float32), rng.standard_normal(C).astype(np.float32)
+    T1, F1 = T // 2 + 1, F // 2 + 1
+    T2, F2 = T1 // 2 + 1, F1 // 2 + 1
+    Y = dev(np.zeros((streams, T2, F2, C), np.float32))
+    nb.check(nb.api().nemo_subsample_front(p(dev(X)), (T + 3) * F, p(dev(W0)), p(dev(b0)), p(dev(W2)), p(dev(b2)), p(Y), 0, 0, streams, T, F, C,
+                                           None))
+    y = host(Y)
+    for s in range(streams):
+        ref = orc.dwconv2d_s2(orc.conv2d_c1_s2_relu(X[s, :T], W0, b0), W2, b2)
+        assert rel_err(y[s], ref) < FP32_TOL
