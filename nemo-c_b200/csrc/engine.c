@@ -8,6 +8,7 @@
 #include <stdlib.h>
 #include <string.h>
 
+#define NB_MAX_GRAPHS 48
 #define CK(x) do { cudaError_t e_ = (x); if (e_ != cudaSuccess) { snprintf(err, errlen, "%s: %s", #x, cudaGetErrorString(e_)); goto fail; } } while (0)
 #define KL(x) do { if ((x) != 0) { snprintf(err, errlen, "%s", nemo_gpu_last_error()); return -1; } } while (0)
 
@@ -46,7 +47,14 @@ struct nb_engine {
     double enc_ms, dec_ms, gpu_ms;
     size_t chunks;
     cudaEvent_t ev0, ev1;
+    /* captured CUDA graphs: encoder step per (window rows, chunk rows), decoder iteration per
+       chunk rows; NEMO_GRAPHS=0 launches kernel by kernel instead */
+    int use_graphs;
+    struct { int kind, k1, k2; cudaGraphExec_t exec; uint64_t kernels; } graphs[NB_MAX_GRAPHS];
+    int ngraphs;
 };
+
+uint64_t nb_graph_kernel_nodes(cudaGraph_t g);
 
 double nb_engine_gpu_ms(const nb_engine_t *e) { return e->gpu_ms; }
 
@@ -150,6 +158,11 @@ nb_engine_t *nb_engine_create(nb_model_t *m, int B, int right, char *err, size_t
         for (int s = 0; s < B; ++s) CK(cudaMemcpy(e->b_eff + (size_t)s * PRH, be, PRH * 4, cudaMemcpyHostToDevice));
         free(be);
     }
+    if (nb_gemm_tc_init()) { snprintf(err, errlen, "%s", nemo_gpu_last_error()); goto fail; }
+    {
+        const char *gr = getenv("NEMO_GRAPHS");
+        e->use_graphs = !(gr && !strcmp(gr, "0"));
+    }
     if (nb_engine_reset(e, err, errlen)) goto fail;
     return e;
 fail:
@@ -178,6 +191,7 @@ void nb_engine_destroy(nb_engine_t *e) {
     if (e->st) cudaStreamDestroy(e->st);
     if (e->ev0) cudaEventDestroy(e->ev0);
     if (e->ev1) cudaEventDestroy(e->ev1);
+    for (int i = 0; i < e->ngraphs; ++i) cudaGraphExecDestroy(e->graphs[i].exec);
     if (e->pending) for (int s = 0; s < e->B; ++s) free(e->pending[s]);
     free(e->pending);
     free(e->mel_cache);
@@ -353,16 +367,19 @@ static int launch_encoder(nb_engine_t *e, int nwin, int c) {
 }
 
 /* ---- greedy RNNT decode of the chunk's c frames for every stream (src/decoder.c:92-127) --- */
-static int run_decoder(nb_engine_t *e, int c, char *err, size_t errlen) {
+/* One greedy-decoding iteration of every stream (one frame decision each), ending with the
+   read-back of the still-active count. */
+static int dec_iteration(nb_engine_t *e, int c, int unused) {
+    (void)unused;
     const nb_model_t *m = e->m;
     const nb_config_t *g = &m->g;
     const int B = e->B, PH = g->pred_hidden, JH = g->joint_hidden;
     DecState *d = &e->dec;
     cudaStream_t st = e->st;
-    KL(nb_dec_chunk_init(d, c, st));
-    const int max_it = c * (g->max_symbols + 1) + 2;
-    int it;
-    for (it = 0; it < max_it; ++it) {
+    char err[8];
+    const size_t errlen = 0;
+    (void)err; (void)errlen;
+    {
         KL(nb_dec_plan(d, c, st));
         KL(nb_dec_gather(d, m->embed, PH, g->blank_id, st));
         nemo_gemm_args_t a = gemm_args(d->A0, 2 * PH, d->fmt, d->a_plane, m->lstm_w[0], 2 * PH, m->lstm_b[0], d->gates, 4 * PH, B, 4 * PH, 2 * PH, 0, 0, 1.0f);
@@ -383,8 +400,61 @@ static int run_decoder(nb_engine_t *e, int c, char *err, size_t errlen) {
         else
             KL(nb_joint_argmax_rows(e->joint_enc, JH, d->pred, JH, 1, m->joint_out_w, m->joint_out_b, g->num_classes, JH, B, d->erow, d->idx, NULL, st));
         KL(nb_dec_update(d, c, PH, g->blank_id, g->max_symbols, st));
-        if (cudaMemcpyAsync(e->h_cnt, d->cnt, 2 * sizeof(int), cudaMemcpyDeviceToHost, st) != cudaSuccess ||
-            cudaStreamSynchronize(st) != cudaSuccess) {
+        if (cudaMemcpyAsync(e->h_cnt, d->cnt, 2 * sizeof(int), cudaMemcpyDeviceToHost, st) != cudaSuccess)
+            return nb_set_error("decoder: %s", cudaGetErrorString(cudaGetLastError()));
+    }
+    return 0;
+}
+
+static int enc_body(nb_engine_t *e, int nwin, int c) { return launch_encoder(e, nwin, c); }
+
+/* Launch `body` through a captured graph keyed by (kind, k1, k2), capturing it on first use. */
+static int run_graph(nb_engine_t *e, int kind, int k1, int k2, int (*body)(nb_engine_t *, int, int)) {
+    if (!e->use_graphs) return body(e, k1, k2);
+    int slot = -1;
+    for (int i = 0; i < e->ngraphs; ++i)
+        if (e->graphs[i].kind == kind && e->graphs[i].k1 == k1 && e->graphs[i].k2 == k2) { slot = i; break; }
+    if (slot < 0) {
+        if (e->ngraphs == NB_MAX_GRAPHS) return body(e, k1, k2);
+        cudaGraph_t graph;
+        if (cudaStreamBeginCapture(e->st, cudaStreamCaptureModeThreadLocal) != cudaSuccess)
+            return nb_set_error("graph capture: %s", cudaGetErrorString(cudaGetLastError()));
+        nb_set_launch_counting(0);
+        const int rc = body(e, k1, k2);
+        nb_set_launch_counting(1);
+        const cudaError_t ce = cudaStreamEndCapture(e->st, &graph);
+        if (rc || ce != cudaSuccess) {
+            if (ce == cudaSuccess) cudaGraphDestroy(graph);
+            return rc ? -1 : nb_set_error("graph capture: %s", cudaGetErrorString(ce));
+        }
+        cudaGraphExec_t exec;
+        if (cudaGraphInstantiate(&exec, graph, 0) != cudaSuccess) {
+            cudaGraphDestroy(graph);
+            return nb_set_error("graph instantiate: %s", cudaGetErrorString(cudaGetLastError()));
+        }
+        slot = e->ngraphs++;
+        e->graphs[slot].kind = kind;
+        e->graphs[slot].k1 = k1;
+        e->graphs[slot].k2 = k2;
+        e->graphs[slot].exec = exec;
+        e->graphs[slot].kernels = nb_graph_kernel_nodes(graph);
+        cudaGraphDestroy(graph);
+    }
+    if (cudaGraphLaunch(e->graphs[slot].exec, e->st) != cudaSuccess) return nb_set_error("graph launch: %s", cudaGetErrorString(cudaGetLastError()));
+    nb_count_launches(e->graphs[slot].kernels);
+    return 0;
+}
+
+static int run_decoder(nb_engine_t *e, int c, char *err, size_t errlen) {
+    const nb_config_t *g = &e->m->g;
+    DecState *d = &e->dec;
+    cudaStream_t st = e->st;
+    KL(nb_dec_chunk_init(d, c, st));
+    const int max_it = c * (g->max_symbols + 1) + 2;
+    int it;
+    for (it = 0; it < max_it; ++it) {
+        if (run_graph(e, 1, c, 0, dec_iteration)) { snprintf(err, errlen, "decoder: %s", nemo_gpu_last_error()); return -1; }
+        if (cudaStreamSynchronize(st) != cudaSuccess) {
             snprintf(err, errlen, "decoder: %s", cudaGetErrorString(cudaGetLastError()));
             return -1;
         }
@@ -461,7 +531,7 @@ int nb_engine_step(nb_engine_t *e, int final, int *tokens, int max_tokens, int *
         snprintf(err, errlen, "upload: %s", cudaGetErrorString(cudaGetLastError()));
         return -1;
     }
-    if (launch_encoder(e, nwin, c)) { snprintf(err, errlen, "encoder: %s", nemo_gpu_last_error()); return -1; }
+    if (run_graph(e, 0, nwin, c, enc_body)) { snprintf(err, errlen, "encoder: %s", nemo_gpu_last_error()); return -1; }
     if (cudaStreamSynchronize(st) != cudaSuccess) { snprintf(err, errlen, "encoder: %s", cudaGetErrorString(cudaGetLastError())); return -1; }
     if (nemo_gpu_check_device_errors()) { snprintf(err, errlen, "encoder: %s", nemo_gpu_last_error()); return -1; }
     const double t1 = nb_now_ms();

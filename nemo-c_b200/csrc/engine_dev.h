@@ -21,6 +21,10 @@ typedef struct {
     float *logits;                    /* [streams][num_classes] */
 } DecState;
 
+int nb_set_error(const char *fmt, ...);
+int nb_gemm_tc_init(void);
+void nb_set_launch_counting(int on);
+void nb_count_launches(uint64_t n);
 int nb_compact(float *kv, float *din, int layers, int streams, int64_t cap, int D, int src_kv, int cache_len, int src_din, int dst_din,
                int conv_left, void *stream);
 int nb_dec_chunk_init(const DecState *d, int c, void *stream);

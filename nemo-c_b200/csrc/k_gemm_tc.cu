@@ -387,6 +387,9 @@ int launch(const nemo_gemm_args_t *a, cudaStream_t st) {
 
 }  // namespace
 
+// One-time setup (driver entry point, split-K workspace): call before capturing a CUDA graph.
+extern "C" int nb_gemm_tc_init(void) { return init_once(); }
+
 int nb_gemm_tc(const nemo_gemm_args_t *a, void *stream) {
     if (init_once()) return -1;
     if (a->act == NEMO_ACT_GLU && ((a->N / 2) % 64)) return nb_set_error("tensor-core GEMM: GLU needs N/2 to be a multiple of 64");

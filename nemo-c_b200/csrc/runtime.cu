@@ -18,9 +18,29 @@ extern "C" const char *nemo_gpu_last_error(void) { return g_err; }
 extern "C" void nb_count_launches(uint64_t n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
 extern "C" uint64_t nemo_gpu_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
 
+static thread_local int g_counting = 1;
+// While a stream is being captured into a CUDA graph, launches are recorded, not executed: the
+// engine turns counting off and adds the graph's kernel nodes each time it launches the graph.
+extern "C" void nb_set_launch_counting(int on) { g_counting = on; }
+
 int nb_check_launch(const char *what) {
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return nb_set_error("%s: %s", what, cudaGetErrorString(e));
-    nb_count_launches(1);
+    if (g_counting) nb_count_launches(1);
     return 0;
+}
+
+// Number of kernel nodes in a graph (launch accounting of graph replays).
+extern "C" uint64_t nb_graph_kernel_nodes(cudaGraph_t g) {
+    size_t n = 0;
+    if (cudaGraphGetNodes(g, nullptr, &n) != cudaSuccess || n == 0) return 0;
+    cudaGraphNode_t *nodes = new cudaGraphNode_t[n];
+    uint64_t k = 0;
+    if (cudaGraphGetNodes(g, nodes, &n) == cudaSuccess)
+        for (size_t i = 0; i < n; ++i) {
+            cudaGraphNodeType t;
+            if (cudaGraphNodeGetType(nodes[i], &t) == cudaSuccess && t == cudaGraphNodeTypeKernel) ++k;
+        }
+    delete[] nodes;
+    return k;
 }
