@@ -398,8 +398,9 @@ int nb_gemm_tc(const nemo_gemm_args_t *a, void *stream) {
     if (a->M <= 16) return launch<16>(a, st);
     if (a->M <= 32) return launch<32>(a, st);
     if (a->M <= 64) return launch<64>(a, st);
-    if (a->M <= 128) return launch<128>(a, st);
-    return launch<256>(a, st);
+    // 128-row activation tiles beat 256 at batch sizes (four pipeline stages instead of two,
+    // more units per SM to overlap epilogues): measured 1.3-2x at 1792 rows
+    return launch<128>(a, st);
 }
 
 extern "C" int nemo_gpu_check_device_errors(void) {
