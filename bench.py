@@ -99,7 +99,7 @@ def make_inputs(nb, a, rank):
     from concurrent.futures import ThreadPoolExecutor
     n = int(round(a.seconds * 16000))
     audio = np.zeros((a.streams, n), np.float32)
-    seeds = [100000 * (rank + 1) + s for s in range(a.streams)]
+    seeds = stream_seeds(a, rank)
     with ThreadPoolExecutor(min(32, os.cpu_count() or 8)) as ex:
         for s, x in enumerate(ex.map(lambda sd: nb.synth_audio(sd, 16000, n=n, pauses=True), seeds)):
             audio[s] = x
@@ -107,6 +107,22 @@ def make_inputs(nb, a, rank):
     T = min(m.shape[0] for m in mels)
     mel = np.stack([m[:T] for m in mels])
     return audio, mel
+
+
+def stream_seeds(a, rank):
+    """Audio seeds of this rank's streams: every rank owns a disjoint set of streams (weak scaling;
+    nothing is exchanged between ranks)."""
+    return [100000 * (rank + 1) + s for s in range(a.streams)]
+
+
+def max_over_ranks(dist, x, device):
+    """Max of a host float over ranks (the step time of the slowest GPU); x itself when alone."""
+    if dist is None:
+        return x
+    import torch
+    t = torch.tensor([x], device=device, dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
 
 
 def languages(a, rank):
@@ -237,12 +253,6 @@ def main():
         if dist:
             dist.barrier()
 
-    def max_over_ranks(x):
-        if not dist:
-            return x
-        t = torch.tensor([x], device="cuda", dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
 
     launches0 = nb.api().nemo_gpu_launch_count()
     audio, mel = make_inputs(nb, a, rank)
@@ -270,7 +280,7 @@ def main():
     gpu_ms = batch.gpu_ms() - g0
     launches = nb.api().nemo_gpu_launch_count() - l0
     clk = clocks.stop()
-    gpu_ms = max_over_ranks(gpu_ms)
+    gpu_ms = max_over_ranks(dist, gpu_ms, "cuda")
     value = a.steps * chunk_s * B * world / (gpu_ms / 1000.0)
 
     # ---- e2e: host audio through nemoasr_batch_feed -----------------------------------------
@@ -286,7 +296,7 @@ def main():
         for i in range(a.warmup + 1, a.warmup + 1 + a.steps):
             batch.feed(audio[:, i * blk:(i + 1) * blk])
         torch.cuda.synchronize()
-        wall = max_over_ranks(time.perf_counter() - t0)
+        wall = max_over_ranks(dist, time.perf_counter() - t0, "cuda")
         nwin = 16 + a.latency // 10 + 1
         e2e = {"value": a.steps * chunk_s * B * world / wall, "unit": UNIT,
                "h2d_bytes_per_step": B * nwin * 128 * 4 + 12,
