@@ -52,6 +52,16 @@ int nemo_gemm(const nemo_gemm_args_t *a, void *stream);
 /* Force a kernel family for tests and the kernel sweep: 0 = by row count (default),
    1 = CUDA-core weight streaming, 2 = tcgen05 tensor cores. */
 int nemo_gemm_forced(const nemo_gemm_args_t *a, int kind, void *stream);
+/* Allocation-free tensor-core GEMM (no counterpart in the reference, whose Metal GEMMs need no
+   split-K scratch). Same arguments and results as nemo_gemm for NEMO_FMT_BF16X2 activations of
+   1..32 rows; its split-K scratch is a fixed 5 MiB array inside the library, so it never
+   allocates device memory. For hosts that cannot allocate once running: a real-time audio
+   callback driving one stream (cudaMalloc may synchronize the device) and servers that reserve
+   their device memory up front. Returns -1 with nemo_gpu_last_error() set for more rows, other
+   activation formats, or a plan that would exceed the scratch. The first call on each device
+   (that device current) does the set-up; make it before any stream capture. Calls on one device
+   share the scratch: calls that overlap in time race and must be serialized on one stream. */
+int nemo_gemm_noalloc(const nemo_gemm_args_t *a, void *stream);
 
 /* Row LayerNorm. Replaces k_layernorm (src/model.h:73; kernel src/kernels.metal:258-288).
    Y may be written as NEMO_FMT_BF16X2 planes (y_plane apart) for a tensor-core consumer. */

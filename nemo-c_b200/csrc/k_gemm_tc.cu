@@ -409,3 +409,139 @@ extern "C" int nemo_gpu_check_device_errors(void) {
     if (v) return nb_set_error("tensor-core GEMM: a bounded wait gave up (code %d)", v);
     return 0;
 }
+
+// ---- allocation-free entry point -------------------------------------------------------------
+// The same kernel and split-K plan as nb_gemm_tc for activation tiles of up to 32 rows (the
+// single-stream and small-batch shapes, which are the ones that split K), with the partial tiles
+// and arrival counters in a fixed array compiled into this module instead of the cudaMalloc'd
+// workspace. It exists for hosts that must not allocate device memory once they are running: a
+// real-time audio callback that drives one stream (cudaMalloc may synchronize the device and
+// stall the callback), and servers that reserve their whole device-memory budget up front and
+// refuse allocations afterwards.
+//
+// Limits: at most NA_MAX_ROWS activation rows; a plan that would need more partial-tile bytes
+// or counters than the array holds is rejected with an error (with 148 SMs no shape of <= 32
+// rows does). All calls on one device share the one array, so calls whose executions overlap
+// (two streams, or two host threads without ordering) race on it and corrupt each other's sums:
+// serialize them on one stream or order them with events.
+//
+// The first call on each device (with that device current) does the one-time set-up: the
+// array's device address (cudaGetSymbolAddress), the kernels' shared-memory attribute and the
+// driver's tensor-map encoder. Make that first call before any stream capture.
+constexpr int NA_MAX_ROWS = 32;
+constexpr size_t NA_PART_BYTES = (size_t)5 << 20;  // split-K partial tiles: 5 MiB
+constexpr int NA_COUNTERS = 1024;                  // one arrival counter per output tile
+constexpr size_t NA_BYTES = NA_PART_BYTES + NA_COUNTERS * sizeof(int);
+constexpr int NA_MAX_DEVICES = 64;
+
+static __device__ __align__(256) unsigned char g_noalloc_scratch[NA_BYTES];
+
+namespace {
+
+std::mutex g_na_mu;
+EncodeTiled g_na_encode = nullptr;             // kept apart from g_encode, whose presence marks the workspace as allocated
+unsigned char *g_na_ptr[NA_MAX_DEVICES] = {};  // device address of g_noalloc_scratch per device
+int g_na_sms[NA_MAX_DEVICES] = {};
+
+int na_setup(unsigned char **scratch, int *sms) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return nb_set_error("nemo_gemm_noalloc: no current CUDA device");
+    if (dev < 0 || dev >= NA_MAX_DEVICES) return nb_set_error("nemo_gemm_noalloc: device %d beyond the %d supported", dev, NA_MAX_DEVICES);
+    std::lock_guard<std::mutex> lk(g_na_mu);
+    if (!g_na_ptr[dev]) {
+        if (!g_na_encode) {
+            void *fn = nullptr;
+            cudaDriverEntryPointQueryResult q;
+            if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) != cudaSuccess || !fn)
+                return nb_set_error("nemo_gemm_noalloc: cuTensorMapEncodeTiled unavailable");
+            g_na_encode = (EncodeTiled)fn;
+        }
+        void *p = nullptr;
+        cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (e != cudaSuccess || !p) return nb_set_error("nemo_gemm_noalloc: cudaGetSymbolAddress failed: %s", cudaGetErrorString(e));
+        int n = 0;
+        if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
+            return nb_set_error("nemo_gemm_noalloc: cannot read the SM count");
+        if (cudaFuncSetAttribute(gemm_tc_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<16>::SMEM) != cudaSuccess ||
+            cudaFuncSetAttribute(gemm_tc_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<32>::SMEM) != cudaSuccess)
+            return nb_set_error("nemo_gemm_noalloc: cannot set the kernels' shared-memory size");
+        g_na_sms[dev] = n;
+        g_na_ptr[dev] = (unsigned char *)p;
+    }
+    *scratch = g_na_ptr[dev];
+    *sms = g_na_sms[dev];
+    return 0;
+}
+
+int na_map(CUtensorMap *m, const void *base, int64_t cols, int64_t rows, int64_t ld_elems, int box_rows) {
+    if (((uintptr_t)base & 15) || ((ld_elems * 2) & 15)) return nb_set_error("nemo_gemm_noalloc: base and row pitch must be 16-byte aligned");
+    cuuint64_t dims[2] = { (cuuint64_t)cols, (cuuint64_t)rows };
+    cuuint64_t strides[1] = { (cuuint64_t)(ld_elems * 2) };
+    cuuint32_t box[2] = { (cuuint32_t)BK, (cuuint32_t)box_rows };
+    cuuint32_t es[2] = { 1, 1 };
+    CUresult r = g_na_encode(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                             CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return nb_set_error("nemo_gemm_noalloc: cuTensorMapEncodeTiled failed (%d)", (int)r);
+    return 0;
+}
+
+template <int BN>
+int na_launch(const nemo_gemm_args_t *a, cudaStream_t st, unsigned char *scratch, int sms) {
+    CUtensorMap mw, mh, ml;
+    const bool glu = a->act == NEMO_ACT_GLU;
+    if (na_map(&mw, a->W, a->K, a->N, a->ldw, glu ? 64 : BM)) return -1;
+    const uint16_t *A = (const uint16_t *)a->A;
+    if (na_map(&mh, A, a->K, a->M, a->lda, BN) || na_map(&ml, A + a->a_plane, a->K, a->M, a->lda, BN)) return -1;
+    TcArgs p;
+    memset(&p, 0, sizeof p);
+    p.M = a->M; p.N = a->N; p.K = a->K;
+    p.kblocks = (a->K + BK - 1) / BK;
+    p.glu = glu;
+    p.n_wtiles = glu ? (a->N / 2 + 63) / 64 : (a->N + BM - 1) / BM;
+    p.n_mtiles = (a->M + BN - 1) / BN;
+    const int tiles = p.n_wtiles * p.n_mtiles;
+    int splits = 1;
+    if (tiles < sms) {
+        splits = (sms + tiles - 1) / tiles;
+        if (splits > p.kblocks) splits = p.kblocks;
+    }
+    p.kb_per_split = (p.kblocks + splits - 1) / splits;
+    p.splits = (p.kblocks + p.kb_per_split - 1) / p.kb_per_split;
+    p.units = tiles * p.splits;
+    if (p.splits > 1) {
+        const size_t need = (size_t)p.units * BN * BM * sizeof(float);
+        if (need > NA_PART_BYTES || tiles > NA_COUNTERS)
+            return nb_set_error("nemo_gemm_noalloc: this shape needs %zu bytes of split-K partials and %d counters; the static scratch holds %zu and %d",
+                                need, tiles, NA_PART_BYTES, NA_COUNTERS);
+    }
+    p.dynM = a->dynM;
+    p.rowoff = a->rowoff;
+    p.e = nb::make_epi(a);
+    p.ws = (float *)scratch;
+    p.counters = (int *)(scratch + NA_PART_BYTES);
+    // the arrival counters must start at zero (a launch that gave up on a wait leaves them dirty)
+    if (p.splits > 1 && cudaMemsetAsync(p.counters, 0, (size_t)tiles * sizeof(int), st) != cudaSuccess)
+        return nb_set_error("nemo_gemm_noalloc: cannot clear the arrival counters");
+    const int grid = p.units < sms ? p.units : sms;
+    gemm_tc_kernel<BN><<<grid, THREADS, Cfg<BN>::SMEM, st>>>(mw, mh, ml, p);
+    return nb_check_launch("gemm_tc_kernel");
+}
+
+}  // namespace
+
+extern "C" int nemo_gemm_noalloc(const nemo_gemm_args_t *a, void *stream) {
+    if (!a) return nb_set_error("nemo_gemm_noalloc: null arguments");
+    if (a->M < 1 || a->M > NA_MAX_ROWS)
+        return nb_set_error("nemo_gemm_noalloc: M=%d rows; the allocation-free GEMM takes 1..%d rows (its static scratch is sized for that)", a->M,
+                            NA_MAX_ROWS);
+    if (a->a_fmt != NEMO_FMT_BF16X2) return nb_set_error("nemo_gemm_noalloc: activations must be NEMO_FMT_BF16X2 planes");
+    if (a->N < 1 || a->K < 1) return nb_set_error("nemo_gemm_noalloc: empty N or K");
+    if (a->act == NEMO_ACT_GLU && ((a->N / 2) % 64)) return nb_set_error("nemo_gemm_noalloc: GLU needs N/2 to be a multiple of 64");
+    if (a->K % 8) return nb_set_error("nemo_gemm_noalloc: K must be a multiple of 8");
+    unsigned char *scratch = nullptr;
+    int sms = 0;
+    if (na_setup(&scratch, &sms)) return -1;
+    cudaStream_t st = (cudaStream_t)stream;
+    if (a->M <= 16) return na_launch<16>(a, st, scratch, sms);
+    return na_launch<32>(a, st, scratch, sms);
+}
