@@ -50,7 +50,9 @@ typedef struct {
 } nemo_gemm_args_t;
 int nemo_gemm(const nemo_gemm_args_t *a, void *stream);
 /* Force a kernel family for tests and the kernel sweep: 0 = by row count (default),
-   1 = CUDA-core weight streaming, 2 = tcgen05 tensor cores. */
+   1 = CUDA-core weight streaming, 2 = tcgen05 tensor cores (tile layout by row count),
+   3 = CUDA-core tiled, 4 = tensor cores with weight-major tiles (weights on the MMA's 128-row
+   side), 5 = tensor cores with activation-major tiles (128 activation rows x 128/256 weights). */
 int nemo_gemm_forced(const nemo_gemm_args_t *a, int kind, void *stream);
 /* Allocation-free tensor-core GEMM (no counterpart in the reference, whose Metal GEMMs need no
    split-K scratch). Same arguments and results as nemo_gemm for NEMO_FMT_BF16X2 activations of

@@ -35,6 +35,7 @@ __device__ int g_tc_error;  // set when a bounded wait gave up (host reads it ba
 
 struct TcArgs {
     int M, N, K, kblocks, splits, kb_per_split, n_wtiles, n_mtiles, units, glu;
+    int vec;       // activation-major epilogue may use 16-byte accesses (alignment checked on the host)
     const int *dynM, *rowoff;
     nb::Epi e;
     float *ws;     // split-K partial tiles
@@ -300,6 +301,297 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
     }
 }
 
+// ---- activation-major tiles for batches -------------------------------------------------------
+// For many rows the roles swap: 128 activation rows are the MMA's M side (TMEM lanes) and BW
+// weight rows (128 or 256) its N side (TMEM columns). One k-step stages 2 x 16 KB of activation
+// planes and BW x 128 B of weights for 128 x BW x 64 x 2 multiply-adds, 1.5x fewer bytes per
+// MMA than the weight-major tile at BW = 256. Each epilogue thread owns one activation row and
+// reads 16 consecutive output columns per TMEM load; a GLU tile holds the value half in TMEM
+// columns [0, BW/2) and the gate half in [BW/2, BW), so both halves sit in the same thread.
+template <int BW>
+struct CfgR {
+    static constexpr int A_PLANE = 128 * BK * 2;                 // 16 KB
+    static constexpr int W_BYTES = BW * BK * 2;                  // 16 / 32 KB
+    static constexpr int STAGE = 2 * A_PLANE + W_BYTES;
+    static constexpr int STAGES = BW == 256 ? 3 : 4;
+    static constexpr int TMEM_COLS = 2 * BW;                     // two accumulator buffers
+    static constexpr int SMEM = 1024 + STAGES * STAGE + 1024;    // stages | barriers
+};
+
+template <int BW>
+__global__ void __launch_bounds__(THREADS, 1) gemm_tcr_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmAh,
+                                                            const __grid_constant__ CUtensorMap tmAl, const __grid_constant__ TcArgs p) {
+    using C = CfgR<BW>;
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    uint8_t *stages = smem;
+    uint64_t *full = (uint64_t *)(smem + C::STAGES * C::STAGE);
+    uint64_t *empty = full + C::STAGES;
+    uint64_t *acc_full = empty + C::STAGES;
+    uint64_t *acc_empty = acc_full + 2;
+    uint32_t *tmem_holder = (uint32_t *)(acc_empty + 2);
+    volatile int *flags = (volatile int *)(tmem_holder + 1); // [0] abort, [1] last split of the unit, [2] epilogue abort
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    nb::pdl_wait();
+    const int M = p.dynM ? min(p.M, *p.dynM) : p.M;
+    const int live_mtiles = (M + 127) / 128;
+    const int units = live_mtiles * p.n_wtiles * p.splits;
+    if ((int)blockIdx.x >= units) return;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < C::STAGES; ++s) { sm100::mbar_init(&full[s], 1); sm100::mbar_init(&empty[s], 1); }
+        for (int b = 0; b < 2; ++b) { sm100::mbar_init(&acc_full[b], 1); sm100::mbar_init(&acc_empty[b], 1); }
+        flags[0] = 0;
+        flags[2] = 0;
+        sm100::fence_mbar_init();
+        sm100::tma_prefetch_desc(&tmW);
+        sm100::tma_prefetch_desc(&tmAh);
+        sm100::tma_prefetch_desc(&tmAl);
+    }
+    if (warp == 1) {
+        sm100::tmem_alloc(tmem_holder, C::TMEM_COLS);
+        sm100::tmem_relinquish();
+    }
+    sm100::tc_fence_before();
+    __syncthreads();
+    sm100::tc_fence_after();
+    const uint32_t tmem = *tmem_holder;
+
+    if (warp == 0 && lane == 0) {
+        // ---- producer: activation hi/lo tiles + weight tile (value and gate halves for GLU) ----
+        int i = 0;
+        for (int u = blockIdx.x; u < units && !flags[0]; u += gridDim.x) {
+            const int split = u % p.splits, tile = u / p.splits, wt = tile % p.n_wtiles, mt = tile / p.n_wtiles;
+            const int kb0 = split * p.kb_per_split, kb1 = min(p.kblocks, kb0 + p.kb_per_split);
+            for (int kb = kb0; kb < kb1; ++kb, ++i) {
+                const int s = i % C::STAGES;
+                if (i >= C::STAGES && !sm100::mbar_wait(&empty[s], ((i / C::STAGES) - 1) & 1)) { flags[0] = 1; atomicExch(&g_tc_error, 5); break; }
+                if (flags[0]) break;
+                uint8_t *st = stages + s * C::STAGE;
+                const int k0 = kb * BK;
+                sm100::mbar_arrive_expect_tx(&full[s], C::STAGE);
+                sm100::tma_load_2d(st, &tmAh, &full[s], k0, mt * 128);
+                sm100::tma_load_2d(st + C::A_PLANE, &tmAl, &full[s], k0, mt * 128);
+                if (p.glu) {
+                    sm100::tma_load_2d(st + 2 * C::A_PLANE, &tmW, &full[s], k0, wt * (BW / 2));
+                    sm100::tma_load_2d(st + 2 * C::A_PLANE + C::W_BYTES / 2, &tmW, &full[s], k0, p.N / 2 + wt * (BW / 2));
+                } else {
+                    sm100::tma_load_2d(st + 2 * C::A_PLANE, &tmW, &full[s], k0, wt * BW);
+                }
+            }
+        }
+    } else if (warp == 1 && lane == 0) {
+        // ---- MMA issuer ----
+        constexpr uint32_t idesc = sm100::idesc_bf16_f32(128, BW);
+        int i = 0, t = 0;
+        for (int u = blockIdx.x; u < units && !flags[0]; u += gridDim.x, ++t) {
+            const int split = u % p.splits;
+            const int kb0 = split * p.kb_per_split, kb1 = min(p.kblocks, kb0 + p.kb_per_split);
+            const int b = t & 1;
+            if (t >= 2 && !sm100::mbar_wait(&acc_empty[b], ((t >> 1) - 1) & 1)) { flags[0] = 1; atomicExch(&g_tc_error, 6); break; }
+            sm100::tc_fence_after();
+            const uint32_t dacc = tmem + (uint32_t)(b * BW);
+            for (int kb = kb0; kb < kb1; ++kb, ++i) {
+                const int s = i % C::STAGES;
+                if (!sm100::mbar_wait(&full[s], (i / C::STAGES) & 1)) { flags[0] = 1; atomicExch(&g_tc_error, 7); break; }
+                sm100::tc_fence_after();
+                const uint32_t h_addr = sm100::smem_u32(stages + s * C::STAGE);
+                const uint32_t l_addr = h_addr + C::A_PLANE, w_addr = h_addr + 2 * C::A_PLANE;
+#pragma unroll
+                for (int kk = 0; kk < BK / 16; ++kk) {
+                    const uint64_t bd = sm100::desc_k_sw128(w_addr + kk * 32);
+                    sm100::mma_bf16(dacc, sm100::desc_k_sw128(h_addr + kk * 32), bd, idesc, (kb != kb0 || kk != 0) ? 1u : 0u);
+                    sm100::mma_bf16(dacc, sm100::desc_k_sw128(l_addr + kk * 32), bd, idesc, 1u);
+                }
+                sm100::mma_commit(&empty[s]);
+            }
+            sm100::mma_commit(&acc_full[b]);
+        }
+    } else if (warp >= 2) {
+        // ---- epilogue: thread = activation row, 16 output columns per TMEM load ----
+        const int ew = warp - 2, q = warp & 3, half = ew >> 2;
+        const int row = q * 32 + lane;
+        const int etid = threadIdx.x - 64;
+        const int nout = p.glu ? p.N / 2 : p.N;
+        constexpr int OUT_COLS = BW;                 // output columns of a non-GLU tile
+        const bool row_bias = p.e.bias && p.e.bias_gstride != 0;
+        const int rowoff = p.rowoff ? *p.rowoff : 0;
+        float *__restrict__ C32 = (float *)p.e.C;
+        uint16_t *__restrict__ C16 = (uint16_t *)p.e.C;
+        int t = 0;
+        for (int u = blockIdx.x; u < units; u += gridDim.x, ++t) {
+            const int split = u % p.splits, tile = u / p.splits, wt = tile % p.n_wtiles, mt = tile / p.n_wtiles;
+            const int b = t & 1;
+            const int m = mt * 128 + row;
+            const bool row_ok = m < M;
+            int64_t rowbase = 0, brow = 0;
+            if (row_ok) {
+                const int g = m / p.e.rpg, r = m - g * p.e.rpg;
+                rowbase = (int64_t)g * p.e.gstride + (int64_t)(rowoff + r) * p.e.ldc;
+                brow = (int64_t)g * p.e.bias_gstride;
+            }
+            if (!sm100::mbar_wait(&acc_full[b], (t >> 1) & 1)) { flags[2] = 1; flags[0] = 1; atomicExch(&g_tc_error, 8); }
+            sm100::named_barrier(1, 256);
+            const bool ok = !flags[2];
+            sm100::tc_fence_after();
+            const uint32_t tacc = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(b * BW);
+            // columns of this thread: GLU -> value cols [half*BW/4, +BW/4) and their gates at +BW/2;
+            // plain -> [half*BW/2, +BW/2)
+            const int span = p.glu ? BW / 4 : BW / 2;
+            const int j0 = half * span;
+            const int n_base = p.glu ? wt * (BW / 2) : wt * OUT_COLS;
+            float *wsb = p.ws + (int64_t)tile * p.splits * 128 * BW;
+            bool finish = ok;
+            if (ok && p.splits > 1) {
+                // partial tile [split][row][BW] (all TMEM columns, value and gate alike)
+                for (int j = half * (BW / 2); j < (half + 1) * (BW / 2); j += 16) {
+                    float v[16];
+                    sm100::tmem_ld16(tacc + j, v);
+                    float4 *dst = (float4 *)(wsb + ((int64_t)split * 128 + row) * BW + j);
+#pragma unroll
+                    for (int x = 0; x < 4; ++x) dst[x] = make_float4(v[4 * x], v[4 * x + 1], v[4 * x + 2], v[4 * x + 3]);
+                }
+                __threadfence();
+                sm100::named_barrier(1, 256);
+                if (etid == 0) flags[1] = atomicAdd(&p.counters[tile], 1) == p.splits - 1;
+                sm100::named_barrier(1, 256);
+                finish = flags[1];
+                if (finish) __threadfence();
+            }
+            if (finish) {
+                for (int jj0 = j0; jj0 < j0 + span; jj0 += 16) {
+                    float va[16], vg[16];
+                    if (p.splits == 1) {
+                        sm100::tmem_ld16(tacc + jj0, va);
+                        if (p.glu) sm100::tmem_ld16(tacc + BW / 2 + jj0, vg);
+                    } else {
+#pragma unroll
+                        for (int x = 0; x < 16; ++x) va[x] = vg[x] = 0.0f;
+                        if (row_ok)
+                            for (int s = 0; s < p.splits; ++s) {
+                                const float *src = wsb + ((int64_t)s * 128 + row) * BW;
+#pragma unroll
+                                for (int x = 0; x < 16; x += 4) {
+                                    const float4 a4 = __ldcg((const float4 *)(src + jj0 + x));
+                                    va[x] += a4.x; va[x + 1] += a4.y; va[x + 2] += a4.z; va[x + 3] += a4.w;
+                                    if (p.glu) {
+                                        const float4 g4 = __ldcg((const float4 *)(src + BW / 2 + jj0 + x));
+                                        vg[x] += g4.x; vg[x + 1] += g4.y; vg[x + 2] += g4.z; vg[x + 3] += g4.w;
+                                    }
+                                }
+                            }
+                    }
+                    if (!row_ok) continue;
+                    const int n0 = n_base + jj0;
+                    if (n0 >= nout) continue;
+                    const int cnt = min(16, nout - n0);
+                    if (p.vec && cnt == 16) {
+                        // 16-byte loads and stores (alignment of every pointer and stride checked on the host)
+                        float cin[16], bv[16], bg[16];
+#pragma unroll
+                        for (int x = 0; x < 16; x += 4) {
+                            float4 c4 = make_float4(0.f, 0.f, 0.f, 0.f), b4 = c4, g4 = c4;
+                            if (p.e.accumulate) c4 = *(const float4 *)(C32 + rowbase + n0 + x);
+                            if (p.e.bias) {
+                                b4 = __ldg((const float4 *)(p.e.bias + brow + n0 + x));
+                                if (p.glu) g4 = __ldg((const float4 *)(p.e.bias + brow + n0 + x + p.N / 2));
+                            }
+                            cin[x] = c4.x; cin[x + 1] = c4.y; cin[x + 2] = c4.z; cin[x + 3] = c4.w;
+                            bv[x] = b4.x; bv[x + 1] = b4.y; bv[x + 2] = b4.z; bv[x + 3] = b4.w;
+                            bg[x] = g4.x; bg[x + 1] = g4.y; bg[x + 2] = g4.z; bg[x + 3] = g4.w;
+                        }
+                        float o[16];
+#pragma unroll
+                        for (int x = 0; x < 16; ++x) {
+                            float v;
+                            if (p.glu) {
+                                v = (va[x] + bv[x]) * fast_sigmoid(vg[x] + bg[x]) * p.e.alpha;
+                            } else {
+                                v = va[x] + bv[x];
+                                if (p.e.act == NEMO_ACT_SILU) v = v * fast_sigmoid(v);
+                                else if (p.e.act == NEMO_ACT_RELU) v = fmaxf(v, 0.0f);
+                                v *= p.e.alpha;
+                            }
+                            o[x] = v + cin[x];
+                        }
+                        const int64_t idx = rowbase + n0;
+                        if (p.e.c_fmt == NEMO_FMT_F32) {
+#pragma unroll
+                            for (int x = 0; x < 16; x += 4) *(float4 *)(C32 + idx + x) = make_float4(o[x], o[x + 1], o[x + 2], o[x + 3]);
+                        } else {
+                            uint32_t h[8], l[8];
+#pragma unroll
+                            for (int x = 0; x < 8; ++x) {
+                                const uint16_t h0 = nb::f2bf(o[2 * x]), h1 = nb::f2bf(o[2 * x + 1]);
+                                const uint16_t l0 = nb::f2bf(o[2 * x] - nb::bf2f(h0)), l1 = nb::f2bf(o[2 * x + 1] - nb::bf2f(h1));
+                                h[x] = (uint32_t)h0 | ((uint32_t)h1 << 16);
+                                l[x] = (uint32_t)l0 | ((uint32_t)l1 << 16);
+                            }
+                            uint4 *dh = (uint4 *)(C16 + idx), *dl = (uint4 *)(C16 + idx + p.e.c_plane);
+                            dh[0] = make_uint4(h[0], h[1], h[2], h[3]);
+                            dh[1] = make_uint4(h[4], h[5], h[6], h[7]);
+                            dl[0] = make_uint4(l[0], l[1], l[2], l[3]);
+                            dl[1] = make_uint4(l[4], l[5], l[6], l[7]);
+                        }
+                        if (p.e.c32)
+#pragma unroll
+                            for (int x = 0; x < 16; x += 4)
+                                *(float4 *)(p.e.c32 + (int64_t)m * p.e.ldc32 + n0 + x) = make_float4(o[x], o[x + 1], o[x + 2], o[x + 3]);
+                        continue;
+                    }
+                    float cin[16], bv[16], bg[16];
+#pragma unroll
+                    for (int x = 0; x < 16; ++x) {
+                        cin[x] = bv[x] = bg[x] = 0.0f;
+                        if (x < cnt) {
+                            if (p.e.accumulate) cin[x] = C32[rowbase + n0 + x];
+                            if (p.e.bias) {
+                                bv[x] = p.e.bias[brow + n0 + x];
+                                if (p.glu) bg[x] = p.e.bias[brow + n0 + x + p.N / 2];
+                            }
+                        }
+                    }
+#pragma unroll
+                    for (int x = 0; x < 16; ++x) {
+                        if (x >= cnt) break;
+                        float v;
+                        if (p.glu) {
+                            v = (va[x] + bv[x]) * fast_sigmoid(vg[x] + bg[x]) * p.e.alpha;
+                        } else {
+                            v = va[x] + bv[x];
+                            if (p.e.act == NEMO_ACT_SILU) v = v * fast_sigmoid(v);
+                            else if (p.e.act == NEMO_ACT_RELU) v = fmaxf(v, 0.0f);
+                            v *= p.e.alpha;
+                        }
+                        v += cin[x];
+                        const int64_t idx = rowbase + n0 + x;
+                        if (p.e.c_fmt == NEMO_FMT_F32) {
+                            C32[idx] = v;
+                        } else {
+                            const uint16_t hi = nb::f2bf(v);
+                            C16[idx] = hi;
+                            C16[idx + p.e.c_plane] = nb::f2bf(v - nb::bf2f(hi));
+                        }
+                        if (p.e.c32) p.e.c32[(int64_t)m * p.e.ldc32 + n0 + x] = v;
+                    }
+                }
+                if (p.splits > 1 && etid == 0) p.counters[tile] = 0;
+            }
+            sm100::tc_fence_before();
+            sm100::named_barrier(1, 256);
+            if (etid == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(sm100::smem_u32(&acc_empty[b])) : "memory");
+            if (!ok) break;
+        }
+    }
+    sm100::tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        sm100::tc_fence_after();
+        sm100::tmem_dealloc(tmem, C::TMEM_COLS);
+    }
+}
+
 // ---- host side -------------------------------------------------------------------------------
 typedef CUresult (*EncodeTiled)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *, const cuuint64_t *, const cuuint32_t *,
                                 const cuuint32_t *, CUtensorMapInterleave, CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
@@ -335,6 +627,8 @@ int init_once() {
     cudaFuncSetAttribute(gemm_tc_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<64>::SMEM);
     cudaFuncSetAttribute(gemm_tc_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<128>::SMEM);
     cudaFuncSetAttribute(gemm_tc_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<256>::SMEM);
+    cudaFuncSetAttribute(gemm_tcr_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, CfgR<128>::SMEM);
+    cudaFuncSetAttribute(gemm_tcr_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize, CfgR<256>::SMEM);
     g_encode = (EncodeTiled)fn;
     return 0;
 }
@@ -385,23 +679,105 @@ int launch(const nemo_gemm_args_t *a, cudaStream_t st) {
     return nb_check_launch("gemm_tc_kernel");
 }
 
+// Plan of an activation-major launch: BW weight rows per tile and the k-split. The split count
+// fills the SMs when there are fewer tiles than SMs (k-blocks of at least 4 per split).
+struct PlanR {
+    int bw, tiles, splits, kb_per_split, units;
+    long long cost;  // rounds of units over the SMs x (BW x k-blocks per unit): proportional to time
+};
+
+PlanR plan_r(const nemo_gemm_args_t *a, int bw) {
+    PlanR r;
+    const bool glu = a->act == NEMO_ACT_GLU;
+    const int kblocks = (a->K + BK - 1) / BK;
+    const int n_wtiles = glu ? (a->N / 2) / (bw / 2) : (a->N + bw - 1) / bw;
+    r.bw = bw;
+    r.tiles = n_wtiles * ((a->M + 127) / 128);
+    int splits = 1;
+    if (r.tiles < g_sms) {
+        splits = g_sms / r.tiles;
+        if (splits > kblocks / 4) splits = kblocks / 4;
+        if (splits < 1) splits = 1;
+        if ((size_t)r.tiles * splits * 128 * bw > g_ws_floats || r.tiles > g_ncounters) splits = 1;
+    }
+    r.kb_per_split = (kblocks + splits - 1) / splits;
+    r.splits = (kblocks + r.kb_per_split - 1) / r.kb_per_split;
+    r.units = r.tiles * r.splits;
+    const long long rounds = (r.units + g_sms - 1) / g_sms;
+    r.cost = rounds * bw * r.kb_per_split + (r.splits > 1 ? bw * 2 : 0);
+    return r;
+}
+
+// 16-byte epilogue accesses: every row start, plane offset and bias row of the output must keep
+// a 16-column chunk on a 16-byte boundary.
+int vec_ok(const nemo_gemm_args_t *a) {
+    const bool f32 = a->c_fmt == NEMO_FMT_F32;
+    const int64_t q = f32 ? 4 : 8;  // elements per 16 bytes
+    const uintptr_t c = (uintptr_t)a->C;
+    if (c & 15) return 0;
+    if (a->ldc % q || a->gstride % q || (!f32 && a->c_plane % 8)) return 0;
+    if (a->accumulate && !f32) return 0;
+    if (a->bias && (((uintptr_t)a->bias & 15) || a->bias_gstride % 4 || (a->act == NEMO_ACT_GLU && (a->N / 2) % 4))) return 0;
+    if (a->c32 && (((uintptr_t)a->c32 & 15) || a->ldc32 % 4)) return 0;
+    return 1;
+}
+
+template <int BW>
+int launch_r(const nemo_gemm_args_t *a, const PlanR &pl, cudaStream_t st) {
+    CUtensorMap mw, mh, ml;
+    const bool glu = a->act == NEMO_ACT_GLU;
+    if (make_map(&mw, a->W, a->K, a->N, a->ldw, glu ? BW / 2 : BW)) return -1;
+    const uint16_t *A = (const uint16_t *)a->A;
+    if (make_map(&mh, A, a->K, a->M, a->lda, 128) || make_map(&ml, A + a->a_plane, a->K, a->M, a->lda, 128)) return -1;
+    TcArgs p;
+    memset(&p, 0, sizeof p);
+    p.M = a->M; p.N = a->N; p.K = a->K;
+    p.kblocks = (a->K + BK - 1) / BK;
+    p.glu = glu;
+    p.n_wtiles = glu ? (a->N / 2) / (BW / 2) : (a->N + BW - 1) / BW;
+    p.n_mtiles = (a->M + 127) / 128;
+    p.splits = pl.splits;
+    p.kb_per_split = pl.kb_per_split;
+    p.units = pl.units;
+    p.dynM = a->dynM;
+    p.rowoff = a->rowoff;
+    p.e = nb::make_epi(a);
+    p.ws = g_ws;
+    p.counters = g_counters;
+    p.vec = vec_ok(a);
+    const int grid = p.units < g_sms ? p.units : g_sms;
+    gemm_tcr_kernel<BW><<<grid, THREADS, CfgR<BW>::SMEM, st>>>(mw, mh, ml, p);
+    return nb_check_launch("gemm_tcr_kernel");
+}
+
+int launch_rows(const nemo_gemm_args_t *a, cudaStream_t st) {
+    const bool glu = a->act == NEMO_ACT_GLU;
+    const PlanR p256 = plan_r(a, 256), p128 = plan_r(a, 128);
+    const bool ok256 = !glu || (a->N / 2) % 128 == 0;
+    if (ok256 && p256.cost <= p128.cost) return launch_r<256>(a, p256, st);
+    return launch_r<128>(a, p128, st);
+}
+
 }  // namespace
 
 // One-time setup (driver entry point, split-K workspace): call before capturing a CUDA graph.
 extern "C" int nb_gemm_tc_init(void) { return init_once(); }
 
-int nb_gemm_tc(const nemo_gemm_args_t *a, void *stream) {
+// layout: 0 = by row count, 1 = weight-major tiles, 2 = activation-major tiles
+int nb_gemm_tc_layout(const nemo_gemm_args_t *a, int layout, void *stream) {
     if (init_once()) return -1;
     if (a->act == NEMO_ACT_GLU && ((a->N / 2) % 64)) return nb_set_error("tensor-core GEMM: GLU needs N/2 to be a multiple of 64");
     if (a->K % 8) return nb_set_error("tensor-core GEMM: K must be a multiple of 8");
     cudaStream_t st = (cudaStream_t)stream;
+    if (layout == 0) layout = a->M >= 128 ? 2 : 1;
+    if (layout == 2) return launch_rows(a, st);
     if (a->M <= 16) return launch<16>(a, st);
     if (a->M <= 32) return launch<32>(a, st);
     if (a->M <= 64) return launch<64>(a, st);
-    // 128-row activation tiles beat 256 at batch sizes (four pipeline stages instead of two,
-    // more units per SM to overlap epilogues): measured 1.3-2x at 1792 rows
     return launch<128>(a, st);
 }
+
+int nb_gemm_tc(const nemo_gemm_args_t *a, void *stream) { return nb_gemm_tc_layout(a, 0, stream); }
 
 extern "C" int nemo_gpu_check_device_errors(void) {
     int v = 0;

@@ -65,3 +65,69 @@ def test_tc_gemm_is_deterministic():
     a = run_gemm(A, W, kind=2, a_fmt=1)
     b = run_gemm(A, W, kind=2, a_fmt=1)
     assert np.array_equal(a, b)
+
+
+# ---- activation-major tiles (kind 5): 128 activation rows x 128/256 weight rows per tile ----
+
+@pytest.mark.parametrize("M", [128, 200, 600, 1792])
+@pytest.mark.parametrize("act", [0, 1, 2, 3])
+def test_tcr_gemm_epilogues(M, act):
+    rng = np.random.default_rng(3000 + M * 4 + act)
+    N, K = 512, 320
+    A = rng.standard_normal((M, K)).astype(np.float32)
+    W = bf16(rng, (N, K))
+    b = (rng.standard_normal(N) * 0.1).astype(np.float32)
+    C0 = rng.standard_normal((M, N // 2 if act == 3 else N)).astype(np.float32)
+    got = run_gemm(A, W, b, C0, act=act, acc=1, alpha=0.5, kind=5, a_fmt=1)
+    ref = orc.gemm(A, W, b, C0=C0, act=act, accumulate=True, alpha=0.5)
+    assert rel_err(got, ref) < BF16X2_TOL
+
+
+@pytest.mark.parametrize("shape", [(3072, 1024), (4096, 1024), (1024, 4096), (2048, 1024), (640, 1024), (1025, 640), (1024, 4352)])
+def test_tcr_gemm_model_shapes(shape):
+    rng = np.random.default_rng(11 + sum(shape))
+    N, K = shape
+    A = rng.standard_normal((1792, K)).astype(np.float32)
+    W = bf16(rng, (N, K), 0.02)
+    got = run_gemm(A, W, kind=5, a_fmt=1)
+    assert rel_err(got, orc.gemm(A, W)) < BF16X2_TOL
+
+
+@pytest.mark.parametrize("act", [0, 3])
+def test_tcr_gemm_split_k(act):
+    # one or two tiles: the k-blocks are split over many CTAs and reduced in a fixed order
+    rng = np.random.default_rng(23 + act)
+    M, N, K = 130, 256, 4096
+    A = rng.standard_normal((M, K)).astype(np.float32)
+    W = bf16(rng, (N, K), 0.02)
+    b = (rng.standard_normal(N) * 0.1).astype(np.float32)
+    C0 = rng.standard_normal((M, N // 2 if act == 3 else N)).astype(np.float32)
+    got = run_gemm(A, W, b, C0, act=act, acc=1, alpha=0.5, kind=5, a_fmt=1)
+    assert rel_err(got, orc.gemm(A, W, b, C0=C0, act=act, accumulate=True, alpha=0.5)) < BF16X2_TOL
+    again = run_gemm(A, W, b, C0, act=act, acc=1, alpha=0.5, kind=5, a_fmt=1)
+    assert np.array_equal(got, again)
+
+
+def test_tcr_gemm_row_mapping_dynamic_rows():
+    rng = np.random.default_rng(29)
+    streams, c, N, K, cap, off = 40, 7, 256, 256, 30, 9
+    A = rng.standard_normal((streams * c, K)).astype(np.float32)
+    W = bf16(rng, (N, K))
+    bias = rng.standard_normal((streams, N)).astype(np.float32)
+    got = run_gemm(A, W, bias.ravel(), kind=5, a_fmt=1, rpg=c, gstride=cap * N, rowoff=off, crows=streams * cap, bias_gstride=N)
+    got = got.reshape(streams, cap, N)
+    for s in range(streams):
+        assert rel_err(got[s, off:off + c], orc.gemm(A[s * c:(s + 1) * c], W, bias[s])) < BF16X2_TOL
+        assert np.all(got[s, :off] == 0) and np.all(got[s, off + c:] == 0)
+    got = run_gemm(A, W, kind=5, a_fmt=1, dynM=150)
+    assert rel_err(got[:150], orc.gemm(A[:150], W)) < BF16X2_TOL and np.all(got[150:] == 0)
+
+
+def test_tcr_matches_weight_major_tiles():
+    rng = np.random.default_rng(31)
+    A = rng.standard_normal((448, 1024)).astype(np.float32)
+    W = bf16(rng, (2048, 1024), 0.02)
+    for act in (1, 3):
+        a = run_gemm(A, W, act=act, kind=4, a_fmt=1)
+        b = run_gemm(A, W, act=act, kind=5, a_fmt=1)
+        assert rel_err(b, a) < 1e-6
