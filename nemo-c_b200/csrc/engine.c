@@ -369,8 +369,12 @@ static int launch_encoder(nb_engine_t *e, int nwin, int c) {
 /* ---- greedy RNNT decode of the chunk's c frames for every stream (src/decoder.c:92-127) --- */
 /* One greedy-decoding iteration of every stream (one frame decision each), ending with the
    read-back of the still-active count. */
-static int dec_iteration(nb_engine_t *e, int c, int unused) {
-    (void)unused;
+static int dec_max_iterations(const nb_engine_t *e, int c) { return c * (e->m->g.max_symbols + 1) + 2; }
+
+/* One greedy iteration over all streams (src/decoder.c:97-123). cond is the WHILE-loop handle
+   when the iteration is the body of the decoder graph (the device decides whether it repeats),
+   0 when the host drives the loop (the active count is then copied back each iteration). */
+static int dec_iteration_body(nb_engine_t *e, int c, unsigned long long cond) {
     const nb_model_t *m = e->m;
     const nb_config_t *g = &m->g;
     const int B = e->B, PH = g->pred_hidden, JH = g->joint_hidden;
@@ -399,11 +403,63 @@ static int dec_iteration(nb_engine_t *e, int c, int unused) {
                                     g->num_classes, d->idx, NULL, st));
         else
             KL(nb_joint_argmax_rows(e->joint_enc, JH, d->pred, JH, 1, m->joint_out_w, m->joint_out_b, g->num_classes, JH, B, d->erow, d->idx, NULL, st));
-        KL(nb_dec_update(d, c, PH, g->blank_id, g->max_symbols, st));
-        if (cudaMemcpyAsync(e->h_cnt, d->cnt, 2 * sizeof(int), cudaMemcpyDeviceToHost, st) != cudaSuccess)
+        KL(nb_dec_update(d, c, PH, g->blank_id, g->max_symbols, dec_max_iterations(e, c), cond, st));
+        if (!cond && cudaMemcpyAsync(e->h_cnt, d->cnt, 2 * sizeof(int), cudaMemcpyDeviceToHost, st) != cudaSuccess)
             return nb_set_error("decoder: %s", cudaGetErrorString(cudaGetLastError()));
     }
     return 0;
+}
+
+static int dec_iteration(nb_engine_t *e, int c, int unused) {
+    (void)unused;
+    return dec_iteration_body(e, c, 0);
+}
+
+/* The greedy loop of a chunk as one graph: a WHILE node whose body is one iteration; the body's
+   last kernel sets the loop condition on the device, so no host round trip happens per emitted
+   token (src/decoder.c:97-123 loops on the host). Cached per chunk length c. Returns the slot,
+   or -1 on error, or -2 when the cache is full (the host loop is used instead). */
+static int dec_graph(nb_engine_t *e, int c) {
+    for (int i = 0; i < e->ngraphs; ++i)
+        if (e->graphs[i].kind == 2 && e->graphs[i].k1 == c) return i;
+    if (e->ngraphs == NB_MAX_GRAPHS) return -2;
+    cudaGraph_t G = NULL;
+    cudaGraphConditionalHandle h;
+    if (cudaGraphCreate(&G, 0) != cudaSuccess) return nb_set_error("decoder graph: %s", cudaGetErrorString(cudaGetLastError()));
+    struct cudaGraphNodeParams p;
+    memset(&p, 0, sizeof p);
+    cudaGraphNode_t node;
+    if (cudaGraphConditionalHandleCreate(&h, G, 1, cudaGraphCondAssignDefault) != cudaSuccess) goto fail;
+    p.type = cudaGraphNodeTypeConditional;
+    p.conditional.handle = h;
+    p.conditional.type = cudaGraphCondTypeWhile;
+    p.conditional.size = 1;
+    if (cudaGraphAddNode(&node, G, NULL, 0, &p) != cudaSuccess) goto fail;
+    cudaGraph_t body = p.conditional.phGraph_out[0];
+    if (cudaStreamBeginCaptureToGraph(e->st, body, NULL, NULL, 0, cudaStreamCaptureModeThreadLocal) != cudaSuccess) goto fail;
+    nb_set_launch_counting(0);
+    const int rc = dec_iteration_body(e, c, (unsigned long long)h);
+    nb_set_launch_counting(1);
+    cudaGraph_t captured = NULL;
+    const cudaError_t ce = cudaStreamEndCapture(e->st, &captured);
+    if (rc || ce != cudaSuccess) {
+        cudaGraphDestroy(G);
+        return rc ? -1 : nb_set_error("decoder graph capture: %s", cudaGetErrorString(ce));
+    }
+    cudaGraphExec_t exec;
+    if (cudaGraphInstantiate(&exec, G, 0) != cudaSuccess) goto fail;
+    const int slot = e->ngraphs++;
+    e->graphs[slot].kind = 2;
+    e->graphs[slot].k1 = c;
+    e->graphs[slot].k2 = 0;
+    e->graphs[slot].exec = exec;
+    e->graphs[slot].kernels = nb_graph_kernel_nodes(body); /* per iteration */
+    cudaGraphDestroy(G);
+    return slot;
+fail:
+    nb_set_error("decoder graph: %s", cudaGetErrorString(cudaGetLastError()));
+    cudaGraphDestroy(G);
+    return -1;
 }
 
 static int enc_body(nb_engine_t *e, int nwin, int c) { return launch_encoder(e, nwin, c); }
@@ -450,7 +506,23 @@ static int run_decoder(nb_engine_t *e, int c, char *err, size_t errlen) {
     DecState *d = &e->dec;
     cudaStream_t st = e->st;
     KL(nb_dec_chunk_init(d, c, st));
-    const int max_it = c * (g->max_symbols + 1) + 2;
+    const int max_it = dec_max_iterations(e, c);
+    (void)g;
+    if (e->use_graphs) {
+        const int slot = dec_graph(e, c);
+        if (slot == -1) { snprintf(err, errlen, "%s", nemo_gpu_last_error()); return -1; }
+        if (slot >= 0) {
+            if (cudaGraphLaunch(e->graphs[slot].exec, st) != cudaSuccess ||
+                cudaMemcpyAsync(e->h_cnt, d->cnt, 4 * sizeof(int), cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+                cudaStreamSynchronize(st) != cudaSuccess) {
+                snprintf(err, errlen, "decoder: %s", cudaGetErrorString(cudaGetLastError()));
+                return -1;
+            }
+            nb_count_launches(e->graphs[slot].kernels * (uint64_t)e->h_cnt[2]);
+            if (e->h_cnt[1] != 0) { snprintf(err, errlen, "decoder did not finish the chunk in %d iterations", max_it); return -1; }
+            return 0;
+        }
+    }
     int it;
     for (it = 0; it < max_it; ++it) {
         if (run_graph(e, 1, c, 0, dec_iteration)) { snprintf(err, errlen, "decoder: %s", nemo_gpu_last_error()); return -1; }

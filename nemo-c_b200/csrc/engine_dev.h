@@ -11,7 +11,8 @@ extern "C" {
 typedef struct {
     int streams, tok_cap;
     int *t, *symbols, *active, *pred_valid, *last_token, *ntok, *tokens;
-    int *need_idx, *erow, *idx, *cnt; /* cnt[0] streams needing the prediction net, cnt[1] still active */
+    int *need_idx, *erow, *idx, *cnt; /* cnt[0] streams needing the prediction net, cnt[1] still active,
+                                         cnt[2] iterations this chunk, cnt[3] dec_update blocks done */
     float *h, *c, *hp, *cp;           /* [2][streams][PH] committed / provisional LSTM state */
     float *pred;                      /* [streams][JH] joint prediction projection */
     float *A0, *A1, *gates, *hp1c, *predc; /* compact per-iteration work rows */
@@ -32,7 +33,10 @@ int nb_dec_plan(const DecState *d, int c, void *stream);
 int nb_dec_gather(const DecState *d, const uint16_t *embed, int PH, int blank, void *stream);
 int nb_dec_cell(const DecState *d, int layer, int PH, float *next, int64_t next_ld, int64_t next_plane, void *stream);
 int nb_dec_scatter_pred(const DecState *d, int JH, void *stream);
-int nb_dec_update(const DecState *d, int c, int PH, int blank, int max_symbols, void *stream);
+/* cond: handle of the CUDA graph WHILE loop this launch belongs to (0 outside such a loop); the
+   last block sets it to "another iteration" while streams remain active and fewer than max_it
+   iterations ran. cnt[2] counts the iterations of the chunk. */
+int nb_dec_update(const DecState *d, int c, int PH, int blank, int max_symbols, int max_it, unsigned long long cond, void *stream);
 int nb_dec_reset(const DecState *d, int PH, int blank, void *stream);
 int nb_joint_argmax_rows(const float *enc, int64_t enc_ld, const float *pred, int64_t pred_ld, int pred_rpg, const uint16_t *W,
                          const float *bias, int V, int H, int rows, const int *enc_row_of, int *out_idx, float *out_val, void *stream);

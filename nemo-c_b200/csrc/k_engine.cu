@@ -28,6 +28,7 @@ __global__ void compact_kernel(float *kv, float *din, int layers, int streams, i
 
 __global__ void dec_chunk_init_kernel(DecState d, int streams, int c) {
     const int b = blockIdx.x * blockDim.x + threadIdx.x;
+    if (b == 0) { d.cnt[2] = 0; d.cnt[3] = 0; } // iterations run, blocks of dec_update done
     if (b >= streams) return;
     d.t[b] = 0;
     d.symbols[b] = 0;
@@ -95,33 +96,48 @@ __global__ void dec_scatter_pred_kernel(DecState d, int JH) {
 // One decision per active stream (src/decoder.c:106-121): blank -> next frame, symbols = 0;
 // token -> emit, commit the provisional LSTM state, re-score the same frame unless max_symbols
 // tokens came from it.
-__global__ void dec_update_kernel(DecState d, int c, int PH, int blank, int max_symbols) {
+// One greedy step per active stream (src/decoder.c:104-122). When the decoder runs as a CUDA
+// graph WHILE loop (cond != 0), the last block to finish sets the loop condition: another
+// iteration while some stream still has frames, at most max_it iterations per chunk.
+__global__ void dec_update_kernel(DecState d, int c, int PH, int blank, int max_symbols, int max_it, cudaGraphConditionalHandle cond) {
     const int b = blockIdx.x;
-    if (!d.active[b]) return;
-    const int k = d.idx[b];
-    if (k != blank) {
+    const bool live = d.active[b];
+    const int k = live ? d.idx[b] : blank;
+    if (live && k != blank) {
         for (int l = 0; l < 2; ++l) {
             const int64_t sb = ((int64_t)l * d.streams + b) * PH;
             for (int j = threadIdx.x; j < PH; j += blockDim.x) { d.h[sb + j] = d.hp[sb + j]; d.c[sb + j] = d.cp[sb + j]; }
         }
     }
     if (threadIdx.x != 0) return;
-    int t = d.t[b], sym = d.symbols[b];
-    if (k == blank) {
-        sym = 0;
-        ++t;
-    } else {
-        if (d.ntok[b] < d.tok_cap) d.tokens[(int64_t)b * d.tok_cap + d.ntok[b]] = k;
-        d.ntok[b]++;
-        d.last_token[b] = k;
-        d.pred_valid[b] = 0;
-        if (++sym >= max_symbols) { sym = 0; ++t; }
+    if (live) {
+        int t = d.t[b], sym = d.symbols[b];
+        if (k == blank) {
+            sym = 0;
+            ++t;
+        } else {
+            if (d.ntok[b] < d.tok_cap) d.tokens[(int64_t)b * d.tok_cap + d.ntok[b]] = k;
+            d.ntok[b]++;
+            d.last_token[b] = k;
+            d.pred_valid[b] = 0;
+            if (++sym >= max_symbols) { sym = 0; ++t; }
+        }
+        d.t[b] = t;
+        d.symbols[b] = sym;
+        const int act = t < c;
+        d.active[b] = act;
+        if (act) atomicAdd(&d.cnt[1], 1);
     }
-    d.t[b] = t;
-    d.symbols[b] = sym;
-    const int act = t < c;
-    d.active[b] = act;
-    if (act) atomicAdd(&d.cnt[1], 1);
+    if (cond) {
+        __threadfence();
+        if (atomicAdd(&d.cnt[3], 1) == (int)gridDim.x - 1) {
+            __threadfence();
+            const int it = d.cnt[2] + 1;
+            d.cnt[2] = it;
+            d.cnt[3] = 0;
+            cudaGraphSetConditional(cond, (atomicAdd(&d.cnt[1], 0) > 0 && it < max_it) ? 1u : 0u);
+        }
+    }
 }
 
 __global__ void dec_reset_kernel(DecState d, int PH, int blank) {
@@ -160,8 +176,8 @@ extern "C" int nb_dec_scatter_pred(const DecState *d, int JH, void *stream) {
     dec_scatter_pred_kernel<<<d->streams, 128, 0, (cudaStream_t)stream>>>(*d, JH);
     return nb_check_launch("dec_scatter_pred_kernel");
 }
-extern "C" int nb_dec_update(const DecState *d, int c, int PH, int blank, int max_symbols, void *stream) {
-    dec_update_kernel<<<d->streams, 128, 0, (cudaStream_t)stream>>>(*d, c, PH, blank, max_symbols);
+extern "C" int nb_dec_update(const DecState *d, int c, int PH, int blank, int max_symbols, int max_it, unsigned long long cond, void *stream) {
+    dec_update_kernel<<<d->streams, 128, 0, (cudaStream_t)stream>>>(*d, c, PH, blank, max_symbols, max_it, (cudaGraphConditionalHandle)cond);
     return nb_check_launch("dec_update_kernel");
 }
 extern "C" int nb_dec_reset(const DecState *d, int PH, int blank, void *stream) {
