@@ -17,6 +17,7 @@
 // MMAs, warps 2-9 run the epilogue (warp w reads TMEM lanes 32*(w%4) .. +31; warps w and w+4
 // split the columns). Every wait is bounded: on a timeout the CTA records an error and unwinds.
 #include <cuda.h>
+#include <cuda_bf16.h>
 #include <cstdio>
 #include <cstring>
 #include <mutex>
@@ -54,7 +55,8 @@ struct Cfg {
     static constexpr int SMEM = 1024 + STAGES * STAGE + 1024 + XCH * 4 + BN * 12;
 };
 
-__device__ __forceinline__ float fast_sigmoid(float x) { return __frcp_rn(1.0f + __expf(-x)); }
+// 1 / (1 + e^-x) with the hardware exp2 and reciprocal approximations (relative error ~1e-6)
+__device__ __forceinline__ float fast_sigmoid(float x) { return __fdividef(1.0f, 1.0f + __expf(-x)); }
 
 // Epilogue for one 16-row chunk of one weight row: va[jj] belongs to activation row m0+j0+jj and
 // output column n. Row offsets (group stride, in-group row offset, ldc) were precomputed once
@@ -318,6 +320,64 @@ struct CfgR {
     static constexpr int SMEM = 1024 + STAGES * STAGE + 1024;    // stages | barriers
 };
 
+// 16 consecutive output columns of one activation row (activation-major epilogue):
+// bias -> activation (ACT: NEMO_ACT_*, GLU pairs value and gate) -> x alpha -> (+= C) -> store as
+// fp32 or bf16 hi/lo planes (BF16 = true), plus the optional fp32 copy. 16-byte accesses.
+template <int ACT, bool BF16>
+__device__ __forceinline__ void epi16(const TcArgs &p, int64_t rowbase, int64_t brow, int m, int n0, const float (&va)[16], const float (&vg)[16]) {
+    float *__restrict__ C32 = (float *)p.e.C;
+    float o[16], bv[16], bg[16];
+#pragma unroll
+    for (int x = 0; x < 16; x += 4) {
+        float4 b4 = make_float4(0.f, 0.f, 0.f, 0.f), g4 = b4;
+        if (p.e.bias) {
+            b4 = __ldg((const float4 *)(p.e.bias + brow + n0 + x));
+            if (ACT == NEMO_ACT_GLU) g4 = __ldg((const float4 *)(p.e.bias + brow + n0 + x + p.N / 2));
+        }
+        bv[x] = b4.x; bv[x + 1] = b4.y; bv[x + 2] = b4.z; bv[x + 3] = b4.w;
+        bg[x] = g4.x; bg[x + 1] = g4.y; bg[x + 2] = g4.z; bg[x + 3] = g4.w;
+    }
+    const float alpha = p.e.alpha;
+#pragma unroll
+    for (int x = 0; x < 16; ++x) {
+        float v = va[x] + bv[x];
+        if (ACT == NEMO_ACT_GLU) v = v * fast_sigmoid(vg[x] + bg[x]);
+        else if (ACT == NEMO_ACT_SILU) v = v * fast_sigmoid(v);
+        else if (ACT == NEMO_ACT_RELU) v = fmaxf(v, 0.0f);
+        o[x] = v * alpha;
+    }
+    const int64_t idx = rowbase + n0;
+    if (!BF16) {
+        if (p.e.accumulate) {
+#pragma unroll
+            for (int x = 0; x < 16; x += 4) {
+                const float4 c4 = *(const float4 *)(C32 + idx + x);
+                o[x] += c4.x; o[x + 1] += c4.y; o[x + 2] += c4.z; o[x + 3] += c4.w;
+            }
+        }
+#pragma unroll
+        for (int x = 0; x < 16; x += 4) *(float4 *)(C32 + idx + x) = make_float4(o[x], o[x + 1], o[x + 2], o[x + 3]);
+    } else {
+        uint16_t *__restrict__ C16 = (uint16_t *)p.e.C;
+        uint32_t h[8], l[8];
+#pragma unroll
+        for (int x = 0; x < 8; ++x) {
+            const __nv_bfloat162 hv = __floats2bfloat162_rn(o[2 * x], o[2 * x + 1]);
+            const __nv_bfloat162 lv = __floats2bfloat162_rn(o[2 * x] - __low2float(hv), o[2 * x + 1] - __high2float(hv));
+            h[x] = *(const uint32_t *)&hv;
+            l[x] = *(const uint32_t *)&lv;
+        }
+        uint4 *dh = (uint4 *)(C16 + idx), *dl = (uint4 *)(C16 + idx + p.e.c_plane);
+        dh[0] = make_uint4(h[0], h[1], h[2], h[3]);
+        dh[1] = make_uint4(h[4], h[5], h[6], h[7]);
+        dl[0] = make_uint4(l[0], l[1], l[2], l[3]);
+        dl[1] = make_uint4(l[4], l[5], l[6], l[7]);
+    }
+    if (p.e.c32)
+#pragma unroll
+        for (int x = 0; x < 16; x += 4) *(float4 *)(p.e.c32 + (int64_t)m * p.e.ldc32 + n0 + x) = make_float4(o[x], o[x + 1], o[x + 2], o[x + 3]);
+}
+
 template <int BW>
 __global__ void __launch_bounds__(THREADS, 1) gemm_tcr_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmAh,
                                                             const __grid_constant__ CUtensorMap tmAl, const __grid_constant__ TcArgs p) {
@@ -487,57 +547,19 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tcr_kernel(const __grid_const
                     if (n0 >= nout) continue;
                     const int cnt = min(16, nout - n0);
                     if (p.vec && cnt == 16) {
-                        // 16-byte loads and stores (alignment of every pointer and stride checked on the host)
-                        float cin[16], bv[16], bg[16];
-#pragma unroll
-                        for (int x = 0; x < 16; x += 4) {
-                            float4 c4 = make_float4(0.f, 0.f, 0.f, 0.f), b4 = c4, g4 = c4;
-                            if (p.e.accumulate) c4 = *(const float4 *)(C32 + rowbase + n0 + x);
-                            if (p.e.bias) {
-                                b4 = __ldg((const float4 *)(p.e.bias + brow + n0 + x));
-                                if (p.glu) g4 = __ldg((const float4 *)(p.e.bias + brow + n0 + x + p.N / 2));
-                            }
-                            cin[x] = c4.x; cin[x + 1] = c4.y; cin[x + 2] = c4.z; cin[x + 3] = c4.w;
-                            bv[x] = b4.x; bv[x + 1] = b4.y; bv[x + 2] = b4.z; bv[x + 3] = b4.w;
-                            bg[x] = g4.x; bg[x + 1] = g4.y; bg[x + 2] = g4.z; bg[x + 3] = g4.w;
+                        // 16-byte accesses (alignment of every pointer and stride checked on the host),
+                        // the activation / output format resolved at compile time
+                        const int mode = (p.glu ? 3 : p.e.act) | (p.e.c_fmt == NEMO_FMT_F32 ? 0 : 4);
+                        switch (mode) {
+                        case 0: epi16<0, false>(p, rowbase, brow, m, n0, va, vg); break;
+                        case 1: epi16<1, false>(p, rowbase, brow, m, n0, va, vg); break;
+                        case 2: epi16<2, false>(p, rowbase, brow, m, n0, va, vg); break;
+                        case 3: epi16<3, false>(p, rowbase, brow, m, n0, va, vg); break;
+                        case 4: epi16<0, true>(p, rowbase, brow, m, n0, va, vg); break;
+                        case 5: epi16<1, true>(p, rowbase, brow, m, n0, va, vg); break;
+                        case 6: epi16<2, true>(p, rowbase, brow, m, n0, va, vg); break;
+                        default: epi16<3, true>(p, rowbase, brow, m, n0, va, vg); break;
                         }
-                        float o[16];
-#pragma unroll
-                        for (int x = 0; x < 16; ++x) {
-                            float v;
-                            if (p.glu) {
-                                v = (va[x] + bv[x]) * fast_sigmoid(vg[x] + bg[x]) * p.e.alpha;
-                            } else {
-                                v = va[x] + bv[x];
-                                if (p.e.act == NEMO_ACT_SILU) v = v * fast_sigmoid(v);
-                                else if (p.e.act == NEMO_ACT_RELU) v = fmaxf(v, 0.0f);
-                                v *= p.e.alpha;
-                            }
-                            o[x] = v + cin[x];
-                        }
-                        const int64_t idx = rowbase + n0;
-                        if (p.e.c_fmt == NEMO_FMT_F32) {
-#pragma unroll
-                            for (int x = 0; x < 16; x += 4) *(float4 *)(C32 + idx + x) = make_float4(o[x], o[x + 1], o[x + 2], o[x + 3]);
-                        } else {
-                            uint32_t h[8], l[8];
-#pragma unroll
-                            for (int x = 0; x < 8; ++x) {
-                                const uint16_t h0 = nb::f2bf(o[2 * x]), h1 = nb::f2bf(o[2 * x + 1]);
-                                const uint16_t l0 = nb::f2bf(o[2 * x] - nb::bf2f(h0)), l1 = nb::f2bf(o[2 * x + 1] - nb::bf2f(h1));
-                                h[x] = (uint32_t)h0 | ((uint32_t)h1 << 16);
-                                l[x] = (uint32_t)l0 | ((uint32_t)l1 << 16);
-                            }
-                            uint4 *dh = (uint4 *)(C16 + idx), *dl = (uint4 *)(C16 + idx + p.e.c_plane);
-                            dh[0] = make_uint4(h[0], h[1], h[2], h[3]);
-                            dh[1] = make_uint4(h[4], h[5], h[6], h[7]);
-                            dl[0] = make_uint4(l[0], l[1], l[2], l[3]);
-                            dl[1] = make_uint4(l[4], l[5], l[6], l[7]);
-                        }
-                        if (p.e.c32)
-#pragma unroll
-                            for (int x = 0; x < 16; x += 4)
-                                *(float4 *)(p.e.c32 + (int64_t)m * p.e.ldc32 + n0 + x) = make_float4(o[x], o[x + 1], o[x + 2], o[x + 3]);
                         continue;
                     }
                     float cin[16], bv[16], bg[16];
