@@ -50,6 +50,12 @@ struct nb_engine {
     /* captured CUDA graphs: encoder step per (window rows, chunk rows), decoder iteration per
        chunk rows; NEMO_GRAPHS=0 launches kernel by kernel instead */
     int use_graphs;
+    /* one stream: the conformer blocks run as one persistent kernel (NEMO_PERSISTENT=0 disables) */
+    int use_enc1, enc1_grid, enc1_slot;
+    NbEnc1Layer *enc1_layers;  /* host copy, passed by value at each launch */
+    NbEnc1Args enc1_args;      /* launch arguments (large: the layer table travels by value) */
+    unsigned *d_enc1_bar;
+    int *d_enc1_err;
     struct { int kind, k1, k2; cudaGraphExec_t exec; uint64_t kernels; } graphs[NB_MAX_GRAPHS];
     int ngraphs;
 };
@@ -66,6 +72,50 @@ static void *dalloc(size_t bytes, int *fail) {
     if (cudaMalloc(&p, bytes ? bytes : 16) != cudaSuccess) { *fail = 1; return NULL; }
     cudaMemset(p, 0, bytes ? bytes : 16);
     return p;
+}
+
+/* One stream: prepare the persistent encoder kernel (every conformer block of a chunk in one
+   launch) when the device and model shapes allow it; otherwise the blocks run kernel by kernel. */
+static int enc1_setup(nb_engine_t *e, char *err, size_t errlen) {
+    const char *ev = getenv("NEMO_PERSISTENT");
+    if (ev && !strcmp(ev, "0")) return 0;
+    const nb_model_t *m = e->m;
+    const nb_config_t *g = &m->g;
+    int dev = 0, sms = 0, optin = 0, coop = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, dev);
+    const int D = g->d_model, FF = g->d_ff;
+    if (!coop || sms <= 0 || D % 128 || D > 1024 || g->n_heads * 128 != D || e->cmax > 16 || e->Lmax > 72 || g->n_layers > NB_ENC1_MAX_LAYERS ||
+        g->conv_kernel > 9)
+        return 0;
+    /* per-CTA weight rows must fit the kernel's 32-row accumulator tiles */
+    if ((FF + sms - 1) / sms > 32 || (3 * D + sms - 1) / sms > 32 || 2 * ((D + sms - 1) / sms) > 32) return 0;
+    const int slot = nb_encoder1_slot_bytes(D, FF, sms);
+    if (nb_encoder1_smem(slot) > (size_t)optin) return 0;
+    NbEnc1Layer *L = calloc((size_t)g->n_layers, sizeof *L);
+    const size_t kv_s = (size_t)e->cap_rows * 3 * D, din_s = (size_t)e->cap_rows * D;
+    for (int l = 0; l < g->n_layers; ++l) {
+        const nb_layer_t *W = &m->L[l];
+        NbEnc1Layer *o = &L[l];
+        o->ff1_w1 = W->ff1_w1; o->ff1_w2 = W->ff1_w2; o->wqkv = W->wqkv; o->wo = W->wo; o->pw1 = W->pw1; o->pw2 = W->pw2;
+        o->ff2_w1 = W->ff2_w1; o->ff2_w2 = W->ff2_w2;
+        o->ln_ff1_g = W->ln_ff1_g; o->ln_ff1_b = W->ln_ff1_b; o->ln_att_g = W->ln_att_g; o->ln_att_b = W->ln_att_b;
+        o->ln_conv_g = W->ln_conv_g; o->ln_conv_b = W->ln_conv_b; o->ln_ff2_g = W->ln_ff2_g; o->ln_ff2_b = W->ln_ff2_b;
+        o->ln_out_g = W->ln_out_g; o->ln_out_b = W->ln_out_b;
+        o->bn_g = W->bn_g; o->bn_b = W->bn_b; o->dw_w = W->dw_w; o->bias_u = W->bias_u; o->bias_v = W->bias_v; o->ptab = W->ptab;
+        o->kv = e->kv + (size_t)l * kv_s;
+        o->din = e->din + (size_t)l * din_s;
+    }
+    e->enc1_layers = L;
+    const int rc = cudaMalloc((void **)&e->d_enc1_bar, 2 * sizeof(unsigned)) != cudaSuccess || cudaMalloc((void **)&e->d_enc1_err, sizeof(int)) != cudaSuccess ||
+                   cudaMemset(e->d_enc1_err, 0, sizeof(int)) != cudaSuccess;
+    if (rc) { snprintf(err, errlen, "persistent encoder set-up: %s", cudaGetErrorString(cudaGetLastError())); return -1; }
+    e->use_enc1 = 1;
+    e->enc1_grid = sms;
+    e->enc1_slot = slot;
+    return 0;
 }
 
 nb_engine_t *nb_engine_create(nb_model_t *m, int B, int right, char *err, size_t errlen) {
@@ -163,6 +213,7 @@ nb_engine_t *nb_engine_create(nb_model_t *m, int B, int right, char *err, size_t
         const char *gr = getenv("NEMO_GRAPHS");
         e->use_graphs = !(gr && !strcmp(gr, "0"));
     }
+    if (B == 1 && fmt == NEMO_FMT_BF16X2 && enc1_setup(e, err, errlen)) goto fail;
     if (nb_engine_reset(e, err, errlen)) goto fail;
     return e;
 fail:
@@ -192,6 +243,9 @@ void nb_engine_destroy(nb_engine_t *e) {
     if (e->ev0) cudaEventDestroy(e->ev0);
     if (e->ev1) cudaEventDestroy(e->ev1);
     for (int i = 0; i < e->ngraphs; ++i) cudaGraphExecDestroy(e->graphs[i].exec);
+    free(e->enc1_layers);
+    if (e->d_enc1_bar) cudaFree(e->d_enc1_bar);
+    if (e->d_enc1_err) cudaFree(e->d_enc1_err);
     if (e->pending) for (int s = 0; s < e->B; ++s) free(e->pending[s]);
     free(e->pending);
     free(e->mel_cache);
@@ -310,7 +364,20 @@ static int launch_encoder(nb_engine_t *e, int nwin, int c) {
     /* 24 conformer blocks (src/encoder.c:145-188) */
     const int64_t plD = pl_row * D, plFF = pl_row * FF;
     const int64_t kv_s = (int64_t)e->cap_rows * 3 * D, din_s = (int64_t)e->cap_rows * D;
-    for (int l = 0; l < g->n_layers; ++l) {
+    if (e->use_enc1) {
+        NbEnc1Args *q = &e->enc1_args;
+        memset(q, 0, sizeof *q);
+        memcpy(q->L, e->enc1_layers, (size_t)g->n_layers * sizeof *e->enc1_layers);
+        q->layers = g->n_layers; q->D = D; q->FF = FF; q->H = g->n_heads; q->taps = g->conv_kernel; q->Lmax = e->Lmax; q->c = c;
+        q->slot_bytes = e->enc1_slot;
+        q->eps = eps; q->scale = 1.0f / sqrtf(128.0f);
+        q->pos = d_pos; q->cache_len = d_cache_len;
+        q->h = h; q->ff = e->ff; q->att = e->att;
+        q->xout = (uint16_t *)e->xin; q->xout_plane = plD;
+        q->bar = e->d_enc1_bar; q->err = e->d_enc1_err;
+        if (nb_encoder1(q, e->enc1_grid, st)) return -1;
+    }
+    for (int l = 0; l < (e->use_enc1 ? 0 : g->n_layers); ++l) {
         const nb_layer_t *W = &m->L[l];
         float *kv = e->kv + (size_t)l * B * kv_s, *din = e->din + (size_t)l * B * din_s;
         if (l == 0 && nemo_layernorm(h, W->ln_ff1_g, W->ln_ff1_b, e->xin, fl, plD, M, D, eps, st)) return -1;
@@ -606,6 +673,13 @@ int nb_engine_step(nb_engine_t *e, int final, int *tokens, int max_tokens, int *
     if (run_graph(e, 0, nwin, c, enc_body)) { snprintf(err, errlen, "encoder: %s", nemo_gpu_last_error()); return -1; }
     if (cudaStreamSynchronize(st) != cudaSuccess) { snprintf(err, errlen, "encoder: %s", cudaGetErrorString(cudaGetLastError())); return -1; }
     if (nemo_gpu_check_device_errors()) { snprintf(err, errlen, "encoder: %s", nemo_gpu_last_error()); return -1; }
+    if (e->use_enc1) {
+        int v = 0;
+        if (cudaMemcpy(&v, e->d_enc1_err, sizeof v, cudaMemcpyDeviceToHost) != cudaSuccess || v) {
+            snprintf(err, errlen, "encoder: the persistent encoder gave up waiting (code %d)", v);
+            return -1;
+        }
+    }
     const double t1 = nb_now_ms();
     e->pos += c;
     const int L = e->cache_len + c;

@@ -2,6 +2,7 @@
    engine.c (host) and k_engine.cu (kernels). */
 #ifndef NB_ENGINE_DEV_H
 #define NB_ENGINE_DEV_H
+#include <stddef.h>
 #include <stdint.h>
 
 #ifdef __cplusplus
@@ -21,6 +22,32 @@ typedef struct {
     uint16_t *jx;                     /* joint GEMM input planes [streams][JH] */
     float *logits;                    /* [streams][num_classes] */
 } DecState;
+
+/* Persistent single-stream encoder (k_encoder1.cu): one conformer block's weights and caches. */
+typedef struct {
+    const uint16_t *ff1_w1, *ff1_w2, *wqkv, *wo, *pw1, *pw2, *ff2_w1, *ff2_w2;
+    const float *ln_ff1_g, *ln_ff1_b, *ln_att_g, *ln_att_b, *ln_conv_g, *ln_conv_b, *ln_ff2_g, *ln_ff2_b, *ln_out_g, *ln_out_b;
+    const float *bn_g, *bn_b, *dw_w, *bias_u, *bias_v, *ptab;
+    float *kv, *din; /* [cap][3D] and [cap][D] cache rows of the stream */
+} NbEnc1Layer;
+
+#define NB_ENC1_MAX_LAYERS 32
+typedef struct {
+    NbEnc1Layer L[NB_ENC1_MAX_LAYERS]; /* by value: the kernel reads it from its parameter space */
+    int layers, D, FF, H, taps, Lmax, c, slot_bytes;
+    float eps, scale;
+    const int *pos, *cache_len; /* device words */
+    float *h;                   /* [c][D] residual stream: pre-encode output in, last block's output out */
+    float *ff, *att;            /* [c][FF], [c][D] scratch */
+    uint16_t *xout;             /* LN_out(h) as bf16 hi / lo planes [c][D], xout_plane elements apart */
+    int64_t xout_plane;
+    unsigned *bar;              /* [2] grid-barrier arrivals, abort flag (zeroed before each launch) */
+    int *err;                   /* nonzero after a bounded wait gave up */
+} NbEnc1Args;
+
+int nb_encoder1(const NbEnc1Args *args, int grid, void *stream);
+int nb_encoder1_slot_bytes(int D, int FF, int grid);
+size_t nb_encoder1_smem(int slot_bytes);
 
 int nb_set_error(const char *fmt, ...);
 int nb_gemm_tc_init(void);
