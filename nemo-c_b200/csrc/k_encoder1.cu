@@ -178,12 +178,12 @@ enum { P_PLAIN = 0, P_LN = 1, P_LN2 = 2, P_DWLN = 3 };
 struct ActRegs { float4 x[8]; };
 
 __device__ __forceinline__ void act_load(ActRegs &R, const float *X, int ldx, int c, int k0, int kc) {
-    const int per_row = kc / 4, total = c * per_row;
+    const int sh = __ffs(kc / 4) - 1, total = c << sh;  // kc / 4 is a power of two
 #pragma unroll
     for (int u = 0; u < 8; ++u) {
         const int e = threadIdx.x + u * CTHREADS;
         if (e < total) {
-            const int r = e / per_row, k = (e - r * per_row) * 4;
+            const int r = e >> sh, k = (e - (r << sh)) * 4;
             R.x[u] = *(const float4 *)(X + (int64_t)r * ldx + k0 + k);
         }
     }
@@ -194,13 +194,13 @@ __device__ __forceinline__ void act_load(ActRegs &R, const float *X, int ldx, in
 // together with the chunk (fused layout: thread t holds columns 4t .. 4t+3 of every row).
 __device__ __forceinline__ void act_store(const ActRegs &R, Smem &S, int mode, int c, int k0, int kc, int apitch, const float *g1, const float *b1,
                                           const float *g2, const float *b2, const float4 (&pre)[4], bool use_pre) {
-    const int per_row = kc / 4, total = c * per_row;
+    const int sh = __ffs(kc / 4) - 1, total = c << sh;
     const int plane = ACT_PLANE;
 #pragma unroll
     for (int u = 0; u < 8; ++u) {
         const int e = threadIdx.x + u * CTHREADS;
         if (e < total) {
-            const int r = e / per_row, k = (e - r * per_row) * 4;
+            const int r = e >> sh, k = (e - (r << sh)) * 4;
             float v[4] = { R.x[u].x, R.x[u].y, R.x[u].z, R.x[u].w };
             if (mode != P_PLAIN) {
                 const float m1 = S.st[r][0], i1 = S.st[r][1];
@@ -305,35 +305,44 @@ __device__ __forceinline__ void group_sync(int kc) {
     sm100::named_barrier(2 + grp, gw * 32);
 }
 
-// acc_h / acc_l[g][nt] += W rows (granule g) . staged hi / lo activation rows (tile nt) over this
-// warp's k-steps: the 8 of its group's 128 columns, split between the group's warps.
-__device__ __forceinline__ void mma_chunk(const Smem &S, const uint8_t *slot, int pitch, int nrows, int k0, int kc, int ng, int nnt, int apitch,
-                                          float (&acc_h)[2][2][4], float (&acc_l)[2][2][4]) {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, mi = lane >> 3, rr = lane & 7;
-    const int span = (kc / 4) / 32, gw = CWARPS / span;  // column ranges, warps per range
-    const int grp = warp % span, member = warp / span;
-    const int per = 8 / gw;                             // k-steps of this warp
-    const uint32_t act = sm100::smem_u32(S.act), wb = sm100::smem_u32(slot);
-#pragma unroll 2
-    for (int q = 0; q < per; ++q) {
-        const int kk = (grp * 8 + member * per + q) * 16;
-        uint32_t b[2][4];
+// One k-step (16 columns at kk of the staged chunk): ah / al[g][nt] += W rows of granule g times
+// the hi / lo activation rows of tile nt.
+__device__ __forceinline__ void mma_kstep(uint32_t act, uint32_t wb, int pitch, int nrows, int k0, int kk, int ng, int nnt, int apitch,
+                                          float (&ah)[2][2][4], float (&al)[2][2][4]) {
+    const int lane = threadIdx.x & 31, mi = lane >> 3, rr = lane & 7;
+    uint32_t b[2][4];
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt)
+        if (nt < nnt) ldsm_x4(act + (mi >> 1) * ACT_PLANE + (nt * 8 + rr) * apitch + (kk + (mi & 1) * 8) * 2, b[nt][0], b[nt][1], b[nt][2], b[nt][3]);
+#pragma unroll
+    for (int g = 0; g < 2; ++g) {
+        if (g >= ng) break;
+        const int row = min(g * 16 + (mi & 1) * 8 + rr, nrows - 1);
+        uint32_t a0, a1, a2, a3;
+        ldsm_x4(wb + row * pitch + (k0 + kk + (mi >> 1) * 8) * 2, a0, a1, a2, a3);
 #pragma unroll
         for (int nt = 0; nt < 2; ++nt)
-            if (nt < nnt) ldsm_x4(act + (mi >> 1) * ACT_PLANE + (nt * 8 + rr) * apitch + (kk + (mi & 1) * 8) * 2, b[nt][0], b[nt][1], b[nt][2], b[nt][3]);
-#pragma unroll
-        for (int g = 0; g < 2; ++g) {
-            if (g >= ng) break;
-            const int row = min(g * 16 + (mi & 1) * 8 + rr, nrows - 1);
-            uint32_t a0, a1, a2, a3;
-            ldsm_x4(wb + row * pitch + (k0 + kk + (mi >> 1) * 8) * 2, a0, a1, a2, a3);
-#pragma unroll
-            for (int nt = 0; nt < 2; ++nt)
-                if (nt < nnt) {
-                    mma16816(acc_h[g][nt], a0, a1, a2, a3, b[nt][0], b[nt][1]);  // hi plane
-                    mma16816(acc_l[g][nt], a0, a1, a2, a3, b[nt][2], b[nt][3]);  // lo plane
-                }
-        }
+            if (nt < nnt) {
+                mma16816(ah[g][nt], a0, a1, a2, a3, b[nt][0], b[nt][1]);  // hi plane
+                mma16816(al[g][nt], a0, a1, a2, a3, b[nt][2], b[nt][3]);  // lo plane
+            }
+    }
+}
+
+// This warp's k-steps of the staged chunk: the 8 k-steps of its group's 128 columns, split
+// between the group's warps; consecutive k-steps alternate between two accumulator sets so the
+// MMA dependency chains are half as long.
+__device__ __forceinline__ void mma_chunk(const Smem &S, const uint8_t *slot, int pitch, int nrows, int k0, int kc, int ng, int nnt, int apitch,
+                                          float (&acc_h)[2][2][4], float (&acc_l)[2][2][4], float (&acc_h2)[2][2][4], float (&acc_l2)[2][2][4]) {
+    const int warp = threadIdx.x >> 5;
+    const int span = (kc / 4) / 32, gw = CWARPS / span;  // column ranges, warps per range
+    const int grp = warp % span, member = warp / span;
+    const int per = 8 / gw;                             // k-steps of this warp: 8, 4 or 2
+    const uint32_t act = sm100::smem_u32(S.act), wb = sm100::smem_u32(slot);
+    for (int q = 0; q < per; q += 2) {
+        const int kk = (grp * 8 + member * per + q) * 16;
+        mma_kstep(act, wb, pitch, nrows, k0, kk, ng, nnt, apitch, acc_h, acc_l);
+        mma_kstep(act, wb, pitch, nrows, k0, kk + 16, ng, nnt, apitch, acc_h2, acc_l2);
     }
 }
 
@@ -545,18 +554,18 @@ __global__ void __launch_bounds__(THREADS, 1) encoder1_kernel(const __grid_const
                 cbar();
                 if (S.abort) break;
                 const uint8_t *ws = slots + (size_t)slot * a.slot_bytes;
-                float acc[2][2][4], acl[2][2][4];
+                float acc[2][2][4], acl[2][2][4], acc2[2][2][4], acl2[2][2][4];
 #pragma unroll
                 for (int g = 0; g < 2; ++g)
 #pragma unroll
                     for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
-                        for (int q = 0; q < 4; ++q) acc[g][nt][q] = acl[g][nt][q] = 0.0f;
+                        for (int q = 0; q < 4; ++q) acc[g][nt][q] = acl[g][nt][q] = acc2[g][nt][q] = acl2[g][nt][q] = 0.0f;
                 for (int k0 = 0; k0 < K; k0 += kc) {
                     act_store(AR, S, mode, c, k0, kc, apitch, g1, b1, g2, b2, pre, fused);
                     group_sync(kc);
                     if (k0 + kc < K) act_load(AR, X, ldx, c, k0 + kc, kc);  // next chunk in flight during the MMAs
-                    if (nrows > 0) mma_chunk(S, ws, pitch, nrows, k0, kc, ng, nnt, apitch, acc, acl);
+                    if (nrows > 0) mma_chunk(S, ws, pitch, nrows, k0, kc, ng, nnt, apitch, acc, acl, acc2, acl2);
                     group_sync(kc);
                 }
 #pragma unroll
@@ -564,7 +573,7 @@ __global__ void __launch_bounds__(THREADS, 1) encoder1_kernel(const __grid_const
 #pragma unroll
                     for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
-                        for (int q = 0; q < 4; ++q) acc[g][nt][q] += acl[g][nt][q];
+                        for (int q = 0; q < 4; ++q) acc[g][nt][q] += acl[g][nt][q] + (acc2[g][nt][q] + acl2[g][nt][q]);
                 // reduce the warps' partial sums: outv[weight row][activation row]
 #pragma unroll
                 for (int g = 0; g < 2; ++g)
