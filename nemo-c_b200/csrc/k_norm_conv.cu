@@ -1,4 +1,5 @@
 // LayerNorms, the conv-module depthwise conv + LN + SiLU, and the subsampling convolutions.
+#include <cuda_bf16.h>
 #include "common.cuh"
 
 namespace {
@@ -205,7 +206,114 @@ __global__ void flatten_rows_kernel(const float *__restrict__ X, void *Y, int y_
     }
 }
 
+// ---- warp-per-row variants (D <= 1024, D % 128 == 0): one wave for thousands of rows, shuffle-only
+// reductions. Lane l holds columns 4 (l + 32 j) .. +3 for j < D / 128 (float4 loads).
+constexpr int WROWS = 8;  // rows (warps) per block
+
+template <int NV>
+__device__ __forceinline__ void ln_warp(float4 (&v)[NV], int nv, int D, const float *__restrict__ g, const float *__restrict__ b, float eps) {
+    const int lane = threadIdx.x & 31;
+    float s = 0.0f;
+#pragma unroll
+    for (int j = 0; j < NV; ++j) if (j < nv) s += v[j].x + v[j].y + v[j].z + v[j].w;
+    const float mean = nb::warp_sum(s) / (float)D;
+    float q = 0.0f;
+#pragma unroll
+    for (int j = 0; j < NV; ++j)
+        if (j < nv) {
+            const float a = v[j].x - mean, bb = v[j].y - mean, cc = v[j].z - mean, d = v[j].w - mean;
+            q += a * a + bb * bb + cc * cc + d * d;
+        }
+    const float inv = 1.0f / sqrtf(nb::warp_sum(q) / (float)D + eps);
+#pragma unroll
+    for (int j = 0; j < NV; ++j)
+        if (j < nv) {
+            const int k = 4 * (lane + 32 * j);
+            const float4 gg = __ldg((const float4 *)(g + k)), bv = __ldg((const float4 *)(b + k));
+            v[j].x = (v[j].x - mean) * inv * gg.x + bv.x;
+            v[j].y = (v[j].y - mean) * inv * gg.y + bv.y;
+            v[j].z = (v[j].z - mean) * inv * gg.z + bv.z;
+            v[j].w = (v[j].w - mean) * inv * gg.w + bv.w;
+        }
+}
+
+__device__ __forceinline__ void store4(void *Y, int fmt, int64_t plane, int64_t idx, const float4 v) {
+    if (fmt == NEMO_FMT_F32) {
+        *(float4 *)((float *)Y + idx) = v;
+    } else {
+        const __nv_bfloat162 h0 = __floats2bfloat162_rn(v.x, v.y), h1 = __floats2bfloat162_rn(v.z, v.w);
+        const __nv_bfloat162 l0 = __floats2bfloat162_rn(v.x - __low2float(h0), v.y - __high2float(h0));
+        const __nv_bfloat162 l1 = __floats2bfloat162_rn(v.z - __low2float(h1), v.w - __high2float(h1));
+        uint16_t *y = (uint16_t *)Y + idx;
+        *(uint2 *)y = make_uint2(*(const uint32_t *)&h0, *(const uint32_t *)&h1);
+        *(uint2 *)(y + plane) = make_uint2(*(const uint32_t *)&l0, *(const uint32_t *)&l1);
+    }
+}
+
+// Y = LN(X; g, b) (src/kernels.metal:258-288); with g2: Y1 = that, Y = LN(Y1; g2, b2) (:212-255).
+__global__ void __launch_bounds__(WROWS * 32) layernorm_warp_kernel(const float *__restrict__ X, const float *__restrict__ g, const float *__restrict__ b,
+                                                                    const float *__restrict__ g2, const float *__restrict__ b2, float *Y1, void *Y,
+                                                                    int y_fmt, int64_t y_plane, int M, int D, float eps) {
+    nb::pdl_wait();
+    const int row = blockIdx.x * WROWS + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (row >= M) return;
+    const int nv = D / 128;
+    float4 v[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) if (j < nv) v[j] = *(const float4 *)(X + (int64_t)row * D + 4 * (lane + 32 * j));
+    ln_warp<8>(v, nv, D, g, b, eps);
+    if (g2) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) if (j < nv) *(float4 *)(Y1 + (int64_t)row * D + 4 * (lane + 32 * j)) = v[j];
+        ln_warp<8>(v, nv, D, g2, b2, eps);
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) if (j < nv) store4(Y, y_fmt, y_plane, (int64_t)row * D + 4 * (lane + 32 * j), v[j]);
+}
+
+// Causal depthwise conv + LN + SiLU (src/kernels.metal:361-409), one warp per (stream, row).
+__global__ void __launch_bounds__(WROWS * 32) dwconv_ln_silu_warp_kernel(const float *__restrict__ din, int64_t din_sstride, const int *pos_p,
+                                                                         const float *__restrict__ W, const float *__restrict__ g,
+                                                                         const float *__restrict__ b, void *Y, int y_fmt, int64_t y_plane, int streams,
+                                                                         int c, int D, int taps, float eps) {
+    nb::pdl_wait();
+    const int item = blockIdx.x * WROWS + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (item >= streams * c) return;
+    const int s = item / c, t = item - s * c;
+    const float *x = din + (int64_t)s * din_sstride + (int64_t)(*pos_p - (taps - 1) + t) * D;
+    const int nv = D / 128;
+    float4 v[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+        if (j < nv) {
+            const int ch = 4 * (lane + 32 * j);
+            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int tap = 0; tap < taps; ++tap) {
+                const float4 xv = *(const float4 *)(x + (int64_t)tap * D + ch);
+                acc.x += W[(ch + 0) * taps + tap] * xv.x;
+                acc.y += W[(ch + 1) * taps + tap] * xv.y;
+                acc.z += W[(ch + 2) * taps + tap] * xv.z;
+                acc.w += W[(ch + 3) * taps + tap] * xv.w;
+            }
+            v[j] = acc;
+        }
+    ln_warp<8>(v, nv, D, g, b, eps);
+    const int64_t row = (int64_t)s * c + t;
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+        if (j < nv) {
+            float4 o = v[j];
+            o.x = nb::silu_f(o.x); o.y = nb::silu_f(o.y); o.z = nb::silu_f(o.z); o.w = nb::silu_f(o.w);
+            store4(Y, y_fmt, y_plane, row * D + 4 * (lane + 32 * j), o);
+        }
+}
+
 }  // namespace
+
+// warp-per-row kernels need D a multiple of 128 up to 1024, 16-byte aligned rows and planes
+static bool warp_rows_ok(const void *X, const void *Y, int y_fmt, int64_t y_plane, int D) {
+    return D % 128 == 0 && D <= 1024 && !((uintptr_t)X & 15) && !((uintptr_t)Y & 15) && (y_fmt == NEMO_FMT_F32 || y_plane % 8 == 0);
+}
 
 static int grid_for(int64_t total) {
     int64_t g = (total + 255) / 256;
@@ -215,6 +323,11 @@ static int grid_for(int64_t total) {
 extern "C" int nemo_layernorm(const float *X, const float *g, const float *b, void *Y, int y_fmt, int64_t y_plane, int M, int D, float eps, void *stream) {
     if (D > LNT * LN_MAXV) return nb_set_error("nemo_layernorm: D=%d too large", D);
     if (M <= 0) return 0;
+    if (warp_rows_ok(X, Y, y_fmt, y_plane, D)) {
+        layernorm_warp_kernel<<<(M + WROWS - 1) / WROWS, WROWS * 32, 0, (cudaStream_t)stream>>>(X, g, b, nullptr, nullptr, nullptr, Y, y_fmt, y_plane, M, D,
+                                                                                              eps);
+        return nb_check_launch("layernorm_warp_kernel");
+    }
     layernorm_kernel<<<M, LNT, 0, (cudaStream_t)stream>>>(X, g, b, Y, y_fmt, y_plane, D, eps);
     return nb_check_launch("layernorm_kernel");
 }
@@ -223,6 +336,10 @@ extern "C" int nemo_layernorm2(const float *X, const float *g1, const float *b1,
                                int y2_fmt, int64_t y2_plane, int M, int D, float eps, void *stream) {
     if (D > LNT * LN_MAXV) return nb_set_error("nemo_layernorm2: D=%d too large", D);
     if (M <= 0) return 0;
+    if (warp_rows_ok(X, Y2, y2_fmt, y2_plane, D) && !((uintptr_t)Y1 & 15)) {
+        layernorm_warp_kernel<<<(M + WROWS - 1) / WROWS, WROWS * 32, 0, (cudaStream_t)stream>>>(X, g1, b1, g2, b2, Y1, Y2, y2_fmt, y2_plane, M, D, eps);
+        return nb_check_launch("layernorm_warp_kernel");
+    }
     layernorm2_kernel<<<M, LNT, 0, (cudaStream_t)stream>>>(X, g1, b1, g2, b2, Y1, Y2, y2_fmt, y2_plane, D, eps);
     return nb_check_launch("layernorm2_kernel");
 }
@@ -231,6 +348,12 @@ extern "C" int nemo_dwconv_ln_silu(const float *din, int64_t din_sstride, const 
                                    int y_fmt, int64_t y_plane, int streams, int c, int D, int taps, float eps, void *stream) {
     if (D > LNT * LN_MAXV) return nb_set_error("nemo_dwconv_ln_silu: D=%d too large", D);
     if (streams <= 0 || c <= 0) return 0;
+    if (warp_rows_ok(din, Y, y_fmt, y_plane, D) && din_sstride % 4 == 0) {
+        const int items = streams * c;
+        dwconv_ln_silu_warp_kernel<<<(items + WROWS - 1) / WROWS, WROWS * 32, 0, (cudaStream_t)stream>>>(din, din_sstride, pos, W, g, b, Y, y_fmt, y_plane,
+                                                                                                       streams, c, D, taps, eps);
+        return nb_check_launch("dwconv_ln_silu_warp_kernel");
+    }
     dwconv_ln_silu_kernel<<<dim3(c, streams), LNT, 0, (cudaStream_t)stream>>>(din, din_sstride, pos, W, g, b, Y, y_fmt, y_plane, c, D, taps, eps);
     return nb_check_launch("dwconv_ln_silu_kernel");
 }

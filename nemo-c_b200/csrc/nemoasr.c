@@ -355,7 +355,11 @@ int nemoasr_batch_reset(nemoasr_batch_t *b, char *err, size_t errlen) {
     return 0;
 }
 
-void nemoasr_batch_stats(const nemoasr_batch_t *b, nemoasr_stats_t *out) { *out = b->stats; }
+void nemoasr_batch_stats(const nemoasr_batch_t *b, nemoasr_stats_t *out) {
+    *out = b->stats;
+    size_t chunks = 0;
+    nb_engine_times(b->eng, &out->encoder_ms, &out->decoder_ms, &chunks); /* also covers steps driven by nemoasr_batch_step */
+}
 void nemoasr_batch_set_taps(nemoasr_batch_t *b, float *prompted, float *joint_enc, size_t cap_rows, int *chunk_rows, size_t cap_chunks) {
     nb_engine_set_taps(b->eng, prompted, joint_enc, cap_rows, chunk_rows, cap_chunks);
 }
