@@ -32,6 +32,9 @@ sys.path.insert(0, os.path.join(ROOT, "nemo-c_b200"))
 sys.path.insert(0, os.path.join(ROOT, "tests"))
 
 METRIC = "audio-sec/sec (RTFx) at N streams on 1/2/4/8 B200"
+# DRAM bytes of one FF-in launch at 1792 rows (8.39 MB weights + 7.34 MB activation planes
+# algorithmic), measured by ncu: 15.82 MB read + 0.03 MB written
+FFIN_TRAFFIC = 15853824
 UNIT = "audio-sec/sec"
 
 
@@ -349,7 +352,9 @@ def main():
     peak = peaks.get("bf16_tflops", 1590.0)
     ach = flops / (ms / 1e3) / 1e12
     roof = {"bound": "tensor", "kernel": "nemo_gemm FF-in (M=%d N=4096 K=1024, SiLU)" % (B * c), "achieved": ach, "peak": peak, "unit": "TFLOP/s",
-            "frac": ach / peak, "traffic": None, "peak_source": "MEASURED_PEAKS.json bf16_tflops (burst)" if peaks else "fallback 1.59 PFLOP/s"}
+            "frac": ach / peak, "traffic": FFIN_TRAFFIC if B * c == 1792 else None,
+            "traffic_source": "dram__bytes_read.sum + dram__bytes_write.sum of one ncu capture of this launch shape",
+            "peak_source": "MEASURED_PEAKS.json bf16_tflops (burst)" if peaks else "fallback 1.59 PFLOP/s"}
 
     cpu = None
     if rank == 0 and world == 1 and not a.no_cpu:
