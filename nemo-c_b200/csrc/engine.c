@@ -54,6 +54,11 @@ struct nb_engine {
     int use_enc1, enc1_grid, enc1_slot;
     NbEnc1Layer *enc1_layers;  /* host copy, passed by value at each launch */
     NbEnc1Args enc1_args;      /* launch arguments (large: the layer table travels by value) */
+    /* one stream: the greedy loop of a chunk runs as one persistent kernel (NEMO_PERSISTENT=0 disables) */
+    int use_dec1, dec1_grid;
+    float *d_dec1;             /* H0 [2][PH] | H1 [2][PH] | PRED [JH] | part_v [grid][16] */
+    int *d_dec1_i;             /* part_i [grid][16] | err */
+    unsigned *d_dec1_bar;
     unsigned *d_enc1_bar;
     int *d_enc1_err;
     struct { int kind, k1, k2; cudaGraphExec_t exec; uint64_t kernels; } graphs[NB_MAX_GRAPHS];
@@ -115,6 +120,30 @@ static int enc1_setup(nb_engine_t *e, char *err, size_t errlen) {
     e->use_enc1 = 1;
     e->enc1_grid = sms;
     e->enc1_slot = slot;
+    return 0;
+}
+
+/* One stream: prepare the persistent greedy decoder when the model's shapes fit it. */
+static int dec1_setup(nb_engine_t *e, char *err, size_t errlen) {
+    const char *ev = getenv("NEMO_PERSISTENT");
+    if (ev && !strcmp(ev, "0")) return 0;
+    const nb_config_t *g = &e->m->g;
+    int dev = 0, sms = 0, optin = 0, coop = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, dev);
+    if (!coop || sms <= 0 || g->pred_layers != 2 || !nb_decoder1_fits(g->pred_hidden, g->joint_hidden, g->num_classes, sms, e->cmax, (size_t)optin))
+        return 0;
+    const size_t PH = (size_t)g->pred_hidden, JH = (size_t)g->joint_hidden;
+    if (cudaMalloc((void **)&e->d_dec1, (4 * PH + 4 * PH + JH + (size_t)sms * 16) * sizeof(float)) != cudaSuccess ||
+        cudaMalloc((void **)&e->d_dec1_i, ((size_t)sms * 16 + 1) * sizeof(int)) != cudaSuccess ||
+        cudaMalloc((void **)&e->d_dec1_bar, 2 * sizeof(unsigned)) != cudaSuccess || cudaMemset(e->d_dec1_i, 0, ((size_t)sms * 16 + 1) * sizeof(int)) != cudaSuccess) {
+        snprintf(err, errlen, "persistent decoder set-up: %s", cudaGetErrorString(cudaGetLastError()));
+        return -1;
+    }
+    e->use_dec1 = 1;
+    e->dec1_grid = sms;
     return 0;
 }
 
@@ -214,6 +243,7 @@ nb_engine_t *nb_engine_create(nb_model_t *m, int B, int right, char *err, size_t
         e->use_graphs = !(gr && !strcmp(gr, "0"));
     }
     if (B == 1 && fmt == NEMO_FMT_BF16X2 && enc1_setup(e, err, errlen)) goto fail;
+    if (B == 1 && dec1_setup(e, err, errlen)) goto fail;
     if (nb_engine_reset(e, err, errlen)) goto fail;
     return e;
 fail:
@@ -244,6 +274,9 @@ void nb_engine_destroy(nb_engine_t *e) {
     if (e->ev1) cudaEventDestroy(e->ev1);
     for (int i = 0; i < e->ngraphs; ++i) cudaGraphExecDestroy(e->graphs[i].exec);
     free(e->enc1_layers);
+    if (e->d_dec1) cudaFree(e->d_dec1);
+    if (e->d_dec1_i) cudaFree(e->d_dec1_i);
+    if (e->d_dec1_bar) cudaFree(e->d_dec1_bar);
     if (e->d_enc1_bar) cudaFree(e->d_enc1_bar);
     if (e->d_enc1_err) cudaFree(e->d_enc1_err);
     if (e->pending) for (int s = 0; s < e->B; ++s) free(e->pending[s]);
@@ -572,8 +605,32 @@ static int run_decoder(nb_engine_t *e, int c, char *err, size_t errlen) {
     const nb_config_t *g = &e->m->g;
     DecState *d = &e->dec;
     cudaStream_t st = e->st;
-    KL(nb_dec_chunk_init(d, c, st));
     const int max_it = dec_max_iterations(e, c);
+    if (e->use_dec1) {
+        const nb_model_t *m = e->m;
+        const size_t PH = (size_t)g->pred_hidden, JH = (size_t)g->joint_hidden;
+        NbDec1Args a;
+        memset(&a, 0, sizeof a);
+        a.d = *d;
+        a.W0 = m->lstm_w[0]; a.W1 = m->lstm_w[1]; a.Wp = m->joint_pred_w; a.Wo = m->joint_out_w; a.embed = m->embed;
+        a.b0 = m->lstm_b[0]; a.b1 = m->lstm_b[1]; a.bp = m->joint_pred_b; a.bo = m->joint_out_b;
+        a.enc = e->joint_enc;
+        a.H0 = e->d_dec1; a.H1 = e->d_dec1 + 2 * PH; a.PRED = e->d_dec1 + 4 * PH; a.part_v = e->d_dec1 + 4 * PH + JH;
+        a.part_i = e->d_dec1_i; a.err = e->d_dec1_i + (size_t)e->dec1_grid * 16; a.bar = e->d_dec1_bar;
+        a.PH = g->pred_hidden; a.JH = g->joint_hidden; a.V = g->num_classes; a.blank = g->blank_id; a.max_symbols = g->max_symbols; a.c = c;
+        int herr = 0;
+        if (nb_decoder1(&a, e->dec1_grid, st)) { snprintf(err, errlen, "decoder: %s", nemo_gpu_last_error()); return -1; }
+        if (cudaMemcpyAsync(e->h_cnt, d->cnt, 4 * sizeof(int), cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+            cudaMemcpyAsync(&e->h_cnt[4], a.err, sizeof(int), cudaMemcpyDeviceToHost, st) != cudaSuccess || cudaStreamSynchronize(st) != cudaSuccess) {
+            snprintf(err, errlen, "decoder: %s", cudaGetErrorString(cudaGetLastError()));
+            return -1;
+        }
+        herr = e->h_cnt[4];
+        if (herr) { snprintf(err, errlen, "decoder: the persistent decoder gave up waiting (code %d)", herr); return -1; }
+        if (c > 0 && e->h_cnt[1] != 0) { snprintf(err, errlen, "decoder did not finish the chunk in %d iterations", max_it); return -1; }
+        return 0;
+    }
+    KL(nb_dec_chunk_init(d, c, st));
     (void)g;
     if (e->use_graphs) {
         const int slot = dec_graph(e, c);

@@ -45,6 +45,25 @@ typedef struct {
     int *err;                   /* nonzero after a bounded wait gave up */
 } NbEnc1Args;
 
+/* Persistent single-stream greedy decoder (k_decoder1.cu). */
+typedef struct {
+    DecState d;                           /* stream 0's greedy state (read at start, written back) */
+    const uint16_t *W0, *W1, *Wp, *Wo, *embed;  /* LSTM [4PH][2PH] x2, prediction [JH][PH], joint out [V][JH], embed [V][PH] */
+    const float *b0, *b1, *bp, *bo;
+    const float *enc;                     /* [c][JH] joint encoder rows of the chunk */
+    float *H0, *H1;                       /* [2][PH] committed / provisional hidden state (roles swap on emission) */
+    float *PRED;                          /* [JH] */
+    float *part_v;                        /* [grid][16] per-CTA best logit per frame */
+    int *part_i;                          /* [grid][16] and its vocabulary index */
+    unsigned *bar;                        /* [2] grid-barrier arrivals, abort flag (zeroed before each launch) */
+    int *err;
+    int PH, JH, V, blank, max_symbols, c;
+} NbDec1Args;
+
+int nb_decoder1(const NbDec1Args *args, int grid, void *stream);
+int nb_decoder1_fits(int PH, int JH, int V, int grid, int cmax, size_t smem_optin);
+size_t nb_decoder1_smem(int PH, int JH, int V, int grid, int c);
+
 int nb_encoder1(const NbEnc1Args *args, int grid, void *stream);
 int nb_encoder1_slot_bytes(int D, int FF, int grid);
 size_t nb_encoder1_smem(int slot_bytes);
