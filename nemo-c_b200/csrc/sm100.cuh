@@ -1,5 +1,5 @@
 // Thin inline-PTX wrappers for the sm_100a features the tensor-core kernels use: mbarriers,
-// TMA tile loads (no multicast), tcgen05 MMA / TMEM allocation / TMEM loads.
+// per-CTA TMA tile loads, tcgen05 MMA / TMEM allocation / TMEM loads.
 #pragma once
 #include <cuda.h>
 #include <stdint.h>
