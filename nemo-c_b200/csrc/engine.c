@@ -79,6 +79,9 @@ static void *dalloc(size_t bytes, int *fail) {
     return p;
 }
 
+/* Row pitch of the joint logits: a multiple of 4 floats, so the GEMM epilogue stores 16 bytes at a time. */
+static int logits_ld(const nb_config_t *g) { return (g->num_classes + 3) & ~3; }
+
 /* One stream: prepare the persistent encoder kernel (every conformer block of a chunk in one
    launch) when the device and model shapes allow it; otherwise the blocks run kernel by kernel. */
 static int enc1_setup(nb_engine_t *e, char *err, size_t errlen) {
@@ -205,7 +208,7 @@ nb_engine_t *nb_engine_create(nb_model_t *m, int B, int right, char *err, size_t
     DecState *d = &e->dec;
     d->streams = B;
     d->tok_cap = e->cmax * g->max_symbols;
-    int **ints[] = { &d->t, &d->symbols, &d->active, &d->pred_valid, &d->last_token, &d->ntok, &d->need_idx, &d->erow, &d->idx };
+    int **ints[] = { &d->t, &d->symbols, &d->active, &d->pred_valid, &d->last_token, &d->ntok, &d->need_idx, &d->need_pos, &d->erow, &d->idx };
     for (size_t i = 0; i < sizeof ints / sizeof *ints; ++i) *ints[i] = dalloc(Bz * sizeof(int), &fail);
     d->tokens = dalloc(Bz * (size_t)d->tok_cap * sizeof(int), &fail);
     d->cnt = dalloc(8 * sizeof(int), &fail);
@@ -223,7 +226,7 @@ nb_engine_t *nb_engine_create(nb_model_t *m, int B, int right, char *err, size_t
     d->a_plane = (int64_t)Bz * 2 * PH;
     d->h_plane = (int64_t)Bz * PH;
     d->jx = dalloc(Bz * JH * 4, &fail);
-    d->logits = dalloc(Bz * (size_t)g->num_classes * 4, &fail);
+    d->logits = dalloc(Bz * (size_t)logits_ld(g) * 4, &fail);
     if (fail) { snprintf(err, errlen, "out of device memory for %d streams", B); goto fail; }
     CK(cudaMallocHost((void **)&e->h_cnt, 8 * sizeof(int)));
     CK(cudaMallocHost((void **)&e->h_ntok, Bz * sizeof(int)));
@@ -261,7 +264,7 @@ void nb_engine_destroy(nb_engine_t *e) {
     if (e->prompted_x && e->prompted_x != e->prompted) cudaFree(e->prompted_x);
     if (e->dec.jx) cudaFree(e->dec.jx);
     if (e->dec.logits) cudaFree(e->dec.logits);
-    int *n[] = { e->d_params, e->dec.t, e->dec.symbols, e->dec.active, e->dec.pred_valid, e->dec.last_token, e->dec.ntok, e->dec.need_idx,
+    int *n[] = { e->d_params, e->dec.t, e->dec.symbols, e->dec.active, e->dec.pred_valid, e->dec.last_token, e->dec.ntok, e->dec.need_idx, e->dec.need_pos,
                  e->dec.erow, e->dec.idx, e->dec.tokens, e->dec.cnt };
     for (size_t i = 0; i < sizeof n / sizeof *n; ++i) if (n[i]) cudaFree(n[i]);
     if (e->h_win) cudaFreeHost(e->h_win);
@@ -497,13 +500,18 @@ static int dec_iteration_body(nb_engine_t *e, int c, unsigned long long cond) {
         a = gemm_args(d->hp1c, PH, d->fmt, d->h_plane, m->joint_pred_w, PH, m->joint_pred_b, d->predc, JH, B, JH, PH, 0, 0, 1.0f);
         a.dynM = d->cnt;
         KL(nemo_gemm(&a, st));
-        KL(nb_dec_scatter_pred(d, JH, st));
-        if (d->fmt == NEMO_FMT_BF16X2)
-            KL(nb_joint_argmax_gemm(e->joint_enc, JH, d->pred, JH, m->joint_out_w, m->joint_out_b, g->num_classes, JH, B, d->erow, d->jx, d->logits,
-                                    g->num_classes, d->idx, NULL, st));
-        else
+        if (d->fmt == NEMO_FMT_BF16X2) {
+            /* joint input (with the prediction scatter), joint GEMM, then the update takes each row's argmax */
+            KL(nb_dec_joint_in(d, e->joint_enc, JH, d->jx, (int64_t)B * JH, st));
+            nemo_gemm_args_t j = gemm_args(d->jx, JH, NEMO_FMT_BF16X2, (int64_t)B * JH, m->joint_out_w, JH, m->joint_out_b, d->logits, logits_ld(g), B,
+                                           g->num_classes, JH, 0, 0, 1.0f);
+            KL(nemo_gemm(&j, st));
+            KL(nb_dec_update(d, c, PH, g->blank_id, g->max_symbols, dec_max_iterations(e, c), cond, d->logits, logits_ld(g), g->num_classes, st));
+        } else {
+            KL(nb_dec_scatter_pred(d, JH, st));
             KL(nb_joint_argmax_rows(e->joint_enc, JH, d->pred, JH, 1, m->joint_out_w, m->joint_out_b, g->num_classes, JH, B, d->erow, d->idx, NULL, st));
-        KL(nb_dec_update(d, c, PH, g->blank_id, g->max_symbols, dec_max_iterations(e, c), cond, st));
+            KL(nb_dec_update(d, c, PH, g->blank_id, g->max_symbols, dec_max_iterations(e, c), cond, NULL, 0, 0, st));
+        }
         if (!cond && cudaMemcpyAsync(e->h_cnt, d->cnt, 2 * sizeof(int), cudaMemcpyDeviceToHost, st) != cudaSuccess)
             return nb_set_error("decoder: %s", cudaGetErrorString(cudaGetLastError()));
     }

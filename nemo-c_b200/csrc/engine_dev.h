@@ -12,6 +12,7 @@ extern "C" {
 typedef struct {
     int streams, tok_cap;
     int *t, *symbols, *active, *pred_valid, *last_token, *ntok, *tokens;
+    int *need_pos;                    /* [streams] compact row of a stream in need_idx, -1 if not listed */
     int *need_idx, *erow, *idx, *cnt; /* cnt[0] streams needing the prediction net, cnt[1] still active,
                                          cnt[2] iterations this chunk, cnt[3] dec_update blocks done */
     float *h, *c, *hp, *cp;           /* [2][streams][PH] committed / provisional LSTM state */
@@ -82,7 +83,12 @@ int nb_dec_scatter_pred(const DecState *d, int JH, void *stream);
 /* cond: handle of the CUDA graph WHILE loop this launch belongs to (0 outside such a loop); the
    last block sets it to "another iteration" while streams remain active and fewer than max_it
    iterations ran. cnt[2] counts the iterations of the chunk. */
-int nb_dec_update(const DecState *d, int c, int PH, int blank, int max_symbols, int max_it, unsigned long long cond, void *stream);
+int nb_dec_update(const DecState *d, int c, int PH, int blank, int max_symbols, int max_it, unsigned long long cond, const float *logits,
+                  int64_t ldl, int V, void *stream);
+/* Joint input of every stream: X[b] = relu(enc[erow[b]] + pred_b) as bf16 hi/lo planes (zeros for
+   inactive streams), where pred_b is the freshly computed compact row of a listed stream (also
+   stored as its prediction) or its kept prediction. */
+int nb_dec_joint_in(const DecState *d, const float *enc, int JH, uint16_t *X, int64_t plane, void *stream);
 int nb_dec_reset(const DecState *d, int PH, int blank, void *stream);
 int nb_joint_argmax_rows(const float *enc, int64_t enc_ld, const float *pred, int64_t pred_ld, int pred_rpg, const uint16_t *W,
                          const float *bias, int V, int H, int rows, const int *enc_row_of, int *out_idx, float *out_val, void *stream);

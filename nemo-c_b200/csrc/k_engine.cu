@@ -45,7 +45,12 @@ __global__ void dec_plan_kernel(DecState d, int streams, int c) {
     for (int b = threadIdx.x; b < streams; b += blockDim.x) {
         const bool act = d.active[b];
         d.erow[b] = act ? b * c + d.t[b] : -1;
-        if (act && !d.pred_valid[b]) d.need_idx[atomicAdd(&n_need, 1)] = b;
+        int pos = -1;
+        if (act && !d.pred_valid[b]) {
+            pos = atomicAdd(&n_need, 1);
+            d.need_idx[pos] = b;
+        }
+        d.need_pos[b] = pos;
     }
     __syncthreads();
     if (threadIdx.x == 0) { d.cnt[0] = n_need; d.cnt[1] = 0; }
@@ -99,10 +104,42 @@ __global__ void dec_scatter_pred_kernel(DecState d, int JH) {
 // One greedy step per active stream (src/decoder.c:104-122). When the decoder runs as a CUDA
 // graph WHILE loop (cond != 0), the last block to finish sets the loop condition: another
 // iteration while some stream still has frames, at most max_it iterations per chunk.
-__global__ void dec_update_kernel(DecState d, int c, int PH, int blank, int max_symbols, int max_it, cudaGraphConditionalHandle cond) {
+// With logits: the decision is the argmax of the stream's row (ties to the lowest index,
+// src/kernels.metal:521-550), taken here by warp 0; without, it was left in d.idx.
+__global__ void dec_update_kernel(DecState d, int c, int PH, int blank, int max_symbols, int max_it, cudaGraphConditionalHandle cond,
+                                  const float *__restrict__ logits, int64_t ldl, int V) {
+    __shared__ int s_k;
     const int b = blockIdx.x;
     const bool live = d.active[b];
-    const int k = live ? d.idx[b] : blank;
+    if (threadIdx.x < 32) {
+        int k0 = blank;
+        if (live) {
+            if (logits) {
+                const float *l = logits + (int64_t)b * ldl;
+                float bv = -INFINITY;
+                int bi = 0x7fffffff;
+                for (int n = threadIdx.x; n < V; n += 32) {
+                    const float v = l[n];
+                    if (v > bv) { bv = v; bi = n; }
+                }
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) {
+                    const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+                    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+                    if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+                }
+                k0 = bi;
+            } else {
+                k0 = d.idx[b];
+            }
+        }
+        if (threadIdx.x == 0) {
+            s_k = k0;
+            if (live) d.idx[b] = k0;
+        }
+    }
+    __syncthreads();
+    const int k = s_k;
     if (live && k != blank) {
         for (int l = 0; l < 2; ++l) {
             const int64_t sb = ((int64_t)l * d.streams + b) * PH;
@@ -138,6 +175,19 @@ __global__ void dec_update_kernel(DecState d, int c, int PH, int blank, int max_
             cudaGraphSetConditional(cond, (atomicAdd(&d.cnt[1], 0) > 0 && it < max_it) ? 1u : 0u);
         }
     }
+}
+
+__global__ void dec_joint_in_kernel(DecState d, const float *__restrict__ enc, int JH, uint16_t *X, int64_t plane) {
+    const int b = blockIdx.x;
+    const int er = d.erow[b], pos = d.need_pos[b];
+    const float *p = pos >= 0 ? d.predc + (int64_t)pos * JH : d.pred + (int64_t)b * JH;
+    const float *e = enc + (int64_t)(er < 0 ? 0 : er) * JH;
+    for (int i = threadIdx.x; i < JH; i += blockDim.x) {
+        const float pv = p[i];
+        if (pos >= 0) d.pred[(int64_t)b * JH + i] = pv;
+        nb::store_act(X, NEMO_FMT_BF16X2, plane, (int64_t)b * JH + i, er < 0 ? 0.0f : fmaxf(e[i] + pv, 0.0f));
+    }
+    if (threadIdx.x == 0 && pos >= 0) d.pred_valid[b] = 1;
 }
 
 __global__ void dec_reset_kernel(DecState d, int PH, int blank) {
@@ -176,9 +226,15 @@ extern "C" int nb_dec_scatter_pred(const DecState *d, int JH, void *stream) {
     dec_scatter_pred_kernel<<<d->streams, 128, 0, (cudaStream_t)stream>>>(*d, JH);
     return nb_check_launch("dec_scatter_pred_kernel");
 }
-extern "C" int nb_dec_update(const DecState *d, int c, int PH, int blank, int max_symbols, int max_it, unsigned long long cond, void *stream) {
-    dec_update_kernel<<<d->streams, 128, 0, (cudaStream_t)stream>>>(*d, c, PH, blank, max_symbols, max_it, (cudaGraphConditionalHandle)cond);
+extern "C" int nb_dec_update(const DecState *d, int c, int PH, int blank, int max_symbols, int max_it, unsigned long long cond, const float *logits,
+                             int64_t ldl, int V, void *stream) {
+    dec_update_kernel<<<d->streams, 128, 0, (cudaStream_t)stream>>>(*d, c, PH, blank, max_symbols, max_it, (cudaGraphConditionalHandle)cond, logits,
+                                                                   ldl, V);
     return nb_check_launch("dec_update_kernel");
+}
+extern "C" int nb_dec_joint_in(const DecState *d, const float *enc, int JH, uint16_t *X, int64_t plane, void *stream) {
+    dec_joint_in_kernel<<<d->streams, 128, 0, (cudaStream_t)stream>>>(*d, enc, JH, X, plane);
+    return nb_check_launch("dec_joint_in_kernel");
 }
 extern "C" int nb_dec_reset(const DecState *d, int PH, int blank, void *stream) {
     dec_reset_kernel<<<d->streams, 128, 0, (cudaStream_t)stream>>>(*d, PH, blank);

@@ -701,14 +701,17 @@ int launch(const nemo_gemm_args_t *a, cudaStream_t st) {
     return nb_check_launch("gemm_tc_kernel");
 }
 
-// Plan of an activation-major launch: BW weight rows per tile and the k-split. The split count
-// fills the SMs when there are fewer tiles than SMs (k-blocks of at least 4 per split).
+// Plan of an activation-major launch: BW weight rows per tile and the k-split. The estimate is
+// fitted to measured launches on a B200 (shapes of this model, 64..14336 rows): a round of
+// units costs ~0.27 us per k-block per 128 weight rows plus ~4 us of pipeline fill and
+// epilogue, and a k-split adds ~6 us (partial tiles through L2, reduced by the tile's last CTA),
+// so splits are only planned for long K (>= 32 k-blocks) over few tiles.
 struct PlanR {
     int bw, tiles, splits, kb_per_split, units;
-    long long cost;  // rounds of units over the SMs x (BW x k-blocks per unit): proportional to time
+    float est_us;
 };
 
-PlanR plan_r(const nemo_gemm_args_t *a, int bw) {
+PlanR plan_r(const nemo_gemm_args_t *a, int bw, bool allow_split) {
     PlanR r;
     const bool glu = a->act == NEMO_ACT_GLU;
     const int kblocks = (a->K + BK - 1) / BK;
@@ -716,17 +719,17 @@ PlanR plan_r(const nemo_gemm_args_t *a, int bw) {
     r.bw = bw;
     r.tiles = n_wtiles * ((a->M + 127) / 128);
     int splits = 1;
-    if (r.tiles < g_sms) {
+    if (allow_split && kblocks >= 32 && 2 * r.tiles < g_sms) {
         splits = g_sms / r.tiles;
-        if (splits > kblocks / 4) splits = kblocks / 4;
+        if (splits > kblocks / 16) splits = kblocks / 16;  // at least 16 k-blocks per split
         if (splits < 1) splits = 1;
         if ((size_t)r.tiles * splits * 128 * bw > g_ws_floats || r.tiles > g_ncounters) splits = 1;
     }
     r.kb_per_split = (kblocks + splits - 1) / splits;
     r.splits = (kblocks + r.kb_per_split - 1) / r.kb_per_split;
     r.units = r.tiles * r.splits;
-    const long long rounds = (r.units + g_sms - 1) / g_sms;
-    r.cost = rounds * bw * r.kb_per_split + (r.splits > 1 ? bw * 2 : 0);
+    const int rounds = (r.units + g_sms - 1) / g_sms;
+    r.est_us = rounds * (0.27f * (bw / 128) * r.kb_per_split + 4.0f) + (r.splits > 1 ? 6.0f : 0.0f);
     return r;
 }
 
@@ -774,10 +777,13 @@ int launch_r(const nemo_gemm_args_t *a, const PlanR &pl, cudaStream_t st) {
 
 int launch_rows(const nemo_gemm_args_t *a, cudaStream_t st) {
     const bool glu = a->act == NEMO_ACT_GLU;
-    const PlanR p256 = plan_r(a, 256), p128 = plan_r(a, 128);
     const bool ok256 = !glu || (a->N / 2) % 128 == 0;
-    if (ok256 && p256.cost <= p128.cost) return launch_r<256>(a, p256, st);
-    return launch_r<128>(a, p128, st);
+    PlanR best = plan_r(a, 128, false);
+    const PlanR cand[3] = { plan_r(a, 256, false), plan_r(a, 128, true), plan_r(a, 256, true) };
+    for (const PlanR &p : cand)
+        if ((p.bw == 128 || ok256) && p.est_us < best.est_us) best = p;
+    if (best.bw == 256) return launch_r<256>(a, best, st);
+    return launch_r<128>(a, best, st);
 }
 
 }  // namespace
@@ -791,7 +797,9 @@ int nb_gemm_tc_layout(const nemo_gemm_args_t *a, int layout, void *stream) {
     if (a->act == NEMO_ACT_GLU && ((a->N / 2) % 64)) return nb_set_error("tensor-core GEMM: GLU needs N/2 to be a multiple of 64");
     if (a->K % 8) return nb_set_error("tensor-core GEMM: K must be a multiple of 8");
     cudaStream_t st = (cudaStream_t)stream;
-    if (layout == 0) layout = a->M >= 128 ? 2 : 1;
+    // activation-major above 32 rows (measured faster at 64 and more); up to 32 rows the weights
+    // must stream through every SM with split-K, which the weight-major tiles do
+    if (layout == 0) layout = a->M > 32 ? 2 : 1;
     if (layout == 2) return launch_rows(a, st);
     if (a->M <= 16) return launch<16>(a, st);
     if (a->M <= 32) return launch<32>(a, st);

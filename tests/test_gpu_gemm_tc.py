@@ -130,4 +130,4 @@ def test_tcr_matches_weight_major_tiles():
     for act in (1, 3):
         a = run_gemm(A, W, act=act, kind=4, a_fmt=1)
         b = run_gemm(A, W, act=act, kind=5, a_fmt=1)
-        assert rel_err(b, a) < 1e-6
+        assert rel_err(b, a) < 1e-5  # same products, fp32 sums in a different order (k-splits differ)
