@@ -191,6 +191,69 @@ __global__ void __launch_bounds__(256) subsample_front_kernel(const float *__res
     }
 }
 
+// The same two stages with the roles flipped: a lane owns one output position (its 7x7 patch in
+// registers) and the warp walks 32 channels, so every weight is loaded once per warp (a
+// broadcast) instead of once per lane; a 32 x 32 shared-memory transpose turns the
+// position-per-lane results into channel-contiguous stores. C % 256 == 0 (8 warps x 32 channels).
+__global__ void __launch_bounds__(256) subsample_front_lanes_kernel(const float *__restrict__ X, int64_t x_sstride, const float *__restrict__ W0,
+                                                                    const float *__restrict__ b0, const float *__restrict__ W2,
+                                                                    const float *__restrict__ b2, void *Y, int y_fmt, int64_t y_plane, int T, int F,
+                                                                    int T1, int F1, int T2, int F2, int C, int64_t positions) {
+    __shared__ float stg[8][32][33];
+    nb::pdl_wait();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t pidx = (int64_t)blockIdx.x * 32 + lane;
+    const bool pv = pidx < positions;
+    const int64_t pp = pv ? pidx : 0;
+    const int f2 = (int)(pp % F2);
+    const int64_t r = pp / F2;
+    const int t2 = (int)(r % T2), s = (int)(r / T2);
+    const float *x = X + (int64_t)s * x_sstride;
+    const int tx0 = 4 * t2 - 6, fx0 = 4 * f2 - 6;
+    float pt[49];
+#pragma unroll
+    for (int e = 0; e < 49; ++e) {
+        const int ti = tx0 + e / 7, fi = fx0 + e % 7;
+        pt[e] = (pv && ti >= 0 && ti < T && fi >= 0 && fi < F) ? x[(int64_t)ti * F + fi] : 0.0f;
+    }
+    bool okt[3], okf[3];
+#pragma unroll
+    for (int k = 0; k < 3; ++k) {
+        const int t1 = 2 * t2 - 2 + k, f1 = 2 * f2 - 2 + k;
+        okt[k] = t1 >= 0 && t1 < T1;
+        okf[k] = f1 >= 0 && f1 < F1;
+    }
+    for (int cb = warp * 32; cb < C; cb += 8 * 32) {
+        for (int q = 0; q < 32; ++q) {
+            const int ch = cb + q;
+            float w0[9], w2[9];
+#pragma unroll
+            for (int k = 0; k < 9; ++k) { w0[k] = __ldg(W0 + ch * 9 + k); w2[k] = __ldg(W2 + ch * 9 + k); }
+            const float bb0 = __ldg(b0 + ch);
+            float acc = __ldg(b2 + ch);
+#pragma unroll
+            for (int kh = 0; kh < 3; ++kh)
+#pragma unroll
+                for (int kw = 0; kw < 3; ++kw) {
+                    if (!okt[kh] || !okf[kw]) continue;
+                    float c0 = bb0;
+#pragma unroll
+                    for (int a = 0; a < 3; ++a)
+#pragma unroll
+                        for (int b = 0; b < 3; ++b) c0 += w0[a * 3 + b] * pt[(2 * kh + a) * 7 + 2 * kw + b];
+                    acc += w2[kh * 3 + kw] * fmaxf(c0, 0.0f);
+                }
+            stg[warp][lane][q] = acc;
+        }
+        __syncwarp();
+        for (int p = 0; p < 32; ++p) {
+            const int64_t po = (int64_t)blockIdx.x * 32 + p;
+            if (po < positions) nb::store_act(Y, y_fmt, y_plane, po * C + cb + lane, stg[warp][p][lane]);
+        }
+        __syncwarp();
+    }
+}
+
 // flatten_cf (src/kernels.metal:457-462) of rows [lo, lo + c) only: Y[s*c + i][ch*F + f] =
 // X[s][lo + i][f][ch]. Thread per output element (f fastest within a channel).
 __global__ void flatten_rows_kernel(const float *__restrict__ X, void *Y, int y_fmt, int64_t y_plane, const int *lo_p, int T, int F, int C, int c,
@@ -288,12 +351,30 @@ __global__ void __launch_bounds__(WROWS * 32) dwconv_ln_silu_warp_kernel(const f
         if (j < nv) {
             const int ch = 4 * (lane + 32 * j);
             float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-            for (int tap = 0; tap < taps; ++tap) {
-                const float4 xv = *(const float4 *)(x + (int64_t)tap * D + ch);
-                acc.x += W[(ch + 0) * taps + tap] * xv.x;
-                acc.y += W[(ch + 1) * taps + tap] * xv.y;
-                acc.z += W[(ch + 2) * taps + tap] * xv.z;
-                acc.w += W[(ch + 3) * taps + tap] * xv.w;
+            if (taps == 9) {
+                // the 4 channels' 36 taps are contiguous ([ch][9]) and 16-byte aligned: 9 vector loads
+                float w[36];
+#pragma unroll
+                for (int q = 0; q < 9; ++q) {
+                    const float4 t4 = __ldg((const float4 *)(W + ch * 9) + q);
+                    w[4 * q] = t4.x; w[4 * q + 1] = t4.y; w[4 * q + 2] = t4.z; w[4 * q + 3] = t4.w;
+                }
+#pragma unroll
+                for (int tap = 0; tap < 9; ++tap) {
+                    const float4 xv = *(const float4 *)(x + (int64_t)tap * D + ch);
+                    acc.x += w[tap] * xv.x;
+                    acc.y += w[9 + tap] * xv.y;
+                    acc.z += w[18 + tap] * xv.z;
+                    acc.w += w[27 + tap] * xv.w;
+                }
+            } else {
+                for (int tap = 0; tap < taps; ++tap) {
+                    const float4 xv = *(const float4 *)(x + (int64_t)tap * D + ch);
+                    acc.x += W[(ch + 0) * taps + tap] * xv.x;
+                    acc.y += W[(ch + 1) * taps + tap] * xv.y;
+                    acc.z += W[(ch + 2) * taps + tap] * xv.z;
+                    acc.w += W[(ch + 3) * taps + tap] * xv.w;
+                }
             }
             v[j] = acc;
         }
@@ -348,7 +429,7 @@ extern "C" int nemo_dwconv_ln_silu(const float *din, int64_t din_sstride, const 
                                    int y_fmt, int64_t y_plane, int streams, int c, int D, int taps, float eps, void *stream) {
     if (D > LNT * LN_MAXV) return nb_set_error("nemo_dwconv_ln_silu: D=%d too large", D);
     if (streams <= 0 || c <= 0) return 0;
-    if (warp_rows_ok(din, Y, y_fmt, y_plane, D) && din_sstride % 4 == 0) {
+    if (warp_rows_ok(din, Y, y_fmt, y_plane, D) && din_sstride % 4 == 0 && !((uintptr_t)W & 15)) {
         const int items = streams * c;
         dwconv_ln_silu_warp_kernel<<<(items + WROWS - 1) / WROWS, WROWS * 32, 0, (cudaStream_t)stream>>>(din, din_sstride, pos, W, g, b, Y, y_fmt, y_plane,
                                                                                                        streams, c, D, taps, eps);
@@ -383,6 +464,11 @@ extern "C" int nemo_subsample_front(const float *X, int64_t x_sstride, const flo
     const int T1 = T / 2 + 1, F1 = F / 2 + 1, T2 = T1 / 2 + 1, F2 = F1 / 2 + 1;
     const int64_t positions = (int64_t)streams * T2 * F2;
     if (positions <= 0) return 0;
+    if (C % 256 == 0) {
+        subsample_front_lanes_kernel<<<(unsigned)((positions + 31) / 32), 256, 0, (cudaStream_t)stream>>>(X, x_sstride, W0, b0, W2, b2, Y, y_fmt, y_plane, T,
+                                                                                                        F, T1, F1, T2, F2, C, positions);
+        return nb_check_launch("subsample_front_lanes_kernel");
+    }
     subsample_front_kernel<<<(unsigned)((positions + 7) / 8), 256, 0, (cudaStream_t)stream>>>(X, x_sstride, W0, b0, W2, b2, Y, y_fmt, y_plane, T, F, T1,
                                                                                               F1, T2, F2, C, positions);
     return nb_check_launch("subsample_front_kernel");
