@@ -20,6 +20,48 @@ constexpr int MAXL = 96;   // keys in the window
 
 __device__ __forceinline__ float dot4(const float4 a, const float4 b) { return a.x * b.x + a.y * b.y + a.z * b.z + a.w * b.w; }
 
+// Content scores sk[i][r] = (q_i + u) . k_r (rows r < L) and position scores gp[i][r - L] =
+// (q_i + v) . P[r - L] (rows L .. L + NP - 1). A warp takes R = 32 / Q rows at a time and forms
+// the R x Q partial dot products of its lanes' 4 dims; one halving butterfly (31 shuffles for 32
+// values instead of 5 per value) leaves lane l with the total of value l = (row l / Q, query l % Q).
+template <int Q>
+__device__ __forceinline__ void score_rows(const float *Kb, int64_t ldk, const float *Pb, int D, int L, int NP, int c, const float (*qu)[DH],
+                                           const float (*qv)[DH], float (*sk)[MAXL], float (*gp)[MAXL + MAXC], int warp, int lane) {
+    constexpr int R = 32 / Q;
+    const int rows = L + NP;
+    for (int r0 = warp * R; r0 < rows; r0 += (THREADS / 32) * R) {
+        float4 x[R];
+#pragma unroll
+        for (int k = 0; k < R; ++k) {
+            const int r = r0 + k;
+            x[k] = r < L ? *(const float4 *)(Kb + (int64_t)r * ldk + 4 * lane)
+                 : r < rows ? *(const float4 *)(Pb + (int64_t)(r - L) * D + 4 * lane) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+        float a[32];
+#pragma unroll
+        for (int k = 0; k < R; ++k) {
+            const bool is_k = r0 + k < L;
+#pragma unroll
+            for (int i = 0; i < Q; ++i) a[k * Q + i] = i < c ? dot4(x[k], *(const float4 *)((is_k ? qu[i] : qv[i]) + 4 * lane)) : 0.0f;
+        }
+#pragma unroll
+        for (int o = 16, n = 32; o >= 1; o >>= 1, n >>= 1) {
+            const bool up = lane & o;
+#pragma unroll
+            for (int k = 0; k < n / 2; ++k) {
+                const float send = up ? a[k] : a[k + n / 2];
+                const float keep = up ? a[k + n / 2] : a[k];
+                a[k] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+            }
+        }
+        const int i = lane % Q, r = r0 + lane / Q;
+        if (i < c && r < rows) {
+            if (r < L) sk[i][r] = a[0];
+            else gp[i][r - L] = a[0];
+        }
+    }
+}
+
 __global__ void __launch_bounds__(THREADS) attention_kernel(const float *__restrict__ Q, int64_t ldq, int64_t q_sstride, const float *__restrict__ K,
                                                             const float *__restrict__ V, int64_t ldk, int64_t kv_sstride, const int *pos_p,
                                                             const int *cache_len_p, const float *__restrict__ P, const float *__restrict__ bias_u,
@@ -44,24 +86,9 @@ __global__ void __launch_bounds__(THREADS) attention_kernel(const float *__restr
     const float *Kb = K + (int64_t)s * kv_sstride + (int64_t)(pos - cache_len) * ldk + off;
     const float *Vb = V + (int64_t)s * kv_sstride + (int64_t)(pos - cache_len) * ldk + off;
     const float *Pb = P + (int64_t)prow0 * D + off;
-    // content scores (rows 0..L-1) and position scores (rows L..L+NP-1), one row per warp step
-    for (int r = warp; r < L + NP; r += THREADS / 32) {
-        const bool is_k = r < L;
-        const float4 x = is_k ? *(const float4 *)(Kb + (int64_t)r * ldk + 4 * lane) : *(const float4 *)(Pb + (int64_t)(r - L) * D + 4 * lane);
-        float part[MAXC];
-#pragma unroll
-        for (int i = 0; i < MAXC; ++i)
-            if (i < c) part[i] = dot4(x, *(const float4 *)((is_k ? qu[i] : qv[i]) + 4 * lane));
-#pragma unroll
-        for (int i = 0; i < MAXC; ++i)
-            if (i < c) {
-                const float v = nb::warp_sum(part[i]);
-                if (lane == 0) {
-                    if (is_k) sk[i][r] = v;
-                    else gp[i][r - L] = v;
-                }
-            }
-    }
+    // content scores (rows 0..L-1) and position scores (rows L..L+NP-1)
+    if (c <= 8) score_rows<8>(Kb, ldk, Pb, D, L, NP, c, qu, qv, sk, gp, warp, lane);
+    else score_rows<16>(Kb, ldk, Pb, D, L, NP, c, qu, qv, sk, gp, warp, lane);
     __syncthreads();
     // softmax of each query row (one warp per row)
     for (int i = warp; i < c; i += THREADS / 32) {
@@ -93,7 +120,20 @@ __global__ void __launch_bounds__(THREADS) attention_kernel(const float *__restr
     float acc[MAXC / 2];
 #pragma unroll
     for (int k = 0; k < MAXC / 2; ++k) acc[k] = 0.0f;
-    for (int j = 0; j < L; ++j) {
+    int j = 0;
+    for (; j + 8 <= L; j += 8) {  // 8 value rows in flight at a time
+        float vj[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) vj[u] = Vb[(int64_t)(j + u) * ldk + d];
+#pragma unroll
+        for (int u = 0; u < 8; ++u)
+#pragma unroll
+            for (int k = 0; k < MAXC / 2; ++k) {
+                const int i = hrow + 2 * k;
+                if (i < c) acc[k] += sk[i][j + u] * vj[u];
+            }
+    }
+    for (; j < L; ++j) {
         const float vj = Vb[(int64_t)j * ldk + d];
 #pragma unroll
         for (int k = 0; k < MAXC / 2; ++k) {
