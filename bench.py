@@ -9,7 +9,8 @@ stream: subsampling, 24 conformer blocks, prompt, joint projection and the greed
   value : audio-sec/sec over all GPUs with the log-mel features already in HBM (CUDA-event time
           on the engine's stream, max over ranks);
   e2e   : the same metric through the public API (nemoasr_batch_feed) from host audio: host
-          resampling/mel, H2D window copies and D2H token reads inside the timed region.
+          pre-emphasis and frame bookkeeping, H2D sample spans, GPU log-mel and the step, D2H token
+          reads inside the timed region.
 
 Streams shard across GPUs with no collective (one process per GPU); torch.distributed is used
 only for the start barrier and the max-over-ranks of the timings.
@@ -333,11 +334,11 @@ def main():
             batch.feed(audio[:, i * blk:(i + 1) * blk])
         torch.cuda.synchronize()
         wall = max_over_ranks(dist, time.perf_counter() - t0, "cuda")
-        nwin = 16 + a.latency // 10 + 1
+        frames = a.latency // 10  # log-mel frames per step and stream
         e2e = {"value": a.steps * chunk_s * B * world / wall, "unit": UNIT,
-               "h2d_bytes_per_step": B * nwin * 128 * 4 + 12,
+               "h2d_bytes_per_step": B * ((frames - 1) * 160 + 512) * 4 + 12,
                "d2h_bytes_per_step": B * 4 + B * 16 * 10 * 4,
-               "note": "host audio -> host resample/log-mel (OpenMP) -> H2D window -> GPU step -> D2H tokens, wall clock"}
+               "note": "host audio -> host pre-emphasis and frame bookkeeping -> H2D sample spans -> GPU log-mel + step -> D2H tokens, wall clock"}
     batch.close()
 
     # ---- dominant kernel roofline ------------------------------------------------------------

@@ -109,6 +109,12 @@ int nemo_dwconv2d_s2(const float *X, const float *W, const float *bias, float *Y
    at src/encoder.c:258). */
 int nemo_flatten_rows(const float *X, float *Y, const int *lo, int streams, int T, int F, int C, int c, void *stream);
 
+/* Log-mel frames (the transform of src/mel.c:115-173: Hann(400) centred in 512 points,
+   double-precision FFT, power, 128 Slaney filters, log(x + 2^-24)) of `streams` sample spans:
+   frame f of stream s reads span[s * span_stride + f * 160 .. + 512) (pre-emphasised samples,
+   already reflected at the stream edges) and goes to out[s * out_stride + f * 128 ..]. */
+int nemo_logmel_frames(const float *span, int64_t span_stride, int streams, int nframes, float *out, int64_t out_stride, void *stream);
+
 /* LSTM cell on gates [rows][4H] (i, f, g, o). Replaces lstm_cell (src/kernels.metal:475-486). */
 int nemo_lstm_cell(const float *gates, const float *c_in, float *c_out, float *h_out, int rows, int H, void *stream);
 /* Joint + argmax per row: logits = W . relu(enc[r] + pred[r]) + b (W bf16 [V][H]); ties ->

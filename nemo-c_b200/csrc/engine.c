@@ -29,6 +29,14 @@ struct nb_engine {
     const float *dev_mel;
     int64_t dev_mel_sstride;
     size_t dev_mel_frames;
+    /* log-mel on the GPU (NEMO_HOST_MEL=1 keeps it on the host): each stream's sample span is
+       staged in pinned memory, the frames go to a device queue the windows are read from */
+    int use_gpu_mel;
+    float *h_span, *d_span;    /* [B][span_cap] */
+    size_t span_cap;
+    float *d_melq;             /* [B][qcap][128] */
+    size_t qcap, q_base, q_end; /* absolute frame index of queue row 0; frames produced */
+    cudaEvent_t span_ev;       /* the last span upload has been read */
     /* device */
     float *d_win, *h_win;      /* [B][nwin_max][128]; h_win pinned */
     float *c0, *c1, *c2, *c3, *c4, *flat;
@@ -240,6 +248,19 @@ nb_engine_t *nb_engine_create(nb_model_t *m, int B, int right, char *err, size_t
         for (int s = 0; s < B; ++s) CK(cudaMemcpy(e->b_eff + (size_t)s * PRH, be, PRH * 4, cudaMemcpyHostToDevice));
         free(be);
     }
+    {
+        const char *hm = getenv("NEMO_HOST_MEL");
+        e->use_gpu_mel = !(hm && !strcmp(hm, "1"));
+        if (e->use_gpu_mel) {
+            e->span_cap = (size_t)(NB_SPAN_FRAMES - 1) * NB_MEL_HOP + NB_MEL_NFFT;
+            e->qcap = 2 * ((size_t)e->chunk_mel + NB_MEL_CACHE + NB_SPAN_FRAMES) + 16;
+            CK(cudaMallocHost((void **)&e->h_span, Bz * e->span_cap * sizeof(float)));
+            CK(cudaEventCreateWithFlags(&e->span_ev, cudaEventDisableTiming));
+            e->d_span = dalloc(Bz * e->span_cap * sizeof(float), &fail);
+            e->d_melq = dalloc(Bz * e->qcap * 128 * sizeof(float), &fail);
+            if (fail) { snprintf(err, errlen, "out of device memory for the mel queue of %d streams", B); goto fail; }
+        }
+    }
     if (nb_gemm_tc_init()) { snprintf(err, errlen, "%s", nemo_gpu_last_error()); goto fail; }
     {
         const char *gr = getenv("NEMO_GRAPHS");
@@ -277,6 +298,10 @@ void nb_engine_destroy(nb_engine_t *e) {
     if (e->ev1) cudaEventDestroy(e->ev1);
     for (int i = 0; i < e->ngraphs; ++i) cudaGraphExecDestroy(e->graphs[i].exec);
     free(e->enc1_layers);
+    if (e->h_span) cudaFreeHost(e->h_span);
+    if (e->d_span) cudaFree(e->d_span);
+    if (e->d_melq) cudaFree(e->d_melq);
+    if (e->span_ev) cudaEventDestroy(e->span_ev);
     if (e->d_dec1) cudaFree(e->d_dec1);
     if (e->d_dec1_i) cudaFree(e->d_dec1_i);
     if (e->d_dec1_bar) cudaFree(e->d_dec1_bar);
@@ -293,6 +318,7 @@ int nb_engine_reset(nb_engine_t *e, char *err, size_t errlen) {
     e->pending_n = 0;
     e->dev_mel = NULL;
     e->dev_mel_frames = 0;
+    e->q_base = e->q_end = 0;
     e->mel_cache_n = 0;
     e->consumed = e->emitted = 0;
     e->closed = 0;
@@ -342,6 +368,55 @@ int nb_engine_push(nb_engine_t *e, const float *const *mel, size_t nframes, char
         for (int s = 0; s < e->B; ++s) e->pending[s] = realloc(e->pending[s], e->pending_cap * 128 * sizeof(float));
     }
     for (int s = 0; s < e->B; ++s) memcpy(e->pending[s] + e->pending_n * 128, mel[s], nframes * 128 * sizeof(float));
+    e->pending_n += nframes;
+    return 0;
+}
+
+int nb_engine_gpu_mel(const nb_engine_t *e) { return e->use_gpu_mel; }
+
+/* Staging span of stream s (pinned host memory, *cap floats); call nb_engine_span_wait first. */
+float *nb_engine_span(nb_engine_t *e, int s, size_t *cap) {
+    *cap = e->span_cap;
+    return e->h_span + (size_t)s * e->span_cap;
+}
+
+/* The previous span upload has left the staging buffers. */
+int nb_engine_span_wait(nb_engine_t *e) { return cudaEventSynchronize(e->span_ev) == cudaSuccess ? 0 : -1; }
+
+/* nframes new frames of every stream from the staged spans (nb_mel_stage): upload, transform on
+   the GPU into the frame queue, and queue them for the next steps. */
+int nb_engine_push_spans(nb_engine_t *e, size_t nframes, char *err, size_t errlen) {
+    if (!nframes) return 0;
+    if (!e->use_gpu_mel || e->dev_mel) { snprintf(err, errlen, "engine does not take sample spans"); return -1; }
+    if (nframes > NB_SPAN_FRAMES) { snprintf(err, errlen, "%zu frames in one span (at most %d)", nframes, NB_SPAN_FRAMES); return -1; }
+    cudaStream_t st = e->st;
+    const size_t row = 128 * sizeof(float), len = (nframes - 1) * NB_MEL_HOP + NB_MEL_NFFT;
+    if (e->q_end - e->q_base + nframes > e->qcap) {
+        /* move the frames a later window can still read (from the next window's first frame on)
+           to the front of the queue; the queue is sized so source and destination never overlap */
+        const size_t keep_from = e->consumed - (size_t)e->mel_cache_n, keep = e->q_end - keep_from;
+        if (keep_from < e->q_base || keep + nframes > e->qcap || keep_from - e->q_base < keep) {
+            snprintf(err, errlen, "mel queue overflow (%zu pending frames)", keep);
+            return -1;
+        }
+        if (keep && cudaMemcpy2DAsync(e->d_melq, e->qcap * row, e->d_melq + (keep_from - e->q_base) * 128, e->qcap * row, keep * row, (size_t)e->B,
+                                      cudaMemcpyDeviceToDevice, st) != cudaSuccess) {
+            snprintf(err, errlen, "mel queue: %s", cudaGetErrorString(cudaGetLastError()));
+            return -1;
+        }
+        e->q_base = keep_from;
+    }
+    if (cudaMemcpy2DAsync(e->d_span, e->span_cap * sizeof(float), e->h_span, e->span_cap * sizeof(float), len * sizeof(float), (size_t)e->B,
+                          cudaMemcpyHostToDevice, st) != cudaSuccess ||
+        cudaEventRecord(e->span_ev, st) != cudaSuccess) {
+        snprintf(err, errlen, "span upload: %s", cudaGetErrorString(cudaGetLastError()));
+        return -1;
+    }
+    if (nb_logmel_frames(e->d_span, (int64_t)e->span_cap, e->B, (int)nframes, e->d_melq, (int64_t)e->qcap * 128, (int64_t)(e->q_end - e->q_base), st)) {
+        snprintf(err, errlen, "%s", nemo_gpu_last_error());
+        return -1;
+    }
+    e->q_end += nframes;
     e->pending_n += nframes;
     return 0;
 }
@@ -681,7 +756,8 @@ int nb_engine_step(nb_engine_t *e, int final, int *tokens, int max_tokens, int *
     const int nwin = e->mel_cache_n + (int)take;
     const size_t wstride = (size_t)e->nwin_max * 128;
     const size_t win_first = e->consumed - (size_t)e->mel_cache_n; /* window = frames [win_first, consumed + take) */
-    if (!e->dev_mel) {
+    const int host_queue = !e->dev_mel && !e->use_gpu_mel;
+    if (host_queue) {
         for (int s = 0; s < e->B; ++s) {
             float *w = e->h_win + (size_t)s * wstride;
             memcpy(w, e->mel_cache + (size_t)s * NB_MEL_CACHE * 128, (size_t)e->mel_cache_n * 128 * sizeof(float));
@@ -696,7 +772,7 @@ int nb_engine_step(nb_engine_t *e, int final, int *tokens, int max_tokens, int *
     const size_t hi = include_boundary ? (size_t)T3 : end / 8 - base;
     e->consumed = end;
     const int keep = nwin < NB_MEL_CACHE ? nwin : NB_MEL_CACHE;
-    if (!e->dev_mel) {
+    if (host_queue) {
         for (int s = 0; s < e->B; ++s)
             memcpy(e->mel_cache + (size_t)s * NB_MEL_CACHE * 128, e->h_win + (size_t)s * wstride + (size_t)(nwin - keep) * 128,
                    (size_t)keep * 128 * sizeof(float));
@@ -728,6 +804,9 @@ int nb_engine_step(nb_engine_t *e, int final, int *tokens, int max_tokens, int *
     cudaError_t wrc;
     if (e->dev_mel)
         wrc = cudaMemcpy2DAsync(e->d_win, wstride * sizeof(float), e->dev_mel + win_first * 128, (size_t)e->dev_mel_sstride * sizeof(float),
+                                (size_t)nwin * 128 * sizeof(float), (size_t)e->B, cudaMemcpyDeviceToDevice, st);
+    else if (e->use_gpu_mel)
+        wrc = cudaMemcpy2DAsync(e->d_win, wstride * sizeof(float), e->d_melq + (win_first - e->q_base) * 128, e->qcap * 128 * sizeof(float),
                                 (size_t)nwin * 128 * sizeof(float), (size_t)e->B, cudaMemcpyDeviceToDevice, st);
     else
         wrc = cudaMemcpyAsync(e->d_win, e->h_win, (size_t)e->B * wstride * sizeof(float), cudaMemcpyHostToDevice, st);

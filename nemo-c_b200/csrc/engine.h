@@ -20,6 +20,12 @@ int nb_engine_set_prompt(nb_engine_t *e, int stream, int prompt_index, char *err
 int nb_engine_attach_device_mel(nb_engine_t *e, const float *d_mel, int64_t sstride_floats, size_t frames, char *err, size_t errlen);
 /* Queue nframes mel rows (128 floats each) for every stream: mel[s] points at stream s's rows. */
 int nb_engine_push(nb_engine_t *e, const float *const *mel, size_t nframes, char *err, size_t errlen);
+/* GPU log-mel: stage each stream's sample span (nb_mel_stage) into nb_engine_span after
+   nb_engine_span_wait, then nb_engine_push_spans with the frame count. */
+int nb_engine_gpu_mel(const nb_engine_t *e);
+float *nb_engine_span(nb_engine_t *e, int s, size_t *cap);
+int nb_engine_span_wait(nb_engine_t *e);
+int nb_engine_push_spans(nb_engine_t *e, size_t nframes, char *err, size_t errlen);
 /* One encoder step + greedy decode (src/encoder.c:213-267 then src/decoder.c:92-127).
    Returns 1 if a piece was consumed, 0 if nothing to do, -1 on error. Tokens of stream s are
    appended to tokens[s*max_tokens + counts[s] ...] and counts[s] advanced; *frames = rows. */

@@ -69,6 +69,10 @@ int nb_encoder1(const NbEnc1Args *args, int grid, void *stream);
 int nb_encoder1_slot_bytes(int D, int FF, int grid);
 size_t nb_encoder1_smem(int slot_bytes);
 
+/* log-mel frames of sample spans (k_mel.cu) into rows out_row0.. of each stream's frame block */
+int nb_logmel_frames(const float *span, int64_t span_stride, int streams, int nframes, float *out, int64_t out_stride, int64_t out_row0,
+                     void *stream);
+
 int nb_set_error(const char *fmt, ...);
 int nb_gemm_tc_init(void);
 void nb_set_launch_counting(int on);

@@ -95,9 +95,12 @@ static float sample_at(const nb_mel_t *m, long g) {
     return (i < 0 || i >= (long)m->y_len) ? 0.0f : m->y[i];
 }
 
-void nb_mel_push(nb_mel_t *m, const float *samples, size_t n, int final, const float **frames, size_t *nframes) {
-    *frames = NULL;
-    *nframes = 0;
+/* Append n samples (pre-emphasised) and return the range [*t0, *t0 + *count) of frames that are
+   now complete: once a frame's right half is present, or every remaining frame on the final call
+   (their right halves reflect). */
+static void mel_advance(nb_mel_t *m, const float *samples, size_t n, int final, size_t *t0, size_t *count) {
+    *t0 = m->next_frame;
+    *count = 0;
     if (m->closed) return;
     if (m->y_len + n > m->y_cap) {
         while (m->y_len + n > m->y_cap) m->y_cap *= 2;
@@ -110,30 +113,13 @@ void nb_mel_push(nb_mel_t *m, const float *samples, size_t n, int final, const f
         m->have_last = 1;
     }
     m->total += n;
-    /* a frame is complete once its right half is present; the final call also emits the
-       frames whose right half is reflected */
     const size_t end = final ? m->total / NB_MEL_HOP + 1 : (m->total >= LOOKAHEAD ? (m->total - LOOKAHEAD) / NB_MEL_HOP + 1 : 0);
     if (final) m->closed = 1;
-    if (end <= m->next_frame) return;
-    const size_t count = end - m->next_frame;
-    if (count * NB_MEL_NMEL > m->out_cap) { m->out_cap = count * NB_MEL_NMEL; m->out = realloc(m->out, m->out_cap * sizeof(float)); }
-    double re[NB_MEL_NFFT], im[NB_MEL_NFFT];
-    float pw[NB_MEL_NFREQ];
-    for (size_t t = m->next_frame; t < end; ++t) {
-        const long start = (long)t * NB_MEL_HOP - LOOKAHEAD;
-        for (int k = 0; k < NB_MEL_NFFT; ++k) { re[k] = (double)(sample_at(m, start + k) * m->window[k]); im[k] = 0.0; }
-        fft(m, re, im);
-        for (int k = 0; k < NB_MEL_NFREQ; ++k) pw[k] = (float)(re[k] * re[k] + im[k] * im[k]);
-        float *row = m->out + (t - m->next_frame) * NB_MEL_NMEL;
-        for (int b = 0; b < NB_MEL_NMEL; ++b) {
-            const float *f = m->fb + b * NB_MEL_NFREQ;
-            float acc = 0.0f;
-            for (int k = 0; k < NB_MEL_NFREQ; ++k) acc += f[k] * pw[k];
-            row[b] = logf(acc + LOG_GUARD);
-        }
-    }
-    *frames = m->out;
-    *nframes = count;
+    if (end > m->next_frame) *count = end - m->next_frame;
+}
+
+/* Frames up to `end` are done: drop the samples no later frame reads. */
+static void mel_retire(nb_mel_t *m, size_t end) {
     m->next_frame = end;
     const long keep = (long)m->next_frame * NB_MEL_HOP - NB_MEL_NFFT - 2;
     if (keep > (long)m->y_start) {
@@ -143,6 +129,56 @@ void nb_mel_push(nb_mel_t *m, const float *samples, size_t n, int final, const f
         m->y_len -= drop;
         m->y_start += drop;
     }
+}
+
+void nb_mel_push(nb_mel_t *m, const float *samples, size_t n, int final, const float **frames, size_t *nframes) {
+    *frames = NULL;
+    *nframes = 0;
+    size_t t0, count;
+    mel_advance(m, samples, n, final, &t0, &count);
+    if (!count) return;
+    if (count * NB_MEL_NMEL > m->out_cap) { m->out_cap = count * NB_MEL_NMEL; m->out = realloc(m->out, m->out_cap * sizeof(float)); }
+    double re[NB_MEL_NFFT], im[NB_MEL_NFFT];
+    float pw[NB_MEL_NFREQ];
+    for (size_t t = t0; t < t0 + count; ++t) {
+        const long start = (long)t * NB_MEL_HOP - LOOKAHEAD;
+        for (int k = 0; k < NB_MEL_NFFT; ++k) { re[k] = (double)(sample_at(m, start + k) * m->window[k]); im[k] = 0.0; }
+        fft(m, re, im);
+        for (int k = 0; k < NB_MEL_NFREQ; ++k) pw[k] = (float)(re[k] * re[k] + im[k] * im[k]);
+        float *row = m->out + (t - t0) * NB_MEL_NMEL;
+        for (int b = 0; b < NB_MEL_NMEL; ++b) {
+            const float *f = m->fb + b * NB_MEL_NFREQ;
+            float acc = 0.0f;
+            for (int k = 0; k < NB_MEL_NFREQ; ++k) acc += f[k] * pw[k];
+            row[b] = logf(acc + LOG_GUARD);
+        }
+    }
+    *frames = m->out;
+    *nframes = count;
+    mel_retire(m, t0 + count);
+}
+
+/* Same bookkeeping as nb_mel_push, without the transform: the samples the new frames read
+   (pre-emphasised, reflected at the stream edges) go to span: frame t0 + i covers
+   span[i * HOP .. i * HOP + NFFT). Returns the frame count, or (size_t)-1 if span_cap is short. */
+size_t nb_mel_stage(nb_mel_t *m, const float *samples, size_t n, int final, float *span, size_t span_cap) {
+    size_t t0, count;
+    mel_advance(m, samples, n, final, &t0, &count);
+    if (!count) return 0;
+    const size_t len = (count - 1) * NB_MEL_HOP + NB_MEL_NFFT;
+    if (len > span_cap) return (size_t)-1;
+    const long start = (long)t0 * NB_MEL_HOP - LOOKAHEAD;
+    for (size_t i = 0; i < len; ++i) span[i] = sample_at(m, start + (long)i);
+    mel_retire(m, t0 + count);
+    return count;
+}
+
+/* The constant tables of the transform (analysis window, filterbank, FFT twiddles). */
+void nb_mel_tables(const nb_mel_t *m, const float **window, const float **fb, const double **wr, const double **wi) {
+    *window = m->window;
+    *fb = m->fb;
+    *wr = m->wr;
+    *wi = m->wi;
 }
 
 /* ---- resampler --------------------------------------------------------------------------- */

@@ -17,6 +17,7 @@ extern "C" {
 #define NB_MEL_NMEL 128
 #define NB_MEL_NFREQ (NB_MEL_NFFT / 2 + 1)
 #define NB_MEL_CACHE 16        /* mel rows carried into the next window */
+#define NB_SPAN_FRAMES 128     /* most frames one staged sample span yields (GPU log-mel) */
 #define NB_EPOCH_CHUNKS 8      /* caches are compacted once per this many max-size chunks */
 #define NB_MIN_CMAX 16         /* cache capacity is sized for at least this many rows per chunk */
 
@@ -89,6 +90,8 @@ typedef struct nb_mel nb_mel_t;
 nb_mel_t *nb_mel_create(void);
 void nb_mel_destroy(nb_mel_t *m);
 void nb_mel_push(nb_mel_t *m, const float *samples, size_t n, int final, const float **frames, size_t *nframes);
+size_t nb_mel_stage(nb_mel_t *m, const float *samples, size_t n, int final, float *span, size_t span_cap);
+void nb_mel_tables(const nb_mel_t *m, const float **window, const float **fb, const double **wr, const double **wi);
 size_t nb_mel_total_samples(const nb_mel_t *m);
 
 typedef struct nb_resampler nb_resampler_t;

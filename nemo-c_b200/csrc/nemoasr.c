@@ -67,6 +67,40 @@ static nb_model_t *load_model(const char *model_dir, const nemoasr_synth_spec_t 
     return m;
 }
 
+/* Feed through the GPU log-mel: every stream's samples (after resampling, `count` each) in pieces
+   whose frames fit one staged span; each piece is staged (host bookkeeping), transformed on the
+   GPU into the engine's frame queue, and stepped. Steps see final only on the last piece. */
+static int feed_gpu_mel(nb_engine_t *eng, nb_mel_t **mel, const float *const *in, size_t count, int B, int final, int *tokens, int max_tokens,
+                        int *counts, size_t *chunks, char *err, size_t errlen) {
+    const size_t piece = (size_t)(NB_SPAN_FRAMES - 3) * NB_MEL_HOP;
+    size_t *nf = malloc((size_t)B * sizeof *nf);
+    size_t off = 0;
+    int rc = 0;
+    do {
+        const size_t len = count - off < piece ? count - off : piece;
+        const int last = final && off + len >= count;
+        if (nb_engine_span_wait(eng)) { snprintf(err, errlen, "span staging: device error"); rc = -1; break; }
+#pragma omp parallel for schedule(static) if (B > 1)
+        for (int s = 0; s < B; ++s) {
+            size_t cap;
+            float *span = nb_engine_span(eng, s, &cap);
+            /* a stream that never saw a sample has no frames, not a reflected empty one */
+            nf[s] = (last && len == 0 && nb_mel_total_samples(mel[s]) == 0) ? 0 : nb_mel_stage(mel[s], in[s] + off, len, last, span, cap);
+        }
+        for (int s = 0; s < B; ++s)
+            if (nf[s] != nf[0] || nf[s] == (size_t)-1) { snprintf(err, errlen, "streams produced different frame counts (%zu vs %zu)", nf[s], nf[0]); rc = -1; break; }
+        if (rc) break;
+        if (nf[0] && nb_engine_push_spans(eng, nf[0], err, errlen)) { rc = -1; break; }
+        int r, rows;
+        while ((r = nb_engine_step(eng, last, tokens, max_tokens, counts, &rows, err, errlen)) == 1)
+            if (rows > 0) ++*chunks;
+        if (r < 0) { rc = -1; break; }
+        off += len;
+    } while (off < count);
+    free(nf);
+    return rc;
+}
+
 static nemoasr_t *open_common(nb_model_t *m, const char *language, int latency_ms, int input_rate, double t0, char *err, size_t errlen) {
     const int right = right_for(latency_ms);
     nemoasr_t *s = calloc(1, sizeof *s);
@@ -144,7 +178,12 @@ static int feed_tokens(nemoasr_t *s, const float *samples, size_t n, int final, 
     }
     s->stats.audio_seconds += (double)count / NB_MEL_SR;
     int got = 0;
-    if (!(final && count == 0 && nb_mel_total_samples(s->mel) == 0)) {
+    if (nb_engine_gpu_mel(s->eng)) {
+        size_t chunks = 0;
+        const float *ins[1] = { in };
+        if (feed_gpu_mel(s->eng, &s->mel, ins, count, 1, final, out, max, &got, &chunks, err, errlen)) return -1;
+        s->stats.chunks += chunks;
+    } else if (!(final && count == 0 && nb_mel_total_samples(s->mel) == 0)) {
         const float *frames;
         size_t nf;
         nb_mel_push(s->mel, in, count, final, &frames, &nf);
@@ -308,6 +347,8 @@ int nemoasr_batch_feed(nemoasr_batch_t *b, const float *const *samples, size_t n
         b->tmp_cap = need * 2;
         for (int s = 0; s < B; ++s) b->tmp[s] = realloc(b->tmp[s], b->tmp_cap * sizeof(float));
     }
+    const int gpu_mel = nb_engine_gpu_mel(b->eng);
+    const float **ins = calloc((size_t)B, sizeof *ins);
 #pragma omp parallel for schedule(dynamic, 4)
     for (int s = 0; s < B; ++s) {
         const float *in = samples[s];
@@ -318,10 +359,30 @@ int nemoasr_batch_feed(nemoasr_batch_t *b, const float *const *samples, size_t n
             in = b->tmp[s];
         }
         cnt[s] = c;
+        ins[s] = in;
+        if (gpu_mel) continue;
         if (final && c == 0 && nb_mel_total_samples(b->mel[s]) == 0) { nf[s] = 0; b->frames[s] = NULL; continue; }
         nb_mel_push(b->mel[s], in, c, final, &b->frames[s], &nf[s]);
     }
     int rc = 0;
+    if (gpu_mel) {
+        for (int s = 1; s < B; ++s)
+            if (cnt[s] != cnt[0]) { snprintf(err, errlen, "streams resampled to different lengths (%zu vs %zu)", cnt[s], cnt[0]); rc = -1; break; }
+        b->stats.audio_seconds += (double)cnt[0] / NB_MEL_SR * B;
+        if (!rc) rc = feed_gpu_mel(b->eng, b->mel, ins, cnt[0], B, final, tokens, max_tokens, counts, &b->stats.chunks, err, errlen);
+        free(ins);
+        free(nf);
+        free(cnt);
+        if (final) b->finished = 1;
+        for (int s = 0; s < B; ++s) b->stats.tokens += (size_t)counts[s];
+        double enc, dec;
+        size_t ch;
+        nb_engine_times(b->eng, &enc, &dec, &ch);
+        b->stats.encoder_ms = enc;
+        b->stats.decoder_ms = dec;
+        return rc;
+    }
+    free(ins);
     for (int s = 1; s < B; ++s)
         if (nf[s] != nf[0]) { snprintf(err, errlen, "streams produced different frame counts (%zu vs %zu)", nf[s], nf[0]); rc = -1; break; }
     b->stats.audio_seconds += (double)cnt[0] / NB_MEL_SR * B;
