@@ -67,5 +67,28 @@ __device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepc
 
 // host side
 extern "C" int nb_set_error(const char *fmt, ...);
+extern "C" int nb_pdl_enabled(void);
+
+namespace nb {
+// Launch with programmatic dependent launch: the grid may be scheduled while its predecessor in
+// the stream (or captured graph) drains, hiding the launch gap between dependent kernels. Every
+// kernel launched this way calls pdl_wait() before its first global memory access, so it still
+// sees all of the predecessor's writes and its writes never race the predecessor's reads.
+// NEMO_PDL=0 launches plainly.
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args &&...args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = nb_pdl_enabled() ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kernel, static_cast<Args &&>(args)...);
+}
+}  // namespace nb
 extern "C" void nb_count_launches(uint64_t n);
 int nb_check_launch(const char *what);

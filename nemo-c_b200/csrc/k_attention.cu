@@ -159,7 +159,7 @@ extern "C" int nemo_attention_rel(const float *Q, int64_t ldq, int64_t q_sstride
     if (c > MAXC || Lmax > MAXL) return nb_set_error("nemo_attention_rel: chunk of %d rows / window %d too large", c, Lmax);
     if (((uintptr_t)Q | (uintptr_t)K | (uintptr_t)V | (uintptr_t)P) & 15 || (ldq | ldk | D) & 3)
         return nb_set_error("nemo_attention_rel: rows must be 16-byte aligned");
-    attention_kernel<<<dim3(H, streams), THREADS, 0, (cudaStream_t)stream>>>(Q, ldq, q_sstride, K, V, ldk, kv_sstride, pos, cache_len, P, bias_u, bias_v,
+    nb::launch(attention_kernel, dim3(H, streams), THREADS, 0, (cudaStream_t)stream, Q, ldq, q_sstride, K, V, ldk, kv_sstride, pos, cache_len, P, bias_u, bias_v,
                                                                            O, o_fmt, o_plane, o_sstride, c, Lmax, D, scale);
     return nb_check_launch("attention_kernel");
 }

@@ -110,7 +110,7 @@ extern "C" int nemo_lstm_cell(const float *gates, const float *c_in, float *c_ou
     const int64_t total = (int64_t)rows * H;
     if (total <= 0) return 0;
     const int grid = (int)((total + 255) / 256 < 1184 ? (total + 255) / 256 : 1184);
-    lstm_cell_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(gates, c_in, c_out, h_out, rows, H);
+    nb::launch(lstm_cell_kernel, grid, 256, 0, (cudaStream_t)stream, gates, c_in, c_out, h_out, rows, H);
     return nb_check_launch("lstm_cell_kernel");
 }
 
@@ -118,7 +118,7 @@ extern "C" int nb_joint_argmax_rows(const float *enc, int64_t enc_ld, const floa
                                     const float *bias, int V, int H, int rows, const int *enc_row_of, int *out_idx, float *out_val, void *stream) {
     if (H > 1024 || (H & 3)) return nb_set_error("nemo_joint_argmax: H must be a multiple of 4 and <= 1024");
     if (rows <= 0) return 0;
-    joint_argmax_kernel<<<rows, 256, 0, (cudaStream_t)stream>>>(enc, enc_ld, pred, pred_ld, pred_rpg > 0 ? pred_rpg : 1, W, bias, V, H, enc_row_of,
+    nb::launch(joint_argmax_kernel, rows, 256, 0, (cudaStream_t)stream, enc, enc_ld, pred, pred_ld, pred_rpg > 0 ? pred_rpg : 1, W, bias, V, H, enc_row_of,
                                                                out_idx, out_val);
     return nb_check_launch("joint_argmax_kernel");
 }
@@ -135,7 +135,7 @@ extern "C" int nb_joint_argmax_gemm(const float *enc, int64_t enc_ld, const floa
                                     float *out_val, void *stream) {
     if (rows <= 0) return 0;
     cudaStream_t st = (cudaStream_t)stream;
-    joint_input_kernel<<<rows, 128, 0, st>>>(enc, enc_ld, pred, pred_ld, enc_row_of, X, (int64_t)rows * H, H);
+    nb::launch(joint_input_kernel, rows, 128, 0, st, enc, enc_ld, pred, pred_ld, enc_row_of, X, (int64_t)rows * H, H);
     if (nb_check_launch("joint_input_kernel")) return -1;
     nemo_gemm_args_t a = {};
     a.A = X; a.lda = H; a.a_fmt = NEMO_FMT_BF16X2; a.a_plane = (int64_t)rows * H;
@@ -143,6 +143,6 @@ extern "C" int nb_joint_argmax_gemm(const float *enc, int64_t enc_ld, const floa
     a.C = logits; a.ldc = ldl; a.c_fmt = NEMO_FMT_F32;
     a.M = rows; a.N = V; a.K = H; a.alpha = 1.0f;
     if (nemo_gemm(&a, stream)) return -1;
-    row_argmax_kernel<<<(rows + 7) / 8, 256, 0, st>>>(logits, ldl, V, enc_row_of, rows, out_idx, out_val);
+    nb::launch(row_argmax_kernel, (rows + 7) / 8, 256, 0, st, logits, ldl, V, enc_row_of, rows, out_idx, out_val);
     return nb_check_launch("row_argmax_kernel");
 }

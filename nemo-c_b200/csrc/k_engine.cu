@@ -11,6 +11,7 @@ namespace {
 // Source and destination never overlap (cap_rows >= 2 * att_left + cmax).
 __global__ void compact_kernel(float *kv, float *din, int layers, int streams, int64_t cap, int D, int src_kv, int cache_len, int src_din,
                                int dst_din, int conv_left) {
+    nb::pdl_wait();
     const int64_t kv_row = 3LL * D, per_kv = (int64_t)cache_len * kv_row, per_din = (int64_t)conv_left * D;
     const int64_t total = (int64_t)layers * streams * (per_kv + per_din);
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
@@ -27,6 +28,7 @@ __global__ void compact_kernel(float *kv, float *din, int layers, int streams, i
 }
 
 __global__ void dec_chunk_init_kernel(DecState d, int streams, int c) {
+    nb::pdl_wait();
     const int b = blockIdx.x * blockDim.x + threadIdx.x;
     if (b == 0) { d.cnt[2] = 0; d.cnt[3] = 0; } // iterations run, blocks of dec_update done
     if (b >= streams) return;
@@ -39,6 +41,7 @@ __global__ void dec_chunk_init_kernel(DecState d, int streams, int c) {
 // Streams that still have frames and whose prediction vector is stale get the prediction
 // network this iteration (src/decoder.c:101); every active stream scores its current frame.
 __global__ void dec_plan_kernel(DecState d, int streams, int c) {
+    nb::pdl_wait();
     __shared__ int n_need;
     if (threadIdx.x == 0) n_need = 0;
     __syncthreads();
@@ -59,6 +62,7 @@ __global__ void dec_plan_kernel(DecState d, int streams, int c) {
 // Prediction-network input for each listed stream: [embed(last token) (zeros for blank) | h0]
 // for layer 0 and [. | h1] for layer 1 (src/decoder.c:61-70).
 __global__ void dec_gather_kernel(DecState d, const uint16_t *__restrict__ embed, int PH, int blank) {
+    nb::pdl_wait();
     const int i = blockIdx.x;
     if (i >= d.cnt[0]) return;
     const int b = d.need_idx[i];
@@ -75,6 +79,7 @@ __global__ void dec_gather_kernel(DecState d, const uint16_t *__restrict__ embed
 // LSTM cell (src/kernels.metal:475-486) from the committed cell state into the provisional
 // state of each listed stream; h' also goes to `next` (the following GEMM's input row).
 __global__ void dec_cell_kernel(DecState d, int layer, int PH, float *next, int64_t next_ld, int64_t next_plane) {
+    nb::pdl_wait();
     const int i = blockIdx.x;
     if (i >= d.cnt[0]) return;
     const int b = d.need_idx[i];
@@ -91,6 +96,7 @@ __global__ void dec_cell_kernel(DecState d, int layer, int PH, float *next, int6
 }
 
 __global__ void dec_scatter_pred_kernel(DecState d, int JH) {
+    nb::pdl_wait();
     const int i = blockIdx.x;
     if (i >= d.cnt[0]) return;
     const int b = d.need_idx[i];
@@ -108,6 +114,7 @@ __global__ void dec_scatter_pred_kernel(DecState d, int JH) {
 // src/kernels.metal:521-550), taken here by warp 0; without, it was left in d.idx.
 __global__ void dec_update_kernel(DecState d, int c, int PH, int blank, int max_symbols, int max_it, cudaGraphConditionalHandle cond,
                                   const float *__restrict__ logits, int64_t ldl, int V) {
+    nb::pdl_wait();
     __shared__ int s_k;
     const int b = blockIdx.x;
     const bool live = d.active[b];
@@ -178,6 +185,7 @@ __global__ void dec_update_kernel(DecState d, int c, int PH, int blank, int max_
 }
 
 __global__ void dec_joint_in_kernel(DecState d, const float *__restrict__ enc, int JH, uint16_t *X, int64_t plane) {
+    nb::pdl_wait();
     const int b = blockIdx.x;
     const int er = d.erow[b], pos = d.need_pos[b];
     const float *p = pos >= 0 ? d.predc + (int64_t)pos * JH : d.pred + (int64_t)b * JH;
@@ -191,6 +199,7 @@ __global__ void dec_joint_in_kernel(DecState d, const float *__restrict__ enc, i
 }
 
 __global__ void dec_reset_kernel(DecState d, int PH, int blank) {
+    nb::pdl_wait();
     const int b = blockIdx.x;
     for (int l = 0; l < 2; ++l) {
         const int64_t sb = ((int64_t)l * d.streams + b) * PH;
@@ -203,40 +212,40 @@ __global__ void dec_reset_kernel(DecState d, int PH, int blank) {
 
 extern "C" int nb_compact(float *kv, float *din, int layers, int streams, int64_t cap, int D, int src_kv, int cache_len, int src_din, int dst_din,
                           int conv_left, void *stream) {
-    compact_kernel<<<148 * 8, 256, 0, (cudaStream_t)stream>>>(kv, din, layers, streams, cap, D, src_kv, cache_len, src_din, dst_din, conv_left);
+    nb::launch(compact_kernel, 148 * 8, 256, 0, (cudaStream_t)stream, kv, din, layers, streams, cap, D, src_kv, cache_len, src_din, dst_din, conv_left);
     return nb_check_launch("compact_kernel");
 }
 extern "C" int nb_dec_chunk_init(const DecState *d, int c, void *stream) {
-    dec_chunk_init_kernel<<<(d->streams + 255) / 256, 256, 0, (cudaStream_t)stream>>>(*d, d->streams, c);
+    nb::launch(dec_chunk_init_kernel, (d->streams + 255) / 256, 256, 0, (cudaStream_t)stream, *d, d->streams, c);
     return nb_check_launch("dec_chunk_init_kernel");
 }
 extern "C" int nb_dec_plan(const DecState *d, int c, void *stream) {
-    dec_plan_kernel<<<1, 1024, 0, (cudaStream_t)stream>>>(*d, d->streams, c);
+    nb::launch(dec_plan_kernel, 1, 1024, 0, (cudaStream_t)stream, *d, d->streams, c);
     return nb_check_launch("dec_plan_kernel");
 }
 extern "C" int nb_dec_gather(const DecState *d, const uint16_t *embed, int PH, int blank, void *stream) {
-    dec_gather_kernel<<<d->streams, 128, 0, (cudaStream_t)stream>>>(*d, embed, PH, blank);
+    nb::launch(dec_gather_kernel, d->streams, 128, 0, (cudaStream_t)stream, *d, embed, PH, blank);
     return nb_check_launch("dec_gather_kernel");
 }
 extern "C" int nb_dec_cell(const DecState *d, int layer, int PH, float *next, int64_t next_ld, int64_t next_plane, void *stream) {
-    dec_cell_kernel<<<d->streams, 128, 0, (cudaStream_t)stream>>>(*d, layer, PH, next, next_ld, next_plane);
+    nb::launch(dec_cell_kernel, d->streams, 128, 0, (cudaStream_t)stream, *d, layer, PH, next, next_ld, next_plane);
     return nb_check_launch("dec_cell_kernel");
 }
 extern "C" int nb_dec_scatter_pred(const DecState *d, int JH, void *stream) {
-    dec_scatter_pred_kernel<<<d->streams, 128, 0, (cudaStream_t)stream>>>(*d, JH);
+    nb::launch(dec_scatter_pred_kernel, d->streams, 128, 0, (cudaStream_t)stream, *d, JH);
     return nb_check_launch("dec_scatter_pred_kernel");
 }
 extern "C" int nb_dec_update(const DecState *d, int c, int PH, int blank, int max_symbols, int max_it, unsigned long long cond, const float *logits,
                              int64_t ldl, int V, void *stream) {
-    dec_update_kernel<<<d->streams, 128, 0, (cudaStream_t)stream>>>(*d, c, PH, blank, max_symbols, max_it, (cudaGraphConditionalHandle)cond, logits,
+    nb::launch(dec_update_kernel, d->streams, 128, 0, (cudaStream_t)stream, *d, c, PH, blank, max_symbols, max_it, (cudaGraphConditionalHandle)cond, logits,
                                                                    ldl, V);
     return nb_check_launch("dec_update_kernel");
 }
 extern "C" int nb_dec_joint_in(const DecState *d, const float *enc, int JH, uint16_t *X, int64_t plane, void *stream) {
-    dec_joint_in_kernel<<<d->streams, 128, 0, (cudaStream_t)stream>>>(*d, enc, JH, X, plane);
+    nb::launch(dec_joint_in_kernel, d->streams, 128, 0, (cudaStream_t)stream, *d, enc, JH, X, plane);
     return nb_check_launch("dec_joint_in_kernel");
 }
 extern "C" int nb_dec_reset(const DecState *d, int PH, int blank, void *stream) {
-    dec_reset_kernel<<<d->streams, 128, 0, (cudaStream_t)stream>>>(*d, PH, blank);
+    nb::launch(dec_reset_kernel, d->streams, 128, 0, (cudaStream_t)stream, *d, PH, blank);
     return nb_check_launch("dec_reset_kernel");
 }

@@ -134,18 +134,18 @@ static int launch_ws(const nemo_gemm_args_t *a, cudaStream_t st) {
     const dim3 grid((nout + 7) / 8);
     const Epi e = make_epi(a);
     const float *A = (const float *)a->A;
-    if (a->M <= 1) gemm_ws_kernel<1><<<grid, 256, 0, st>>>(A, a->lda, a->W, a->ldw, a->M, a->dynM, a->N, a->K, a->rowoff, e);
-    else if (a->M <= 2) gemm_ws_kernel<2><<<grid, 256, 0, st>>>(A, a->lda, a->W, a->ldw, a->M, a->dynM, a->N, a->K, a->rowoff, e);
-    else if (a->M <= 4) gemm_ws_kernel<4><<<grid, 256, 0, st>>>(A, a->lda, a->W, a->ldw, a->M, a->dynM, a->N, a->K, a->rowoff, e);
-    else if (a->M <= 8) gemm_ws_kernel<8><<<grid, 256, 0, st>>>(A, a->lda, a->W, a->ldw, a->M, a->dynM, a->N, a->K, a->rowoff, e);
-    else gemm_ws_kernel<16><<<grid, 256, 0, st>>>(A, a->lda, a->W, a->ldw, a->M, a->dynM, a->N, a->K, a->rowoff, e);
+    if (a->M <= 1) nb::launch(gemm_ws_kernel<1>, grid, 256, 0, st, A, a->lda, a->W, a->ldw, a->M, a->dynM, a->N, a->K, a->rowoff, e);
+    else if (a->M <= 2) nb::launch(gemm_ws_kernel<2>, grid, 256, 0, st, A, a->lda, a->W, a->ldw, a->M, a->dynM, a->N, a->K, a->rowoff, e);
+    else if (a->M <= 4) nb::launch(gemm_ws_kernel<4>, grid, 256, 0, st, A, a->lda, a->W, a->ldw, a->M, a->dynM, a->N, a->K, a->rowoff, e);
+    else if (a->M <= 8) nb::launch(gemm_ws_kernel<8>, grid, 256, 0, st, A, a->lda, a->W, a->ldw, a->M, a->dynM, a->N, a->K, a->rowoff, e);
+    else nb::launch(gemm_ws_kernel<16>, grid, 256, 0, st, A, a->lda, a->W, a->ldw, a->M, a->dynM, a->N, a->K, a->rowoff, e);
     return nb_check_launch("gemm_ws_kernel");
 }
 
 static int launch_tiled(const nemo_gemm_args_t *a, cudaStream_t st) {
     const int nout = a->act == NEMO_ACT_GLU ? a->N / 2 : a->N;
     const dim3 grid((nout + 63) / 64, (a->M + 63) / 64);
-    gemm_tiled_kernel<<<grid, 256, 0, st>>>((const float *)a->A, a->lda, a->W, a->ldw, a->M, a->dynM, a->N, a->K, a->rowoff, make_epi(a));
+    nb::launch(gemm_tiled_kernel, grid, 256, 0, st, (const float *)a->A, a->lda, a->W, a->ldw, a->M, a->dynM, a->N, a->K, a->rowoff, make_epi(a));
     return nb_check_launch("gemm_tiled_kernel");
 }
 

@@ -697,7 +697,7 @@ int launch(const nemo_gemm_args_t *a, cudaStream_t st) {
     p.ws = g_ws;
     p.counters = g_counters;
     const int grid = p.units < g_sms ? p.units : g_sms;
-    gemm_tc_kernel<BN><<<grid, THREADS, Cfg<BN>::SMEM, st>>>(mw, mh, ml, p);
+    nb::launch(gemm_tc_kernel<BN>, grid, THREADS, Cfg<BN>::SMEM, st, mw, mh, ml, p);
     return nb_check_launch("gemm_tc_kernel");
 }
 
@@ -771,7 +771,7 @@ int launch_r(const nemo_gemm_args_t *a, const PlanR &pl, cudaStream_t st) {
     p.counters = g_counters;
     p.vec = vec_ok(a);
     const int grid = p.units < g_sms ? p.units : g_sms;
-    gemm_tcr_kernel<BW><<<grid, THREADS, CfgR<BW>::SMEM, st>>>(mw, mh, ml, p);
+    nb::launch(gemm_tcr_kernel<BW>, grid, THREADS, CfgR<BW>::SMEM, st, mw, mh, ml, p);
     return nb_check_launch("gemm_tcr_kernel");
 }
 
@@ -929,7 +929,7 @@ int na_launch(const nemo_gemm_args_t *a, cudaStream_t st, unsigned char *scratch
     if (p.splits > 1 && cudaMemsetAsync(p.counters, 0, (size_t)tiles * sizeof(int), st) != cudaSuccess)
         return nb_set_error("nemo_gemm_noalloc: cannot clear the arrival counters");
     const int grid = p.units < sms ? p.units : sms;
-    gemm_tc_kernel<BN><<<grid, THREADS, Cfg<BN>::SMEM, st>>>(mw, mh, ml, p);
+    nb::launch(gemm_tc_kernel<BN>, grid, THREADS, Cfg<BN>::SMEM, st, mw, mh, ml, p);
     return nb_check_launch("gemm_tc_kernel");
 }
 

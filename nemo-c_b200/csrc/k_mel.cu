@@ -102,7 +102,7 @@ extern "C" int nb_logmel_frames(const float *span, int64_t span_stride, int stre
     if (nframes <= 0 || streams <= 0) return 0;
     Tables *T;
     if (tables(&T)) return -1;
-    logmel_kernel<<<dim3(nframes, streams), THREADS, 0, (cudaStream_t)stream>>>(span, span_stride, T->window, T->fb, T->rng, T->wr, T->wi, out, out_stride,
+    nb::launch(logmel_kernel, dim3(nframes, streams), THREADS, 0, (cudaStream_t)stream, span, span_stride, T->window, T->fb, T->rng, T->wr, T->wi, out, out_stride,
                                                                                out_row0);
     return nb_check_launch("logmel_kernel");
 }

@@ -405,11 +405,11 @@ extern "C" int nemo_layernorm(const float *X, const float *g, const float *b, vo
     if (D > LNT * LN_MAXV) return nb_set_error("nemo_layernorm: D=%d too large", D);
     if (M <= 0) return 0;
     if (warp_rows_ok(X, Y, y_fmt, y_plane, D)) {
-        layernorm_warp_kernel<<<(M + WROWS - 1) / WROWS, WROWS * 32, 0, (cudaStream_t)stream>>>(X, g, b, nullptr, nullptr, nullptr, Y, y_fmt, y_plane, M, D,
+        nb::launch(layernorm_warp_kernel, (M + WROWS - 1) / WROWS, WROWS * 32, 0, (cudaStream_t)stream, X, g, b, nullptr, nullptr, nullptr, Y, y_fmt, y_plane, M, D,
                                                                                               eps);
         return nb_check_launch("layernorm_warp_kernel");
     }
-    layernorm_kernel<<<M, LNT, 0, (cudaStream_t)stream>>>(X, g, b, Y, y_fmt, y_plane, D, eps);
+    nb::launch(layernorm_kernel, M, LNT, 0, (cudaStream_t)stream, X, g, b, Y, y_fmt, y_plane, D, eps);
     return nb_check_launch("layernorm_kernel");
 }
 
@@ -418,10 +418,10 @@ extern "C" int nemo_layernorm2(const float *X, const float *g1, const float *b1,
     if (D > LNT * LN_MAXV) return nb_set_error("nemo_layernorm2: D=%d too large", D);
     if (M <= 0) return 0;
     if (warp_rows_ok(X, Y2, y2_fmt, y2_plane, D) && !((uintptr_t)Y1 & 15)) {
-        layernorm_warp_kernel<<<(M + WROWS - 1) / WROWS, WROWS * 32, 0, (cudaStream_t)stream>>>(X, g1, b1, g2, b2, Y1, Y2, y2_fmt, y2_plane, M, D, eps);
+        nb::launch(layernorm_warp_kernel, (M + WROWS - 1) / WROWS, WROWS * 32, 0, (cudaStream_t)stream, X, g1, b1, g2, b2, Y1, Y2, y2_fmt, y2_plane, M, D, eps);
         return nb_check_launch("layernorm_warp_kernel");
     }
-    layernorm2_kernel<<<M, LNT, 0, (cudaStream_t)stream>>>(X, g1, b1, g2, b2, Y1, Y2, y2_fmt, y2_plane, D, eps);
+    nb::launch(layernorm2_kernel, M, LNT, 0, (cudaStream_t)stream, X, g1, b1, g2, b2, Y1, Y2, y2_fmt, y2_plane, D, eps);
     return nb_check_launch("layernorm2_kernel");
 }
 
@@ -431,11 +431,11 @@ extern "C" int nemo_dwconv_ln_silu(const float *din, int64_t din_sstride, const 
     if (streams <= 0 || c <= 0) return 0;
     if (warp_rows_ok(din, Y, y_fmt, y_plane, D) && din_sstride % 4 == 0 && !((uintptr_t)W & 15)) {
         const int items = streams * c;
-        dwconv_ln_silu_warp_kernel<<<(items + WROWS - 1) / WROWS, WROWS * 32, 0, (cudaStream_t)stream>>>(din, din_sstride, pos, W, g, b, Y, y_fmt, y_plane,
+        nb::launch(dwconv_ln_silu_warp_kernel, (items + WROWS - 1) / WROWS, WROWS * 32, 0, (cudaStream_t)stream, din, din_sstride, pos, W, g, b, Y, y_fmt, y_plane,
                                                                                                        streams, c, D, taps, eps);
         return nb_check_launch("dwconv_ln_silu_warp_kernel");
     }
-    dwconv_ln_silu_kernel<<<dim3(c, streams), LNT, 0, (cudaStream_t)stream>>>(din, din_sstride, pos, W, g, b, Y, y_fmt, y_plane, c, D, taps, eps);
+    nb::launch(dwconv_ln_silu_kernel, dim3(c, streams), LNT, 0, (cudaStream_t)stream, din, din_sstride, pos, W, g, b, Y, y_fmt, y_plane, c, D, taps, eps);
     return nb_check_launch("dwconv_ln_silu_kernel");
 }
 
@@ -443,7 +443,7 @@ extern "C" int nemo_conv2d_c1_s2_relu(const float *X, int64_t x_sstride, const f
                                       int T1, int F1, int C, void *stream) {
     const int64_t total = (int64_t)streams * T1 * F1 * C;
     if (total <= 0) return 0;
-    conv2d_c1_s2_relu_kernel<<<grid_for(total), 256, 0, (cudaStream_t)stream>>>(X, x_sstride, W, bias, Y, T, F, T1, F1, C, total);
+    nb::launch(conv2d_c1_s2_relu_kernel, grid_for(total), 256, 0, (cudaStream_t)stream, X, x_sstride, W, bias, Y, T, F, T1, F1, C, total);
     return nb_check_launch("conv2d_c1_s2_relu_kernel");
 }
 
@@ -451,7 +451,7 @@ extern "C" int nb_dwconv2d_s2_fmt(const float *X, const float *W, const float *b
                                   int T1, int F1, int C, void *stream) {
     const int64_t total = (int64_t)streams * T1 * F1 * C;
     if (total <= 0) return 0;
-    dwconv2d_s2_kernel<<<grid_for(total), 256, 0, (cudaStream_t)stream>>>(X, W, bias, Y, y_fmt, y_plane, T, F, T1, F1, C, total);
+    nb::launch(dwconv2d_s2_kernel, grid_for(total), 256, 0, (cudaStream_t)stream, X, W, bias, Y, y_fmt, y_plane, T, F, T1, F1, C, total);
     return nb_check_launch("dwconv2d_s2_kernel");
 }
 
@@ -465,11 +465,11 @@ extern "C" int nemo_subsample_front(const float *X, int64_t x_sstride, const flo
     const int64_t positions = (int64_t)streams * T2 * F2;
     if (positions <= 0) return 0;
     if (C % 256 == 0) {
-        subsample_front_lanes_kernel<<<(unsigned)((positions + 31) / 32), 256, 0, (cudaStream_t)stream>>>(X, x_sstride, W0, b0, W2, b2, Y, y_fmt, y_plane, T,
+        nb::launch(subsample_front_lanes_kernel, (unsigned)((positions + 31) / 32), 256, 0, (cudaStream_t)stream, X, x_sstride, W0, b0, W2, b2, Y, y_fmt, y_plane, T,
                                                                                                         F, T1, F1, T2, F2, C, positions);
         return nb_check_launch("subsample_front_lanes_kernel");
     }
-    subsample_front_kernel<<<(unsigned)((positions + 7) / 8), 256, 0, (cudaStream_t)stream>>>(X, x_sstride, W0, b0, W2, b2, Y, y_fmt, y_plane, T, F, T1,
+    nb::launch(subsample_front_kernel, (unsigned)((positions + 7) / 8), 256, 0, (cudaStream_t)stream, X, x_sstride, W0, b0, W2, b2, Y, y_fmt, y_plane, T, F, T1,
                                                                                               F1, T2, F2, C, positions);
     return nb_check_launch("subsample_front_kernel");
 }
@@ -477,7 +477,7 @@ extern "C" int nemo_subsample_front(const float *X, int64_t x_sstride, const flo
 extern "C" int nb_flatten_rows_fmt(const float *X, void *Y, int y_fmt, int64_t y_plane, const int *lo, int streams, int T, int F, int C, int c, void *stream) {
     const int64_t total = (int64_t)streams * c * C * F;
     if (total <= 0) return 0;
-    flatten_rows_kernel<<<grid_for(total), 256, 0, (cudaStream_t)stream>>>(X, Y, y_fmt, y_plane, lo, T, F, C, c, total);
+    nb::launch(flatten_rows_kernel, grid_for(total), 256, 0, (cudaStream_t)stream, X, Y, y_fmt, y_plane, lo, T, F, C, c, total);
     return nb_check_launch("flatten_rows_kernel");
 }
 

@@ -23,6 +23,15 @@ static thread_local int g_counting = 1;
 // engine turns counting off and adds the graph's kernel nodes each time it launches the graph.
 extern "C" void nb_set_launch_counting(int on) { g_counting = on; }
 
+extern "C" int nb_pdl_enabled(void) {
+    static int on = -1;
+    if (on < 0) {
+        const char *v = getenv("NEMO_PDL");
+        on = !(v && !strcmp(v, "0"));
+    }
+    return on;
+}
+
 int nb_check_launch(const char *what) {
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return nb_set_error("%s: %s", what, cudaGetErrorString(e));
