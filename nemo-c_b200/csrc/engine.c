@@ -67,6 +67,12 @@ struct nb_engine {
     float *d_dec1;             /* H0 [2][PH] | H1 [2][PH] | PRED [JH] | part_v [grid][16] */
     int *d_dec1_i;             /* part_i [grid][16] | err */
     unsigned *d_dec1_bar;
+    /* several streams: the greedy loop as four tensor-core GEMMs with decoder epilogues and one
+       step kernel per iteration (NEMO_DEC_FUSED=0 keeps the kernel-by-kernel iteration) */
+    int dec_fused;
+    uint16_t *dec_w0i, *dec_w1i; /* gate-interleaved LSTM layers [4PH][2PH] */
+    float *dec_b0i, *dec_b1i;    /* their biases, interleaved alike */
+    float *dec_table;            /* [vocab + 1][4PH]: b0 + W0x . embed[v] */
     unsigned *d_enc1_bar;
     int *d_enc1_err;
     struct { int kind, k1, k2; cudaGraphExec_t exec; uint64_t kernels; } graphs[NB_MAX_GRAPHS];
@@ -131,6 +137,33 @@ static int enc1_setup(nb_engine_t *e, char *err, size_t errlen) {
     e->use_enc1 = 1;
     e->enc1_grid = sms;
     e->enc1_slot = slot;
+    return 0;
+}
+
+/* Several streams with bf16 hi/lo activations: gate-interleaved LSTM weights and the per-token
+   gate table of layer 0 for the fused greedy iteration. */
+static int dec_fused_setup(nb_engine_t *e, char *err, size_t errlen) {
+    const char *ev = getenv("NEMO_DEC_FUSED");
+    if (ev && !strcmp(ev, "0")) return 0;
+    const nb_model_t *m = e->m;
+    const nb_config_t *g = &m->g;
+    const size_t PH = (size_t)g->pred_hidden, NV = (size_t)g->vocab_size + 1;
+    if (g->pred_layers != 2 || PH % 16 || g->joint_hidden % 16 || g->num_classes > (int)NV || g->blank_id < 0 || g->blank_id >= (int)NV) return 0;
+    int fail = 0;
+    e->dec_w0i = dalloc(4 * PH * 2 * PH * 2, &fail);
+    e->dec_w1i = dalloc(4 * PH * 2 * PH * 2, &fail);
+    e->dec_b0i = dalloc(4 * PH * 4, &fail);
+    e->dec_b1i = dalloc(4 * PH * 4, &fail);
+    e->dec_table = dalloc(NV * 4 * PH * 4, &fail);
+    if (fail) { snprintf(err, errlen, "out of device memory for the decoder tables"); return -1; }
+    if (nb_dec_interleave(m->lstm_w[0], e->dec_w0i, m->lstm_b[0], e->dec_b0i, (int)PH, (int)(2 * PH), e->st) ||
+        nb_dec_interleave(m->lstm_w[1], e->dec_w1i, m->lstm_b[1], e->dec_b1i, (int)PH, (int)(2 * PH), e->st) ||
+        nb_dec_gate_table(e->dec_w0i, (int64_t)(2 * PH), m->embed, (int)NV, (int)PH, e->dec_b0i, g->blank_id, e->dec_table, e->st) ||
+        cudaStreamSynchronize(e->st) != cudaSuccess) {
+        snprintf(err, errlen, "decoder tables: %s", nemo_gpu_last_error());
+        return -1;
+    }
+    e->dec_fused = 1;
     return 0;
 }
 
@@ -268,6 +301,7 @@ nb_engine_t *nb_engine_create(nb_model_t *m, int B, int right, char *err, size_t
     }
     if (B == 1 && fmt == NEMO_FMT_BF16X2 && enc1_setup(e, err, errlen)) goto fail;
     if (B == 1 && dec1_setup(e, err, errlen)) goto fail;
+    if (B > 1 && fmt == NEMO_FMT_BF16X2 && dec_fused_setup(e, err, errlen)) goto fail;
     if (nb_engine_reset(e, err, errlen)) goto fail;
     return e;
 fail:
@@ -298,6 +332,8 @@ void nb_engine_destroy(nb_engine_t *e) {
     if (e->ev1) cudaEventDestroy(e->ev1);
     for (int i = 0; i < e->ngraphs; ++i) cudaGraphExecDestroy(e->graphs[i].exec);
     free(e->enc1_layers);
+    void *dt[] = { e->dec_w0i, e->dec_w1i, e->dec_b0i, e->dec_b1i, e->dec_table };
+    for (size_t i = 0; i < sizeof dt / sizeof *dt; ++i) if (dt[i]) cudaFree(dt[i]);
     if (e->h_span) cudaFreeHost(e->h_span);
     if (e->d_span) cudaFree(e->d_span);
     if (e->d_melq) cudaFree(e->d_melq);
@@ -552,6 +588,64 @@ static int dec_max_iterations(const nb_engine_t *e, int c) { return c * (e->m->g
 /* One greedy iteration over all streams (src/decoder.c:97-123). cond is the WHILE-loop handle
    when the iteration is the body of the decoder graph (the device decides whether it repeats),
    0 when the host drives the loop (the active count is then copied back each iteration). */
+static NbDecStep dec_step_args(const nb_engine_t *e) {
+    const nb_config_t *g = &e->m->g;
+    const DecState *d = &e->dec;
+    NbDecStep s;
+    memset(&s, 0, sizeof s);
+    s.logits = d->logits; s.ldl = logits_ld(g); s.V = g->num_classes; s.blank = g->blank_id; s.max_symbols = g->max_symbols;
+    s.PH = g->pred_hidden; s.JH = g->joint_hidden; s.enc = e->joint_enc;
+    s.A0 = (uint16_t *)d->A0; s.a0_ld = g->pred_hidden; s.a0_plane = d->a_plane;
+    s.A1 = (uint16_t *)d->A1; s.a1_ld = 2 * g->pred_hidden; s.a1_plane = d->a_plane;
+    s.X = d->jx; s.x_plane = (int64_t)e->B * g->joint_hidden;
+    return s;
+}
+
+/* One fused greedy iteration (see NbDecEpi): four GEMMs with decoder epilogues and the step. */
+static int dec_fused_body(nb_engine_t *e, int c, unsigned long long cond) {
+    const nb_model_t *m = e->m;
+    const nb_config_t *g = &m->g;
+    const int B = e->B, PH = g->pred_hidden, JH = g->joint_hidden;
+    DecState *d = &e->dec;
+    cudaStream_t st = e->st;
+    char err[8];
+    const size_t errlen = 0;
+    (void)err; (void)errlen;
+    const NbDecStep s = dec_step_args(e);
+    NbDecEpi de;
+    memset(&de, 0, sizeof de);
+    de.mode = 1;
+    de.need_idx = d->need_idx;
+    de.last_token = d->last_token;
+    de.table = e->dec_table;
+    de.c_in = d->c; de.c_out = d->cp; de.h_out = d->hp;
+    de.next = (uint16_t *)d->A1; de.next_ld = 2 * PH; de.next_plane = d->a_plane;
+    nemo_gemm_args_t a = gemm_args(d->A0, PH, NEMO_FMT_BF16X2, d->a_plane, e->dec_w0i + PH, 2 * PH, NULL, NULL, 0, B, 4 * PH, PH, 0, 0, 1.0f);
+    a.dynM = d->cnt;
+    KL(nb_gemm_dec(&a, &de, st));
+    const int64_t l1 = (int64_t)B * PH;
+    de.last_token = NULL; de.table = NULL;
+    de.c_in = d->c + l1; de.c_out = d->cp + l1; de.h_out = d->hp + l1;
+    de.next = (uint16_t *)d->hp1c; de.next_ld = PH; de.next_plane = d->h_plane;
+    a = gemm_args(d->A1, 2 * PH, NEMO_FMT_BF16X2, d->a_plane, e->dec_w1i, 2 * PH, e->dec_b1i, NULL, 0, B, 4 * PH, 2 * PH, 0, 0, 1.0f);
+    a.dynM = d->cnt;
+    KL(nb_gemm_dec(&a, &de, st));
+    NbDecEpi dp;
+    memset(&dp, 0, sizeof dp);
+    dp.mode = 2;
+    dp.need_idx = d->need_idx; dp.enc = e->joint_enc; dp.erow = d->erow; dp.pred = d->pred; dp.X = d->jx; dp.x_plane = s.x_plane;
+    a = gemm_args(d->hp1c, PH, NEMO_FMT_BF16X2, d->h_plane, m->joint_pred_w, PH, m->joint_pred_b, NULL, 0, B, JH, PH, 0, 0, 1.0f);
+    a.dynM = d->cnt;
+    KL(nb_gemm_dec(&a, &dp, st));
+    nemo_gemm_args_t j = gemm_args(d->jx, JH, NEMO_FMT_BF16X2, s.x_plane, m->joint_out_w, JH, m->joint_out_b, d->logits, logits_ld(g), B,
+                                   g->num_classes, JH, 0, 0, 1.0f);
+    KL(nemo_gemm(&j, st));
+    KL(nb_dec_step(d, &s, c, dec_max_iterations(e, c), cond, st));
+    if (!cond && cudaMemcpyAsync(e->h_cnt, d->cnt, 2 * sizeof(int), cudaMemcpyDeviceToHost, st) != cudaSuccess)
+        return nb_set_error("decoder: %s", cudaGetErrorString(cudaGetLastError()));
+    return 0;
+}
+
 static int dec_iteration_body(nb_engine_t *e, int c, unsigned long long cond) {
     const nb_model_t *m = e->m;
     const nb_config_t *g = &m->g;
@@ -561,6 +655,7 @@ static int dec_iteration_body(nb_engine_t *e, int c, unsigned long long cond) {
     char err[8];
     const size_t errlen = 0;
     (void)err; (void)errlen;
+    if (e->dec_fused) return dec_fused_body(e, c, cond);
     {
         KL(nb_dec_plan(d, c, st));
         KL(nb_dec_gather(d, m->embed, PH, g->blank_id, st));
@@ -713,7 +808,12 @@ static int run_decoder(nb_engine_t *e, int c, char *err, size_t errlen) {
         if (c > 0 && e->h_cnt[1] != 0) { snprintf(err, errlen, "decoder did not finish the chunk in %d iterations", max_it); return -1; }
         return 0;
     }
-    KL(nb_dec_chunk_init(d, c, st));
+    if (e->dec_fused) {
+        const NbDecStep s = dec_step_args(e);
+        KL(nb_dec_chunk_start(d, &s, c, st));
+    } else {
+        KL(nb_dec_chunk_init(d, c, st));
+    }
     (void)g;
     if (e->use_graphs) {
         const int slot = dec_graph(e, c);

@@ -4,6 +4,7 @@
 #define NB_ENGINE_DEV_H
 #include <stddef.h>
 #include <stdint.h>
+#include "../../include/nemo_gpu.h"
 
 #ifdef __cplusplus
 extern "C" {
@@ -94,6 +95,56 @@ int nb_dec_update(const DecState *d, int c, int PH, int blank, int max_symbols, 
    stored as its prediction) or its kept prediction. */
 int nb_dec_joint_in(const DecState *d, const float *enc, int JH, uint16_t *X, int64_t plane, void *stream);
 int nb_dec_reset(const DecState *d, int PH, int blank, void *stream);
+
+/* ---- fused batched greedy decoder (activation-major tensor-core GEMMs with decoder epilogues) --
+   One iteration is four GEMMs and one step kernel:
+     gates0 = table[last_token] + W0h . h0   -> LSTM cell 0 in the epilogue -> A1[:, 0:PH)
+     gates1 = b1 + W1 . [h0' | h1]           -> LSTM cell 1 in the epilogue -> hp1c
+     pred   = bp + Wp . h1'                  -> pred[b], X[b] = relu(enc[erow[b]] + pred) in the epilogue
+     logits = bo + Wo . X                    -> the step kernel: argmax, commit, next iteration's rows
+   The LSTM weights are gate-interleaved (row 4u + g holds gate g of unit u, gates i, f, g, o), so
+   each 16-column epilogue chunk holds all four gates of 4 units. table[v] = b0 + W0x . embed[v]
+   (the input half of layer 0 for every token; the blank row is b0 alone, blank feeding zeros). */
+typedef struct {
+    int mode;                 /* 1: LSTM cell; 2: prediction + joint input */
+    const int *need_idx;      /* GEMM row -> stream */
+    const int *last_token;    /* mode 1 with a table: row of the table each stream adds */
+    const float *table;       /* mode 1: [V][4PH] per-token gate rows used instead of the bias, or NULL */
+    const float *c_in;        /* mode 1: [streams][PH] committed cell state of the layer */
+    float *c_out, *h_out;     /* mode 1: [streams][PH] provisional state of the layer */
+    uint16_t *next;           /* mode 1: next GEMM input, row m, columns [0, PH), bf16 hi/lo planes */
+    int64_t next_ld, next_plane;
+    const float *enc;         /* mode 2: [rows][N] joint encoder rows; erow[b] selects the row */
+    const int *erow;
+    float *pred;              /* mode 2: [streams][N] */
+    uint16_t *X;              /* mode 2: [streams][N] joint input, bf16 hi/lo planes */
+    int64_t x_plane;
+} NbDecEpi;
+
+/* Tensor-core GEMM (activation-major tiles) with a decoder epilogue instead of the plain one. */
+int nb_gemm_dec(const nemo_gemm_args_t *a, const NbDecEpi *de, void *stream);
+
+typedef struct {
+    const float *logits;      /* [streams][ldl] */
+    int64_t ldl;
+    int V, blank, max_symbols, PH, JH;
+    const float *enc;         /* [streams * c][JH] joint encoder rows of the chunk */
+    uint16_t *A0, *A1, *X;    /* next iteration's inputs: h0 rows [.][a0_ld], h1 at A1[., PH..2PH), joint input rows */
+    int64_t a0_ld, a0_plane, a1_ld, a1_plane, x_plane;
+} NbDecStep;
+
+/* Chunk start: per-stream counters, the rows of the streams whose prediction is stale, and the
+   joint input of the others. cnt[0] = streams listed, cnt[1] = streams active, cnt[2] = 0. */
+int nb_dec_chunk_start(const DecState *d, const NbDecStep *s, int c, void *stream);
+/* One greedy decision per active stream from its logits row, then the next iteration's rows as
+   at chunk start; the last block publishes cnt[0], cnt[1], counts the iteration in cnt[2] and
+   sets the WHILE condition (cond != 0). */
+int nb_dec_step(const DecState *d, const NbDecStep *s, int c, int max_it, unsigned long long cond, void *stream);
+/* Gate-interleaved copy of an LSTM layer [4PH][K] (and its bias when given). */
+int nb_dec_interleave(const uint16_t *W, uint16_t *Wi, const float *bias, float *bi, int PH, int K, void *stream);
+/* table[v][n] = bi[n] + sum_{k < PH} Wi[n][k] * embed[v][k] (fp32, k ascending); row blank = bi. */
+int nb_dec_gate_table(const uint16_t *Wi, int64_t ldw, const uint16_t *embed, int V, int PH, const float *bi, int blank, float *table,
+                      void *stream);
 int nb_joint_argmax_rows(const float *enc, int64_t enc_ld, const float *pred, int64_t pred_ld, int pred_rpg, const uint16_t *W,
                          const float *bias, int V, int H, int rows, const int *enc_row_of, int *out_idx, float *out_val, void *stream);
 int nb_joint_argmax_gemm(const float *enc, int64_t enc_ld, const float *pred, int64_t pred_ld, const uint16_t *W, const float *bias, int V, int H,

@@ -198,9 +198,197 @@ __global__ void dec_joint_in_kernel(DecState d, const float *__restrict__ enc, i
     if (threadIdx.x == 0 && pos >= 0) d.pred_valid[b] = 1;
 }
 
+// ---- fused batched greedy decoder -------------------------------------------------------------
+
+constexpr int STEP_T = 160;  // threads of the per-stream kernels: 4 consecutive elements each for 640-wide rows
+
+__device__ __forceinline__ float4 ld4(const float *p) { return *(const float4 *)p; }
+__device__ __forceinline__ void st4(float *p, float4 v) { *(float4 *)p = v; }
+
+// bf16 hi/lo planes of 4 consecutive values (idx a multiple of 4, plane a multiple of 4)
+__device__ __forceinline__ void put4_planes(uint16_t *base, int64_t plane, int64_t idx, float4 v) {
+    const uint16_t h0 = nb::f2bf(v.x), h1 = nb::f2bf(v.y), h2 = nb::f2bf(v.z), h3 = nb::f2bf(v.w);
+    const uint16_t l0 = nb::f2bf(v.x - nb::bf2f(h0)), l1 = nb::f2bf(v.y - nb::bf2f(h1)), l2 = nb::f2bf(v.z - nb::bf2f(h2)), l3 = nb::f2bf(v.w - nb::bf2f(h3));
+    *(uint2 *)(base + idx) = make_uint2((uint32_t)h0 | ((uint32_t)h1 << 16), (uint32_t)h2 | ((uint32_t)h3 << 16));
+    *(uint2 *)(base + idx + plane) = make_uint2((uint32_t)l0 | ((uint32_t)l1 << 16), (uint32_t)l2 | ((uint32_t)l3 << 16));
+}
+
+__device__ __forceinline__ float4 relu_add4(float4 a, float4 b) {
+    return make_float4(fmaxf(a.x + b.x, 0.0f), fmaxf(a.y + b.y, 0.0f), fmaxf(a.z + b.z, 0.0f), fmaxf(a.w + b.w, 0.0f));
+}
+
+// The next iteration's rows of stream b: listed (its prediction is stale) -> h0 into A0 row pos and
+// h1 into A1 row pos at columns [PH, 2PH); otherwise, while active, its joint input row.
+// h0/h1 are read from `hsrc` (the committed state). pos < 0: not listed.
+__device__ __forceinline__ void stream_rows(const DecState &d, const NbDecStep &s, int b, int pos, bool act, int er, const float *h0src,
+                                            const float *h1src) {
+    const int tid = threadIdx.x;
+    if (pos >= 0) {
+        for (int j = tid * 4; j < s.PH; j += STEP_T * 4) {
+            const float4 h0 = ld4(h0src + j), h1 = ld4(h1src + j);
+            put4_planes(s.A0, s.a0_plane, (int64_t)pos * s.a0_ld + j, h0);
+            put4_planes(s.A1, s.a1_plane, (int64_t)pos * s.a1_ld + s.PH + j, h1);
+        }
+    } else if (act) {
+        const float *p = d.pred + (int64_t)b * s.JH, *e = s.enc + (int64_t)er * s.JH;
+        for (int j = tid * 4; j < s.JH; j += STEP_T * 4) put4_planes(s.X, s.x_plane, (int64_t)b * s.JH + j, relu_add4(ld4(e + j), ld4(p + j)));
+    }
+}
+
+// Counts of this kernel's blocks: listed streams accumulate in cnt[4], active ones in cnt[6]; the
+// last block to finish publishes them as cnt[0] / cnt[1] and clears the accumulators.
+__device__ __forceinline__ void publish(const DecState &d, bool first, int max_it, cudaGraphConditionalHandle cond) {
+    __threadfence();
+    if (atomicAdd(&d.cnt[3], 1) != (int)gridDim.x - 1) return;
+    __threadfence();
+    const int n_need = atomicExch(&d.cnt[4], 0), n_act = atomicExch(&d.cnt[6], 0);
+    d.cnt[0] = n_need;
+    d.cnt[1] = n_act;
+    d.cnt[3] = 0;
+    const int it = first ? 0 : d.cnt[2] + 1;
+    d.cnt[2] = it;
+    if (cond) cudaGraphSetConditional(cond, (n_act > 0 && it < max_it) ? 1u : 0u);
+}
+
+__global__ void __launch_bounds__(STEP_T) dec_chunk_start_kernel(DecState d, NbDecStep s, int c) {
+    nb::pdl_wait();
+    __shared__ int s_pos;
+    const int b = blockIdx.x;
+    const bool act = c > 0;
+    const bool need = act && !d.pred_valid[b];
+    if (threadIdx.x == 0) {
+        s_pos = need ? atomicAdd(&d.cnt[4], 1) : -1;
+        d.t[b] = 0;
+        d.symbols[b] = 0;
+        d.active[b] = act;
+        d.ntok[b] = 0;
+        d.erow[b] = act ? b * c : -1;
+        d.need_pos[b] = s_pos;
+        if (need) d.need_idx[s_pos] = b;
+        if (act) atomicAdd(&d.cnt[6], 1);
+    }
+    __syncthreads();
+    stream_rows(d, s, b, s_pos, act, b * c, d.h + (int64_t)b * s.PH, d.h + ((int64_t)d.streams + b) * s.PH);
+    if (threadIdx.x == 0) publish(d, true, 0, 0);
+}
+
+// One greedy step per active stream (src/decoder.c:104-122) from its logits row: argmax with ties
+// to the lowest index (src/kernels.metal:521-550); blank -> next frame; token -> emit, commit the
+// provisional LSTM state, re-score the same frame unless max_symbols tokens came from it. Then
+// the stream's rows for the next iteration (stream_rows).
+__global__ void __launch_bounds__(STEP_T) dec_step_kernel(DecState d, NbDecStep s, int c, int max_it, cudaGraphConditionalHandle cond) {
+    nb::pdl_wait();
+    __shared__ float rv[STEP_T / 32];
+    __shared__ int ri[STEP_T / 32];
+    __shared__ int s_k, s_pos;
+    const int b = blockIdx.x, tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+    const bool live = d.active[b] != 0;
+    if (!live) {
+        if (tid == 0) {
+            d.erow[b] = -1;
+            d.need_pos[b] = -1;
+            publish(d, false, max_it, cond);
+        }
+        return;
+    }
+    int t = d.t[b], sym = d.symbols[b];
+    {
+        const float *l = s.logits + (int64_t)b * s.ldl;
+        float bv = -INFINITY;
+        int bi = 0x7fffffff;
+#pragma unroll 2
+        for (int n = tid * 4; n < s.V; n += STEP_T * 4) {
+            const float4 v = ld4(l + n);  // the row pitch is a multiple of 4 floats
+            // ascending indices within a thread: strict > keeps the lowest index of equal values
+            if (v.x > bv) { bv = v.x; bi = n; }
+            if (n + 1 < s.V && v.y > bv) { bv = v.y; bi = n + 1; }
+            if (n + 2 < s.V && v.z > bv) { bv = v.z; bi = n + 2; }
+            if (n + 3 < s.V && v.w > bv) { bv = v.w; bi = n + 3; }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+        }
+        if (lane == 0) { rv[w] = bv; ri[w] = bi; }
+        __syncthreads();
+        if (tid == 0) {
+            for (int i = 1; i < STEP_T / 32; ++i)
+                if (rv[i] > bv || (rv[i] == bv && ri[i] < bi)) { bv = rv[i]; bi = ri[i]; }
+            s_k = bi;
+        }
+        __syncthreads();
+    }
+    // an index outside the vocabulary (only if every logit were NaN) is taken as blank, so no
+    // table or embedding row beyond the vocabulary is ever read
+    const int k = (s_k >= 0 && s_k < s.V) ? s_k : s.blank;
+    const bool emit = k != s.blank;
+    if (!emit) {
+        sym = 0;
+        ++t;
+    } else if (++sym >= s.max_symbols) {
+        sym = 0;
+        ++t;
+    }
+    const bool act = t < c;
+    const bool need = emit && act;
+    const int64_t s0 = (int64_t)b * s.PH, s1 = ((int64_t)d.streams + b) * s.PH;
+    if (tid == 0) {
+        s_pos = need ? atomicAdd(&d.cnt[4], 1) : -1;
+        d.idx[b] = k;
+        if (emit) {
+            if (d.ntok[b] < d.tok_cap) d.tokens[(int64_t)b * d.tok_cap + d.ntok[b]] = k;
+            d.ntok[b]++;
+            d.last_token[b] = k;
+        }
+        d.t[b] = t;
+        d.symbols[b] = sym;
+        d.active[b] = act;
+        d.pred_valid[b] = !emit;
+        d.erow[b] = act ? b * c + t : -1;
+        d.need_pos[b] = s_pos;
+        if (need) d.need_idx[s_pos] = b;
+        if (act) atomicAdd(&d.cnt[6], 1);
+    }
+    if (emit) {
+        // commit the provisional state of both layers (src/decoder.c:115-118)
+        for (int j = tid * 4; j < s.PH; j += STEP_T * 4) {
+            st4(d.h + s0 + j, ld4(d.hp + s0 + j));
+            st4(d.h + s1 + j, ld4(d.hp + s1 + j));
+            st4(d.c + s0 + j, ld4(d.cp + s0 + j));
+            st4(d.c + s1 + j, ld4(d.cp + s1 + j));
+        }
+    }
+    __syncthreads();
+    stream_rows(d, s, b, s_pos, act, b * c + t, d.hp + s0, d.hp + s1);
+    if (tid == 0) publish(d, false, max_it, cond);
+}
+
+// Gate-interleaved copy: row 4u + g of Wi is row g * PH + u of W.
+__global__ void interleave_gates_kernel(const uint16_t *__restrict__ W, uint16_t *Wi, const float *__restrict__ bias, float *bi, int PH, int K) {
+    nb::pdl_wait();
+    const int r = blockIdx.x, u = r >> 2, g = r & 3;
+    const int64_t src = (int64_t)g * PH + u;
+    for (int k = threadIdx.x; k < K; k += blockDim.x) Wi[(int64_t)r * K + k] = W[src * K + k];
+    if (bias && threadIdx.x == 0) bi[r] = bias[src];
+}
+
+__global__ void gate_table_kernel(const uint16_t *__restrict__ Wi, int64_t ldw, const uint16_t *__restrict__ embed, int PH, const float *__restrict__ bi,
+                                  int blank, float *table, int N) {
+    nb::pdl_wait();
+    const int v = blockIdx.y, n = blockIdx.x * blockDim.x + threadIdx.x;
+    if (n >= N) return;
+    float acc = 0.0f;
+    if (v != blank)
+        for (int k = 0; k < PH; ++k) acc = fmaf(nb::bf2f(Wi[(int64_t)n * ldw + k]), nb::bf2f(embed[(int64_t)v * PH + k]), acc);
+    table[(int64_t)v * N + n] = acc + bi[n];
+}
+
 __global__ void dec_reset_kernel(DecState d, int PH, int blank) {
     nb::pdl_wait();
     const int b = blockIdx.x;
+    if (b == 0 && threadIdx.x < 8) d.cnt[threadIdx.x] = 0;
     for (int l = 0; l < 2; ++l) {
         const int64_t sb = ((int64_t)l * d.streams + b) * PH;
         for (int j = threadIdx.x; j < PH; j += blockDim.x) d.h[sb + j] = d.c[sb + j] = 0.0f;
@@ -248,4 +436,22 @@ extern "C" int nb_dec_joint_in(const DecState *d, const float *enc, int JH, uint
 extern "C" int nb_dec_reset(const DecState *d, int PH, int blank, void *stream) {
     nb::launch(dec_reset_kernel, d->streams, 128, 0, (cudaStream_t)stream, *d, PH, blank);
     return nb_check_launch("dec_reset_kernel");
+}
+extern "C" int nb_dec_chunk_start(const DecState *d, const NbDecStep *s, int c, void *stream) {
+    nb::launch(dec_chunk_start_kernel, d->streams, STEP_T, 0, (cudaStream_t)stream, *d, *s, c);
+    return nb_check_launch("dec_chunk_start_kernel");
+}
+extern "C" int nb_dec_step(const DecState *d, const NbDecStep *s, int c, int max_it, unsigned long long cond, void *stream) {
+    nb::launch(dec_step_kernel, d->streams, STEP_T, 0, (cudaStream_t)stream, *d, *s, c, max_it, (cudaGraphConditionalHandle)cond);
+    return nb_check_launch("dec_step_kernel");
+}
+extern "C" int nb_dec_interleave(const uint16_t *W, uint16_t *Wi, const float *bias, float *bi, int PH, int K, void *stream) {
+    nb::launch(interleave_gates_kernel, 4 * PH, 256, 0, (cudaStream_t)stream, W, Wi, bias, bi, PH, K);
+    return nb_check_launch("interleave_gates_kernel");
+}
+extern "C" int nb_dec_gate_table(const uint16_t *Wi, int64_t ldw, const uint16_t *embed, int V, int PH, const float *bi, int blank, float *table,
+                                 void *stream) {
+    const int N = 4 * PH;
+    nb::launch(gate_table_kernel, dim3((N + 255) / 256, V), 256, 0, (cudaStream_t)stream, Wi, ldw, embed, PH, bi, blank, table, N);
+    return nb_check_launch("gate_table_kernel");
 }

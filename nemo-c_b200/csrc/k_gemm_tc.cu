@@ -23,6 +23,7 @@
 #include <mutex>
 #include "gemm_epi.cuh"
 #include "sm100.cuh"
+#include "engine_dev.h"
 
 namespace {
 
@@ -41,6 +42,7 @@ struct TcArgs {
     nb::Epi e;
     float *ws;     // split-K partial tiles
     int *counters; // one arrival counter per output tile (zero between launches)
+    NbDecEpi de;   // de.mode != 0: a batched greedy decoder epilogue replaces the plain one (activation-major tiles)
 };
 
 template <int BN>
@@ -378,6 +380,71 @@ __device__ __forceinline__ void epi16(const TcArgs &p, int64_t rowbase, int64_t 
         for (int x = 0; x < 16; x += 4) *(float4 *)(p.e.c32 + (int64_t)m * p.e.ldc32 + n0 + x) = make_float4(o[x], o[x + 1], o[x + 2], o[x + 3]);
 }
 
+// Batched greedy decoder epilogues: 16 output columns of GEMM row m, whose stream is b.
+// LSTM cell (src/kernels.metal:475-486) on gate-interleaved columns: columns n0 .. n0 + 15 are
+// gates i, f, g, o of units n0 / 4 .. n0 / 4 + 3. `bias` is the bias row or the stream's table row.
+__device__ __forceinline__ void dec_lstm16(const NbDecEpi &de, const float *__restrict__ bias, int m, int b, int ph, int n0, const float (&va)[16]) {
+    const int u0 = n0 >> 2;
+    float g[16];
+#pragma unroll
+    for (int x = 0; x < 16; x += 4) {
+        const float4 b4 = __ldg((const float4 *)(bias + n0 + x));
+        g[x] = va[x] + b4.x; g[x + 1] = va[x + 1] + b4.y; g[x + 2] = va[x + 2] + b4.z; g[x + 3] = va[x + 3] + b4.w;
+    }
+    const int64_t sb = (int64_t)b * ph + u0;
+    const float4 c4 = *(const float4 *)(de.c_in + sb);
+    const float cold[4] = { c4.x, c4.y, c4.z, c4.w };
+    float cc[4], hh[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        const float ig = nb::sigmoid_f(g[4 * q]), fg = nb::sigmoid_f(g[4 * q + 1]), gg = tanhf(g[4 * q + 2]), og = nb::sigmoid_f(g[4 * q + 3]);
+        cc[q] = fg * cold[q] + ig * gg;
+        hh[q] = og * tanhf(cc[q]);
+    }
+    *(float4 *)(de.c_out + sb) = make_float4(cc[0], cc[1], cc[2], cc[3]);
+    *(float4 *)(de.h_out + sb) = make_float4(hh[0], hh[1], hh[2], hh[3]);
+    uint32_t hi[2], lo[2];
+#pragma unroll
+    for (int x = 0; x < 2; ++x) {
+        const __nv_bfloat162 hv = __floats2bfloat162_rn(hh[2 * x], hh[2 * x + 1]);
+        const __nv_bfloat162 lv = __floats2bfloat162_rn(hh[2 * x] - __low2float(hv), hh[2 * x + 1] - __high2float(hv));
+        hi[x] = *(const uint32_t *)&hv;
+        lo[x] = *(const uint32_t *)&lv;
+    }
+    const int64_t idx = (int64_t)m * de.next_ld + u0;
+    *(uint2 *)(de.next + idx) = make_uint2(hi[0], hi[1]);
+    *(uint2 *)(de.next + idx + de.next_plane) = make_uint2(lo[0], lo[1]);
+}
+
+// Prediction projection row of stream b (pred = bias + acc) and its joint input
+// X[b] = relu(enc[er] + pred) as bf16 hi/lo planes.
+__device__ __forceinline__ void dec_joint16(const NbDecEpi &de, const float *__restrict__ bias, int b, int er, int N, int n0, const float (&va)[16]) {
+    float v[16], x[16];
+#pragma unroll
+    for (int q = 0; q < 16; q += 4) {
+        const float4 b4 = __ldg((const float4 *)(bias + n0 + q));
+        const float4 e4 = *(const float4 *)(de.enc + (int64_t)er * N + n0 + q);
+        v[q] = va[q] + b4.x; v[q + 1] = va[q + 1] + b4.y; v[q + 2] = va[q + 2] + b4.z; v[q + 3] = va[q + 3] + b4.w;
+        x[q] = fmaxf(e4.x + v[q], 0.0f); x[q + 1] = fmaxf(e4.y + v[q + 1], 0.0f);
+        x[q + 2] = fmaxf(e4.z + v[q + 2], 0.0f); x[q + 3] = fmaxf(e4.w + v[q + 3], 0.0f);
+    }
+    const int64_t idx = (int64_t)b * N + n0;
+#pragma unroll
+    for (int q = 0; q < 16; q += 4) *(float4 *)(de.pred + idx + q) = make_float4(v[q], v[q + 1], v[q + 2], v[q + 3]);
+    uint32_t hi[8], lo[8];
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+        const __nv_bfloat162 hv = __floats2bfloat162_rn(x[2 * q], x[2 * q + 1]);
+        const __nv_bfloat162 lv = __floats2bfloat162_rn(x[2 * q] - __low2float(hv), x[2 * q + 1] - __high2float(hv));
+        hi[q] = *(const uint32_t *)&hv;
+        lo[q] = *(const uint32_t *)&lv;
+    }
+    *(uint4 *)(de.X + idx) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+    *(uint4 *)(de.X + idx + 8) = make_uint4(hi[4], hi[5], hi[6], hi[7]);
+    *(uint4 *)(de.X + idx + de.x_plane) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+    *(uint4 *)(de.X + idx + de.x_plane + 8) = make_uint4(lo[4], lo[5], lo[6], lo[7]);
+}
+
 template <int BW>
 __global__ void __launch_bounds__(THREADS, 1) gemm_tcr_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmAh,
                                                             const __grid_constant__ CUtensorMap tmAl, const __grid_constant__ TcArgs p) {
@@ -486,10 +553,17 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tcr_kernel(const __grid_const
             const int m = mt * 128 + row;
             const bool row_ok = m < M;
             int64_t rowbase = 0, brow = 0;
+            int ds = 0, der = 0;               // decoder epilogues: the row's stream and its encoder row
+            const float *dbias = p.e.bias;     // decoder epilogues: bias row (or the stream's table row)
             if (row_ok) {
                 const int g = m / p.e.rpg, r = m - g * p.e.rpg;
                 rowbase = (int64_t)g * p.e.gstride + (int64_t)(rowoff + r) * p.e.ldc;
                 brow = (int64_t)g * p.e.bias_gstride;
+                if (p.de.mode) {
+                    ds = p.de.need_idx[m];
+                    if (p.de.mode == 1 && p.de.table) dbias = p.de.table + (int64_t)p.de.last_token[ds] * p.N;
+                    if (p.de.mode == 2) der = p.de.erow[ds];
+                }
             }
             if (!sm100::mbar_wait(&acc_full[b], (t >> 1) & 1)) { flags[2] = 1; flags[0] = 1; atomicExch(&g_tc_error, 8); }
             sm100::named_barrier(1, 256);
@@ -546,6 +620,8 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tcr_kernel(const __grid_const
                     const int n0 = n_base + jj0;
                     if (n0 >= nout) continue;
                     const int cnt = min(16, nout - n0);
+                    if (p.de.mode == 1) { dec_lstm16(p.de, dbias, m, ds, p.N >> 2, n0, va); continue; }
+                    if (p.de.mode == 2) { dec_joint16(p.de, dbias, ds, der, p.N, n0, va); continue; }
                     if (p.vec && cnt == 16) {
                         // 16-byte accesses (alignment of every pointer and stride checked on the host),
                         // the activation / output format resolved at compile time
@@ -748,7 +824,7 @@ int vec_ok(const nemo_gemm_args_t *a) {
 }
 
 template <int BW>
-int launch_r(const nemo_gemm_args_t *a, const PlanR &pl, cudaStream_t st) {
+int launch_r(const nemo_gemm_args_t *a, const PlanR &pl, cudaStream_t st, const NbDecEpi *de) {
     CUtensorMap mw, mh, ml;
     const bool glu = a->act == NEMO_ACT_GLU;
     if (make_map(&mw, a->W, a->K, a->N, a->ldw, glu ? BW / 2 : BW)) return -1;
@@ -770,20 +846,21 @@ int launch_r(const nemo_gemm_args_t *a, const PlanR &pl, cudaStream_t st) {
     p.ws = g_ws;
     p.counters = g_counters;
     p.vec = vec_ok(a);
+    if (de) p.de = *de;
     const int grid = p.units < g_sms ? p.units : g_sms;
     nb::launch(gemm_tcr_kernel<BW>, grid, THREADS, CfgR<BW>::SMEM, st, mw, mh, ml, p);
     return nb_check_launch("gemm_tcr_kernel");
 }
 
-int launch_rows(const nemo_gemm_args_t *a, cudaStream_t st) {
+int launch_rows(const nemo_gemm_args_t *a, cudaStream_t st, const NbDecEpi *de = nullptr) {
     const bool glu = a->act == NEMO_ACT_GLU;
     const bool ok256 = !glu || (a->N / 2) % 128 == 0;
     PlanR best = plan_r(a, 128, false);
     const PlanR cand[3] = { plan_r(a, 256, false), plan_r(a, 128, true), plan_r(a, 256, true) };
     for (const PlanR &p : cand)
         if ((p.bw == 128 || ok256) && p.est_us < best.est_us) best = p;
-    if (best.bw == 256) return launch_r<256>(a, best, st);
-    return launch_r<128>(a, best, st);
+    if (best.bw == 256) return launch_r<256>(a, best, st, de);
+    return launch_r<128>(a, best, st, de);
 }
 
 }  // namespace
@@ -808,6 +885,23 @@ int nb_gemm_tc_layout(const nemo_gemm_args_t *a, int layout, void *stream) {
 }
 
 int nb_gemm_tc(const nemo_gemm_args_t *a, void *stream) { return nb_gemm_tc_layout(a, 0, stream); }
+
+extern "C" int nb_gemm_dec(const nemo_gemm_args_t *a, const NbDecEpi *de, void *stream) {
+    if (init_once()) return -1;
+    if (!de || (de->mode != 1 && de->mode != 2)) return nb_set_error("decoder GEMM: unknown epilogue mode");
+    if (a->a_fmt != NEMO_FMT_BF16X2 || a->act != NEMO_ACT_NONE || a->accumulate || a->K % 8 || a->N % 16)
+        return nb_set_error("decoder GEMM: needs bf16 hi/lo activations, no activation or accumulation, K %% 8 == 0 and N %% 16 == 0");
+    const float *bias = de->mode == 1 && de->table ? de->table : a->bias;
+    if (!bias || ((uintptr_t)bias & 15) || !de->need_idx) return nb_set_error("decoder GEMM: needs a 16-byte aligned bias or table and the row list");
+    if (de->mode == 1 && ((a->N & 3) || !de->c_in || !de->c_out || !de->h_out || !de->next || (de->table && !de->last_token) ||
+                          (((uintptr_t)de->c_in | (uintptr_t)de->c_out | (uintptr_t)de->h_out) & 15) || ((uintptr_t)de->next & 7) ||
+                          (a->N / 4) % 4 || de->next_ld % 4 || de->next_plane % 4))
+        return nb_set_error("decoder GEMM: LSTM epilogue operands misaligned or missing");
+    if (de->mode == 2 && (!de->enc || !de->erow || !de->pred || !de->X || (((uintptr_t)de->enc | (uintptr_t)de->pred | (uintptr_t)de->X) & 15) ||
+                          de->x_plane % 8))
+        return nb_set_error("decoder GEMM: joint epilogue operands misaligned or missing");
+    return launch_rows(a, (cudaStream_t)stream, de);
+}
 
 extern "C" int nemo_gpu_check_device_errors(void) {
     int v = 0;
