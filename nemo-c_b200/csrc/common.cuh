@@ -59,8 +59,14 @@ __device__ __forceinline__ float block_sum(float v, float *red) {
 }
 
 // Wait for the previous kernel in the stream when launched with programmatic dependent launch
-// (a no-op otherwise), and allow the next one to start its prologue.
-__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+// (a no-op otherwise: the launch itself waited), then let the next kernel be scheduled: it runs
+// its own set-up on free SMs and blocks in its pdl_wait() until this grid has completed and its
+// writes are visible. A grid is released only once all of its CTAs are resident, so waiting
+// grids never keep their predecessor's CTAs from running.
+__device__ __forceinline__ void pdl_wait() {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;" :::);
+}
 __device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" :::); }
 
 }  // namespace nb

@@ -70,6 +70,7 @@ struct nb_engine {
     /* several streams: the greedy loop as four tensor-core GEMMs with decoder epilogues and one
        step kernel per iteration (NEMO_DEC_FUSED=0 keeps the kernel-by-kernel iteration) */
     int dec_fused;
+    int dec_unroll;              /* greedy iterations per pass of the decoder graph's WHILE body */
     uint16_t *dec_w0i, *dec_w1i; /* gate-interleaved LSTM layers [4PH][2PH] */
     float *dec_b0i, *dec_b1i;    /* their biases, interleaved alike */
     float *dec_table;            /* [vocab + 1][4PH]: b0 + W0x . embed[v] */
@@ -302,6 +303,14 @@ nb_engine_t *nb_engine_create(nb_model_t *m, int B, int right, char *err, size_t
     if (B == 1 && fmt == NEMO_FMT_BF16X2 && enc1_setup(e, err, errlen)) goto fail;
     if (B == 1 && dec1_setup(e, err, errlen)) goto fail;
     if (B > 1 && fmt == NEMO_FMT_BF16X2 && dec_fused_setup(e, err, errlen)) goto fail;
+    {
+        /* iterations after the last active stream finished do no work but the joint GEMM; a few
+           per WHILE pass amortise the conditional node's per-pass cost */
+        const char *du = getenv("NEMO_DEC_UNROLL");
+        e->dec_unroll = du ? atoi(du) : 4;
+        if (e->dec_unroll < 1) e->dec_unroll = 1;
+        if (e->dec_unroll > 16) e->dec_unroll = 16;
+    }
     if (nb_engine_reset(e, err, errlen)) goto fail;
     return e;
 fail:
@@ -693,9 +702,10 @@ static int dec_iteration(nb_engine_t *e, int c, int unused) {
     return dec_iteration_body(e, c, 0);
 }
 
-/* The greedy loop of a chunk as one graph: a WHILE node whose body is one iteration; the body's
-   last kernel sets the loop condition on the device, so no host round trip happens per emitted
-   token (src/decoder.c:97-123 loops on the host). Cached per chunk length c. Returns the slot,
+/* The greedy loop of a chunk as one graph: a WHILE node whose body is dec_unroll iterations;
+   each iteration's last kernel sets the loop condition on the device, so no host round trip
+   happens per emitted token (src/decoder.c:97-123 loops on the host). Iterations that run after
+   every stream finished change nothing (no stream is listed or active). Cached per chunk length c. Returns the slot,
    or -1 on error, or -2 when the cache is full (the host loop is used instead). */
 static int dec_graph(nb_engine_t *e, int c) {
     for (int i = 0; i < e->ngraphs; ++i)
@@ -716,7 +726,8 @@ static int dec_graph(nb_engine_t *e, int c) {
     cudaGraph_t body = p.conditional.phGraph_out[0];
     if (cudaStreamBeginCaptureToGraph(e->st, body, NULL, NULL, 0, cudaStreamCaptureModeThreadLocal) != cudaSuccess) goto fail;
     nb_set_launch_counting(0);
-    const int rc = dec_iteration_body(e, c, (unsigned long long)h);
+    int rc = 0;
+    for (int u = 0; u < e->dec_unroll && !rc; ++u) rc = dec_iteration_body(e, c, (unsigned long long)h);
     nb_set_launch_counting(1);
     cudaGraph_t captured = NULL;
     const cudaError_t ce = cudaStreamEndCapture(e->st, &captured);
@@ -731,7 +742,7 @@ static int dec_graph(nb_engine_t *e, int c) {
     e->graphs[slot].k1 = c;
     e->graphs[slot].k2 = 0;
     e->graphs[slot].exec = exec;
-    e->graphs[slot].kernels = nb_graph_kernel_nodes(body); /* per iteration */
+    e->graphs[slot].kernels = nb_graph_kernel_nodes(body) / (uint64_t)e->dec_unroll; /* per iteration */
     cudaGraphDestroy(G);
     return slot;
 fail:

@@ -128,12 +128,7 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
     int *brow = (int *)(rowbase + BN);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    nb::pdl_wait();
-    const int M = p.dynM ? min(p.M, *p.dynM) : p.M;
-    const int live_mtiles = (M + BN - 1) / BN;            // row tiles that hold real rows
-    const int units = live_mtiles * p.n_wtiles * p.splits;
-    if ((int)blockIdx.x >= units) return;                  // nothing for this CTA
-
+    // set-up first: with programmatic dependent launch it overlaps the previous kernel's tail
     if (threadIdx.x == 0) {
         for (int s = 0; s < C::STAGES; ++s) { sm100::mbar_init(&full[s], 1); sm100::mbar_init(&empty[s], 1); }
         for (int b = 0; b < 2; ++b) { sm100::mbar_init(&acc_full[b], 1); sm100::mbar_init(&acc_empty[b], 1); }
@@ -152,6 +147,10 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
     __syncthreads();
     sm100::tc_fence_after();
     const uint32_t tmem = *tmem_holder;
+    nb::pdl_wait();  // inputs of the previous kernel are visible from here on
+    const int M = p.dynM ? min(p.M, *p.dynM) : p.M;
+    const int live_mtiles = (M + BN - 1) / BN;            // row tiles that hold real rows
+    const int units = live_mtiles * p.n_wtiles * p.splits; // CTAs at or beyond it have nothing to do
 
     if (warp == 0 && lane == 0) {
         // ---- producer: weight tile (two 64-row halves for GLU) + activation hi/lo tiles ----
@@ -460,12 +459,7 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tcr_kernel(const __grid_const
     volatile int *flags = (volatile int *)(tmem_holder + 1); // [0] abort, [1] last split of the unit, [2] epilogue abort
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    nb::pdl_wait();
-    const int M = p.dynM ? min(p.M, *p.dynM) : p.M;
-    const int live_mtiles = (M + 127) / 128;
-    const int units = live_mtiles * p.n_wtiles * p.splits;
-    if ((int)blockIdx.x >= units) return;
-
+    // set-up first: with programmatic dependent launch it overlaps the previous kernel's tail
     if (threadIdx.x == 0) {
         for (int s = 0; s < C::STAGES; ++s) { sm100::mbar_init(&full[s], 1); sm100::mbar_init(&empty[s], 1); }
         for (int b = 0; b < 2; ++b) { sm100::mbar_init(&acc_full[b], 1); sm100::mbar_init(&acc_empty[b], 1); }
@@ -484,6 +478,10 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tcr_kernel(const __grid_const
     __syncthreads();
     sm100::tc_fence_after();
     const uint32_t tmem = *tmem_holder;
+    nb::pdl_wait();  // inputs of the previous kernel are visible from here on
+    const int M = p.dynM ? min(p.M, *p.dynM) : p.M;
+    const int live_mtiles = (M + 127) / 128;
+    const int units = live_mtiles * p.n_wtiles * p.splits; // CTAs at or beyond it have nothing to do
 
     if (warp == 0 && lane == 0) {
         // ---- producer: activation hi/lo tiles + weight tile (value and gate halves for GLU) ----
