@@ -222,7 +222,10 @@ class Session:
             self.h = None
 
     def __del__(self):
-        self.close()
+        try:
+            self.close()
+        except TypeError:  # interpreter shutdown: the module's globals are already gone
+            pass
 
 
 class Batch:
@@ -242,10 +245,12 @@ class Batch:
 
     def feed(self, samples, final=False, max_tokens=4096):
         """samples: [B][n] float32 (host). Returns a list of token-id lists, one per stream."""
-        x = _f32(samples)
+        x = samples if isinstance(samples, np.ndarray) and samples.dtype == np.float32 and samples.ndim == 2 and samples.strides[1] == 4 else _f32(samples)
         assert x.shape[0] == self.B
-        ptrs = (f32p * self.B)(*[x[i].ctypes.data_as(f32p) for i in range(self.B)])
-        tok = np.zeros((self.B, max_tokens), np.int32)
+        # one pointer per stream: rows need not be adjacent (a column slice of a larger array is read in place)
+        base, rs = x.ctypes.data, x.strides[0]
+        ptrs = (f32p * self.B)(*[C.cast(base + i * rs, f32p) for i in range(self.B)])
+        tok = np.empty((self.B, max_tokens), np.int32)
         cnt = np.zeros(self.B, np.int32)
         err = C.create_string_buffer(1024)
         rc = api().nemoasr_batch_feed(self.h, ptrs, x.shape[1], int(final), tok.ctypes.data_as(i32p), max_tokens, cnt.ctypes.data_as(i32p), err, 1024)
@@ -295,7 +300,10 @@ class Batch:
             self.h = None
 
     def __del__(self):
-        self.close()
+        try:
+            self.close()
+        except TypeError:  # interpreter shutdown: the module's globals are already gone
+            pass
 
 
 def mel(samples, blocks=None):
