@@ -52,7 +52,9 @@ int nemo_gemm(const nemo_gemm_args_t *a, void *stream);
 /* Force a kernel family for tests and the kernel sweep: 0 = by row count (default),
    1 = CUDA-core weight streaming, 2 = tcgen05 tensor cores (tile layout by row count),
    3 = CUDA-core tiled, 4 = tensor cores with weight-major tiles (weights on the MMA's 128-row
-   side), 5 = tensor cores with activation-major tiles (128 activation rows x 128/256 weights). */
+   side), 5 = tensor cores with activation-major tiles (128 activation rows x 128/256 weights),
+   6 = activation-major tiles scheduled stream-K (every CTA an equal share of the k-blocks of all
+   tiles; kind 5's plan when the row count is dynamic). */
 int nemo_gemm_forced(const nemo_gemm_args_t *a, int kind, void *stream);
 /* Allocation-free tensor-core GEMM (no counterpart in the reference, whose Metal GEMMs need no
    split-K scratch). Same arguments and results as nemo_gemm for NEMO_FMT_BF16X2 activations of

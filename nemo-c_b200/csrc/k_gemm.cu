@@ -157,7 +157,7 @@ extern "C" int nemo_gemm_forced(const nemo_gemm_args_t *a, int kind, void *strea
         if (a->a_fmt == NEMO_FMT_BF16X2) kind = 2;
         else kind = a->M <= 16 ? 1 : 3;
     }
-    if (kind == 2 || kind == 4 || kind == 5) {
+    if (kind == 2 || kind == 4 || kind == 5 || kind == 6) {
         if (a->a_fmt != NEMO_FMT_BF16X2) return nb_set_error("nemo_gemm: tensor-core path needs A as bf16 hi/lo planes");
         return nb_gemm_tc_layout(a, kind == 2 ? 0 : kind - 3, stream);
     }

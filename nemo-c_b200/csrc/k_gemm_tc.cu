@@ -19,6 +19,7 @@
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include "gemm_epi.cuh"
@@ -43,6 +44,52 @@ struct TcArgs {
     float *ws;     // split-K partial tiles
     int *counters; // one arrival counter per output tile (zero between launches)
     NbDecEpi de;   // de.mode != 0: a batched greedy decoder epilogue replaces the plain one (activation-major tiles)
+    int sk_q;      // activation-major stream-K: k-blocks per CTA (0: units of whole k-splits instead)
+    int slots;     // partial-tile slots per output tile in ws (splits, or the most stream-K pieces of a tile)
+};
+
+// The work of one activation-major CTA, walked identically by its producer, MMA and epilogue
+// roles: pieces (tile, k-blocks [kb0, kb1), slot of the piece among the tile's `parts`).
+// k-split units: unit u = blockIdx.x, blockIdx.x + gridDim.x, ... is (tile u / splits, split u % splits).
+// Stream-K: the CTA owns the k-blocks [blockIdx.x * q, (blockIdx.x + 1) * q) of the flattened
+// (tile, k-block) space, cut at tile boundaries; a tile's pieces are numbered by CTA.
+struct Piece {
+    int tile, kb0, kb1, slot, parts;
+};
+struct PieceIter {
+    int cur, end;
+    __device__ __forceinline__ PieceIter(const TcArgs &p, int tiles) {
+        if (p.sk_q) {
+            cur = blockIdx.x * p.sk_q;
+            end = min(tiles * p.kblocks, cur + p.sk_q);
+        } else {
+            cur = blockIdx.x;
+            end = tiles * p.splits;
+        }
+    }
+    __device__ __forceinline__ bool next(const TcArgs &p, Piece &w) {
+        if (cur >= end) return false;
+        if (!p.sk_q) {
+            const int split = cur % p.splits;
+            w.tile = cur / p.splits;
+            w.kb0 = split * p.kb_per_split;
+            w.kb1 = min(p.kblocks, w.kb0 + p.kb_per_split);
+            w.slot = split;
+            w.parts = p.splits;
+            cur += gridDim.x;
+            return true;
+        }
+        const int kb = p.kblocks, q = p.sk_q;
+        w.tile = cur / kb;
+        w.kb0 = cur - w.tile * kb;
+        const int tile_end = (w.tile + 1) * kb, e = min(end, tile_end);
+        w.kb1 = w.kb0 + (e - cur);
+        const int first = (w.tile * kb) / q;
+        w.parts = (tile_end - 1) / q - first + 1;
+        w.slot = (int)blockIdx.x - first;
+        cur = e;
+        return true;
+    }
 };
 
 template <int BN>
@@ -481,15 +528,16 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tcr_kernel(const __grid_const
     nb::pdl_wait();  // inputs of the previous kernel are visible from here on
     const int M = p.dynM ? min(p.M, *p.dynM) : p.M;
     const int live_mtiles = (M + 127) / 128;
-    const int units = live_mtiles * p.n_wtiles * p.splits; // CTAs at or beyond it have nothing to do
+    const int tiles = live_mtiles * p.n_wtiles;            // output tiles that hold real rows
 
     if (warp == 0 && lane == 0) {
         // ---- producer: activation hi/lo tiles + weight tile (value and gate halves for GLU) ----
         int i = 0;
-        for (int u = blockIdx.x; u < units && !flags[0]; u += gridDim.x) {
-            const int split = u % p.splits, tile = u / p.splits, wt = tile % p.n_wtiles, mt = tile / p.n_wtiles;
-            const int kb0 = split * p.kb_per_split, kb1 = min(p.kblocks, kb0 + p.kb_per_split);
-            for (int kb = kb0; kb < kb1; ++kb, ++i) {
+        PieceIter it(p, tiles);
+        Piece w;
+        while (!flags[0] && it.next(p, w)) {
+            const int wt = w.tile % p.n_wtiles, mt = w.tile / p.n_wtiles;
+            for (int kb = w.kb0; kb < w.kb1; ++kb, ++i) {
                 const int s = i % C::STAGES;
                 if (i >= C::STAGES && !sm100::mbar_wait(&empty[s], ((i / C::STAGES) - 1) & 1)) { flags[0] = 1; atomicExch(&g_tc_error, 5); break; }
                 if (flags[0]) break;
@@ -510,9 +558,10 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tcr_kernel(const __grid_const
         // ---- MMA issuer ----
         constexpr uint32_t idesc = sm100::idesc_bf16_f32(128, BW);
         int i = 0, t = 0;
-        for (int u = blockIdx.x; u < units && !flags[0]; u += gridDim.x, ++t) {
-            const int split = u % p.splits;
-            const int kb0 = split * p.kb_per_split, kb1 = min(p.kblocks, kb0 + p.kb_per_split);
+        PieceIter it(p, tiles);
+        Piece w;
+        for (; !flags[0] && it.next(p, w); ++t) {
+            const int kb0 = w.kb0, kb1 = w.kb1;
             const int b = t & 1;
             if (t >= 2 && !sm100::mbar_wait(&acc_empty[b], ((t >> 1) - 1) & 1)) { flags[0] = 1; atomicExch(&g_tc_error, 6); break; }
             sm100::tc_fence_after();
@@ -545,8 +594,10 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tcr_kernel(const __grid_const
         float *__restrict__ C32 = (float *)p.e.C;
         uint16_t *__restrict__ C16 = (uint16_t *)p.e.C;
         int t = 0;
-        for (int u = blockIdx.x; u < units; u += gridDim.x, ++t) {
-            const int split = u % p.splits, tile = u / p.splits, wt = tile % p.n_wtiles, mt = tile / p.n_wtiles;
+        PieceIter it(p, tiles);
+        Piece w;
+        for (; it.next(p, w); ++t) {
+            const int tile = w.tile, wt = tile % p.n_wtiles, mt = tile / p.n_wtiles;
             const int b = t & 1;
             const int m = mt * 128 + row;
             const bool row_ok = m < M;
@@ -573,20 +624,20 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tcr_kernel(const __grid_const
             const int span = p.glu ? BW / 4 : BW / 2;
             const int j0 = half * span;
             const int n_base = p.glu ? wt * (BW / 2) : wt * OUT_COLS;
-            float *wsb = p.ws + (int64_t)tile * p.splits * 128 * BW;
+            float *wsb = p.ws + (int64_t)tile * p.slots * 128 * BW;
             bool finish = ok;
-            if (ok && p.splits > 1) {
-                // partial tile [split][row][BW] (all TMEM columns, value and gate alike)
+            if (ok && w.parts > 1) {
+                // partial tile [slot][row][BW] (all TMEM columns, value and gate alike)
                 for (int j = half * (BW / 2); j < (half + 1) * (BW / 2); j += 16) {
                     float v[16];
                     sm100::tmem_ld16(tacc + j, v);
-                    float4 *dst = (float4 *)(wsb + ((int64_t)split * 128 + row) * BW + j);
+                    float4 *dst = (float4 *)(wsb + ((int64_t)w.slot * 128 + row) * BW + j);
 #pragma unroll
                     for (int x = 0; x < 4; ++x) dst[x] = make_float4(v[4 * x], v[4 * x + 1], v[4 * x + 2], v[4 * x + 3]);
                 }
                 __threadfence();
                 sm100::named_barrier(1, 256);
-                if (etid == 0) flags[1] = atomicAdd(&p.counters[tile], 1) == p.splits - 1;
+                if (etid == 0) flags[1] = atomicAdd(&p.counters[tile], 1) == w.parts - 1;
                 sm100::named_barrier(1, 256);
                 finish = flags[1];
                 if (finish) __threadfence();
@@ -594,14 +645,14 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tcr_kernel(const __grid_const
             if (finish) {
                 for (int jj0 = j0; jj0 < j0 + span; jj0 += 16) {
                     float va[16], vg[16];
-                    if (p.splits == 1) {
+                    if (w.parts == 1) {
                         sm100::tmem_ld16(tacc + jj0, va);
                         if (p.glu) sm100::tmem_ld16(tacc + BW / 2 + jj0, vg);
                     } else {
 #pragma unroll
                         for (int x = 0; x < 16; ++x) va[x] = vg[x] = 0.0f;
                         if (row_ok)
-                            for (int s = 0; s < p.splits; ++s) {
+                            for (int s = 0; s < w.parts; ++s) {
                                 const float *src = wsb + ((int64_t)s * 128 + row) * BW;
 #pragma unroll
                                 for (int x = 0; x < 16; x += 4) {
@@ -672,7 +723,7 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tcr_kernel(const __grid_const
                         if (p.e.c32) p.e.c32[(int64_t)m * p.e.ldc32 + n0 + x] = v;
                     }
                 }
-                if (p.splits > 1 && etid == 0) p.counters[tile] = 0;
+                if (w.parts > 1 && etid == 0) p.counters[tile] = 0;
             }
             sm100::tc_fence_before();
             sm100::named_barrier(1, 256);
@@ -782,6 +833,7 @@ int launch(const nemo_gemm_args_t *a, cudaStream_t st) {
 // so splits are only planned for long K (>= 32 k-blocks) over few tiles.
 struct PlanR {
     int bw, tiles, splits, kb_per_split, units;
+    int sk_q, slots, grid;  // stream-K share per CTA (0: k-split units), partial slots per tile, CTAs
     float est_us;
 };
 
@@ -802,9 +854,45 @@ PlanR plan_r(const nemo_gemm_args_t *a, int bw, bool allow_split) {
     r.kb_per_split = (kblocks + splits - 1) / splits;
     r.splits = (kblocks + r.kb_per_split - 1) / r.kb_per_split;
     r.units = r.tiles * r.splits;
+    r.sk_q = 0;
+    r.slots = r.splits;
+    r.grid = r.units < g_sms ? r.units : g_sms;
     const int rounds = (r.units + g_sms - 1) / g_sms;
     r.est_us = rounds * (0.27f * (bw / 128) * r.kb_per_split + 4.0f) + (r.splits > 1 ? 6.0f : 0.0f);
     return r;
+}
+
+// Stream-K plan: every CTA gets an equal share q of the tiles' k-blocks, so no SM idles through
+// a last, partly filled round of tiles; tiles cut between CTAs are summed through partial slots
+// by the last of their pieces to finish. Needs a row count known at launch (no dynM). ok = 0
+// when the partial slots would not fit the workspace.
+PlanR plan_sk(const nemo_gemm_args_t *a, int bw, int *ok) {
+    PlanR r = plan_r(a, bw, false);
+    const int kb = (a->K + BK - 1) / BK, total = r.tiles * kb;
+    const int q = (total + g_sms - 1) / g_sms;
+    int parts = 1;
+    for (int t = 0; t < r.tiles; ++t) {
+        const int n = (t * kb + kb - 1) / q - (t * kb) / q + 1;
+        parts = n > parts ? n : parts;
+    }
+    *ok = !a->dynM && (size_t)r.tiles * parts * 128 * bw <= g_ws_floats && r.tiles <= g_ncounters;
+    r.sk_q = q;
+    r.slots = parts;
+    r.grid = (total + q - 1) / q;
+    r.est_us = 0.27f * (bw / 128) * q + 4.0f + (parts > 1 ? 14.0f : 0.0f);
+    return r;
+}
+
+// Stream-K is planned only on request (NEMO_GEMM_SK=1, or layout 3): measured on a B200 at this
+// model's shapes (64..3584 rows) it was 1.1-2.4x slower than the best k-split plan, the partial
+// tiles' round trip (store, fence, arrival, reload) costing more than the idle SMs it saves.
+int sk_policy() {
+    static int v = -2;
+    if (v == -2) {
+        const char *e = getenv("NEMO_GEMM_SK");
+        v = e && atoi(e) == 1 ? 1 : 0;
+    }
+    return v;
 }
 
 // 16-byte epilogue accesses: every row start, plane offset and bias row of the output must keep
@@ -845,18 +933,30 @@ int launch_r(const nemo_gemm_args_t *a, const PlanR &pl, cudaStream_t st, const 
     p.counters = g_counters;
     p.vec = vec_ok(a);
     if (de) p.de = *de;
-    const int grid = p.units < g_sms ? p.units : g_sms;
+    p.sk_q = pl.sk_q;
+    p.slots = pl.slots;
+    const int grid = pl.grid;
     nb::launch(gemm_tcr_kernel<BW>, grid, THREADS, CfgR<BW>::SMEM, st, mw, mh, ml, p);
     return nb_check_launch("gemm_tcr_kernel");
 }
 
-int launch_rows(const nemo_gemm_args_t *a, cudaStream_t st, const NbDecEpi *de = nullptr) {
+// sched: 0 = best estimate, 1 = k-split units only, 2 = stream-K (when the shape allows it)
+int launch_rows(const nemo_gemm_args_t *a, cudaStream_t st, const NbDecEpi *de = nullptr, int sched = 0) {
     const bool glu = a->act == NEMO_ACT_GLU;
     const bool ok256 = !glu || (a->N / 2) % 128 == 0;
     PlanR best = plan_r(a, 128, false);
     const PlanR cand[3] = { plan_r(a, 256, false), plan_r(a, 128, true), plan_r(a, 256, true) };
-    for (const PlanR &p : cand)
-        if ((p.bw == 128 || ok256) && p.est_us < best.est_us) best = p;
+    const int pol = sched == 1 ? 0 : sched == 2 ? 1 : sk_policy();
+    if (pol != 1)
+        for (const PlanR &p : cand)
+            if ((p.bw == 128 || ok256) && p.est_us < best.est_us) best = p;
+    if (pol != 0) {
+        int ok128 = 0, ok2 = 0;
+        const PlanR s128 = plan_sk(a, 128, &ok128), s256 = plan_sk(a, 256, &ok2);
+        if (pol == 1 && ok128) best = s128;
+        if (ok128 && s128.est_us < best.est_us) best = s128;
+        if (ok2 && ok256 && s256.est_us < best.est_us) best = s256;
+    }
     if (best.bw == 256) return launch_r<256>(a, best, st, de);
     return launch_r<128>(a, best, st, de);
 }
@@ -866,7 +966,8 @@ int launch_rows(const nemo_gemm_args_t *a, cudaStream_t st, const NbDecEpi *de =
 // One-time setup (driver entry point, split-K workspace): call before capturing a CUDA graph.
 extern "C" int nb_gemm_tc_init(void) { return init_once(); }
 
-// layout: 0 = by row count, 1 = weight-major tiles, 2 = activation-major tiles
+// layout: 0 = by row count, 1 = weight-major tiles, 2 = activation-major tiles, 3 = activation-major
+// tiles scheduled stream-K (falls back to the planner when the shape does not allow it)
 int nb_gemm_tc_layout(const nemo_gemm_args_t *a, int layout, void *stream) {
     if (init_once()) return -1;
     if (a->act == NEMO_ACT_GLU && ((a->N / 2) % 64)) return nb_set_error("tensor-core GEMM: GLU needs N/2 to be a multiple of 64");
@@ -876,6 +977,7 @@ int nb_gemm_tc_layout(const nemo_gemm_args_t *a, int layout, void *stream) {
     // must stream through every SM with split-K, which the weight-major tiles do
     if (layout == 0) layout = a->M > 32 ? 2 : 1;
     if (layout == 2) return launch_rows(a, st);
+    if (layout == 3) return launch_rows(a, st, nullptr, 2);
     if (a->M <= 16) return launch<16>(a, st);
     if (a->M <= 32) return launch<32>(a, st);
     if (a->M <= 64) return launch<64>(a, st);

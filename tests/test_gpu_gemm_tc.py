@@ -131,3 +131,45 @@ def test_tcr_matches_weight_major_tiles():
         a = run_gemm(A, W, act=act, kind=4, a_fmt=1)
         b = run_gemm(A, W, act=act, kind=5, a_fmt=1)
         assert rel_err(b, a) < 1e-5  # same products, fp32 sums in a different order (k-splits differ)
+
+
+# ---- stream-K schedule (kind 6): every CTA an equal share of all tiles' k-blocks ----
+
+@pytest.mark.parametrize("M", [128, 200, 600, 1792])
+@pytest.mark.parametrize("act", [0, 1, 2, 3])
+def test_tcr_stream_k_epilogues(M, act):
+    rng = np.random.default_rng(5000 + M * 4 + act)
+    N, K = 512, 1280
+    A = rng.standard_normal((M, K)).astype(np.float32)
+    W = bf16(rng, (N, K), 0.03)
+    b = (rng.standard_normal(N) * 0.1).astype(np.float32)
+    C0 = rng.standard_normal((M, N // 2 if act == 3 else N)).astype(np.float32)
+    got = run_gemm(A, W, b, C0, act=act, acc=1, alpha=0.5, kind=6, a_fmt=1)
+    ref = orc.gemm(A, W, b, C0=C0, act=act, accumulate=True, alpha=0.5)
+    assert rel_err(got, ref) < BF16X2_TOL
+    # pieces are summed in slot order: the result does not depend on which piece finishes last
+    assert np.array_equal(got, run_gemm(A, W, b, C0, act=act, acc=1, alpha=0.5, kind=6, a_fmt=1))
+
+
+@pytest.mark.parametrize("shape", [(3072, 1024), (4096, 1024), (1024, 4096), (2048, 1024), (1024, 1024), (1025, 640)])
+def test_tcr_stream_k_model_shapes(shape):
+    rng = np.random.default_rng(17 + sum(shape))
+    N, K = shape
+    A = rng.standard_normal((1792, K)).astype(np.float32)
+    W = bf16(rng, (N, K), 0.02)
+    got = run_gemm(A, W, kind=6, a_fmt=1)
+    assert rel_err(got, orc.gemm(A, W)) < BF16X2_TOL
+    assert rel_err(got, run_gemm(A, W, kind=5, a_fmt=1)) < 1e-5
+
+
+def test_tcr_stream_k_row_mapping():
+    rng = np.random.default_rng(37)
+    streams, c, N, K, cap, off = 40, 7, 256, 1024, 30, 9
+    A = rng.standard_normal((streams * c, K)).astype(np.float32)
+    W = bf16(rng, (N, K), 0.03)
+    bias = rng.standard_normal((streams, N)).astype(np.float32)
+    got = run_gemm(A, W, bias.ravel(), kind=6, a_fmt=1, rpg=c, gstride=cap * N, rowoff=off, crows=streams * cap, bias_gstride=N)
+    got = got.reshape(streams, cap, N)
+    for s in range(streams):
+        assert rel_err(got[s, off:off + c], orc.gemm(A[s * c:(s + 1) * c], W, bias[s])) < BF16X2_TOL
+        assert np.all(got[s, :off] == 0) and np.all(got[s, off + c:] == 0)
