@@ -71,9 +71,11 @@ struct nb_engine {
        step kernel per iteration (NEMO_DEC_FUSED=0 keeps the kernel-by-kernel iteration) */
     int dec_fused;
     int dec_unroll;              /* greedy iterations per pass of the decoder graph's WHILE body */
-    uint16_t *dec_w0i, *dec_w1i; /* gate-interleaved LSTM layers [4PH][2PH] */
-    float *dec_b0i, *dec_b1i;    /* their biases, interleaved alike */
-    float *dec_table;            /* [vocab + 1][4PH]: b0 + W0x . embed[v] */
+    uint16_t *dec_wg1;           /* [8PH][PH]: gate-interleaved W1x rows, then W0h rows */
+    uint16_t *dec_wg2;           /* [JH + 4PH][PH]: Wp rows, then gate-interleaved W1h rows */
+    float *dec_b1i;              /* interleaved b1 */
+    float *dec_table;            /* [vocab + 1][4PH]: b0 + W0x . embed[v], interleaved */
+    float *dec_r0, *dec_r1;      /* [B][4PH]: W0h . h0 and b1 + W1h . h1 of each stream's committed state */
     unsigned *d_enc1_bar;
     int *d_enc1_err;
     struct { int kind, k1, k2; cudaGraphExec_t exec; uint64_t kernels; } graphs[NB_MAX_GRAPHS];
@@ -141,27 +143,41 @@ static int enc1_setup(nb_engine_t *e, char *err, size_t errlen) {
     return 0;
 }
 
-/* Several streams with bf16 hi/lo activations: gate-interleaved LSTM weights and the per-token
-   gate table of layer 0 for the fused greedy iteration. */
+/* Several streams with bf16 hi/lo activations: the fused greedy iteration's weights (gate-
+   interleaved, the recurrent halves appended to the GEMMs that read the same input), the
+   per-token gate table of layer 0 and the per-stream recurrent gate parts. */
 static int dec_fused_setup(nb_engine_t *e, char *err, size_t errlen) {
     const char *ev = getenv("NEMO_DEC_FUSED");
     if (ev && !strcmp(ev, "0")) return 0;
     const nb_model_t *m = e->m;
     const nb_config_t *g = &m->g;
-    const size_t PH = (size_t)g->pred_hidden, NV = (size_t)g->vocab_size + 1;
-    if (g->pred_layers != 2 || PH % 16 || g->joint_hidden % 16 || g->num_classes > (int)NV || g->blank_id < 0 || g->blank_id >= (int)NV) return 0;
+    const size_t PH = (size_t)g->pred_hidden, JH = (size_t)g->joint_hidden, NV = (size_t)g->vocab_size + 1;
+    if (g->pred_layers != 2 || PH % 16 || JH % 16 || g->num_classes > (int)NV || g->blank_id < 0 || g->blank_id >= (int)NV) return 0;
     int fail = 0;
-    e->dec_w0i = dalloc(4 * PH * 2 * PH * 2, &fail);
-    e->dec_w1i = dalloc(4 * PH * 2 * PH * 2, &fail);
-    e->dec_b0i = dalloc(4 * PH * 4, &fail);
+    uint16_t *w0i = dalloc(4 * PH * 2 * PH * 2, &fail), *w1i = dalloc(4 * PH * 2 * PH * 2, &fail);
+    float *b0i = dalloc(4 * PH * 4, &fail);
     e->dec_b1i = dalloc(4 * PH * 4, &fail);
     e->dec_table = dalloc(NV * 4 * PH * 4, &fail);
-    if (fail) { snprintf(err, errlen, "out of device memory for the decoder tables"); return -1; }
-    if (nb_dec_interleave(m->lstm_w[0], e->dec_w0i, m->lstm_b[0], e->dec_b0i, (int)PH, (int)(2 * PH), e->st) ||
-        nb_dec_interleave(m->lstm_w[1], e->dec_w1i, m->lstm_b[1], e->dec_b1i, (int)PH, (int)(2 * PH), e->st) ||
-        nb_dec_gate_table(e->dec_w0i, (int64_t)(2 * PH), m->embed, (int)NV, (int)PH, e->dec_b0i, g->blank_id, e->dec_table, e->st) ||
-        cudaStreamSynchronize(e->st) != cudaSuccess) {
-        snprintf(err, errlen, "decoder tables: %s", nemo_gpu_last_error());
+    e->dec_wg1 = dalloc(8 * PH * PH * 2, &fail);
+    e->dec_wg2 = dalloc((JH + 4 * PH) * PH * 2, &fail);
+    e->dec_r0 = dalloc((size_t)e->B * 4 * PH * 4, &fail);
+    e->dec_r1 = dalloc((size_t)e->B * 4 * PH * 4, &fail);
+    int rc = fail ? -1 : 0;
+    const size_t row = PH * 2;  /* bytes of PH bf16 */
+    if (!rc)
+        rc = nb_dec_interleave(m->lstm_w[0], w0i, m->lstm_b[0], b0i, (int)PH, (int)(2 * PH), e->st) ||
+             nb_dec_interleave(m->lstm_w[1], w1i, m->lstm_b[1], e->dec_b1i, (int)PH, (int)(2 * PH), e->st) ||
+             nb_dec_gate_table(w0i, (int64_t)(2 * PH), m->embed, (int)NV, (int)PH, b0i, g->blank_id, e->dec_table, e->st) ||
+             cudaMemcpy2DAsync(e->dec_wg1, row, w1i, 2 * row, row, 4 * PH, cudaMemcpyDeviceToDevice, e->st) != cudaSuccess ||
+             cudaMemcpy2DAsync(e->dec_wg1 + 4 * PH * PH, row, w0i + PH, 2 * row, row, 4 * PH, cudaMemcpyDeviceToDevice, e->st) != cudaSuccess ||
+             cudaMemcpyAsync(e->dec_wg2, m->joint_pred_w, JH * row, cudaMemcpyDeviceToDevice, e->st) != cudaSuccess ||
+             cudaMemcpy2DAsync(e->dec_wg2 + JH * PH, row, w1i + PH, 2 * row, row, 4 * PH, cudaMemcpyDeviceToDevice, e->st) != cudaSuccess ||
+             cudaStreamSynchronize(e->st) != cudaSuccess;
+    if (w0i) cudaFree(w0i);
+    if (w1i) cudaFree(w1i);
+    if (b0i) cudaFree(b0i);
+    if (rc) {
+        snprintf(err, errlen, "decoder tables: %s", fail ? "out of device memory" : nemo_gpu_last_error());
         return -1;
     }
     e->dec_fused = 1;
@@ -341,7 +357,7 @@ void nb_engine_destroy(nb_engine_t *e) {
     if (e->ev1) cudaEventDestroy(e->ev1);
     for (int i = 0; i < e->ngraphs; ++i) cudaGraphExecDestroy(e->graphs[i].exec);
     free(e->enc1_layers);
-    void *dt[] = { e->dec_w0i, e->dec_w1i, e->dec_b0i, e->dec_b1i, e->dec_table };
+    void *dt[] = { e->dec_wg1, e->dec_wg2, e->dec_b1i, e->dec_table, e->dec_r0, e->dec_r1 };
     for (size_t i = 0; i < sizeof dt / sizeof *dt; ++i) if (dt[i]) cudaFree(dt[i]);
     if (e->h_span) cudaFreeHost(e->h_span);
     if (e->d_span) cudaFree(e->d_span);
@@ -376,7 +392,11 @@ int nb_engine_reset(nb_engine_t *e, char *err, size_t errlen) {
             float *base = e->din + ((size_t)l * e->B + s) * (size_t)e->cap_rows * D;
             if (cudaMemsetAsync(base, 0, (size_t)e->conv_left * rowb, e->st) != cudaSuccess) { snprintf(err, errlen, "reset failed"); return -1; }
         }
-    if (nb_dec_reset(&e->dec, e->m->g.pred_hidden, e->m->g.blank_id, e->st)) { snprintf(err, errlen, "%s", nemo_gpu_last_error()); return -1; }
+    if (nb_dec_reset(&e->dec, e->m->g.pred_hidden, e->m->g.blank_id, e->st) ||
+        (e->dec_fused && nb_dec_rows_init(e->dec_r0, e->dec_r1, e->dec_b1i, e->B, 4 * e->m->g.pred_hidden, e->st))) {
+        snprintf(err, errlen, "%s", nemo_gpu_last_error());
+        return -1;
+    }
     if (cudaStreamSynchronize(e->st) != cudaSuccess) { snprintf(err, errlen, "reset: %s", cudaGetErrorString(cudaGetLastError())); return -1; }
     return 0;
 }
@@ -604,13 +624,13 @@ static NbDecStep dec_step_args(const nb_engine_t *e) {
     memset(&s, 0, sizeof s);
     s.logits = d->logits; s.ldl = logits_ld(g); s.V = g->num_classes; s.blank = g->blank_id; s.max_symbols = g->max_symbols;
     s.PH = g->pred_hidden; s.JH = g->joint_hidden; s.enc = e->joint_enc;
-    s.A0 = (uint16_t *)d->A0; s.a0_ld = g->pred_hidden; s.a0_plane = d->a_plane;
-    s.A1 = (uint16_t *)d->A1; s.a1_ld = 2 * g->pred_hidden; s.a1_plane = d->a_plane;
+    s.T = e->dec_table; s.R0 = e->dec_r0; s.c0 = d->c;
+    s.A = (uint16_t *)d->A0; s.a_ld = g->pred_hidden; s.a_plane = d->a_plane;
     s.X = d->jx; s.x_plane = (int64_t)e->B * g->joint_hidden;
     return s;
 }
 
-/* One fused greedy iteration (see NbDecEpi): four GEMMs with decoder epilogues and the step. */
+/* One fused greedy iteration (see NbDecEpi): three GEMMs with decoder epilogues and the step. */
 static int dec_fused_body(nb_engine_t *e, int c, unsigned long long cond) {
     const nb_model_t *m = e->m;
     const nb_config_t *g = &m->g;
@@ -624,28 +644,23 @@ static int dec_fused_body(nb_engine_t *e, int c, unsigned long long cond) {
     NbDecEpi de;
     memset(&de, 0, sizeof de);
     de.mode = 1;
+    de.n_split = 4 * PH;
     de.need_idx = d->need_idx;
-    de.last_token = d->last_token;
-    de.table = e->dec_table;
-    de.c_in = d->c; de.c_out = d->cp; de.h_out = d->hp;
-    de.next = (uint16_t *)d->A1; de.next_ld = 2 * PH; de.next_plane = d->a_plane;
-    nemo_gemm_args_t a = gemm_args(d->A0, PH, NEMO_FMT_BF16X2, d->a_plane, e->dec_w0i + PH, 2 * PH, NULL, NULL, 0, B, 4 * PH, PH, 0, 0, 1.0f);
-    a.dynM = d->cnt;
-    KL(nb_gemm_dec(&a, &de, st));
-    const int64_t l1 = (int64_t)B * PH;
-    de.last_token = NULL; de.table = NULL;
-    de.c_in = d->c + l1; de.c_out = d->cp + l1; de.h_out = d->hp + l1;
+    de.row = e->dec_r1;
+    de.c = d->c + (int64_t)B * PH;
     de.next = (uint16_t *)d->hp1c; de.next_ld = PH; de.next_plane = d->h_plane;
-    a = gemm_args(d->A1, 2 * PH, NEMO_FMT_BF16X2, d->a_plane, e->dec_w1i, 2 * PH, e->dec_b1i, NULL, 0, B, 4 * PH, 2 * PH, 0, 0, 1.0f);
+    de.aux = e->dec_r0;
+    nemo_gemm_args_t a = gemm_args(d->A0, PH, NEMO_FMT_BF16X2, d->a_plane, e->dec_wg1, PH, NULL, NULL, 0, B, 8 * PH, PH, 0, 0, 1.0f);
     a.dynM = d->cnt;
     KL(nb_gemm_dec(&a, &de, st));
-    NbDecEpi dp;
-    memset(&dp, 0, sizeof dp);
-    dp.mode = 2;
-    dp.need_idx = d->need_idx; dp.enc = e->joint_enc; dp.erow = d->erow; dp.pred = d->pred; dp.X = d->jx; dp.x_plane = s.x_plane;
-    a = gemm_args(d->hp1c, PH, NEMO_FMT_BF16X2, d->h_plane, m->joint_pred_w, PH, m->joint_pred_b, NULL, 0, B, JH, PH, 0, 0, 1.0f);
+    memset(&de, 0, sizeof de);
+    de.mode = 2;
+    de.n_split = JH;
+    de.need_idx = d->need_idx; de.enc = e->joint_enc; de.erow = d->erow; de.pred = d->pred; de.X = d->jx; de.x_plane = s.x_plane;
+    de.aux = e->dec_r1; de.aux_bias = e->dec_b1i;
+    a = gemm_args(d->hp1c, PH, NEMO_FMT_BF16X2, d->h_plane, e->dec_wg2, PH, m->joint_pred_b, NULL, 0, B, JH + 4 * PH, PH, 0, 0, 1.0f);
     a.dynM = d->cnt;
-    KL(nb_gemm_dec(&a, &dp, st));
+    KL(nb_gemm_dec(&a, &de, st));
     nemo_gemm_args_t j = gemm_args(d->jx, JH, NEMO_FMT_BF16X2, s.x_plane, m->joint_out_w, JH, m->joint_out_b, d->logits, logits_ld(g), B,
                                    g->num_classes, JH, 0, 0, 1.0f);
     KL(nemo_gemm(&j, st));

@@ -97,28 +97,38 @@ int nb_dec_joint_in(const DecState *d, const float *enc, int JH, uint16_t *X, in
 int nb_dec_reset(const DecState *d, int PH, int blank, void *stream);
 
 /* ---- fused batched greedy decoder (activation-major tensor-core GEMMs with decoder epilogues) --
-   One iteration is four GEMMs and one step kernel:
-     gates0 = table[last_token] + W0h . h0   -> LSTM cell 0 in the epilogue -> A1[:, 0:PH)
-     gates1 = b1 + W1 . [h0' | h1]           -> LSTM cell 1 in the epilogue -> hp1c
-     pred   = bp + Wp . h1'                  -> pred[b], X[b] = relu(enc[erow[b]] + pred) in the epilogue
-     logits = bo + Wo . X                    -> the step kernel: argmax, commit, next iteration's rows
    The LSTM weights are gate-interleaved (row 4u + g holds gate g of unit u, gates i, f, g, o), so
-   each 16-column epilogue chunk holds all four gates of 4 units. table[v] = b0 + W0x . embed[v]
-   (the input half of layer 0 for every token; the blank row is b0 alone, blank feeding zeros). */
+   each 16-column epilogue chunk holds all four gates of 4 units. A stream runs the prediction
+   network only right after it emitted a token, and the state it then commits is the provisional
+   state of its last prediction run; so the recurrent halves W0h . h0 and W1h . h1 of its next
+   run are computed as soon as that state exists, by the GEMMs that read h0' and h1' anyway
+   (their weight rows concatenated), and kept per stream as R0 = W0h . h0, R1 = b1 + W1h . h1.
+   One iteration, for the streams listed (rows of the compact GEMMs):
+     step kernel:  gates0 = T[token] + R0[b] -> cell 0 (c0)        -> h0' into the G1 input row
+     G1:  [W1x ; W0h] . h0'   -> gates1 = . + R1[b] -> cell 1 (c1) -> h1' into the G2 input row
+                              -> R0[b] = W0h . h0'
+     G2:  [Wp ; W1h] . h1'    -> pred[b] = bp + ., X[b] = relu(enc[erow[b]] + pred[b])
+                              -> R1[b] = b1 + W1h . h1'
+     G3:  Wo . X              -> logits; the step kernel takes each active stream's argmax.
+   T[v] = b0 + W0x . embed[v] (blank's row is b0: blank feeds zeros). The cell state c of each
+   layer is kept once per stream: it is read and rewritten by the same run, which always follows
+   the commit of the previous run's state. */
 typedef struct {
     int mode;                 /* 1: LSTM cell; 2: prediction + joint input */
+    int n_split;              /* columns [0, n_split) take the cell / prediction; [n_split, N) go to aux */
     const int *need_idx;      /* GEMM row -> stream */
-    const int *last_token;    /* mode 1 with a table: row of the table each stream adds */
-    const float *table;       /* mode 1: [V][4PH] per-token gate rows used instead of the bias, or NULL */
-    const float *c_in;        /* mode 1: [streams][PH] committed cell state of the layer */
-    float *c_out, *h_out;     /* mode 1: [streams][PH] provisional state of the layer */
-    uint16_t *next;           /* mode 1: next GEMM input, row m, columns [0, PH), bf16 hi/lo planes */
+    const int *last_token;    /* mode 1: if set, the gate row of stream b is row[last_token[b]], else row[b] */
+    const float *row;         /* mode 1: [.][n_split] gate rows added to the product (bias included) */
+    float *c;                 /* mode 1: [streams][n_split / 4] cell state, read and rewritten */
+    uint16_t *next;           /* mode 1: next GEMM input, row m, columns [0, n_split / 4): bf16 hi/lo planes */
     int64_t next_ld, next_plane;
-    const float *enc;         /* mode 2: [rows][N] joint encoder rows; erow[b] selects the row */
+    const float *enc;         /* mode 2: [rows][n_split] joint encoder rows; erow[b] selects the row */
     const int *erow;
-    float *pred;              /* mode 2: [streams][N] */
-    uint16_t *X;              /* mode 2: [streams][N] joint input, bf16 hi/lo planes */
+    float *pred;              /* mode 2: [streams][n_split] */
+    uint16_t *X;              /* mode 2: [streams][n_split] joint input, bf16 hi/lo planes */
     int64_t x_plane;
+    float *aux;               /* [streams][N - n_split]: aux[b][n - n_split] = product (+ aux_bias) */
+    const float *aux_bias;
 } NbDecEpi;
 
 /* Tensor-core GEMM (activation-major tiles) with a decoder epilogue instead of the plain one. */
@@ -129,17 +139,22 @@ typedef struct {
     int64_t ldl;
     int V, blank, max_symbols, PH, JH;
     const float *enc;         /* [streams * c][JH] joint encoder rows of the chunk */
-    uint16_t *A0, *A1, *X;    /* next iteration's inputs: h0 rows [.][a0_ld], h1 at A1[., PH..2PH), joint input rows */
-    int64_t a0_ld, a0_plane, a1_ld, a1_plane, x_plane;
+    const float *T, *R0;      /* [V][4PH] token gate rows of layer 0, [streams][4PH] recurrent part */
+    float *c0;                /* [streams][PH] layer-0 cell state */
+    uint16_t *A, *X;          /* G1 input rows (h0', compact) and joint input rows (per stream) */
+    int64_t a_ld, a_plane, x_plane;
 } NbDecStep;
 
-/* Chunk start: per-stream counters, the rows of the streams whose prediction is stale, and the
-   joint input of the others. cnt[0] = streams listed, cnt[1] = streams active, cnt[2] = 0. */
+/* Chunk start: per-stream counters, layer 0 of the streams whose prediction is stale (their G1
+   input rows) and the joint input of the others. cnt[0] = streams listed, cnt[1] = streams
+   active, cnt[2] = 0. */
 int nb_dec_chunk_start(const DecState *d, const NbDecStep *s, int c, void *stream);
 /* One greedy decision per active stream from its logits row, then the next iteration's rows as
    at chunk start; the last block publishes cnt[0], cnt[1], counts the iteration in cnt[2] and
    sets the WHILE condition (cond != 0). */
 int nb_dec_step(const DecState *d, const NbDecStep *s, int c, int max_it, unsigned long long cond, void *stream);
+/* R0[b] = 0 and R1[b] = b1 for every stream (the recurrent gate parts of a zero state). */
+int nb_dec_rows_init(float *R0, float *R1, const float *b1, int streams, int W, void *stream);
 /* Gate-interleaved copy of an LSTM layer [4PH][K] (and its bias when given). */
 int nb_dec_interleave(const uint16_t *W, uint16_t *Wi, const float *bias, float *bi, int PH, int K, void *stream);
 /* table[v][n] = bi[n] + sum_{k < PH} Wi[n][k] * embed[v][k] (fp32, k ascending); row blank = bi. */

@@ -200,10 +200,9 @@ __global__ void dec_joint_in_kernel(DecState d, const float *__restrict__ enc, i
 
 // ---- fused batched greedy decoder -------------------------------------------------------------
 
-constexpr int STEP_T = 160;  // threads of the per-stream kernels: 4 consecutive elements each for 640-wide rows
+constexpr int STEP_T = 160;  // threads of the per-stream kernels: 4 consecutive units / elements each for 640-wide rows
 
 __device__ __forceinline__ float4 ld4(const float *p) { return *(const float4 *)p; }
-__device__ __forceinline__ void st4(float *p, float4 v) { *(float4 *)p = v; }
 
 // bf16 hi/lo planes of 4 consecutive values (idx a multiple of 4, plane a multiple of 4)
 __device__ __forceinline__ void put4_planes(uint16_t *base, int64_t plane, int64_t idx, float4 v) {
@@ -217,17 +216,33 @@ __device__ __forceinline__ float4 relu_add4(float4 a, float4 b) {
     return make_float4(fmaxf(a.x + b.x, 0.0f), fmaxf(a.y + b.y, 0.0f), fmaxf(a.z + b.z, 0.0f), fmaxf(a.w + b.w, 0.0f));
 }
 
-// The next iteration's rows of stream b: listed (its prediction is stale) -> h0 into A0 row pos and
-// h1 into A1 row pos at columns [PH, 2PH); otherwise, while active, its joint input row.
-// h0/h1 are read from `hsrc` (the committed state). pos < 0: not listed.
-__device__ __forceinline__ void stream_rows(const DecState &d, const NbDecStep &s, int b, int pos, bool act, int er, const float *h0src,
-                                            const float *h1src) {
+// One LSTM unit (src/kernels.metal:475-486) from its gates i, f, g, o and cell state.
+__device__ __forceinline__ float lstm_unit(float gi, float gf, float gg, float go, float &c) {
+    const float ig = nb::sigmoid_f(gi), fg = nb::sigmoid_f(gf), g = tanhf(gg), og = nb::sigmoid_f(go);
+    c = fg * c + ig * g;
+    return og * tanhf(c);
+}
+
+// The next iteration's work of stream b. Listed (pos >= 0: it emitted, its prediction is stale):
+// layer 0 of the prediction network, gates = T[token] + R0[b] (gate-interleaved), its cell state
+// updated and h0' written to G1 input row pos. Otherwise, while active: its joint input row
+// relu(enc[er] + pred[b]). The element loads are issued before the first store.
+__device__ __forceinline__ void stream_rows(const DecState &d, const NbDecStep &s, int b, int tok, int pos, bool act, int er) {
     const int tid = threadIdx.x;
     if (pos >= 0) {
-        for (int j = tid * 4; j < s.PH; j += STEP_T * 4) {
-            const float4 h0 = ld4(h0src + j), h1 = ld4(h1src + j);
-            put4_planes(s.A0, s.a0_plane, (int64_t)pos * s.a0_ld + j, h0);
-            put4_planes(s.A1, s.a1_plane, (int64_t)pos * s.a1_ld + s.PH + j, h1);
+        const float *tr = s.T + (int64_t)tok * 4 * s.PH, *rr = s.R0 + (int64_t)b * 4 * s.PH;
+        float *c0 = s.c0 + (int64_t)b * s.PH;
+        for (int u = tid * 4; u < s.PH; u += STEP_T * 4) {
+            float4 t[4], r[4];
+#pragma unroll
+            for (int q = 0; q < 4; ++q) { t[q] = ld4(tr + 4 * u + 4 * q); r[q] = ld4(rr + 4 * u + 4 * q); }
+            float4 c = ld4(c0 + u), h;
+            h.x = lstm_unit(t[0].x + r[0].x, t[0].y + r[0].y, t[0].z + r[0].z, t[0].w + r[0].w, c.x);
+            h.y = lstm_unit(t[1].x + r[1].x, t[1].y + r[1].y, t[1].z + r[1].z, t[1].w + r[1].w, c.y);
+            h.z = lstm_unit(t[2].x + r[2].x, t[2].y + r[2].y, t[2].z + r[2].z, t[2].w + r[2].w, c.z);
+            h.w = lstm_unit(t[3].x + r[3].x, t[3].y + r[3].y, t[3].z + r[3].z, t[3].w + r[3].w, c.w);
+            *(float4 *)(c0 + u) = c;
+            put4_planes(s.A, s.a_plane, (int64_t)pos * s.a_ld + u, h);
         }
     } else if (act) {
         const float *p = d.pred + (int64_t)b * s.JH, *e = s.enc + (int64_t)er * s.JH;
@@ -256,6 +271,7 @@ __global__ void __launch_bounds__(STEP_T) dec_chunk_start_kernel(DecState d, NbD
     const int b = blockIdx.x;
     const bool act = c > 0;
     const bool need = act && !d.pred_valid[b];
+    const int tok = d.last_token[b];
     if (threadIdx.x == 0) {
         s_pos = need ? atomicAdd(&d.cnt[4], 1) : -1;
         d.t[b] = 0;
@@ -268,14 +284,14 @@ __global__ void __launch_bounds__(STEP_T) dec_chunk_start_kernel(DecState d, NbD
         if (act) atomicAdd(&d.cnt[6], 1);
     }
     __syncthreads();
-    stream_rows(d, s, b, s_pos, act, b * c, d.h + (int64_t)b * s.PH, d.h + ((int64_t)d.streams + b) * s.PH);
+    stream_rows(d, s, b, (tok >= 0 && tok < s.V) ? tok : s.blank, s_pos, act, b * c);
     if (threadIdx.x == 0) publish(d, true, 0, 0);
 }
 
 // One greedy step per active stream (src/decoder.c:104-122) from its logits row: argmax with ties
-// to the lowest index (src/kernels.metal:521-550); blank -> next frame; token -> emit, commit the
-// provisional LSTM state, re-score the same frame unless max_symbols tokens came from it. Then
-// the stream's rows for the next iteration (stream_rows).
+// to the lowest index (src/kernels.metal:521-550); blank -> next frame; token -> emit (its
+// provisional LSTM state becomes the committed one), re-score the same frame unless max_symbols
+// tokens came from it. Then the stream's work for the next iteration (stream_rows).
 __global__ void __launch_bounds__(STEP_T) dec_step_kernel(DecState d, NbDecStep s, int c, int max_it, cudaGraphConditionalHandle cond) {
     nb::pdl_wait();
     __shared__ float rv[STEP_T / 32];
@@ -321,7 +337,7 @@ __global__ void __launch_bounds__(STEP_T) dec_step_kernel(DecState d, NbDecStep 
         __syncthreads();
     }
     // an index outside the vocabulary (only if every logit were NaN) is taken as blank, so no
-    // table or embedding row beyond the vocabulary is ever read
+    // table row beyond the vocabulary is ever read
     const int k = (s_k >= 0 && s_k < s.V) ? s_k : s.blank;
     const bool emit = k != s.blank;
     if (!emit) {
@@ -333,7 +349,6 @@ __global__ void __launch_bounds__(STEP_T) dec_step_kernel(DecState d, NbDecStep 
     }
     const bool act = t < c;
     const bool need = emit && act;
-    const int64_t s0 = (int64_t)b * s.PH, s1 = ((int64_t)d.streams + b) * s.PH;
     if (tid == 0) {
         s_pos = need ? atomicAdd(&d.cnt[4], 1) : -1;
         d.idx[b] = k;
@@ -351,18 +366,19 @@ __global__ void __launch_bounds__(STEP_T) dec_step_kernel(DecState d, NbDecStep 
         if (need) d.need_idx[s_pos] = b;
         if (act) atomicAdd(&d.cnt[6], 1);
     }
-    if (emit) {
-        // commit the provisional state of both layers (src/decoder.c:115-118)
-        for (int j = tid * 4; j < s.PH; j += STEP_T * 4) {
-            st4(d.h + s0 + j, ld4(d.hp + s0 + j));
-            st4(d.h + s1 + j, ld4(d.hp + s1 + j));
-            st4(d.c + s0 + j, ld4(d.cp + s0 + j));
-            st4(d.c + s1 + j, ld4(d.cp + s1 + j));
-        }
-    }
     __syncthreads();
-    stream_rows(d, s, b, s_pos, act, b * c + t, d.hp + s0, d.hp + s1);
+    stream_rows(d, s, b, k, s_pos, act, b * c + t);
     if (tid == 0) publish(d, false, max_it, cond);
+}
+
+// Recurrent gate parts of a zero state: R0[b] = 0, R1[b] = b1 (both [streams][W]).
+__global__ void dec_rows_init_kernel(float *R0, float *R1, const float *__restrict__ b1, int W) {
+    nb::pdl_wait();
+    const int b = blockIdx.x;
+    for (int n = threadIdx.x; n < W; n += blockDim.x) {
+        R0[(int64_t)b * W + n] = 0.0f;
+        R1[(int64_t)b * W + n] = b1[n];
+    }
 }
 
 // Gate-interleaved copy: row 4u + g of Wi is row g * PH + u of W.
@@ -454,4 +470,8 @@ extern "C" int nb_dec_gate_table(const uint16_t *Wi, int64_t ldw, const uint16_t
     const int N = 4 * PH;
     nb::launch(gate_table_kernel, dim3((N + 255) / 256, V), 256, 0, (cudaStream_t)stream, Wi, ldw, embed, PH, bi, blank, table, N);
     return nb_check_launch("gate_table_kernel");
+}
+extern "C" int nb_dec_rows_init(float *R0, float *R1, const float *b1, int streams, int W, void *stream) {
+    nb::launch(dec_rows_init_kernel, streams, 256, 0, (cudaStream_t)stream, R0, R1, b1, W);
+    return nb_check_launch("dec_rows_init_kernel");
 }

@@ -428,17 +428,17 @@ __device__ __forceinline__ void epi16(const TcArgs &p, int64_t rowbase, int64_t 
 
 // Batched greedy decoder epilogues: 16 output columns of GEMM row m, whose stream is b.
 // LSTM cell (src/kernels.metal:475-486) on gate-interleaved columns: columns n0 .. n0 + 15 are
-// gates i, f, g, o of units n0 / 4 .. n0 / 4 + 3. `bias` is the bias row or the stream's table row.
-__device__ __forceinline__ void dec_lstm16(const NbDecEpi &de, const float *__restrict__ bias, int m, int b, int ph, int n0, const float (&va)[16]) {
-    const int u0 = n0 >> 2;
+// gates i, f, g, o of units n0 / 4 .. n0 / 4 + 3; `row` is the stream's gate row (bias included).
+__device__ __forceinline__ void dec_lstm16(const NbDecEpi &de, const float *__restrict__ row, int m, int b, int n0, const float (&va)[16]) {
+    const int u0 = n0 >> 2, ph = de.n_split >> 2;
     float g[16];
 #pragma unroll
     for (int x = 0; x < 16; x += 4) {
-        const float4 b4 = __ldg((const float4 *)(bias + n0 + x));
+        const float4 b4 = *(const float4 *)(row + n0 + x);
         g[x] = va[x] + b4.x; g[x + 1] = va[x + 1] + b4.y; g[x + 2] = va[x + 2] + b4.z; g[x + 3] = va[x + 3] + b4.w;
     }
-    const int64_t sb = (int64_t)b * ph + u0;
-    const float4 c4 = *(const float4 *)(de.c_in + sb);
+    float *cp = de.c + (int64_t)b * ph + u0;
+    const float4 c4 = *(const float4 *)cp;
     const float cold[4] = { c4.x, c4.y, c4.z, c4.w };
     float cc[4], hh[4];
 #pragma unroll
@@ -447,8 +447,7 @@ __device__ __forceinline__ void dec_lstm16(const NbDecEpi &de, const float *__re
         cc[q] = fg * cold[q] + ig * gg;
         hh[q] = og * tanhf(cc[q]);
     }
-    *(float4 *)(de.c_out + sb) = make_float4(cc[0], cc[1], cc[2], cc[3]);
-    *(float4 *)(de.h_out + sb) = make_float4(hh[0], hh[1], hh[2], hh[3]);
+    *(float4 *)cp = make_float4(cc[0], cc[1], cc[2], cc[3]);
     uint32_t hi[2], lo[2];
 #pragma unroll
     for (int x = 0; x < 2; ++x) {
@@ -462,9 +461,10 @@ __device__ __forceinline__ void dec_lstm16(const NbDecEpi &de, const float *__re
     *(uint2 *)(de.next + idx + de.next_plane) = make_uint2(lo[0], lo[1]);
 }
 
-// Prediction projection row of stream b (pred = bias + acc) and its joint input
+// Prediction projection row of stream b (pred = bias + acc, n_split columns) and its joint input
 // X[b] = relu(enc[er] + pred) as bf16 hi/lo planes.
-__device__ __forceinline__ void dec_joint16(const NbDecEpi &de, const float *__restrict__ bias, int b, int er, int N, int n0, const float (&va)[16]) {
+__device__ __forceinline__ void dec_joint16(const NbDecEpi &de, const float *__restrict__ bias, int b, int er, int n0, const float (&va)[16]) {
+    const int N = de.n_split;
     float v[16], x[16];
 #pragma unroll
     for (int q = 0; q < 16; q += 4) {
@@ -489,6 +489,18 @@ __device__ __forceinline__ void dec_joint16(const NbDecEpi &de, const float *__r
     *(uint4 *)(de.X + idx + 8) = make_uint4(hi[4], hi[5], hi[6], hi[7]);
     *(uint4 *)(de.X + idx + de.x_plane) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
     *(uint4 *)(de.X + idx + de.x_plane + 8) = make_uint4(lo[4], lo[5], lo[6], lo[7]);
+}
+
+// Columns at or past n_split: the stream's aux row (product plus aux_bias).
+__device__ __forceinline__ void dec_aux16(const NbDecEpi &de, int N, int b, int n0, const float (&va)[16]) {
+    const int w = N - de.n_split, col = n0 - de.n_split;
+    float *dst = de.aux + (int64_t)b * w + col;
+#pragma unroll
+    for (int q = 0; q < 16; q += 4) {
+        float4 b4 = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (de.aux_bias) b4 = __ldg((const float4 *)(de.aux_bias + col + q));
+        *(float4 *)(dst + q) = make_float4(va[q] + b4.x, va[q + 1] + b4.y, va[q + 2] + b4.z, va[q + 3] + b4.w);
+    }
 }
 
 template <int BW>
@@ -610,7 +622,7 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tcr_kernel(const __grid_const
                 brow = (int64_t)g * p.e.bias_gstride;
                 if (p.de.mode) {
                     ds = p.de.need_idx[m];
-                    if (p.de.mode == 1 && p.de.table) dbias = p.de.table + (int64_t)p.de.last_token[ds] * p.N;
+                    if (p.de.mode == 1) dbias = p.de.row + (int64_t)(p.de.last_token ? p.de.last_token[ds] : ds) * p.de.n_split;
                     if (p.de.mode == 2) der = p.de.erow[ds];
                 }
             }
@@ -669,8 +681,12 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tcr_kernel(const __grid_const
                     const int n0 = n_base + jj0;
                     if (n0 >= nout) continue;
                     const int cnt = min(16, nout - n0);
-                    if (p.de.mode == 1) { dec_lstm16(p.de, dbias, m, ds, p.N >> 2, n0, va); continue; }
-                    if (p.de.mode == 2) { dec_joint16(p.de, dbias, ds, der, p.N, n0, va); continue; }
+                    if (p.de.mode) {
+                        if (n0 >= p.de.n_split) dec_aux16(p.de, p.N, ds, n0, va);
+                        else if (p.de.mode == 1) dec_lstm16(p.de, dbias, m, ds, n0, va);
+                        else dec_joint16(p.de, dbias, ds, der, n0, va);
+                        continue;
+                    }
                     if (p.vec && cnt == 16) {
                         // 16-byte accesses (alignment of every pointer and stride checked on the host),
                         // the activation / output format resolved at compile time
@@ -991,14 +1007,14 @@ extern "C" int nb_gemm_dec(const nemo_gemm_args_t *a, const NbDecEpi *de, void *
     if (!de || (de->mode != 1 && de->mode != 2)) return nb_set_error("decoder GEMM: unknown epilogue mode");
     if (a->a_fmt != NEMO_FMT_BF16X2 || a->act != NEMO_ACT_NONE || a->accumulate || a->K % 8 || a->N % 16)
         return nb_set_error("decoder GEMM: needs bf16 hi/lo activations, no activation or accumulation, K %% 8 == 0 and N %% 16 == 0");
-    const float *bias = de->mode == 1 && de->table ? de->table : a->bias;
-    if (!bias || ((uintptr_t)bias & 15) || !de->need_idx) return nb_set_error("decoder GEMM: needs a 16-byte aligned bias or table and the row list");
-    if (de->mode == 1 && ((a->N & 3) || !de->c_in || !de->c_out || !de->h_out || !de->next || (de->table && !de->last_token) ||
-                          (((uintptr_t)de->c_in | (uintptr_t)de->c_out | (uintptr_t)de->h_out) & 15) || ((uintptr_t)de->next & 7) ||
-                          (a->N / 4) % 4 || de->next_ld % 4 || de->next_plane % 4))
+    const int ns = de->n_split;
+    if (ns <= 0 || ns > a->N || ns % 16 || !de->need_idx || (ns < a->N && (!de->aux || ((uintptr_t)de->aux & 15) || ((uintptr_t)de->aux_bias & 15))))
+        return nb_set_error("decoder GEMM: bad column split or aux output");
+    if (de->mode == 1 && (!de->row || !de->c || !de->next || (((uintptr_t)de->row | (uintptr_t)de->c) & 15) || ((uintptr_t)de->next & 7) ||
+                          de->next_ld % 4 || de->next_plane % 4))
         return nb_set_error("decoder GEMM: LSTM epilogue operands misaligned or missing");
-    if (de->mode == 2 && (!de->enc || !de->erow || !de->pred || !de->X || (((uintptr_t)de->enc | (uintptr_t)de->pred | (uintptr_t)de->X) & 15) ||
-                          de->x_plane % 8))
+    if (de->mode == 2 && (!a->bias || ((uintptr_t)a->bias & 15) || !de->enc || !de->erow || !de->pred || !de->X ||
+                          (((uintptr_t)de->enc | (uintptr_t)de->pred | (uintptr_t)de->X) & 15) || de->x_plane % 8))
         return nb_set_error("decoder GEMM: joint epilogue operands misaligned or missing");
     return launch_rows(a, (cudaStream_t)stream, de);
 }
