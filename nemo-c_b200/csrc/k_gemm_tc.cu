@@ -1019,10 +1019,15 @@ extern "C" int nb_gemm_dec(const nemo_gemm_args_t *a, const NbDecEpi *de, void *
     return launch_rows(a, (cudaStream_t)stream, de);
 }
 
+extern "C" int nb_attention_device_error(void);
+
 extern "C" int nemo_gpu_check_device_errors(void) {
     int v = 0;
     if (cudaMemcpyFromSymbol(&v, g_tc_error, sizeof v) != cudaSuccess) return nb_set_error("cannot read the device error flag");
     if (v) return nb_set_error("tensor-core GEMM: a bounded wait gave up (code %d)", v);
+    const int a = nb_attention_device_error();
+    if (a < 0) return nb_set_error("cannot read the attention error flag");
+    if (a) return nb_set_error("attention: a bounded wait for the window's rows gave up");
     return 0;
 }
 

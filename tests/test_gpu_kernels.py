@@ -181,7 +181,8 @@ def test_attention_over_cache(c, cache_len):
     for s in range(streams):
         win = kv[s, pos - cache_len:pos + c]
         ref = orc.attention_rel(kv[s, pos:pos + c, :D], win[:, D:2 * D], win[:, 2 * D:], P, bu, bv, c, L, Lmax, H, dh)
-        assert rel_err(got[s], ref) < FP32_TOL
+        # score and value products on the tensor cores with both operands split into bf16 hi + lo
+        assert rel_err(got[s], ref) < BF16X2_TOL
 
 
 def test_dwconv_ln_silu():
