@@ -61,11 +61,12 @@ __device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], 
                  : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
-// The three products of split operands into three accumulators (hi.hi, lo.hi, hi.lo): independent
-// chains, so consecutive MMAs of a warp overlap instead of waiting on one another.
+// The four products of split operands into three accumulators (hi.hi; lo.hi; hi.lo and lo.lo):
+// independent chains, so consecutive MMAs of a warp overlap instead of waiting on one another.
 __device__ __forceinline__ void mma3(float (&d)[3][4], const uint32_t (&ah)[4], const uint32_t (&al)[4], const uint32_t (&bh)[2], const uint32_t (&bl)[2]) {
     mma16816(d[0], ah, bh[0], bh[1]);
     mma16816(d[1], al, bh[0], bh[1]);
+    mma16816(d[2], al, bl[0], bl[1]);
     mma16816(d[2], ah, bl[0], bl[1]);
 }
 
