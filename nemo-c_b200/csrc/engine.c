@@ -76,6 +76,8 @@ struct nb_engine {
     float *dec_b1i;              /* interleaved b1 */
     float *dec_table;            /* [vocab + 1][4PH]: b0 + W0x . embed[v], interleaved */
     float *dec_r0, *dec_r1;      /* [B][4PH]: W0h . h0 and b1 + W1h . h1 of each stream's committed state */
+    float *dec_pv;               /* [B][dec_np]: joint argmax partials (value, column) per 128-column tile half */
+    int *dec_pi, dec_np;
     unsigned *d_enc1_bar;
     int *d_enc1_err;
     struct { int kind, k1, k2; cudaGraphExec_t exec; uint64_t kernels; } graphs[NB_MAX_GRAPHS];
@@ -153,6 +155,7 @@ static int dec_fused_setup(nb_engine_t *e, char *err, size_t errlen) {
     const nb_config_t *g = &m->g;
     const size_t PH = (size_t)g->pred_hidden, JH = (size_t)g->joint_hidden, NV = (size_t)g->vocab_size + 1;
     if (g->pred_layers != 2 || PH % 16 || JH % 16 || g->num_classes > (int)NV || g->blank_id < 0 || g->blank_id >= (int)NV) return 0;
+    if (2 * ((g->num_classes + 127) / 128) > 32) return 0;  /* the step kernel reduces the argmax partials within one warp */
     int fail = 0;
     uint16_t *w0i = dalloc(4 * PH * 2 * PH * 2, &fail), *w1i = dalloc(4 * PH * 2 * PH * 2, &fail);
     float *b0i = dalloc(4 * PH * 4, &fail);
@@ -162,6 +165,9 @@ static int dec_fused_setup(nb_engine_t *e, char *err, size_t errlen) {
     e->dec_wg2 = dalloc((JH + 4 * PH) * PH * 2, &fail);
     e->dec_r0 = dalloc((size_t)e->B * 4 * PH * 4, &fail);
     e->dec_r1 = dalloc((size_t)e->B * 4 * PH * 4, &fail);
+    e->dec_np = 2 * ((g->num_classes + 127) / 128);
+    e->dec_pv = dalloc((size_t)e->B * e->dec_np * 4, &fail);
+    e->dec_pi = dalloc((size_t)e->B * e->dec_np * 4, &fail);
     int rc = fail ? -1 : 0;
     const size_t row = PH * 2;  /* bytes of PH bf16 */
     if (!rc)
@@ -357,7 +363,7 @@ void nb_engine_destroy(nb_engine_t *e) {
     if (e->ev1) cudaEventDestroy(e->ev1);
     for (int i = 0; i < e->ngraphs; ++i) cudaGraphExecDestroy(e->graphs[i].exec);
     free(e->enc1_layers);
-    void *dt[] = { e->dec_wg1, e->dec_wg2, e->dec_b1i, e->dec_table, e->dec_r0, e->dec_r1 };
+    void *dt[] = { e->dec_wg1, e->dec_wg2, e->dec_b1i, e->dec_table, e->dec_r0, e->dec_r1, e->dec_pv, e->dec_pi };
     for (size_t i = 0; i < sizeof dt / sizeof *dt; ++i) if (dt[i]) cudaFree(dt[i]);
     if (e->h_span) cudaFreeHost(e->h_span);
     if (e->d_span) cudaFree(e->d_span);
@@ -625,6 +631,7 @@ static NbDecStep dec_step_args(const nb_engine_t *e) {
     s.logits = d->logits; s.ldl = logits_ld(g); s.V = g->num_classes; s.blank = g->blank_id; s.max_symbols = g->max_symbols;
     s.PH = g->pred_hidden; s.JH = g->joint_hidden; s.enc = e->joint_enc;
     s.T = e->dec_table; s.R0 = e->dec_r0; s.c0 = d->c;
+    s.part_v = e->dec_pv; s.part_i = e->dec_pi; s.nparts = e->dec_np;
     s.A = (uint16_t *)d->A0; s.a_ld = g->pred_hidden; s.a_plane = d->a_plane;
     s.X = d->jx; s.x_plane = (int64_t)e->B * g->joint_hidden;
     return s;
@@ -661,9 +668,14 @@ static int dec_fused_body(nb_engine_t *e, int c, unsigned long long cond) {
     a = gemm_args(d->hp1c, PH, NEMO_FMT_BF16X2, d->h_plane, e->dec_wg2, PH, m->joint_pred_b, NULL, 0, B, JH + 4 * PH, PH, 0, 0, 1.0f);
     a.dynM = d->cnt;
     KL(nb_gemm_dec(&a, &de, st));
-    nemo_gemm_args_t j = gemm_args(d->jx, JH, NEMO_FMT_BF16X2, s.x_plane, m->joint_out_w, JH, m->joint_out_b, d->logits, logits_ld(g), B,
-                                   g->num_classes, JH, 0, 0, 1.0f);
-    KL(nemo_gemm(&j, st));
+    /* joint logits reduced to (value, column) partials per 128-column tile half in the epilogue */
+    memset(&de, 0, sizeof de);
+    de.mode = 3;
+    de.n_split = g->num_classes;
+    de.part_v = e->dec_pv; de.part_i = e->dec_pi; de.part_ld = e->dec_np;
+    nemo_gemm_args_t j = gemm_args(d->jx, JH, NEMO_FMT_BF16X2, s.x_plane, m->joint_out_w, JH, m->joint_out_b, NULL, 0, B, g->num_classes, JH, 0, 0,
+                                   1.0f);
+    KL(nb_gemm_dec(&j, &de, st));
     KL(nb_dec_step(d, &s, c, dec_max_iterations(e, c), cond, st));
     if (!cond && cudaMemcpyAsync(e->h_cnt, d->cnt, 2 * sizeof(int), cudaMemcpyDeviceToHost, st) != cudaSuccess)
         return nb_set_error("decoder: %s", cudaGetErrorString(cudaGetLastError()));

@@ -114,7 +114,7 @@ int nb_dec_reset(const DecState *d, int PH, int blank, void *stream);
    layer is kept once per stream: it is read and rewritten by the same run, which always follows
    the commit of the previous run's state. */
 typedef struct {
-    int mode;                 /* 1: LSTM cell; 2: prediction + joint input */
+    int mode;                 /* 1: LSTM cell; 2: prediction + joint input; 3: per-row argmax of bias + product */
     int n_split;              /* columns [0, n_split) take the cell / prediction; [n_split, N) go to aux */
     const int *need_idx;      /* GEMM row -> stream */
     const int *last_token;    /* mode 1: if set, the gate row of stream b is row[last_token[b]], else row[b] */
@@ -129,6 +129,9 @@ typedef struct {
     int64_t x_plane;
     float *aux;               /* [streams][N - n_split]: aux[b][n - n_split] = product (+ aux_bias) */
     const float *aux_bias;
+    float *part_v;            /* mode 3: [rows][part_ld] best value of each (column tile, half), ties to */
+    int *part_i;              /*         the lowest column; and its column */
+    int part_ld;
 } NbDecEpi;
 
 /* Tensor-core GEMM (activation-major tiles) with a decoder epilogue instead of the plain one. */
@@ -139,6 +142,9 @@ typedef struct {
     int64_t ldl;
     int V, blank, max_symbols, PH, JH;
     const float *enc;         /* [streams * c][JH] joint encoder rows of the chunk */
+    const float *part_v;      /* if set: the logits' argmax comes as nparts partial (value, index) pairs per stream */
+    const int *part_i;
+    int nparts;
     const float *T, *R0;      /* [V][4PH] token gate rows of layer 0, [streams][4PH] recurrent part */
     float *c0;                /* [streams][PH] layer-0 cell state */
     uint16_t *A, *X;          /* G1 input rows (h0', compact) and joint input rows (per stream) */

@@ -250,6 +250,40 @@ __device__ __forceinline__ void stream_rows(const DecState &d, const NbDecStep &
     }
 }
 
+// stream_rows for rows of exactly 4 * STEP_T units / columns, with the decision-independent
+// operands (the recurrent gate part, the cell state, the kept prediction and the next frame's
+// encoder row) loaded before the decision was known.
+struct StreamPre {
+    float4 r[4], c, p, e;
+};
+__device__ __forceinline__ void stream_pre_load(const DecState &d, const NbDecStep &s, int b, int er_next, StreamPre &P) {
+    const int u = threadIdx.x * 4;
+    const float *rr = s.R0 + (int64_t)b * 4 * s.PH + 4 * u;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) P.r[q] = ld4(rr + 4 * q);
+    P.c = ld4(s.c0 + (int64_t)b * s.PH + u);
+    P.p = ld4(d.pred + (int64_t)b * s.JH + u);
+    P.e = ld4(s.enc + (int64_t)er_next * s.JH + u);
+}
+__device__ __forceinline__ void stream_rows_pre(const NbDecStep &s, int b, int tok, int pos, bool act, const StreamPre &P) {
+    const int u = threadIdx.x * 4;
+    if (pos >= 0) {
+        const float *tr = s.T + (int64_t)tok * 4 * s.PH + 4 * u;
+        float4 t[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) t[q] = ld4(tr + 4 * q);
+        float4 c = P.c, h;
+        h.x = lstm_unit(t[0].x + P.r[0].x, t[0].y + P.r[0].y, t[0].z + P.r[0].z, t[0].w + P.r[0].w, c.x);
+        h.y = lstm_unit(t[1].x + P.r[1].x, t[1].y + P.r[1].y, t[1].z + P.r[1].z, t[1].w + P.r[1].w, c.y);
+        h.z = lstm_unit(t[2].x + P.r[2].x, t[2].y + P.r[2].y, t[2].z + P.r[2].z, t[2].w + P.r[2].w, c.z);
+        h.w = lstm_unit(t[3].x + P.r[3].x, t[3].y + P.r[3].y, t[3].z + P.r[3].z, t[3].w + P.r[3].w, c.w);
+        *(float4 *)(s.c0 + (int64_t)b * s.PH + u) = c;
+        put4_planes(s.A, s.a_plane, (int64_t)pos * s.a_ld + u, h);
+    } else if (act) {
+        put4_planes(s.X, s.x_plane, (int64_t)b * s.JH + u, relu_add4(P.e, P.p));
+    }
+}
+
 // Counts of this kernel's blocks: listed streams accumulate in cnt[4], active ones in cnt[6]; the
 // last block to finish publishes them as cnt[0] / cnt[1] and clears the accumulators.
 __device__ __forceinline__ void publish(const DecState &d, bool first, int max_it, cudaGraphConditionalHandle cond) {
@@ -308,7 +342,30 @@ __global__ void __launch_bounds__(STEP_T) dec_step_kernel(DecState d, NbDecStep 
         return;
     }
     int t = d.t[b], sym = d.symbols[b];
-    {
+    // the decision-independent operands of the next iteration, in flight during the argmax
+    const bool pre = s.PH == 4 * STEP_T && s.JH == 4 * STEP_T;
+    StreamPre P;
+    if (pre) stream_pre_load(d, s, b, b * c + min(t + 1, c - 1), P);
+    if (s.part_v) {
+        // the joint GEMM left (value, column) partials per column tile: reduce them, ties to the
+        // lowest column
+        float bv = -INFINITY;
+        int bi = 0x7fffffff;
+        if (tid < s.nparts) {
+            bv = s.part_v[(int64_t)b * s.nparts + tid];
+            bi = s.part_i[(int64_t)b * s.nparts + tid];
+        }
+        if (tid < 32) {
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+                const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+                if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+            }
+            if (tid == 0) s_k = bi;
+        }
+        __syncthreads();
+    } else {
         const float *l = s.logits + (int64_t)b * s.ldl;
         float bv = -INFINITY;
         int bi = 0x7fffffff;
@@ -367,7 +424,8 @@ __global__ void __launch_bounds__(STEP_T) dec_step_kernel(DecState d, NbDecStep 
         if (act) atomicAdd(&d.cnt[6], 1);
     }
     __syncthreads();
-    stream_rows(d, s, b, k, s_pos, act, b * c + t);
+    if (pre) stream_rows_pre(s, b, k, s_pos, act, P);
+    else stream_rows(d, s, b, k, s_pos, act, b * c + t);
     if (tid == 0) publish(d, false, max_it, cond);
 }
 

@@ -620,7 +620,7 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tcr_kernel(const __grid_const
                 const int g = m / p.e.rpg, r = m - g * p.e.rpg;
                 rowbase = (int64_t)g * p.e.gstride + (int64_t)(rowoff + r) * p.e.ldc;
                 brow = (int64_t)g * p.e.bias_gstride;
-                if (p.de.mode) {
+                if (p.de.mode == 1 || p.de.mode == 2) {
                     ds = p.de.need_idx[m];
                     if (p.de.mode == 1) dbias = p.de.row + (int64_t)(p.de.last_token ? p.de.last_token[ds] : ds) * p.de.n_split;
                     if (p.de.mode == 2) der = p.de.erow[ds];
@@ -655,6 +655,8 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tcr_kernel(const __grid_const
                 if (finish) __threadfence();
             }
             if (finish) {
+                float amax = -INFINITY;  // mode 3: this thread's best column (ascending, strict >: lowest index on ties)
+                int aidx = 0x7fffffff;
                 for (int jj0 = j0; jj0 < j0 + span; jj0 += 16) {
                     float va[16], vg[16];
                     if (w.parts == 1) {
@@ -681,6 +683,15 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tcr_kernel(const __grid_const
                     const int n0 = n_base + jj0;
                     if (n0 >= nout) continue;
                     const int cnt = min(16, nout - n0);
+                    if (p.de.mode == 3) {
+#pragma unroll
+                        for (int x = 0; x < 16; ++x) {
+                            if (x >= cnt) break;
+                            const float v = va[x] + __ldg(p.e.bias + n0 + x);
+                            if (v > amax) { amax = v; aidx = n0 + x; }
+                        }
+                        continue;
+                    }
                     if (p.de.mode) {
                         if (n0 >= p.de.n_split) dec_aux16(p.de, p.N, ds, n0, va);
                         else if (p.de.mode == 1) dec_lstm16(p.de, dbias, m, ds, n0, va);
@@ -738,6 +749,10 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tcr_kernel(const __grid_const
                         }
                         if (p.e.c32) p.e.c32[(int64_t)m * p.e.ldc32 + n0 + x] = v;
                     }
+                }
+                if (p.de.mode == 3 && row_ok) {
+                    p.de.part_v[(int64_t)m * p.de.part_ld + 2 * wt + half] = amax;
+                    p.de.part_i[(int64_t)m * p.de.part_ld + 2 * wt + half] = aidx;
                 }
                 if (w.parts > 1 && etid == 0) p.counters[tile] = 0;
             }
@@ -1004,7 +1019,15 @@ int nb_gemm_tc(const nemo_gemm_args_t *a, void *stream) { return nb_gemm_tc_layo
 
 extern "C" int nb_gemm_dec(const nemo_gemm_args_t *a, const NbDecEpi *de, void *stream) {
     if (init_once()) return -1;
-    if (!de || (de->mode != 1 && de->mode != 2)) return nb_set_error("decoder GEMM: unknown epilogue mode");
+    if (!de || de->mode < 1 || de->mode > 3) return nb_set_error("decoder GEMM: unknown epilogue mode");
+    if (de->mode == 3) {
+        // rows are streams (no row list); partials per (column tile of 128, half): 2 * ceil(N / 128) <= part_ld
+        if (a->a_fmt != NEMO_FMT_BF16X2 || a->act != NEMO_ACT_NONE || a->accumulate || a->K % 8 || !a->bias || !de->part_v || !de->part_i ||
+            de->part_ld < 2 * ((a->N + 127) / 128) || a->dynM)
+            return nb_set_error("decoder GEMM: argmax epilogue needs bf16 hi/lo activations, a bias, partial buffers of %d columns", 2 * ((a->N + 127) / 128));
+        const PlanR pl = plan_r(a, 128, false);
+        return launch_r<128>(a, pl, (cudaStream_t)stream, de);  // 128-column tiles: the partial layout above
+    }
     if (a->a_fmt != NEMO_FMT_BF16X2 || a->act != NEMO_ACT_NONE || a->accumulate || a->K % 8 || a->N % 16)
         return nb_set_error("decoder GEMM: needs bf16 hi/lo activations, no activation or accumulation, K %% 8 == 0 and N %% 16 == 0");
     const int ns = de->n_split;
