@@ -152,6 +152,17 @@ __global__ void __launch_bounds__(THREADS) attention_kernel(const float *__restr
     const int NP = L + c - 1, prow0 = Lmax - L, off = h * DH;
     const float *Kb = K + (int64_t)s * kv_sstride + (int64_t)(pos - cache_len) * ldk + off;
     const float *Vb = V + (int64_t)s * kv_sstride + (int64_t)(pos - cache_len) * ldk + off;
+    // the query pairs straight from global memory (just written by the projection) and the biases,
+    // requested first: the position scores wait on them, not on the window
+    const float *Qb = Q + (int64_t)s * q_sstride + (int64_t)pos * ldq + off;
+    float2 qq[4], bu2[4], bv2[4];  // this thread's pairs (i, 2p .. 2p + 1), i = e / 64, p = e % 64
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+        const int e = tid + r * THREADS, i = e >> 6, k = 2 * (e & 63);
+        qq[r] = i < c ? *(const float2 *)(Qb + (int64_t)i * ldq + k) : make_float2(0.f, 0.f);
+        bu2[r] = *(const float2 *)(bias_u + off + k);
+        bv2[r] = *(const float2 *)(bias_v + off + k);
+    }
     // the window's K rows and its V rows into shared memory by the bulk copy engine, one 512-byte
     // row per copy, each group on its own barrier
     __shared__ uint64_t bars[2];
@@ -160,7 +171,6 @@ __global__ void __launch_bounds__(THREADS) attention_kernel(const float *__restr
         sm100::fence_mbar_init();
     }
     __syncthreads();
-    const float *Qb = Q + (int64_t)s * q_sstride + (int64_t)pos * ldq + off;
     if (warp == 0) {
         if (lane == 0) {
             sm100::mbar_arrive_expect_tx(&bars[0], (uint32_t)L * DH * 4);
@@ -170,21 +180,7 @@ __global__ void __launch_bounds__(THREADS) attention_kernel(const float *__restr
         for (int r = lane; r < L; r += 32) bulk_row(Ks + r * KP, Kb + (int64_t)r * ldk, DH * 4, &bars[0]);
         for (int r = lane; r < L; r += 32) bulk_row(Vs + r * VP, Vb + (int64_t)r * ldk, DH * 4, &bars[1]);
     }
-    // each thread's pairs of the query operands: (i, 2p .. 2p + 1) for i = e / 64, p = e % 64
-    float2 bu2[4], bv2[4];
-#pragma unroll
-    for (int r = 0; r < 4; ++r) {
-        const int k = 2 * ((tid + r * THREADS) & 63);
-        bu2[r] = *(const float2 *)(bias_u + off + k);
-        bv2[r] = *(const float2 *)(bias_v + off + k);
-    }
     bool bad = false;
-    float2 qq[4];  // the query pairs straight from global memory (just written by the projection)
-#pragma unroll
-    for (int r = 0; r < 4; ++r) {
-        const int e = tid + r * THREADS, i = e >> 6, k = 2 * (e & 63);
-        qq[r] = i < c ? *(const float2 *)(Qb + (int64_t)i * ldq + k) : make_float2(0.f, 0.f);
-    }
 #pragma unroll
     for (int r = 0; r < 4; ++r) {
         const int e = tid + r * THREADS, i = e >> 6, k = 2 * (e & 63);

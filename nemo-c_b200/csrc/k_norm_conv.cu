@@ -191,66 +191,136 @@ __global__ void __launch_bounds__(256) subsample_front_kernel(const float *__res
     }
 }
 
-// The same two stages with the roles flipped: a lane owns one output position (its 7x7 patch in
-// registers) and the warp walks 32 channels, so every weight is loaded once per warp (a
-// broadcast) instead of once per lane; a 32 x 32 shared-memory transpose turns the
-// position-per-lane results into channel-contiguous stores. C % 256 == 0 (8 warps x 32 channels).
-__global__ void __launch_bounds__(256) subsample_front_lanes_kernel(const float *__restrict__ X, int64_t x_sstride, const float *__restrict__ W0,
-                                                                    const float *__restrict__ b0, const float *__restrict__ W2,
-                                                                    const float *__restrict__ b2, void *Y, int y_fmt, int64_t y_plane, int T, int F,
-                                                                    int T1, int F1, int T2, int F2, int C, int64_t positions) {
-    __shared__ float stg[8][32][33];
+// The same two stages computed by tiles: a block owns TR consecutive second-stage rows t2 of one
+// stream and 32 channels. It stages the input rows those rows read (4 * TR + 3 rows, zero outside
+// the input) in shared memory, computes every first-stage output they need once (2 * TR + 1 rows
+// t1 x F1 columns x 32 channels, zero for t1 outside [0, T1): the depthwise conv's padding) into
+// shared memory, and then the depthwise outputs from there. Each first-stage value is computed
+// once per block instead of once per depthwise tap that reads it. Lanes are channels: input
+// reads are broadcasts, first-stage reads and output stores are 32 consecutive channels.
+constexpr int FT_TR = 4;         // second-stage rows per block
+
+__device__ __forceinline__ void front_split2(float x0, float x1, uint32_t &hi, uint32_t &lo) {
+    const __nv_bfloat162 h = __floats2bfloat162_rn(x0, x1);
+    const __nv_bfloat162 l = __floats2bfloat162_rn(x0 - __low2float(h), x1 - __high2float(h));
+    hi = *(const uint32_t *)&h;
+    lo = *(const uint32_t *)&l;
+}
+__device__ __forceinline__ void front_mma(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+                 : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+                 : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+constexpr int FT_IN_W = 136;     // staged input columns: fi = -2 .. 133 (F <= 128 + 2 * (F1 - F / 2 - 1) checked on the host)
+
+// First-stage rows in shared memory are F1 + 3 columns wide: f1 = -2 .. F1 (the depthwise conv's
+// zero padding stored, so its taps need no bounds checks).
+__host__ __device__ __forceinline__ size_t front_tile_smem(int F1) {
+    return ((size_t)(4 * FT_TR + 3) * FT_IN_W + (size_t)(2 * FT_TR + 1) * (F1 + 3) * 32) * sizeof(float);
+}
+
+// FC: mel bins fixed at compile time (0: F at run time); BF: output as bf16 hi / lo planes.
+template <int FC, bool BF>
+__global__ void __launch_bounds__(256) subsample_front_tile_kernel(const float *__restrict__ X, int64_t x_sstride, const float *__restrict__ W0,
+                                                                   const float *__restrict__ b0, const float *__restrict__ W2,
+                                                                   const float *__restrict__ b2, void *Y, int64_t y_plane, int T, int Frt, int T1,
+                                                                   int T2, int C) {
+    extern __shared__ float fsm[];
+    const int F = FC ? FC : Frt, F1 = F / 2 + 1, F2 = F1 / 2 + 1, CW = F1 + 3;
+    float *xin = fsm, *c1 = fsm + (4 * FT_TR + 3) * FT_IN_W;  // c1[r][f1 + 2][32]
     nb::pdl_wait();
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int64_t pidx = (int64_t)blockIdx.x * 32 + lane;
-    const bool pv = pidx < positions;
-    const int64_t pp = pv ? pidx : 0;
-    const int f2 = (int)(pp % F2);
-    const int64_t r = pp / F2;
-    const int t2 = (int)(r % T2), s = (int)(r / T2);
+    const int tiles_t = (T2 + FT_TR - 1) / FT_TR;
+    const int s = blockIdx.x / tiles_t, t2_0 = (blockIdx.x % tiles_t) * FT_TR;
+    const int cb = blockIdx.y * 32, lane = threadIdx.x & 31, grp = threadIdx.x >> 5, ch = cb + lane;
     const float *x = X + (int64_t)s * x_sstride;
-    const int tx0 = 4 * t2 - 6, fx0 = 4 * f2 - 6;
-    float pt[49];
+    // input rows ti = 4 * t2_0 - 6 + i, columns fi = j - 2
+    const int ti0 = 4 * t2_0 - 6;
+    constexpr int NIN = (4 * FT_TR + 3) * FT_IN_W, NPT = (NIN + 255) / 256;  // 256 threads
+    float v[NPT];  // every load of the staging issued before the first store
 #pragma unroll
-    for (int e = 0; e < 49; ++e) {
-        const int ti = tx0 + e / 7, fi = fx0 + e % 7;
-        pt[e] = (pv && ti >= 0 && ti < T && fi >= 0 && fi < F) ? x[(int64_t)ti * F + fi] : 0.0f;
+    for (int q = 0; q < NPT; ++q) {
+        const int e = threadIdx.x + q * 256, i = e / FT_IN_W, j = e - i * FT_IN_W, ti = ti0 + i, fi = j - 2;
+        v[q] = (e < NIN && ti >= 0 && ti < T && fi >= 0 && fi < F) ? x[(int64_t)ti * F + fi] : 0.0f;
     }
-    bool okt[3], okf[3];
 #pragma unroll
-    for (int k = 0; k < 3; ++k) {
-        const int t1 = 2 * t2 - 2 + k, f1 = 2 * f2 - 2 + k;
-        okt[k] = t1 >= 0 && t1 < T1;
-        okf[k] = f1 >= 0 && f1 < F1;
+    for (int q = 0; q < NPT; ++q)
+        if (threadIdx.x + q * 256 < NIN) xin[threadIdx.x + q * 256] = v[q];
+    // the padding columns f1 = -2, -1, F1 of every first-stage row
+    for (int e = threadIdx.x; e < (2 * FT_TR + 1) * 3 * 32; e += 256) {
+        const int r = e / 96, q = (e / 32) % 3, l = e % 32;
+        c1[(r * CW + (q < 2 ? q : F1 + 2)) * 32 + l] = 0.0f;
     }
-    for (int cb = warp * 32; cb < C; cb += 8 * 32) {
-        for (int q = 0; q < 32; ++q) {
-            const int ch = cb + q;
-            float w0[9], w2[9];
+    float w2[9];
 #pragma unroll
-            for (int k = 0; k < 9; ++k) { w0[k] = __ldg(W0 + ch * 9 + k); w2[k] = __ldg(W2 + ch * 9 + k); }
-            const float bb0 = __ldg(b0 + ch);
-            float acc = __ldg(b2 + ch);
+    for (int k = 0; k < 9; ++k) w2[k] = __ldg(W2 + ch * 9 + k);
+    const float bb2 = __ldg(b2 + ch);
+    // first-stage weights as the MMA's B operand (k = tap, n = channel), split into bf16 hi + lo:
+    // b0 = (taps 2t, 2t + 1; channel g), b1 = (taps 2t + 8, 2t + 9; channel g) per 8-channel tile
+    const int g = lane >> 2, t = lane & 3;
+    uint32_t wbh[4][2], wbl[4][2];
+    float bias0[4][2];
+#pragma unroll
+    for (int nt = 0; nt < 4; ++nt) {
+        const float *wr = W0 + (cb + nt * 8 + g) * 9;
+        const float k0a = __ldg(wr + 2 * t), k0b = __ldg(wr + 2 * t + 1);
+        const float k1a = t == 0 ? __ldg(wr + 8) : 0.0f;
+        front_split2(k0a, k0b, wbh[nt][0], wbl[nt][0]);
+        front_split2(k1a, 0.0f, wbh[nt][1], wbl[nt][1]);
+        bias0[nt][0] = __ldg(b0 + cb + nt * 8 + 2 * t);
+        bias0[nt][1] = __ldg(b0 + cb + nt * 8 + 2 * t + 1);
+    }
+    __syncthreads();
+    // first stage on the tensor cores: for positions p = r * F1 + f1 (t1 = 2 * t2_0 - 2 + r) the
+    // 3 x 3 input patch (taps k = 3a + b, padded to 16) times the block's 32 channels, mma.sync
+    // m16n8k16 on bf16 hi / lo splits of both operands (four products, fp32 accumulation); then
+    // bias and ReLU, and zero for t1 outside [0, T1)
+    const int P = (2 * FT_TR + 1) * F1;
+    for (int mt = grp; mt * 16 < P; mt += 8) {
+        uint32_t ah[4], al[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const int pp = mt * 16 + g + 8 * (e & 1), k = 2 * t + 8 * (e >> 1);
+            float v0 = 0.0f, v1 = 0.0f;
+            if (pp < P) {
+                const int r = pp / F1, f1 = pp - r * F1;
+                const float *xr = xin + 2 * r * FT_IN_W + 2 * f1;
+                if (k < 9) v0 = xr[(k / 3) * FT_IN_W + k % 3];
+                if (k + 1 < 9) v1 = xr[((k + 1) / 3) * FT_IN_W + (k + 1) % 3];
+            }
+            front_split2(v0, v1, ah[e], al[e]);
+        }
+#pragma unroll
+        for (int nt = 0; nt < 4; ++nt) {
+            float d[4] = { 0.f, 0.f, 0.f, 0.f };
+            front_mma(d, al, wbl[nt][0], wbl[nt][1]);
+            front_mma(d, al, wbh[nt][0], wbh[nt][1]);
+            front_mma(d, ah, wbl[nt][0], wbl[nt][1]);
+            front_mma(d, ah, wbh[nt][0], wbh[nt][1]);
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const int pp = mt * 16 + g + 8 * h;
+                if (pp >= P) continue;
+                const int r = pp / F1, t1 = 2 * t2_0 - 2 + r;
+                const bool okt = t1 >= 0 && t1 < T1;
+                const int n = nt * 8 + 2 * t, idx = (r * CW + (pp - r * F1) + 2) * 32 + n;
+                c1[idx] = okt ? fmaxf(d[2 * h] + bias0[nt][0], 0.0f) : 0.0f;
+                c1[idx + 1] = okt ? fmaxf(d[2 * h + 1] + bias0[nt][1], 0.0f) : 0.0f;
+            }
+        }
+    }
+    __syncthreads();
+    // depthwise stride-2 stage over the staged first-stage outputs
+    for (int tr = 0; tr < FT_TR; ++tr) {
+        const int t2 = t2_0 + tr;
+        if (t2 >= T2) break;
+        for (int f2 = grp; f2 < F2; f2 += 8) {
+            float acc = bb2;
 #pragma unroll
             for (int kh = 0; kh < 3; ++kh)
 #pragma unroll
-                for (int kw = 0; kw < 3; ++kw) {
-                    if (!okt[kh] || !okf[kw]) continue;
-                    float c0 = bb0;
-#pragma unroll
-                    for (int a = 0; a < 3; ++a)
-#pragma unroll
-                        for (int b = 0; b < 3; ++b) c0 += w0[a * 3 + b] * pt[(2 * kh + a) * 7 + 2 * kw + b];
-                    acc += w2[kh * 3 + kw] * fmaxf(c0, 0.0f);
-                }
-            stg[warp][lane][q] = acc;
+                for (int kw = 0; kw < 3; ++kw) acc += w2[kh * 3 + kw] * c1[((2 * tr + kh) * CW + 2 * f2 + kw) * 32 + lane];  // f1 = 2 f2 - 2 + kw
+            nb::store_act(Y, BF ? NEMO_FMT_BF16X2 : NEMO_FMT_F32, y_plane, (((int64_t)s * T2 + t2) * F2 + f2) * C + ch, acc);
         }
-        __syncwarp();
-        for (int p = 0; p < 32; ++p) {
-            const int64_t po = (int64_t)blockIdx.x * 32 + p;
-            if (po < positions) nb::store_act(Y, y_fmt, y_plane, po * C + cb + lane, stg[warp][p][lane]);
-        }
-        __syncwarp();
     }
 }
 
@@ -464,10 +534,22 @@ extern "C" int nemo_subsample_front(const float *X, int64_t x_sstride, const flo
     const int T1 = T / 2 + 1, F1 = F / 2 + 1, T2 = T1 / 2 + 1, F2 = F1 / 2 + 1;
     const int64_t positions = (int64_t)streams * T2 * F2;
     if (positions <= 0) return 0;
-    if (C % 256 == 0) {
-        nb::launch(subsample_front_lanes_kernel, (unsigned)((positions + 31) / 32), 256, 0, (cudaStream_t)stream, X, x_sstride, W0, b0, W2, b2, Y, y_fmt, y_plane, T,
-                                                                                                        F, T1, F1, T2, F2, C, positions);
-        return nb_check_launch("subsample_front_lanes_kernel");
+    if (C % 32 == 0 && 2 * F1 + 1 <= FT_IN_W - 2) {
+        const size_t smem = front_tile_smem(F1);
+        const bool bf = y_fmt == NEMO_FMT_BF16X2;
+        void (*k)(const float *, int64_t, const float *, const float *, const float *, const float *, void *, int64_t, int, int, int, int, int) =
+            F == 128 ? (bf ? subsample_front_tile_kernel<128, true> : subsample_front_tile_kernel<128, false>)
+                     : (bf ? subsample_front_tile_kernel<0, true> : subsample_front_tile_kernel<0, false>);
+        static size_t attr_set[4] = {};  // largest dynamic shared-memory size enabled so far, per instantiation
+        const int ki = (F == 128 ? 0 : 2) + (bf ? 1 : 0);
+        if (smem > attr_set[ki]) {
+            if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+                return nb_set_error("nemo_subsample_front: %zu bytes of shared memory unavailable", smem);
+            attr_set[ki] = smem;
+        }
+        const dim3 grid((unsigned)(streams * ((T2 + FT_TR - 1) / FT_TR)), (unsigned)(C / 32));
+        nb::launch(k, grid, 256, smem, (cudaStream_t)stream, X, x_sstride, W0, b0, W2, b2, Y, y_plane, T, F, T1, T2, C);
+        return nb_check_launch("subsample_front_tile_kernel");
     }
     nb::launch(subsample_front_kernel, (unsigned)((positions + 7) / 8), 256, 0, (cudaStream_t)stream, X, x_sstride, W0, b0, W2, b2, Y, y_fmt, y_plane, T, F, T1,
                                                                                               F1, T2, F2, C, positions);
