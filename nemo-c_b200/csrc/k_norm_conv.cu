@@ -137,6 +137,36 @@ __global__ void dwconv2d_s2_kernel(const float *__restrict__ X, const float *__r
     }
 }
 
+// The same by output rows: one block per (stream, output row t1), threads over channels (weights
+// in registers), looping over the row's columns; no per-element index arithmetic.
+__global__ void __launch_bounds__(256) dwconv2d_s2_rows_kernel(const float *__restrict__ X, const float *__restrict__ W, const float *__restrict__ bias,
+                                                               void *Y, int y_fmt, int64_t y_plane, int T, int F, int T1, int F1, int C) {
+    nb::pdl_wait();
+    const int s = blockIdx.x / T1, t1 = blockIdx.x - s * T1;
+    const float *x = X + (int64_t)s * T * F * C;
+    for (int ch = threadIdx.x; ch < C; ch += blockDim.x) {
+        float w[9];
+#pragma unroll
+        for (int k = 0; k < 9; ++k) w[k] = __ldg(W + ch * 9 + k);
+        const float b = __ldg(bias + ch);
+        for (int f1 = 0; f1 < F1; ++f1) {
+            float acc = b;
+#pragma unroll
+            for (int kh = 0; kh < 3; ++kh) {
+                const int ti = 2 * t1 + kh - 2;
+                if (ti < 0 || ti >= T) continue;
+#pragma unroll
+                for (int kw = 0; kw < 3; ++kw) {
+                    const int fi = 2 * f1 + kw - 2;
+                    if (fi < 0 || fi >= F) continue;
+                    acc += w[kh * 3 + kw] * x[((int64_t)ti * F + fi) * C + ch];
+                }
+            }
+            nb::store_act(Y, y_fmt, y_plane, (((int64_t)s * T1 + t1) * F1 + f1) * C + ch, acc);
+        }
+    }
+}
+
 // The first two subsampling stages fused: conv2d_c1_s2_relu (src/kernels.metal:413-432) then
 // dwconv2d_s2 (src/kernels.metal:435-454), without materialising the first stage's output.
 // Output (t2, f2) needs first-stage outputs t1 = 2*t2-2+kh, f1 = 2*f2-2+kw (zero when outside
@@ -326,6 +356,24 @@ __global__ void __launch_bounds__(256) subsample_front_tile_kernel(const float *
 
 // flatten_cf (src/kernels.metal:457-462) of rows [lo, lo + c) only: Y[s*c + i][ch*F + f] =
 // X[s][lo + i][f][ch]. Thread per output element (f fastest within a channel).
+// The same by rows: one block per output row (stream s, row r); the [F][C] source row is read
+// coalesced into shared memory and written out in [C][F] order.
+__global__ void __launch_bounds__(256) flatten_rows_smem_kernel(const float *__restrict__ X, void *Y, int y_fmt, int64_t y_plane, const int *lo_p, int T,
+                                                                int F, int C, int c) {
+    extern __shared__ float frow[];  // [F][C]
+    nb::pdl_wait();
+    const int lo = *lo_p;
+    const int s = blockIdx.x / c, r = blockIdx.x - s * c, n = F * C;
+    const float *src = X + ((int64_t)s * T + lo + r) * n;
+    for (int e = threadIdx.x; e < n; e += blockDim.x) frow[e] = src[e];
+    __syncthreads();
+    const int64_t row = (int64_t)blockIdx.x * n;
+    for (int e = threadIdx.x; e < n; e += blockDim.x) {
+        const int ch = e / F, f = e - ch * F;
+        nb::store_act(Y, y_fmt, y_plane, row + e, frow[f * C + ch]);
+    }
+}
+
 __global__ void flatten_rows_kernel(const float *__restrict__ X, void *Y, int y_fmt, int64_t y_plane, const int *lo_p, int T, int F, int C, int c,
                                     int64_t total) {
     nb::pdl_wait();
@@ -521,6 +569,10 @@ extern "C" int nb_dwconv2d_s2_fmt(const float *X, const float *W, const float *b
                                   int T1, int F1, int C, void *stream) {
     const int64_t total = (int64_t)streams * T1 * F1 * C;
     if (total <= 0) return 0;
+    if ((int64_t)streams * T1 <= 0x7fffffff) {
+        nb::launch(dwconv2d_s2_rows_kernel, (unsigned)(streams * T1), 256, 0, (cudaStream_t)stream, X, W, bias, Y, y_fmt, y_plane, T, F, T1, F1, C);
+        return nb_check_launch("dwconv2d_s2_rows_kernel");
+    }
     nb::launch(dwconv2d_s2_kernel, grid_for(total), 256, 0, (cudaStream_t)stream, X, W, bias, Y, y_fmt, y_plane, T, F, T1, F1, C, total);
     return nb_check_launch("dwconv2d_s2_kernel");
 }
@@ -559,6 +611,11 @@ extern "C" int nemo_subsample_front(const float *X, int64_t x_sstride, const flo
 extern "C" int nb_flatten_rows_fmt(const float *X, void *Y, int y_fmt, int64_t y_plane, const int *lo, int streams, int T, int F, int C, int c, void *stream) {
     const int64_t total = (int64_t)streams * c * C * F;
     if (total <= 0) return 0;
+    if ((size_t)F * C * sizeof(float) <= 48 * 1024 && (int64_t)streams * c <= 0x7fffffff) {
+        nb::launch(flatten_rows_smem_kernel, (unsigned)(streams * c), 256, (size_t)F * C * sizeof(float), (cudaStream_t)stream, X, Y, y_fmt, y_plane, lo, T,
+                   F, C, c);
+        return nb_check_launch("flatten_rows_smem_kernel");
+    }
     nb::launch(flatten_rows_kernel, grid_for(total), 256, 0, (cudaStream_t)stream, X, Y, y_fmt, y_plane, lo, T, F, C, c, total);
     return nb_check_launch("flatten_rows_kernel");
 }
