@@ -472,8 +472,29 @@ __global__ void dec_reset_kernel(DecState d, int PH, int blank) {
 
 }  // namespace
 
+// The same with one block per (layer, stream): both moves are contiguous runs of whole rows, copied
+// as float4 (every row start is 16-byte aligned when D % 4 == 0).
+__global__ void __launch_bounds__(256) compact_rows_kernel(float *kv, float *din, int64_t cap, int D, int src_kv, int cache_len, int src_din, int dst_din,
+                                                           int conv_left) {
+    nb::pdl_wait();
+    const int64_t ls = blockIdx.x, kv_row = 3LL * D;
+    float4 *kd = (float4 *)(kv + ls * cap * kv_row);
+    const float4 *ks = (const float4 *)(kv + ls * cap * kv_row + (int64_t)src_kv * kv_row);
+    const int64_t nkv = (int64_t)cache_len * kv_row / 4;
+    for (int64_t i = threadIdx.x; i < nkv; i += blockDim.x) kd[i] = ks[i];
+    float4 *dd = (float4 *)(din + ls * cap * D + (int64_t)dst_din * D);
+    const float4 *ds = (const float4 *)(din + ls * cap * D + (int64_t)src_din * D);
+    const int64_t ndin = (int64_t)conv_left * D / 4;
+    for (int64_t i = threadIdx.x; i < ndin; i += blockDim.x) dd[i] = ds[i];
+}
+
 extern "C" int nb_compact(float *kv, float *din, int layers, int streams, int64_t cap, int D, int src_kv, int cache_len, int src_din, int dst_din,
                           int conv_left, void *stream) {
+    if (D % 4 == 0 && ((uintptr_t)kv & 15) == 0 && ((uintptr_t)din & 15) == 0 && (int64_t)layers * streams <= 0x7fffffff) {
+        nb::launch(compact_rows_kernel, (unsigned)(layers * streams), 256, 0, (cudaStream_t)stream, kv, din, cap, D, src_kv, cache_len, src_din, dst_din,
+                   conv_left);
+        return nb_check_launch("compact_rows_kernel");
+    }
     nb::launch(compact_kernel, 148 * 8, 256, 0, (cudaStream_t)stream, kv, din, layers, streams, cap, D, src_kv, cache_len, src_din, dst_din, conv_left);
     return nb_check_launch("compact_kernel");
 }
