@@ -54,7 +54,8 @@ struct nb_engine {
     size_t tap_chunk_cap, tap_chunks;
     double enc_ms, dec_ms, gpu_ms;
     size_t chunks;
-    cudaEvent_t ev0, ev1;
+    cudaEvent_t ev0, ev1, ev_mid;  /* step start, step end, encoder done */
+    int dec_pending_slot, dec_pending_max_it;  /* decoder graph launched, its counters not read yet */
     /* captured CUDA graphs: encoder step per (window rows, chunk rows), decoder iteration per
        chunk rows; NEMO_GRAPHS=0 launches kernel by kernel instead */
     int use_graphs;
@@ -244,6 +245,8 @@ nb_engine_t *nb_engine_create(nb_model_t *m, int B, int right, char *err, size_t
     CK(cudaStreamCreateWithFlags(&e->st, cudaStreamNonBlocking));
     CK(cudaEventCreate(&e->ev0));
     CK(cudaEventCreate(&e->ev1));
+    CK(cudaEventCreate(&e->ev_mid));
+    e->dec_pending_slot = -1;
     e->d_win = dalloc(Bz * (size_t)e->nwin_max * 128 * 4, &fail);
     CK(cudaMallocHost((void **)&e->h_win, Bz * (size_t)e->nwin_max * 128 * 4));
     e->c0 = NULL; /* the first subsampling stage is fused into the second (no [T1][F1][C] map) */
@@ -361,6 +364,7 @@ void nb_engine_destroy(nb_engine_t *e) {
     if (e->st) cudaStreamDestroy(e->st);
     if (e->ev0) cudaEventDestroy(e->ev0);
     if (e->ev1) cudaEventDestroy(e->ev1);
+    if (e->ev_mid) cudaEventDestroy(e->ev_mid);
     for (int i = 0; i < e->ngraphs; ++i) cudaGraphExecDestroy(e->graphs[i].exec);
     free(e->enc1_layers);
     void *dt[] = { e->dec_wg1, e->dec_wg2, e->dec_b1i, e->dec_table, e->dec_r0, e->dec_r1, e->dec_pv, e->dec_pi };
@@ -857,14 +861,14 @@ static int run_decoder(nb_engine_t *e, int c, char *err, size_t errlen) {
         const int slot = dec_graph(e, c);
         if (slot == -1) { snprintf(err, errlen, "%s", nemo_gpu_last_error()); return -1; }
         if (slot >= 0) {
+            /* no host wait here: the step's single synchronisation reads the counters */
             if (cudaGraphLaunch(e->graphs[slot].exec, st) != cudaSuccess ||
-                cudaMemcpyAsync(e->h_cnt, d->cnt, 4 * sizeof(int), cudaMemcpyDeviceToHost, st) != cudaSuccess ||
-                cudaStreamSynchronize(st) != cudaSuccess) {
+                cudaMemcpyAsync(e->h_cnt, d->cnt, 4 * sizeof(int), cudaMemcpyDeviceToHost, st) != cudaSuccess) {
                 snprintf(err, errlen, "decoder: %s", cudaGetErrorString(cudaGetLastError()));
                 return -1;
             }
-            nb_count_launches(e->graphs[slot].kernels * (uint64_t)e->h_cnt[2]);
-            if (e->h_cnt[1] != 0) { snprintf(err, errlen, "decoder did not finish the chunk in %d iterations", max_it); return -1; }
+            e->dec_pending_slot = slot;
+            e->dec_pending_max_it = max_it;
             return 0;
         }
     }
@@ -886,7 +890,6 @@ int nb_engine_step(nb_engine_t *e, int final, int *tokens, int max_tokens, int *
     if (e->closed) return 0;
     if (e->pending_n == 0) { if (final) e->closed = 1; return 0; }
     if ((int)e->pending_n < e->chunk_mel && !final) return 0;
-    const double t0 = nb_now_ms();
     size_t take = (size_t)e->chunk_mel < e->pending_n ? (size_t)e->chunk_mel : e->pending_n;
     if (final && e->pending_n <= (size_t)e->chunk_mel) take = e->pending_n;
     const int include_boundary = final && e->pending_n == take;
@@ -953,20 +956,19 @@ int nb_engine_step(nb_engine_t *e, int final, int *tokens, int max_tokens, int *
         return -1;
     }
     if (run_graph(e, 0, nwin, c, enc_body)) { snprintf(err, errlen, "encoder: %s", nemo_gpu_last_error()); return -1; }
-    if (cudaStreamSynchronize(st) != cudaSuccess) { snprintf(err, errlen, "encoder: %s", cudaGetErrorString(cudaGetLastError())); return -1; }
-    if (nemo_gpu_check_device_errors()) { snprintf(err, errlen, "encoder: %s", nemo_gpu_last_error()); return -1; }
-    if (e->use_enc1) {
-        int v = 0;
-        if (cudaMemcpy(&v, e->d_enc1_err, sizeof v, cudaMemcpyDeviceToHost) != cudaSuccess || v) {
-            snprintf(err, errlen, "encoder: the persistent encoder gave up waiting (code %d)", v);
-            return -1;
-        }
+    /* the decoder is queued behind the encoder without a host round trip; the device error words
+       are read after the step's one synchronisation */
+    if (cudaEventRecord(e->ev_mid, st) != cudaSuccess ||
+        (e->use_enc1 && cudaMemcpyAsync(&e->h_cnt[5], e->d_enc1_err, sizeof(int), cudaMemcpyDeviceToHost, st) != cudaSuccess)) {
+        snprintf(err, errlen, "encoder: %s", cudaGetErrorString(cudaGetLastError()));
+        return -1;
     }
-    const double t1 = nb_now_ms();
     e->pos += c;
     const int L = e->cache_len + c;
     e->cache_len = L < e->left ? L : e->left;
     if (e->tap_prompted) {
+        /* taps (tests only): the encoder's rows once it finished */
+        if (cudaStreamSynchronize(st) != cudaSuccess) { snprintf(err, errlen, "encoder: %s", cudaGetErrorString(cudaGetLastError())); return -1; }
         const size_t rows = (size_t)e->B * c;
         if (e->tap_rows + rows <= e->tap_cap) {
             cudaMemcpy(e->tap_prompted + e->tap_rows * D, e->prompted, rows * D * 4, cudaMemcpyDeviceToHost);
@@ -981,18 +983,30 @@ int nb_engine_step(nb_engine_t *e, int final, int *tokens, int max_tokens, int *
     if (cudaMemcpyAsync(e->h_ntok, d->ntok, (size_t)e->B * sizeof(int), cudaMemcpyDeviceToHost, st) != cudaSuccess ||
         cudaMemcpyAsync(e->h_tokens, d->tokens, (size_t)e->B * (size_t)d->tok_cap * sizeof(int), cudaMemcpyDeviceToHost, st) != cudaSuccess ||
         cudaEventRecord(e->ev1, st) != cudaSuccess || cudaStreamSynchronize(st) != cudaSuccess) {
-        snprintf(err, errlen, "tokens: %s", cudaGetErrorString(cudaGetLastError()));
+        snprintf(err, errlen, "step: %s", cudaGetErrorString(cudaGetLastError()));
         return -1;
     }
-    float step_ms = 0.0f;
+    if (nemo_gpu_check_device_errors()) { snprintf(err, errlen, "step: %s", nemo_gpu_last_error()); return -1; }
+    if (e->use_enc1 && e->h_cnt[5]) {
+        snprintf(err, errlen, "encoder: the persistent encoder gave up waiting (code %d)", e->h_cnt[5]);
+        return -1;
+    }
+    if (e->dec_pending_slot >= 0) {
+        nb_count_launches(e->graphs[e->dec_pending_slot].kernels * (uint64_t)e->h_cnt[2]);
+        e->dec_pending_slot = -1;
+        if (e->h_cnt[1] != 0) { snprintf(err, errlen, "decoder did not finish the chunk in %d iterations", e->dec_pending_max_it); return -1; }
+    }
+    float step_ms = 0.0f, enc_ms = 0.0f;
     if (cudaEventElapsedTime(&step_ms, e->ev0, e->ev1) == cudaSuccess) e->gpu_ms += step_ms;
+    if (cudaEventElapsedTime(&enc_ms, e->ev0, e->ev_mid) == cudaSuccess) {
+        e->enc_ms += enc_ms;
+        e->dec_ms += step_ms - enc_ms;
+    }
     for (int s = 0; s < e->B; ++s) {
         const int n = e->h_ntok[s] < d->tok_cap ? e->h_ntok[s] : d->tok_cap;
         for (int i = 0; i < n; ++i)
             if (counts[s] < max_tokens) tokens[(size_t)s * max_tokens + counts[s]++] = e->h_tokens[(size_t)s * d->tok_cap + i];
     }
-    e->enc_ms += t1 - t0;
-    e->dec_ms += nb_now_ms() - t1;
     e->chunks++;
     *frames = c;
     return 1;
