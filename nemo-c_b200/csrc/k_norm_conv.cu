@@ -543,10 +543,65 @@ extern "C" int nemo_layernorm2(const float *X, const float *g1, const float *b1,
     return nb_check_launch("layernorm2_kernel");
 }
 
+// The same for D = 1024 and 9 taps with one block (8 warps) per output row: warp j owns channels
+// [128 j, 128 j + 128), so each thread has only its 4 channels' 9 weight and 9 input vectors to
+// load (all in flight at once), and the two-pass LayerNorm reduces across the warps in shared
+// memory. Eight times the warps of the warp-per-row kernel for the same rows.
+__global__ void __launch_bounds__(256) dwconv_ln_silu_row_kernel(const float *__restrict__ din, int64_t din_sstride, const int *pos_p,
+                                                                 const float *__restrict__ W, const float *__restrict__ g, const float *__restrict__ b,
+                                                                 void *Y, int y_fmt, int64_t y_plane, int c, float eps) {
+    constexpr int D = 1024, TAPS = 9;
+    __shared__ float red[2][8];
+    nb::pdl_wait();
+    const int item = blockIdx.x, s = item / c, t = item - s * c;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, ch = 4 * (lane + 32 * warp);
+    const float *x = din + (int64_t)s * din_sstride + (int64_t)(*pos_p - (TAPS - 1) + t) * D;
+    float4 wv[TAPS], xv[TAPS];
+#pragma unroll
+    for (int q = 0; q < TAPS; ++q) wv[q] = __ldg((const float4 *)(W + ch * TAPS) + q);  // the 4 channels' 36 taps, [ch][9]
+#pragma unroll
+    for (int tap = 0; tap < TAPS; ++tap) xv[tap] = *(const float4 *)(x + (int64_t)tap * D + ch);
+    const float4 gg = __ldg((const float4 *)(g + ch)), bv = __ldg((const float4 *)(b + ch));
+    const float *w = (const float *)wv;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int tap = 0; tap < TAPS; ++tap) {
+        acc.x += w[tap] * xv[tap].x;
+        acc.y += w[9 + tap] * xv[tap].y;
+        acc.z += w[18 + tap] * xv[tap].z;
+        acc.w += w[27 + tap] * xv[tap].w;
+    }
+    float sum = nb::warp_sum(acc.x + acc.y + acc.z + acc.w);
+    if (lane == 0) red[0][warp] = sum;
+    __syncthreads();
+    float tot = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) tot += red[0][i];
+    const float mean = tot / (float)D;
+    const float a0 = acc.x - mean, a1 = acc.y - mean, a2 = acc.z - mean, a3 = acc.w - mean;
+    float q = nb::warp_sum(a0 * a0 + a1 * a1 + a2 * a2 + a3 * a3);
+    if (lane == 0) red[1][warp] = q;
+    __syncthreads();
+    float qt = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) qt += red[1][i];
+    const float inv = 1.0f / sqrtf(qt / (float)D + eps);
+    float4 o;
+    o.x = nb::silu_f(a0 * inv * gg.x + bv.x);
+    o.y = nb::silu_f(a1 * inv * gg.y + bv.y);
+    o.z = nb::silu_f(a2 * inv * gg.z + bv.z);
+    o.w = nb::silu_f(a3 * inv * gg.w + bv.w);
+    store4(Y, y_fmt, y_plane, (int64_t)item * D + ch, o);
+}
+
 extern "C" int nemo_dwconv_ln_silu(const float *din, int64_t din_sstride, const int *pos, const float *W, const float *g, const float *b, void *Y,
                                    int y_fmt, int64_t y_plane, int streams, int c, int D, int taps, float eps, void *stream) {
     if (D > LNT * LN_MAXV) return nb_set_error("nemo_dwconv_ln_silu: D=%d too large", D);
     if (streams <= 0 || c <= 0) return 0;
+    if (D == 1024 && taps == 9 && warp_rows_ok(din, Y, y_fmt, y_plane, D) && din_sstride % 4 == 0 && !((uintptr_t)W & 15)) {
+        nb::launch(dwconv_ln_silu_row_kernel, streams * c, 256, 0, (cudaStream_t)stream, din, din_sstride, pos, W, g, b, Y, y_fmt, y_plane, c, eps);
+        return nb_check_launch("dwconv_ln_silu_row_kernel");
+    }
     if (warp_rows_ok(din, Y, y_fmt, y_plane, D) && din_sstride % 4 == 0 && !((uintptr_t)W & 15)) {
         const int items = streams * c;
         nb::launch(dwconv_ln_silu_warp_kernel, (items + WROWS - 1) / WROWS, WROWS * 32, 0, (cudaStream_t)stream, din, din_sstride, pos, W, g, b, Y, y_fmt, y_plane,
