@@ -452,6 +452,48 @@ __global__ void __launch_bounds__(WROWS * 32) layernorm_warp_kernel(const float 
     for (int j = 0; j < 8; ++j) if (j < nv) store4(Y, y_fmt, y_plane, (int64_t)row * D + 4 * (lane + 32 * j), v[j]);
 }
 
+// Two-pass LayerNorm of one 1024-wide row held as one float4 per thread of a 256-thread block
+// (thread i owns columns 4i .. 4i + 3); the warps' partial sums meet in shared memory.
+__device__ __forceinline__ float4 ln_block1024(float4 v, float4 gg, float4 bb, float eps, float (&red)[2][8]) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const float s = nb::warp_sum(v.x + v.y + v.z + v.w);
+    if (lane == 0) red[0][warp] = s;
+    __syncthreads();
+    float tot = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) tot += red[0][i];
+    const float mean = tot / 1024.0f;
+    const float a0 = v.x - mean, a1 = v.y - mean, a2 = v.z - mean, a3 = v.w - mean;
+    const float q = nb::warp_sum(a0 * a0 + a1 * a1 + a2 * a2 + a3 * a3);
+    if (lane == 0) red[1][warp] = q;
+    __syncthreads();
+    float qt = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) qt += red[1][i];
+    const float inv = 1.0f / sqrtf(qt / 1024.0f + eps);
+    return make_float4(a0 * inv * gg.x + bb.x, a1 * inv * gg.y + bb.y, a2 * inv * gg.z + bb.z, a3 * inv * gg.w + bb.w);
+}
+
+// LayerNorm (and the paired second LayerNorm of layernorm2) for D = 1024 with one block per row:
+// 8x the warps of the warp-per-row kernel, one load per thread.
+__global__ void __launch_bounds__(256) layernorm_row_kernel(const float *__restrict__ X, const float *__restrict__ g, const float *__restrict__ b,
+                                                            const float *__restrict__ g2, const float *__restrict__ b2, float *Y1, void *Y, int y_fmt,
+                                                            int64_t y_plane, float eps) {
+    __shared__ float red[2][8];
+    nb::pdl_wait();
+    const int64_t base = (int64_t)blockIdx.x * 1024 + 4 * threadIdx.x;
+    const float4 x = *(const float4 *)(X + base);
+    const float4 gg = __ldg((const float4 *)(g + 4 * threadIdx.x)), bb = __ldg((const float4 *)(b + 4 * threadIdx.x));
+    float4 gg2 = make_float4(0.f, 0.f, 0.f, 0.f), bb2 = gg2;
+    if (g2) { gg2 = __ldg((const float4 *)(g2 + 4 * threadIdx.x)); bb2 = __ldg((const float4 *)(b2 + 4 * threadIdx.x)); }
+    float4 v = ln_block1024(x, gg, bb, eps, red);
+    if (g2) {
+        *(float4 *)(Y1 + base) = v;
+        v = ln_block1024(v, gg2, bb2, eps, red);  // red is free again: every warp read it before the last barrier
+    }
+    store4(Y, y_fmt, y_plane, base, v);
+}
+
 // Causal depthwise conv + LN + SiLU (src/kernels.metal:361-409), one warp per (stream, row).
 __global__ void __launch_bounds__(WROWS * 32) dwconv_ln_silu_warp_kernel(const float *__restrict__ din, int64_t din_sstride, const int *pos_p,
                                                                          const float *__restrict__ W, const float *__restrict__ g,
@@ -522,6 +564,10 @@ static int grid_for(int64_t total) {
 extern "C" int nemo_layernorm(const float *X, const float *g, const float *b, void *Y, int y_fmt, int64_t y_plane, int M, int D, float eps, void *stream) {
     if (D > LNT * LN_MAXV) return nb_set_error("nemo_layernorm: D=%d too large", D);
     if (M <= 0) return 0;
+    if (D == 1024 && warp_rows_ok(X, Y, y_fmt, y_plane, D)) {
+        nb::launch(layernorm_row_kernel, M, 256, 0, (cudaStream_t)stream, X, g, b, nullptr, nullptr, nullptr, Y, y_fmt, y_plane, eps);
+        return nb_check_launch("layernorm_row_kernel");
+    }
     if (warp_rows_ok(X, Y, y_fmt, y_plane, D)) {
         nb::launch(layernorm_warp_kernel, (M + WROWS - 1) / WROWS, WROWS * 32, 0, (cudaStream_t)stream, X, g, b, nullptr, nullptr, nullptr, Y, y_fmt, y_plane, M, D,
                                                                                               eps);
@@ -535,6 +581,10 @@ extern "C" int nemo_layernorm2(const float *X, const float *g1, const float *b1,
                                int y2_fmt, int64_t y2_plane, int M, int D, float eps, void *stream) {
     if (D > LNT * LN_MAXV) return nb_set_error("nemo_layernorm2: D=%d too large", D);
     if (M <= 0) return 0;
+    if (D == 1024 && warp_rows_ok(X, Y2, y2_fmt, y2_plane, D) && !((uintptr_t)Y1 & 15)) {
+        nb::launch(layernorm_row_kernel, M, 256, 0, (cudaStream_t)stream, X, g1, b1, g2, b2, Y1, Y2, y2_fmt, y2_plane, eps);
+        return nb_check_launch("layernorm_row_kernel");
+    }
     if (warp_rows_ok(X, Y2, y2_fmt, y2_plane, D) && !((uintptr_t)Y1 & 15)) {
         nb::launch(layernorm_warp_kernel, (M + WROWS - 1) / WROWS, WROWS * 32, 0, (cudaStream_t)stream, X, g1, b1, g2, b2, Y1, Y2, y2_fmt, y2_plane, M, D, eps);
         return nb_check_launch("layernorm_warp_kernel");
