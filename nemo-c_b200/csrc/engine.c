@@ -460,12 +460,29 @@ int nb_engine_span_wait(nb_engine_t *e) { return cudaEventSynchronize(e->span_ev
 
 /* nframes new frames of every stream from the staged spans (nb_mel_stage): upload, transform on
    the GPU into the frame queue, and queue them for the next steps. */
-int nb_engine_push_spans(nb_engine_t *e, size_t nframes, char *err, size_t errlen) {
+int nb_engine_upload_spans(nb_engine_t *e, int s0, int s1, size_t nframes, char *err, size_t errlen) {
+    if (!nframes || s1 <= s0) return 0;
+    if (!e->use_gpu_mel || e->dev_mel) { snprintf(err, errlen, "engine does not take sample spans"); return -1; }
+    if (nframes > NB_SPAN_FRAMES || s0 < 0 || s1 > e->B) { snprintf(err, errlen, "span upload of %zu frames, streams %d..%d", nframes, s0, s1); return -1; }
+    const size_t len = (nframes - 1) * NB_MEL_HOP + NB_MEL_NFFT, pitch = e->span_cap * sizeof(float);
+    if (cudaMemcpy2DAsync(e->d_span + (size_t)s0 * e->span_cap, pitch, e->h_span + (size_t)s0 * e->span_cap, pitch, len * sizeof(float), (size_t)(s1 - s0),
+                          cudaMemcpyHostToDevice, e->st) != cudaSuccess) {
+        snprintf(err, errlen, "span upload: %s", cudaGetErrorString(cudaGetLastError()));
+        return -1;
+    }
+    return 0;
+}
+
+int nb_engine_finish_spans(nb_engine_t *e, size_t nframes, char *err, size_t errlen) {
     if (!nframes) return 0;
     if (!e->use_gpu_mel || e->dev_mel) { snprintf(err, errlen, "engine does not take sample spans"); return -1; }
     if (nframes > NB_SPAN_FRAMES) { snprintf(err, errlen, "%zu frames in one span (at most %d)", nframes, NB_SPAN_FRAMES); return -1; }
     cudaStream_t st = e->st;
-    const size_t row = 128 * sizeof(float), len = (nframes - 1) * NB_MEL_HOP + NB_MEL_NFFT;
+    const size_t row = 128 * sizeof(float);
+    if (cudaEventRecord(e->span_ev, st) != cudaSuccess) {  /* the staging buffers are free again once this passes */
+        snprintf(err, errlen, "span upload: %s", cudaGetErrorString(cudaGetLastError()));
+        return -1;
+    }
     if (e->q_end - e->q_base + nframes > e->qcap) {
         /* move the frames a later window can still read (from the next window's first frame on)
            to the front of the queue; the queue is sized so source and destination never overlap */
@@ -481,12 +498,6 @@ int nb_engine_push_spans(nb_engine_t *e, size_t nframes, char *err, size_t errle
         }
         e->q_base = keep_from;
     }
-    if (cudaMemcpy2DAsync(e->d_span, e->span_cap * sizeof(float), e->h_span, e->span_cap * sizeof(float), len * sizeof(float), (size_t)e->B,
-                          cudaMemcpyHostToDevice, st) != cudaSuccess ||
-        cudaEventRecord(e->span_ev, st) != cudaSuccess) {
-        snprintf(err, errlen, "span upload: %s", cudaGetErrorString(cudaGetLastError()));
-        return -1;
-    }
     if (nb_logmel_frames(e->d_span, (int64_t)e->span_cap, e->B, (int)nframes, e->d_melq, (int64_t)e->qcap * 128, (int64_t)(e->q_end - e->q_base), st)) {
         snprintf(err, errlen, "%s", nemo_gpu_last_error());
         return -1;
@@ -494,6 +505,12 @@ int nb_engine_push_spans(nb_engine_t *e, size_t nframes, char *err, size_t errle
     e->q_end += nframes;
     e->pending_n += nframes;
     return 0;
+}
+
+int nb_engine_push_spans(nb_engine_t *e, size_t nframes, char *err, size_t errlen) {
+    if (!nframes) return 0;
+    if (nb_engine_upload_spans(e, 0, e->B, nframes, err, errlen)) return -1;
+    return nb_engine_finish_spans(e, nframes, err, errlen);
 }
 
 void nb_engine_set_taps(nb_engine_t *e, float *prompted, float *joint_enc, size_t cap_rows, int *chunk_rows, size_t cap_chunks) {

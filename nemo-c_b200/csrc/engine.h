@@ -26,6 +26,10 @@ int nb_engine_gpu_mel(const nb_engine_t *e);
 float *nb_engine_span(nb_engine_t *e, int s, size_t *cap);
 int nb_engine_span_wait(nb_engine_t *e);
 int nb_engine_push_spans(nb_engine_t *e, size_t nframes, char *err, size_t errlen);
+/* The same in two parts, so staging and uploading can overlap: upload streams [s0, s1) of the
+   staged spans (nframes frames each), then, once every stream was uploaded, transform them. */
+int nb_engine_upload_spans(nb_engine_t *e, int s0, int s1, size_t nframes, char *err, size_t errlen);
+int nb_engine_finish_spans(nb_engine_t *e, size_t nframes, char *err, size_t errlen);
 /* One encoder step + greedy decode (src/encoder.c:213-267 then src/decoder.c:92-127).
    Returns 1 if a piece was consumed, 0 if nothing to do, -1 on error. Tokens of stream s are
    appended to tokens[s*max_tokens + counts[s] ...] and counts[s] advanced; *frames = rows. */

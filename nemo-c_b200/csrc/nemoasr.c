@@ -80,17 +80,23 @@ static int feed_gpu_mel(nb_engine_t *eng, nb_mel_t **mel, const float *const *in
         const size_t len = count - off < piece ? count - off : piece;
         const int last = final && off + len >= count;
         if (nb_engine_span_wait(eng)) { snprintf(err, errlen, "span staging: device error"); rc = -1; break; }
-#pragma omp parallel for schedule(static) if (B > 1)
-        for (int s = 0; s < B; ++s) {
-            size_t cap;
-            float *span = nb_engine_span(eng, s, &cap);
-            /* a stream that never saw a sample has no frames, not a reflected empty one */
-            nf[s] = (last && len == 0 && nb_mel_total_samples(mel[s]) == 0) ? 0 : nb_mel_stage(mel[s], in[s] + off, len, last, span, cap);
+        /* streams staged in groups, each group's upload in flight while the next is staged */
+        const int G = B >= 64 ? 4 : 1;
+        for (int grp = 0; grp < G && !rc; ++grp) {
+            const int s0 = (int)((int64_t)B * grp / G), s1 = (int)((int64_t)B * (grp + 1) / G);
+#pragma omp parallel for schedule(static) if (s1 - s0 > 1)
+            for (int s = s0; s < s1; ++s) {
+                size_t cap;
+                float *span = nb_engine_span(eng, s, &cap);
+                /* a stream that never saw a sample has no frames, not a reflected empty one */
+                nf[s] = (last && len == 0 && nb_mel_total_samples(mel[s]) == 0) ? 0 : nb_mel_stage(mel[s], in[s] + off, len, last, span, cap);
+            }
+            for (int s = s0; s < s1; ++s)
+                if (nf[s] != nf[0] || nf[s] == (size_t)-1) { snprintf(err, errlen, "streams produced different frame counts (%zu vs %zu)", nf[s], nf[0]); rc = -1; break; }
+            if (!rc && nf[0] && nb_engine_upload_spans(eng, s0, s1, nf[0], err, errlen)) rc = -1;
         }
-        for (int s = 0; s < B; ++s)
-            if (nf[s] != nf[0] || nf[s] == (size_t)-1) { snprintf(err, errlen, "streams produced different frame counts (%zu vs %zu)", nf[s], nf[0]); rc = -1; break; }
         if (rc) break;
-        if (nf[0] && nb_engine_push_spans(eng, nf[0], err, errlen)) { rc = -1; break; }
+        if (nf[0] && nb_engine_finish_spans(eng, nf[0], err, errlen)) { rc = -1; break; }
         int r, rows;
         while ((r = nb_engine_step(eng, last, tokens, max_tokens, counts, &rows, err, errlen)) == 1)
             if (rows > 0) ++*chunks;

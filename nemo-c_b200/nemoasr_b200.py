@@ -248,8 +248,8 @@ class Batch:
         x = samples if isinstance(samples, np.ndarray) and samples.dtype == np.float32 and samples.ndim == 2 and samples.strides[1] == 4 else _f32(samples)
         assert x.shape[0] == self.B
         # one pointer per stream: rows need not be adjacent (a column slice of a larger array is read in place)
-        base, rs = x.ctypes.data, x.strides[0]
-        ptrs = (f32p * self.B)(*[C.cast(base + i * rs, f32p) for i in range(self.B)])
+        addr = np.uint64(x.ctypes.data) + np.arange(self.B, dtype=np.uint64) * np.uint64(x.strides[0])
+        ptrs = addr.ctypes.data_as(C.POINTER(f32p))
         tok = np.empty((self.B, max_tokens), np.int32)
         cnt = np.zeros(self.B, np.int32)
         err = C.create_string_buffer(1024)

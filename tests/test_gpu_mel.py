@@ -76,3 +76,33 @@ def test_stream_with_gpu_mel_matches_host_mel(tiny_ckpt, lat, block):
     np.testing.assert_array_equal(a["chunk_rows"], b["chunk_rows"])
     assert max(per_chunk_rel(a["prompted"], b["prompted"], a["chunk_rows"])) < REL_TOL
     assert a["tokens"] == b["tokens"]
+
+
+def _batch(host_mel, B, ckpt, lat):
+    old = os.environ.get("NEMO_HOST_MEL")
+    os.environ["NEMO_HOST_MEL"] = "1" if host_mel else "0"
+    try:
+        return nb.Batch(B, model_dir=ckpt, latency_ms=lat)
+    finally:
+        if old is None:
+            os.environ.pop("NEMO_HOST_MEL", None)
+        else:
+            os.environ["NEMO_HOST_MEL"] = old
+
+
+def test_batch_gpu_mel_grouped_staging_matches_host_mel(tiny_ckpt):
+    # 64 streams: the spans are staged and uploaded in groups
+    B, lat, block = 64, 560, 8960
+    audio = np.stack([nb.synth_audio(300 + i, 16000, seconds=3.0, pauses=True) for i in range(B)])
+    out = []
+    for host in (False, True):
+        b = _batch(host, B, tiny_ckpt, lat)
+        toks = [[] for _ in range(B)]
+        for q in range(0, audio.shape[1], block):
+            o = b.feed(audio[:, q:q + block], final=q + block >= audio.shape[1])
+            for i in range(B):
+                toks[i] += o[i]
+        b.close()
+        out.append(toks)
+    assert sum(len(t) for t in out[0]) > 0
+    assert out[0] == out[1]
