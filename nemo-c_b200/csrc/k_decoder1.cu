@@ -33,12 +33,6 @@ constexpr int MAXV = 8;      // vocabulary rows per CTA
 constexpr int MAXF = 16;     // frames per chunk
 constexpr long long WAIT_LIMIT = 2000000000LL;
 
-__device__ __forceinline__ unsigned ld_acquire(const unsigned *p) {
-    unsigned v;
-    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-    return v;
-}
-
 __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
     asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(sm100::smem_u32(dst)),
                  "l"(src), "r"(bytes), "r"(sm100::smem_u32(bar))
@@ -69,8 +63,13 @@ __device__ bool grid_sync(const NbDec1Args &a, Shared &S, unsigned &epoch) {
         asm volatile("red.relaxed.gpu.global.add.u32 [%0], 1;" ::"l"(a.bar) : "memory");
         const unsigned target = epoch * gridDim.x;
         const long long t0 = clock64();
-        while (ld_acquire(&a.bar[0]) < target) {
-            if (ld_acquire(&a.bar[1])) { S.abort = 1; break; }
+        // one relaxed 8-byte load polls the arrival count and the abort word together; the fence
+        // after the loop orders this CTA's later reads after every arrival it observed
+        for (;;) {
+            unsigned cnt, ab;
+            asm volatile("ld.relaxed.gpu.global.v2.u32 {%0, %1}, [%2];" : "=r"(cnt), "=r"(ab) : "l"(a.bar) : "memory");
+            if (cnt >= target) break;
+            if (ab) { S.abort = 1; break; }
             if (clock64() - t0 > WAIT_LIMIT) {
                 atomicExch(&a.bar[1], 1u);
                 atomicCAS(a.err, 0, 1);

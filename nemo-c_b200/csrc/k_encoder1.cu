@@ -63,12 +63,6 @@ struct Smem {
 // attention keeps the value rows of its window in the activation tile + reduction area
 static_assert(offsetof(Smem, red) + sizeof(float) * CWARPS * 2 * 2 * 128 >= MAXL * 512, "value rows do not fit");
 
-__device__ __forceinline__ unsigned ld_acquire(const unsigned *p) {
-    unsigned v;
-    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-    return v;
-}
-
 __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
     asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(sm100::smem_u32(dst)),
                  "l"(src), "r"(bytes), "r"(sm100::smem_u32(bar))
@@ -122,8 +116,13 @@ __device__ bool grid_sync(const NbEnc1Args &a, Smem &S, unsigned &epoch) {
         asm volatile("red.relaxed.gpu.global.add.u32 [%0], 1;" ::"l"(a.bar) : "memory");
         const unsigned target = epoch * gridDim.x;
         const long long t0 = clock64();
-        while (ld_acquire(&a.bar[0]) < target) {
-            if (ld_acquire(&a.bar[1])) { S.abort = 1; break; }
+        // one relaxed 8-byte load polls the arrival count and the abort word together; the fence
+        // after the loop orders this CTA's later reads after every arrival it observed
+        for (;;) {
+            unsigned cnt, ab;
+            asm volatile("ld.relaxed.gpu.global.v2.u32 {%0, %1}, [%2];" : "=r"(cnt), "=r"(ab) : "l"(a.bar) : "memory");
+            if (cnt >= target) break;
+            if (ab) { S.abort = 1; break; }
             if (clock64() - t0 > WAIT_LIMIT) {
                 atomicExch(&a.bar[1], 1u);
                 atomicCAS(a.err, 0, 1);
