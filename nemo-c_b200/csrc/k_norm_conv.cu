@@ -674,7 +674,9 @@ extern "C" int nb_dwconv2d_s2_fmt(const float *X, const float *W, const float *b
                                   int T1, int F1, int C, void *stream) {
     const int64_t total = (int64_t)streams * T1 * F1 * C;
     if (total <= 0) return 0;
-    if ((int64_t)streams * T1 <= 0x7fffffff) {
+    // by rows when there are enough rows to fill the GPU (batches); a single stream's few rows go
+    // to the element-parallel kernel
+    if ((int64_t)streams * T1 >= 148 && (int64_t)streams * T1 <= 0x7fffffff) {
         nb::launch(dwconv2d_s2_rows_kernel, (unsigned)(streams * T1), 256, 0, (cudaStream_t)stream, X, W, bias, Y, y_fmt, y_plane, T, F, T1, F1, C);
         return nb_check_launch("dwconv2d_s2_rows_kernel");
     }
@@ -716,7 +718,7 @@ extern "C" int nemo_subsample_front(const float *X, int64_t x_sstride, const flo
 extern "C" int nb_flatten_rows_fmt(const float *X, void *Y, int y_fmt, int64_t y_plane, const int *lo, int streams, int T, int F, int C, int c, void *stream) {
     const int64_t total = (int64_t)streams * c * C * F;
     if (total <= 0) return 0;
-    if ((size_t)F * C * sizeof(float) <= 48 * 1024 && (int64_t)streams * c <= 0x7fffffff) {
+    if ((size_t)F * C * sizeof(float) <= 48 * 1024 && (int64_t)streams * c >= 148 && (int64_t)streams * c <= 0x7fffffff) {
         nb::launch(flatten_rows_smem_kernel, (unsigned)(streams * c), 256, (size_t)F * C * sizeof(float), (cudaStream_t)stream, X, Y, y_fmt, y_plane, lo, T,
                    F, C, c);
         return nb_check_launch("flatten_rows_smem_kernel");
