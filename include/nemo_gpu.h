@@ -117,6 +117,16 @@ int nemo_flatten_rows(const float *X, float *Y, const int *lo, int streams, int 
    already reflected at the stream edges) and goes to out[s * out_stride + f * 128 ..]. */
 int nemo_logmel_frames(const float *span, int64_t span_stride, int streams, int nframes, float *out, int64_t out_stride, void *stream);
 
+/* Sample-rate conversion of `streams` streams at once: outputs [out0, out0 + count) of the
+   windowed-sinc resampler of src/resample.c:34-82 (the sums of produce(), src/resample.c:52-71;
+   the host keeps the FIFO bookkeeping). Output j is sum_k h(k - j r) x[k] / sum_k h(k - j r),
+   r = in_rate / out_rate, over ceil(j r - half) <= k <= floor(j r + half), with x zero outside
+   [0, nin). Row s of `in` (in_ld apart) holds input samples [in_start, in_start + in_len) of
+   stream s, which must include every k in [0, nin) the outputs reach; output j of stream s goes
+   to out[s * out_ld + j - out0]. Rates up to about 20x the output rate (shared-memory bound). */
+int nemo_resample(const float *in, int64_t in_ld, int64_t in_start, int64_t in_len, int64_t nin, int64_t out0, int count, int in_rate,
+                  int out_rate, float *out, int64_t out_ld, int streams, void *stream);
+
 /* LSTM cell on gates [rows][4H] (i, f, g, o). Replaces lstm_cell (src/kernels.metal:475-486). */
 int nemo_lstm_cell(const float *gates, const float *c_in, float *c_out, float *h_out, int rows, int H, void *stream);
 /* Joint + argmax per row: logits = W . relu(enc[r] + pred[r]) + b (W bf16 [V][H]); ties ->

@@ -37,6 +37,10 @@ struct nb_engine {
     float *d_melq;             /* [B][qcap][128] */
     size_t qcap, q_base, q_end; /* absolute frame index of queue row 0; frames produced */
     cudaEvent_t span_ev;       /* the last span upload has been read */
+    /* GPU resampler (input rates other than 16 kHz): each stream's input FIFO staged in pinned
+       memory, the outputs come back to pinned memory for the mel bookkeeping */
+    float *h_rs_in, *d_rs_in, *d_rs_out, *h_rs_out;  /* [B][rs_in_cap], [B][rs_out_cap] */
+    size_t rs_in_cap, rs_out_cap;
     /* device */
     float *d_win, *h_win;      /* [B][nwin_max][128]; h_win pinned */
     float *c0, *c1, *c2, *c3, *c4, *flat;
@@ -373,6 +377,10 @@ void nb_engine_destroy(nb_engine_t *e) {
     if (e->d_span) cudaFree(e->d_span);
     if (e->d_melq) cudaFree(e->d_melq);
     if (e->span_ev) cudaEventDestroy(e->span_ev);
+    if (e->h_rs_in) cudaFreeHost(e->h_rs_in);
+    if (e->h_rs_out) cudaFreeHost(e->h_rs_out);
+    if (e->d_rs_in) cudaFree(e->d_rs_in);
+    if (e->d_rs_out) cudaFree(e->d_rs_out);
     if (e->d_dec1) cudaFree(e->d_dec1);
     if (e->d_dec1_i) cudaFree(e->d_dec1_i);
     if (e->d_dec1_bar) cudaFree(e->d_dec1_bar);
@@ -504,6 +512,85 @@ int nb_engine_finish_spans(nb_engine_t *e, size_t nframes, char *err, size_t err
     }
     e->q_end += nframes;
     e->pending_n += nframes;
+    return 0;
+}
+
+/* Input at in_rate goes through the GPU resampler: with the log-mel on the GPU, for the rates
+   nemo_resample takes (NEMO_GPU_RESAMPLE=0 keeps the host resampler). */
+int nb_engine_gpu_resample(const nb_engine_t *e, int in_rate) {
+    const char *v = getenv("NEMO_GPU_RESAMPLE");
+    return e->use_gpu_mel && !e->dev_mel && in_rate != NB_MEL_SR && !(v && !strcmp(v, "0")) && nb_resample_smem_ok(in_rate, NB_MEL_SR);
+}
+
+/* Resample every stream's new input on the GPU. jobs[s] (nb_resampler_plan) must agree across
+   streams on everything but the FIFO contents; on success out[s] points at job.count outputs of
+   stream s in pinned memory, valid until the next call. The stream is idle on return. */
+int nb_engine_resample(nb_engine_t *e, const nb_resample_job_t *jobs, const float **out, char *err, size_t errlen) {
+    const int B = e->B;
+    const nb_resample_job_t *j = &jobs[0];
+    for (int s = 1; s < B; ++s)
+        if (jobs[s].start != j->start || jobs[s].len != j->len || jobs[s].nin != j->nin || jobs[s].out0 != j->out0 || jobs[s].count != j->count ||
+            jobs[s].in_rate != j->in_rate || jobs[s].out_rate != j->out_rate) {
+            snprintf(err, errlen, "streams resampled to different lengths (%zu vs %zu outputs)", jobs[s].count, j->count);
+            return -1;
+        }
+    if (!j->count) {
+        for (int s = 0; s < B; ++s) out[s] = jobs[s].win;  /* no outputs: any valid pointer */
+        return 0;
+    }
+    if (!nb_resample_smem_ok(j->in_rate, j->out_rate)) {
+        snprintf(err, errlen, "input rate %d Hz is beyond the GPU resampler", j->in_rate);
+        return -1;
+    }
+    if (j->count > (size_t)INT32_MAX) { snprintf(err, errlen, "%zu resampler outputs in one call", j->count); return -1; }
+    cudaStream_t st = e->st;
+    if (cudaStreamSynchronize(st) != cudaSuccess) { snprintf(err, errlen, "resampler: %s", cudaGetErrorString(cudaGetLastError())); return -1; }
+    const size_t Bz = (size_t)B;
+    if (j->len > e->rs_in_cap) {
+        if (e->h_rs_in) cudaFreeHost(e->h_rs_in);
+        if (e->d_rs_in) cudaFree(e->d_rs_in);
+        e->h_rs_in = e->d_rs_in = NULL;
+        e->rs_in_cap = 0;
+        const size_t cap = (j->len + 4095) / 4096 * 4096 * 2;
+        if (cudaMallocHost((void **)&e->h_rs_in, Bz * cap * sizeof(float)) != cudaSuccess || cudaMalloc((void **)&e->d_rs_in, Bz * cap * sizeof(float)) != cudaSuccess) {
+            snprintf(err, errlen, "resampler input buffers: %s", cudaGetErrorString(cudaGetLastError()));
+            return -1;
+        }
+        e->rs_in_cap = cap;
+    }
+    if (j->count > e->rs_out_cap) {
+        if (e->h_rs_out) cudaFreeHost(e->h_rs_out);
+        if (e->d_rs_out) cudaFree(e->d_rs_out);
+        e->h_rs_out = e->d_rs_out = NULL;
+        e->rs_out_cap = 0;
+        const size_t cap = (j->count + 4095) / 4096 * 4096 * 2;
+        if (cudaMallocHost((void **)&e->h_rs_out, Bz * cap * sizeof(float)) != cudaSuccess || cudaMalloc((void **)&e->d_rs_out, Bz * cap * sizeof(float)) != cudaSuccess) {
+            snprintf(err, errlen, "resampler output buffers: %s", cudaGetErrorString(cudaGetLastError()));
+            return -1;
+        }
+        e->rs_out_cap = cap;
+    }
+    if (j->len) {
+#pragma omp parallel for schedule(static) if (B > 1)
+        for (int s = 0; s < B; ++s) memcpy(e->h_rs_in + (size_t)s * e->rs_in_cap, jobs[s].win, j->len * sizeof(float));
+        if (cudaMemcpy2DAsync(e->d_rs_in, e->rs_in_cap * sizeof(float), e->h_rs_in, e->rs_in_cap * sizeof(float), j->len * sizeof(float), Bz,
+                              cudaMemcpyHostToDevice, st) != cudaSuccess) {
+            snprintf(err, errlen, "resampler upload: %s", cudaGetErrorString(cudaGetLastError()));
+            return -1;
+        }
+    }
+    if (nemo_resample(e->d_rs_in, (int64_t)e->rs_in_cap, j->start, (int64_t)j->len, (int64_t)j->nin, (int64_t)j->out0, (int)j->count, j->in_rate, j->out_rate,
+                      e->d_rs_out, (int64_t)e->rs_out_cap, B, st)) {
+        snprintf(err, errlen, "%s", nemo_gpu_last_error());
+        return -1;
+    }
+    if (cudaMemcpy2DAsync(e->h_rs_out, e->rs_out_cap * sizeof(float), e->d_rs_out, e->rs_out_cap * sizeof(float), j->count * sizeof(float), Bz,
+                          cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+        cudaStreamSynchronize(st) != cudaSuccess) {
+        snprintf(err, errlen, "resampler: %s", cudaGetErrorString(cudaGetLastError()));
+        return -1;
+    }
+    for (int s = 0; s < B; ++s) out[s] = e->h_rs_out + (size_t)s * e->rs_out_cap;
     return 0;
 }
 

@@ -30,6 +30,10 @@ int nb_engine_push_spans(nb_engine_t *e, size_t nframes, char *err, size_t errle
    staged spans (nframes frames each), then, once every stream was uploaded, transform them. */
 int nb_engine_upload_spans(nb_engine_t *e, int s0, int s1, size_t nframes, char *err, size_t errlen);
 int nb_engine_finish_spans(nb_engine_t *e, size_t nframes, char *err, size_t errlen);
+/* GPU resampler: the sums of every stream's nb_resampler_plan job (identical across streams but
+   for the FIFO contents); out[s] gets stream s's job.count outputs in pinned host memory. */
+int nb_engine_resample(nb_engine_t *e, const nb_resample_job_t *jobs, const float **out, char *err, size_t errlen);
+int nb_engine_gpu_resample(const nb_engine_t *e, int in_rate);
 /* One encoder step + greedy decode (src/encoder.c:213-267 then src/decoder.c:92-127).
    Returns 1 if a piece was consumed, 0 if nothing to do, -1 on error. Tokens of stream s are
    appended to tokens[s*max_tokens + counts[s] ...] and counts[s] advanced; *frames = rows. */

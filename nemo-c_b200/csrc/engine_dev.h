@@ -74,6 +74,9 @@ size_t nb_encoder1_smem(int slot_bytes);
 int nb_logmel_frames(const float *span, int64_t span_stride, int streams, int nframes, float *out, int64_t out_stride, int64_t out_row0,
                      void *stream);
 
+/* nonzero if nemo_resample (k_resample.cu) takes this rate pair */
+int nb_resample_smem_ok(int in_rate, int out_rate);
+
 int nb_set_error(const char *fmt, ...);
 int nb_gemm_tc_init(void);
 void nb_set_launch_counting(int on);

@@ -187,12 +187,14 @@ struct nb_resampler {
     float *buf;
     size_t len, cap;
     unsigned long long start, nin, nout;
-    int same;
+    int same, in_rate, out_rate;
 };
 
 nb_resampler_t *nb_resampler_create(int in_rate, int out_rate) {
     nb_resampler_t *r = calloc(1, sizeof *r);
     r->same = in_rate == out_rate;
+    r->in_rate = in_rate;
+    r->out_rate = out_rate;
     r->ratio = (double)in_rate / (double)out_rate;
     r->half = 16.0 * fmax(r->ratio, 1.0);
     r->fc2 = fmin(1.0, 1.0 / r->ratio);
@@ -210,13 +212,41 @@ static double taper(const nb_resampler_t *r, double u) {
     return r->fc2 * (fabs(a) < 1e-9 ? 1.0 : sin(a) / a) * blackman;
 }
 
+/* output nout may be produced now: its last tap has arrived, or (final) its first tap is input */
+static int ready(const nb_resampler_t *r, unsigned long long nout, int final, long *a, long *b) {
+    const double t = (double)nout * r->ratio;
+    *a = (long)ceil(t - r->half);
+    *b = (long)floor(t + r->half);
+    return final ? (unsigned long long)*a < r->nin : (unsigned long long)(*b + 1) <= r->nin;
+}
+
+/* drop input no longer reachable by any future output */
+static void retire(nb_resampler_t *r) {
+    const long keep = (long)floor((double)r->nout * r->ratio - r->half) - 2;
+    if (keep > (long)r->start) {
+        size_t drop = (size_t)keep - (size_t)r->start;
+        if (drop > r->len) drop = r->len;
+        memmove(r->buf, r->buf + drop, (r->len - drop) * sizeof(float));
+        r->len -= drop;
+        r->start += drop;
+    }
+}
+
+static void append(nb_resampler_t *r, const float *in, size_t n) {
+    if (r->len + n > r->cap) {
+        while (r->len + n > r->cap) r->cap *= 2;
+        r->buf = realloc(r->buf, r->cap * sizeof(float));
+    }
+    memcpy(r->buf + r->len, in, n * sizeof(float));
+    r->len += n;
+    r->nin += n;
+}
+
 static size_t produce(nb_resampler_t *r, float *out, size_t out_max, int final) {
     size_t k = 0;
-    while (k < out_max) {
+    long a, b;
+    while (k < out_max && ready(r, r->nout, final, &a, &b)) {
         const double t = (double)r->nout * r->ratio;
-        const long a = (long)ceil(t - r->half), b = (long)floor(t + r->half);
-        if (!final && (unsigned long long)(b + 1) > r->nin) break;
-        if (final && (unsigned long long)a >= r->nin) break;
         double acc = 0.0, wsum = 0.0;
         for (long i = a; i <= b; ++i) {
             const double h = taper(r, (double)i - t);
@@ -229,26 +259,39 @@ static size_t produce(nb_resampler_t *r, float *out, size_t out_max, int final) 
         out[k++] = (float)(wsum > 0 ? acc / wsum : 0.0);
         r->nout++;
     }
-    const long keep = (long)floor((double)r->nout * r->ratio - r->half) - 2;
-    if (keep > (long)r->start) {
-        size_t drop = (size_t)keep - (size_t)r->start;
-        if (drop > r->len) drop = r->len;
-        memmove(r->buf, r->buf + drop, (r->len - drop) * sizeof(float));
-        r->len -= drop;
-        r->start += drop;
-    }
+    retire(r);
     return k;
 }
 
 size_t nb_resampler_process(nb_resampler_t *r, const float *in, size_t n, float *out, size_t out_max) {
     if (r->same) { const size_t k = n < out_max ? n : out_max; memcpy(out, in, k * sizeof(float)); return k; }
-    if (r->len + n > r->cap) {
-        while (r->len + n > r->cap) r->cap *= 2;
-        r->buf = realloc(r->buf, r->cap * sizeof(float));
-    }
-    memcpy(r->buf + r->len, in, n * sizeof(float));
-    r->len += n;
-    r->nin += n;
+    append(r, in, n);
     return produce(r, out, out_max, 0);
 }
 size_t nb_resampler_flush(nb_resampler_t *r, float *out, size_t out_max) { return r->same ? 0 : produce(r, out, out_max, 1); }
+
+/* process (when n > 0) followed by flush (when final) of a resampler whose rates differ, with
+   the sums left to the caller: both calls' outputs form one run from nout on. */
+void nb_resampler_plan(nb_resampler_t *r, const float *in, size_t n, int final, nb_resample_job_t *job) {
+    size_t count = 0;
+    long a, b;
+    if (n) {
+        append(r, in, n);
+        while (ready(r, r->nout + count, 0, &a, &b)) ++count;
+    }
+    if (final)
+        while (ready(r, r->nout + count, 1, &a, &b)) ++count;
+    job->win = r->buf;
+    job->start = (long long)r->start;
+    job->len = r->len;
+    job->nin = r->nin;
+    job->out0 = r->nout;
+    job->count = count;
+    job->in_rate = r->in_rate;
+    job->out_rate = r->out_rate;
+}
+
+void nb_resampler_commit(nb_resampler_t *r, size_t count) {
+    r->nout += count;
+    retire(r);
+}

@@ -99,6 +99,20 @@ nb_resampler_t *nb_resampler_create(int in_rate, int out_rate);
 void nb_resampler_destroy(nb_resampler_t *r);
 size_t nb_resampler_process(nb_resampler_t *r, const float *in, size_t n, float *out, size_t out_max);
 size_t nb_resampler_flush(nb_resampler_t *r, float *out, size_t out_max);
+/* The sums of one process (+ flush when final) call, left to the GPU (nemo_resample): the input
+   FIFO after appending `in`, and the outputs [out0, out0 + count) it now allows. */
+typedef struct {
+    const float *win;        /* input samples [start, start + len) */
+    long long start;
+    size_t len;
+    unsigned long long nin;  /* input samples seen (zero beyond) */
+    unsigned long long out0;
+    size_t count;
+    int in_rate, out_rate;
+} nb_resample_job_t;
+void nb_resampler_plan(nb_resampler_t *r, const float *in, size_t n, int final, nb_resample_job_t *job);
+/* The job's outputs are done: advance past them and drop the input no later output reads. */
+void nb_resampler_commit(nb_resampler_t *r, size_t count);
 
 double nb_now_ms(void);
 

@@ -175,7 +175,13 @@ static int feed_tokens(nemoasr_t *s, const float *samples, size_t n, int final, 
     if (s->finished) return 0;
     const float *in = samples;
     size_t count = n;
-    if (s->rs) {
+    if (s->rs && nb_engine_gpu_resample(s->eng, s->input_rate)) {
+        nb_resample_job_t job;
+        nb_resampler_plan(s->rs, samples, n, final, &job);
+        if (nb_engine_resample(s->eng, &job, &in, err, errlen)) return -1;
+        nb_resampler_commit(s->rs, job.count);
+        count = job.count;
+    } else if (s->rs) {
         const size_t need = (size_t)((double)n * NB_MEL_SR / s->input_rate) + 4096;
         if (need > s->tmp_cap) { s->tmp_cap = need * 2; s->tmp = realloc(s->tmp, s->tmp_cap * sizeof(float)); }
         count = n ? nb_resampler_process(s->rs, samples, n, s->tmp, s->tmp_cap) : 0;
@@ -354,11 +360,17 @@ int nemoasr_batch_feed(nemoasr_batch_t *b, const float *const *samples, size_t n
         for (int s = 0; s < B; ++s) b->tmp[s] = realloc(b->tmp[s], b->tmp_cap * sizeof(float));
     }
     const int gpu_mel = nb_engine_gpu_mel(b->eng);
+    const int gpu_rs = b->rs[0] && nb_engine_gpu_resample(b->eng, b->input_rate);
     const float **ins = calloc((size_t)B, sizeof *ins);
+    nb_resample_job_t *jobs = gpu_rs ? calloc((size_t)B, sizeof *jobs) : NULL;
 #pragma omp parallel for schedule(dynamic, 4)
     for (int s = 0; s < B; ++s) {
         const float *in = samples[s];
         size_t c = n;
+        if (gpu_rs) {
+            nb_resampler_plan(b->rs[s], samples[s], n, final, &jobs[s]);
+            continue;
+        }
         if (b->rs[s]) {
             c = n ? nb_resampler_process(b->rs[s], samples[s], n, b->tmp[s], b->tmp_cap) : 0;
             if (final) c += nb_resampler_flush(b->rs[s], b->tmp[s] + c, b->tmp_cap - c);
@@ -371,8 +383,16 @@ int nemoasr_batch_feed(nemoasr_batch_t *b, const float *const *samples, size_t n
         nb_mel_push(b->mel[s], in, c, final, &b->frames[s], &nf[s]);
     }
     int rc = 0;
+    if (gpu_rs) {
+        rc = nb_engine_resample(b->eng, jobs, ins, err, errlen);
+        for (int s = 0; s < B && !rc; ++s) {
+            nb_resampler_commit(b->rs[s], jobs[s].count);
+            cnt[s] = jobs[s].count;
+        }
+        free(jobs);
+    }
     if (gpu_mel) {
-        for (int s = 1; s < B; ++s)
+        for (int s = 1; s < B && !rc; ++s)
             if (cnt[s] != cnt[0]) { snprintf(err, errlen, "streams resampled to different lengths (%zu vs %zu)", cnt[s], cnt[0]); rc = -1; break; }
         b->stats.audio_seconds += (double)cnt[0] / NB_MEL_SR * B;
         if (!rc) rc = feed_gpu_mel(b->eng, b->mel, ins, cnt[0], B, final, tokens, max_tokens, counts, &b->stats.chunks, err, errlen);
