@@ -52,6 +52,8 @@ def parse():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-single", action="store_true", help="skip the single-stream (config #1) chunk latency")
     ap.add_argument("--kernel-only", action="store_true", help="time only the dominant GEMM (small device footprint, for ncu captures)")
+    ap.add_argument("--resample-only", type=int, default=0, metavar="RATE",
+                    help="time only the GPU resampler: one chunk of every stream arriving at RATE Hz (small device footprint, for ncu captures)")
     return ap.parse_args()
 
 
@@ -164,6 +166,44 @@ def dominant_gemm(nb, torch, a, B, c):
     return ms, 2.0 * M * N * K
 
 
+def resample_kernel(nb, torch, a, rate):
+    """CUDA-event time of nemo_resample over one chunk of every stream (the outputs of one
+    latency-long chunk, from the inputs they reach), averaged over 20 launches; beside it the
+    host resampler's time for the same chunk of one stream on one thread."""
+    import ctypes as C
+    L = nb.api()
+    L.nemo_resample.argtypes = [C.c_void_p, C.c_int64, C.c_int64, C.c_int64, C.c_int64, C.c_int64, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_int64,
+                                C.c_int, C.c_void_p]
+    B, count = a.streams, a.latency * 16
+    ratio = rate / 16000
+    out0 = 1000
+    start = int(np.ceil(out0 * ratio - 16.0 * max(ratio, 1.0)))
+    nin = int(np.floor((out0 + count - 1) * ratio + 16.0 * max(ratio, 1.0))) + 1
+    x = torch.randn(B, nin - start, device="cuda") * 0.1
+    y = torch.empty(B, count, device="cuda")
+    st = torch.cuda.current_stream()
+
+    def run():
+        if L.nemo_resample(x.data_ptr(), nin - start, start, nin - start, nin, out0, count, rate, 16000, y.data_ptr(), count, B, st.cuda_stream):
+            raise RuntimeError(L.nemo_gpu_last_error().decode())
+    for _ in range(3):
+        run()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record(st)
+    for _ in range(20):
+        run()
+    e1.record(st)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / 20
+    audio = np.ascontiguousarray(nb.synth_audio(1, rate, seconds=a.latency / 1000 * 4), np.float32)
+    t0 = time.perf_counter()
+    nb.resample(audio, rate, 16000, block=rate * a.latency // 1000)
+    host_ms = (time.perf_counter() - t0) / 4 * 1e3
+    return {"kernel": "nemo_resample", "rate": rate, "streams": B, "outputs_per_stream": count, "inputs_per_stream": nin - start, "us": ms * 1e3,
+            "outputs_per_s": B * count / (ms / 1e3), "host_ms_per_stream_chunk_1_thread": host_ms}
+
+
 def single_stream(nb, torch, peaks, seconds=12.0, latency=560):
     """BASELINE config #1 shape: one stream, full model, 560 ms chunks, mel resident in HBM.
     Per-chunk device time (CUDA events around each chunk's graphs); HBM fraction = the chunk's
@@ -274,6 +314,11 @@ def main():
         c = a.latency // 80
         ms, flops = dominant_gemm(nb, torch, a, a.streams, c)
         print(json.dumps({"kernel": "nemo_gemm FF-in", "M": a.streams * c, "N": 4096, "K": 1024, "us": ms * 1e3, "tflops": flops / ms / 1e9}))
+        return
+    if a.resample_only:
+        import torch
+        import nemoasr_b200 as nb
+        print(json.dumps(resample_kernel(nb, torch, a, a.resample_only)))
         return
     a.seconds = max(a.seconds, (a.warmup + a.steps + 3) * a.latency / 1000.0)
     import torch
