@@ -52,6 +52,8 @@ def parse():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-single", action="store_true", help="skip the single-stream (config #1) chunk latency")
     ap.add_argument("--kernel-only", action="store_true", help="time only the dominant GEMM (small device footprint, for ncu captures)")
+    ap.add_argument("--session48k", type=float, default=0, metavar="SECONDS",
+                    help="BASELINE config #3 only: one stream, 80 ms chunks, SECONDS of 48 kHz audio through the public API, GPU vs host resampler")
     ap.add_argument("--resample-only", type=int, default=0, metavar="RATE",
                     help="time only the GPU resampler: one chunk of every stream arriving at RATE Hz (small device footprint, for ncu captures)")
     return ap.parse_args()
@@ -204,6 +206,42 @@ def resample_kernel(nb, torch, a, rate):
             "outputs_per_s": B * count / (ms / 1e3), "host_ms_per_stream_chunk_1_thread": host_ms}
 
 
+def session_48k(nb, seconds, latency=80, rate=48000):
+    """BASELINE config #3 shape: one stream of the full model, 80 ms chunks, 48 kHz audio fed in
+    100 ms blocks through the public API (nemoasr_feed_tokens), host buffers in, tokens out.
+    Wall time of every feed, with the GPU resampler and with the host resampler
+    (NEMO_GPU_RESAMPLE=0, read at each feed); a 2 s pass first captures the graphs."""
+    audio = nb.synth_audio(3, rate, seconds=seconds, pauses=True)
+    s = nb.Session(spec=nb.synth_default(), latency_ms=latency, rate=rate)
+    block = rate // 10
+    out = {}
+    old = os.environ.get("NEMO_GPU_RESAMPLE")
+    try:
+        for mode in ("warm-up", "gpu", "host"):
+            os.environ["NEMO_GPU_RESAMPLE"] = "0" if mode == "host" else "1"
+            s.reset(latency_ms=latency)
+            x = audio[: 2 * rate] if mode == "warm-up" else audio
+            ts, toks, c0 = [], 0, s.stats()["chunks"]  # stats run on across resets
+            t_all = time.perf_counter()
+            for q in range(0, len(x), block):
+                t0 = time.perf_counter()
+                toks += len(s.feed_tokens(x[q:q + block], final=q + block >= len(x)))
+                ts.append(time.perf_counter() - t0)
+            wall = time.perf_counter() - t_all
+            if mode != "warm-up":
+                st = s.stats()
+                out[mode] = {"rtfx": len(x) / rate / wall, "p50_feed_ms": float(np.median(ts)) * 1e3, "p99_feed_ms": float(np.percentile(ts, 99)) * 1e3,
+                             "chunks": st["chunks"] - c0, "tokens": toks}
+    finally:
+        if old is None:
+            os.environ.pop("NEMO_GPU_RESAMPLE", None)
+        else:
+            os.environ["NEMO_GPU_RESAMPLE"] = old
+    s.close()
+    return {"workload": f"BASELINE config #3 shape: 1 stream, {latency} ms chunks, {seconds:g} s of 48 kHz audio in 100 ms feeds, public API",
+            "gpu_resampler": out["gpu"], "host_resampler": out["host"]}
+
+
 def single_stream(nb, torch, peaks, seconds=12.0, latency=560):
     """BASELINE config #1 shape: one stream, full model, 560 ms chunks, mel resident in HBM.
     Per-chunk device time (CUDA events around each chunk's graphs); HBM fraction = the chunk's
@@ -314,6 +352,11 @@ def main():
         c = a.latency // 80
         ms, flops = dominant_gemm(nb, torch, a, a.streams, c)
         print(json.dumps({"kernel": "nemo_gemm FF-in", "M": a.streams * c, "N": 4096, "K": 1024, "us": ms * 1e3, "tflops": flops / ms / 1e9}))
+        return
+    if a.session48k:
+        import torch  # noqa: F401 (CUDA context as in the other modes)
+        import nemoasr_b200 as nb
+        print(json.dumps(session_48k(nb, a.session48k)))
         return
     if a.resample_only:
         import torch
