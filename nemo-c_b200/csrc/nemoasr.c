@@ -346,12 +346,51 @@ void nemoasr_batch_close(nemoasr_batch_t *b) {
     free(b);
 }
 
+/* Batch feed at an input rate other than 16 kHz through the GPU resampler, in passes of at most
+   one second of input per stream so that the staging buffers stay bounded whatever the feed size
+   (the streaming resampler and log-mel give the same outputs under any split of the input). */
+static int batch_feed_resampled(nemoasr_batch_t *b, const float *const *samples, size_t n, int final, int *tokens, int max_tokens, int *counts,
+                                char *err, size_t errlen) {
+    const int B = b->B;
+    const size_t piece = (size_t)b->input_rate;
+    nb_resample_job_t *jobs = calloc((size_t)B, sizeof *jobs);
+    const float **ins = calloc((size_t)B, sizeof *ins);
+    size_t off = 0;
+    int rc = 0;
+    do {
+        const size_t len = n - off < piece ? n - off : piece;
+        const int last = final && off + len >= n;
+#pragma omp parallel for schedule(static) if (B > 1)
+        for (int s = 0; s < B; ++s) nb_resampler_plan(b->rs[s], len ? samples[s] + off : NULL, len, last, &jobs[s]);
+        if ((rc = nb_engine_resample(b->eng, jobs, ins, err, errlen))) break;
+        const size_t count = jobs[0].count;
+        for (int s = 0; s < B; ++s) nb_resampler_commit(b->rs[s], jobs[s].count);
+        b->stats.audio_seconds += (double)count / NB_MEL_SR * B;
+        if ((rc = feed_gpu_mel(b->eng, b->mel, ins, count, B, last, tokens, max_tokens, counts, &b->stats.chunks, err, errlen))) break;
+        off += len;
+    } while (off < n);
+    free(jobs);
+    free(ins);
+    return rc;
+}
+
 int nemoasr_batch_feed(nemoasr_batch_t *b, const float *const *samples, size_t n, int final, int *tokens, int max_tokens, int *counts, char *err,
                        size_t errlen) {
     if (errlen) err[0] = 0;
     for (int s = 0; s < b->B; ++s) counts[s] = 0;
     if (b->finished) return 0;
     const int B = b->B;
+    if (b->rs[0] && nb_engine_gpu_resample(b->eng, b->input_rate)) {
+        const int rc = batch_feed_resampled(b, samples, n, final, tokens, max_tokens, counts, err, errlen);
+        if (final) b->finished = 1;
+        for (int s = 0; s < B; ++s) b->stats.tokens += (size_t)counts[s];
+        double enc, dec;
+        size_t ch;
+        nb_engine_times(b->eng, &enc, &dec, &ch);
+        b->stats.encoder_ms = enc;
+        b->stats.decoder_ms = dec;
+        return rc;
+    }
     size_t *nf = calloc((size_t)B, sizeof *nf);
     size_t *cnt = calloc((size_t)B, sizeof *cnt);
     const size_t need = (size_t)((double)n * NB_MEL_SR / b->input_rate) + 4096;
@@ -360,17 +399,11 @@ int nemoasr_batch_feed(nemoasr_batch_t *b, const float *const *samples, size_t n
         for (int s = 0; s < B; ++s) b->tmp[s] = realloc(b->tmp[s], b->tmp_cap * sizeof(float));
     }
     const int gpu_mel = nb_engine_gpu_mel(b->eng);
-    const int gpu_rs = b->rs[0] && nb_engine_gpu_resample(b->eng, b->input_rate);
     const float **ins = calloc((size_t)B, sizeof *ins);
-    nb_resample_job_t *jobs = gpu_rs ? calloc((size_t)B, sizeof *jobs) : NULL;
 #pragma omp parallel for schedule(dynamic, 4)
     for (int s = 0; s < B; ++s) {
         const float *in = samples[s];
         size_t c = n;
-        if (gpu_rs) {
-            nb_resampler_plan(b->rs[s], samples[s], n, final, &jobs[s]);
-            continue;
-        }
         if (b->rs[s]) {
             c = n ? nb_resampler_process(b->rs[s], samples[s], n, b->tmp[s], b->tmp_cap) : 0;
             if (final) c += nb_resampler_flush(b->rs[s], b->tmp[s] + c, b->tmp_cap - c);
@@ -383,16 +416,8 @@ int nemoasr_batch_feed(nemoasr_batch_t *b, const float *const *samples, size_t n
         nb_mel_push(b->mel[s], in, c, final, &b->frames[s], &nf[s]);
     }
     int rc = 0;
-    if (gpu_rs) {
-        rc = nb_engine_resample(b->eng, jobs, ins, err, errlen);
-        for (int s = 0; s < B && !rc; ++s) {
-            nb_resampler_commit(b->rs[s], jobs[s].count);
-            cnt[s] = jobs[s].count;
-        }
-        free(jobs);
-    }
     if (gpu_mel) {
-        for (int s = 1; s < B && !rc; ++s)
+        for (int s = 1; s < B; ++s)
             if (cnt[s] != cnt[0]) { snprintf(err, errlen, "streams resampled to different lengths (%zu vs %zu)", cnt[s], cnt[0]); rc = -1; break; }
         b->stats.audio_seconds += (double)cnt[0] / NB_MEL_SR * B;
         if (!rc) rc = feed_gpu_mel(b->eng, b->mel, ins, cnt[0], B, final, tokens, max_tokens, counts, &b->stats.chunks, err, errlen);

@@ -82,7 +82,8 @@ def _batch(gpu_rs, B, ckpt, langs, rate):
             os.environ["NEMO_GPU_RESAMPLE"] = old
 
 
-@pytest.mark.parametrize("rate,block", [(48000, 4800), (44100, 7777)])
+# the last case feeds each stream's 3 s in one call: three one-second resampler passes on the GPU side
+@pytest.mark.parametrize("rate,block", [(48000, 4800), (44100, 7777), (48000, 1 << 30)])
 def test_batch_gpu_resampler_matches_host_resampler(tiny_ckpt, tiny_oracle, rate, block):
     B = 6
     langs = ["auto", "en-US"] * (B // 2)
