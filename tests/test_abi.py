@@ -90,3 +90,19 @@ def test_gemm_rejects_bad_shapes():
     a = nb.GemmArgs()
     assert lib.nemo_gemm(C.byref(a), None) == -1
     assert b"null pointer" in lib.nemo_gpu_last_error()
+
+
+def test_resample_rejects_bad_arguments():
+    """Checked on the host before any launch: rates, a window past the samples seen, an output
+    row shorter than the outputs asked for, and rates whose weight rows exceed shared memory."""
+    lib = nb.api()
+    lib.nemo_resample.argtypes = [C.c_void_p, C.c_int64, C.c_int64, C.c_int64, C.c_int64, C.c_int64, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_int64,
+                                  C.c_int, C.c_void_p]
+    assert lib.nemo_resample(None, 64, 0, 64, 64, 0, 8, 0, 16000, None, 64, 1, None) == -1
+    assert b"rates" in lib.nemo_gpu_last_error()
+    assert lib.nemo_resample(None, 64, 10, 64, 32, 0, 8, 48000, 16000, None, 64, 1, None) == -1
+    assert b"window" in lib.nemo_gpu_last_error()
+    assert lib.nemo_resample(None, 64, 0, 64, 64, 0, 80, 48000, 16000, None, 64, 1, None) == -1
+    assert lib.nemo_resample(None, 1 << 20, 0, 1 << 20, 1 << 20, 0, 8, 1000000, 16000, None, 64, 1, None) == -1
+    assert b"shared memory" in lib.nemo_gpu_last_error()
+    assert lib.nemo_resample(None, 64, 0, 64, 64, 0, 0, 48000, 16000, None, 64, 1, None) == 0  # nothing to do
