@@ -106,11 +106,14 @@ static void mel_advance(nb_mel_t *m, const float *samples, size_t n, int final, 
         while (m->y_len + n > m->y_cap) m->y_cap *= 2;
         m->y = realloc(m->y, m->y_cap * sizeof(float));
     }
-    for (size_t i = 0; i < n; ++i) {
-        const float x = samples[i];
-        m->y[m->y_len++] = m->have_last ? x - 0.97f * m->last_x : x;
-        m->last_x = x;
+    if (n) {
+        /* y[i] = x[i] - 0.97 x[i-1]; the first sample of the stream is kept as it is */
+        float *y = m->y + m->y_len;
+        y[0] = m->have_last ? samples[0] - 0.97f * m->last_x : samples[0];
+        for (size_t i = 1; i < n; ++i) y[i] = samples[i] - 0.97f * samples[i - 1];
+        m->last_x = samples[n - 1];
         m->have_last = 1;
+        m->y_len += n;
     }
     m->total += n;
     const size_t end = final ? m->total / NB_MEL_HOP + 1 : (m->total >= LOOKAHEAD ? (m->total - LOOKAHEAD) / NB_MEL_HOP + 1 : 0);
@@ -167,8 +170,20 @@ size_t nb_mel_stage(nb_mel_t *m, const float *samples, size_t n, int final, floa
     if (!count) return 0;
     const size_t len = (count - 1) * NB_MEL_HOP + NB_MEL_NFFT;
     if (len > span_cap) return (size_t)-1;
-    const long start = (long)t0 * NB_MEL_HOP - LOOKAHEAD;
-    for (size_t i = 0; i < len; ++i) span[i] = sample_at(m, start + (long)i);
+    /* samples inside the stream and the buffer are copied as a run; only the reflected edges
+       (and anything outside the buffer) go through sample_at */
+    const long s0 = (long)t0 * NB_MEL_HOP - LOOKAHEAD, s1 = s0 + (long)len;
+    const long lo_buf = (long)m->y_start, hi_buf = lo_buf + (long)m->y_len;
+    long a = s0 > 0 ? s0 : 0, b = s1 < (long)m->total ? s1 : (long)m->total;
+    if (a < lo_buf) a = lo_buf;
+    if (b > hi_buf) b = hi_buf;
+    if (a < b) {
+        for (long g = s0; g < a; ++g) span[g - s0] = sample_at(m, g);
+        memcpy(span + (a - s0), m->y + (a - lo_buf), (size_t)(b - a) * sizeof(float));
+        for (long g = b; g < s1; ++g) span[g - s0] = sample_at(m, g);
+    } else {
+        for (long g = s0; g < s1; ++g) span[g - s0] = sample_at(m, g);
+    }
     mel_retire(m, t0 + count);
     return count;
 }

@@ -228,6 +228,20 @@ class Session:
             pass
 
 
+def _token_lists(tok, cnt):
+    """Row s of tok holds cnt[s] token ids: one list per row, converted in one pass over the
+    tokens actually written."""
+    m = int(cnt.max()) if len(cnt) else 0
+    if m == 0:
+        return [[] for _ in range(len(cnt))]
+    flat = tok[:, :m][np.arange(m)[None, :] < cnt[:, None]].tolist()
+    out, s = [], 0
+    for e in np.cumsum(cnt).tolist():
+        out.append(flat[s:e])
+        s = e
+    return out
+
+
 class Batch:
     """B lockstep streams on the current GPU (nemoasr_batch_*)."""
 
@@ -250,13 +264,15 @@ class Batch:
         # one pointer per stream: rows need not be adjacent (a column slice of a larger array is read in place)
         addr = np.uint64(x.ctypes.data) + np.arange(self.B, dtype=np.uint64) * np.uint64(x.strides[0])
         ptrs = addr.ctypes.data_as(C.POINTER(f32p))
-        tok = np.empty((self.B, max_tokens), np.int32)
+        tok = getattr(self, "_tok", None)
+        if tok is None or tok.shape[1] != max_tokens:
+            tok = self._tok = np.empty((self.B, max_tokens), np.int32)
         cnt = np.zeros(self.B, np.int32)
         err = C.create_string_buffer(1024)
         rc = api().nemoasr_batch_feed(self.h, ptrs, x.shape[1], int(final), tok.ctypes.data_as(i32p), max_tokens, cnt.ctypes.data_as(i32p), err, 1024)
         if rc:
             raise RuntimeError(err.value.decode())
-        return [tok[i, :cnt[i]].tolist() for i in range(self.B)]
+        return _token_lists(tok, cnt)
 
     def set_taps(self, rows, d_model, joint_hidden):
         self.tp = np.zeros((rows, d_model), np.float32)
