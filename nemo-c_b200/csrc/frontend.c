@@ -285,17 +285,30 @@ size_t nb_resampler_process(nb_resampler_t *r, const float *in, size_t n, float 
 }
 size_t nb_resampler_flush(nb_resampler_t *r, float *out, size_t out_max) { return r->same ? 0 : produce(r, out, out_max, 1); }
 
+/* How many outputs from j on are ready (the same count as testing ready() one output at a
+   time). From a ready output on, the ready outputs form one run: the first and last taps only
+   grow with the output index. The run's end is estimated from the tap formula and then settled
+   with ready() itself, a step or two either way. */
+static size_t ready_run(const nb_resampler_t *r, unsigned long long j, int final) {
+    long a, b;
+    if (!ready(r, j, final, &a, &b)) return 0;
+    /* last ready output: final, ceil(k ratio - half) <= nin - 1; else floor(k ratio + half) <= nin - 1 */
+    const double est = ((double)r->nin - 1.0 + (final ? r->half : -r->half)) / r->ratio;
+    unsigned long long k = est > (double)j ? (unsigned long long)est : j;
+    while (k > j && !ready(r, k, final, &a, &b)) --k;
+    while (ready(r, k + 1, final, &a, &b)) ++k;
+    return (size_t)(k - j + 1);
+}
+
 /* process (when n > 0) followed by flush (when final) of a resampler whose rates differ, with
    the sums left to the caller: both calls' outputs form one run from nout on. */
 void nb_resampler_plan(nb_resampler_t *r, const float *in, size_t n, int final, nb_resample_job_t *job) {
     size_t count = 0;
-    long a, b;
     if (n) {
         append(r, in, n);
-        while (ready(r, r->nout + count, 0, &a, &b)) ++count;
+        count = ready_run(r, r->nout, 0);
     }
-    if (final)
-        while (ready(r, r->nout + count, 1, &a, &b)) ++count;
+    if (final) count += ready_run(r, r->nout + count, 1);
     job->win = r->buf;
     job->start = (long long)r->start;
     job->len = r->len;
