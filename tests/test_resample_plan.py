@@ -105,3 +105,32 @@ def test_plan_final_only_short_input():
     assert job.count == n
     L.nb_resampler_destroy(r)
     L.nemoasr_resampler_destroy(h)
+
+
+def test_plan_counts_match_host_across_rates():
+    """Output counts of planned feeds against the host's process + flush, for down- and
+    upsampling rates (including ones that share no factor with 16 kHz), random splits, with and
+    without a final call."""
+    L = lib()
+    rng = np.random.default_rng(11)
+    for trial in range(60):
+        rate = int(rng.choice([7999, 8000, 11025, 12345, 22050, 44100, 48000, 96000, 15999, 16001]))
+        n = int(rng.integers(0, 20000))
+        x = rng.standard_normal(n).astype(np.float32)
+        pieces = np.split(x, np.sort(rng.integers(0, n + 1, size=int(rng.integers(0, 6))))) if n else [x]
+        final = bool(rng.integers(0, 2))
+        rh, rp = L.nemoasr_resampler_create(rate, 16000), L.nb_resampler_create(rate, 16000)
+        for i, p in enumerate(pieces):
+            last = final and i == len(pieces) - 1
+            p = np.ascontiguousarray(p, np.float32)
+            cap = int(p.size * 16000 / rate) + 8192
+            buf = np.zeros(cap, np.float32)
+            c = L.nemoasr_resampler_process(rh, p.ctypes.data_as(f32p), p.size, buf.ctypes.data_as(f32p), cap) if p.size else 0
+            if last:
+                c += L.nemoasr_resampler_flush(rh, buf[c:].ctypes.data_as(f32p), cap - c)
+            job = Job()
+            L.nb_resampler_plan(rp, p.ctypes.data_as(f32p), p.size, int(last), C.byref(job))
+            assert job.count == c, f"rate {rate}, {n} samples, piece {i}: planned {job.count}, host {c}"
+            L.nb_resampler_commit(rp, job.count)
+        L.nemoasr_resampler_destroy(rh)
+        L.nb_resampler_destroy(rp)
