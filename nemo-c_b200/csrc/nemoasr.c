@@ -400,7 +400,7 @@ int nemoasr_batch_feed(nemoasr_batch_t *b, const float *const *samples, size_t n
     }
     const int gpu_mel = nb_engine_gpu_mel(b->eng);
     const float **ins = calloc((size_t)B, sizeof *ins);
-#pragma omp parallel for schedule(dynamic, 4)
+#pragma omp parallel for schedule(dynamic, 4) if (!gpu_mel || b->rs[0])  /* with the GPU log-mel and no resampler the loop only copies pointers */
     for (int s = 0; s < B; ++s) {
         const float *in = samples[s];
         size_t c = n;
