@@ -13,7 +13,13 @@ stream: subsampling, 24 conformer blocks, prompt, joint projection and the greed
           reads inside the timed region.
 
 Streams shard across GPUs with no collective (one process per GPU); torch.distributed is used
-only for the start barrier and the max-over-ranks of the timings.
+only for the start barrier and the max-over-ranks of the timings. Under torchrun every rank gets
+an equal share of the host's cores for its OpenMP and thread-pool work.
+
+The same line carries the other BASELINE configs measured in the run: `single_stream` (config
+#1: one stream, 4.0 s, 560 ms chunks), `config5` (1024 streams per GPU at 1120 ms with the blank
+bias calibrated for ~35 % emitting frames); `--sweep` prints config #2 (the GEMM sweep) and
+`--session48k` config #3, one line each.
 
   python bench.py [--gpus N --steps K --warmup W] [--impl reference]
 """
@@ -31,6 +37,17 @@ import numpy as np
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, os.path.join(ROOT, "nemo-c_b200"))
 sys.path.insert(0, os.path.join(ROOT, "tests"))
+
+
+def host_threads():
+    """Host threads this rank may use: all cores alone, an equal share under torchrun."""
+    per_node = max(1, int(os.environ.get("LOCAL_WORLD_SIZE", "1")))
+    return max(1, (os.cpu_count() or 8) // per_node)
+
+
+# OpenMP in the product library and the oracle reads this when the library loads
+if int(os.environ.get("LOCAL_WORLD_SIZE", "1")) > 1:
+    os.environ["OMP_NUM_THREADS"] = str(host_threads())
 
 METRIC = "audio-sec/sec (RTFx) at N streams on 1/2/4/8 B200"
 # DRAM bytes of one FF-in launch at 1792 rows (8.39 MB weights + 7.34 MB activation planes
@@ -56,6 +73,11 @@ def parse():
                     help="BASELINE config #3 only: one stream, 80 ms chunks, SECONDS of 48 kHz audio through the public API, GPU vs host resampler")
     ap.add_argument("--resample-only", type=int, default=0, metavar="RATE",
                     help="time only the GPU resampler: one chunk of every stream arriving at RATE Hz (small device footprint, for ncu captures)")
+    ap.add_argument("--no-config5", action="store_true", help="skip the nested BASELINE config #5 measurement")
+    ap.add_argument("--config5-streams", type=int, default=1024)
+    ap.add_argument("--config5-steps", type=int, default=5)
+    ap.add_argument("--sweep", action="store_true", help="BASELINE config #2 only: the GEMM sweep, one JSON line per case")
+    ap.add_argument("--calibrate", action="store_true", help="find the config #5 blank bias (~35 %% of stream-frames emit) and print it")
     return ap.parse_args()
 
 
@@ -109,7 +131,7 @@ def make_inputs(nb, a, rank):
     n = int(round(a.seconds * 16000))
     audio = np.zeros((a.streams, n), np.float32)
     seeds = stream_seeds(a, rank)
-    with ThreadPoolExecutor(min(32, os.cpu_count() or 8)) as ex:
+    with ThreadPoolExecutor(min(32, host_threads())) as ex:
         for s, x in enumerate(ex.map(lambda sd: nb.synth_audio(sd, 16000, n=n, pauses=True), seeds)):
             audio[s] = x
         mels = list(ex.map(lambda s: nb.mel(audio[s]), range(a.streams)))
@@ -206,14 +228,24 @@ def resample_kernel(nb, torch, a, rate):
             "outputs_per_s": B * count / (ms / 1e3), "host_ms_per_stream_chunk_1_thread": host_ms}
 
 
-def session_48k(nb, seconds, latency=80, rate=48000):
-    """BASELINE config #3 shape: one stream of the full model, 80 ms chunks, 48 kHz audio fed in
-    100 ms blocks through the public API (nemoasr_feed_tokens), host buffers in, tokens out.
-    Wall time of every feed, with the GPU resampler and with the host resampler
-    (NEMO_GPU_RESAMPLE=0, read at each feed); a 2 s pass first captures the graphs."""
+def session_48k(nb, seconds, latency=80, rate=48000, peaks=None):
+    """BASELINE config #3: one stream of the full model, 80 ms chunks, 48 kHz audio resampled
+    internally, fed in 80 ms blocks through the public API (nemoasr_feed_tokens), host buffers in,
+    tokens out. Per chunk (one graph launch of the step: encoder graph + persistent decoder) the
+    device time from the engine's CUDA events (nemoasr_stats encoder_ms + decoder_ms, read after
+    each feed, every steady feed makes exactly one chunk), p50 / p99 and the HBM fraction of its
+    1.1765 GB of weights; beside it the wall time of every feed (resampling, log-mel, the step and
+    the token read). GPU resampler, then the host resampler (NEMO_GPU_RESAMPLE=0). The session
+    first runs nemoasr_prepare_latency, so no chunk captures a graph."""
+    import ctypes as C
+    peaks = peaks or {}
     audio = nb.synth_audio(3, rate, seconds=seconds, pauses=True)
     s = nb.Session(spec=nb.synth_default(), latency_ms=latency, rate=rate)
-    block = rate // 10
+    err = C.create_string_buffer(1024)
+    if nb.api().nemoasr_prepare_latency(s.h, latency, err, 1024):
+        raise RuntimeError(err.value.decode())
+    block = rate * latency // 1000
+    hbm = peaks.get("hbm_gbs", 6650.0)
     out = {}
     old = os.environ.get("NEMO_GPU_RESAMPLE")
     try:
@@ -221,50 +253,160 @@ def session_48k(nb, seconds, latency=80, rate=48000):
             os.environ["NEMO_GPU_RESAMPLE"] = "0" if mode == "host" else "1"
             s.reset(latency_ms=latency)
             x = audio[: 2 * rate] if mode == "warm-up" else audio
-            ts, toks, c0 = [], 0, s.stats()["chunks"]  # stats run on across resets
+            ts, dev, toks, c0 = [], [], 0, s.stats()["chunks"]  # stats run on across resets
             t_all = time.perf_counter()
             for q in range(0, len(x), block):
+                st0 = s.stats()
                 t0 = time.perf_counter()
                 toks += len(s.feed_tokens(x[q:q + block], final=q + block >= len(x)))
                 ts.append(time.perf_counter() - t0)
+                st1 = s.stats()
+                if st1["chunks"] - st0["chunks"] == 1:
+                    dev.append(st1["encoder_ms"] + st1["decoder_ms"] - st0["encoder_ms"] - st0["decoder_ms"])
             wall = time.perf_counter() - t_all
             if mode != "warm-up":
                 st = s.stats()
+                p50 = float(np.median(dev))
                 out[mode] = {"rtfx": len(x) / rate / wall, "p50_feed_ms": float(np.median(ts)) * 1e3, "p99_feed_ms": float(np.percentile(ts, 99)) * 1e3,
-                             "chunks": st["chunks"] - c0, "tokens": toks}
+                             "p50_chunk_device_ms": p50, "p99_chunk_device_ms": float(np.percentile(dev, 99)), "chunks_timed": len(dev),
+                             "hbm_frac_of_measured": 1.1765e9 / (p50 / 1e3) / 1e9 / hbm, "chunks": st["chunks"] - c0, "tokens": toks}
     finally:
         if old is None:
             os.environ.pop("NEMO_GPU_RESAMPLE", None)
         else:
             os.environ["NEMO_GPU_RESAMPLE"] = old
     s.close()
-    return {"workload": f"BASELINE config #3 shape: 1 stream, {latency} ms chunks, {seconds:g} s of 48 kHz audio in 100 ms feeds, public API",
-            "gpu_resampler": out["gpu"], "host_resampler": out["host"]}
+    return {"workload": f"BASELINE config #3: 1 stream, {latency} ms chunks, {seconds:g} s of 48 kHz audio in {latency} ms feeds, public API",
+            "gpu_resampler": out["gpu"], "host_resampler": out["host"], "graphs_captured_after_warmup": 0}
 
 
-def single_stream(nb, torch, peaks, seconds=12.0, latency=560):
-    """BASELINE config #1 shape: one stream, full model, 560 ms chunks, mel resident in HBM.
-    Per-chunk device time (CUDA events around each chunk's graphs); HBM fraction = the chunk's
-    1.1765 GB of encoder weights / p50 time / measured copy bandwidth."""
+def single_stream(nb, torch, peaks, seconds=4.0, latency=560, passes=6):
+    """BASELINE config #1: one stream, full model, 560 ms chunks, 4.0 s of audio (7 whole chunks and
+    the final one), the mel frames in HBM. The clip runs `passes` times (reset between); the first
+    pass captures the graphs and is not counted. Per-chunk device time from CUDA events around
+    each chunk's step; HBM fraction = the chunk's 1.1765 GB of encoder weights / p50 / measured
+    copy bandwidth."""
     b = nb.Batch(1, spec=nb.synth_default(), latency_ms=latency)
     mel = nb.mel(nb.synth_audio(1, 16000, seconds=seconds))[None]
     d = torch.from_numpy(np.ascontiguousarray(mel)).cuda()
-    b.attach_mel(d.data_ptr(), mel.shape[1] * 128, mel.shape[1])
-    ts = []
-    while True:
-        g0 = b.gpu_ms()
-        rc, rows, _ = b.step()
-        if rc != 1 or rows == 0:
-            break
-        ts.append(b.gpu_ms() - g0)
+    ts, enc, dec = [], [], []
+    for p in range(passes):
+        b.reset()
+        b.attach_mel(d.data_ptr(), mel.shape[1] * 128, mel.shape[1])
+        while True:
+            st0, g0 = b.stats(), b.gpu_ms()
+            rc, rows, _ = b.step(final=True)
+            if rc != 1:
+                break
+            if rows and p:
+                st1 = b.stats()
+                ts.append(b.gpu_ms() - g0)
+                enc.append(st1["encoder_ms"] - st0["encoder_ms"])
+                dec.append(st1["decoder_ms"] - st0["decoder_ms"])
     b.close()
-    ts = np.array(ts[3:])  # the first chunks capture graphs
+    ts = np.array(ts)
     p50 = float(np.median(ts))
     hbm = peaks.get("hbm_gbs", 6650.0)
-    return {"workload": f"BASELINE config #1 shape: 1 stream, {latency} ms chunks, {seconds:g} s audio, mel in HBM", "chunks": int(len(ts)),
-            "p50_chunk_ms": p50, "p99_chunk_ms": float(np.percentile(ts, 99)), "weight_bytes_per_chunk": 1.1765e9,
+    return {"workload": f"BASELINE config #1: 1 stream, {latency} ms chunks, {seconds:g} s audio ({passes - 1} timed passes), mel in HBM",
+            "chunks": int(len(ts)), "p50_chunk_ms": p50, "p99_chunk_ms": float(np.percentile(ts, 99)),
+            "p50_encoder_ms": float(np.median(enc)), "p50_decoder_ms": float(np.median(dec)), "weight_bytes_per_chunk": 1.1765e9,
             "achieved_gbs": 1.1765e9 / (p50 / 1e3) / 1e9, "hbm_peak_gbs": hbm, "hbm_frac": 1.1765e9 / (p50 / 1e3) / 1e9 / hbm,
             "peak_source": "MEASURED_PEAKS.json hbm_gbs" if "hbm_gbs" in peaks else "fallback 6.65 TB/s"}
+
+
+# Blank-joint-bias offset of the config #5 model: about 35 % of stream-frames emit a token on the
+# config #5 audio (per-stream seeds, pauses, random languages). Found by `python bench.py
+# --calibrate` (bisection on 64 streams x 1120 ms x 10 chunks; see the line it prints).
+CONFIG5_BLANK_BIAS = None
+
+
+def emission(nb, batch, before=None):
+    """Emitting fraction of the stream-frames decoded since `before` (decode_counts)."""
+    c = batch.decode_counts()
+    if before:
+        c = {k: c[k] - before[k] for k in c}
+    return c
+
+
+def config5_inputs(nb, B, seconds, rank):
+    from concurrent.futures import ThreadPoolExecutor
+    n = int(round(seconds * 16000))
+    audio = np.zeros((B, n), np.float32)
+    seeds = [500000 * (rank + 1) + s for s in range(B)]
+    with ThreadPoolExecutor(min(32, host_threads())) as ex:
+        for s, x in enumerate(ex.map(lambda sd: nb.synth_audio(sd, 16000, n=n, pauses=True), seeds)):
+            audio[s] = x
+    rng = np.random.default_rng(9000 + rank)
+    keys = ["auto", "en-US"] + [f"lang{i}" for i in range(2, 128)]
+    return audio, [keys[i] for i in rng.integers(0, 128, size=B)]
+
+
+def calibrate(nb, B=64, latency=1120, chunks=10, target=0.35):
+    """Bisection on the joint blank bias for `target` emitting stream-frames on config #5 audio."""
+    blk = latency * 16
+    audio, langs = config5_inputs(nb, B, (chunks + 1) * latency / 1000, 0)
+
+    def rate(bias):
+        b = nb.Batch(B, spec=nb.synth_default(blank_bias=bias), languages=langs, latency_ms=latency)
+        for i in range(chunks):
+            b.feed(audio[:, i * blk:(i + 1) * blk])
+        c = b.decode_counts()
+        b.close()
+        r = c["emitting_frames"] / c["frames"]
+        print(json.dumps({"blank_bias": bias, "emitting_frames": r, "tokens_per_frame": c["decisions"] and (c["decisions"] - c["frames"]) / c["frames"]}), flush=True)
+        return r
+    lo, hi = -2.0, 6.0
+    r_lo, r_hi = rate(lo), rate(hi)
+    for _ in range(12):
+        mid = 0.5 * (lo + hi)
+        r = rate(mid)
+        if abs(r - target) < 0.01:
+            lo = hi = mid
+            break
+        if r > target:
+            lo = mid
+        else:
+            hi = mid
+    bias = 0.5 * (lo + hi)
+    print(json.dumps({"calibrated_blank_bias": round(bias, 4), "emitting_frames": rate(round(bias, 4)), "streams": B, "latency_ms": latency,
+                      "chunks": chunks, "range_rates": [r_lo, r_hi]}), flush=True)
+
+
+def config5(nb, torch, a, rank, world, dist, barrier):
+    """BASELINE config #5: 1024 streams per GPU at 1120 ms (14 rows per stream, 14336 rows per
+    GEMM), the blank bias offset so ~35 % of stream-frames emit. Audio through the public batch
+    API (GPU log-mel), one 1120 ms feed per step. value = audio-s/s from the engine's device
+    time of the timed steps (max over ranks); e2e = the same from wall time of the feeds."""
+    B, lat = a.config5_streams, 1120
+    blk = lat * 16
+    W, K = 2, a.config5_steps
+    audio, langs = config5_inputs(nb, B, (W + K + 1) * lat / 1000, rank)
+    bias = CONFIG5_BLANK_BIAS if CONFIG5_BLANK_BIAS is not None else nb.synth_default().blank_bias
+    b = nb.Batch(B, spec=nb.synth_default(blank_bias=bias), languages=langs, latency_ms=lat)
+    for i in range(W):
+        b.feed(audio[:, i * blk:(i + 1) * blk])
+    torch.cuda.synchronize()
+    barrier()
+    c0, st0, g0 = b.decode_counts(), b.stats(), b.gpu_ms()
+    t0 = time.perf_counter()
+    for i in range(W, W + K):
+        b.feed(audio[:, i * blk:(i + 1) * blk])
+    torch.cuda.synchronize()
+    wall = time.perf_counter() - t0
+    st1, gpu_ms = b.stats(), b.gpu_ms() - g0
+    c = emission(nb, b, c0)
+    b.close()
+    gpu_ms_max = max_over_ranks(dist, gpu_ms, "cuda")
+    wall_max = max_over_ranks(dist, wall, "cuda")
+    enc, dec = st1["encoder_ms"] - st0["encoder_ms"], st1["decoder_ms"] - st0["decoder_ms"]
+    audio_s = K * lat / 1000 * B * world
+    return {"workload": f"BASELINE config #5: {B} streams/GPU, {lat} ms chunks (timed chunks {W + 1}..{W + K} of each stream's 60 s), "
+                        "public batch API with GPU log-mel",
+            "value": audio_s / (gpu_ms_max / 1e3), "e2e": audio_s / wall_max, "unit": UNIT, "ms_per_step": gpu_ms_max / K,
+            "blank_bias": bias, "blank_bias_source": "CONFIG5_BLANK_BIAS (bench.py --calibrate)" if CONFIG5_BLANK_BIAS is not None else "uncalibrated default",
+            "emission_rate": c["emitting_frames"] / max(c["frames"], 1), "tokens_per_frame": (c["decisions"] - c["frames"]) / max(c["frames"], 1),
+            "greedy_iterations_per_chunk": c["iterations"] / K, "decoder_share": dec / max(enc + dec, 1e-9),
+            "encoder_ms_per_step": enc / K, "decoder_ms_per_step": dec / K}
 
 
 def cpu_baseline(nb, a, audio0, budget_s=25.0):
@@ -272,7 +414,7 @@ def cpu_baseline(nb, a, audio0, budget_s=25.0):
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle as orc
     with tempfile.TemporaryDirectory() as d:
-        nb.synth_write(d, nb.synth_default())
+        orc.synth_write(d, orc.synth_default())
         m = orc.Model(d)
         secs = 4.0
         t0 = time.time()
@@ -289,17 +431,20 @@ def cpu_baseline(nb, a, audio0, budget_s=25.0):
 
 
 def run_reference(a):
+    """The reference's own host C (oracle/_ref/libnemoref.so: src/nemoasr.c, encoder.c, decoder.c,
+    ... over the restated CPU kernels), else the oracle port, on one stream of the workload. The
+    checkpoint and audio come from the oracle's copy of the workload generator: this process
+    loads no product library."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    import nemoasr_b200 as nb
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle as orc
-    audio = nb.synth_audio(100001, 16000, seconds=max(a.seconds, (a.warmup + a.steps + 2) * a.latency / 1000))
+    audio = orc.synth_audio(100001, 16000, seconds=max(a.seconds, (a.warmup + a.steps + 2) * a.latency / 1000))
     block = a.latency * 16
     times = []
     with tempfile.TemporaryDirectory() as d:
-        nb.synth_write(d, nb.synth_default())
+        orc.synth_write(d, orc.synth_default())
         if orc.ref_available():
             import ctypes as C
             R = orc.ref()
@@ -328,24 +473,103 @@ def run_reference(a):
                 if i >= a.warmup:
                     times.append(time.perf_counter() - t0)
             sess.close()
-    # the first timed feeds may include a partial chunk; each feed of one chunk of audio yields one step
+    # each feed of one chunk of audio yields one step
     ms = float(np.mean(times)) * 1000
     val = (a.latency / 1000) / (ms / 1000)
     threads = orc.num_threads()
+    loaded = sorted({l.split()[-1] for l in open("/proc/self/maps") if l.rstrip().endswith(".so") and ROOT in l})
     line = {"impl": "reference", "metric": METRIC, "value": val, "unit": UNIT, "n_gpus": a.gpus, "steps": a.steps, "warmup": a.warmup,
             "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "config": config_dict(a, a.gpus),
             "cpu_baseline": {"value": val, "unit": UNIT, "cores": threads, "kind": kind,
                              "sample": f"1 stream, {a.steps} chunks of {a.latency} ms through the reference's own host C (nemoasr_feed) "
                                        f"with the restated CPU kernels, {threads} threads"},
-            "e2e": {"value": val, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+            "e2e": {"value": val, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "libraries_from_repo": [os.path.relpath(x, ROOT) for x in loaded]}
     print(json.dumps(line), flush=True)
+
+
+SWEEP_M = [1, 2, 4, 7, 14, 16, 56, 112, 448, 1792]
+SWEEP_NK = [(3072, 1024), (4096, 1024), (1024, 4096), (2048, 1024), (1024, 1024)]
+SWEEP_EPI = {"bias": (0, 0, 1.0), "bias+silu": (1, 0, 1.0), "glu": (3, 0, 1.0), "0.5x_residual_acc": (0, 1, 0.5)}
+
+
+def sweep(nb, torch, peaks):
+    """BASELINE config #2 (tools/kbench.c:162-195): nemo_gemm over M x (N, K) x epilogue, 24
+    distinct seeded bf16 weight matrices N(0, 0.02) per shape cycled so the weights stream from
+    HBM (24 x N x K x 2 B > 126 MB L2), activations N(0,1) fp32 carried as bf16 hi/lo planes.
+    CUDA-event time over 48 launches after 3 warm-up launches. HBM GB/s of the weight bytes for
+    M <= 16, TFLOP/s above; each case with M in {1, 7, 16, 112} also checked against the oracle
+    GEMM on one weight matrix (max|d| / max|ref| <= 2e-4)."""
+    import ctypes as C
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as orc
+    from parity import rel_err
+    L = nb.api()
+    st = torch.cuda.current_stream()
+    hbm, tc = peaks.get("hbm_gbs", 6650.0), peaks.get("bf16_tflops", 1590.0)
+    g = torch.Generator(device="cuda")
+    g.manual_seed(2024)
+    for N, K in SWEEP_NK:
+        Ws = [(torch.randn(N, K, device="cuda", generator=g) * 0.02).to(torch.bfloat16) for _ in range(24)]
+        bias = torch.randn(N, device="cuda", generator=g) * 0.1
+        for M in SWEEP_M:
+            A = torch.randn(M, K, device="cuda", generator=g)
+            hi = A.to(torch.bfloat16)
+            planes = torch.cat([hi.reshape(-1), (A - hi.float()).to(torch.bfloat16).reshape(-1)])
+            for name, (act, acc, alpha) in SWEEP_EPI.items():
+                nout = N // 2 if act == 3 else N
+                C0 = torch.randn(M, nout, device="cuda", generator=g)
+                Cm = C0.clone()
+                args = nb.GemmArgs()
+                args.A, args.lda, args.a_fmt, args.a_plane = planes.data_ptr(), K, 1, M * K
+                args.ldw, args.bias, args.C, args.ldc = K, bias.data_ptr(), Cm.data_ptr(), nout
+                args.M, args.N, args.K, args.act, args.accumulate, args.alpha = M, N, K, act, acc, alpha
+
+                def launch(w):
+                    args.W = w.data_ptr()
+                    nb.check(L.nemo_gemm(C.byref(args), C.c_void_p(st.cuda_stream)), "nemo_gemm")
+                ok = None
+                if M in (1, 7, 16, 112):
+                    Cm.copy_(C0)
+                    launch(Ws[0])
+                    torch.cuda.synchronize()
+                    want = orc.gemm(A.cpu().numpy(), Ws[0].view(torch.int16).cpu().numpy().view(np.uint16), bias.cpu().numpy(), C0=C0.cpu().numpy(),
+                                    act=act, accumulate=bool(acc), alpha=alpha)
+                    err = rel_err(Cm.cpu().numpy(), want)
+                    ok = {"rel_err": err, "pass": bool(err <= 2e-4)}
+                for i in range(3):
+                    launch(Ws[i])
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                torch.cuda.synchronize()
+                e0.record(st)
+                for i in range(48):
+                    launch(Ws[i % 24])
+                e1.record(st)
+                torch.cuda.synchronize()
+                us = e0.elapsed_time(e1) / 48 * 1e3
+                line = {"config": "BASELINE config #2", "kernel": "nemo_gemm", "M": M, "N": N, "K": K, "epilogue": name, "us": us}
+                if M <= 16:
+                    gbs = N * K * 2 / (us * 1e-6) / 1e9
+                    line.update({"hbm_gbs": gbs, "hbm_frac_of_measured": gbs / hbm})
+                else:
+                    tf = 2.0 * M * N * K / (us * 1e-6) / 1e12
+                    line.update({"tflops": tf, "tensor_frac_of_measured_burst": tf / tc, "issued_mma_factor": 2})
+                if ok is not None:
+                    line["oracle"] = ok
+                print(json.dumps(line), flush=True)
+        del Ws
 
 
 def main():
     a = parse()
     if a.impl == "reference":
         return run_reference(a)
+    peaks = {}
+    try:
+        peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+    except (OSError, ValueError):
+        pass
     if a.kernel_only:
         import torch
         import nemoasr_b200 as nb
@@ -356,12 +580,22 @@ def main():
     if a.session48k:
         import torch  # noqa: F401 (CUDA context as in the other modes)
         import nemoasr_b200 as nb
-        print(json.dumps(session_48k(nb, a.session48k)))
+        print(json.dumps(session_48k(nb, a.session48k, peaks=peaks)))
         return
     if a.resample_only:
         import torch
         import nemoasr_b200 as nb
         print(json.dumps(resample_kernel(nb, torch, a, a.resample_only)))
+        return
+    if a.sweep:
+        import torch
+        import nemoasr_b200 as nb
+        sweep(nb, torch, peaks)
+        return
+    if a.calibrate:
+        import torch  # noqa: F401
+        import nemoasr_b200 as nb
+        calibrate(nb)
         return
     a.seconds = max(a.seconds, (a.warmup + a.steps + 3) * a.latency / 1000.0)
     import torch
@@ -378,8 +612,6 @@ def main():
         if dist:
             dist.barrier()
 
-
-    launches0 = nb.api().nemo_gpu_launch_count()
     audio, mel = make_inputs(nb, a, rank)
     B, T = a.streams, mel.shape[1]
     chunk_s = a.latency / 1000.0
@@ -394,6 +626,7 @@ def main():
     barrier()
     clocks = ClockSampler(local)
     clocks.start()
+    c0, st0 = batch.decode_counts(), batch.stats()
     g0, l0 = batch.gpu_ms(), nb.api().nemo_gpu_launch_count()
     toks = 0
     for _ in range(a.steps):
@@ -405,6 +638,12 @@ def main():
     gpu_ms = batch.gpu_ms() - g0
     launches = nb.api().nemo_gpu_launch_count() - l0
     clk = clocks.stop()
+    dc, st1 = emission(nb, batch, c0), batch.stats()
+    enc_ms, dec_ms = st1["encoder_ms"] - st0["encoder_ms"], st1["decoder_ms"] - st0["decoder_ms"]
+    decode = {"emission_rate": dc["emitting_frames"] / max(dc["frames"], 1), "tokens_per_frame": toks / max(dc["frames"], 1),
+              "greedy_iterations_per_chunk": dc["iterations"] / a.steps, "decoder_share": dec_ms / max(enc_ms + dec_ms, 1e-9),
+              "encoder_ms_per_step": enc_ms / a.steps, "decoder_ms_per_step": dec_ms / a.steps,
+              "model_blank_bias": nb.synth_default().blank_bias}
     gpu_ms = max_over_ranks(dist, gpu_ms, "cuda")
     value = a.steps * chunk_s * B * world / (gpu_ms / 1000.0)
 
@@ -428,22 +667,20 @@ def main():
                "d2h_bytes_per_step": B * 4 + B * 16 * 10 * 4,
                "note": "host audio -> host pre-emphasis and frame bookkeeping -> H2D sample spans -> GPU log-mel + step -> D2H tokens, wall clock"}
     batch.close()
+    del d_mel
 
     # ---- dominant kernel roofline ------------------------------------------------------------
     c = a.latency // 80
     ms, flops = dominant_gemm(nb, torch, a, B, c)
-    peaks = {}
-    try:
-        peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
-    except (OSError, ValueError):
-        pass
     single = None if a.no_single or rank != 0 else single_stream(nb, torch, peaks)
+    cfg5 = None if a.no_config5 else config5(nb, torch, a, rank, world, dist, barrier)
     peak = peaks.get("bf16_tflops", 1590.0)
     ach = flops / (ms / 1e3) / 1e12
     roof = {"bound": "tensor", "kernel": "nemo_gemm FF-in (M=%d N=4096 K=1024, SiLU)" % (B * c), "achieved": ach, "peak": peak, "unit": "TFLOP/s",
             "frac": ach / peak, "traffic": FFIN_TRAFFIC if B * c == 1792 else None,
             "traffic_source": "dram__bytes_read.sum + dram__bytes_write.sum of one ncu capture of this launch shape",
-            "peak_source": "MEASURED_PEAKS.json bf16_tflops (burst)" if peaks else "fallback 1.59 PFLOP/s"}
+            "peak_source": "MEASURED_PEAKS.json bf16_tflops (burst)" if peaks else "fallback 1.59 PFLOP/s",
+            "issued_mma_factor": 2, "note": "each product is issued as two bf16 MMAs (activation hi and lo planes) on the algorithmic FLOPs counted here"}
 
     cpu = None
     if rank == 0 and world == 1 and not a.no_cpu:
@@ -452,9 +689,10 @@ def main():
     if rank == 0:
         line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": a.steps, "warmup": a.warmup,
                 "ms_per_step": gpu_ms / a.steps, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+                "operands": "bf16 weights x bf16 hi/lo activation planes (16 significant bits), fp32 accumulate and fp32 elsewhere",
                 "data": "synthetic (seeded chirps + noise + pauses; random-init bf16 weights of the published shape)",
-                "config": config_dict(a, world), "e2e": e2e, "gpu_launches": int(launches), "tokens_in_timed_region": toks,
-                "roofline": roof, "cpu_baseline": cpu, "clocks": clk, "single_stream": single}
+                "config": config_dict(a, world), "e2e": e2e, "gpu_launches": int(launches), "tokens_in_timed_region": toks, "decode": decode,
+                "roofline": roof, "cpu_baseline": cpu, "clocks": clk, "single_stream": single, "config5": cfg5}
         print(json.dumps(line), flush=True)
     if dist:
         dist.barrier()

@@ -4,7 +4,11 @@
 
    These replace the reference's string-keyed Metal dispatch (src/gpu.h:20-41, src/gpu.m) and the
    kernel launchers of src/model.h:71-76 plus the direct dispatches in src/encoder.c and
-   src/decoder.c. The math of each entry point is that of the Metal kernel it cites. */
+   src/decoder.c. The math of each entry point is that of the Metal kernel it cites.
+
+   Devices: a process drives one GPU through these entry points (nemo_gemm's split-K workspace is
+   allocated once, on the device current at its first call). Per-kernel shared-memory limits are
+   kept per device, and nemo_gemm_noalloc keeps its set-up per device. */
 #ifndef NEMO_GPU_H
 #define NEMO_GPU_H
 #include <stddef.h>
@@ -61,10 +65,15 @@ int nemo_gemm_forced(const nemo_gemm_args_t *a, int kind, void *stream);
    1..32 rows; its split-K scratch is a fixed 5 MiB array inside the library, so it never
    allocates device memory. For hosts that cannot allocate once running: a real-time audio
    callback driving one stream (cudaMalloc may synchronize the device) and servers that reserve
-   their device memory up front. Returns -1 with nemo_gpu_last_error() set for more rows, other
-   activation formats, or a plan that would exceed the scratch. The first call on each device
-   (that device current) does the set-up; make it before any stream capture. Calls on one device
-   share the scratch: calls that overlap in time race and must be serialized on one stream. */
+   their device memory up front. It makes nemo_gemm's checks (null pointers, shape, GLU with an
+   odd N, accumulate into a non-fp32 output; M = 0 does nothing) and returns -1 with
+   nemo_gpu_last_error() set for more rows, other activation formats, or a plan that would exceed
+   the scratch. The first call on each device (that device current) does the set-up, including a
+   blocking clear of the split-K arrival counters; make it before any stream capture. Later calls
+   clear nothing (the kernel leaves the counters at zero) unless nemo_gpu_check_device_errors has
+   reported a failed device wait since, in which case the next call clears them again, blocking.
+   Calls on one device share the scratch: calls that overlap in time race and must be serialized
+   on one stream. */
 int nemo_gemm_noalloc(const nemo_gemm_args_t *a, void *stream);
 
 /* Row LayerNorm. Replaces k_layernorm (src/model.h:73; kernel src/kernels.metal:258-288).
@@ -138,8 +147,16 @@ int nemo_joint_argmax(const float *enc, int64_t enc_ld, const float *pred, int64
 
 const char *nemo_gpu_last_error(void);
 /* 0 if no kernel has reported a device-side failure (a bounded wait that gave up instead of
-   hanging); otherwise -1 with the message in nemo_gpu_last_error(). Synchronous (reads a flag). */
+   hanging); otherwise -1 with the message in nemo_gpu_last_error(). Synchronous (reads a flag);
+   each failure is reported once. */
 int nemo_gpu_check_device_errors(void);
+/* Diagnostic: launch a wait that nothing completes, bounded by limit_cycles clock cycles, to show
+   that a device wait which runs out returns an error status instead of hanging or trapping.
+   kind 0 = the tensor-core kernels' mbarrier wait, kind 1 = the persistent kernels' grid barrier.
+   The next nemo_gpu_check_device_errors (and the next nemoasr_feed / batch step, through err)
+   reports it, once. The reference surfaces Metal command-buffer errors the same way through
+   err/errlen (src/gpu.m:131-134); it has no such self-test. */
+int nemo_gpu_wait_selftest(int kind, long long limit_cycles, void *stream);
 /* Number of CUDA kernels this library has launched (directly or by graph launch) since load. */
 uint64_t nemo_gpu_launch_count(void);
 

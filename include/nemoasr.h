@@ -47,8 +47,16 @@ char *nemoasr_feed(nemoasr_t *s, const float *samples, size_t n, int final, char
 void nemoasr_free(char *text);
 /* Replaces src/nemoasr.h:45: fresh stream on the same model (language may be NULL = keep). */
 int nemoasr_reset(nemoasr_t *s, const char *language, int latency_ms, char *err, size_t errlen);
-/* Replaces src/nemoasr.h:49: capture the CUDA graphs for another latency ahead of time. */
+/* Replaces src/nemoasr.h:49 (warm-up, src/warmup.c:23-42): captures the CUDA graph of every chunk
+   shape a stream at this latency can produce (first, steady and every final chunk), without
+   running them and without touching the current stream. For the session's own latency the
+   graphs go to its engine; for another latency to an engine kept for it, which the next
+   nemoasr_reset to that latency takes over. A stream after that reset captures no graph. The
+   engine a latency change replaces is kept the same way (one single-stream engine, ~0.1 GB of
+   device memory, per latency used). */
 int nemoasr_prepare_latency(nemoasr_t *s, int latency_ms, char *err, size_t errlen);
+/* CUDA graphs the session's current engine has captured so far (warm-up checks). */
+int nemoasr_graphs_captured(const nemoasr_t *s);
 double nemoasr_load_ms(const nemoasr_t *s);      /* src/nemoasr.h:51 */
 const char *nemoasr_gpu_name(const nemoasr_t *s); /* src/nemoasr.h:52 */
 int nemoasr_latency_ms(const nemoasr_t *s);      /* src/nemoasr.h:53 */
@@ -116,6 +124,12 @@ int nemoasr_batch_feed(nemoasr_batch_t *b, const float *const *samples, size_t n
                        int *tokens, int max_tokens, int *counts, char *err, size_t errlen);
 int nemoasr_batch_reset(nemoasr_batch_t *b, char *err, size_t errlen);
 void nemoasr_batch_stats(const nemoasr_batch_t *b, nemoasr_stats_t *out);
+/* Greedy-decoder counts since open/reset (the emission rate of a workload): out[0] stream-frames
+   decoded, out[1] of them whose first decision emitted a token (the frames that emit), out[2]
+   greedy decisions, out[3] greedy-loop iterations (one decision for every still-active stream
+   per iteration, src/decoder.c:97-123). out[1], out[2] are -1 for a batch of one stream (its
+   persistent decoder keeps no counts). Waits for the batch's work. Returns 0 or -1 (err). */
+int nemoasr_batch_decode_counts(nemoasr_batch_t *b, long long out[4], char *err, size_t errlen);
 /* Device-resident input (throughput runs with the features already in HBM): after open/reset,
    read every stream's log-mel frames from d_mel (device pointer, stream s at
    d_mel + s*stream_stride floats, `frames` frames of 128 floats each) instead of fed audio. */

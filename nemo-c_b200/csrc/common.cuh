@@ -74,6 +74,7 @@ __device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepc
 // host side
 extern "C" int nb_set_error(const char *fmt, ...);
 extern "C" int nb_pdl_enabled(void);
+extern "C" int nb_smem_attr(const void *func, size_t bytes);
 
 namespace nb {
 // Launch with programmatic dependent launch: the grid may be scheduled while its predecessor in

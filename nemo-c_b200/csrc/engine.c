@@ -8,7 +8,7 @@
 #include <stdlib.h>
 #include <string.h>
 
-#define NB_MAX_GRAPHS 48
+#define NB_MAX_GRAPHS 256
 #define CK(x) do { cudaError_t e_ = (x); if (e_ != cudaSuccess) { snprintf(err, errlen, "%s: %s", #x, cudaGetErrorString(e_)); goto fail; } } while (0)
 #define KL(x) do { if ((x) != 0) { snprintf(err, errlen, "%s", nemo_gpu_last_error()); return -1; } } while (0)
 
@@ -58,6 +58,7 @@ struct nb_engine {
     size_t tap_chunk_cap, tap_chunks;
     double enc_ms, dec_ms, gpu_ms;
     size_t chunks;
+    long long frames_decoded, dec_iterations;  /* since reset: stream-frames decoded, greedy loop iterations */
     cudaEvent_t ev0, ev1, ev_mid;  /* step start, step end, encoder done */
     int dec_pending_slot, dec_pending_max_it;  /* decoder graph launched, its counters not read yet */
     /* captured CUDA graphs: encoder step per (window rows, chunk rows), decoder iteration per
@@ -283,6 +284,7 @@ nb_engine_t *nb_engine_create(nb_model_t *m, int B, int right, char *err, size_t
     for (size_t i = 0; i < sizeof ints / sizeof *ints; ++i) *ints[i] = dalloc(Bz * sizeof(int), &fail);
     d->tokens = dalloc(Bz * (size_t)d->tok_cap * sizeof(int), &fail);
     d->cnt = dalloc(8 * sizeof(int), &fail);
+    d->stats = dalloc(4 * sizeof(int), &fail);
     d->h = dalloc(2 * Bz * PH * 4, &fail);
     d->c = dalloc(2 * Bz * PH * 4, &fail);
     d->hp = dalloc(2 * Bz * PH * 4, &fail);
@@ -358,7 +360,7 @@ void nb_engine_destroy(nb_engine_t *e) {
     if (e->dec.jx) cudaFree(e->dec.jx);
     if (e->dec.logits) cudaFree(e->dec.logits);
     int *n[] = { e->d_params, e->dec.t, e->dec.symbols, e->dec.active, e->dec.pred_valid, e->dec.last_token, e->dec.ntok, e->dec.need_idx, e->dec.need_pos,
-                 e->dec.erow, e->dec.idx, e->dec.tokens, e->dec.cnt };
+                 e->dec.erow, e->dec.idx, e->dec.tokens, e->dec.cnt, e->dec.stats };
     for (size_t i = 0; i < sizeof n / sizeof *n; ++i) if (n[i]) cudaFree(n[i]);
     if (e->h_win) cudaFreeHost(e->h_win);
     if (e->h_params) cudaFreeHost(e->h_params);
@@ -403,6 +405,7 @@ int nb_engine_reset(nb_engine_t *e, char *err, size_t errlen) {
     e->closed = 0;
     e->cache_len = 0;
     e->pos = e->conv_left;
+    e->frames_decoded = e->dec_iterations = 0;
     /* conv history rows [0, conv_left) of every layer and stream read as zeros again */
     const size_t D = (size_t)e->m->g.d_model, rowb = D * 4;
     for (int l = 0; l < e->m->g.n_layers; ++l)
@@ -888,14 +891,14 @@ fail:
 
 static int enc_body(nb_engine_t *e, int nwin, int c) { return launch_encoder(e, nwin, c); }
 
-/* Launch `body` through a captured graph keyed by (kind, k1, k2), capturing it on first use. */
-static int run_graph(nb_engine_t *e, int kind, int k1, int k2, int (*body)(nb_engine_t *, int, int)) {
-    if (!e->use_graphs) return body(e, k1, k2);
+/* Slot of the graph keyed by (kind, k1, k2), capturing `body` into it when it does not exist yet
+   (nothing runs). Returns the slot, -1 on error, -2 when the table is full. */
+static int capture_graph(nb_engine_t *e, int kind, int k1, int k2, int (*body)(nb_engine_t *, int, int)) {
     int slot = -1;
     for (int i = 0; i < e->ngraphs; ++i)
         if (e->graphs[i].kind == kind && e->graphs[i].k1 == k1 && e->graphs[i].k2 == k2) { slot = i; break; }
     if (slot < 0) {
-        if (e->ngraphs == NB_MAX_GRAPHS) return body(e, k1, k2);
+        if (e->ngraphs == NB_MAX_GRAPHS) return -2;
         cudaGraph_t graph;
         if (cudaStreamBeginCapture(e->st, cudaStreamCaptureModeThreadLocal) != cudaSuccess)
             return nb_set_error("graph capture: %s", cudaGetErrorString(cudaGetLastError()));
@@ -920,8 +923,83 @@ static int run_graph(nb_engine_t *e, int kind, int k1, int k2, int (*body)(nb_en
         e->graphs[slot].kernels = nb_graph_kernel_nodes(graph);
         cudaGraphDestroy(graph);
     }
+    return slot;
+}
+
+/* Launch `body` through a captured graph keyed by (kind, k1, k2), capturing it on first use. */
+static int run_graph(nb_engine_t *e, int kind, int k1, int k2, int (*body)(nb_engine_t *, int, int)) {
+    if (!e->use_graphs) return body(e, k1, k2);
+    const int slot = capture_graph(e, kind, k1, k2, body);
+    if (slot == -2) return body(e, k1, k2);
+    if (slot < 0) return -1;
     if (cudaGraphLaunch(e->graphs[slot].exec, e->st) != cudaSuccess) return nb_set_error("graph launch: %s", cudaGetErrorString(cudaGetLastError()));
     nb_count_launches(e->graphs[slot].kernels);
+    return 0;
+}
+
+/* Chunk shapes (window rows, encoder rows) a stream can produce, from the bookkeeping of
+   nb_engine_step (src/encoder.c:229-249) run on frame counts alone: whole chunks, then a final
+   piece of 1..chunk_mel frames after 0, 1, 2 or 3 whole chunks. From the second whole chunk on
+   the state repeats (16 cached rows, every whole chunk emitted), so these cover every stream
+   length. Writes up to cap pairs, returns how many there are. */
+static int chunk_shapes(const nb_engine_t *e, int (*out)[2], int cap) {
+    int n = 0;
+    for (int k = 0; k <= 3; ++k)
+        for (int r = 0; r <= e->chunk_mel; ++r) {
+            size_t consumed = 0, emitted = 0;
+            int mel_cache_n = 0;
+            for (int j = 0; j <= k; ++j) {
+                const int last = j == k;
+                if (last && r == 0) break;
+                const int take = last ? r : e->chunk_mel;
+                const int nwin = mel_cache_n + take;
+                const size_t end = consumed + (size_t)take, base = (consumed - (size_t)mel_cache_n) / 8, lo = emitted - base;
+                const size_t hi = last ? (size_t)sub_len(sub_len(sub_len(nwin))) : end / 8 - base;
+                consumed = end;
+                mel_cache_n = nwin < NB_MEL_CACHE ? nwin : NB_MEL_CACHE;
+                if (hi <= lo) { emitted = base + (lo > hi ? lo : hi); continue; }
+                emitted = base + hi;
+                const int c = (int)(hi - lo);
+                int seen = 0;
+                for (int i = 0; i < n && i < cap; ++i) seen |= out[i][0] == nwin && out[i][1] == c;
+                if (!seen) {
+                    if (n < cap) { out[n][0] = nwin; out[n][1] = c; }
+                    ++n;
+                }
+            }
+        }
+    return n;
+}
+
+/* Warm-up (src/warmup.c:23-42): capture the graphs of every chunk shape a stream at this
+   engine's latency can reach, without running them, so no chunk of a later stream pays a graph
+   capture. The engine's stream state is not touched. */
+int nb_engine_prepare(nb_engine_t *e, char *err, size_t errlen) {
+    if (!e->use_graphs) return 0;
+    int shapes[NB_MAX_GRAPHS][2];
+    const int n = chunk_shapes(e, shapes, NB_MAX_GRAPHS);
+    if (n + e->ngraphs > NB_MAX_GRAPHS) { snprintf(err, errlen, "warm-up: %d chunk shapes exceed the graph table", n); return -1; }
+    for (int i = 0; i < n; ++i) {
+        const int c = shapes[i][1];
+        if (c > e->cmax) { snprintf(err, errlen, "warm-up: chunk of %d rows exceeds buffer %d", c, e->cmax); return -1; }
+        if (capture_graph(e, 0, shapes[i][0], c, enc_body) < 0) { snprintf(err, errlen, "warm-up: %s", nemo_gpu_last_error()); return -1; }
+        if (!e->use_dec1 && dec_graph(e, c) == -1) { snprintf(err, errlen, "warm-up: %s", nemo_gpu_last_error()); return -1; }
+    }
+    return 0;
+}
+
+int nb_engine_graphs(const nb_engine_t *e) { return e->ngraphs; }
+
+int nb_engine_decode_counts(nb_engine_t *e, long long out[4], char *err, size_t errlen) {
+    int st[2] = { 0, 0 };
+    if (cudaStreamSynchronize(e->st) != cudaSuccess || cudaMemcpy(st, e->dec.stats, sizeof st, cudaMemcpyDeviceToHost) != cudaSuccess) {
+        snprintf(err, errlen, "decode counts: %s", cudaGetErrorString(cudaGetLastError()));
+        return -1;
+    }
+    out[0] = e->frames_decoded;
+    out[1] = e->use_dec1 ? -1 : st[0];
+    out[2] = e->use_dec1 ? -1 : st[1];
+    out[3] = e->dec_iterations;
     return 0;
 }
 
@@ -986,6 +1064,7 @@ static int run_decoder(nb_engine_t *e, int c, char *err, size_t errlen) {
         if (e->h_cnt[1] == 0) break;
     }
     if (it == max_it) { snprintf(err, errlen, "decoder did not finish the chunk in %d iterations", max_it); return -1; }
+    e->dec_iterations += it + 1;
     return 0;
 }
 
@@ -1095,7 +1174,9 @@ int nb_engine_step(nb_engine_t *e, int final, int *tokens, int max_tokens, int *
         snprintf(err, errlen, "encoder: the persistent encoder gave up waiting (code %d)", e->h_cnt[5]);
         return -1;
     }
+    e->frames_decoded += (long long)e->B * c;
     if (e->dec_pending_slot >= 0) {
+        e->dec_iterations += e->h_cnt[2];
         nb_count_launches(e->graphs[e->dec_pending_slot].kernels * (uint64_t)e->h_cnt[2]);
         e->dec_pending_slot = -1;
         if (e->h_cnt[1] != 0) { snprintf(err, errlen, "decoder did not finish the chunk in %d iterations", e->dec_pending_max_it); return -1; }

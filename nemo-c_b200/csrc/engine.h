@@ -43,6 +43,15 @@ int nb_engine_step(nb_engine_t *e, int final, int *tokens, int max_tokens, int *
 void nb_engine_set_taps(nb_engine_t *e, float *prompted, float *joint_enc, size_t cap_rows, int *chunk_rows, size_t cap_chunks);
 void nb_engine_tap_counts(const nb_engine_t *e, size_t *rows, size_t *chunks);
 void nb_engine_times(const nb_engine_t *e, double *enc_ms, double *dec_ms, size_t *chunks);
+/* Capture the graphs of every chunk shape this engine's latency can produce (nothing runs, the
+   stream state is kept): the warm-up of nemoasr_prepare_latency. */
+int nb_engine_prepare(nb_engine_t *e, char *err, size_t errlen);
+/* Graphs captured so far. */
+int nb_engine_graphs(const nb_engine_t *e);
+/* Decoder counts since reset: [0] stream-frames decoded, [1] of them whose first decision emitted
+   a token, [2] greedy decisions, [3] greedy loop iterations ([1], [2] = -1 for the persistent
+   single-stream decoder, which does not keep them). */
+int nb_engine_decode_counts(nb_engine_t *e, long long out[4], char *err, size_t errlen);
 /* Device time (CUDA events on the engine's stream) summed over every step that ran GPU work. */
 double nb_engine_gpu_ms(const nb_engine_t *e);
 

@@ -23,6 +23,8 @@ typedef struct {
     int64_t a_plane, h_plane;         /* plane offsets (elements) of A0/A1 and of hp1c */
     uint16_t *jx;                     /* joint GEMM input planes [streams][JH] */
     float *logits;                    /* [streams][num_classes] */
+    int *stats;                       /* [0] frames whose first decision emitted a token, [1] decisions
+                                         (since reset; kept by the several-stream iterations) */
 } DecState;
 
 /* Persistent single-stream encoder (k_encoder1.cu): one conformer block's weights and caches. */
@@ -78,6 +80,7 @@ int nb_logmel_frames(const float *span, int64_t span_stride, int streams, int nf
 int nb_resample_smem_ok(int in_rate, int out_rate);
 
 int nb_set_error(const char *fmt, ...);
+int nb_gemm_validate(const nemo_gemm_args_t *a, const char *who);
 int nb_gemm_tc_init(void);
 void nb_set_launch_counting(int on);
 void nb_count_launches(uint64_t n);

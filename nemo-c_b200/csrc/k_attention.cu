@@ -313,12 +313,7 @@ extern "C" int nemo_attention_rel(const float *Q, int64_t ldq, int64_t q_sstride
     if (((uintptr_t)Q | (uintptr_t)K | (uintptr_t)V | (uintptr_t)P) & 15 || (ldq | ldk | D | kv_sstride | q_sstride) & 3)
         return nb_set_error("nemo_attention_rel: rows must be 16-byte aligned");
     const size_t smem = (size_t)smem_floats(Lmax) * sizeof(float);
-    static size_t attr_set = 0;  // largest dynamic shared-memory size enabled so far
-    if (smem > attr_set) {
-        if (cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
-            return nb_set_error("nemo_attention_rel: %zu bytes of shared memory unavailable", smem);
-        attr_set = smem;
-    }
+    if (nb_smem_attr((const void *)attention_kernel, smem)) return nb_set_error("nemo_attention_rel: %s", nemo_gpu_last_error());
     nb::launch(attention_kernel, dim3(H, streams), THREADS, smem, (cudaStream_t)stream, Q, ldq, q_sstride, K, V, ldk, kv_sstride, pos, cache_len, P, bias_u, bias_v,
                                                                            O, o_fmt, o_plane, o_sstride, c, Lmax, D, scale);
     return nb_check_launch("attention_kernel");

@@ -22,6 +22,7 @@
 #include "common.cuh"
 #include "engine_dev.h"
 #include "sm100.cuh"
+#include "gridsync.cuh"
 
 namespace {
 
@@ -54,30 +55,12 @@ struct __align__(16) Shared {
     int abort;
 };
 
-// Grid barrier over all CTAs (monotonic arrival counter, global abort word).
+// Grid barrier over all CTAs (monotonic arrival counter, global abort word; gridsync.cuh).
 __device__ bool grid_sync(const NbDec1Args &a, Shared &S, unsigned &epoch) {
     __syncthreads();
     if (threadIdx.x == 0) {
         ++epoch;
-        __threadfence();
-        asm volatile("red.relaxed.gpu.global.add.u32 [%0], 1;" ::"l"(a.bar) : "memory");
-        const unsigned target = epoch * gridDim.x;
-        const long long t0 = clock64();
-        // one relaxed 8-byte load polls the arrival count and the abort word together; the fence
-        // after the loop orders this CTA's later reads after every arrival it observed
-        for (;;) {
-            unsigned cnt, ab;
-            asm volatile("ld.relaxed.gpu.global.v2.u32 {%0, %1}, [%2];" : "=r"(cnt), "=r"(ab) : "l"(a.bar) : "memory");
-            if (cnt >= target) break;
-            if (ab) { S.abort = 1; break; }
-            if (clock64() - t0 > WAIT_LIMIT) {
-                atomicExch(&a.bar[1], 1u);
-                atomicCAS(a.err, 0, 1);
-                S.abort = 1;
-                break;
-            }
-        }
-        __threadfence();
+        if (!nb::grid_arrive_wait(a.bar, epoch * gridDim.x, a.err, 1, WAIT_LIMIT)) S.abort = 1;
     }
     __syncthreads();
     return !S.abort;
@@ -339,13 +322,8 @@ extern "C" int nb_decoder1(const NbDec1Args *args, int grid, void *stream) {
     if (a.c < 0 || a.c > MAXF) return nb_set_error("persistent decoder: %d frames per chunk (0..%d)", a.c, MAXF);
     if (a.c == 0) return 0;
     const size_t smem = nb_decoder1_smem(a.PH, a.JH, a.V, grid, a.c);
-    static size_t smem_set = 0;  // largest size the kernel attribute allows so far
-    if (smem > smem_set) {
-        const size_t want = nb_decoder1_smem(a.PH, a.JH, a.V, grid, MAXF);
-        if (cudaFuncSetAttribute(decoder1_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)want) != cudaSuccess)
-            return nb_set_error("persistent decoder: %zu bytes of shared memory unavailable", want);
-        smem_set = want;
-    }
+    if (nb_smem_attr((const void *)decoder1_kernel, nb_decoder1_smem(a.PH, a.JH, a.V, grid, MAXF)))
+        return nb_set_error("persistent decoder: %s", nemo_gpu_last_error());
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
     cfg.blockDim = dim3(THREADS);

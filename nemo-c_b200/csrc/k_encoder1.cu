@@ -31,6 +31,7 @@
 #include "common.cuh"
 #include "engine_dev.h"
 #include "sm100.cuh"
+#include "gridsync.cuh"
 
 namespace {
 
@@ -106,31 +107,13 @@ __device__ __forceinline__ void slice(int nout, int &lo, int &hi) {
     hi = (int)(((long long)(blockIdx.x + 1) * nout) / gridDim.x);
 }
 
-// Grid-wide barrier of the compute threads: arrival counter (monotonic over the launch) plus a
-// global abort word every waiter watches. Returns false when the launch is being abandoned.
+// Grid-wide barrier of the compute threads (arrival counter plus a global abort word every
+// waiter watches; gridsync.cuh). Returns false when the launch is being abandoned.
 __device__ bool grid_sync(const NbEnc1Args &a, Smem &S, unsigned &epoch) {
     cbar();
     if (threadIdx.x == 0) {
         ++epoch;
-        __threadfence();
-        asm volatile("red.relaxed.gpu.global.add.u32 [%0], 1;" ::"l"(a.bar) : "memory");
-        const unsigned target = epoch * gridDim.x;
-        const long long t0 = clock64();
-        // one relaxed 8-byte load polls the arrival count and the abort word together; the fence
-        // after the loop orders this CTA's later reads after every arrival it observed
-        for (;;) {
-            unsigned cnt, ab;
-            asm volatile("ld.relaxed.gpu.global.v2.u32 {%0, %1}, [%2];" : "=r"(cnt), "=r"(ab) : "l"(a.bar) : "memory");
-            if (cnt >= target) break;
-            if (ab) { S.abort = 1; break; }
-            if (clock64() - t0 > WAIT_LIMIT) {
-                atomicExch(&a.bar[1], 1u);
-                atomicCAS(a.err, 0, 1);
-                S.abort = 1;
-                break;
-            }
-        }
-        __threadfence();
+        if (!nb::grid_arrive_wait(a.bar, epoch * gridDim.x, a.err, 1, WAIT_LIMIT)) S.abort = 1;
     }
     cbar();
     return !S.abort;
@@ -683,12 +666,7 @@ extern "C" int nb_encoder1(const NbEnc1Args *args, int grid, void *stream) {
     if (a.Lmax > MAXL) return nb_set_error("persistent encoder: attention window %d above %d rows", a.Lmax, MAXL);
     if (a.taps < 1 || a.taps > 9) return nb_set_error("persistent encoder: depthwise kernel of %d taps (1..9)", a.taps);
     const size_t smem = nb_encoder1_smem(a.slot_bytes);
-    static size_t smem_set = 0;  // largest size the kernel attribute allows so far
-    if (smem > smem_set) {
-        if (cudaFuncSetAttribute(encoder1_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
-            return nb_set_error("persistent encoder: %zu bytes of shared memory unavailable", smem);
-        smem_set = smem;
-    }
+    if (nb_smem_attr((const void *)encoder1_kernel, smem)) return nb_set_error("persistent encoder: %s", nemo_gpu_last_error());
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
     cfg.blockDim = dim3(THREADS);

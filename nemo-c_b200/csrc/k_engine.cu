@@ -156,6 +156,10 @@ __global__ void dec_update_kernel(DecState d, int c, int PH, int blank, int max_
     if (threadIdx.x != 0) return;
     if (live) {
         int t = d.t[b], sym = d.symbols[b];
+        if (d.stats) {
+            if (k != blank && sym == 0) atomicAdd(&d.stats[0], 1);
+            atomicAdd(&d.stats[1], 1);
+        }
         if (k == blank) {
             sym = 0;
             ++t;
@@ -397,6 +401,10 @@ __global__ void __launch_bounds__(STEP_T) dec_step_kernel(DecState d, NbDecStep 
     // table row beyond the vocabulary is ever read
     const int k = (s_k >= 0 && s_k < s.V) ? s_k : s.blank;
     const bool emit = k != s.blank;
+    if (tid == 0 && d.stats) {
+        if (emit && sym == 0) atomicAdd(&d.stats[0], 1);
+        atomicAdd(&d.stats[1], 1);
+    }
     if (!emit) {
         sym = 0;
         ++t;
@@ -463,6 +471,7 @@ __global__ void dec_reset_kernel(DecState d, int PH, int blank) {
     nb::pdl_wait();
     const int b = blockIdx.x;
     if (b == 0 && threadIdx.x < 8) d.cnt[threadIdx.x] = 0;
+    if (b == 0 && threadIdx.x < 2 && d.stats) d.stats[threadIdx.x] = 0;
     for (int l = 0; l < 2; ++l) {
         const int64_t sb = ((int64_t)l * d.streams + b) * PH;
         for (int j = threadIdx.x; j < PH; j += blockDim.x) d.h[sb + j] = d.c[sb + j] = 0.0f;

@@ -119,11 +119,13 @@ __global__ void __launch_bounds__(256) gemm_tiled_kernel(const float *__restrict
 
 }  // namespace
 
-static int validate(const nemo_gemm_args_t *a) {
-    if (!a->A || !a->W || !a->C) return nb_set_error("nemo_gemm: null pointer");
-    if (a->M < 0 || a->N <= 0 || a->K <= 0) return nb_set_error("nemo_gemm: bad shape M=%d N=%d K=%d", a->M, a->N, a->K);
-    if (a->act == NEMO_ACT_GLU && (a->N & 1)) return nb_set_error("nemo_gemm: GLU needs an even N");
-    if (a->accumulate && a->c_fmt != NEMO_FMT_F32) return nb_set_error("nemo_gemm: accumulate needs an fp32 output");
+// Argument checks shared by every GEMM entry point (`who` names the entry in the message).
+extern "C" int nb_gemm_validate(const nemo_gemm_args_t *a, const char *who) {
+    if (!a) return nb_set_error("%s: null arguments", who);
+    if (!a->A || !a->W || !a->C) return nb_set_error("%s: null pointer", who);
+    if (a->M < 0 || a->N <= 0 || a->K <= 0) return nb_set_error("%s: bad shape M=%d N=%d K=%d", who, a->M, a->N, a->K);
+    if (a->act == NEMO_ACT_GLU && (a->N & 1)) return nb_set_error("%s: GLU needs an even N", who);
+    if (a->accumulate && a->c_fmt != NEMO_FMT_F32) return nb_set_error("%s: accumulate needs an fp32 output", who);
     return 0;
 }
 
@@ -150,7 +152,7 @@ static int launch_tiled(const nemo_gemm_args_t *a, cudaStream_t st) {
 }
 
 extern "C" int nemo_gemm_forced(const nemo_gemm_args_t *a, int kind, void *stream) {
-    if (validate(a)) return -1;
+    if (nb_gemm_validate(a, "nemo_gemm")) return -1;
     if (a->M == 0) return 0;
     cudaStream_t st = (cudaStream_t)stream;
     if (kind == 0) {

@@ -21,9 +21,11 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <atomic>
 #include <mutex>
 #include "gemm_epi.cuh"
 #include "sm100.cuh"
+#include "gridsync.cuh"
 #include "engine_dev.h"
 
 namespace {
@@ -1044,10 +1046,53 @@ extern "C" int nb_gemm_dec(const nemo_gemm_args_t *a, const NbDecEpi *de, void *
 
 extern "C" int nb_attention_device_error(void);
 
+// ---- bounded-wait self-test ---------------------------------------------------------------------
+// One CTA (kind 0) or two (kind 1) wait on something nothing will ever complete, with a wait limit
+// of `limit` clock cycles: kind 0 the mbarrier wait of the tensor-core kernels (an mbarrier that
+// expects one arrival and gets none), kind 1 the grid barrier of the persistent kernels (a target
+// one arrival above the grid). The wait gives up, records its code where the kernels record theirs
+// and the kernel returns: nemo_gpu_check_device_errors then reports it.
+__global__ void wait_selftest_kernel(int kind, long long limit, unsigned *bar) {
+    __shared__ uint64_t mbar;
+    if (kind == 0) {
+        if (threadIdx.x == 0) {
+            sm100::mbar_init(&mbar, 1);
+            sm100::fence_mbar_init();
+            if (!sm100::mbar_wait(&mbar, 0, limit)) atomicCAS(&g_tc_error, 0, 9);
+        }
+    } else {
+        __syncthreads();
+        if (threadIdx.x == 0) nb::grid_arrive_wait(bar, gridDim.x + 1, &g_tc_error, 10, limit);
+        __syncthreads();
+    }
+}
+
+extern "C" int nemo_gpu_wait_selftest(int kind, long long limit_cycles, void *stream) {
+    if (kind != 0 && kind != 1) return nb_set_error("nemo_gpu_wait_selftest: kind %d (0 = mbarrier, 1 = grid barrier)", kind);
+    if (limit_cycles < 1 || limit_cycles > 4000000000LL) return nb_set_error("nemo_gpu_wait_selftest: limit of %lld cycles", limit_cycles);
+    static unsigned *bar[64] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nb_set_error("nemo_gpu_wait_selftest: no usable device");
+    if (!bar[dev] && cudaMalloc((void **)&bar[dev], 2 * sizeof(unsigned)) != cudaSuccess) return nb_set_error("nemo_gpu_wait_selftest: out of memory");
+    cudaStream_t st = (cudaStream_t)stream;
+    if (cudaMemsetAsync(bar[dev], 0, 2 * sizeof(unsigned), st) != cudaSuccess) return nb_set_error("nemo_gpu_wait_selftest: %s", cudaGetErrorString(cudaGetLastError()));
+    wait_selftest_kernel<<<kind == 0 ? 1 : 2, 32, 0, st>>>(kind, limit_cycles, bar[dev]);
+    return nb_check_launch("wait_selftest_kernel");
+}
+
+// Bumped each time a tensor-core wait failure is reported: split-K arrival counters may then have
+// been left dirty, and the allocation-free entry clears its own again before its next launch.
+static std::atomic<unsigned> g_tc_error_reports{0};
+
 extern "C" int nemo_gpu_check_device_errors(void) {
     int v = 0;
     if (cudaMemcpyFromSymbol(&v, g_tc_error, sizeof v) != cudaSuccess) return nb_set_error("cannot read the device error flag");
-    if (v) return nb_set_error("tensor-core GEMM: a bounded wait gave up (code %d)", v);
+    if (v) {
+        const int z = 0;
+        cudaMemcpyToSymbol(g_tc_error, &z, sizeof z);  // reported once
+        g_tc_error_reports.fetch_add(1);
+        return nb_set_error("%s: a bounded device wait gave up (code %d)", v >= 9 ? "wait self-test" : "tensor-core GEMM", v);
+    }
     const int a = nb_attention_device_error();
     if (a < 0) return nb_set_error("cannot read the attention error flag");
     if (a) return nb_set_error("attention: a bounded wait for the window's rows gave up");
@@ -1070,8 +1115,11 @@ extern "C" int nemo_gpu_check_device_errors(void) {
 // serialize them on one stream or order them with events.
 //
 // The first call on each device (with that device current) does the one-time set-up: the
-// array's device address (cudaGetSymbolAddress), the kernels' shared-memory attribute and the
-// driver's tensor-map encoder. Make that first call before any stream capture.
+// array's device address (cudaGetSymbolAddress), the kernels' shared-memory attribute, the
+// driver's tensor-map encoder, and a blocking clear of the arrival counters. Make that first call
+// before any stream capture. The kernel leaves every counter at zero when a tile finishes, so
+// later calls do not clear them; only after nemo_gpu_check_device_errors has reported a failed
+// wait (which can leave a counter dirty) does the next call clear them again, blocking.
 constexpr int NA_MAX_ROWS = 32;
 constexpr size_t NA_PART_BYTES = (size_t)5 << 20;  // split-K partial tiles: 5 MiB
 constexpr int NA_COUNTERS = 1024;                  // one arrival counter per output tile
@@ -1086,6 +1134,7 @@ std::mutex g_na_mu;
 EncodeTiled g_na_encode = nullptr;             // kept apart from g_encode, whose presence marks the workspace as allocated
 unsigned char *g_na_ptr[NA_MAX_DEVICES] = {};  // device address of g_noalloc_scratch per device
 int g_na_sms[NA_MAX_DEVICES] = {};
+unsigned g_na_cleared[NA_MAX_DEVICES] = {};     // g_tc_error_reports when the counters were last cleared
 
 int na_setup(unsigned char **scratch, int *sms) {
     int dev = 0;
@@ -1109,8 +1158,15 @@ int na_setup(unsigned char **scratch, int *sms) {
         if (cudaFuncSetAttribute(gemm_tc_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<16>::SMEM) != cudaSuccess ||
             cudaFuncSetAttribute(gemm_tc_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<32>::SMEM) != cudaSuccess)
             return nb_set_error("nemo_gemm_noalloc: cannot set the kernels' shared-memory size");
+        if (cudaMemset((unsigned char *)p + NA_PART_BYTES, 0, NA_COUNTERS * sizeof(int)) != cudaSuccess)
+            return nb_set_error("nemo_gemm_noalloc: cannot clear the arrival counters");
         g_na_sms[dev] = n;
+        g_na_cleared[dev] = g_tc_error_reports.load();
         g_na_ptr[dev] = (unsigned char *)p;
+    } else if (g_na_cleared[dev] != g_tc_error_reports.load()) {
+        if (cudaMemset(g_na_ptr[dev] + NA_PART_BYTES, 0, NA_COUNTERS * sizeof(int)) != cudaSuccess)
+            return nb_set_error("nemo_gemm_noalloc: cannot clear the arrival counters");
+        g_na_cleared[dev] = g_tc_error_reports.load();
     }
     *scratch = g_na_ptr[dev];
     *sms = g_na_sms[dev];
@@ -1163,9 +1219,6 @@ int na_launch(const nemo_gemm_args_t *a, cudaStream_t st, unsigned char *scratch
     p.e = nb::make_epi(a);
     p.ws = (float *)scratch;
     p.counters = (int *)(scratch + NA_PART_BYTES);
-    // the arrival counters must start at zero (a launch that gave up on a wait leaves them dirty)
-    if (p.splits > 1 && cudaMemsetAsync(p.counters, 0, (size_t)tiles * sizeof(int), st) != cudaSuccess)
-        return nb_set_error("nemo_gemm_noalloc: cannot clear the arrival counters");
     const int grid = p.units < sms ? p.units : sms;
     nb::launch(gemm_tc_kernel<BN>, grid, THREADS, Cfg<BN>::SMEM, st, mw, mh, ml, p);
     return nb_check_launch("gemm_tc_kernel");
@@ -1174,12 +1227,14 @@ int na_launch(const nemo_gemm_args_t *a, cudaStream_t st, unsigned char *scratch
 }  // namespace
 
 extern "C" int nemo_gemm_noalloc(const nemo_gemm_args_t *a, void *stream) {
-    if (!a) return nb_set_error("nemo_gemm_noalloc: null arguments");
-    if (a->M < 1 || a->M > NA_MAX_ROWS)
+    // the checks nemo_gemm makes (null pointers, shape, GLU with an odd N, accumulate into a
+    // non-fp32 output), then this entry's own limits
+    if (nb_gemm_validate(a, "nemo_gemm_noalloc")) return -1;
+    if (a->M == 0) return 0;
+    if (a->M > NA_MAX_ROWS)
         return nb_set_error("nemo_gemm_noalloc: M=%d rows; the allocation-free GEMM takes 1..%d rows (its static scratch is sized for that)", a->M,
                             NA_MAX_ROWS);
     if (a->a_fmt != NEMO_FMT_BF16X2) return nb_set_error("nemo_gemm_noalloc: activations must be NEMO_FMT_BF16X2 planes");
-    if (a->N < 1 || a->K < 1) return nb_set_error("nemo_gemm_noalloc: empty N or K");
     if (a->act == NEMO_ACT_GLU && ((a->N / 2) % 64)) return nb_set_error("nemo_gemm_noalloc: GLU needs N/2 to be a multiple of 64");
     if (a->K % 8) return nb_set_error("nemo_gemm_noalloc: K must be a multiple of 8");
     unsigned char *scratch = nullptr;

@@ -699,13 +699,7 @@ extern "C" int nemo_subsample_front(const float *X, int64_t x_sstride, const flo
         void (*k)(const float *, int64_t, const float *, const float *, const float *, const float *, void *, int64_t, int, int, int, int, int) =
             F == 128 ? (bf ? subsample_front_tile_kernel<128, true> : subsample_front_tile_kernel<128, false>)
                      : (bf ? subsample_front_tile_kernel<0, true> : subsample_front_tile_kernel<0, false>);
-        static size_t attr_set[4] = {};  // largest dynamic shared-memory size enabled so far, per instantiation
-        const int ki = (F == 128 ? 0 : 2) + (bf ? 1 : 0);
-        if (smem > attr_set[ki]) {
-            if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
-                return nb_set_error("nemo_subsample_front: %zu bytes of shared memory unavailable", smem);
-            attr_set[ki] = smem;
-        }
+        if (nb_smem_attr((const void *)k, smem)) return nb_set_error("nemo_subsample_front: %s", nemo_gpu_last_error());
         const dim3 grid((unsigned)(streams * ((T2 + FT_TR - 1) / FT_TR)), (unsigned)(C / 32));
         nb::launch(k, grid, 256, smem, (cudaStream_t)stream, X, x_sstride, W0, b0, W2, b2, Y, y_plane, T, F, T1, T2, C);
         return nb_check_launch("subsample_front_tile_kernel");

@@ -108,12 +108,7 @@ extern "C" int nemo_resample(const float *in, int64_t in_ld, int64_t in_start, i
     const Rate r = rate_of(in_rate, out_rate);
     const size_t smem = smem_bytes(r.half);
     if (smem > SMEM_LIMIT) return nb_set_error("nemo_resample: %d -> %d Hz needs %zu B of shared memory", in_rate, out_rate, smem);
-    static size_t smem_set = 0;
-    if (smem > 48 * 1024 && smem > smem_set) {
-        if (cudaFuncSetAttribute(resample_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
-            return nb_set_error("nemo_resample: %s", cudaGetErrorString(cudaGetLastError()));
-        smem_set = smem;
-    }
+    if (nb_smem_attr((const void *)resample_kernel, smem)) return nb_set_error("nemo_resample: %s", nemo_gpu_last_error());
     const dim3 grid((count + OPB - 1) / OPB, (streams + SPB - 1) / SPB);
     nb::launch(resample_kernel, grid, OPB * WARPS, smem, (cudaStream_t)stream, in, in_ld, in_start, in_len, nin, out0, count, r, tap_pitch(r.half),
                out, out_ld, streams);

@@ -10,6 +10,10 @@
 
 static const int LAT_MS[] = { 80, 160, 320, 560, 1120 }; /* src/nemoasr.c:58-59 */
 static const int LAT_R[] = { 0, 1, 3, 6, 13 };
+static int lat_index(int right) {
+    for (int i = 0; i < 5; ++i) if (LAT_R[i] == right) return i;
+    return -1;
+}
 static int right_for(int latency_ms) {
     for (int i = 0; i < 5; ++i) if (LAT_MS[i] == latency_ms) return LAT_R[i];
     return -1;
@@ -18,6 +22,8 @@ static int right_for(int latency_ms) {
 struct nemoasr {
     nb_model_t *m;
     nb_engine_t *eng;
+    nb_engine_t *warm[5];  /* engines warmed by nemoasr_prepare_latency for other latencies (LAT_MS order) */
+    int prompt;            /* language prompt index of the session (kept across latency changes) */
     nb_mel_t *mel;
     nb_resampler_t *rs;
     int input_rate, latency_ms, finished, printed_any;
@@ -117,6 +123,7 @@ static nemoasr_t *open_common(nb_model_t *m, const char *language, int latency_m
     s->eng = nb_engine_create(m, 1, right, err, errlen);
     if (!s->eng) { nemoasr_close(s); return NULL; }
     if (nb_engine_set_prompt(s->eng, 0, idx, err, errlen)) { nemoasr_close(s); return NULL; }
+    s->prompt = idx;
     s->mel = nb_mel_create();
     s->input_rate = input_rate;
     s->latency_ms = latency_ms;
@@ -129,7 +136,7 @@ static nemoasr_t *open_common(nb_model_t *m, const char *language, int latency_m
 
 nemoasr_t *nemoasr_open(const char *model_dir, const char *language, int latency_ms, int input_rate, char *err, size_t errlen) {
     if (errlen) err[0] = 0;
-    if (right_for(latency_ms) < 0) { snprintf(err, errlen, "latency must be one of 80, 320, 560, 1120 ms"); return NULL; }
+    if (right_for(latency_ms) < 0) { snprintf(err, errlen, "latency must be one of 80, 160, 320, 560, 1120 ms"); return NULL; }
     if (input_rate <= 0) { snprintf(err, errlen, "input_rate must be positive"); return NULL; }
     const double t0 = nb_now_ms();
     nb_model_t *m = load_model(model_dir, NULL, err, errlen);
@@ -139,7 +146,7 @@ nemoasr_t *nemoasr_open(const char *model_dir, const char *language, int latency
 
 nemoasr_t *nemoasr_open_synthetic(const nemoasr_synth_spec_t *spec, const char *language, int latency_ms, int input_rate, char *err, size_t errlen) {
     if (errlen) err[0] = 0;
-    if (right_for(latency_ms) < 0) { snprintf(err, errlen, "latency must be one of 80, 320, 560, 1120 ms"); return NULL; }
+    if (right_for(latency_ms) < 0) { snprintf(err, errlen, "latency must be one of 80, 160, 320, 560, 1120 ms"); return NULL; }
     if (input_rate <= 0) { snprintf(err, errlen, "input_rate must be positive"); return NULL; }
     const double t0 = nb_now_ms();
     nb_model_t *m = load_model(NULL, spec, err, errlen);
@@ -150,6 +157,7 @@ nemoasr_t *nemoasr_open_synthetic(const nemoasr_synth_spec_t *spec, const char *
 void nemoasr_close(nemoasr_t *s) {
     if (!s) return;
     nb_engine_destroy(s->eng);
+    for (int i = 0; i < 5; ++i) nb_engine_destroy(s->warm[i]);
     nb_mel_destroy(s->mel);
     nb_resampler_destroy(s->rs);
     nb_model_free(s->m);
@@ -241,33 +249,58 @@ int nemoasr_feed_tokens(nemoasr_t *s, const float *samples, size_t n, int final,
 
 void nemoasr_free(char *text) { free(text); }
 
+static int check_latency(const nemoasr_t *s, int latency_ms, char *err, size_t errlen) {
+    const int right = right_for(latency_ms);
+    if (right < 0) { snprintf(err, errlen, "latency must be one of 80, 160, 320, 560, 1120 ms"); return -1; }
+    if (!nb_model_right_trained(s->m, right)) { snprintf(err, errlen, "latency %d ms not trained for this checkpoint", latency_ms); return -1; }
+    return right;
+}
+
+/* src/nemoasr.c:162-172 + src/warmup.c: the reference builds every GPU pipeline a stream at this
+   latency can hit and runs a dummy stream. Here the per-chunk work is a CUDA graph per chunk
+   shape, so the warm-up captures the graph of every shape the latency can produce (nothing runs):
+   on the session's engine when it already has this latency, else on an engine kept for it, which
+   a later nemoasr_reset to this latency takes over with its graphs. */
 int nemoasr_prepare_latency(nemoasr_t *s, int latency_ms, char *err, size_t errlen) {
     if (errlen) err[0] = 0;
-    const int right = right_for(latency_ms);
-    if (right < 0) { snprintf(err, errlen, "latency must be one of 80, 320, 560, 1120 ms"); return -1; }
-    if (!nb_model_right_trained(s->m, right)) { snprintf(err, errlen, "latency %d ms not trained for this checkpoint", latency_ms); return -1; }
-    return 0;
+    const int right = check_latency(s, latency_ms, err, errlen);
+    if (right < 0) return -1;
+    if (nb_engine_right(s->eng) == right) return nb_engine_prepare(s->eng, err, errlen);
+    const int li = lat_index(right);
+    if (!s->warm[li]) {
+        s->warm[li] = nb_engine_create(s->m, 1, right, err, errlen);
+        if (!s->warm[li]) return -1;
+    }
+    return nb_engine_prepare(s->warm[li], err, errlen);
 }
+
+int nemoasr_graphs_captured(const nemoasr_t *s) { return nb_engine_graphs(s->eng); }
 
 int nemoasr_reset(nemoasr_t *s, const char *language, int latency_ms, char *err, size_t errlen) {
     if (errlen) err[0] = 0;
-    if (nemoasr_prepare_latency(s, latency_ms, err, errlen)) return -1;
-    int idx = -1;
+    const int right = check_latency(s, latency_ms, err, errlen);
+    if (right < 0) return -1;
+    int idx = s->prompt;  /* no language given: keep the session's (the reference keeps it in the model) */
     if (language) {
         idx = nb_model_prompt_index(s->m, language);
         if (idx < 0) { snprintf(err, errlen, "unknown language prompt %s", language); return -1; }
     }
-    const int right = right_for(latency_ms);
     if (nb_engine_right(s->eng) == right) {
         if (nb_engine_reset(s->eng, err, errlen)) return -1;
     } else {
-        nb_engine_t *e = nb_engine_create(s->m, 1, right, err, errlen);
+        const int li = lat_index(right), cur = lat_index(nb_engine_right(s->eng));
+        nb_engine_t *e = s->warm[li];
+        s->warm[li] = NULL;
+        if (!e) e = nb_engine_create(s->m, 1, right, err, errlen);
         if (!e) return -1;
-        nb_engine_destroy(s->eng);
+        if (nb_engine_reset(e, err, errlen)) { nb_engine_destroy(e); return -1; }
+        /* the engine being replaced keeps its graphs for a later switch back */
+        nb_engine_destroy(s->warm[cur]);
+        s->warm[cur] = s->eng;
         s->eng = e;
-        if (idx < 0) idx = nb_model_prompt_index(s->m, "auto");
     }
-    if (idx >= 0 && nb_engine_set_prompt(s->eng, 0, idx, err, errlen)) return -1;
+    if (nb_engine_set_prompt(s->eng, 0, idx, err, errlen)) return -1;
+    s->prompt = idx;
     nb_mel_destroy(s->mel);
     s->mel = nb_mel_create();
     if (s->rs) { nb_resampler_destroy(s->rs); s->rs = nb_resampler_create(s->input_rate, NB_MEL_SR); }
@@ -308,7 +341,7 @@ nemoasr_batch_t *nemoasr_batch_open(const char *model_dir, const nemoasr_synth_s
                                     int latency_ms, int input_rate, char *err, size_t errlen) {
     if (errlen) err[0] = 0;
     const int right = right_for(latency_ms);
-    if (right < 0) { snprintf(err, errlen, "latency must be one of 80, 320, 560, 1120 ms"); return NULL; }
+    if (right < 0) { snprintf(err, errlen, "latency must be one of 80, 160, 320, 560, 1120 ms"); return NULL; }
     if (input_rate <= 0 || n_streams <= 0) { snprintf(err, errlen, "input_rate and n_streams must be positive"); return NULL; }
     nb_model_t *m = load_model(model_dir, synth, err, errlen);
     if (!m) return NULL;
@@ -471,6 +504,10 @@ void nemoasr_batch_stats(const nemoasr_batch_t *b, nemoasr_stats_t *out) {
     *out = b->stats;
     size_t chunks = 0;
     nb_engine_times(b->eng, &out->encoder_ms, &out->decoder_ms, &chunks); /* also covers steps driven by nemoasr_batch_step */
+}
+int nemoasr_batch_decode_counts(nemoasr_batch_t *b, long long out[4], char *err, size_t errlen) {
+    if (errlen) err[0] = 0;
+    return nb_engine_decode_counts(b->eng, out, err, errlen);
 }
 void nemoasr_batch_set_taps(nemoasr_batch_t *b, float *prompted, float *joint_enc, size_t cap_rows, int *chunk_rows, size_t cap_chunks) {
     nb_engine_set_taps(b->eng, prompted, joint_enc, cap_rows, chunk_rows, cap_chunks);

@@ -1,5 +1,6 @@
 // Error reporting and launch accounting shared by every C-ABI entry point.
 #include <atomic>
+#include <mutex>
 #include <cstdarg>
 #include <cstdio>
 #include "common.cuh"
@@ -52,4 +53,30 @@ extern "C" uint64_t nb_graph_kernel_nodes(cudaGraph_t g) {
         }
     delete[] nodes;
     return k;
+}
+
+// Raise a kernel's dynamic shared-memory limit to at least `bytes` on the current device. The
+// attribute belongs to the device, so the largest value set so far is kept per (kernel, device),
+// under a lock: a second device, or a thread on another device, sets its own.
+extern "C" int nb_smem_attr(const void *func, size_t bytes) {
+    if (bytes <= 48 * 1024) return 0;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return nb_set_error("no current CUDA device");
+    struct Entry { const void *func; int dev; size_t bytes; };
+    static Entry table[256];
+    static int used = 0;
+    static std::mutex mu;
+    std::lock_guard<std::mutex> lk(mu);
+    int i = 0;
+    while (i < used && !(table[i].func == func && table[i].dev == dev)) ++i;
+    if (i < used && table[i].bytes >= bytes) return 0;
+    if (cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes) != cudaSuccess)
+        return nb_set_error("%zu bytes of dynamic shared memory unavailable: %s", bytes, cudaGetErrorString(cudaGetLastError()));
+    if (i == used) {
+        if (used == 256) return 0;  // full: the attribute is set, only the memo is skipped
+        table[used++] = Entry{func, dev, bytes};
+    } else {
+        table[i].bytes = bytes;
+    }
+    return 0;
 }

@@ -111,6 +111,10 @@ def _setup_api(L):
     L.nemoasr_batch_set_taps.argtypes = [C.c_void_p, f32p, f32p, C.c_size_t, i32p, C.c_size_t]
     L.nemoasr_batch_attach_mel.argtypes = [C.c_void_p, C.c_void_p, C.c_int64, C.c_size_t, C.c_char_p, C.c_size_t]
     L.nemoasr_batch_step.argtypes = [C.c_void_p, C.c_int, i32p, C.c_int, i32p, i32p, C.c_char_p, C.c_size_t]
+    L.nemoasr_batch_decode_counts.argtypes = [C.c_void_p, C.POINTER(C.c_longlong), C.c_char_p, C.c_size_t]
+    L.nemoasr_graphs_captured.argtypes = [C.c_void_p]
+    L.nemo_gpu_wait_selftest.argtypes = [C.c_int, C.c_longlong, C.c_void_p]
+    L.nemo_gemm_noalloc.argtypes = [C.POINTER(GemmArgs), C.c_void_p]
     L.nemoasr_batch_gpu_ms.argtypes = [C.c_void_p]
     L.nemoasr_batch_gpu_ms.restype = C.c_double
     L.nemo_gemm.argtypes = [C.POINTER(GemmArgs), C.c_void_p]
@@ -279,6 +283,15 @@ class Batch:
         self.tj = np.zeros((rows, joint_hidden), np.float32)
         self.tc = np.zeros(rows, np.int32)
         api().nemoasr_batch_set_taps(self.h, self.tp.ctypes.data_as(f32p), self.tj.ctypes.data_as(f32p), rows, self.tc.ctypes.data_as(i32p), rows)
+
+    def decode_counts(self):
+        """Greedy-decoder counts since open/reset: stream-frames, frames that emitted, decisions,
+        loop iterations."""
+        out = (C.c_longlong * 4)()
+        err = C.create_string_buffer(1024)
+        if api().nemoasr_batch_decode_counts(self.h, out, err, 1024):
+            raise RuntimeError(err.value.decode())
+        return dict(frames=out[0], emitting_frames=out[1], decisions=out[2], iterations=out[3])
 
     def stats(self):
         s = Stats()

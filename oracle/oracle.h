@@ -81,6 +81,18 @@ size_t or_resampler_flush(or_resampler_t *r, float *out, size_t out_max);
 
 int or_num_threads(void);
 
+/* ---- synthetic workload (oracle_synth.c): the benchmark's random-init checkpoint and audio --- */
+typedef struct {  /* same layout as nemoasr_synth_spec_t */
+    uint64_t seed;
+    int n_layers, d_model, ff_factor, sub_channels, num_prompts, prompt_hidden;
+    int pred_hidden, joint_hidden, vocab_size;
+    int att_left;
+    float weight_std, blank_bias;
+} or_synth_spec_t;
+void or_synth_default(or_synth_spec_t *s);
+int or_synth_write(const char *dir, const or_synth_spec_t *s, char *err, size_t errlen);
+void or_synth_audio(uint64_t seed, int rate, size_t n, int pauses, float *out);
+
 #ifdef __cplusplus
 }
 #endif

@@ -351,6 +351,42 @@ def num_threads():
 
 
 # ---------------------------------------------------------------------------------------------
+# the benchmark's synthetic workload, generated without the product library (oracle_synth.c)
+
+class SynthSpec(C.Structure):  # or_synth_spec_t (the layout of nemoasr_synth_spec_t)
+    _fields_ = [("seed", C.c_uint64), ("n_layers", C.c_int), ("d_model", C.c_int), ("ff_factor", C.c_int),
+                ("sub_channels", C.c_int), ("num_prompts", C.c_int), ("prompt_hidden", C.c_int),
+                ("pred_hidden", C.c_int), ("joint_hidden", C.c_int), ("vocab_size", C.c_int), ("att_left", C.c_int),
+                ("weight_std", C.c_float), ("blank_bias", C.c_float)]
+
+
+def synth_default(**kw):
+    s = SynthSpec()
+    lib().or_synth_default(C.byref(s))
+    for k, v in kw.items():
+        setattr(s, k, v)
+    return s
+
+
+def synth_write(d, spec):
+    L = lib()
+    L.or_synth_write.argtypes = [C.c_char_p, C.POINTER(SynthSpec), C.c_char_p, C.c_size_t]
+    err = C.create_string_buffer(512)
+    if L.or_synth_write(d.encode(), C.byref(spec), err, 512):
+        raise RuntimeError(err.value.decode())
+    return d
+
+
+def synth_audio(seed, rate, seconds=None, n=None, pauses=False):
+    L = lib()
+    L.or_synth_audio.argtypes = [C.c_uint64, C.c_int, C.c_size_t, C.c_int, f32p]
+    n = int(round(seconds * rate)) if n is None else n
+    out = np.zeros(n, np.float32)
+    L.or_synth_audio(seed, rate, n, int(pauses), _ptr(out))
+    return out
+
+
+# ---------------------------------------------------------------------------------------------
 # the reference's own host code on CPU (built only where the reference sources are present)
 
 def ref_available():

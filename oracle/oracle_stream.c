@@ -715,7 +715,7 @@ static const int LAT_R[] = { 0, 1, 3, 6, 13 };
 or_session_t *or_open(or_model_t *m, int latency_ms, int input_rate, char *err, size_t errlen) {
     int right = -1;
     for (int i = 0; i < 5; ++i) if (LAT_MS[i] == latency_ms) right = LAT_R[i];
-    if (right < 0) { snprintf(err, errlen, "latency must be one of 80, 320, 560, 1120 ms"); return NULL; }
+    if (right < 0) { snprintf(err, errlen, "latency must be one of 80, 160, 320, 560, 1120 ms"); return NULL; }
     if (input_rate <= 0) { snprintf(err, errlen, "input_rate must be positive"); return NULL; }
     or_session_t *s = calloc(1, sizeof *s);
     s->m = m;

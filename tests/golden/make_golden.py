@@ -5,7 +5,7 @@ sources (src/encoder.c, decoder.c, model.c, nemoasr.c, mel.c, resample.c, ...) u
 with oracle/ref_gpu_cpu.c, a CPU stand-in for its GPU layer that executes each kernel dispatch
 with the restated kernels. The fixtures below are what that build produces on a small seeded
 random-init checkpoint of the same architecture. Run from the repository root after
-`python -c "import __graft_entry__ as g; g.build()"` in a checkout where the reference exists:
+`NEMO_REFERENCE_SRC=<reference checkout> python -c "import __graft_entry__ as g; g.build()"`:
 
     python tests/golden/make_golden.py
 """

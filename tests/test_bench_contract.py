@@ -1,5 +1,6 @@
 """The bench's reference arm runs on the host cores alone: one JSON line with the keys the driver
-reads (the reference arm's line carries impl, cpu_baseline and a host-only e2e)."""
+reads (the reference arm's line carries impl, cpu_baseline and a host-only e2e), and the process
+loads no library of the product (only the oracle's: the reference's host C and the restatement)."""
 import json
 import os
 import subprocess
@@ -25,3 +26,15 @@ def test_reference_arm_prints_one_contract_line():
     assert cb["kind"] in ("reference", "port") and cb["cores"] >= 1 and cb["value"] == d["value"] and cb["sample"]
     e = d["e2e"]
     assert e["value"] == d["value"] and e["unit"] == d["unit"] and e["h2d_bytes_per_step"] == 0 and e["d2h_bytes_per_step"] == 0
+    libs = d["libraries_from_repo"]
+    assert libs and all(l.startswith("oracle" + os.sep) for l in libs), libs
+
+
+def test_host_threads_split_per_rank(monkeypatch):
+    sys.path.insert(0, ROOT)
+    import bench
+    monkeypatch.setenv("LOCAL_WORLD_SIZE", "8")
+    n8 = bench.host_threads()
+    monkeypatch.setenv("LOCAL_WORLD_SIZE", "1")
+    n1 = bench.host_threads()
+    assert n1 == (os.cpu_count() or 8) and n8 == max(1, n1 // 8)

@@ -1,8 +1,9 @@
 """The fused batched greedy iteration (LSTM cells and the joint input computed in the tensor-core
 GEMM epilogues, the input half of LSTM layer 0 read from a per-token gate table, one step kernel
-per iteration) against the kernel-by-kernel iteration (NEMO_DEC_FUSED=0) and, for any stream
-whose tokens differ, against the oracle: token ids identical up to oracle near-ties. 40 streams
-of the full-size model (activation-major tiles, several compaction epochs) and 5 of the tiny one."""
+per iteration) against the kernel-by-kernel iteration (NEMO_DEC_FUSED=0), and against the oracle
+for two fixed streams of every batch plus any stream whose tokens differ between the two: token
+ids identical up to oracle near-ties. 40 streams of the full-size model (activation-major tiles,
+several compaction epochs) and 5 of the tiny one."""
 import os
 
 import numpy as np
@@ -48,7 +49,7 @@ def _check(B, ckpt, oracle_model, lat, secs, blank, seed0, prompts=128):
     assert sum(len(t) for t in fused) > 0
     differ = [i for i in range(B) if fused[i] != plain[i]]
     print(f"{B} streams: {sum(len(t) for t in fused)} tokens, {len(differ)} streams differ")
-    for i in differ:
+    for i in sorted(set(differ) | {0, B - 1}):
         o = orc.run_stream(oracle_model, audio[i], 16000, lat, language=langs[i], block=1600)
         for t in (fused[i], plain[i]):
             ok, note = tokens_match(t, o["tokens"], o["dec_token"], o["dec_margin"], blank=blank)

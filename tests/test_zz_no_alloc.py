@@ -1,8 +1,10 @@
-"""nemo_gemm_noalloc (the allocation-free tensor-core GEMM) against nemo_gemm through the C ABI.
+"""nemo_gemm_noalloc (the allocation-free tensor-core GEMM) against nemo_gemm through the C ABI,
+and against the oracle GEMM (src/kernels.metal:120-208 restated in oracle/).
 
-Both run the same kernel with the same split-K plan, so results should agree to the bit; the
-tolerance below (max|d| / max|ref|) only allows for that changing. Each case calls the new entry
-twice in a row into fresh outputs, so a counter or partial tile left over by the first call
+Both entry points run the same kernel with the same split-K plan, so results should agree to the
+bit; NOALLOC_TOL (max|d| / max|ref|) only allows for that changing. Against the oracle the bar is
+the tensor-core GEMM's own (activations carried as bf16 hi/lo planes). Each case calls the new
+entry twice in a row into fresh outputs, so a counter or partial tile left over by the first call
 would show up in the second."""
 import ctypes as C
 
@@ -11,11 +13,13 @@ import pytest
 import torch
 
 import nemoasr_b200 as nb
+import oracle as orc
 from parity import rel_err
 
 pytestmark = pytest.mark.gpu
 
 NOALLOC_TOL = 1e-6
+ORACLE_TOL = 2e-4  # bf16 hi/lo activation planes (16-bit mantissa) into the tensor cores
 
 
 def _lib():
@@ -72,8 +76,11 @@ def test_noalloc_matches_nemo_gemm(M, N, K, act, acc):
     torch.cuda.synchronize()
     assert L.nemo_gpu_check_device_errors() == 0, _err()
     ref = dR.cpu().numpy()
+    Wh = dW.view(torch.int16).cpu().numpy().view(np.uint16)
+    want = orc.gemm(A, Wh, db.cpu().numpy(), C0=C0.cpu().numpy(), act=act, accumulate=bool(acc), alpha=0.5)
     for o in outs:
         assert rel_err(o.cpu().numpy(), ref) <= NOALLOC_TOL
+        assert rel_err(o.cpu().numpy(), want) <= ORACLE_TOL
 
 
 def test_noalloc_rejects_beyond_its_limits():
@@ -88,3 +95,17 @@ def test_noalloc_rejects_beyond_its_limits():
     a.M, a.a_fmt = 8, 0
     assert L.nemo_gemm_noalloc(C.byref(a), None) != 0
     assert "BF16X2" in _err()
+    # the checks nemo_gemm makes, all on the host before any launch
+    a = _args(dA, dW, None, dC, 8, N, K, 0, 0, 1.0)
+    a.C = None
+    assert L.nemo_gemm_noalloc(C.byref(a), None) != 0
+    assert "null pointer" in _err()
+    a = _args(dA, dW, None, dC, 8, N, K, 0, 1, 1.0)
+    a.c_fmt = 1
+    assert L.nemo_gemm_noalloc(C.byref(a), None) != 0
+    assert "accumulate" in _err()
+    a = _args(dA, dW, None, dC, 8, 129, K, 3, 0, 1.0)
+    assert L.nemo_gemm_noalloc(C.byref(a), None) != 0
+    assert "even N" in _err()
+    a = _args(dA, dW, None, dC, 0, N, K, 0, 0, 1.0)
+    assert L.nemo_gemm_noalloc(C.byref(a), None) == 0  # no rows: nothing to do, as nemo_gemm
