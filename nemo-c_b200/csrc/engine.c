@@ -8,7 +8,7 @@
 #include <stdlib.h>
 #include <string.h>
 
-#define NB_MAX_GRAPHS 256
+#define NB_MAX_GRAPHS 512
 #define CK(x) do { cudaError_t e_ = (x); if (e_ != cudaSuccess) { snprintf(err, errlen, "%s: %s", #x, cudaGetErrorString(e_)); goto fail; } } while (0)
 #define KL(x) do { if ((x) != 0) { snprintf(err, errlen, "%s", nemo_gpu_last_error()); return -1; } } while (0)
 
@@ -67,6 +67,7 @@ struct nb_engine {
     /* one stream: the conformer blocks run as one persistent kernel (NEMO_PERSISTENT=0 disables) */
     int use_enc1, enc1_grid, enc1_slot;
     NbEnc1Layer *enc1_layers;  /* host copy, passed by value at each launch */
+    uint8_t *enc1_image;       /* the weights laid out per CTA of the persistent grid */
     NbEnc1Args enc1_args;      /* launch arguments (large: the layer table travels by value) */
     /* one stream: the greedy loop of a chunk runs as one persistent kernel (NEMO_PERSISTENT=0 disables) */
     int use_dec1, dec1_grid;
@@ -123,10 +124,10 @@ static int enc1_setup(nb_engine_t *e, char *err, size_t errlen) {
     if (!coop || sms <= 0 || D % 128 || D > 1024 || g->n_heads * 128 != D || e->cmax > 16 || e->Lmax > 72 || g->n_layers > NB_ENC1_MAX_LAYERS ||
         g->conv_kernel > 9)
         return 0;
-    /* per-CTA weight rows must fit the kernel's 32-row accumulator tiles */
-    if ((FF + sms - 1) / sms > 32 || (3 * D + sms - 1) / sms > 32 || 2 * ((D + sms - 1) / sms) > 32) return 0;
-    const int slot = nb_encoder1_slot_bytes(D, FF, sms);
-    if (nb_encoder1_smem(slot) > (size_t)optin) return 0;
+    /* per-CTA weight rows must fit the kernel's 32-row accumulator tiles and two of the largest
+       entries its weight ring (0 otherwise) */
+    const int ring = nb_encoder1_ring_bytes(D, FF, sms, (size_t)optin);
+    if (!ring || nb_encoder1_smem(ring) > (size_t)optin) return 0;
     NbEnc1Layer *L = calloc((size_t)g->n_layers, sizeof *L);
     const size_t kv_s = (size_t)e->cap_rows * 3 * D, din_s = (size_t)e->cap_rows * D;
     for (int l = 0; l < g->n_layers; ++l) {
@@ -142,12 +143,30 @@ static int enc1_setup(nb_engine_t *e, char *err, size_t errlen) {
         o->din = e->din + (size_t)l * din_s;
     }
     e->enc1_layers = L;
+    /* the weights re-laid out in the order the persistent grid reads them (one bulk copy per CTA
+       and projection); without room for the copy the blocks run kernel by kernel */
+    const size_t img = nb_encoder1_image_bytes(D, FF, g->n_layers);
+    if (cudaMalloc((void **)&e->enc1_image, img) != cudaSuccess) {
+        cudaGetLastError();
+        e->enc1_image = NULL;
+        return 0;
+    }
+    {
+        NbEnc1Args *q = &e->enc1_args;
+        memset(q, 0, sizeof *q);
+        memcpy(q->L, L, (size_t)g->n_layers * sizeof *L);
+        q->layers = g->n_layers; q->D = D; q->FF = FF;
+        if (nb_encoder1_repack(q, sms, e->enc1_image, e->st) || cudaStreamSynchronize(e->st) != cudaSuccess) {
+            snprintf(err, errlen, "persistent encoder set-up: %s", nemo_gpu_last_error());
+            return -1;
+        }
+    }
     const int rc = cudaMalloc((void **)&e->d_enc1_bar, 2 * sizeof(unsigned)) != cudaSuccess || cudaMalloc((void **)&e->d_enc1_err, sizeof(int)) != cudaSuccess ||
                    cudaMemset(e->d_enc1_err, 0, sizeof(int)) != cudaSuccess;
     if (rc) { snprintf(err, errlen, "persistent encoder set-up: %s", cudaGetErrorString(cudaGetLastError())); return -1; }
     e->use_enc1 = 1;
     e->enc1_grid = sms;
-    e->enc1_slot = slot;
+    e->enc1_slot = ring;
     return 0;
 }
 
@@ -387,6 +406,7 @@ void nb_engine_destroy(nb_engine_t *e) {
     if (e->d_dec1_i) cudaFree(e->d_dec1_i);
     if (e->d_dec1_bar) cudaFree(e->d_dec1_bar);
     if (e->d_enc1_bar) cudaFree(e->d_enc1_bar);
+    if (e->enc1_image) cudaFree(e->enc1_image);
     if (e->d_enc1_err) cudaFree(e->d_enc1_err);
     if (e->pending) for (int s = 0; s < e->B; ++s) free(e->pending[s]);
     free(e->pending);
@@ -662,10 +682,10 @@ static int launch_encoder(nb_engine_t *e, int nwin, int c) {
         memset(q, 0, sizeof *q);
         memcpy(q->L, e->enc1_layers, (size_t)g->n_layers * sizeof *e->enc1_layers);
         q->layers = g->n_layers; q->D = D; q->FF = FF; q->H = g->n_heads; q->taps = g->conv_kernel; q->Lmax = e->Lmax; q->c = c;
-        q->slot_bytes = e->enc1_slot;
+        q->ring_bytes = e->enc1_slot;
         q->eps = eps; q->scale = 1.0f / sqrtf(128.0f);
         q->pos = d_pos; q->cache_len = d_cache_len;
-        q->h = h; q->ff = e->ff; q->att = e->att;
+        q->h = h; q->h2 = hn; q->ff = e->ff; q->att = e->att; q->image = e->enc1_image;
         q->xout = (uint16_t *)e->xin; q->xout_plane = plD;
         q->bar = e->d_enc1_bar; q->err = e->d_enc1_err;
         if (nb_encoder1(q, e->enc1_grid, st)) return -1;
@@ -978,7 +998,16 @@ int nb_engine_prepare(nb_engine_t *e, char *err, size_t errlen) {
     if (!e->use_graphs) return 0;
     int shapes[NB_MAX_GRAPHS][2];
     const int n = chunk_shapes(e, shapes, NB_MAX_GRAPHS);
-    if (n + e->ngraphs > NB_MAX_GRAPHS) { snprintf(err, errlen, "warm-up: %d chunk shapes exceed the graph table", n); return -1; }
+    int missing = 0;
+    for (int i = 0; i < n && i < NB_MAX_GRAPHS; ++i) {
+        int have = 0;
+        for (int j = 0; j < e->ngraphs; ++j) have |= e->graphs[j].kind == 0 && e->graphs[j].k1 == shapes[i][0] && e->graphs[j].k2 == shapes[i][1];
+        missing += !have;
+    }
+    if (n > NB_MAX_GRAPHS || missing * (e->use_dec1 ? 1 : 2) + e->ngraphs > NB_MAX_GRAPHS) {
+        snprintf(err, errlen, "warm-up: %d chunk shapes exceed the graph table", n);
+        return -1;
+    }
     for (int i = 0; i < n; ++i) {
         const int c = shapes[i][1];
         if (c > e->cmax) { snprintf(err, errlen, "warm-up: chunk of %d rows exceeds buffer %d", c, e->cmax); return -1; }

@@ -12,12 +12,13 @@
 namespace nb {
 
 __device__ __forceinline__ bool grid_arrive_wait(unsigned *bar, unsigned target, int *err, int code, long long limit) {
-    __threadfence();
-    asm volatile("red.relaxed.gpu.global.add.u32 [%0], 1;" ::"l"(bar) : "memory");
+    asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(bar) : "memory");
     const long long t0 = clock64();
     bool ok = true;
-    // one relaxed 8-byte load polls the arrival count and the abort word together; the fence
-    // after the loop orders this CTA's later reads after every arrival it observed
+    // the arrival is a release (this CTA's writes, ordered before it by the caller's CTA barrier,
+    // are visible to whoever observes it); one relaxed 8-byte load polls the arrival count and the
+    // abort word together; the fence after the loop orders this CTA's later reads after every
+    // arrival it observed
     for (;;) {
         unsigned cnt, ab;
         asm volatile("ld.relaxed.gpu.global.v2.u32 {%0, %1}, [%2];" : "=r"(cnt), "=r"(ab) : "l"(bar) : "memory");
@@ -30,7 +31,7 @@ __device__ __forceinline__ bool grid_arrive_wait(unsigned *bar, unsigned target,
             break;
         }
     }
-    __threadfence();
+    asm volatile("fence.acq_rel.gpu;" ::: "memory");
     return ok;
 }
 

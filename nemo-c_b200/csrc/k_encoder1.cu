@@ -3,30 +3,37 @@
 //
 // Why: with a handful of rows the chunk is a chain of ~220 small dependent steps, each of which
 // streams a few MB of bf16 weights (1.18 GB per chunk). Launched one by one, every step pays a
-// launch, a pipeline fill and a split-K reduction. Here each CTA owns a fixed slice of output
-// columns of every projection, so a projection needs no cross-CTA reduction, and a producer warp
-// streams the CTA's weight rows of the NEXT projections into a ring of shared-memory slots
-// (bulk copies) while the compute warps are still waiting on the grid barrier of the current
-// one: the weight stream does not wait on the dependency chain.
+// launch, a pipeline fill and a split-K reduction. Here the weight stream runs ahead of the
+// dependency chain: one warp of each CTA requests the CTA's weight rows of the coming projections
+// into a ring of shared memory as far ahead as the ring holds, one bulk copy per projection out
+// of a copy of the weights laid out per CTA at set-up (the weight image), so each stage
+// of the chain costs one grid barrier, one gather of its input rows from L2 and a few hundred
+// cycles of math.
 //
-// Stages of block l (grid barrier after each):
-//   FF1a  ff = SiLU(LN_ff1(x) W1^T)            x = h (l = 0) or LN_out_{l-1}(h)
-//   FF1b  h  = x + 0.5 ff W2^T
-//   QKV   kv[pos + r] = LN_att(h) Wqkv^T        (cache rows, src/encoder.c:160)
+// Stages of block l (a grid barrier after each); x = h (l = 0) or LN_out_{l-1}(h):
+//   FF1a  ff = SiLU(LN_ff1(x) W1^T)                  CTA b: a slice of the FF hidden columns
+//   FF1b  h' = x + 0.5 ff W2^T                       CTA (kr, g): output columns of group g over
+//                                                    the kr-th 1024-wide range of the hidden;
+//                                                    the ranges' partial sums meet in h' through
+//                                                    red.add (h' zeroed one stage ahead)
+//   QKV   kv[pos + r] = LN_att(h') Wqkv^T            (cache rows, src/encoder.c:160)
 //   ATT   att = rel-pos attention over the cache window, one CTA per (head, row)
-//   WO    h += att Wo^T
-//   PW1   din[pos + r] = GLU(LN_conv(h) Wpw1^T); then each CTA runs the causal depthwise conv of
-//         its own channels (they depend on its own din columns only) into xdw
-//   PW2   h += SiLU(LN_bn(xdw)) Wpw2^T
-//   FF2a  ff = SiLU(LN_ff2(h) W1^T)
-//   FF2b  h += 0.5 ff W2^T
+//   WO    h' += att Wo^T
+//   PW1   din[pos + r] = GLU(LN_conv(h') Wpw1^T); each CTA then runs the causal depthwise conv
+//         of its own channels (they need its own din columns only) into y
+//   PW2   h' += SiLU(LN_bn(y)) Wpw2^T
+//   FF2a  ff = SiLU(LN_ff2(h') W1^T)
+//   FF2b  h = h' + 0.5 ff W2^T                       (as FF1b, back into the block's input buffer)
 // and after the last block xout = LN_out(h) as bf16 hi/lo planes for the prompt projection.
 //
-// Projections run on the tensor cores with mma.sync m16n8k16 (weights as the 16-row operand,
-// activation rows as the 8-column operand, bf16 hi/lo activation planes as in the batched path),
-// K split over the 8 compute warps and reduced through shared memory. Every wait is bounded:
-// on a timeout the CTA records an error, raises a global abort flag that every other wait also
-// watches, lets its producer drain its copies in flight, and returns.
+// Every stage's input is at most 1024 columns wide: each thread gathers four columns of every
+// row with one 16-byte L2 load per row, reduces the LayerNorm statistics in registers,
+// normalises, and stores bf16 hi/lo planes in shared memory. Projections run on the tensor cores
+// with mma.sync m16n8k16 (weights as the 16-row operand, activation rows as the 8-column
+// operand, hi and lo planes as two products), K split over the 8 compute warps and reduced
+// through shared memory. Every wait is bounded: on a timeout the CTA records an error, raises a
+// global abort flag that every other wait also watches, waits (bounded) for its copies in flight,
+// and returns.
 #include <cuda_bf16.h>
 #include "common.cuh"
 #include "engine_dev.h"
@@ -38,36 +45,59 @@ namespace {
 constexpr int CWARPS = 8;
 constexpr int CTHREADS = CWARPS * 32;
 constexpr int THREADS = CTHREADS;
+constexpr int ISSUE_WARP = CWARPS - 1;
 constexpr int MAXC = 16;
-constexpr int KC = 512;                 // activation k-chunk staged in shared memory
-constexpr int ACT_PITCH = KC * 2 + 16;  // bytes per staged activation row (+16: ldmatrix bank spread)
-constexpr int ACT_PLANE = MAXC * ACT_PITCH;
-constexpr int NSLOT = 3;
-constexpr int MAXL = 72;              // attention window rows (56 history + 16 new)
-constexpr int NSTAGE = 8;               // projections per block
+constexpr int KRW = 1024;                // widest k-range of one stage
+constexpr int APITCH = KRW * 2 + 16;     // bytes per staged activation row (+16: ldmatrix bank spread)
+constexpr int ACT_PLANE = MAXC * APITCH;
+constexpr int ACT_BYTES = 2 * ACT_PLANE; // bf16 hi and lo planes
+constexpr int NB = 8;                    // projections in flight in the weight ring at most
+constexpr int MAXL = 72;                 // attention window rows (56 history + 16 new)
+constexpr int MAXR = 32;                 // weight rows of one CTA in one projection
+constexpr int NSTAGE = 8;                // projections per block
 constexpr long long WAIT_LIMIT = 2000000000LL;  // clock cycles (~1 s)
 
 struct Smem {
-    // weight slots live at the front of dynamic shared memory; this struct follows them
-    __align__(16) uint8_t act[2 * ACT_PLANE];        // bf16 hi / lo activation planes of one k-chunk
-    float red[CWARPS][2][2][128];                     // per-warp partial accumulators
-    float outv[32][MAXC];                             // reduced outputs [weight row][activation row]
-    float st[MAXC][4];                                // row statistics: mean1, inv1, mean2, inv2
-    float rs[CWARPS][16];                             // per-warp partial row sums
-    float hs[MAXC][32];                               // this CTA's columns of the residual stream
-    float glu[32][MAXC];                              // conv-module GLU outputs of this CTA's channels
-    float sc[MAXL];                                   // attention scores / probabilities
-    float vpart[2][128];                              // attention value halves
-    uint64_t full[NSLOT], vbar;
+    float red[CWARPS][2][2][128];  // per-warp partial accumulators
+    float outv[MAXR][MAXC];        // reduced outputs [weight row][activation row]
+    float st[MAXC][4];             // row statistics: mean1, inv1, mean2, inv2
+    float rs[2][CWARPS][2 * MAXC]; // per-warp row sums (two buffers)
+    float glu[8][MAXC];            // conv-module GLU outputs of this CTA's channels
+    float sc[MAXL];                // attention scores / probabilities
+    float vpart[2][128];           // attention value halves
+    uint64_t full[NB], vbar;
+    int ring_off[NB];              // byte offset of projection i's rows in the ring (slot i % NB)
+    int ring_size[NB];             // and its bytes
+    int g_lo[NSTAGE], g_hi[NSTAGE], g_kr[NSTAGE], g_krw[NSTAGE], g_rows[NSTAGE], g_pitch[NSTAGE];
+    long long g_img[NSTAGE];       // byte offset of this CTA's block of projection s in block 0 of the image
+    int consumed;                  // projections taken by the compute warps (set when they stop)
+    int issued;                    // projections requested so far
+    int vpending;                  // 1 + phase of a value-row copy the compute warps gave up on
     int abort;
 };
-// attention keeps the value rows of its window in the activation tile + reduction area
-static_assert(offsetof(Smem, red) + sizeof(float) * CWARPS * 2 * 2 * 128 >= MAXL * 512, "value rows do not fit");
+static_assert(ACT_BYTES >= MAXL * 512, "attention value rows do not fit the activation area");
 
 __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
     asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(sm100::smem_u32(dst)),
                  "l"(src), "r"(bytes), "r"(sm100::smem_u32(bar))
                  : "memory");
+}
+// The same for weight rows, which are read once per chunk: marked first to leave L2, so the 1.2 GB
+// weight stream does not push out the activations and the small per-layer tensors.
+__device__ __forceinline__ void bulk_g2s_stream(void *dst, const void *src, uint32_t bytes, uint64_t *bar, uint64_t policy) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
+                     sm100::smem_u32(dst)),
+                 "l"(src), "r"(bytes), "r"(sm100::smem_u32(bar)), "l"(policy)
+                 : "memory");
+}
+__device__ __forceinline__ uint64_t evict_first_policy() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+// Bring [p, p + bytes) into L2 (bytes and p multiples of 16).
+__device__ __forceinline__ void prefetch_l2(const void *p, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
 }
 
 __device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t &r0, uint32_t &r1, uint32_t &r2, uint32_t &r3) {
@@ -75,286 +105,291 @@ __device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t &r0, uint32_t &r
 }
 
 __device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0, uint32_t b1) {
-    asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+    // register operands only (not volatile): the compiler may schedule it among the fragment loads
+    asm("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
                  : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
                  : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
+
+__device__ __forceinline__ void red_add(float *p, float v) { asm volatile("red.relaxed.gpu.global.add.f32 [%0], %1;" ::"l"(p), "f"(v) : "memory"); }
 
 __device__ __forceinline__ float sigm(float x) { return __fdividef(1.0f, 1.0f + __expf(-x)); }
 
 __device__ __forceinline__ void cbar() { sm100::named_barrier(1, CTHREADS); }
 
-// Weight operand of projection s of block l.
-__device__ __forceinline__ void stage_w(const NbEnc1Args &a, int l, int s, const uint16_t *&W, int &N, int &K, bool &glu) {
+// Where CTA `cta` works in projection s of block l: its weight rows [lo, hi) (plus the gate rows
+// N/2 + [lo, hi) for GLU) over columns [kr * krw, (kr + 1) * krw) of K. A projection whose K is
+// wider than KRW is split two ways: KT / KRW k-ranges x (grid / ranges) column groups.
+struct Geo {
+    const uint16_t *W;
+    int N, K, krw, kr, lo, hi;
+    bool glu;
+};
+
+__device__ __forceinline__ void slice(int n, int parts, int part, int &lo, int &hi) {
+    lo = (int)(((long long)part * n) / parts);
+    hi = (int)(((long long)(part + 1) * n) / parts);
+}
+
+__device__ __forceinline__ Geo stage_geo(const NbEnc1Args &a, int l, int s, int cta, int grid) {
     const NbEnc1Layer &w = a.L[l];
     const int D = a.D, FF = a.FF;
-    glu = false;
+    Geo g;
+    g.glu = false;
     switch (s) {
-    case 0: W = w.ff1_w1; N = FF; K = D; break;
-    case 1: W = w.ff1_w2; N = D; K = FF; break;
-    case 2: W = w.wqkv; N = 3 * D; K = D; break;
-    case 3: W = w.wo; N = D; K = D; break;
-    case 4: W = w.pw1; N = 2 * D; K = D; glu = true; break;
-    case 5: W = w.pw2; N = D; K = D; break;
-    case 6: W = w.ff2_w1; N = FF; K = D; break;
-    default: W = w.ff2_w2; N = D; K = FF; break;
+    case 0: g.W = w.ff1_w1; g.N = FF; g.K = D; break;
+    case 1: g.W = w.ff1_w2; g.N = D; g.K = FF; break;
+    case 2: g.W = w.wqkv; g.N = 3 * D; g.K = D; break;
+    case 3: g.W = w.wo; g.N = D; g.K = D; break;
+    case 4: g.W = w.pw1; g.N = 2 * D; g.K = D; g.glu = true; break;
+    case 5: g.W = w.pw2; g.N = D; g.K = D; break;
+    case 6: g.W = w.ff2_w1; g.N = FF; g.K = D; break;
+    default: g.W = w.ff2_w2; g.N = D; g.K = FF; break;
     }
-}
-
-// This CTA's output columns [lo, hi) of an N-output projection.
-__device__ __forceinline__ void slice(int nout, int &lo, int &hi) {
-    lo = (int)(((long long)blockIdx.x * nout) / gridDim.x);
-    hi = (int)(((long long)(blockIdx.x + 1) * nout) / gridDim.x);
-}
-
-// Grid-wide barrier of the compute threads (arrival counter plus a global abort word every
-// waiter watches; gridsync.cuh). Returns false when the launch is being abandoned.
-__device__ bool grid_sync(const NbEnc1Args &a, Smem &S, unsigned &epoch) {
-    cbar();
-    if (threadIdx.x == 0) {
-        ++epoch;
-        if (!nb::grid_arrive_wait(a.bar, epoch * gridDim.x, a.err, 1, WAIT_LIMIT)) S.abort = 1;
-    }
-    cbar();
-    return !S.abort;
-}
-
-// Row statistics of the c rows of X ([c][D] fp32) for LayerNorm (src/kernels.metal:258-288:
-// mean, then the mean of squared deviations): st[r] = {mean, inv}. With (g2, b2) the rows are
-// normalised with (g1, b1) first and the statistics of that result go to st[r][2..3].
-__device__ void row_stats(Smem &S, const float *X, int c, int D, float eps, const float *g1, const float *b1, bool twice) {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    for (int r = warp; r < c; r += CWARPS) {
-        float v[32];
-        const int per = D / 32;  // values per lane (D <= 1024)
-#pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] = j < per ? X[(int64_t)r * D + j * 32 + lane] : 0.0f;
-        float s = 0.0f;
-#pragma unroll
-        for (int j = 0; j < 32; ++j) s += v[j];
-        const float mean = nb::warp_sum(s) / (float)D;
-        float q = 0.0f;
-#pragma unroll
-        for (int j = 0; j < 32; ++j) if (j < per) { const float d = v[j] - mean; q += d * d; }
-        const float inv = 1.0f / sqrtf(nb::warp_sum(q) / (float)D + eps);
-        float m2 = 0.0f, inv2 = 0.0f;
-        if (twice) {
-            float s2 = 0.0f;
-#pragma unroll
-            for (int j = 0; j < 32; ++j) if (j < per) { const int k = j * 32 + lane; v[j] = (v[j] - mean) * inv * g1[k] + b1[k]; s2 += v[j]; }
-            m2 = nb::warp_sum(s2) / (float)D;
-            float q2 = 0.0f;
-#pragma unroll
-            for (int j = 0; j < 32; ++j) if (j < per) { const float d = v[j] - m2; q2 += d * d; }
-            inv2 = 1.0f / sqrtf(nb::warp_sum(q2) / (float)D + eps);
+    const int nout = g.glu ? g.N / 2 : g.N;
+    if (g.K <= KRW) {
+        g.krw = g.K;
+        g.kr = 0;
+        slice(nout, grid, cta, g.lo, g.hi);
+    } else {
+        g.krw = KRW;
+        const int ranges = g.K / KRW, groups = grid / ranges;
+        if (cta >= ranges * groups) {
+            g.kr = 0;
+            g.lo = g.hi = 0;
+        } else {
+            g.kr = cta / groups;
+            slice(nout, groups, cta % groups, g.lo, g.hi);
         }
-        if (lane == 0) { S.st[r][0] = mean; S.st[r][1] = inv; S.st[r][2] = m2; S.st[r][3] = inv2; }
+    }
+    return g;
+}
+
+__device__ __forceinline__ int geo_rows(const Geo &g) { return (g.glu ? 2 : 1) * (g.hi - g.lo); }
+__device__ __forceinline__ int geo_pitch(const Geo &g) { return g.krw * 2 + 16; }
+
+// ---- weight image ------------------------------------------------------------------------------
+// The weights re-laid out once, at set-up, in the order and padded row pitch the CTAs read them:
+// block (l, s, b) holds CTA b's rows of projection s of block l (value rows then, for GLU, gate
+// rows; the k-range of its column group for a split projection), each row krw bf16 followed by 16
+// zero bytes, so one bulk copy brings a projection into the ring. Blocks follow (l, s, b) order;
+// within a projection CTA b's block starts after the rows of the CTAs before it.
+__host__ __device__ inline void stage_shape(int s, int D, int FF, int &nout, int &K, int &mult) {
+    const int outs[NSTAGE] = { FF, D, 3 * D, D, D, D, FF, D }, Ks[NSTAGE] = { D, FF, D, D, D, D, D, FF }, m[NSTAGE] = { 1, 1, 1, 1, 2, 1, 1, 1 };
+    nout = outs[s];
+    K = Ks[s];
+    mult = m[s];
+}
+__host__ __device__ inline long long stage_image_bytes(int s, int D, int FF) {
+    int nout, K, mult;
+    stage_shape(s, D, FF, nout, K, mult);
+    const int krw = K <= KRW ? K : KRW;
+    return (long long)(krw * 2 + 16) * mult * nout * (K / krw);
+}
+__host__ __device__ inline long long layer_image_bytes(int D, int FF) {
+    long long b = 0;
+    for (int s = 0; s < NSTAGE; ++s) b += stage_image_bytes(s, D, FF);
+    return b;
+}
+__device__ __forceinline__ long long image_offset(const NbEnc1Args &a, int l, int s, const Geo &g, int cta, int grid) {
+    long long off = (long long)l * layer_image_bytes(a.D, a.FF);
+    for (int t = 0; t < s; ++t) off += stage_image_bytes(t, a.D, a.FF);
+    const int nout = g.glu ? g.N / 2 : g.N, mult = g.glu ? 2 : 1;
+    long long rows_before = (long long)mult * g.lo;
+    if (g.K > KRW) rows_before += (long long)g.kr * nout;
+    (void)cta; (void)grid;
+    return off + rows_before * geo_pitch(g);
+}
+
+// Set-up: one CTA per (CTA of the persistent grid, projection, block) copies that CTA's rows.
+__global__ void encoder1_repack_kernel(const __grid_constant__ NbEnc1Args a, uint8_t *image) {
+    const int cta = blockIdx.x, s = blockIdx.y, l = blockIdx.z;
+    const Geo g = stage_geo(a, l, s, cta, gridDim.x);
+    const int rows = geo_rows(g), pitch = geo_pitch(g), R = g.hi - g.lo, vec = g.krw / 8;  // 16-byte pieces per row
+    uint8_t *dst = image + image_offset(a, l, s, g, cta, gridDim.x);
+    for (int e = threadIdx.x; e < rows * (vec + 1); e += blockDim.x) {
+        const int j = e / (vec + 1), v = e % (vec + 1);
+        uint4 x = make_uint4(0u, 0u, 0u, 0u);
+        if (v < vec) {
+            const int wrow = j < R ? g.lo + j : g.N / 2 + g.lo + (j - R);
+            x = *(const uint4 *)(g.W + (int64_t)wrow * g.K + (int64_t)g.kr * g.krw + v * 8);
+        }
+        *(uint4 *)(dst + (size_t)j * pitch + v * 16) = x;
+    }
+}
+
+// ---- weight ring: the CTA's weight rows of every projection, in order ---------------------------
+// Warp ISSUE_WARP requests projections `issued`, `issued` + 1, ... (below `limit`) while they fit: at
+// most NB in flight, and
+// their bytes not overlapping any entry the compute warps have not released yet (released =
+// `consumed`; entries are released in order). Called at the start and at the beginning of every
+// stage's math, which touches only shared memory: issued at a grid barrier instead, the requests
+// (one ~57 KB copy per CTA at once) delay the barrier's own few latency-critical accesses.
+__device__ void issue_ahead(const NbEnc1Args &a, Smem &S, uint8_t *ring, int &issued, int &head, int consumed, uint64_t pol, int limit) {
+    if ((threadIdx.x >> 5) != ISSUE_WARP) return;
+    const int lane = threadIdx.x & 31, RB = a.ring_bytes;
+    const long long layer_bytes = layer_image_bytes(a.D, a.FF);
+    limit = min(limit, a.layers * NSTAGE);
+    while (issued < limit && issued - consumed < NB) {
+        const int i = issued, st = i % NSTAGE;
+        const int sz = S.g_rows[st] * S.g_pitch[st];
+        const int off = head + sz > RB ? 0 : head;
+        bool clash = false;
+        for (int j = consumed; j < i && !clash; ++j) {
+            const int o = S.ring_off[j % NB], z = S.ring_size[j % NB];
+            clash = z > 0 && sz > 0 && o < off + sz && off < o + z;
+        }
+        if (clash) break;
+        __syncwarp();  // every lane has read the ring table before lane 0 updates it
+        if (lane == 0) {
+            S.ring_off[i % NB] = off;
+            S.ring_size[i % NB] = sz;
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // the bytes' earlier generic reads before the copies
+            sm100::mbar_arrive_expect_tx(&S.full[i % NB], (uint32_t)sz);
+        }
+        __syncwarp();
+        if (lane == 0 && sz > 0)
+            bulk_g2s_stream(ring + off, a.image + (long long)(i / NSTAGE) * layer_bytes + S.g_img[st], (uint32_t)sz, &S.full[i % NB], pol);
+        head = off + sz;
+        issued = i + 1;
+    }
+    if (lane == 0) S.issued = issued;
+}
+
+// ---- compute warps -----------------------------------------------------------------------------
+
+// Sums over the compute threads of two values per row (every thread gets the totals). One
+// butterfly per warp reduces all 32 values at once: at the step with lane offset o each lane keeps
+// the half of its values selected by (lane & o) and adds its partner's copy of that half, so after
+// five steps lane l holds the warp's total of value l; the eight warps' totals then meet in shared
+// memory (two buffers, alternating, so back-to-back calls need one barrier each).
+__device__ __forceinline__ void rows_sum2(float (&v)[MAXC], float (&w)[MAXC], Smem &S, int &buf) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    float x[2 * MAXC];
+#pragma unroll
+    for (int u = 0; u < MAXC; ++u) { x[2 * u] = v[u]; x[2 * u + 1] = w[u]; }
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) {
+        const bool up = (lane & o) != 0;
+#pragma unroll
+        for (int j = 0; j < o; ++j) {
+            const float send = up ? x[j] : x[j + o];
+            const float keep = up ? x[j + o] : x[j];
+            x[j] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+        }
+    }
+    S.rs[buf][warp][lane] = x[0];
+    cbar();
+    float t = 0.0f;
+#pragma unroll
+    for (int ww = 0; ww < CWARPS; ++ww) t += S.rs[buf][ww][lane];
+    buf ^= 1;
+#pragma unroll
+    for (int u = 0; u < MAXC; ++u) {
+        v[u] = __shfl_sync(0xffffffffu, t, 2 * u);
+        w[u] = __shfl_sync(0xffffffffu, t, 2 * u + 1);
     }
 }
 
 enum { P_PLAIN = 0, P_LN = 1, P_LN2 = 2, P_DWLN = 3 };
 
-// One k-chunk of the activation rows in registers: element e = threadIdx.x + u * CTHREADS is
-// row e / (kc / 4), columns 4 (e % (kc / 4)) .. +3. A chunk holds at most 8 x CTHREADS float4
-// (c <= 8 rows of 1024 columns or c <= 16 rows of 512), so all its loads go out at once.
-struct ActRegs { float4 x[8]; };
+// The stage's input rows in registers: thread t holds columns 4t .. 4t+3 of every row (t < K/4).
+struct Act { float4 x[MAXC]; };
 
-__device__ __forceinline__ void act_load(ActRegs &R, const float *X, int ldx, int c, int k0, int kc) {
-    const int sh = __ffs(kc / 4) - 1, total = c << sh;  // kc / 4 is a power of two
+// Predicated 16-byte L2 load into a register that keeps its value when the predicate is false (so
+// the loads of all rows are in flight together, with nothing waiting on any of them).
+__device__ __forceinline__ void ld_cg_pred(float4 &v, const float *p, bool pred) {
+    asm volatile(
+        "{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %5, 0;\n\t"
+        "@q ld.global.cg.v4.f32 {%0, %1, %2, %3}, [%4];\n\t}"
+        : "+f"(v.x), "+f"(v.y), "+f"(v.z), "+f"(v.w)
+        : "l"(p), "r"((int)pred));
+}
+
+__device__ __forceinline__ void gather(Act &A, const float *X, int ldx, int k0, int K, int c) {
+    const int t = threadIdx.x;
+    const bool own = 4 * t < K;
 #pragma unroll
-    for (int u = 0; u < 8; ++u) {
-        const int e = threadIdx.x + u * CTHREADS;
-        if (e < total) {
-            const int r = e >> sh, k = (e - (r << sh)) * 4;
-            R.x[u] = *(const float4 *)(X + (int64_t)r * ldx + k0 + k);
-        }
+    for (int u = 0; u < MAXC; ++u) {
+        A.x[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+        ld_cg_pred(A.x[u], X + (int64_t)u * ldx + k0 + 4 * t, own && u < c);
     }
 }
 
-// Normalise (mode) and store the chunk as bf16 hi/lo planes, rows apitch bytes apart.
-// pre: when non-null, the normalisation vectors of this thread's columns (g1, b1, g2, b2), loaded
-// together with the chunk (fused layout: thread t holds columns 4t .. 4t+3 of every row).
-__device__ __forceinline__ void act_store(const ActRegs &R, Smem &S, int mode, int c, int k0, int kc, int apitch, const float *g1, const float *b1,
-                                          const float *g2, const float *b2, const float4 (&pre)[4], bool use_pre) {
-    const int sh = __ffs(kc / 4) - 1, total = c << sh;
-    const int plane = ACT_PLANE;
+// LayerNorm statistics of each row (mean, inv = 1/sqrt(var + eps)) over K columns, from the sums of
+// x and x^2 in one reduction (the Metal kernel subtracts the mean first; the two agree to fp32
+// rounding for these activations).
+__device__ __forceinline__ void row_stats(const Act &A, Smem &S, int &buf, int K, float eps, float (&mean)[MAXC], float (&inv)[MAXC]) {
+    float s1[MAXC], s2[MAXC];
 #pragma unroll
-    for (int u = 0; u < 8; ++u) {
-        const int e = threadIdx.x + u * CTHREADS;
-        if (e < total) {
-            const int r = e >> sh, k = (e - (r << sh)) * 4;
-            float v[4] = { R.x[u].x, R.x[u].y, R.x[u].z, R.x[u].w };
-            if (mode != P_PLAIN) {
-                const float m1 = S.st[r][0], i1 = S.st[r][1];
-                const float4 ga = use_pre ? pre[0] : __ldg((const float4 *)(g1 + k0 + k)), ba = use_pre ? pre[1] : __ldg((const float4 *)(b1 + k0 + k));
-                const float gg[4] = { ga.x, ga.y, ga.z, ga.w }, bb[4] = { ba.x, ba.y, ba.z, ba.w };
-                float g2v[4] = { 0.f, 0.f, 0.f, 0.f }, b2v[4] = { 0.f, 0.f, 0.f, 0.f };
-                if (mode == P_LN2) {
-                    const float4 gc = use_pre ? pre[2] : __ldg((const float4 *)(g2 + k0 + k)), bc = use_pre ? pre[3] : __ldg((const float4 *)(b2 + k0 + k));
-                    g2v[0] = gc.x; g2v[1] = gc.y; g2v[2] = gc.z; g2v[3] = gc.w;
-                    b2v[0] = bc.x; b2v[1] = bc.y; b2v[2] = bc.z; b2v[3] = bc.w;
-                }
+    for (int u = 0; u < MAXC; ++u) {
+        const float4 x = A.x[u];
+        s1[u] = x.x + x.y + x.z + x.w;
+        s2[u] = x.x * x.x + x.y * x.y + x.z * x.z + x.w * x.w;
+    }
+    rows_sum2(s1, s2, S, buf);
+    const float invK = 1.0f / (float)K;
 #pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    float y = (v[j] - m1) * i1 * gg[j] + bb[j];
-                    if (mode == P_LN2) y = (y - S.st[r][2]) * S.st[r][3] * g2v[j] + b2v[j];
-                    else if (mode == P_DWLN) y = y * sigm(y);
-                    v[j] = y;
-                }
-            }
-            const __nv_bfloat162 h0 = __floats2bfloat162_rn(v[0], v[1]), h1 = __floats2bfloat162_rn(v[2], v[3]);
-            const __nv_bfloat162 l0 = __floats2bfloat162_rn(v[0] - __low2float(h0), v[1] - __high2float(h0));
-            const __nv_bfloat162 l1 = __floats2bfloat162_rn(v[2] - __low2float(h1), v[3] - __high2float(h1));
-            uint8_t *hp = S.act + r * apitch + k * 2, *lp = hp + plane;
+    for (int u = 0; u < MAXC; ++u) {
+        mean[u] = s1[u] * invK;
+        inv[u] = rsqrtf(fmaxf(s2[u] * invK - mean[u] * mean[u], 0.0f) + eps);
+    }
+}
+
+// Store the (normalised) rows as bf16 hi / lo planes of the activation tile.
+__device__ __forceinline__ void stage_store(const Act &A, uint8_t *act, int c, int K) {
+    const int t = threadIdx.x;
+    if (4 * t >= K) return;
+#pragma unroll
+    for (int u = 0; u < MAXC; ++u) {
+        if (u < c) {
+            const float4 v = A.x[u];
+            const __nv_bfloat162 h0 = __floats2bfloat162_rn(v.x, v.y), h1 = __floats2bfloat162_rn(v.z, v.w);
+            const __nv_bfloat162 l0 = __floats2bfloat162_rn(v.x - __low2float(h0), v.y - __high2float(h0));
+            const __nv_bfloat162 l1 = __floats2bfloat162_rn(v.z - __low2float(h1), v.w - __high2float(h1));
+            uint8_t *hp = act + u * APITCH + t * 8;
             *(uint2 *)hp = make_uint2(*(const uint32_t *)&h0, *(const uint32_t *)&h1);
-            *(uint2 *)lp = make_uint2(*(const uint32_t *)&l0, *(const uint32_t *)&l1);
+            *(uint2 *)(hp + ACT_PLANE) = make_uint2(*(const uint32_t *)&l0, *(const uint32_t *)&l1);
         }
     }
 }
 
-// Sums over the CTA of two values per row u < 8 (every compute thread gets the totals).
-__device__ __forceinline__ void rows_sum8x2(float (&v)[8], float (&w2)[8], Smem &S) {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-#pragma unroll
-    for (int u = 0; u < 8; ++u) {
-        const float t = nb::warp_sum(v[u]), t2 = nb::warp_sum(w2[u]);
-        if (lane == 0) { S.rs[warp][u] = t; S.rs[warp][8 + u] = t2; }
-    }
-    cbar();
-#pragma unroll
-    for (int u = 0; u < 8; ++u) {
-        float t = 0.0f, t2 = 0.0f;
-#pragma unroll
-        for (int w = 0; w < CWARPS; ++w) { t += S.rs[w][u]; t2 += S.rs[w][8 + u]; }
-        v[u] = t;
-        w2[u] = t2;
-    }
-    cbar();
-}
+__device__ __forceinline__ float4 ld4g(const float *p) { return __ldg((const float4 *)p); }
 
-// LayerNorm statistics straight from a chunk that holds whole rows (kc == K == 4 * CTHREADS:
-// thread t has columns 4t .. 4t+3 of every row u in x[u]), from the sums of x and x^2 in one
-// reduction: mean = S1 / D, variance = S2 / D - mean^2 (the Metal kernel subtracts the mean
-// first; the two agree to fp32 rounding for normalised activations).
-__device__ __forceinline__ void stats_regs(const ActRegs &R, Smem &S, int c, int D, float eps, bool twice, const float4 ga, const float4 ba) {
-    float s1[8], s2[8], mean[8], inv[8];
-#pragma unroll
-    for (int u = 0; u < 8; ++u) {
-        const float4 x = R.x[u];
-        s1[u] = u < c ? x.x + x.y + x.z + x.w : 0.0f;
-        s2[u] = u < c ? x.x * x.x + x.y * x.y + x.z * x.z + x.w * x.w : 0.0f;
-    }
-    rows_sum8x2(s1, s2, S);
-    const float invD = 1.0f / (float)D;
-#pragma unroll
-    for (int u = 0; u < 8; ++u) {
-        mean[u] = s1[u] * invD;
-        inv[u] = rsqrtf(fmaxf(s2[u] * invD - mean[u] * mean[u], 0.0f) + eps);
-    }
-    float m2[8], inv2[8];
-#pragma unroll
-    for (int u = 0; u < 8; ++u) m2[u] = inv2[u] = 0.0f;
-    if (twice) {
-#pragma unroll
-        for (int u = 0; u < 8; ++u) {
-            const float y0 = (R.x[u].x - mean[u]) * inv[u] * ga.x + ba.x, y1 = (R.x[u].y - mean[u]) * inv[u] * ga.y + ba.y;
-            const float y2 = (R.x[u].z - mean[u]) * inv[u] * ga.z + ba.z, y3 = (R.x[u].w - mean[u]) * inv[u] * ga.w + ba.w;
-            s1[u] = u < c ? y0 + y1 + y2 + y3 : 0.0f;
-            s2[u] = u < c ? y0 * y0 + y1 * y1 + y2 * y2 + y3 * y3 : 0.0f;
-        }
-        rows_sum8x2(s1, s2, S);
-#pragma unroll
-        for (int u = 0; u < 8; ++u) {
-            m2[u] = s1[u] * invD;
-            inv2[u] = rsqrtf(fmaxf(s2[u] * invD - m2[u] * m2[u], 0.0f) + eps);
-        }
-    }
-    if (threadIdx.x < c) {
-        const int u = threadIdx.x;
-        S.st[u][0] = mean[u]; S.st[u][1] = inv[u]; S.st[u][2] = m2[u]; S.st[u][3] = inv2[u];
-    }
-}
+// The fragments of one k-step (16 columns at kk): activation tiles (hi and lo planes) and the weight
+// rows of each granule.
+struct Frag { uint32_t b[2][4], a[2][4]; };
 
-// The staging group of a warp: act_store gives thread t the columns 4 (t % (kc / 4)) .. +3 of
-// its rows, so the 32 threads of a warp stage 128 consecutive columns, shared with the other
-// warps of its group (kc / 4 threads per row span: groups of 256 / (kc / 4) warps... 1, 2 or 4).
-// The group stages those columns for all rows and multiplies them, so it only syncs with itself.
-__device__ __forceinline__ void group_sync(int kc) {
-    const int gw = CTHREADS / (kc / 4);          // warps sharing a column range
-    if (gw <= 1) { __syncwarp(); return; }
-    const int span = (kc / 4) / 32;              // column ranges (groups)
-    const int grp = (threadIdx.x >> 5) % span;
-    sm100::named_barrier(2 + grp, gw * 32);
-}
-
-// One k-step (16 columns at kk of the staged chunk): ah / al[g][nt] += W rows of granule g times
-// the hi / lo activation rows of tile nt.
-__device__ __forceinline__ void mma_kstep(uint32_t act, uint32_t wb, int pitch, int nrows, int k0, int kk, int ng, int nnt, int apitch,
-                                          float (&ah)[2][2][4], float (&al)[2][2][4]) {
+__device__ __forceinline__ void frag_load(Frag &f, uint32_t act, uint32_t wb, int pitch, int nrows, int kk, int ng, int nnt) {
     const int lane = threadIdx.x & 31, mi = lane >> 3, rr = lane & 7;
-    uint32_t b[2][4];
 #pragma unroll
     for (int nt = 0; nt < 2; ++nt)
-        if (nt < nnt) ldsm_x4(act + (mi >> 1) * ACT_PLANE + (nt * 8 + rr) * apitch + (kk + (mi & 1) * 8) * 2, b[nt][0], b[nt][1], b[nt][2], b[nt][3]);
+        if (nt < nnt) ldsm_x4(act + (mi >> 1) * ACT_PLANE + (nt * 8 + rr) * APITCH + (kk + (mi & 1) * 8) * 2, f.b[nt][0], f.b[nt][1], f.b[nt][2], f.b[nt][3]);
 #pragma unroll
-    for (int g = 0; g < 2; ++g) {
-        if (g >= ng) break;
-        const int row = min(g * 16 + (mi & 1) * 8 + rr, nrows - 1);
-        uint32_t a0, a1, a2, a3;
-        ldsm_x4(wb + row * pitch + (k0 + kk + (mi >> 1) * 8) * 2, a0, a1, a2, a3);
-#pragma unroll
-        for (int nt = 0; nt < 2; ++nt)
-            if (nt < nnt) {
-                mma16816(ah[g][nt], a0, a1, a2, a3, b[nt][0], b[nt][1]);  // hi plane
-                mma16816(al[g][nt], a0, a1, a2, a3, b[nt][2], b[nt][3]);  // lo plane
-            }
-    }
+    for (int g = 0; g < 2; ++g)
+        if (g < ng) {
+            const int row = min(g * 16 + (mi & 1) * 8 + rr, nrows - 1);
+            ldsm_x4(wb + row * pitch + (kk + (mi >> 1) * 8) * 2, f.a[g][0], f.a[g][1], f.a[g][2], f.a[g][3]);
+        }
 }
 
-// This warp's k-steps of the staged chunk: the 8 k-steps of its group's 128 columns, split
-// between the group's warps; consecutive k-steps alternate between two accumulator sets so the
-// MMA dependency chains are half as long.
-__device__ __forceinline__ void mma_chunk(const Smem &S, const uint8_t *slot, int pitch, int nrows, int k0, int kc, int ng, int nnt, int apitch,
-                                          float (&acc_h)[2][2][4], float (&acc_l)[2][2][4], float (&acc_h2)[2][2][4], float (&acc_l2)[2][2][4]) {
-    const int warp = threadIdx.x >> 5;
-    const int span = (kc / 4) / 32, gw = CWARPS / span;  // column ranges, warps per range
-    const int grp = warp % span, member = warp / span;
-    const int per = 8 / gw;                             // k-steps of this warp: 8, 4 or 2
-    const uint32_t act = sm100::smem_u32(S.act), wb = sm100::smem_u32(slot);
-    for (int q = 0; q < per; q += 2) {
-        const int kk = (grp * 8 + member * per + q) * 16;
-        mma_kstep(act, wb, pitch, nrows, k0, kk, ng, nnt, apitch, acc_h, acc_l);
-        mma_kstep(act, wb, pitch, nrows, k0, kk + 16, ng, nnt, apitch, acc_h2, acc_l2);
-    }
-}
-
-// Warp 0 requests this CTA's weight rows of projection i (block i / 8, projection i % 8) into
-// ring slot i % NSLOT: one bulk copy per row, completion counted on full[slot]. Called once the
-// CTA's last reads of the slot (projection i - NSLOT) are behind a CTA barrier.
-__device__ __forceinline__ void issue_weights(const NbEnc1Args &a, Smem &S, uint8_t *slots, int i, int total) {
-    if ((threadIdx.x >> 5) != 0 || i >= total) return;
-    const int lane = threadIdx.x & 31, slot = i % NSLOT;
-    const uint16_t *W;
-    int N, K;
-    bool glu;
-    stage_w(a, i / NSTAGE, i % NSTAGE, W, N, K, glu);
-    int lo, hi;
-    slice(glu ? N / 2 : N, lo, hi);
-    const int R = hi - lo, nrows = glu ? 2 * R : R, pitch = K * 2 + 16;
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // earlier reads of the slot before the copy's writes
-    if (lane == 0) sm100::mbar_arrive_expect_tx(&S.full[slot], (uint32_t)(nrows * K * 2));
-    __syncwarp();
-    uint8_t *dst = slots + (size_t)slot * a.slot_bytes;
-    for (int j = lane; j < nrows; j += 32) {
-        const int wrow = j < R ? lo + j : N / 2 + lo + (j - R);
-        bulk_g2s(dst + (size_t)j * pitch, W + (int64_t)wrow * K, (uint32_t)(K * 2), &S.full[slot]);
-    }
+// acc_h / acc_l[g][nt] += weight rows of granule g times the hi / lo activation rows of tile nt.
+__device__ __forceinline__ void frag_mma(const Frag &f, int ng, int nnt, float (&ah)[2][2][4], float (&al)[2][2][4]) {
+#pragma unroll
+    for (int g = 0; g < 2; ++g)
+        if (g < ng)
+#pragma unroll
+            for (int nt = 0; nt < 2; ++nt)
+                if (nt < nnt) {
+                    mma16816(ah[g][nt], f.a[g][0], f.a[g][1], f.a[g][2], f.a[g][3], f.b[nt][0], f.b[nt][1]);  // hi plane
+                    mma16816(al[g][nt], f.a[g][0], f.a[g][1], f.a[g][2], f.a[g][3], f.b[nt][2], f.b[nt][3]);  // lo plane
+                }
 }
 
 // Relative-position attention of one (head, query row) (src/kernels.metal:293-348). Right after
 // the barrier the item requests everything it needs at once: the value rows go to shared memory
 // by bulk copy (they are needed last), the query, key and position rows to registers.
-__device__ __forceinline__ bool attention_item(const NbEnc1Args &a, Smem &S, const NbEnc1Layer &w, int hd, int r, int pos, int cache_len,
+__device__ __forceinline__ bool attention_item(const NbEnc1Args &a, Smem &S, uint8_t *act, const NbEnc1Layer &w, int hd, int r, int pos, int cache_len,
                                                unsigned &vphase) {
     const int D = a.D, c = a.c, L = cache_len + c, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int64_t ld = 3 * (int64_t)D;
@@ -362,38 +397,38 @@ __device__ __forceinline__ bool attention_item(const NbEnc1Args &a, Smem &S, con
     const float *Kb = w.kv + (int64_t)(pos - cache_len) * ld + D + off;
     const float *Vb = Kb + D;
     const float *Pb = w.ptab + (int64_t)(a.Lmax - L + c - 1 - r) * D + off;
-    float *Vs = (float *)S.act;  // [L][128]: the activation tile and reduction area are idle here
+    float *Vs = (float *)act;  // [L][128]: the activation tile is idle here
     if (warp == 0) {
+        // the value rows were written in this launch (the QKV stage): order those writes, seen
+        // through the barrier, before the bulk copies that read them
+        asm volatile("fence.proxy.async.global;" ::: "memory");
         if (lane == 0) sm100::mbar_arrive_expect_tx(&S.vbar, (uint32_t)(L * 512));
         __syncwarp();
         for (int j = lane; j < L; j += 32) bulk_g2s(Vs + j * 128, Vb + (int64_t)j * ld, 512u, &S.vbar);
     }
     // query (lane's 4 dims) and this warp's keys j = warp + 8 i (i < 9 covers L <= 72)
-    const float4 q4 = *(const float4 *)(w.kv + (int64_t)(pos + r) * ld + off + 4 * lane);
-    const float4 u4 = __ldg((const float4 *)(w.bias_u + off + 4 * lane)), v4 = __ldg((const float4 *)(w.bias_v + off + 4 * lane));
+    const float4 q4 = __ldcg((const float4 *)(w.kv + (int64_t)(pos + r) * ld + off + 4 * lane));
+    const float4 u4 = ld4g(w.bias_u + off + 4 * lane), v4 = ld4g(w.bias_v + off + 4 * lane);
     const float4 qu = make_float4(q4.x + u4.x, q4.y + u4.y, q4.z + u4.z, q4.w + u4.w);
     const float4 qv = make_float4(q4.x + v4.x, q4.y + v4.y, q4.z + v4.z, q4.w + v4.w);
+    float4 k4[9], p4[9];
 #pragma unroll
-    for (int i0 = 0; i0 < 9; i0 += 5) {  // keys in two batches of loads (register budget)
-        float4 k4[5], p4[5];
-#pragma unroll
-        for (int i = 0; i < 5; ++i) {
-            const int j = warp + CWARPS * (i0 + i);
-            if (i0 + i < 9 && j < L) {
-                k4[i] = *(const float4 *)(Kb + (int64_t)j * ld + 4 * lane);
-                p4[i] = __ldg((const float4 *)(Pb + (int64_t)j * D + 4 * lane));
-            }
+    for (int i = 0; i < 9; ++i) {
+        const int j = warp + CWARPS * i;
+        if (j < L) {
+            k4[i] = __ldcg((const float4 *)(Kb + (int64_t)j * ld + 4 * lane));
+            p4[i] = ld4g(Pb + (int64_t)j * D + 4 * lane);
         }
+    }
 #pragma unroll
-        for (int i = 0; i < 5; ++i) {
-            const int j = warp + CWARPS * (i0 + i);
-            if (i0 + i < 9 && j < L) {
-                float sc = qu.x * k4[i].x + qu.y * k4[i].y + qu.z * k4[i].z + qu.w * k4[i].w;
-                float tp = qv.x * p4[i].x + qv.y * p4[i].y + qv.z * p4[i].z + qv.w * p4[i].w;
-                sc = nb::warp_sum(sc);
-                tp = nb::warp_sum(tp);
-                if (lane == 0) S.sc[j] = (sc + tp) * a.scale;
-            }
+    for (int i = 0; i < 9; ++i) {
+        const int j = warp + CWARPS * i;
+        if (j < L) {
+            float sc = qu.x * k4[i].x + qu.y * k4[i].y + qu.z * k4[i].z + qu.w * k4[i].w;
+            float tp = qv.x * p4[i].x + qv.y * p4[i].y + qv.z * p4[i].z + qv.w * p4[i].w;
+            sc = nb::warp_sum(sc);
+            tp = nb::warp_sum(tp);
+            if (lane == 0) S.sc[j] = (sc + tp) * a.scale;
         }
     }
     cbar();
@@ -409,9 +444,9 @@ __device__ __forceinline__ bool attention_item(const NbEnc1Args &a, Smem &S, con
 #pragma unroll
         for (int t = 0; t < 3; ++t) { const int j = lane + 32 * t; if (j < L) S.sc[j] = sv[t] / sum; }
     }
-    // the value rows
     if (tid == 0 && !sm100::mbar_wait(&S.vbar, vphase & 1, WAIT_LIMIT)) {
         S.abort = 1;
+        S.vpending = 1 + (int)(vphase & 1);
         atomicExch(&a.bar[1], 1u);
         atomicCAS(a.err, 0, 4);
     }
@@ -428,244 +463,388 @@ __device__ __forceinline__ bool attention_item(const NbEnc1Args &a, Smem &S, con
     return true;
 }
 
-__global__ void __launch_bounds__(THREADS, 1) encoder1_kernel(const __grid_constant__ NbEnc1Args a) {
-    extern __shared__ __align__(1024) uint8_t smem_raw[];
-    uint8_t *slots = smem_raw;
-    Smem &S = *(Smem *)(smem_raw + NSLOT * a.slot_bytes);
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int D = a.D, c = a.c;
-    if (threadIdx.x == 0) {
-        for (int s = 0; s < NSLOT; ++s) sm100::mbar_init(&S.full[s], 1);
-        sm100::mbar_init(&S.vbar, 1);
-        S.abort = 0;
-        sm100::fence_mbar_init();
-    }
-    // activation rows past c stay zero for the whole launch (the MMAs read 8 or 16 rows)
-    for (int i = threadIdx.x; i < 2 * ACT_PLANE / 16; i += THREADS) ((uint4 *)S.act)[i] = make_uint4(0u, 0u, 0u, 0u);
-    __syncthreads();
-    const int total = a.layers * NSTAGE;
+// Grid-wide barrier of the compute threads (gridsync.cuh). Returns false when the launch is being
+// abandoned.
+// The small tensors block l reads (LayerNorm vectors, depthwise taps, position biases, the rows
+// of its position table this chunk's attention reads) brought into L2 by the issue warp one block
+// ahead, so the stages that read them find them there instead of waiting on HBM.
+__device__ void prefetch_layer(const NbEnc1Args &a, int l, int pos_rows0, int pos_rows) {
+    if (l >= a.layers || (threadIdx.x >> 5) != ISSUE_WARP) return;
+    const NbEnc1Layer &w = a.L[l];
+    const uint32_t vb = (uint32_t)a.D * 4;
+    const float *vec[14] = { w.ln_ff1_g, w.ln_ff1_b, w.ln_att_g, w.ln_att_b, w.ln_conv_g, w.ln_conv_b, w.ln_ff2_g,
+                             w.ln_ff2_b, w.ln_out_g, w.ln_out_b, w.bn_g, w.bn_b, w.bias_u, w.bias_v };
+    const int lane = threadIdx.x & 31;
+    if (lane < 14) prefetch_l2(vec[lane], vb);
+    else if (lane == 14) prefetch_l2(w.dw_w, vb * (uint32_t)a.taps);
+    else if (lane == 15) prefetch_l2(w.ptab + (int64_t)pos_rows0 * a.D, vb * (uint32_t)pos_rows);  // the rows are contiguous
+}
 
-    {
-        // ---- compute warps ----
-        unsigned epoch = 0, vphase = 0;
-        const int pos = *a.pos, cache_len = *a.cache_len;
-        for (int i = 0; i < NSLOT; ++i) issue_weights(a, S, slots, i, total);
-        int issued = min(NSLOT, total);  // projections whose weight copies were requested
-        const int nnt = (c + 7) / 8;
-        int dlo, dhi;
-        slice(D, dlo, dhi);  // this CTA's columns of every D-wide output: its slice of h
-        const int dR = dhi - dlo;
-        // the CTA's columns of the residual stream live in shared memory between stages
-        for (int e = threadIdx.x; e < dR * c; e += CTHREADS) S.hs[e / dR][e % dR] = a.h[(int64_t)(e / dR) * D + dlo + e % dR];
-        int gi = 0;  // projection index (ring position)
-        for (int l = 0; l < a.layers && !S.abort; ++l) {
-            const NbEnc1Layer &w = a.L[l];
-            const NbEnc1Layer *prev = l > 0 ? &a.L[l - 1] : nullptr;
-            for (int s = 0; s < NSTAGE; ++s, ++gi) {
-                if (s == 3) {
-                    // attention over the cache window (the QKV stage's barrier made the rows visible)
-                    const int items = a.H * c;
-                    for (int it = blockIdx.x; it < items; it += gridDim.x)
-                        if (!attention_item(a, S, w, it % a.H, it / a.H, pos, cache_len, vphase)) break;
-                    if (!grid_sync(a, S, epoch)) break;
-                }
-                const uint16_t *W;
-                int N, K;
-                bool glu;
-                stage_w(a, l, s, W, N, K, glu);
-                int lo, hi;
-                slice(glu ? N / 2 : N, lo, hi);
-                const int R = hi - lo, nrows = glu ? 2 * R : R, pitch = K * 2 + 16, ng = (nrows + 15) / 16;
-                // activation source and normalisation of this projection
-                int mode = P_PLAIN, ldx = D;
-                const float *X = a.h, *g1 = nullptr, *b1 = nullptr, *g2 = nullptr, *b2 = nullptr;
-                switch (s) {
-                case 0:
-                    if (prev) { mode = P_LN2; g1 = prev->ln_out_g; b1 = prev->ln_out_b; g2 = w.ln_ff1_g; b2 = w.ln_ff1_b; }
-                    else { mode = P_LN; g1 = w.ln_ff1_g; b1 = w.ln_ff1_b; }
-                    break;
-                case 1: case 7: X = a.ff; ldx = a.FF; break;
-                case 2: mode = P_LN; g1 = w.ln_att_g; b1 = w.ln_att_b; break;
-                case 3: X = a.att; break;
-                case 4: mode = P_LN; g1 = w.ln_conv_g; b1 = w.ln_conv_b; break;
-                case 5: mode = P_DWLN; X = a.att; g1 = w.bn_g; b1 = w.bn_b; break;  // att holds the depthwise-conv output
-                default: mode = P_LN; g1 = w.ln_ff2_g; b1 = w.ln_ff2_b; break;
-                }
-                // activation chunks: c <= 8 rows of up to 1024 columns, or 16 rows of 512
-                const int kcmax = nnt == 1 ? 2 * KC : KC, apitch = kcmax * 2 + 16;
-                const int kc = K < kcmax ? K : kcmax;
-                const bool fused = mode != P_PLAIN && kc == K && K == 4 * CTHREADS;
-                // one burst of loads: the first chunk, this thread's normalisation vectors, and what
-                // the epilogue needs (output-LN vectors of its column; depthwise taps and history)
-                ActRegs AR;
-                act_load(AR, X, ldx, c, 0, kc);
-                float4 pre[4];
-                pre[0] = pre[1] = pre[2] = pre[3] = make_float4(0.f, 0.f, 0.f, 0.f);
-                if (fused) {
-                    const int k = 4 * threadIdx.x;
-                    pre[0] = __ldg((const float4 *)(g1 + k));
-                    pre[1] = __ldg((const float4 *)(b1 + k));
-                    if (mode == P_LN2) { pre[2] = __ldg((const float4 *)(g2 + k)); pre[3] = __ldg((const float4 *)(b2 + k)); }
-                }
-                const int e0 = threadIdx.x;             // epilogue item of this thread (R * c <= CTHREADS)
-                const int en = R > 0 ? e0 % R : 0, er = R > 0 ? e0 / R : 0;
-                const bool eact = R > 0 && e0 < R * c;
-                float og = 1.0f, ob = 0.0f, dw[9], hist[8];
-                if (eact && s == 1 && prev) { og = __ldg(prev->ln_out_g + lo + en); ob = __ldg(prev->ln_out_b + lo + en); }
-                if (eact && s == 4) {
-                    const int ch = lo + en;
-#pragma unroll
-                    for (int t = 0; t < 9; ++t) dw[t] = t < a.taps ? __ldg(w.dw_w + ch * a.taps + t) : 0.0f;
-#pragma unroll
-                    for (int t = 0; t < 8; ++t) {
-                        const int row = pos - (a.taps - 1) + er + t;  // history rows precede pos
-                        hist[t] = (t < a.taps - 1 && row < pos) ? w.din[(int64_t)row * D + ch] : 0.0f;
-                    }
-                }
-                if (mode != P_PLAIN) {
-                    if (fused) stats_regs(AR, S, c, D, a.eps, mode == P_LN2, pre[0], pre[1]);
-                    else row_stats(S, X, c, D, a.eps, g1, b1, mode == P_LN2);
-                }
-                // wait for this projection's weight rows (one thread; the others at the barrier)
-                const int slot = gi % NSLOT;
-                if (threadIdx.x == 0 && !sm100::mbar_wait(&S.full[slot], (gi / NSLOT) & 1, WAIT_LIMIT)) {
-                    S.abort = 1;
-                    atomicExch(&a.bar[1], 1u);
-                    atomicCAS(a.err, 0, 3);
-                }
-                cbar();
-                if (S.abort) break;
-                const uint8_t *ws = slots + (size_t)slot * a.slot_bytes;
-                float acc[2][2][4], acl[2][2][4], acc2[2][2][4], acl2[2][2][4];
-#pragma unroll
-                for (int g = 0; g < 2; ++g)
-#pragma unroll
-                    for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-                        for (int q = 0; q < 4; ++q) acc[g][nt][q] = acl[g][nt][q] = acc2[g][nt][q] = acl2[g][nt][q] = 0.0f;
-                for (int k0 = 0; k0 < K; k0 += kc) {
-                    act_store(AR, S, mode, c, k0, kc, apitch, g1, b1, g2, b2, pre, fused);
-                    group_sync(kc);
-                    if (k0 + kc < K) act_load(AR, X, ldx, c, k0 + kc, kc);  // next chunk in flight during the MMAs
-                    if (nrows > 0) mma_chunk(S, ws, pitch, nrows, k0, kc, ng, nnt, apitch, acc, acl, acc2, acl2);
-                    group_sync(kc);
-                }
-#pragma unroll
-                for (int g = 0; g < 2; ++g)
-#pragma unroll
-                    for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-                        for (int q = 0; q < 4; ++q) acc[g][nt][q] += acl[g][nt][q] + (acc2[g][nt][q] + acl2[g][nt][q]);
-                // reduce the warps' partial sums: outv[weight row][activation row]
-#pragma unroll
-                for (int g = 0; g < 2; ++g)
-#pragma unroll
-                    for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-                        for (int q = 0; q < 4; ++q) S.red[warp][g][nt][lane * 4 + q] = acc[g][nt][q];
-                cbar();
-                // every warp is done with the slot: request the projection NSLOT ahead into it
-                issue_weights(a, S, slots, gi + NSLOT, total);
-                issued = min(gi + NSLOT + 1, total);
-                for (int e = threadIdx.x; e < 2 * 2 * 128; e += CTHREADS) {
-                    const int g = e >> 8, nt = (e >> 7) & 1, v = e & 127, ln = v >> 2, q = v & 3;
-                    float sum = 0.0f;
-#pragma unroll
-                    for (int ww = 0; ww < CWARPS; ++ww) sum += S.red[ww][g][nt][v];
-                    const int n = g * 16 + (ln >> 2) + (q >= 2 ? 8 : 0), r = nt * 8 + (ln & 3) * 2 + (q & 1);
-                    S.outv[n][r] = sum;
-                }
-                cbar();
-                // epilogue: output (column lo + e % R, row e / R); the stages that use prefetched
-                // per-item values (1 and 4) have R * c <= CTHREADS, so there e == e0
-                for (int e = threadIdx.x; R > 0 && e < R * c; e += CTHREADS) {
-                    const int n = e % R, r = e / R, col = lo + n;
-                    const float v = S.outv[n][r];
-                    switch (s) {
-                    case 0: case 6: a.ff[(int64_t)r * a.FF + col] = v * sigm(v); break;
-                    case 1: {
-                        float base = S.hs[r][n];
-                        if (prev) base = (base - S.st[r][0]) * S.st[r][1] * og + ob;
-                        const float hv = base + 0.5f * v;
-                        S.hs[r][n] = hv;
-                        a.h[(int64_t)r * D + col] = hv;
-                        break;
-                    }
-                    case 2: w.kv[(int64_t)(pos + r) * 3 * D + col] = v; break;
-                    case 3: case 5: { const float hv = S.hs[r][n] + v; S.hs[r][n] = hv; a.h[(int64_t)r * D + col] = hv; break; }
-                    case 4: {
-                        const float gv = v * sigm(S.outv[R + n][r]);
-                        w.din[(int64_t)(pos + r) * D + col] = gv;
-                        S.glu[n][r] = gv;
-                        break;
-                    }
-                    default: { const float hv = S.hs[r][n] + 0.5f * v; S.hs[r][n] = hv; a.h[(int64_t)r * D + col] = hv; break; }
-                    }
-                }
-                if (s == 4) {
-                    // causal depthwise conv of this CTA's channels (src/kernels.metal:361-380) over
-                    // rows pos - (taps - 1) .. pos + c - 1: history from registers, new rows from glu
-                    cbar();
-                    if (eact) {
-                        float x = 0.0f;
-#pragma unroll
-                        for (int t = 0; t < 9; ++t) {
-                            if (t >= a.taps) break;
-                            const int rr = er - (a.taps - 1) + t;  // row relative to pos
-                            x += dw[t] * (rr < 0 ? hist[t] : S.glu[en][rr]);
-                        }
-                        a.att[(int64_t)er * D + lo + en] = x;
-                    }
-                }
+
+__device__ bool grid_sync(const NbEnc1Args &a, Smem &S, unsigned &epoch) {
+    cbar();
+    if (threadIdx.x == 0) {
+        ++epoch;
+        if (!nb::grid_arrive_wait(a.bar, epoch * gridDim.x, a.err, 1, WAIT_LIMIT)) S.abort = 1;
+    }
+    cbar();
+    return !S.abort;
+}
+
+// Input rows of projection s of block l (hA: the block's input, hB: its residual after FF1b) and
+// how they are normalised; the normalisation vectors (up to two LayerNorms).
+__device__ __forceinline__ void stage_input(const NbEnc1Args &a, int l, int s, const float *hA, const float *hB, const float *&X, int &ldx, int &mode) {
+    ldx = a.D;
+    switch (s) {
+    case 0: X = hA; mode = l > 0 ? P_LN2 : P_LN; break;
+    case 1: case 7: X = a.ff; ldx = a.FF; mode = P_PLAIN; break;
+    case 2: case 4: case 6: X = hB; mode = P_LN; break;
+    case 3: X = a.att; mode = P_PLAIN; break;
+    default: X = a.att; mode = P_DWLN; break;  // att holds the depthwise-conv output
+    }
+}
+__device__ __forceinline__ void stage_norm(const NbEnc1Args &a, int l, int s, float4 &ga, float4 &ba, float4 &gb, float4 &bb) {
+    const NbEnc1Layer &w = a.L[l];
+    const float *g1 = nullptr, *b1 = nullptr, *g2 = nullptr, *b2 = nullptr;
+    switch (s) {
+    case 0:
+        if (l > 0) { g1 = a.L[l - 1].ln_out_g; b1 = a.L[l - 1].ln_out_b; g2 = w.ln_ff1_g; b2 = w.ln_ff1_b; }
+        else { g1 = w.ln_ff1_g; b1 = w.ln_ff1_b; }
+        break;
+    case 2: g1 = w.ln_att_g; b1 = w.ln_att_b; break;
+    case 4: g1 = w.ln_conv_g; b1 = w.ln_conv_b; break;
+    case 5: g1 = w.bn_g; b1 = w.bn_b; break;
+    case 6: g1 = w.ln_ff2_g; b1 = w.ln_ff2_b; break;
+    default: break;
+    }
+    const int k = 4 * threadIdx.x;
+    ga = make_float4(1.f, 1.f, 1.f, 1.f);
+    ba = make_float4(0.f, 0.f, 0.f, 0.f);
+    gb = ga;
+    bb = ba;
+    if (g1 && k < (s == 1 || s == 7 ? a.FF : a.D)) {
+        ga = ld4g(g1 + k);
+        ba = ld4g(b1 + k);
+        if (g2) { gb = ld4g(g2 + k); bb = ld4g(b2 + k); }
+    }
+}
+
+__device__ void compute(const NbEnc1Args &a, Smem &S, uint8_t *ring, uint8_t *act) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
+    const int D = a.D, c = a.c, nnt = (c + 7) / 8;
+    const int pos = *a.pos, cache_len = *a.cache_len;
+    unsigned epoch = 0, vphase = 0;
+    int rbuf = 0;  // row-sum buffer
+    int dlo, dhi;
+    slice(D, gridDim.x, blockIdx.x, dlo, dhi);  // this CTA's columns of the D-wide buffers it zeroes
+    float *hA = a.h, *hB = a.h2;                // a block runs hA -> hB (FF1b) -> hA (FF2b)
+    int gi = 0;                                 // projection index
+    int issued = 0, head = 0;                   // weight ring (warp ISSUE_WARP)
+    const uint64_t pol = evict_first_policy();
+    issue_ahead(a, S, ring, issued, head, 0, pol, 1 << 30);
+    float4 nga, nba, ngb, nbb;  // the next stage's normalisation vectors (this thread's columns)
+    stage_norm(a, 0, 0, nga, nba, ngb, nbb);
+    // position-table rows this chunk's attention reads: (Lmax - L) + (c - 1 - r) + j, j < L, r < c
+    const int L_att = cache_len + c, pos_rows0 = a.Lmax - L_att, pos_rows = L_att + c - 1;
+    prefetch_layer(a, 0, pos_rows0, pos_rows);
+    prefetch_layer(a, 1, pos_rows0, pos_rows);
+    for (int l = 0; l < a.layers && !S.abort; ++l) {
+        const NbEnc1Layer &w = a.L[l];
+        const NbEnc1Layer *prev = l > 0 ? &a.L[l - 1] : nullptr;
+        for (int s = 0; s < NSTAGE; ++s, ++gi) {
+            if (s == 3) {
+                // attention over the cache window (the QKV stage's barrier made the rows visible)
+                const int items = a.H * c;
+                for (int it = blockIdx.x; it < items; it += gridDim.x)
+                    if (!attention_item(a, S, act, w, it % a.H, it / a.H, pos, cache_len, vphase)) break;
                 if (!grid_sync(a, S, epoch)) break;
             }
-        }
-        // output LayerNorm of the last block, as bf16 hi/lo planes for the prompt projection
-        if (!S.abort) {
-            const NbEnc1Layer &w = a.L[a.layers - 1];
-            row_stats(S, a.h, c, D, a.eps, nullptr, nullptr, false);
+            struct { int lo, hi, kr, krw; } g = { S.g_lo[s], S.g_hi[s], S.g_kr[s], S.g_krw[s] };
+            const int R = g.hi - g.lo, nrows = S.g_rows[s], pitch = S.g_pitch[s], ng = (nrows + 15) / 16, K = g.krw;
+            // input rows and their normalisation (this thread's vectors were requested before the
+            // barrier that opened the stage)
+            int mode, ldx;
+            const float *X;
+            stage_input(a, l, s, hA, hB, X, ldx, mode);
+            const float4 ga = nga, ba = nba, gb = ngb, bb = nbb;
+            // one burst of loads: the input rows and what the epilogue needs (residual values of
+            // its outputs, depthwise taps and history)
+            Act A;
+            gather(A, X, ldx, g.kr * g.krw, K, c);
+            const bool own = 4 * tid < K;
+            // epilogue items e = tid + 256 q (q < 2): output column g.lo + e % R, row e / R
+            float base[2] = { 0.f, 0.f }, og[2] = { 1.f, 1.f }, ob[2] = { 0.f, 0.f };
+            const float *resid = (s == 1) ? hA : hB;
+#pragma unroll
+            for (int q = 0; q < 2; ++q) {
+                const int e = tid + CTHREADS * q;
+                if (R > 0 && e < R * c) {
+                    const int col = g.lo + e % R, r = e / R;
+                    if (((s == 1 || s == 7) && g.kr == 0) || s == 3 || s == 5) base[q] = __ldcg(resid + (int64_t)r * D + col);
+                    if (s == 1 && g.kr == 0 && prev) { og[q] = __ldg(prev->ln_out_g + col); ob[q] = __ldg(prev->ln_out_b + col); }
+                }
+            }
+            const int en = R > 0 ? tid % R : 0, er = R > 0 ? tid / R : 0;
+            const bool dact = s == 4 && R > 0 && tid < R * c;
+            float dw[9], hist[8];
+            if (dact) {
+                const int ch = g.lo + en;
+#pragma unroll
+                for (int t = 0; t < 9; ++t) dw[t] = t < a.taps ? __ldg(w.dw_w + ch * a.taps + t) : 0.0f;
+#pragma unroll
+                for (int t = 0; t < 8; ++t) {
+                    const int row = pos - (a.taps - 1) + er + t;  // history rows precede pos
+                    hist[t] = (t < a.taps - 1 && row < pos) ? __ldcg(w.din + (int64_t)row * D + ch) : 0.0f;
+                }
+            }
+            // the residual buffer the next FF-out stage accumulates into starts at zero
+            if (s == 0 || s == 6) {
+                float *z = s == 0 ? hB : hA;
+                for (int e = tid; e < (dhi - dlo) * c; e += CTHREADS) z[(int64_t)(e / (dhi - dlo)) * D + dlo + e % (dhi - dlo)] = 0.0f;
+            }
+            if (mode != P_PLAIN) {
+                float mean[MAXC], inv[MAXC];
+                row_stats(A, S, rbuf, K, a.eps, mean, inv);
+                if (s == 0) {
+#pragma unroll
+                    for (int u = 0; u < MAXC; ++u)
+                        if (u == tid && u < c) { S.st[u][0] = mean[u]; S.st[u][1] = inv[u]; }
+                }
+#pragma unroll
+                for (int u = 0; u < MAXC; ++u) {
+                    float4 &x = A.x[u];
+                    x.x = (x.x - mean[u]) * inv[u] * ga.x + ba.x;
+                    x.y = (x.y - mean[u]) * inv[u] * ga.y + ba.y;
+                    x.z = (x.z - mean[u]) * inv[u] * ga.z + ba.z;
+                    x.w = (x.w - mean[u]) * inv[u] * ga.w + ba.w;
+                    if (mode == P_DWLN) { x.x *= sigm(x.x); x.y *= sigm(x.y); x.z *= sigm(x.z); x.w *= sigm(x.w); }
+                    if (!own) x = make_float4(0.f, 0.f, 0.f, 0.f);
+                }
+                if (mode == P_LN2) {
+                    row_stats(A, S, rbuf, K, a.eps, mean, inv);
+#pragma unroll
+                    for (int u = 0; u < MAXC; ++u) {
+                        float4 &x = A.x[u];
+                        x.x = (x.x - mean[u]) * inv[u] * gb.x + bb.x;
+                        x.y = (x.y - mean[u]) * inv[u] * gb.y + bb.y;
+                        x.z = (x.z - mean[u]) * inv[u] * gb.z + bb.z;
+                        x.w = (x.w - mean[u]) * inv[u] * gb.w + bb.w;
+                    }
+                }
+            }
+            stage_store(A, act, c, K);
+            // this projection's weight rows: requested now if the ring had no room for them while
+            // the previous entry was held (everything before gi is released here); one thread
+            // waits, the others at the barrier
+            issue_ahead(a, S, ring, issued, head, gi, pol, gi + 1);
+            const int slot = gi % NB;
+            if (tid == 0 && !sm100::mbar_wait(&S.full[slot], (gi / NB) & 1, WAIT_LIMIT)) {
+                S.abort = 1;
+                atomicExch(&a.bar[1], 1u);
+                atomicCAS(a.err, 0, 3);
+            }
             cbar();
-            for (int e = threadIdx.x; e < dR * c; e += CTHREADS) {
-                const int n = e % dR, r = e / dR, col = dlo + n;
-                const float y = (S.hs[r][n] - S.st[r][0]) * S.st[r][1] * w.ln_out_g[col] + w.ln_out_b[col];
-                const uint16_t hb = nb::f2bf(y);
-                a.xout[(int64_t)r * D + col] = hb;
-                a.xout[(int64_t)r * D + col + a.xout_plane] = nb::f2bf(y - nb::bf2f(hb));
+            if (S.abort) break;
+            // the weight stream's next requests go out now, during this stage's shared-memory-only
+            // math, and not at the barrier, whose few latency-critical accesses would queue behind
+            // them (this entry stays held until the stage ends, so consumed = gi)
+            issue_ahead(a, S, ring, issued, head, gi, pol, 1 << 30);
+            if (s == 0) prefetch_layer(a, l + 2, pos_rows0, pos_rows);
+            float acc[2][2][4], acl[2][2][4], acc2[2][2][4], acl2[2][2][4];
+#pragma unroll
+            for (int gg = 0; gg < 2; ++gg)
+#pragma unroll
+                for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) acc[gg][nt][q] = acl[gg][nt][q] = acc2[gg][nt][q] = acl2[gg][nt][q] = 0.0f;
+            if (nrows > 0) {
+                // warp w: k-steps [w * K / 128, (w + 1) * K / 128), alternating two accumulator sets
+                const uint32_t actb = sm100::smem_u32(act), wb = sm100::smem_u32(ring + S.ring_off[slot]);
+                // k-steps of this warp: the issue warp, which spent the start of the phase on the
+                // weight requests, takes a sixteenth of them; the others share the rest. Software-
+                // pipelined: the next k-step's fragments are requested before this one's MMAs, which
+                // alternate between two accumulator sets.
+                const int T = K / 16, t7 = T / 16, base = (T - t7) / (CWARPS - 1), extra = (T - t7) % (CWARPS - 1);
+                const int per = warp == ISSUE_WARP ? t7 : base + (warp < extra ? 1 : 0);
+                const int k0 = 16 * (warp == ISSUE_WARP ? T - t7 : warp * base + min(warp, extra));
+                Frag f[2];
+                if (per > 0) frag_load(f[0], actb, wb, pitch, nrows, k0, ng, nnt);
+#pragma unroll
+                for (int q = 0; q < 10; ++q) {
+                    if (q >= per) break;
+                    if (q + 1 < per) frag_load(f[(q + 1) & 1], actb, wb, pitch, nrows, k0 + (q + 1) * 16, ng, nnt);
+                    if (q & 1) frag_mma(f[q & 1], ng, nnt, acc2, acl2);
+                    else frag_mma(f[q & 1], ng, nnt, acc, acl);
+                }
+            }
+#pragma unroll
+            for (int gg = 0; gg < 2; ++gg)
+#pragma unroll
+                for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) S.red[warp][gg][nt][lane * 4 + q] = acc[gg][nt][q] + acl[gg][nt][q] + (acc2[gg][nt][q] + acl2[gg][nt][q]);
+            cbar();
+            for (int e = tid; e < 2 * 2 * 128; e += CTHREADS) {
+                const int gg = e >> 8, nt = (e >> 7) & 1, v = e & 127, ln = v >> 2, q = v & 3;
+                float sum = 0.0f;
+#pragma unroll
+                for (int ww = 0; ww < CWARPS; ++ww) sum += S.red[ww][gg][nt][v];
+                const int n = gg * 16 + (ln >> 2) + (q >= 2 ? 8 : 0), r = nt * 8 + (ln & 3) * 2 + (q & 1);
+                S.outv[n][r] = sum;
+            }
+            cbar();
+            // epilogue
+#pragma unroll
+            for (int q = 0; q < 2; ++q) {
+                const int e = tid + CTHREADS * q;
+                if (R == 0 || e >= R * c) continue;
+                const int n = e % R, r = e / R, col = g.lo + n;
+                const float v = S.outv[n][r];
+                switch (s) {
+                case 0: case 6: a.ff[(int64_t)r * a.FF + col] = v * sigm(v); break;
+                case 1: case 7: {
+                    float add = 0.5f * v;
+                    if (g.kr == 0) {
+                        float b = base[q];
+                        if (s == 1 && prev) b = (b - S.st[r][0]) * S.st[r][1] * og[q] + ob[q];  // x = LN_out_{l-1}(h)
+                        add += b;
+                    }
+                    red_add((s == 1 ? hB : hA) + (int64_t)r * D + col, add);
+                    break;
+                }
+                case 2: w.kv[(int64_t)(pos + r) * 3 * D + col] = v; break;
+                case 3: case 5: hB[(int64_t)r * D + col] = base[q] + v; break;
+                default: {  // s == 4: GLU
+                    const float gv = v * sigm(S.outv[R + n][r]);
+                    w.din[(int64_t)(pos + r) * D + col] = gv;
+                    S.glu[n][r] = gv;
+                    break;
+                }
+                }
+            }
+            if (s == 4) {
+                // causal depthwise conv of this CTA's channels (src/kernels.metal:361-380) over rows
+                // pos - (taps - 1) .. pos + c - 1: history from registers, new rows from glu
+                cbar();
+                if (dact) {
+                    float x = 0.0f;
+#pragma unroll
+                    for (int t = 0; t < 9; ++t) {
+                        if (t >= a.taps) break;
+                        const int rr = er - (a.taps - 1) + t;  // row relative to pos
+                        x += dw[t] * (rr < 0 ? hist[t] : S.glu[en][rr]);
+                    }
+                    a.att[(int64_t)er * D + g.lo + en] = x;
+                }
+            }
+            if (s + 1 < NSTAGE) stage_norm(a, l, s + 1, nga, nba, ngb, nbb);
+            else if (l + 1 < a.layers) stage_norm(a, l + 1, 0, nga, nba, ngb, nbb);
+            if (!grid_sync(a, S, epoch)) break;
+        }
+    }
+    if (tid == 0) S.consumed = gi;
+    // output LayerNorm of the last block, as bf16 hi/lo planes for the prompt projection (one CTA:
+    // 16 KB of stores after the last barrier)
+    if (!S.abort && blockIdx.x == 0) {
+        const NbEnc1Layer &w = a.L[a.layers - 1];
+        Act A;
+        gather(A, hA, D, 0, D, c);
+        float mean[MAXC], inv[MAXC];
+        row_stats(A, S, rbuf, D, a.eps, mean, inv);
+        if (4 * tid < D) {
+            const float4 gg = ld4g(w.ln_out_g + 4 * tid), bb = ld4g(w.ln_out_b + 4 * tid);
+#pragma unroll
+            for (int u = 0; u < MAXC; ++u) {
+                if (u >= c) break;
+                const float y[4] = { (A.x[u].x - mean[u]) * inv[u] * gg.x + bb.x, (A.x[u].y - mean[u]) * inv[u] * gg.y + bb.y,
+                                     (A.x[u].z - mean[u]) * inv[u] * gg.z + bb.z, (A.x[u].w - mean[u]) * inv[u] * gg.w + bb.w };
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const int64_t idx = (int64_t)u * D + 4 * tid + j;
+                    const uint16_t hb = nb::f2bf(y[j]);
+                    a.xout[idx] = hb;
+                    a.xout[idx + a.xout_plane] = nb::f2bf(y[j] - nb::bf2f(hb));
+                }
             }
         }
-        // copies requested but not consumed (the launch was abandoned): wait for them (bounded)
-        if (threadIdx.x == 0)
-            for (int j = gi; j < issued; ++j) sm100::mbar_wait(&S.full[j % NSLOT], (j / NSLOT) & 1, WAIT_LIMIT);
     }
+}
+
+__global__ void __launch_bounds__(THREADS, 1) encoder1_kernel(const __grid_constant__ NbEnc1Args a) {
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t *ring = smem_raw;
+    uint8_t *act = smem_raw + a.ring_bytes;
+    Smem &S = *(Smem *)(act + ACT_BYTES);
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < NB; ++s) sm100::mbar_init(&S.full[s], 1);
+        sm100::mbar_init(&S.vbar, 1);
+        S.abort = 0;
+        S.consumed = S.issued = S.vpending = 0;
+        sm100::fence_mbar_init();
+    }
+    // this CTA's part of each projection type (the same in every block)
+    if (threadIdx.x < NSTAGE) {
+        const int st = threadIdx.x;
+        const Geo g = stage_geo(a, 0, st, blockIdx.x, gridDim.x);
+        S.g_lo[st] = g.lo; S.g_hi[st] = g.hi; S.g_kr[st] = g.kr; S.g_krw[st] = g.krw;
+        S.g_rows[st] = geo_rows(g); S.g_pitch[st] = geo_pitch(g);
+        S.g_img[st] = image_offset(a, 0, st, g, blockIdx.x, gridDim.x);
+    }
+    // activation rows past c stay zero for the whole launch (the MMAs read 8 or 16 rows)
+    for (int i = threadIdx.x; i < ACT_BYTES / 16; i += THREADS) ((uint4 *)act)[i] = make_uint4(0u, 0u, 0u, 0u);
     __syncthreads();
+    compute(a, S, ring, act);
+    __syncthreads();
+    // copies requested but never taken (an abandoned launch): wait for them (bounded) before the
+    // CTA's shared memory goes away. At most NB entries are in flight, each in its own slot.
+    if (threadIdx.x == 0 && S.abort) {
+        for (int j = S.consumed; j < S.issued; ++j) sm100::mbar_wait(&S.full[j % NB], (j / NB) & 1, WAIT_LIMIT / 8);
+        if (S.vpending) sm100::mbar_wait(&S.vbar, (uint32_t)(S.vpending - 1), WAIT_LIMIT / 8);
+    }
 }
 
 }  // namespace
 
-extern "C" size_t nb_encoder1_smem(int slot_bytes) { return (size_t)NSLOT * slot_bytes + sizeof(Smem); }
-
-// Largest weight slice (rows x padded row bytes) any CTA loads for a model of width D / FF on a
-// grid of `grid` CTAs.
-extern "C" int nb_encoder1_slot_bytes(int D, int FF, int grid) {
-    const int outs[NSTAGE] = { FF, D, 3 * D, D, D, D, FF, D }, Ks[NSTAGE] = { D, FF, D, D, D, D, D, FF }, rows_per[NSTAGE] = { 1, 1, 1, 1, 2, 1, 1, 1 };
-    int best = 0;
+// Bytes of the weight ring for a model of width D / FF on `grid` CTAs with `smem_optin` bytes of
+// shared memory per CTA; 0 when the ring could not hold two of the largest entries.
+extern "C" int nb_encoder1_ring_bytes(int D, int FF, int grid, size_t smem_optin) {
+    int biggest = 0;
+    const int outs[NSTAGE] = { FF, D, 3 * D, D, D, D, FF, D }, Ks[NSTAGE] = { D, FF, D, D, D, D, D, FF }, mult[NSTAGE] = { 1, 1, 1, 1, 2, 1, 1, 1 };
     for (int s = 0; s < NSTAGE; ++s) {
-        const int R = (outs[s] + grid - 1) / grid;
-        const int b = R * rows_per[s] * (Ks[s] * 2 + 16);
-        if (b > best) best = b;
+        const int krw = Ks[s] <= KRW ? Ks[s] : KRW, ranges = Ks[s] / krw, groups = grid / ranges;
+        if (groups < 1) return 0;
+        const int R = (outs[s] + groups - 1) / groups;
+        if (mult[s] * R > MAXR) return 0;
+        const int b = mult[s] * R * (krw * 2 + 16);
+        if (b > biggest) biggest = b;
     }
-    return (best + 127) & ~127;
+    const long long avail = (long long)smem_optin - ACT_BYTES - (long long)sizeof(Smem) - 1024;
+    const long long ring = avail / 128 * 128;
+    return ring >= 2LL * biggest ? (int)ring : 0;
+}
+
+extern "C" size_t nb_encoder1_smem(int ring_bytes) { return (size_t)ring_bytes + ACT_BYTES + sizeof(Smem); }
+
+extern "C" size_t nb_encoder1_image_bytes(int D, int FF, int layers) { return (size_t)layers * (size_t)layer_image_bytes(D, FF); }
+
+// Builds the weight image for a persistent grid of `grid` CTAs (args: the layer table and widths).
+extern "C" int nb_encoder1_repack(const NbEnc1Args *args, int grid, uint8_t *image, void *stream) {
+    if (!image || ((uintptr_t)image & 15)) return nb_set_error("persistent encoder: weight image missing or misaligned");
+    encoder1_repack_kernel<<<dim3(grid, NSTAGE, args->layers), 256, 0, (cudaStream_t)stream>>>(*args, image);
+    return nb_check_launch("encoder1_repack_kernel");
 }
 
 extern "C" int nb_encoder1(const NbEnc1Args *args, int grid, void *stream) {
     const NbEnc1Args &a = *args;
     if (a.c < 1 || a.c > MAXC) return nb_set_error("persistent encoder: %d rows per chunk (1..%d)", a.c, MAXC);
-    if (a.D % 128 || a.D > 1024 || a.FF % 16 || (a.D < KC ? KC % a.D : a.D % KC) || (a.FF < KC ? KC % a.FF : a.FF % KC))
+    if (a.D % 128 || a.D > KRW || a.FF % 128 || (a.FF > KRW && a.FF % KRW))
         return nb_set_error("persistent encoder: unsupported widths D=%d FF=%d", a.D, a.FF);
     if (a.H * 128 != a.D) return nb_set_error("persistent encoder: heads of 128 expected");
     if (a.Lmax > MAXL) return nb_set_error("persistent encoder: attention window %d above %d rows", a.Lmax, MAXL);
     if (a.taps < 1 || a.taps > 9) return nb_set_error("persistent encoder: depthwise kernel of %d taps (1..9)", a.taps);
-    const size_t smem = nb_encoder1_smem(a.slot_bytes);
+    if (!a.h2 || a.h2 == a.h) return nb_set_error("persistent encoder: needs two residual buffers");
+    if (!a.image) return nb_set_error("persistent encoder: no weight image");
+    const size_t smem = nb_encoder1_smem(a.ring_bytes);
     if (nb_smem_attr((const void *)encoder1_kernel, smem)) return nb_set_error("persistent encoder: %s", nemo_gpu_last_error());
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
