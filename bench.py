@@ -314,11 +314,12 @@ def single_stream(nb, torch, peaks, seconds=4.0, latency=560, passes=6):
             "peak_source": "MEASURED_PEAKS.json hbm_gbs" if "hbm_gbs" in peaks else "fallback 6.65 TB/s"}
 
 
-# Blank-joint-bias offset of the config #5 model: about 35 % of stream-frames emit a token on the
-# config #5 audio (per-stream seeds, pauses, random languages). Found by `python bench.py
-# --calibrate` (bisection on 64 streams x 1120 ms x 10 chunks): 0.38671875 -> 37.3 % of the
-# stream-frames emit; the next representable offset up (0.388671875) gives 30.2 %.
-CONFIG5_BLANK_BIAS = 0.38671875
+# Blank-joint-bias offset of the config #5 model: about 35 % of stream-frames emit a token over the
+# chunks config #5 times (its 1024 streams, chunks 3..7: per-stream seeds, pauses, random
+# languages). Found by `python bench.py --calibrate` (bisection down to adjacent bf16-representable
+# offsets): 0.390625 -> 38.4 % of the stream-frames emit; the next offset up (0.3916015625) gives
+# 30.1 %. The rate is a steep function of the offset with these random-init weights.
+CONFIG5_BLANK_BIAS = 0.390625
 
 
 def emission(nb, batch, before=None):
@@ -342,19 +343,23 @@ def config5_inputs(nb, B, seconds, rank):
     return audio, [keys[i] for i in rng.integers(0, 128, size=B)]
 
 
-def calibrate(nb, B=64, latency=1120, chunks=10, target=0.35):
-    """Bisection on the joint blank bias for `target` emitting stream-frames on config #5 audio."""
+def calibrate(nb, B=1024, latency=1120, warm=2, chunks=5, target=0.35):
+    """Bisection on the joint blank bias for `target` emitting stream-frames, counted over the chunks
+    config #5 times (chunks warm + 1 .. warm + chunks of its 1024 streams)."""
     blk = latency * 16
-    audio, langs = config5_inputs(nb, B, (chunks + 1) * latency / 1000, 0)
+    audio, langs = config5_inputs(nb, B, (warm + chunks + 1) * latency / 1000, 0)
 
     def rate(bias):
         b = nb.Batch(B, spec=nb.synth_default(blank_bias=bias), languages=langs, latency_ms=latency)
-        for i in range(chunks):
+        for i in range(warm):
+            b.feed(audio[:, i * blk:(i + 1) * blk])
+        c0 = b.decode_counts()
+        for i in range(warm, warm + chunks):
             b.feed(audio[:, i * blk:(i + 1) * blk])
         c = b.decode_counts()
         b.close()
-        r = c["emitting_frames"] / c["frames"]
-        print(json.dumps({"blank_bias": bias, "emitting_frames": r, "tokens_per_frame": c["decisions"] and (c["decisions"] - c["frames"]) / c["frames"]}), flush=True)
+        r = (c["emitting_frames"] - c0["emitting_frames"]) / (c["frames"] - c0["frames"])
+        print(json.dumps({"blank_bias": bias, "emitting_frames": r}), flush=True)
         return r
     # the offset lands in a bf16 bias (steps of ~0.002 near 0.4) and the rate jumps between steps:
     # bisect down to adjacent representable offsets, then keep the one nearer the target
@@ -373,8 +378,8 @@ def calibrate(nb, B=64, latency=1120, chunks=10, target=0.35):
         if hi - lo < 1e-3:
             break
     bias = min((lo, hi), key=lambda x: abs(rates[x] - target))
-    print(json.dumps({"calibrated_blank_bias": bias, "emitting_frames": rates[bias], "streams": B, "latency_ms": latency, "chunks": chunks,
-                      "neighbours": {str(lo): rates[lo], str(hi): rates[hi]}}), flush=True)
+    print(json.dumps({"calibrated_blank_bias": bias, "emitting_frames": rates[bias], "streams": B, "latency_ms": latency,
+                      "counted_chunks": [warm + 1, warm + chunks], "neighbours": {str(lo): rates[lo], str(hi): rates[hi]}}), flush=True)
 
 
 def config5(nb, torch, a, rank, world, dist, barrier):
