@@ -74,6 +74,7 @@ def parse():
     ap.add_argument("--resample-only", type=int, default=0, metavar="RATE",
                     help="time only the GPU resampler: one chunk of every stream arriving at RATE Hz (small device footprint, for ncu captures)")
     ap.add_argument("--no-config5", action="store_true", help="skip the nested BASELINE config #5 measurement")
+    ap.add_argument("--single-only", action="store_true", help="BASELINE config #1 only: one stream, 560 ms chunks, 4.0 s (small device footprint, for ncu captures)")
     ap.add_argument("--config5-streams", type=int, default=1024)
     ap.add_argument("--config5-steps", type=int, default=5)
     ap.add_argument("--sweep", action="store_true", help="BASELINE config #2 only: the GEMM sweep, one JSON line per case")
@@ -601,6 +602,11 @@ def main():
         import torch
         import nemoasr_b200 as nb
         sweep(nb, torch, peaks)
+        return
+    if a.single_only:
+        import torch
+        import nemoasr_b200 as nb
+        print(json.dumps(single_stream(nb, torch, peaks)))
         return
     if a.calibrate:
         import torch  # noqa: F401

@@ -5,9 +5,12 @@
 // The position term only depends on c - 1 - i + j, so G[i][r] = (q_i + v) . P[r0 + r] is
 // computed once per position row r (L + c - 1 rows) and read back diagonally.
 //
-// One CTA (8 warps) per (head, stream). The stream's K and V rows of the head (the HBM traffic
-// of the kernel) are copied into shared memory by the bulk copy engine as the CTA starts, K and
-// V on separate barriers, while the queries are read directly and the position scores formed. The three products (content and position scores, probabilities times V) run on the
+// One CTA (8 warps) per (head, stream). The stream's V rows of the head (half of the HBM traffic
+// of the kernel) are requested as the CTA starts, 16-byte loads spread over all threads, and land
+// in shared memory once the position scores are formed; the K rows are read straight into the
+// score tiles' fragments (each 32-byte sector read whole, by one thread group). Issuing one bulk
+// copy per 512-byte row instead cost more than the transfer itself. The three products (content
+// and position scores, probabilities times V) run on the
 // tensor cores as mma.sync m16n8k16 tiles (the chunk's <= 16 query rows are the M side) with
 // both operands split into bf16 hi + lo parts and three products per tile (hi.hi, hi.lo, lo.hi;
 // the dropped lo.lo term is below 2^-16 of each product), accumulating in fp32. The softmax stays
@@ -22,30 +25,11 @@ constexpr int DH = 128;
 constexpr int THREADS = 256;
 constexpr int MAXC = 16;   // rows per chunk (the MMA's 16 rows)
 constexpr int MAXL = 96;   // keys in the window
-// Shared-memory row pitches (floats), chosen for conflict-free fragment loads: rows read as
-// float2 pairs by 8 row groups (K, queries) want a pitch of 8 mod 32 banks; V, read as scalars
-// down 4 row pairs, wants 4 mod 32.
-constexpr int KP = DH + 8;
+// Shared-memory row pitch of V (floats), read as scalars down 4 row pairs: 4 mod 32 banks keeps the
+// fragment loads conflict-free.
 constexpr int VP = DH + 4;
 
-__device__ int g_att_error;  // nonzero once a CTA gave up waiting for its rows (bounded wait)
-
-// One row (bytes a multiple of 16, both addresses 16-byte aligned) global -> shared by the bulk
-// copy engine, completion counted on `bar`.
-__device__ __forceinline__ void bulk_row(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
-    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(sm100::smem_u32(dst)), "l"(src),
-                 "r"(bytes), "r"(sm100::smem_u32(bar))
-                 : "memory");
-}
-
-// Wait for a group of rows; a wait that runs out records the error and lets the CTA finish (its
-// results are then not used: the host checks the flag after the step).
-__device__ __forceinline__ void wait_rows(uint64_t *bar, bool &bad) {
-    if (!sm100::mbar_wait(bar, 0)) {
-        atomicExch(&g_att_error, 1);
-        bad = true;
-    }
-}
+__device__ int g_att_error;  // nonzero once a CTA gave up waiting (no wait left in this kernel: stays 0)
 
 // hi = bf16(x), lo = bf16(x - hi) of a pair, packed two per register (first element low)
 __device__ __forceinline__ void split2(float x0, float x1, uint32_t &hi, uint32_t &lo) {
@@ -128,12 +112,13 @@ __device__ __forceinline__ void score_tile(const uint16_t *qhi, const uint16_t *
     for (int e = 0; e < 4; ++e) d[e] = d0[e] + d1[e];
 }
 
-// Shared-memory floats of one CTA: K rows [Lmax][KP], V rows [Lmax][VP], content scores /
-// probabilities [16][Lmax], position scores [16][Lmax + 16], then the query operands (q + v) and
-// (q + u) as bf16 hi / lo planes [16][QP] each.
+// Shared-memory floats of one CTA: V rows [Lmax][VP], content scores / probabilities [16][Lmax],
+// position scores [16][Lmax + 16], then the query operands (q + v) and (q + u) as bf16 hi / lo
+// planes [16][QP] each.
 __host__ __device__ __forceinline__ int smem_floats(int Lmax) {
-    return Lmax * KP + Lmax * VP + MAXC * Lmax + MAXC * (Lmax + MAXC) + 4 * MAXC * QP / 2;
+    return Lmax * VP + MAXC * Lmax + MAXC * (Lmax + MAXC) + 4 * MAXC * QP / 2;
 }
+constexpr int VLOADS = (MAXL * DH / 4 + THREADS - 1) / THREADS;  // 16-byte V loads per thread
 
 __global__ void __launch_bounds__(THREADS) attention_kernel(const float *__restrict__ Q, int64_t ldq, int64_t q_sstride, const float *__restrict__ K,
                                                             const float *__restrict__ V, int64_t ldk, int64_t kv_sstride, const int *pos_p,
@@ -141,7 +126,7 @@ __global__ void __launch_bounds__(THREADS) attention_kernel(const float *__restr
                                                             const float *__restrict__ bias_v, void *O, int o_fmt, int64_t o_plane, int64_t o_sstride,
                                                             int c, int Lmax, int D, float scale) {
     extern __shared__ __align__(16) float sm[];
-    float *Ks = sm, *Vs = Ks + Lmax * KP, *sk = Vs + Lmax * VP, *gp = sk + MAXC * Lmax;
+    float *Vs = sm, *sk = Vs + Lmax * VP, *gp = sk + MAXC * Lmax;
     uint16_t *qvh = (uint16_t *)(gp + MAXC * (Lmax + MAXC)), *qvl = qvh + MAXC * QP, *quh = qvl + MAXC * QP, *qul = quh + MAXC * QP;
     const int gpl = Lmax + MAXC;  // pitch of gp
     nb::pdl_wait();
@@ -163,24 +148,14 @@ __global__ void __launch_bounds__(THREADS) attention_kernel(const float *__restr
         bu2[r] = *(const float2 *)(bias_u + off + k);
         bv2[r] = *(const float2 *)(bias_v + off + k);
     }
-    // the window's K rows and its V rows into shared memory by the bulk copy engine, one 512-byte
-    // row per copy, each group on its own barrier
-    __shared__ uint64_t bars[2];
-    if (tid == 0) {
-        for (int i = 0; i < 2; ++i) sm100::mbar_init(&bars[i], 1);
-        sm100::fence_mbar_init();
+    // the window's V rows: every load in flight now, stored to shared memory after the position
+    // scores (element e: row e / 32, columns 4 (e % 32) .. +3)
+    float4 vr[VLOADS];
+#pragma unroll
+    for (int u = 0; u < VLOADS; ++u) {
+        const int e = tid + u * THREADS, r = e >> 5;
+        vr[u] = r < L ? __ldg((const float4 *)(Vb + (int64_t)r * ldk) + (e & 31)) : make_float4(0.f, 0.f, 0.f, 0.f);
     }
-    __syncthreads();
-    if (warp == 0) {
-        if (lane == 0) {
-            sm100::mbar_arrive_expect_tx(&bars[0], (uint32_t)L * DH * 4);
-            sm100::mbar_arrive_expect_tx(&bars[1], (uint32_t)L * DH * 4);
-        }
-        __syncwarp();
-        for (int r = lane; r < L; r += 32) bulk_row(Ks + r * KP, Kb + (int64_t)r * ldk, DH * 4, &bars[0]);
-        for (int r = lane; r < L; r += 32) bulk_row(Vs + r * VP, Vb + (int64_t)r * ldk, DH * 4, &bars[1]);
-    }
-    bool bad = false;
 #pragma unroll
     for (int r = 0; r < 4; ++r) {
         const int e = tid + r * THREADS, i = e >> 6, k = 2 * (e & 63);
@@ -204,12 +179,15 @@ __global__ void __launch_bounds__(THREADS) attention_kernel(const float *__restr
         if (g < c) { if (col < NP) gp[g * gpl + col] = d[0]; if (col + 1 < NP) gp[g * gpl + col + 1] = d[1]; }
         if (g + 8 < c) { if (col < NP) gp[(g + 8) * gpl + col] = d[2]; if (col + 1 < NP) gp[(g + 8) * gpl + col + 1] = d[3]; }
     }
-    wait_rows(&bars[0], bad);
-    __syncthreads();
-    // content scores (q + u) . k from the K rows in shared memory
+#pragma unroll
+    for (int u = 0; u < VLOADS; ++u) {
+        const int e = tid + u * THREADS, r = e >> 5;
+        if (r < L) *(float4 *)(Vs + r * VP + 4 * (e & 31)) = vr[u];
+    }
+    // content scores (q + u) . k from the K rows, read straight from global memory
     for (int nt = warp; nt < ntK; nt += THREADS / 32) {
         float d[4];
-        score_tile(quh, qul, Ks, KP, nt * 8, L, lane, d);
+        score_tile(quh, qul, Kb, ldk, nt * 8, L, lane, d);
         const int col = nt * 8 + 2 * t;
         if (g < c) { if (col < L) sk[g * Lmax + col] = d[0]; if (col + 1 < L) sk[g * Lmax + col + 1] = d[1]; }
         if (g + 8 < c) { if (col < L) sk[(g + 8) * Lmax + col] = d[2]; if (col + 1 < L) sk[(g + 8) * Lmax + col + 1] = d[3]; }
@@ -243,7 +221,6 @@ __global__ void __launch_bounds__(THREADS) attention_kernel(const float *__restr
             if (j < Lmax) sk[i * Lmax + j] = j < L ? sv[q] / sum : 0.0f;
         }
     }
-    wait_rows(&bars[1], bad);
     __syncthreads();
     // o = p . V: warp w owns head dims [16w, 16w + 16) (two n-tiles); k runs over the L keys
     // (probabilities beyond L are zero and V rows beyond L are not read)
@@ -297,8 +274,6 @@ __global__ void __launch_bounds__(THREADS) attention_kernel(const float *__restr
             nb::store_act(O, o_fmt, o_plane, (int64_t)s * o_sstride + (int64_t)(g + 8) * D + col + 1, o[nt][3]);
         }
     }
-    if (bad)  // copies may still be landing in this CTA's shared memory: wait (bounded) before exiting
-        for (int i = 0; i < 2; ++i) sm100::mbar_wait(&bars[i], 0);
 }
 
 }  // namespace
