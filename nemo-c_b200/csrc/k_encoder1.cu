@@ -65,14 +65,13 @@ struct Smem {
     float glu[8][MAXC];            // conv-module GLU outputs of this CTA's channels
     float sc[MAXL];                // attention scores / probabilities
     float vpart[2][128];           // attention value halves
-    uint64_t full[NB], vbar;
+    uint64_t full[NB];
     int ring_off[NB];              // byte offset of projection i's rows in the ring (slot i % NB)
     int ring_size[NB];             // and its bytes
     int g_lo[NSTAGE], g_hi[NSTAGE], g_kr[NSTAGE], g_krw[NSTAGE], g_rows[NSTAGE], g_pitch[NSTAGE];
     long long g_img[NSTAGE];       // byte offset of this CTA's block of projection s in block 0 of the image
     int consumed;                  // projections taken by the compute warps (set when they stop)
     int issued;                    // projections requested so far
-    int vpending;                  // 1 + phase of a value-row copy the compute warps gave up on
     int abort;
 };
 static_assert(ACT_BYTES >= MAXL * 512, "attention value rows do not fit the activation area");
@@ -387,10 +386,10 @@ __device__ __forceinline__ void frag_mma(const Frag &f, int ng, int nnt, float (
 }
 
 // Relative-position attention of one (head, query row) (src/kernels.metal:293-348). Right after
-// the barrier the item requests everything it needs at once: the value rows go to shared memory
-// by bulk copy (they are needed last), the query, key and position rows to registers.
-__device__ __forceinline__ bool attention_item(const NbEnc1Args &a, Smem &S, uint8_t *act, const NbEnc1Layer &w, int hd, int r, int pos, int cache_len,
-                                               unsigned &vphase) {
+// the barrier the item requests everything it needs at once: the query, key and position rows to
+// registers, the value rows through registers into shared memory (16-byte L2 loads spread over all
+// threads; they are needed last).
+__device__ __forceinline__ void attention_item(const NbEnc1Args &a, Smem &S, uint8_t *act, const NbEnc1Layer &w, int hd, int r, int pos, int cache_len) {
     const int D = a.D, c = a.c, L = cache_len + c, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int64_t ld = 3 * (int64_t)D;
     const int off = hd * 128;
@@ -398,19 +397,9 @@ __device__ __forceinline__ bool attention_item(const NbEnc1Args &a, Smem &S, uin
     const float *Vb = Kb + D;
     const float *Pb = w.ptab + (int64_t)(a.Lmax - L + c - 1 - r) * D + off;
     float *Vs = (float *)act;  // [L][128]: the activation tile is idle here
-    if (warp == 0) {
-        // the value rows were written in this launch (the QKV stage): order those writes, seen
-        // through the barrier, before the bulk copies that read them
-        asm volatile("fence.proxy.async.global;" ::: "memory");
-        if (lane == 0) sm100::mbar_arrive_expect_tx(&S.vbar, (uint32_t)(L * 512));
-        __syncwarp();
-        for (int j = lane; j < L; j += 32) bulk_g2s(Vs + j * 128, Vb + (int64_t)j * ld, 512u, &S.vbar);
-    }
     // query (lane's 4 dims) and this warp's keys j = warp + 8 i (i < 9 covers L <= 72)
     const float4 q4 = __ldcg((const float4 *)(w.kv + (int64_t)(pos + r) * ld + off + 4 * lane));
     const float4 u4 = ld4g(w.bias_u + off + 4 * lane), v4 = ld4g(w.bias_v + off + 4 * lane);
-    const float4 qu = make_float4(q4.x + u4.x, q4.y + u4.y, q4.z + u4.z, q4.w + u4.w);
-    const float4 qv = make_float4(q4.x + v4.x, q4.y + v4.y, q4.z + v4.z, q4.w + v4.w);
     float4 k4[9], p4[9];
 #pragma unroll
     for (int i = 0; i < 9; ++i) {
@@ -420,6 +409,10 @@ __device__ __forceinline__ bool attention_item(const NbEnc1Args &a, Smem &S, uin
             p4[i] = ld4g(Pb + (int64_t)j * D + 4 * lane);
         }
     }
+    // value rows: element e = row e / 32, columns 4 (e % 32) .. +3
+    for (int e = tid; e < L * 32; e += CTHREADS) ((float4 *)Vs)[e] = __ldcg((const float4 *)(Vb + (int64_t)(e >> 5) * ld) + (e & 31));
+    const float4 qu = make_float4(q4.x + u4.x, q4.y + u4.y, q4.z + u4.z, q4.w + u4.w);
+    const float4 qv = make_float4(q4.x + v4.x, q4.y + v4.y, q4.z + v4.z, q4.w + v4.w);
 #pragma unroll
     for (int i = 0; i < 9; ++i) {
         const int j = warp + CWARPS * i;
@@ -444,15 +437,7 @@ __device__ __forceinline__ bool attention_item(const NbEnc1Args &a, Smem &S, uin
 #pragma unroll
         for (int t = 0; t < 3; ++t) { const int j = lane + 32 * t; if (j < L) S.sc[j] = sv[t] / sum; }
     }
-    if (tid == 0 && !sm100::mbar_wait(&S.vbar, vphase & 1, WAIT_LIMIT)) {
-        S.abort = 1;
-        S.vpending = 1 + (int)(vphase & 1);
-        atomicExch(&a.bar[1], 1u);
-        atomicCAS(a.err, 0, 4);
-    }
-    ++vphase;
     cbar();
-    if (S.abort) return false;
     const int d = tid & 127, half = tid >> 7;
     float acc = 0.0f;
     for (int j = half; j < L; j += 2) acc += S.sc[j] * Vs[j * 128 + d];
@@ -460,7 +445,6 @@ __device__ __forceinline__ bool attention_item(const NbEnc1Args &a, Smem &S, uin
     cbar();
     if (tid < 128) a.att[(int64_t)r * D + off + tid] = S.vpart[0][tid] + S.vpart[1][tid];
     cbar();  // the value rows are read before the area is reused
-    return true;
 }
 
 // Grid-wide barrier of the compute threads (gridsync.cuh). Returns false when the launch is being
@@ -533,7 +517,7 @@ __device__ void compute(const NbEnc1Args &a, Smem &S, uint8_t *ring, uint8_t *ac
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
     const int D = a.D, c = a.c, nnt = (c + 7) / 8;
     const int pos = *a.pos, cache_len = *a.cache_len;
-    unsigned epoch = 0, vphase = 0;
+    unsigned epoch = 0;
     int rbuf = 0;  // row-sum buffer
     int dlo, dhi;
     slice(D, gridDim.x, blockIdx.x, dlo, dhi);  // this CTA's columns of the D-wide buffers it zeroes
@@ -555,8 +539,7 @@ __device__ void compute(const NbEnc1Args &a, Smem &S, uint8_t *ring, uint8_t *ac
             if (s == 3) {
                 // attention over the cache window (the QKV stage's barrier made the rows visible)
                 const int items = a.H * c;
-                for (int it = blockIdx.x; it < items; it += gridDim.x)
-                    if (!attention_item(a, S, act, w, it % a.H, it / a.H, pos, cache_len, vphase)) break;
+                for (int it = blockIdx.x; it < items; it += gridDim.x) attention_item(a, S, act, w, it % a.H, it / a.H, pos, cache_len);
                 if (!grid_sync(a, S, epoch)) break;
             }
             struct { int lo, hi, kr, krw; } g = { S.g_lo[s], S.g_hi[s], S.g_kr[s], S.g_krw[s] };
@@ -777,9 +760,8 @@ __global__ void __launch_bounds__(THREADS, 1) encoder1_kernel(const __grid_const
     Smem &S = *(Smem *)(act + ACT_BYTES);
     if (threadIdx.x == 0) {
         for (int s = 0; s < NB; ++s) sm100::mbar_init(&S.full[s], 1);
-        sm100::mbar_init(&S.vbar, 1);
         S.abort = 0;
-        S.consumed = S.issued = S.vpending = 0;
+        S.consumed = S.issued = 0;
         sm100::fence_mbar_init();
     }
     // this CTA's part of each projection type (the same in every block)
@@ -799,7 +781,6 @@ __global__ void __launch_bounds__(THREADS, 1) encoder1_kernel(const __grid_const
     // CTA's shared memory goes away. At most NB entries are in flight, each in its own slot.
     if (threadIdx.x == 0 && S.abort) {
         for (int j = S.consumed; j < S.issued; ++j) sm100::mbar_wait(&S.full[j % NB], (j / NB) & 1, WAIT_LIMIT / 8);
-        if (S.vpending) sm100::mbar_wait(&S.vbar, (uint32_t)(S.vpending - 1), WAIT_LIMIT / 8);
     }
 }
 
