@@ -67,7 +67,7 @@ struct nb_engine {
     /* one stream: the conformer blocks run as one persistent kernel (NEMO_PERSISTENT=0 disables) */
     int use_enc1, enc1_grid, enc1_slot;
     NbEnc1Layer *enc1_layers;  /* host copy, passed by value at each launch */
-    uint8_t *enc1_image;       /* the weights laid out per CTA of the persistent grid */
+    uint8_t *enc1_image;       /* the model's weights laid out per CTA of the persistent grid (owned by the model) */
     NbEnc1Args enc1_args;      /* launch arguments (large: the layer table travels by value) */
     /* one stream: the greedy loop of a chunk runs as one persistent kernel (NEMO_PERSISTENT=0 disables) */
     int use_dec1, dec1_grid;
@@ -144,23 +144,30 @@ static int enc1_setup(nb_engine_t *e, char *err, size_t errlen) {
     }
     e->enc1_layers = L;
     /* the weights re-laid out in the order the persistent grid reads them (one bulk copy per CTA
-       and projection); without room for the copy the blocks run kernel by kernel */
-    const size_t img = nb_encoder1_image_bytes(D, FF, g->n_layers);
-    if (cudaMalloc((void **)&e->enc1_image, img) != cudaSuccess) {
-        cudaGetLastError();
-        e->enc1_image = NULL;
-        return 0;
-    }
-    {
+       and projection), built once per model; without room for the copy the blocks run kernel by
+       kernel */
+    nb_model_t *mm = e->m;
+    if (!mm->enc1_image || mm->enc1_grid != sms) {
+        if (mm->enc1_image) cudaFree(mm->enc1_image);
+        mm->enc1_image = NULL;
+        mm->enc1_grid = 0;
+        const size_t img = nb_encoder1_image_bytes(D, FF, g->n_layers);
+        if (cudaMalloc((void **)&mm->enc1_image, img) != cudaSuccess) {
+            cudaGetLastError();
+            mm->enc1_image = NULL;
+            return 0;
+        }
         NbEnc1Args *q = &e->enc1_args;
         memset(q, 0, sizeof *q);
         memcpy(q->L, L, (size_t)g->n_layers * sizeof *L);
         q->layers = g->n_layers; q->D = D; q->FF = FF;
-        if (nb_encoder1_repack(q, sms, e->enc1_image, e->st) || cudaStreamSynchronize(e->st) != cudaSuccess) {
+        if (nb_encoder1_repack(q, sms, mm->enc1_image, e->st) || cudaStreamSynchronize(e->st) != cudaSuccess) {
             snprintf(err, errlen, "persistent encoder set-up: %s", nemo_gpu_last_error());
             return -1;
         }
+        mm->enc1_grid = sms;
     }
+    e->enc1_image = mm->enc1_image;
     const int rc = cudaMalloc((void **)&e->d_enc1_bar, 2 * sizeof(unsigned)) != cudaSuccess || cudaMalloc((void **)&e->d_enc1_err, sizeof(int)) != cudaSuccess ||
                    cudaMemset(e->d_enc1_err, 0, sizeof(int)) != cudaSuccess;
     if (rc) { snprintf(err, errlen, "persistent encoder set-up: %s", cudaGetErrorString(cudaGetLastError())); return -1; }
@@ -406,7 +413,6 @@ void nb_engine_destroy(nb_engine_t *e) {
     if (e->d_dec1_i) cudaFree(e->d_dec1_i);
     if (e->d_dec1_bar) cudaFree(e->d_dec1_bar);
     if (e->d_enc1_bar) cudaFree(e->d_enc1_bar);
-    if (e->enc1_image) cudaFree(e->enc1_image);
     if (e->d_enc1_err) cudaFree(e->d_enc1_err);
     if (e->pending) for (int s = 0; s < e->B; ++s) free(e->pending[s]);
     free(e->pending);

@@ -233,6 +233,7 @@ nb_model_t *nb_model_load(nb_source_t *src, char *err, size_t errlen) {
 void nb_model_free(nb_model_t *m) {
     if (!m) return;
     if (m->arena) cudaFree(m->arena);
+    if (m->enc1_image) cudaFree(m->enc1_image);
     free(m->L);
     free(m->prompt_b0_host);
     free(m->prompt_onehot_host);

@@ -38,6 +38,10 @@ typedef struct nb_model {
     int *lang_idx;
     int n_lang;
     double load_ms;
+    /* the encoder weights laid out for the persistent single-stream encoder on a grid of
+       enc1_grid CTAs (built by the first single-stream engine, shared by all of the model's) */
+    uint8_t *enc1_image;
+    int enc1_grid;
 } nb_model_t;
 
 nb_model_t *nb_model_load(nb_source_t *src, char *err, size_t errlen);
