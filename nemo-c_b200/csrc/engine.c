@@ -68,6 +68,7 @@ struct nb_engine {
     int use_enc1, enc1_grid, enc1_slot;
     NbEnc1Layer *enc1_layers;  /* host copy, passed by value at each launch */
     uint8_t *enc1_image;       /* the model's weights laid out per CTA of the persistent grid (owned by the model) */
+    float *enc1_fold;          /* and its LayerNorm fold constants (owned by the model) */
     NbEnc1Args enc1_args;      /* launch arguments (large: the layer table travels by value) */
     /* one stream: the greedy loop of a chunk runs as one persistent kernel (NEMO_PERSISTENT=0 disables) */
     int use_dec1, dec1_grid;
@@ -126,8 +127,8 @@ static int enc1_setup(nb_engine_t *e, char *err, size_t errlen) {
         return 0;
     /* per-CTA weight rows must fit the kernel's 32-row accumulator tiles and two of the largest
        entries its weight ring (0 otherwise) */
-    const int ring = nb_encoder1_ring_bytes(D, FF, sms, (size_t)optin);
-    if (!ring || nb_encoder1_smem(ring) > (size_t)optin) return 0;
+    const int ring = nb_encoder1_ring_bytes(D, FF, sms, (size_t)optin, e->cmax, e->Lmax);
+    if (!ring || nb_encoder1_smem(ring, e->cmax, e->Lmax) > (size_t)optin) return 0;
     NbEnc1Layer *L = calloc((size_t)g->n_layers, sizeof *L);
     const size_t kv_s = (size_t)e->cap_rows * 3 * D, din_s = (size_t)e->cap_rows * D;
     for (int l = 0; l < g->n_layers; ++l) {
@@ -149,25 +150,30 @@ static int enc1_setup(nb_engine_t *e, char *err, size_t errlen) {
     nb_model_t *mm = e->m;
     if (!mm->enc1_image || mm->enc1_grid != sms) {
         if (mm->enc1_image) cudaFree(mm->enc1_image);
+        if (mm->enc1_fold) cudaFree(mm->enc1_fold);
         mm->enc1_image = NULL;
+        mm->enc1_fold = NULL;
         mm->enc1_grid = 0;
-        const size_t img = nb_encoder1_image_bytes(D, FF, g->n_layers);
-        if (cudaMalloc((void **)&mm->enc1_image, img) != cudaSuccess) {
+        const size_t img = nb_encoder1_image_bytes(D, FF, g->n_layers), fb = nb_encoder1_fold_bytes(D, FF, g->n_layers);
+        if (cudaMalloc((void **)&mm->enc1_image, img) != cudaSuccess || cudaMalloc((void **)&mm->enc1_fold, fb) != cudaSuccess) {
             cudaGetLastError();
+            if (mm->enc1_image) cudaFree(mm->enc1_image);
             mm->enc1_image = NULL;
+            mm->enc1_fold = NULL;
             return 0;
         }
         NbEnc1Args *q = &e->enc1_args;
         memset(q, 0, sizeof *q);
         memcpy(q->L, L, (size_t)g->n_layers * sizeof *L);
         q->layers = g->n_layers; q->D = D; q->FF = FF;
-        if (nb_encoder1_repack(q, sms, mm->enc1_image, e->st) || cudaStreamSynchronize(e->st) != cudaSuccess) {
+        if (nb_encoder1_repack(q, sms, mm->enc1_image, mm->enc1_fold, e->st) || cudaStreamSynchronize(e->st) != cudaSuccess) {
             snprintf(err, errlen, "persistent encoder set-up: %s", nemo_gpu_last_error());
             return -1;
         }
         mm->enc1_grid = sms;
     }
     e->enc1_image = mm->enc1_image;
+    e->enc1_fold = mm->enc1_fold;
     const int rc = cudaMalloc((void **)&e->d_enc1_bar, 2 * sizeof(unsigned)) != cudaSuccess || cudaMalloc((void **)&e->d_enc1_err, sizeof(int)) != cudaSuccess ||
                    cudaMemset(e->d_enc1_err, 0, sizeof(int)) != cudaSuccess;
     if (rc) { snprintf(err, errlen, "persistent encoder set-up: %s", cudaGetErrorString(cudaGetLastError())); return -1; }
@@ -691,7 +697,7 @@ static int launch_encoder(nb_engine_t *e, int nwin, int c) {
         q->ring_bytes = e->enc1_slot;
         q->eps = eps; q->scale = 1.0f / sqrtf(128.0f);
         q->pos = d_pos; q->cache_len = d_cache_len;
-        q->h = h; q->h2 = hn; q->ff = e->ff; q->att = e->att; q->image = e->enc1_image;
+        q->h = h; q->h2 = hn; q->ff = e->ff; q->att = e->att; q->image = e->enc1_image; q->fold = e->enc1_fold;
         q->xout = (uint16_t *)e->xin; q->xout_plane = plD;
         q->bar = e->d_enc1_bar; q->err = e->d_enc1_err;
         if (nb_encoder1(q, e->enc1_grid, st)) return -1;

@@ -44,6 +44,7 @@ typedef struct {
     float *h;                   /* [c][D] residual stream: pre-encode output in, last block's output out */
     float *h2;                  /* [c][D] the residual stream between the two halves of a block */
     const uint8_t *image;       /* the weights laid out per CTA (nb_encoder1_repack) */
+    const float *fold;          /* LayerNorm fold constants (nb_encoder1_repack) */
     float *ff, *att;            /* [c][FF], [c][D] scratch */
     uint16_t *xout;             /* LN_out(h) as bf16 hi / lo planes [c][D], xout_plane elements apart */
     int64_t xout_plane;
@@ -71,10 +72,11 @@ int nb_decoder1_fits(int PH, int JH, int V, int grid, int cmax, size_t smem_opti
 size_t nb_decoder1_smem(int PH, int JH, int V, int grid, int c);
 
 int nb_encoder1(const NbEnc1Args *args, int grid, void *stream);
-int nb_encoder1_ring_bytes(int D, int FF, int grid, size_t smem_optin);
-size_t nb_encoder1_smem(int ring_bytes);
+int nb_encoder1_ring_bytes(int D, int FF, int grid, size_t smem_optin, int cmax, int Lmax);
+size_t nb_encoder1_smem(int ring_bytes, int c, int Lmax);
 size_t nb_encoder1_image_bytes(int D, int FF, int layers);
-int nb_encoder1_repack(const NbEnc1Args *args, int grid, uint8_t *image, void *stream);
+size_t nb_encoder1_fold_bytes(int D, int FF, int layers);
+int nb_encoder1_repack(const NbEnc1Args *args, int grid, uint8_t *image, float *fold, void *stream);
 
 /* log-mel frames of sample spans (k_mel.cu) into rows out_row0.. of each stream's frame block */
 int nb_logmel_frames(const float *span, int64_t span_stride, int streams, int nframes, float *out, int64_t out_stride, int64_t out_row0,

@@ -32,6 +32,7 @@ constexpr int MAXU = 8;      // hidden units per CTA (4 gate rows each)
 constexpr int MAXP = 8;      // prediction rows per CTA
 constexpr int MAXV = 8;      // vocabulary rows per CTA
 constexpr int MAXF = 16;     // frames per chunk
+constexpr int MAXCTA = 256;  // CTAs of the grid at most (the decision reads 8 per lane)
 constexpr long long WAIT_LIMIT = 2000000000LL;
 
 __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
@@ -64,6 +65,22 @@ __device__ bool grid_sync(const NbDec1Args &a, Shared &S, unsigned &epoch) {
     }
     __syncthreads();
     return !S.abort;
+}
+
+// dst[k] = src[k] for k < n <= 4 * THREADS (a vector another CTA wrote, read from L2): every load
+// of the thread is issued before the first store, so the copy costs one L2 round trip.
+__device__ __forceinline__ void copy_vec(float *dst, const float *src, int n) {
+    float v[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        const int k = threadIdx.x + q * THREADS;
+        v[q] = k < n ? __ldcg(src + k) : 0.0f;
+    }
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        const int k = threadIdx.x + q * THREADS;
+        if (k < n) dst[k] = v[q];
+    }
 }
 
 // out[r] = sum_k W[r][k] x[k] for the nr rows of a bf16 [nr][K] block in shared memory (row r
@@ -155,10 +172,8 @@ __global__ void __launch_bounds__(THREADS, 1) decoder1_kernel(const __grid_const
             // ---- L0: x = [embed(last) | h0 committed] ----
             float *H0c = a.H0 + cur * PH, *H0p = a.H0 + (1 - cur) * PH;
             float *H1c = a.H1 + cur * PH, *H1p = a.H1 + (1 - cur) * PH;
-            for (int k = tid; k < PH; k += THREADS) {
-                S.x[k] = last == a.blank ? 0.0f : nb::bf2f(a.embed[(size_t)last * PH + k]);
-                S.x[PH + k] = H0c[k];
-            }
+            for (int k = tid; k < PH; k += THREADS) S.x[k] = last == a.blank ? 0.0f : nb::bf2f(a.embed[(size_t)last * PH + k]);
+            copy_vec(S.x + PH, H0c, PH);
             __syncthreads();
             rows_dot(W0s, 4 * U, 2 * PH, S.x, S.gates);
             __syncthreads();
@@ -171,10 +186,8 @@ __global__ void __launch_bounds__(THREADS, 1) decoder1_kernel(const __grid_const
             }
             if (!(ok = grid_sync(a, S, epoch))) break;
             // ---- L1: x = [h0' | h1 committed] ----
-            for (int k = tid; k < PH; k += THREADS) {
-                S.x[k] = H0p[k];
-                S.x[PH + k] = H1c[k];
-            }
+            copy_vec(S.x, H0p, PH);
+            copy_vec(S.x + PH, H1c, PH);
             __syncthreads();
             rows_dot(W1s, 4 * U, 2 * PH, S.x, S.gates);
             __syncthreads();
@@ -187,7 +200,7 @@ __global__ void __launch_bounds__(THREADS, 1) decoder1_kernel(const __grid_const
             }
             if (!(ok = grid_sync(a, S, epoch))) break;
             // ---- PRED: pred = bp + Wp h1' ----
-            for (int k = tid; k < PH; k += THREADS) S.x[k] = H1p[k];
+            copy_vec(S.x, H1p, PH);
             __syncthreads();
             rows_dot(Wps, P, PH, S.x, S.gates);
             __syncthreads();
@@ -196,7 +209,7 @@ __global__ void __launch_bounds__(THREADS, 1) decoder1_kernel(const __grid_const
             pred_valid = 1;
         }
         // ---- JOINT: this CTA's vocabulary rows for every remaining frame ----
-        for (int k = tid; k < JH; k += THREADS) S.pred[k] = a.PRED[k];
+        copy_vec(S.pred, a.PRED, JH);
         __syncthreads();
         const int nf = c - t;
         {
@@ -239,15 +252,33 @@ __global__ void __launch_bounds__(THREADS, 1) decoder1_kernel(const __grid_const
         }
         if (!(ok = grid_sync(a, S, epoch))) break;
         // ---- decision (every CTA): argmax per frame over the CTAs, first non-blank frame ----
-        if (tid < nf) {
+        // warp w reduces frames w, w + 8: lane l reads the maxima of CTAs l, l + 32, ... (all its
+        // loads in flight at once), then a warp-wide max, ties to the lowest index
+        for (int fr = warp; fr < nf; fr += NWARPS) {
+            float pv[MAXCTA / 32];
+            int pix[MAXCTA / 32];
+#pragma unroll
+            for (int q = 0; q < MAXCTA / 32; ++q) {
+                const int b = lane + 32 * q;
+                pv[q] = -INFINITY;
+                pix[q] = 0x7fffffff;
+                if (b < (int)gridDim.x) {
+                    pv[q] = __ldcg(a.part_v + (size_t)b * MAXF + fr);
+                    pix[q] = __ldcg(a.part_i + (size_t)b * MAXF + fr);
+                }
+            }
             float best = -INFINITY;
             int bidx = 0x7fffffff;
-            for (int b = 0; b < (int)gridDim.x; ++b) {
-                const float v = a.part_v[(size_t)b * MAXF + tid];
-                const int i = a.part_i[(size_t)b * MAXF + tid];
-                if (v > best || (v == best && i < bidx)) { best = v; bidx = i; }
+#pragma unroll
+            for (int q = 0; q < MAXCTA / 32; ++q)
+                if (pv[q] > best || (pv[q] == best && pix[q] < bidx)) { best = pv[q]; bidx = pix[q]; }
+#pragma unroll
+            for (int o = 16; o >= 1; o >>= 1) {
+                const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+                const int oi = __shfl_xor_sync(0xffffffffu, bidx, o);
+                if (ov > best || (ov == best && oi < bidx)) { best = ov; bidx = oi; }
             }
-            S.pi[0][tid] = bidx;
+            if (lane == 0) S.pi[0][fr] = bidx;
         }
         __syncthreads();
         int f = 0;
@@ -313,7 +344,7 @@ extern "C" size_t nb_decoder1_smem(int PH, int JH, int V, int grid, int c) {
 // Whether the persistent decoder fits this model on `grid` CTAs.
 extern "C" int nb_decoder1_fits(int PH, int JH, int V, int grid, int cmax, size_t smem_optin) {
     const int U = (PH + grid - 1) / grid, P = (JH + grid - 1) / grid, Vr = (V + grid - 1) / grid;
-    if (U > MAXU || P > MAXP || Vr > MAXV || cmax > MAXF || 2 * PH > 2048 || JH > 1024 || PH % 4 || JH % 4) return 0;
+    if (grid > MAXCTA || U > MAXU || P > MAXP || Vr > MAXV || cmax > MAXF || 2 * PH > 2048 || JH > 1024 || PH % 4 || JH % 4) return 0;
     return nb_decoder1_smem(PH, JH, V, grid, cmax) <= smem_optin;
 }
 
@@ -321,6 +352,7 @@ extern "C" int nb_decoder1(const NbDec1Args *args, int grid, void *stream) {
     const NbDec1Args &a = *args;
     if (a.c < 0 || a.c > MAXF) return nb_set_error("persistent decoder: %d frames per chunk (0..%d)", a.c, MAXF);
     if (a.c == 0) return 0;
+    if (grid > MAXCTA) return nb_set_error("persistent decoder: %d CTAs above %d", grid, MAXCTA);
     const size_t smem = nb_decoder1_smem(a.PH, a.JH, a.V, grid, a.c);
     if (nb_smem_attr((const void *)decoder1_kernel, nb_decoder1_smem(a.PH, a.JH, a.V, grid, MAXF)))
         return nb_set_error("persistent decoder: %s", nemo_gpu_last_error());

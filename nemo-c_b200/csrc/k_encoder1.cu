@@ -49,8 +49,6 @@ constexpr int ISSUE_WARP = CWARPS - 1;
 constexpr int MAXC = 16;
 constexpr int KRW = 1024;                // widest k-range of one stage
 constexpr int APITCH = KRW * 2 + 16;     // bytes per staged activation row (+16: ldmatrix bank spread)
-constexpr int ACT_PLANE = MAXC * APITCH;
-constexpr int ACT_BYTES = 2 * ACT_PLANE; // bf16 hi and lo planes
 constexpr int NB = 8;                    // projections in flight in the weight ring at most
 constexpr int MAXL = 72;                 // attention window rows (56 history + 16 new)
 constexpr int MAXR = 32;                 // weight rows of one CTA in one projection
@@ -58,23 +56,36 @@ constexpr int NSTAGE = 8;                // projections per block
 constexpr long long WAIT_LIMIT = 2000000000LL;  // clock cycles (~1 s)
 
 struct Smem {
-    float red[CWARPS][2][2][128];  // per-warp partial accumulators
+    float red[CWARPS - 1][2][2][128];  // per-warp partial accumulators of the MMA warps
     float outv[MAXR][MAXC];        // reduced outputs [weight row][activation row]
-    float st[MAXC][4];             // row statistics: mean1, inv1, mean2, inv2
+    float st[MAXC][8];             // per row: LN_out mean, inv of the block input (FF1a, read by FF1b);
+                                   // the stage's folded statistics mu1, inv1, mu2, inv2
     float rs[2][CWARPS][2 * MAXC]; // per-warp row sums (two buffers)
-    float glu[8][MAXC];            // conv-module GLU outputs of this CTA's channels
+    float fs[CWARPS][128];         // per-warp row sums of a folded LayerNorm
+    float ep_base[MAXR * MAXC];    // residual values of the epilogue items
+    float ep_og[MAXR], ep_ob[MAXR];  // LN_out vectors of the output columns (FF1b)
+    float ep_dw[16 * 9];           // depthwise taps of the CTA's channels [channel][tap]
+    float ep_hist[8][16];          // conv history rows [pos - (taps - 1) + h][channel]
+    float glu[16][MAXC];           // conv-module GLU outputs of this CTA's channels
     float sc[MAXL];                // attention scores / probabilities
     float vpart[2][128];           // attention value halves
     uint64_t full[NB];
     int ring_off[NB];              // byte offset of projection i's rows in the ring (slot i % NB)
     int ring_size[NB];             // and its bytes
-    int g_lo[NSTAGE], g_hi[NSTAGE], g_kr[NSTAGE], g_krw[NSTAGE], g_rows[NSTAGE], g_pitch[NSTAGE];
+    int g_lo[NSTAGE], g_hi[NSTAGE], g_kr[NSTAGE], g_krw[NSTAGE], g_rows[NSTAGE], g_pitch[NSTAGE], g_bytes[NSTAGE];
     long long g_img[NSTAGE];       // byte offset of this CTA's block of projection s in block 0 of the image
     int consumed;                  // projections taken by the compute warps (set when they stop)
     int issued;                    // projections requested so far
     int abort;
 };
-static_assert(ACT_BYTES >= MAXL * 512, "attention value rows do not fit the activation area");
+// Bytes of the activation area for chunks of up to c rows and an attention window of Lmax rows:
+// the bf16 hi and lo planes of the NR-row tile (NR rows each, the lo plane NR * APITCH bytes
+// after the hi plane), or the attention stage's value rows, whichever is larger.
+__host__ __device__ inline int act_rows(int c) { return c <= 8 ? 8 : 16; }
+__host__ __device__ inline int act_bytes(int c, int Lmax) {
+    const int tile = 2 * act_rows(c) * APITCH, vals = Lmax * 512;
+    return ((tile > vals ? tile : vals) + 127) / 128 * 128;
+}
 
 __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
     asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(sm100::smem_u32(dst)),
@@ -179,11 +190,15 @@ __host__ __device__ inline void stage_shape(int s, int D, int FF, int &nout, int
     K = Ks[s];
     mult = m[s];
 }
+// Image bytes per weight row of projection s: the padded row, plus for a projection that follows a
+// folded LayerNorm (FF1a, QKV, PW1, FF2a: s even) its float4 of fold constants, stored after all
+// rows of the CTA's block (one bulk copy brings both).
+__host__ __device__ inline int stage_row_bytes(int s, int krw) { return krw * 2 + 16 + ((s & 1) ? 0 : 16); }
 __host__ __device__ inline long long stage_image_bytes(int s, int D, int FF) {
     int nout, K, mult;
     stage_shape(s, D, FF, nout, K, mult);
     const int krw = K <= KRW ? K : KRW;
-    return (long long)(krw * 2 + 16) * mult * nout * (K / krw);
+    return (long long)stage_row_bytes(s, krw) * mult * nout * (K / krw);
 }
 __host__ __device__ inline long long layer_image_bytes(int D, int FF) {
     long long b = 0;
@@ -197,10 +212,14 @@ __device__ __forceinline__ long long image_offset(const NbEnc1Args &a, int l, in
     long long rows_before = (long long)mult * g.lo;
     if (g.K > KRW) rows_before += (long long)g.kr * nout;
     (void)cta; (void)grid;
-    return off + rows_before * geo_pitch(g);
+    return off + rows_before * stage_row_bytes(s, g.krw);
 }
 
-// Set-up: one CTA per (CTA of the persistent grid, projection, block) copies that CTA's rows.
+__host__ __device__ inline int fold_rows(int D, int FF);
+__host__ __device__ inline int fold_off(int s, int D, int FF);
+
+// Set-up: one CTA per (CTA of the persistent grid, projection, block) copies that CTA's rows (and
+// for s even their fold constants, from a.fold, computed before).
 __global__ void encoder1_repack_kernel(const __grid_constant__ NbEnc1Args a, uint8_t *image) {
     const int cta = blockIdx.x, s = blockIdx.y, l = blockIdx.z;
     const Geo g = stage_geo(a, l, s, cta, gridDim.x);
@@ -215,6 +234,11 @@ __global__ void encoder1_repack_kernel(const __grid_constant__ NbEnc1Args a, uin
         }
         *(uint4 *)(dst + (size_t)j * pitch + v * 16) = x;
     }
+    if (!(s & 1))
+        for (int j = threadIdx.x; j < rows; j += blockDim.x) {
+            const int wrow = j < R ? g.lo + j : g.N / 2 + g.lo + (j - R);
+            ((float4 *)(dst + (size_t)rows * pitch))[j] = ((const float4 *)a.fold)[(int64_t)l * fold_rows(a.D, a.FF) + fold_off(s, a.D, a.FF) + wrow];
+        }
 }
 
 // ---- weight ring: the CTA's weight rows of every projection, in order ---------------------------
@@ -231,7 +255,7 @@ __device__ void issue_ahead(const NbEnc1Args &a, Smem &S, uint8_t *ring, int &is
     limit = min(limit, a.layers * NSTAGE);
     while (issued < limit && issued - consumed < NB) {
         const int i = issued, st = i % NSTAGE;
-        const int sz = S.g_rows[st] * S.g_pitch[st];
+        const int sz = S.g_bytes[st];
         const int off = head + sz > RB ? 0 : head;
         bool clash = false;
         for (int j = consumed; j < i && !clash; ++j) {
@@ -257,26 +281,51 @@ __device__ void issue_ahead(const NbEnc1Args &a, Smem &S, uint8_t *ring, int &is
 
 // ---- compute warps -----------------------------------------------------------------------------
 
-// Sums over the compute threads of two values per row (every thread gets the totals). One
-// butterfly per warp reduces all 32 values at once: at the step with lane offset o each lane keeps
-// the half of its values selected by (lane & o) and adds its partner's copy of that half, so after
-// five steps lane l holds the warp's total of value l; the eight warps' totals then meet in shared
-// memory (two buffers, alternating, so back-to-back calls need one barrier each).
-__device__ __forceinline__ void rows_sum2(float (&v)[MAXC], float (&w)[MAXC], Smem &S, int &buf) {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    float x[2 * MAXC];
+// Butterfly of V values per lane over the warp (V a power of two, 16 <= V <= 128): at the step with
+// lane offset O each lane keeps the half of its values selected by (lane & O) and adds its
+// partner's copy of that half; once one value is left the remaining steps add it plainly. After it,
+// lane l holds in x[j] (j < max(V / 32, 1)) the warp's total of value l * V / 32 + j (V >= 32) or of
+// value l >> 1 (V = 16); stored at position lane * max(V / 32, 1) + j, value v sits at fs_pos(v).
+// (Templates, so that every index is a constant and the values stay in registers.)
+template <int N, int O>
+struct WarpFold {
+    static __device__ __forceinline__ void run(float *x, int lane) {
+        if constexpr (O > 0) {
+            if constexpr (N > 1) {
+                constexpr int H = N / 2;
+                const bool up = (lane & O) != 0;
 #pragma unroll
-    for (int u = 0; u < MAXC; ++u) { x[2 * u] = v[u]; x[2 * u + 1] = w[u]; }
-#pragma unroll
-    for (int o = 16; o >= 1; o >>= 1) {
-        const bool up = (lane & o) != 0;
-#pragma unroll
-        for (int j = 0; j < o; ++j) {
-            const float send = up ? x[j] : x[j + o];
-            const float keep = up ? x[j + o] : x[j];
-            x[j] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+                for (int j = 0; j < H; ++j) {
+                    const float send = up ? x[j] : x[j + H];
+                    const float keep = up ? x[j + H] : x[j];
+                    x[j] = keep + __shfl_xor_sync(0xffffffffu, send, O);
+                }
+                WarpFold<H, O / 2>::run(x, lane);
+            } else {
+                x[0] += __shfl_xor_sync(0xffffffffu, x[0], O);
+                WarpFold<1, O / 2>::run(x, lane);
+            }
         }
     }
+};
+template <int V>
+__device__ __forceinline__ void warp_fold(float (&x)[V]) { WarpFold<V, 16>::run(x, threadIdx.x & 31); }
+
+// Sums over the compute threads of two values per row (every thread gets the totals), NR rows
+// (8 or 16). One butterfly per warp reduces all 2 NR values at once: at the step with lane offset
+// o each lane keeps the half of its values selected by (lane & o) and adds its partner's copy of
+// that half; once one value is left the remaining steps add it plainly. Lane l then holds the
+// warp's total of value l >> SH (SH = 1 for 16 values, 0 for 32); the eight warps' totals meet in
+// shared memory (two buffers, alternating, so back-to-back calls need one barrier each).
+template <int NR>
+__device__ __forceinline__ void rows_sum2(float (&v)[NR], float (&w)[NR], Smem &S, int &buf) {
+    static_assert(NR == 8 || NR == 16, "8 or 16 rows");
+    constexpr int V = 2 * NR, SH = NR == 16 ? 0 : 1;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    float x[V];
+#pragma unroll
+    for (int u = 0; u < NR; ++u) { x[2 * u] = v[u]; x[2 * u + 1] = w[u]; }
+    warp_fold<V>(x);
     S.rs[buf][warp][lane] = x[0];
     cbar();
     float t = 0.0f;
@@ -284,16 +333,23 @@ __device__ __forceinline__ void rows_sum2(float (&v)[MAXC], float (&w)[MAXC], Sm
     for (int ww = 0; ww < CWARPS; ++ww) t += S.rs[buf][ww][lane];
     buf ^= 1;
 #pragma unroll
-    for (int u = 0; u < MAXC; ++u) {
-        v[u] = __shfl_sync(0xffffffffu, t, 2 * u);
-        w[u] = __shfl_sync(0xffffffffu, t, 2 * u + 1);
+    for (int u = 0; u < NR; ++u) {
+        v[u] = __shfl_sync(0xffffffffu, t, (2 * u) << SH);
+        w[u] = __shfl_sync(0xffffffffu, t, (2 * u + 1) << SH);
     }
 }
+
+// e / R and e % R for 0 <= e < 2048 and 1 <= R <= 32 without a division: q = e m >> 16 with
+// m = ceil(2^16 / R). e m / 2^16 exceeds e / R by less than e / 2^16 < 1 / R, which never carries
+// it past the next integer.
+struct Div { int R, m; };
+__device__ __forceinline__ Div make_div(int R) { R = max(R, 1); return { R, (65536 + R - 1) / R }; }
+__device__ __forceinline__ int div_q(const Div &d, int e) { return (e * d.m) >> 16; }
 
 enum { P_PLAIN = 0, P_LN = 1, P_LN2 = 2, P_DWLN = 3 };
 
 // The stage's input rows in registers: thread t holds columns 4t .. 4t+3 of every row (t < K/4).
-struct Act { float4 x[MAXC]; };
+template <int NR> struct Act { float4 x[NR]; };
 
 // Predicated 16-byte L2 load into a register that keeps its value when the predicate is false (so
 // the loads of all rows are in flight together, with nothing waiting on any of them).
@@ -305,11 +361,12 @@ __device__ __forceinline__ void ld_cg_pred(float4 &v, const float *p, bool pred)
         : "l"(p), "r"((int)pred));
 }
 
-__device__ __forceinline__ void gather(Act &A, const float *X, int ldx, int k0, int K, int c) {
+template <int NR>
+__device__ __forceinline__ void gather(Act<NR> &A, const float *X, int ldx, int k0, int K, int c) {
     const int t = threadIdx.x;
     const bool own = 4 * t < K;
 #pragma unroll
-    for (int u = 0; u < MAXC; ++u) {
+    for (int u = 0; u < NR; ++u) {
         A.x[u] = make_float4(0.f, 0.f, 0.f, 0.f);
         ld_cg_pred(A.x[u], X + (int64_t)u * ldx + k0 + 4 * t, own && u < c);
     }
@@ -318,37 +375,44 @@ __device__ __forceinline__ void gather(Act &A, const float *X, int ldx, int k0, 
 // LayerNorm statistics of each row (mean, inv = 1/sqrt(var + eps)) over K columns, from the sums of
 // x and x^2 in one reduction (the Metal kernel subtracts the mean first; the two agree to fp32
 // rounding for these activations).
-__device__ __forceinline__ void row_stats(const Act &A, Smem &S, int &buf, int K, float eps, float (&mean)[MAXC], float (&inv)[MAXC]) {
-    float s1[MAXC], s2[MAXC];
+template <int NR>
+__device__ __forceinline__ void row_stats(const Act<NR> &A, Smem &S, int &buf, int K, float eps, float (&mean)[NR], float (&inv)[NR]) {
+    float s1[NR], s2[NR];
 #pragma unroll
-    for (int u = 0; u < MAXC; ++u) {
+    for (int u = 0; u < NR; ++u) {
         const float4 x = A.x[u];
         s1[u] = x.x + x.y + x.z + x.w;
         s2[u] = x.x * x.x + x.y * x.y + x.z * x.z + x.w * x.w;
     }
-    rows_sum2(s1, s2, S, buf);
+    rows_sum2<NR>(s1, s2, S, buf);
     const float invK = 1.0f / (float)K;
 #pragma unroll
-    for (int u = 0; u < MAXC; ++u) {
+    for (int u = 0; u < NR; ++u) {
         mean[u] = s1[u] * invK;
         inv[u] = rsqrtf(fmaxf(s2[u] * invK - mean[u] * mean[u], 0.0f) + eps);
     }
 }
 
 // Store the (normalised) rows as bf16 hi / lo planes of the activation tile.
-__device__ __forceinline__ void stage_store(const Act &A, uint8_t *act, int c, int K) {
+template <int NR>
+__device__ __forceinline__ void stage_store(const Act<NR> &A, uint8_t *act, int c, int K) {
     const int t = threadIdx.x;
     if (4 * t >= K) return;
 #pragma unroll
-    for (int u = 0; u < MAXC; ++u) {
+    for (int u = 0; u < NR; ++u) {
         if (u < c) {
+            // hi = bf16(x) (two per cvt, the first operand to the upper half), lo = bf16(x - hi)
             const float4 v = A.x[u];
-            const __nv_bfloat162 h0 = __floats2bfloat162_rn(v.x, v.y), h1 = __floats2bfloat162_rn(v.z, v.w);
-            const __nv_bfloat162 l0 = __floats2bfloat162_rn(v.x - __low2float(h0), v.y - __high2float(h0));
-            const __nv_bfloat162 l1 = __floats2bfloat162_rn(v.z - __low2float(h1), v.w - __high2float(h1));
+            uint32_t h0, h1, l0, l1;
+            asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(h0) : "f"(v.y), "f"(v.x));
+            asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(h1) : "f"(v.w), "f"(v.z));
+            const float r0 = v.x - __uint_as_float(h0 << 16), r1 = v.y - __uint_as_float(h0 & 0xffff0000u);
+            const float r2 = v.z - __uint_as_float(h1 << 16), r3 = v.w - __uint_as_float(h1 & 0xffff0000u);
+            asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(l0) : "f"(r1), "f"(r0));
+            asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(l1) : "f"(r3), "f"(r2));
             uint8_t *hp = act + u * APITCH + t * 8;
-            *(uint2 *)hp = make_uint2(*(const uint32_t *)&h0, *(const uint32_t *)&h1);
-            *(uint2 *)(hp + ACT_PLANE) = make_uint2(*(const uint32_t *)&l0, *(const uint32_t *)&l1);
+            *(uint2 *)hp = make_uint2(h0, h1);
+            *(uint2 *)(hp + NR * APITCH) = make_uint2(l0, l1);
         }
     }
 }
@@ -359,11 +423,13 @@ __device__ __forceinline__ float4 ld4g(const float *p) { return __ldg((const flo
 // rows of each granule.
 struct Frag { uint32_t b[2][4], a[2][4]; };
 
+// (activation planes of NR rows: the lo plane NR * APITCH bytes after the hi plane)
+template <int NR>
 __device__ __forceinline__ void frag_load(Frag &f, uint32_t act, uint32_t wb, int pitch, int nrows, int kk, int ng, int nnt) {
     const int lane = threadIdx.x & 31, mi = lane >> 3, rr = lane & 7;
 #pragma unroll
-    for (int nt = 0; nt < 2; ++nt)
-        if (nt < nnt) ldsm_x4(act + (mi >> 1) * ACT_PLANE + (nt * 8 + rr) * APITCH + (kk + (mi & 1) * 8) * 2, f.b[nt][0], f.b[nt][1], f.b[nt][2], f.b[nt][3]);
+    for (int nt = 0; nt < NR / 8; ++nt)
+        if (nt < nnt) ldsm_x4(act + (mi >> 1) * (NR * APITCH) + (nt * 8 + rr) * APITCH + (kk + (mi & 1) * 8) * 2, f.b[nt][0], f.b[nt][1], f.b[nt][2], f.b[nt][3]);
 #pragma unroll
     for (int g = 0; g < 2; ++g)
         if (g < ng) {
@@ -373,12 +439,13 @@ __device__ __forceinline__ void frag_load(Frag &f, uint32_t act, uint32_t wb, in
 }
 
 // acc_h / acc_l[g][nt] += weight rows of granule g times the hi / lo activation rows of tile nt.
-__device__ __forceinline__ void frag_mma(const Frag &f, int ng, int nnt, float (&ah)[2][2][4], float (&al)[2][2][4]) {
+template <int NT>
+__device__ __forceinline__ void frag_mma(const Frag &f, int ng, int nnt, float (&ah)[2][NT][4], float (&al)[2][NT][4]) {
 #pragma unroll
     for (int g = 0; g < 2; ++g)
         if (g < ng)
 #pragma unroll
-            for (int nt = 0; nt < 2; ++nt)
+            for (int nt = 0; nt < NT; ++nt)
                 if (nt < nnt) {
                     mma16816(ah[g][nt], f.a[g][0], f.a[g][1], f.a[g][2], f.a[g][3], f.b[nt][0], f.b[nt][1]);  // hi plane
                     mma16816(al[g][nt], f.a[g][0], f.a[g][1], f.a[g][2], f.a[g][3], f.b[nt][2], f.b[nt][3]);  // lo plane
@@ -409,20 +476,36 @@ __device__ __forceinline__ void attention_item(const NbEnc1Args &a, Smem &S, uin
             p4[i] = ld4g(Pb + (int64_t)j * D + 4 * lane);
         }
     }
-    // value rows: element e = row e / 32, columns 4 (e % 32) .. +3
-    for (int e = tid; e < L * 32; e += CTHREADS) ((float4 *)Vs)[e] = __ldcg((const float4 *)(Vb + (int64_t)(e >> 5) * ld) + (e & 31));
+    // value rows: element e = row e / 32, columns 4 (e % 32) .. +3; every load in flight at once,
+    // stored to shared memory after the scores
+    constexpr int VIT = MAXL * 32 / CTHREADS;
+    float4 vv[VIT];
+#pragma unroll
+    for (int q = 0; q < VIT; ++q) {
+        const int e = tid + q * CTHREADS;
+        if (e < L * 32) vv[q] = __ldcg((const float4 *)(Vb + (int64_t)(e >> 5) * ld) + (e & 31));
+    }
     const float4 qu = make_float4(q4.x + u4.x, q4.y + u4.y, q4.z + u4.z, q4.w + u4.w);
     const float4 qv = make_float4(q4.x + v4.x, q4.y + v4.y, q4.z + v4.z, q4.w + v4.w);
+    // this lane's part of the nine scores (q + u).k_j + (q + v).p_j, all nine reduced over the warp
+    // by one butterfly (lane 2 i then holds score i)
+    float sv[16];
 #pragma unroll
-    for (int i = 0; i < 9; ++i) {
+    for (int i = 0; i < 16; ++i) {
         const int j = warp + CWARPS * i;
-        if (j < L) {
-            float sc = qu.x * k4[i].x + qu.y * k4[i].y + qu.z * k4[i].z + qu.w * k4[i].w;
-            float tp = qv.x * p4[i].x + qv.y * p4[i].y + qv.z * p4[i].z + qv.w * p4[i].w;
-            sc = nb::warp_sum(sc);
-            tp = nb::warp_sum(tp);
-            if (lane == 0) S.sc[j] = (sc + tp) * a.scale;
-        }
+        sv[i] = 0.0f;
+        if (i < 9 && j < L)
+            sv[i] = (qu.x * k4[i].x + qu.y * k4[i].y + qu.z * k4[i].z + qu.w * k4[i].w) + (qv.x * p4[i].x + qv.y * p4[i].y + qv.z * p4[i].z + qv.w * p4[i].w);
+    }
+    warp_fold<16>(sv);
+    {
+        const int i = lane >> 1, j = warp + CWARPS * i;
+        if ((lane & 1) == 0 && i < 9 && j < L) S.sc[j] = sv[0] * a.scale;
+    }
+#pragma unroll
+    for (int q = 0; q < VIT; ++q) {
+        const int e = tid + q * CTHREADS;
+        if (e < L * 32) ((float4 *)Vs)[e] = vv[q];
     }
     cbar();
     if (warp == 0) {
@@ -450,18 +533,33 @@ __device__ __forceinline__ void attention_item(const NbEnc1Args &a, Smem &S, uin
 // Grid-wide barrier of the compute threads (gridsync.cuh). Returns false when the launch is being
 // abandoned.
 // The small tensors block l reads (LayerNorm vectors, depthwise taps, position biases, the rows
-// of its position table this chunk's attention reads) brought into L2 by the issue warp one block
-// ahead, so the stages that read them find them there instead of waiting on HBM.
-__device__ void prefetch_layer(const NbEnc1Args &a, int l, int pos_rows0, int pos_rows) {
+// of its position table this chunk's attention reads) and its cache rows from earlier chunks (the
+// attention's key/value history, the depthwise conv's history) brought into L2 by the issue warp
+// ahead of the block, so the stages that read them find them there instead of waiting on HBM.
+// The items are spread over the grid (CTA b takes items b, b + grid, ...; lane j of its issue warp
+// the j-th of those), each requested once: 14 vectors, the depthwise taps, the conv history rows
+// [pos - (taps - 1), pos) of the GLU output (pos >= taps - 1: they precede every chunk), the
+// position-table rows, the history rows [pos - cache_len, pos) of q|k|v (3 D wide).
+__device__ void prefetch_layer(const NbEnc1Args &a, int l, int pos, int cache_len, int pos_rows0, int pos_rows) {
     if (l >= a.layers || (threadIdx.x >> 5) != ISSUE_WARP) return;
     const NbEnc1Layer &w = a.L[l];
     const uint32_t vb = (uint32_t)a.D * 4;
-    const float *vec[14] = { w.ln_ff1_g, w.ln_ff1_b, w.ln_att_g, w.ln_att_b, w.ln_conv_g, w.ln_conv_b, w.ln_ff2_g,
-                             w.ln_ff2_b, w.ln_out_g, w.ln_out_b, w.bn_g, w.bn_b, w.bias_u, w.bias_v };
-    const int lane = threadIdx.x & 31;
-    if (lane < 14) prefetch_l2(vec[lane], vb);
-    else if (lane == 14) prefetch_l2(w.dw_w, vb * (uint32_t)a.taps);
-    else if (lane == 15) prefetch_l2(w.ptab + (int64_t)pos_rows0 * a.D, vb * (uint32_t)pos_rows);  // the rows are contiguous
+    const int lane = threadIdx.x & 31, G = gridDim.x, nitems = 16 + pos_rows + cache_len;
+    for (int i = blockIdx.x + lane * G; i < nitems; i += 32 * G) {
+        if (i < 14) {
+            const float *vec[14] = { w.ln_ff1_g, w.ln_ff1_b, w.ln_att_g, w.ln_att_b, w.ln_conv_g, w.ln_conv_b, w.ln_ff2_g,
+                                     w.ln_ff2_b, w.ln_out_g, w.ln_out_b, w.bn_g, w.bn_b, w.bias_u, w.bias_v };
+            prefetch_l2(vec[i], vb);
+        } else if (i == 14) {
+            prefetch_l2(w.dw_w, vb * (uint32_t)a.taps);
+        } else if (i == 15) {
+            if (a.taps > 1) prefetch_l2(w.din + (int64_t)(pos - (a.taps - 1)) * a.D, vb * (uint32_t)(a.taps - 1));
+        } else if (i < 16 + pos_rows) {
+            prefetch_l2(w.ptab + (int64_t)(pos_rows0 + i - 16) * a.D, vb);
+        } else {
+            prefetch_l2(w.kv + (int64_t)(pos - cache_len + (i - 16 - pos_rows)) * 3 * a.D, 3 * vb);
+        }
+    }
 }
 
 
@@ -513,9 +611,245 @@ __device__ __forceinline__ void stage_norm(const NbEnc1Args &a, int l, int s, fl
     }
 }
 
+// ---- LayerNorm folded into the projection that follows it ---------------------------------------
+// For a row x with mean mu and inv = 1/sqrt(var + eps),
+//   LN(x) W^T = inv (x (.) g) W^T - inv mu (g W^T) + b W^T,
+// so the MMA runs on x (.) g while the statistics are reduced beside it, and the epilogue applies
+//   out = inv (acc - mu F.x) + F.y,   F.x = sum_k g_k W_nk, F.y = sum_k b_k W_nk
+// (per weight row, computed at set-up). The input of block l > 0 passes through LN_out of block
+// l - 1 (g1, b1) and then LN_ff1 (g2, b2): the MMA runs on x (.) g1 (.) g2 and
+//   out = inv2 (inv1 (acc - mu1 F.x) + F.y - mu2 F.z) + F.w,
+//   F = (sum g1 g2 W, sum b1 g2 W, sum g2 W, sum b2 W),
+// where mu2, inv2 (the statistics of y = LN_out(x)) follow from six row sums of x (x, x^2, x g1,
+// x^2 g1^2, x g1^2, x g1 b1) and five sums of g1, b1 over the row (lnsum). With mu2 = 0, inv2 = 1
+// and F.z = F.w = 0 the second form is the first, which is how the epilogue applies both.
+
+// Rows of fold constants per block: FF1a (FF), QKV (3 D), PW1 (2 D, value and gate rows), FF2a (FF).
+__host__ __device__ inline int fold_rows(int D, int FF) { return 2 * FF + 5 * D; }
+__host__ __device__ inline int fold_off(int s, int D, int FF) { return s == 0 ? 0 : s == 2 ? FF : s == 4 ? FF + 3 * D : FF + 5 * D; }
+
+// Set-up: one warp per (weight row, folded projection, block).
+__global__ void encoder1_fold_kernel(const __grid_constant__ NbEnc1Args a, float4 *fold) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, s = 2 * blockIdx.y, l = blockIdx.z, D = a.D, FF = a.FF;
+    const int rows = (s == 0 || s == 6) ? FF : s == 2 ? 3 * D : 2 * D, row = blockIdx.x * 8 + warp;
+    if (row >= rows) return;
+    const NbEnc1Layer &w = a.L[l];
+    const uint16_t *W = (s == 0 ? w.ff1_w1 : s == 2 ? w.wqkv : s == 4 ? w.pw1 : w.ff2_w1) + (int64_t)row * D;
+    const float *g2 = s == 0 ? w.ln_ff1_g : s == 2 ? w.ln_att_g : s == 4 ? w.ln_conv_g : w.ln_ff2_g;
+    const float *b2 = s == 0 ? w.ln_ff1_b : s == 2 ? w.ln_att_b : s == 4 ? w.ln_conv_b : w.ln_ff2_b;
+    const bool two = s == 0 && l > 0;
+    const float *g1 = two ? a.L[l - 1].ln_out_g : g2, *b1 = two ? a.L[l - 1].ln_out_b : b2;
+    float f0 = 0.0f, f1 = 0.0f, f2 = 0.0f, f3 = 0.0f;
+    for (int k = lane; k < D; k += 32) {
+        const float wk = nb::bf2f(W[k]);
+        if (two) {
+            f0 += (g1[k] * g2[k]) * wk;
+            f1 += (b1[k] * g2[k]) * wk;
+            f2 += g2[k] * wk;
+            f3 += b2[k] * wk;
+        } else {
+            f0 += g2[k] * wk;
+            f1 += b2[k] * wk;
+        }
+    }
+    f0 = nb::warp_sum(f0);
+    f1 = nb::warp_sum(f1);
+    f2 = nb::warp_sum(f2);
+    f3 = nb::warp_sum(f3);
+    if (lane == 0) fold[(int64_t)l * fold_rows(D, FF) + fold_off(s, D, FF) + row] = make_float4(f0, f1, f2, f3);
+}
+
+// Set-up: the sums of LN_out's vectors of block l - 1 over the row, for block l (one warp each):
+// lnsum[2 l] = (sum g1, sum g1^2, sum g1 b1, sum b1), lnsum[2 l + 1].x = sum b1^2.
+__global__ void encoder1_lnsum_kernel(const __grid_constant__ NbEnc1Args a, float4 *lnsum) {
+    const int l = blockIdx.x, lane = threadIdx.x;
+    if (l == 0 || lane >= 32) return;
+    const float *g1 = a.L[l - 1].ln_out_g, *b1 = a.L[l - 1].ln_out_b;
+    float t[5] = { 0.f, 0.f, 0.f, 0.f, 0.f };
+    for (int k = lane; k < a.D; k += 32) {
+        t[0] += g1[k];
+        t[1] += g1[k] * g1[k];
+        t[2] += g1[k] * b1[k];
+        t[3] += b1[k];
+        t[4] += b1[k] * b1[k];
+    }
+#pragma unroll
+    for (int j = 0; j < 5; ++j) t[j] = nb::warp_sum(t[j]);
+    if (lane == 0) {
+        lnsum[2 * l] = make_float4(t[0], t[1], t[2], t[3]);
+        lnsum[2 * l + 1] = make_float4(t[4], 0.f, 0.f, 0.f);
+    }
+}
+
+template <int V>
+__device__ __forceinline__ void warp_fold_store(float (&x)[V], float *dst) {
+    constexpr int VPL = V >= 32 ? V / 32 : 1;
+    warp_fold<V>(x);
+    const int lane = threadIdx.x & 31;
+#pragma unroll
+    for (int j = 0; j < VPL; ++j) dst[lane * VPL + j] = x[j];
+}
+template <int V>
+__device__ __forceinline__ int fs_pos(int v) { return V >= 32 ? v : 2 * v; }
+
+// The row sums of a folded LayerNorm's input rows (this thread's columns), reduced per warp into
+// S.fs[warp]: (sum x, sum x^2) per row, or for the block input of block l > 0 (two LayerNorms,
+// g1 b1 the first one's vectors) (x, x^2, x g1, x^2 g1^2) per row at 0 and (x g1^2, x g1 b1) per
+// row at 64.
+template <int NR>
+__device__ __forceinline__ void fold_sums(const Act<NR> &A, Smem &S, bool two, float4 g1, float4 b1) {
+    float *dst = S.fs[threadIdx.x >> 5];
+    if (!two) {
+        float v[2 * NR];
+#pragma unroll
+        for (int u = 0; u < NR; ++u) {
+            const float4 x = A.x[u];
+            v[2 * u] = (x.x + x.y) + (x.z + x.w);
+            v[2 * u + 1] = (x.x * x.x + x.y * x.y) + (x.z * x.z + x.w * x.w);
+        }
+        warp_fold_store<2 * NR>(v, dst);
+    } else {
+        const float4 g2 = make_float4(g1.x * g1.x, g1.y * g1.y, g1.z * g1.z, g1.w * g1.w);
+        const float4 gb = make_float4(g1.x * b1.x, g1.y * b1.y, g1.z * b1.z, g1.w * b1.w);
+        {
+            float v[4 * NR];
+#pragma unroll
+            for (int u = 0; u < NR; ++u) {
+                const float4 x = A.x[u];
+                const float4 xx = make_float4(x.x * x.x, x.y * x.y, x.z * x.z, x.w * x.w);
+                v[4 * u] = (x.x + x.y) + (x.z + x.w);
+                v[4 * u + 1] = (xx.x + xx.y) + (xx.z + xx.w);
+                v[4 * u + 2] = (x.x * g1.x + x.y * g1.y) + (x.z * g1.z + x.w * g1.w);
+                v[4 * u + 3] = (xx.x * g2.x + xx.y * g2.y) + (xx.z * g2.z + xx.w * g2.w);
+            }
+            warp_fold_store<4 * NR>(v, dst);
+        }
+        float v[2 * NR];
+#pragma unroll
+        for (int u = 0; u < NR; ++u) {
+            const float4 x = A.x[u];
+            v[2 * u] = (x.x * g2.x + x.y * g2.y) + (x.z * g2.z + x.w * g2.w);
+            v[2 * u + 1] = (x.x * gb.x + x.y * gb.y) + (x.z * gb.z + x.w * gb.w);
+        }
+        warp_fold_store<2 * NR>(v, dst + 64);
+    }
+}
+
+// Statistics of a folded LayerNorm for row u < c from the per-warp sums (the issue warp, after the
+// CTA barrier that follows fold_sums): S.st[u][2..5] = mu1, inv1, mu2, inv2 (mu2 = 0, inv2 = 1 for
+// one LayerNorm) and, for two, S.st[u][0..1] = mu1, inv1 for the FF1b epilogue.
+template <int NR>
+__device__ __forceinline__ void fold_stats(Smem &S, int u, bool two, int K, float eps, float4 G0, float G4) {
+    const float invK = 1.0f / (float)K;
+    if (!two) {
+        float s1 = 0.f, s2 = 0.f;
+#pragma unroll
+        for (int w = 0; w < CWARPS; ++w) {
+            s1 += S.fs[w][fs_pos<2 * NR>(2 * u)];
+            s2 += S.fs[w][fs_pos<2 * NR>(2 * u + 1)];
+        }
+        const float mu = s1 * invK, inv = rsqrtf(fmaxf(s2 * invK - mu * mu, 0.0f) + eps);
+        S.st[u][2] = mu; S.st[u][3] = inv; S.st[u][4] = 0.0f; S.st[u][5] = 1.0f;
+        return;
+    }
+    float t[6] = { 0.f, 0.f, 0.f, 0.f, 0.f, 0.f };
+#pragma unroll
+    for (int w = 0; w < CWARPS; ++w) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) t[j] += S.fs[w][fs_pos<4 * NR>(4 * u + j)];
+        t[4] += S.fs[w][64 + fs_pos<2 * NR>(2 * u)];
+        t[5] += S.fs[w][64 + fs_pos<2 * NR>(2 * u + 1)];
+    }
+    // G0 = (sum g1, sum g1^2, sum g1 b1, sum b1), G4 = sum b1^2
+    const float mu1 = t[0] * invK, inv1 = rsqrtf(fmaxf(t[1] * invK - mu1 * mu1, 0.0f) + eps);
+    const float sy = inv1 * (t[2] - mu1 * G0.x) + G0.w;
+    const float sa = t[3] - 2.0f * mu1 * t[4] + mu1 * mu1 * G0.y;  // sum (x - mu1)^2 g1^2
+    const float sb = t[5] - mu1 * G0.z;                             // sum (x - mu1) g1 b1
+    const float syy = inv1 * inv1 * sa + 2.0f * inv1 * sb + G4;
+    const float mu2 = sy * invK, inv2 = rsqrtf(fmaxf(syy * invK - mu2 * mu2, 0.0f) + eps);
+    S.st[u][0] = mu1; S.st[u][1] = inv1;
+    S.st[u][2] = mu1; S.st[u][3] = inv1; S.st[u][4] = mu2; S.st[u][5] = inv2;
+}
+
+// The issue warp's part of a stage, while the other warps run the MMAs: the weight requests; what
+// the epilogue reads, brought into shared memory (residual values of the outputs, LN_out vectors,
+// depthwise taps and conv history); the statistics of a folded LayerNorm; the layer prefetches.
+// Its loads are all issued before their first use. (The fold constants of the CTA's weight rows
+// arrive with the rows in the ring.)
+struct StagePrep {
+    int l, s, mode, lo, R, kr, nrows, pos, cache_len, pos_rows0, pos_rows;
+    const float *resid;
+};
+template <int NR>
+__device__ void stage_prep(const NbEnc1Args &a, Smem &S, uint8_t *ring, int &issued, int &head, int gi, uint64_t pol, const StagePrep &p) {
+    const int lane = threadIdx.x & 31, c = a.c, D = a.D, R = p.R, s = p.s;
+    issue_ahead(a, S, ring, issued, head, gi, pol, 1 << 30);
+    const bool fold = p.mode == P_LN || p.mode == P_LN2, two = p.mode == P_LN2;
+    const bool need_base = ((s == 1 || s == 7) && p.kr == 0) || s == 3 || s == 5;
+    const bool need_ln = s == 1 && p.kr == 0 && p.l > 0;
+    const NbEnc1Layer &w = a.L[p.l];
+    const Div dR = make_div(R);
+    constexpr int QB = MAXR * MAXC / 32;
+    float vb[QB];
+#pragma unroll
+    for (int q = 0; q < QB; ++q) {
+        const int e = lane + 32 * q, r = div_q(dR, e);
+        vb[q] = 0.0f;
+        if (need_base && e < R * c) vb[q] = __ldcg(p.resid + (int64_t)r * D + p.lo + (e - r * R));
+    }
+    float og = 1.0f, ob = 0.0f;
+    if (need_ln && lane < R) { og = __ldg(a.L[p.l - 1].ln_out_g + p.lo + lane); ob = __ldg(a.L[p.l - 1].ln_out_b + p.lo + lane); }
+    float4 G0 = make_float4(0.f, 0.f, 0.f, 0.f);
+    float G4 = 0.0f;
+    if (two) {
+        const float4 *ls = (const float4 *)a.fold + (int64_t)a.layers * fold_rows(D, a.FF) + 2 * p.l;
+        G0 = __ldg(ls);
+        G4 = __ldg(ls + 1).x;
+    }
+    float dw[5], hs[4];
+    if (s == 4) {
+#pragma unroll
+        for (int q = 0; q < 5; ++q) {
+            const int e = lane + 32 * q;
+            dw[q] = e < R * a.taps ? __ldg(w.dw_w + (int64_t)p.lo * a.taps + e) : 0.0f;
+        }
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            const int e = lane + 32 * q;
+            const int h = div_q(dR, e);
+            hs[q] = e < (a.taps - 1) * R ? __ldcg(w.din + (int64_t)(p.pos - (a.taps - 1) + h) * D + p.lo + (e - h * R)) : 0.0f;
+        }
+    }
+    // the statistics (shared memory only) while the loads are in flight
+    if (fold && lane < c) fold_stats<NR>(S, lane, two, D, a.eps, G0, G4);
+#pragma unroll
+    for (int q = 0; q < QB; ++q) {
+        const int e = lane + 32 * q;
+        if (need_base && e < R * c) S.ep_base[e] = vb[q];
+    }
+    if (need_ln && lane < R) { S.ep_og[lane] = og; S.ep_ob[lane] = ob; }
+    if (s == 4) {
+#pragma unroll
+        for (int q = 0; q < 5; ++q) {
+            const int e = lane + 32 * q;
+            if (e < R * a.taps) S.ep_dw[e] = dw[q];
+        }
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            const int e = lane + 32 * q;
+            const int h = div_q(dR, e);
+            if (e < (a.taps - 1) * R) S.ep_hist[h][e - h * R] = hs[q];
+        }
+    }
+    if (s == 0) prefetch_layer(a, p.l + 2, p.pos, p.cache_len, p.pos_rows0, p.pos_rows);
+}
+
+// NR: activation rows handled per stage (8 when c <= 8, else 16), NR / 8 MMA column tiles.
+template <int NR>
 __device__ void compute(const NbEnc1Args &a, Smem &S, uint8_t *ring, uint8_t *act) {
+    constexpr int NT = NR / 8;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
-    const int D = a.D, c = a.c, nnt = (c + 7) / 8;
+    const int D = a.D, c = a.c, nnt = NT;
     const int pos = *a.pos, cache_len = *a.cache_len;
     unsigned epoch = 0;
     int rbuf = 0;  // row-sum buffer
@@ -530,11 +864,11 @@ __device__ void compute(const NbEnc1Args &a, Smem &S, uint8_t *ring, uint8_t *ac
     stage_norm(a, 0, 0, nga, nba, ngb, nbb);
     // position-table rows this chunk's attention reads: (Lmax - L) + (c - 1 - r) + j, j < L, r < c
     const int L_att = cache_len + c, pos_rows0 = a.Lmax - L_att, pos_rows = L_att + c - 1;
-    prefetch_layer(a, 0, pos_rows0, pos_rows);
-    prefetch_layer(a, 1, pos_rows0, pos_rows);
+    prefetch_layer(a, 0, pos, cache_len, pos_rows0, pos_rows);
+    prefetch_layer(a, 1, pos, cache_len, pos_rows0, pos_rows);
     for (int l = 0; l < a.layers && !S.abort; ++l) {
         const NbEnc1Layer &w = a.L[l];
-        const NbEnc1Layer *prev = l > 0 ? &a.L[l - 1] : nullptr;
+#pragma unroll 1
         for (int s = 0; s < NSTAGE; ++s, ++gi) {
             if (s == 3) {
                 // attention over the cache window (the QKV stage's barrier made the rows visible)
@@ -549,73 +883,42 @@ __device__ void compute(const NbEnc1Args &a, Smem &S, uint8_t *ring, uint8_t *ac
             int mode, ldx;
             const float *X;
             stage_input(a, l, s, hA, hB, X, ldx, mode);
-            const float4 ga = nga, ba = nba, gb = ngb, bb = nbb;
-            // one burst of loads: the input rows and what the epilogue needs (residual values of
-            // its outputs, depthwise taps and history)
-            Act A;
-            gather(A, X, ldx, g.kr * g.krw, K, c);
+            const float4 ga = nga, ba = nba, gb = ngb;
+            const bool fold = mode == P_LN || mode == P_LN2;
+            // the input rows, all loads in flight together
+            Act<NR> A;
+            gather<NR>(A, X, ldx, g.kr * g.krw, K, c);
             const bool own = 4 * tid < K;
-            // epilogue items e = tid + 256 q (q < 2): output column g.lo + e % R, row e / R
-            float base[2] = { 0.f, 0.f }, og[2] = { 1.f, 1.f }, ob[2] = { 0.f, 0.f };
-            const float *resid = (s == 1) ? hA : hB;
-#pragma unroll
-            for (int q = 0; q < 2; ++q) {
-                const int e = tid + CTHREADS * q;
-                if (R > 0 && e < R * c) {
-                    const int col = g.lo + e % R, r = e / R;
-                    if (((s == 1 || s == 7) && g.kr == 0) || s == 3 || s == 5) base[q] = __ldcg(resid + (int64_t)r * D + col);
-                    if (s == 1 && g.kr == 0 && prev) { og[q] = __ldg(prev->ln_out_g + col); ob[q] = __ldg(prev->ln_out_b + col); }
-                }
-            }
-            const int en = R > 0 ? tid % R : 0, er = R > 0 ? tid / R : 0;
-            const bool dact = s == 4 && R > 0 && tid < R * c;
-            float dw[9], hist[8];
-            if (dact) {
-                const int ch = g.lo + en;
-#pragma unroll
-                for (int t = 0; t < 9; ++t) dw[t] = t < a.taps ? __ldg(w.dw_w + ch * a.taps + t) : 0.0f;
-#pragma unroll
-                for (int t = 0; t < 8; ++t) {
-                    const int row = pos - (a.taps - 1) + er + t;  // history rows precede pos
-                    hist[t] = (t < a.taps - 1 && row < pos) ? __ldcg(w.din + (int64_t)row * D + ch) : 0.0f;
-                }
-            }
             // the residual buffer the next FF-out stage accumulates into starts at zero
             if (s == 0 || s == 6) {
                 float *z = s == 0 ? hB : hA;
                 for (int e = tid; e < (dhi - dlo) * c; e += CTHREADS) z[(int64_t)(e / (dhi - dlo)) * D + dlo + e % (dhi - dlo)] = 0.0f;
             }
-            if (mode != P_PLAIN) {
-                float mean[MAXC], inv[MAXC];
-                row_stats(A, S, rbuf, K, a.eps, mean, inv);
-                if (s == 0) {
+            if (fold) {
+                // the MMA runs on x (.) g (x (.) g1 (.) g2 for two LayerNorms); the statistics are
+                // finished by the issue warp during the MMAs
+                fold_sums<NR>(A, S, mode == P_LN2, ga, ba);
+                const float4 gp = mode == P_LN2 ? make_float4(ga.x * gb.x, ga.y * gb.y, ga.z * gb.z, ga.w * gb.w) : ga;
 #pragma unroll
-                    for (int u = 0; u < MAXC; ++u)
-                        if (u == tid && u < c) { S.st[u][0] = mean[u]; S.st[u][1] = inv[u]; }
+                for (int u = 0; u < NR; ++u) {
+                    float4 &x = A.x[u];
+                    x = own ? make_float4(x.x * gp.x, x.y * gp.y, x.z * gp.z, x.w * gp.w) : make_float4(0.f, 0.f, 0.f, 0.f);
                 }
+            } else if (mode == P_DWLN) {
+                float mean[NR], inv[NR];
+                row_stats<NR>(A, S, rbuf, K, a.eps, mean, inv);
 #pragma unroll
-                for (int u = 0; u < MAXC; ++u) {
+                for (int u = 0; u < NR; ++u) {
                     float4 &x = A.x[u];
                     x.x = (x.x - mean[u]) * inv[u] * ga.x + ba.x;
                     x.y = (x.y - mean[u]) * inv[u] * ga.y + ba.y;
                     x.z = (x.z - mean[u]) * inv[u] * ga.z + ba.z;
                     x.w = (x.w - mean[u]) * inv[u] * ga.w + ba.w;
-                    if (mode == P_DWLN) { x.x *= sigm(x.x); x.y *= sigm(x.y); x.z *= sigm(x.z); x.w *= sigm(x.w); }
+                    x.x *= sigm(x.x); x.y *= sigm(x.y); x.z *= sigm(x.z); x.w *= sigm(x.w);
                     if (!own) x = make_float4(0.f, 0.f, 0.f, 0.f);
                 }
-                if (mode == P_LN2) {
-                    row_stats(A, S, rbuf, K, a.eps, mean, inv);
-#pragma unroll
-                    for (int u = 0; u < MAXC; ++u) {
-                        float4 &x = A.x[u];
-                        x.x = (x.x - mean[u]) * inv[u] * gb.x + bb.x;
-                        x.y = (x.y - mean[u]) * inv[u] * gb.y + bb.y;
-                        x.z = (x.z - mean[u]) * inv[u] * gb.z + bb.z;
-                        x.w = (x.w - mean[u]) * inv[u] * gb.w + bb.w;
-                    }
-                }
             }
-            stage_store(A, act, c, K);
+            stage_store<NR>(A, act, c, K);
             // this projection's weight rows: requested now if the ring had no room for them while
             // the previous entry was held (everything before gi is released here); one thread
             // waits, the others at the barrier
@@ -628,77 +931,82 @@ __device__ void compute(const NbEnc1Args &a, Smem &S, uint8_t *ring, uint8_t *ac
             }
             cbar();
             if (S.abort) break;
-            // the weight stream's next requests go out now, during this stage's shared-memory-only
-            // math, and not at the barrier, whose few latency-critical accesses would queue behind
-            // them (this entry stays held until the stage ends, so consumed = gi)
-            issue_ahead(a, S, ring, issued, head, gi, pol, 1 << 30);
-            if (s == 0) prefetch_layer(a, l + 2, pos_rows0, pos_rows);
-            float acc[2][2][4], acl[2][2][4], acc2[2][2][4], acl2[2][2][4];
+            if (warp == ISSUE_WARP) {
+                const StagePrep p = { l, s, mode, g.lo, R, g.kr, nrows, pos, cache_len, pos_rows0, pos_rows, (s == 1) ? hA : hB };
+                stage_prep<NR>(a, S, ring, issued, head, gi, pol, p);
+            } else {
+                float acc[2][NT][4], acl[2][NT][4], acc2[2][NT][4], acl2[2][NT][4];
 #pragma unroll
-            for (int gg = 0; gg < 2; ++gg)
+                for (int gg = 0; gg < 2; ++gg)
 #pragma unroll
-                for (int nt = 0; nt < 2; ++nt)
+                    for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-                    for (int q = 0; q < 4; ++q) acc[gg][nt][q] = acl[gg][nt][q] = acc2[gg][nt][q] = acl2[gg][nt][q] = 0.0f;
-            if (nrows > 0) {
-                // warp w: k-steps [w * K / 128, (w + 1) * K / 128), alternating two accumulator sets
-                const uint32_t actb = sm100::smem_u32(act), wb = sm100::smem_u32(ring + S.ring_off[slot]);
-                // k-steps of this warp: the issue warp, which spent the start of the phase on the
-                // weight requests, takes a sixteenth of them; the others share the rest. Software-
-                // pipelined: the next k-step's fragments are requested before this one's MMAs, which
-                // alternate between two accumulator sets.
-                const int T = K / 16, t7 = T / 16, base = (T - t7) / (CWARPS - 1), extra = (T - t7) % (CWARPS - 1);
-                const int per = warp == ISSUE_WARP ? t7 : base + (warp < extra ? 1 : 0);
-                const int k0 = 16 * (warp == ISSUE_WARP ? T - t7 : warp * base + min(warp, extra));
-                Frag f[2];
-                if (per > 0) frag_load(f[0], actb, wb, pitch, nrows, k0, ng, nnt);
+                        for (int q = 0; q < 4; ++q) acc[gg][nt][q] = acl[gg][nt][q] = acc2[gg][nt][q] = acl2[gg][nt][q] = 0.0f;
+                if (nrows > 0) {
+                    const uint32_t actb = sm100::smem_u32(act), wb = sm100::smem_u32(ring + S.ring_off[slot]);
+                    // k-steps of this warp (the seven MMA warps share them). Software-pipelined: the
+                    // next k-step's fragments are requested before this one's MMAs, which alternate
+                    // between two accumulator sets.
+                    const int T = K / 16, kb = T / (CWARPS - 1), extra = T % (CWARPS - 1);
+                    const int per = kb + (warp < extra ? 1 : 0), k0 = 16 * (warp * kb + min(warp, extra));
+                    Frag f[2];
+                    if (per > 0) frag_load<NR>(f[0], actb, wb, pitch, nrows, k0, ng, nnt);
 #pragma unroll
-                for (int q = 0; q < 10; ++q) {
-                    if (q >= per) break;
-                    if (q + 1 < per) frag_load(f[(q + 1) & 1], actb, wb, pitch, nrows, k0 + (q + 1) * 16, ng, nnt);
-                    if (q & 1) frag_mma(f[q & 1], ng, nnt, acc2, acl2);
-                    else frag_mma(f[q & 1], ng, nnt, acc, acl);
+                    for (int q = 0; q < KRW / 16 / (CWARPS - 1) + 1; ++q) {
+                        if (q >= per) break;
+                        if (q + 1 < per) frag_load<NR>(f[(q + 1) & 1], actb, wb, pitch, nrows, k0 + (q + 1) * 16, ng, nnt);
+                        if (q & 1) frag_mma<NT>(f[q & 1], ng, nnt, acc2, acl2);
+                        else frag_mma<NT>(f[q & 1], ng, nnt, acc, acl);
+                    }
                 }
+#pragma unroll
+                for (int gg = 0; gg < 2; ++gg)
+#pragma unroll
+                    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                        for (int q = 0; q < 4; ++q) S.red[warp][gg][nt][lane * 4 + q] = acc[gg][nt][q] + acl[gg][nt][q] + (acc2[gg][nt][q] + acl2[gg][nt][q]);
             }
-#pragma unroll
-            for (int gg = 0; gg < 2; ++gg)
-#pragma unroll
-                for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-                    for (int q = 0; q < 4; ++q) S.red[warp][gg][nt][lane * 4 + q] = acc[gg][nt][q] + acl[gg][nt][q] + (acc2[gg][nt][q] + acl2[gg][nt][q]);
             cbar();
-            for (int e = tid; e < 2 * 2 * 128; e += CTHREADS) {
-                const int gg = e >> 8, nt = (e >> 7) & 1, v = e & 127, ln = v >> 2, q = v & 3;
+            for (int e = tid; e < 2 * NT * 128; e += CTHREADS) {
+                const int gg = e / (NT * 128), nt = (e >> 7) % NT, v = e & 127, ln = v >> 2, q = v & 3;
                 float sum = 0.0f;
 #pragma unroll
-                for (int ww = 0; ww < CWARPS; ++ww) sum += S.red[ww][gg][nt][v];
+                for (int ww = 0; ww < CWARPS - 1; ++ww) sum += S.red[ww][gg][nt][v];
                 const int n = gg * 16 + (ln >> 2) + (q >= 2 ? 8 : 0), r = nt * 8 + (ln & 3) * 2 + (q & 1);
                 S.outv[n][r] = sum;
             }
             cbar();
-            // epilogue
+            // epilogue: items e = tid + 256 q (q < 2), output column g.lo + e % R, row e / R
+            const Div dR = make_div(R);
 #pragma unroll
             for (int q = 0; q < 2; ++q) {
                 const int e = tid + CTHREADS * q;
                 if (R == 0 || e >= R * c) continue;
-                const int n = e % R, r = e / R, col = g.lo + n;
-                const float v = S.outv[n][r];
+                const int r = div_q(dR, e), n = e - r * R, col = g.lo + n;
+                float v = S.outv[n][r];
+                const float4 *Fr = (const float4 *)(ring + S.ring_off[slot] + nrows * pitch);  // fold constants of the rows
+                if (fold) {
+                    const float4 F = Fr[n];
+                    v = S.st[r][5] * (S.st[r][3] * (v - S.st[r][2] * F.x) + F.y - S.st[r][4] * F.z) + F.w;
+                }
                 switch (s) {
                 case 0: case 6: a.ff[(int64_t)r * a.FF + col] = v * sigm(v); break;
                 case 1: case 7: {
                     float add = 0.5f * v;
                     if (g.kr == 0) {
-                        float b = base[q];
-                        if (s == 1 && prev) b = (b - S.st[r][0]) * S.st[r][1] * og[q] + ob[q];  // x = LN_out_{l-1}(h)
+                        float b = S.ep_base[e];
+                        if (s == 1 && l > 0) b = (b - S.st[r][0]) * S.st[r][1] * S.ep_og[n] + S.ep_ob[n];  // x = LN_out_{l-1}(h)
                         add += b;
                     }
                     red_add((s == 1 ? hB : hA) + (int64_t)r * D + col, add);
                     break;
                 }
                 case 2: w.kv[(int64_t)(pos + r) * 3 * D + col] = v; break;
-                case 3: case 5: hB[(int64_t)r * D + col] = base[q] + v; break;
-                default: {  // s == 4: GLU
-                    const float gv = v * sigm(S.outv[R + n][r]);
+                case 3: case 5: hB[(int64_t)r * D + col] = S.ep_base[e] + v; break;
+                default: {  // s == 4: GLU (gate row R + n, folded likewise)
+                    const float4 F = Fr[R + n];
+                    const float gt = S.st[r][5] * (S.st[r][3] * (S.outv[R + n][r] - S.st[r][2] * F.x) + F.y - S.st[r][4] * F.z) + F.w;
+                    const float gv = v * sigm(gt);
                     w.din[(int64_t)(pos + r) * D + col] = gv;
                     S.glu[n][r] = gv;
                     break;
@@ -707,15 +1015,17 @@ __device__ void compute(const NbEnc1Args &a, Smem &S, uint8_t *ring, uint8_t *ac
             }
             if (s == 4) {
                 // causal depthwise conv of this CTA's channels (src/kernels.metal:361-380) over rows
-                // pos - (taps - 1) .. pos + c - 1: history from registers, new rows from glu
+                // pos - (taps - 1) .. pos + c - 1: tap t of row er reads history row er + t while that
+                // precedes pos, else the GLU output of row er + t - (taps - 1)
                 cbar();
-                if (dact) {
+                if (R > 0 && tid < R * c) {
+                    const int er = div_q(dR, tid), en = tid - er * R;
                     float x = 0.0f;
 #pragma unroll
                     for (int t = 0; t < 9; ++t) {
                         if (t >= a.taps) break;
-                        const int rr = er - (a.taps - 1) + t;  // row relative to pos
-                        x += dw[t] * (rr < 0 ? hist[t] : S.glu[en][rr]);
+                        const int h = er + t;
+                        x += S.ep_dw[en * a.taps + t] * (h < a.taps - 1 ? S.ep_hist[h][en] : S.glu[en][h - (a.taps - 1)]);
                     }
                     a.att[(int64_t)er * D + g.lo + en] = x;
                 }
@@ -730,14 +1040,14 @@ __device__ void compute(const NbEnc1Args &a, Smem &S, uint8_t *ring, uint8_t *ac
     // 16 KB of stores after the last barrier)
     if (!S.abort && blockIdx.x == 0) {
         const NbEnc1Layer &w = a.L[a.layers - 1];
-        Act A;
-        gather(A, hA, D, 0, D, c);
-        float mean[MAXC], inv[MAXC];
-        row_stats(A, S, rbuf, D, a.eps, mean, inv);
+        Act<NR> A;
+        gather<NR>(A, hA, D, 0, D, c);
+        float mean[NR], inv[NR];
+        row_stats<NR>(A, S, rbuf, D, a.eps, mean, inv);
         if (4 * tid < D) {
             const float4 gg = ld4g(w.ln_out_g + 4 * tid), bb = ld4g(w.ln_out_b + 4 * tid);
 #pragma unroll
-            for (int u = 0; u < MAXC; ++u) {
+            for (int u = 0; u < NR; ++u) {
                 if (u >= c) break;
                 const float y[4] = { (A.x[u].x - mean[u]) * inv[u] * gg.x + bb.x, (A.x[u].y - mean[u]) * inv[u] * gg.y + bb.y,
                                      (A.x[u].z - mean[u]) * inv[u] * gg.z + bb.z, (A.x[u].w - mean[u]) * inv[u] * gg.w + bb.w };
@@ -753,11 +1063,13 @@ __device__ void compute(const NbEnc1Args &a, Smem &S, uint8_t *ring, uint8_t *ac
     }
 }
 
+template <int NR>
 __global__ void __launch_bounds__(THREADS, 1) encoder1_kernel(const __grid_constant__ NbEnc1Args a) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t *ring = smem_raw;
     uint8_t *act = smem_raw + a.ring_bytes;
-    Smem &S = *(Smem *)(act + ACT_BYTES);
+    const int abytes = act_bytes(a.c, a.Lmax);
+    Smem &S = *(Smem *)(act + abytes);
     if (threadIdx.x == 0) {
         for (int s = 0; s < NB; ++s) sm100::mbar_init(&S.full[s], 1);
         S.abort = 0;
@@ -769,13 +1081,13 @@ __global__ void __launch_bounds__(THREADS, 1) encoder1_kernel(const __grid_const
         const int st = threadIdx.x;
         const Geo g = stage_geo(a, 0, st, blockIdx.x, gridDim.x);
         S.g_lo[st] = g.lo; S.g_hi[st] = g.hi; S.g_kr[st] = g.kr; S.g_krw[st] = g.krw;
-        S.g_rows[st] = geo_rows(g); S.g_pitch[st] = geo_pitch(g);
+        S.g_rows[st] = geo_rows(g); S.g_pitch[st] = geo_pitch(g); S.g_bytes[st] = geo_rows(g) * stage_row_bytes(st, g.krw);
         S.g_img[st] = image_offset(a, 0, st, g, blockIdx.x, gridDim.x);
     }
     // activation rows past c stay zero for the whole launch (the MMAs read 8 or 16 rows)
-    for (int i = threadIdx.x; i < ACT_BYTES / 16; i += THREADS) ((uint4 *)act)[i] = make_uint4(0u, 0u, 0u, 0u);
+    for (int i = threadIdx.x; i < abytes / 16; i += THREADS) ((uint4 *)act)[i] = make_uint4(0u, 0u, 0u, 0u);
     __syncthreads();
-    compute(a, S, ring, act);
+    compute<NR>(a, S, ring, act);
     __syncthreads();
     // copies requested but never taken (an abandoned launch): wait for them (bounded) before the
     // CTA's shared memory goes away. At most NB entries are in flight, each in its own slot.
@@ -787,8 +1099,9 @@ __global__ void __launch_bounds__(THREADS, 1) encoder1_kernel(const __grid_const
 }  // namespace
 
 // Bytes of the weight ring for a model of width D / FF on `grid` CTAs with `smem_optin` bytes of
-// shared memory per CTA; 0 when the ring could not hold two of the largest entries.
-extern "C" int nb_encoder1_ring_bytes(int D, int FF, int grid, size_t smem_optin) {
+// shared memory per CTA, chunks of up to cmax rows and attention windows of up to Lmax rows; 0
+// when the ring could not hold two of the largest entries.
+extern "C" int nb_encoder1_ring_bytes(int D, int FF, int grid, size_t smem_optin, int cmax, int Lmax) {
     int biggest = 0;
     const int outs[NSTAGE] = { FF, D, 3 * D, D, D, D, FF, D }, Ks[NSTAGE] = { D, FF, D, D, D, D, D, FF }, mult[NSTAGE] = { 1, 1, 1, 1, 2, 1, 1, 1 };
     for (int s = 0; s < NSTAGE; ++s) {
@@ -796,22 +1109,38 @@ extern "C" int nb_encoder1_ring_bytes(int D, int FF, int grid, size_t smem_optin
         if (groups < 1) return 0;
         const int R = (outs[s] + groups - 1) / groups;
         if (mult[s] * R > MAXR) return 0;
-        const int b = mult[s] * R * (krw * 2 + 16);
+        const int b = mult[s] * R * stage_row_bytes(s, krw);
         if (b > biggest) biggest = b;
     }
-    const long long avail = (long long)smem_optin - ACT_BYTES - (long long)sizeof(Smem) - 1024;
+    const long long avail = (long long)smem_optin - act_bytes(cmax, Lmax) - (long long)sizeof(Smem) - 1024;
     const long long ring = avail / 128 * 128;
     return ring >= 2LL * biggest ? (int)ring : 0;
 }
 
-extern "C" size_t nb_encoder1_smem(int ring_bytes) { return (size_t)ring_bytes + ACT_BYTES + sizeof(Smem); }
+extern "C" size_t nb_encoder1_smem(int ring_bytes, int c, int Lmax) { return (size_t)ring_bytes + act_bytes(c, Lmax) + sizeof(Smem); }
 
 extern "C" size_t nb_encoder1_image_bytes(int D, int FF, int layers) { return (size_t)layers * (size_t)layer_image_bytes(D, FF); }
 
-// Builds the weight image for a persistent grid of `grid` CTAs (args: the layer table and widths).
-extern "C" int nb_encoder1_repack(const NbEnc1Args *args, int grid, uint8_t *image, void *stream) {
+// Bytes of the LayerNorm fold constants: per block one float4 per row of the folded projections,
+// then two float4 of LN_out sums per block.
+extern "C" size_t nb_encoder1_fold_bytes(int D, int FF, int layers) { return (size_t)layers * (size_t)(fold_rows(D, FF) + 2) * 16; }
+
+// Builds the weight image for a persistent grid of `grid` CTAs and the LayerNorm fold constants
+// (args: the layer table and widths).
+extern "C" int nb_encoder1_repack(const NbEnc1Args *args, int grid, uint8_t *image, float *fold, void *stream) {
     if (!image || ((uintptr_t)image & 15)) return nb_set_error("persistent encoder: weight image missing or misaligned");
-    encoder1_repack_kernel<<<dim3(grid, NSTAGE, args->layers), 256, 0, (cudaStream_t)stream>>>(*args, image);
+    if (!fold || ((uintptr_t)fold & 15)) return nb_set_error("persistent encoder: fold constants missing or misaligned");
+    NbEnc1Args a = *args;
+    a.fold = fold;  // the repack kernel copies the constants into the image
+    cudaStream_t st = (cudaStream_t)stream;
+    const int maxrows = a.FF > 3 * a.D ? a.FF : 3 * a.D;
+    if (cudaMemsetAsync(fold, 0, nb_encoder1_fold_bytes(a.D, a.FF, a.layers), st) != cudaSuccess)
+        return nb_set_error("persistent encoder: %s", cudaGetErrorString(cudaGetLastError()));
+    encoder1_fold_kernel<<<dim3((maxrows + 7) / 8, 4, a.layers), 256, 0, st>>>(a, (float4 *)fold);
+    if (nb_check_launch("encoder1_fold_kernel")) return -1;
+    encoder1_lnsum_kernel<<<a.layers, 32, 0, st>>>(a, (float4 *)fold + (size_t)a.layers * fold_rows(a.D, a.FF));
+    if (nb_check_launch("encoder1_lnsum_kernel")) return -1;
+    encoder1_repack_kernel<<<dim3(grid, NSTAGE, a.layers), 256, 0, st>>>(a, image);
     return nb_check_launch("encoder1_repack_kernel");
 }
 
@@ -824,9 +1153,11 @@ extern "C" int nb_encoder1(const NbEnc1Args *args, int grid, void *stream) {
     if (a.Lmax > MAXL) return nb_set_error("persistent encoder: attention window %d above %d rows", a.Lmax, MAXL);
     if (a.taps < 1 || a.taps > 9) return nb_set_error("persistent encoder: depthwise kernel of %d taps (1..9)", a.taps);
     if (!a.h2 || a.h2 == a.h) return nb_set_error("persistent encoder: needs two residual buffers");
-    if (!a.image) return nb_set_error("persistent encoder: no weight image");
-    const size_t smem = nb_encoder1_smem(a.ring_bytes);
-    if (nb_smem_attr((const void *)encoder1_kernel, smem)) return nb_set_error("persistent encoder: %s", nemo_gpu_last_error());
+    if (!a.image || !a.fold) return nb_set_error("persistent encoder: no weight image or fold constants");
+    const size_t smem = nb_encoder1_smem(a.ring_bytes, a.c, a.Lmax);
+    // rows <= 8: one MMA column tile and half the registers of the 16-row form
+    const void *fn = a.c <= 8 ? (const void *)encoder1_kernel<8> : (const void *)encoder1_kernel<16>;
+    if (nb_smem_attr(fn, smem)) return nb_set_error("persistent encoder: %s", nemo_gpu_last_error());
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
     cfg.blockDim = dim3(THREADS);
@@ -839,6 +1170,7 @@ extern "C" int nb_encoder1(const NbEnc1Args *args, int grid, void *stream) {
     cfg.numAttrs = 1;
     if (cudaMemsetAsync(a.bar, 0, 2 * sizeof(unsigned), (cudaStream_t)stream) != cudaSuccess)
         return nb_set_error("persistent encoder: %s", cudaGetErrorString(cudaGetLastError()));
-    if (cudaLaunchKernelEx(&cfg, encoder1_kernel, a) != cudaSuccess) return nb_set_error("persistent encoder: %s", cudaGetErrorString(cudaGetLastError()));
+    const cudaError_t e = a.c <= 8 ? cudaLaunchKernelEx(&cfg, encoder1_kernel<8>, a) : cudaLaunchKernelEx(&cfg, encoder1_kernel<16>, a);
+    if (e != cudaSuccess) return nb_set_error("persistent encoder: %s", cudaGetErrorString(cudaGetLastError()));
     return nb_check_launch("encoder1_kernel");
 }

@@ -234,6 +234,7 @@ void nb_model_free(nb_model_t *m) {
     if (!m) return;
     if (m->arena) cudaFree(m->arena);
     if (m->enc1_image) cudaFree(m->enc1_image);
+    if (m->enc1_fold) cudaFree(m->enc1_fold);
     free(m->L);
     free(m->prompt_b0_host);
     free(m->prompt_onehot_host);

@@ -41,6 +41,7 @@ typedef struct nb_model {
     /* the encoder weights laid out for the persistent single-stream encoder on a grid of
        enc1_grid CTAs (built by the first single-stream engine, shared by all of the model's) */
     uint8_t *enc1_image;
+    float *enc1_fold;  /* and the LayerNorm fold constants of the persistent encoder */
     int enc1_grid;
 } nb_model_t;
 
