@@ -44,6 +44,36 @@ __device__ __forceinline__ float warp_max(float v) {
     return v;
 }
 
+// Butterfly of V values per lane over the warp (V a power of two, 2 <= V <= 128): at the step with
+// lane offset O each lane keeps the half of its values selected by (lane & O) and adds its
+// partner's copy of that half; once one value is left the remaining steps add it plainly. After it,
+// lane l holds in x[j] (j < max(V / 32, 1)) the warp's total of value l * V / 32 + j (V >= 32) or,
+// in x[0], of value l >> (5 - log2 V) (V < 32: l >> 1 for 16 values). (Templates, so that every
+// index is a constant and the values stay in registers.)
+template <int N, int O>
+struct WarpFold {
+    static __device__ __forceinline__ void run(float *x, int lane) {
+        if constexpr (O > 0) {
+            if constexpr (N > 1) {
+                constexpr int H = N / 2;
+                const bool up = (lane & O) != 0;
+#pragma unroll
+                for (int j = 0; j < H; ++j) {
+                    const float send = up ? x[j] : x[j + H];
+                    const float keep = up ? x[j + H] : x[j];
+                    x[j] = keep + __shfl_xor_sync(0xffffffffu, send, O);
+                }
+                WarpFold<H, O / 2>::run(x, lane);
+            } else {
+                x[0] += __shfl_xor_sync(0xffffffffu, x[0], O);
+                WarpFold<1, O / 2>::run(x, lane);
+            }
+        }
+    }
+};
+template <int V>
+__device__ __forceinline__ void warp_fold(float (&x)[V]) { WarpFold<V, 16>::run(x, threadIdx.x & 31); }
+
 // Block-wide sum for blockDim.x == NT (multiple of 32); red must hold NT/32 floats.
 template <int NT>
 __device__ __forceinline__ float block_sum(float v, float *red) {

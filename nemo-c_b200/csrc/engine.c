@@ -65,7 +65,7 @@ struct nb_engine {
        chunk rows; NEMO_GRAPHS=0 launches kernel by kernel instead */
     int use_graphs;
     /* one stream: the conformer blocks run as one persistent kernel (NEMO_PERSISTENT=0 disables) */
-    int use_enc1, enc1_grid, enc1_slot;
+    int use_enc1, enc1_grid, enc1_optin;
     NbEnc1Layer *enc1_layers;  /* host copy, passed by value at each launch */
     uint8_t *enc1_image;       /* the model's weights laid out per CTA of the persistent grid (owned by the model) */
     float *enc1_fold;          /* and its LayerNorm fold constants (owned by the model) */
@@ -127,8 +127,8 @@ static int enc1_setup(nb_engine_t *e, char *err, size_t errlen) {
         return 0;
     /* per-CTA weight rows must fit the kernel's 32-row accumulator tiles and two of the largest
        entries its weight ring (0 otherwise) */
-    const int ring = nb_encoder1_ring_bytes(D, FF, sms, (size_t)optin, e->cmax, e->Lmax);
-    if (!ring || nb_encoder1_smem(ring, e->cmax, e->Lmax) > (size_t)optin) return 0;
+    const int ring = nb_encoder1_ring_bytes(D, FF, sms, (size_t)optin, e->cmax, e->left + e->cmax);  /* the largest chunk */
+    if (!ring || nb_encoder1_smem(ring, e->cmax, e->left + e->cmax) > (size_t)optin) return 0;
     NbEnc1Layer *L = calloc((size_t)g->n_layers, sizeof *L);
     const size_t kv_s = (size_t)e->cap_rows * 3 * D, din_s = (size_t)e->cap_rows * D;
     for (int l = 0; l < g->n_layers; ++l) {
@@ -179,7 +179,7 @@ static int enc1_setup(nb_engine_t *e, char *err, size_t errlen) {
     if (rc) { snprintf(err, errlen, "persistent encoder set-up: %s", cudaGetErrorString(cudaGetLastError())); return -1; }
     e->use_enc1 = 1;
     e->enc1_grid = sms;
-    e->enc1_slot = ring;
+    e->enc1_optin = optin;
     return 0;
 }
 
@@ -694,7 +694,8 @@ static int launch_encoder(nb_engine_t *e, int nwin, int c) {
         memset(q, 0, sizeof *q);
         memcpy(q->L, e->enc1_layers, (size_t)g->n_layers * sizeof *e->enc1_layers);
         q->layers = g->n_layers; q->D = D; q->FF = FF; q->H = g->n_heads; q->taps = g->conv_kernel; q->Lmax = e->Lmax; q->c = c;
-        q->ring_bytes = e->enc1_slot;
+        q->left = e->left;
+        q->ring_bytes = nb_encoder1_ring_bytes(D, FF, e->enc1_grid, (size_t)e->enc1_optin, c, e->left + c);  /* per chunk shape */
         q->eps = eps; q->scale = 1.0f / sqrtf(128.0f);
         q->pos = d_pos; q->cache_len = d_cache_len;
         q->h = h; q->h2 = hn; q->ff = e->ff; q->att = e->att; q->image = e->enc1_image; q->fold = e->enc1_fold;

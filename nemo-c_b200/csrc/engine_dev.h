@@ -39,6 +39,7 @@ typedef struct {
 typedef struct {
     NbEnc1Layer L[NB_ENC1_MAX_LAYERS]; /* by value: the kernel reads it from its parameter space */
     int layers, D, FF, H, taps, Lmax, c, ring_bytes;
+    int left;                   /* attention history rows at most: windows of left + c rows */
     float eps, scale;
     const int *pos, *cache_len; /* device words */
     float *h;                   /* [c][D] residual stream: pre-encode output in, last block's output out */
@@ -72,8 +73,8 @@ int nb_decoder1_fits(int PH, int JH, int V, int grid, int cmax, size_t smem_opti
 size_t nb_decoder1_smem(int PH, int JH, int V, int grid, int c);
 
 int nb_encoder1(const NbEnc1Args *args, int grid, void *stream);
-int nb_encoder1_ring_bytes(int D, int FF, int grid, size_t smem_optin, int cmax, int Lmax);
-size_t nb_encoder1_smem(int ring_bytes, int c, int Lmax);
+int nb_encoder1_ring_bytes(int D, int FF, int grid, size_t smem_optin, int c, int Lw);
+size_t nb_encoder1_smem(int ring_bytes, int c, int Lw);
 size_t nb_encoder1_image_bytes(int D, int FF, int layers);
 size_t nb_encoder1_fold_bytes(int D, int FF, int layers);
 int nb_encoder1_repack(const NbEnc1Args *args, int grid, uint8_t *image, float *fold, void *stream);

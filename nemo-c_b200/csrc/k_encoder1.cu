@@ -56,34 +56,30 @@ constexpr int NSTAGE = 8;                // projections per block
 constexpr long long WAIT_LIMIT = 2000000000LL;  // clock cycles (~1 s)
 
 struct Smem {
-    float red[CWARPS - 1][2][2][128];  // per-warp partial accumulators of the MMA warps
+    float red[CWARPS][2][2][128];  // per-warp partial accumulators
     float outv[MAXR][MAXC];        // reduced outputs [weight row][activation row]
     float st[MAXC][8];             // per row: LN_out mean, inv of the block input (FF1a, read by FF1b);
                                    // the stage's folded statistics mu1, inv1, mu2, inv2
     float rs[2][CWARPS][2 * MAXC]; // per-warp row sums (two buffers)
     float fs[CWARPS][128];         // per-warp row sums of a folded LayerNorm
-    float ep_base[MAXR * MAXC];    // residual values of the epilogue items
-    float ep_og[MAXR], ep_ob[MAXR];  // LN_out vectors of the output columns (FF1b)
-    float ep_dw[16 * 9];           // depthwise taps of the CTA's channels [channel][tap]
-    float ep_hist[8][16];          // conv history rows [pos - (taps - 1) + h][channel]
     float glu[16][MAXC];           // conv-module GLU outputs of this CTA's channels
     float sc[MAXL];                // attention scores / probabilities
     float vpart[2][128];           // attention value halves
     uint64_t full[NB];
     int ring_off[NB];              // byte offset of projection i's rows in the ring (slot i % NB)
-    int ring_size[NB];             // and its bytes
     int g_lo[NSTAGE], g_hi[NSTAGE], g_kr[NSTAGE], g_krw[NSTAGE], g_rows[NSTAGE], g_pitch[NSTAGE], g_bytes[NSTAGE];
     long long g_img[NSTAGE];       // byte offset of this CTA's block of projection s in block 0 of the image
     int consumed;                  // projections taken by the compute warps (set when they stop)
     int issued;                    // projections requested so far
     int abort;
 };
-// Bytes of the activation area for chunks of up to c rows and an attention window of Lmax rows:
+// Bytes of the activation area for chunks of up to c rows and attention windows of up to Lw rows:
 // the bf16 hi and lo planes of the NR-row tile (NR rows each, the lo plane NR * APITCH bytes
 // after the hi plane), or the attention stage's value rows, whichever is larger.
-__host__ __device__ inline int act_rows(int c) { return c <= 8 ? 8 : 16; }
-__host__ __device__ inline int act_bytes(int c, int Lmax) {
-    const int tile = 2 * act_rows(c) * APITCH, vals = Lmax * 512;
+// (The 8-row form serves chunks of up to 8 rows with attention windows of up to 64 rows.)
+__host__ __device__ inline int act_rows(int c, int Lw) { return c <= 8 && Lw <= 64 ? 8 : 16; }
+__host__ __device__ inline int act_bytes(int c, int Lw) {
+    const int tile = 2 * act_rows(c, Lw) * APITCH, vals = Lw * 512;
     return ((tile > vals ? tile : vals) + 127) / 128 * 128;
 }
 
@@ -243,73 +239,58 @@ __global__ void encoder1_repack_kernel(const __grid_constant__ NbEnc1Args a, uin
 
 // ---- weight ring: the CTA's weight rows of every projection, in order ---------------------------
 // Warp ISSUE_WARP requests projections `issued`, `issued` + 1, ... (below `limit`) while they fit: at
-// most NB in flight, and
-// their bytes not overlapping any entry the compute warps have not released yet (released =
-// `consumed`; entries are released in order). Called at the start and at the beginning of every
-// stage's math, which touches only shared memory: issued at a grid barrier instead, the requests
-// (one ~57 KB copy per CTA at once) delay the barrier's own few latency-critical accesses.
-__device__ void issue_ahead(const NbEnc1Args &a, Smem &S, uint8_t *ring, int &issued, int &head, int consumed, uint64_t pol, int limit) {
+// most NB in flight, and their bytes not overlapping any entry the compute warps have not released
+// yet (released = `consumed`; entries are released in order). The warp keeps the ring table in
+// registers (lane j: the entry in slot j; lane s < NSTAGE: projection type s's bytes and image
+// offset), so a request costs a vote and one bulk copy, and the compute warps find each entry's
+// offset in S.ring_off. Called at the start, before a stage's weights are waited for (if they were
+// not requested yet), and during every stage's math, which touches only shared memory: issued at a
+// grid barrier instead, the requests (one ~57 KB copy per CTA at once) delay the barrier's own few
+// latency-critical accesses.
+struct Ring {
+    int o, z, j;     // lane's slot: byte offset, bytes, projection (-1: none)
+    int bytes;       // lane s < NSTAGE: bytes of projection type s
+    long long img;   // and its offset in block 0 of the image
+    int issued, head;
+};
+__device__ __forceinline__ void ring_init(const Smem &S, Ring &q) {
+    const int lane = threadIdx.x & 31;
+    q.o = q.z = 0;
+    q.j = -1;
+    q.bytes = lane < NSTAGE ? S.g_bytes[lane] : 0;
+    q.img = lane < NSTAGE ? S.g_img[lane] : 0;
+    q.issued = q.head = 0;
+}
+__device__ void issue_ahead(const NbEnc1Args &a, Smem &S, uint8_t *ring, Ring &q, int consumed, uint64_t pol, int limit) {
     if ((threadIdx.x >> 5) != ISSUE_WARP) return;
     const int lane = threadIdx.x & 31, RB = a.ring_bytes;
     const long long layer_bytes = layer_image_bytes(a.D, a.FF);
     limit = min(limit, a.layers * NSTAGE);
-    while (issued < limit && issued - consumed < NB) {
-        const int i = issued, st = i % NSTAGE;
-        const int sz = S.g_bytes[st];
-        const int off = head + sz > RB ? 0 : head;
-        bool clash = false;
-        for (int j = consumed; j < i && !clash; ++j) {
-            const int o = S.ring_off[j % NB], z = S.ring_size[j % NB];
-            clash = z > 0 && sz > 0 && o < off + sz && off < o + z;
-        }
-        if (clash) break;
-        __syncwarp();  // every lane has read the ring table before lane 0 updates it
+    while (q.issued < limit && q.issued - consumed < NB) {
+        const int i = q.issued, st = i % NSTAGE, slot = i % NB;
+        const int sz = __shfl_sync(0xffffffffu, q.bytes, st);
+        const long long img = __shfl_sync(0xffffffffu, q.img, st);
+        const int off = q.head + sz > RB ? 0 : q.head;
+        const bool live = lane < NB && q.j >= consumed && q.j < i;
+        if (__any_sync(0xffffffffu, live && q.z > 0 && sz > 0 && q.o < off + sz && off < q.o + q.z)) break;
+        if (lane == slot) { q.o = off; q.z = sz; q.j = i; }
         if (lane == 0) {
-            S.ring_off[i % NB] = off;
-            S.ring_size[i % NB] = sz;
+            S.ring_off[slot] = off;
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // the bytes' earlier generic reads before the copies
-            sm100::mbar_arrive_expect_tx(&S.full[i % NB], (uint32_t)sz);
+            sm100::mbar_arrive_expect_tx(&S.full[slot], (uint32_t)sz);
+            if (sz > 0) bulk_g2s_stream(ring + off, a.image + (long long)(i / NSTAGE) * layer_bytes + img, (uint32_t)sz, &S.full[slot], pol);
         }
-        __syncwarp();
-        if (lane == 0 && sz > 0)
-            bulk_g2s_stream(ring + off, a.image + (long long)(i / NSTAGE) * layer_bytes + S.g_img[st], (uint32_t)sz, &S.full[i % NB], pol);
-        head = off + sz;
-        issued = i + 1;
+        q.head = off + sz;
+        q.issued = i + 1;
     }
-    if (lane == 0) S.issued = issued;
+    if (lane == 0) S.issued = q.issued;
 }
 
 // ---- compute warps -----------------------------------------------------------------------------
 
-// Butterfly of V values per lane over the warp (V a power of two, 16 <= V <= 128): at the step with
-// lane offset O each lane keeps the half of its values selected by (lane & O) and adds its
-// partner's copy of that half; once one value is left the remaining steps add it plainly. After it,
-// lane l holds in x[j] (j < max(V / 32, 1)) the warp's total of value l * V / 32 + j (V >= 32) or of
+// warp_fold (common.cuh): lane l ends with the warp totals of values l * V / 32 + j (V >= 32) or of
 // value l >> 1 (V = 16); stored at position lane * max(V / 32, 1) + j, value v sits at fs_pos(v).
-// (Templates, so that every index is a constant and the values stay in registers.)
-template <int N, int O>
-struct WarpFold {
-    static __device__ __forceinline__ void run(float *x, int lane) {
-        if constexpr (O > 0) {
-            if constexpr (N > 1) {
-                constexpr int H = N / 2;
-                const bool up = (lane & O) != 0;
-#pragma unroll
-                for (int j = 0; j < H; ++j) {
-                    const float send = up ? x[j] : x[j + H];
-                    const float keep = up ? x[j + H] : x[j];
-                    x[j] = keep + __shfl_xor_sync(0xffffffffu, send, O);
-                }
-                WarpFold<H, O / 2>::run(x, lane);
-            } else {
-                x[0] += __shfl_xor_sync(0xffffffffu, x[0], O);
-                WarpFold<1, O / 2>::run(x, lane);
-            }
-        }
-    }
-};
-template <int V>
-__device__ __forceinline__ void warp_fold(float (&x)[V]) { WarpFold<V, 16>::run(x, threadIdx.x & 31); }
+using nb::warp_fold;
 
 // Sums over the compute threads of two values per row (every thread gets the totals), NR rows
 // (8 or 16). One butterfly per warp reduces all 2 NR values at once: at the step with lane offset
@@ -456,7 +437,10 @@ __device__ __forceinline__ void frag_mma(const Frag &f, int ng, int nnt, float (
 // the barrier the item requests everything it needs at once: the query, key and position rows to
 // registers, the value rows through registers into shared memory (16-byte L2 loads spread over all
 // threads; they are needed last).
+// LM: the window's rows at most (64 for the 8-row form, 72 for the 16-row one), LM / 8 keys per warp.
+template <int LM>
 __device__ __forceinline__ void attention_item(const NbEnc1Args &a, Smem &S, uint8_t *act, const NbEnc1Layer &w, int hd, int r, int pos, int cache_len) {
+    constexpr int KI = LM / CWARPS;
     const int D = a.D, c = a.c, L = cache_len + c, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int64_t ld = 3 * (int64_t)D;
     const int off = hd * 128;
@@ -464,12 +448,12 @@ __device__ __forceinline__ void attention_item(const NbEnc1Args &a, Smem &S, uin
     const float *Vb = Kb + D;
     const float *Pb = w.ptab + (int64_t)(a.Lmax - L + c - 1 - r) * D + off;
     float *Vs = (float *)act;  // [L][128]: the activation tile is idle here
-    // query (lane's 4 dims) and this warp's keys j = warp + 8 i (i < 9 covers L <= 72)
+    // query (lane's 4 dims) and this warp's keys j = warp + 8 i (i < KI covers L <= LM)
     const float4 q4 = __ldcg((const float4 *)(w.kv + (int64_t)(pos + r) * ld + off + 4 * lane));
     const float4 u4 = ld4g(w.bias_u + off + 4 * lane), v4 = ld4g(w.bias_v + off + 4 * lane);
-    float4 k4[9], p4[9];
+    float4 k4[KI], p4[KI];
 #pragma unroll
-    for (int i = 0; i < 9; ++i) {
+    for (int i = 0; i < KI; ++i) {
         const int j = warp + CWARPS * i;
         if (j < L) {
             k4[i] = __ldcg((const float4 *)(Kb + (int64_t)j * ld + 4 * lane));
@@ -478,7 +462,7 @@ __device__ __forceinline__ void attention_item(const NbEnc1Args &a, Smem &S, uin
     }
     // value rows: element e = row e / 32, columns 4 (e % 32) .. +3; every load in flight at once,
     // stored to shared memory after the scores
-    constexpr int VIT = MAXL * 32 / CTHREADS;
+    constexpr int VIT = LM * 32 / CTHREADS;
     float4 vv[VIT];
 #pragma unroll
     for (int q = 0; q < VIT; ++q) {
@@ -487,20 +471,21 @@ __device__ __forceinline__ void attention_item(const NbEnc1Args &a, Smem &S, uin
     }
     const float4 qu = make_float4(q4.x + u4.x, q4.y + u4.y, q4.z + u4.z, q4.w + u4.w);
     const float4 qv = make_float4(q4.x + v4.x, q4.y + v4.y, q4.z + v4.z, q4.w + v4.w);
-    // this lane's part of the nine scores (q + u).k_j + (q + v).p_j, all nine reduced over the warp
-    // by one butterfly (lane 2 i then holds score i)
+    // this lane's part of the KI scores (q + u).k_j + (q + v).p_j, all reduced over the warp by one
+    // butterfly (lane 2 i then holds score i)
+    static_assert(KI <= 16, "scores of one butterfly");
     float sv[16];
 #pragma unroll
     for (int i = 0; i < 16; ++i) {
         const int j = warp + CWARPS * i;
         sv[i] = 0.0f;
-        if (i < 9 && j < L)
+        if (i < KI && j < L)
             sv[i] = (qu.x * k4[i].x + qu.y * k4[i].y + qu.z * k4[i].z + qu.w * k4[i].w) + (qv.x * p4[i].x + qv.y * p4[i].y + qv.z * p4[i].z + qv.w * p4[i].w);
     }
     warp_fold<16>(sv);
     {
         const int i = lane >> 1, j = warp + CWARPS * i;
-        if ((lane & 1) == 0 && i < 9 && j < L) S.sc[j] = sv[0] * a.scale;
+        if ((lane & 1) == 0 && i < KI && j < L) S.sc[j] = sv[0] * a.scale;
     }
 #pragma unroll
     for (int q = 0; q < VIT; ++q) {
@@ -771,79 +756,6 @@ __device__ __forceinline__ void fold_stats(Smem &S, int u, bool two, int K, floa
     S.st[u][2] = mu1; S.st[u][3] = inv1; S.st[u][4] = mu2; S.st[u][5] = inv2;
 }
 
-// The issue warp's part of a stage, while the other warps run the MMAs: the weight requests; what
-// the epilogue reads, brought into shared memory (residual values of the outputs, LN_out vectors,
-// depthwise taps and conv history); the statistics of a folded LayerNorm; the layer prefetches.
-// Its loads are all issued before their first use. (The fold constants of the CTA's weight rows
-// arrive with the rows in the ring.)
-struct StagePrep {
-    int l, s, mode, lo, R, kr, nrows, pos, cache_len, pos_rows0, pos_rows;
-    const float *resid;
-};
-template <int NR>
-__device__ void stage_prep(const NbEnc1Args &a, Smem &S, uint8_t *ring, int &issued, int &head, int gi, uint64_t pol, const StagePrep &p) {
-    const int lane = threadIdx.x & 31, c = a.c, D = a.D, R = p.R, s = p.s;
-    issue_ahead(a, S, ring, issued, head, gi, pol, 1 << 30);
-    const bool fold = p.mode == P_LN || p.mode == P_LN2, two = p.mode == P_LN2;
-    const bool need_base = ((s == 1 || s == 7) && p.kr == 0) || s == 3 || s == 5;
-    const bool need_ln = s == 1 && p.kr == 0 && p.l > 0;
-    const NbEnc1Layer &w = a.L[p.l];
-    const Div dR = make_div(R);
-    constexpr int QB = MAXR * MAXC / 32;
-    float vb[QB];
-#pragma unroll
-    for (int q = 0; q < QB; ++q) {
-        const int e = lane + 32 * q, r = div_q(dR, e);
-        vb[q] = 0.0f;
-        if (need_base && e < R * c) vb[q] = __ldcg(p.resid + (int64_t)r * D + p.lo + (e - r * R));
-    }
-    float og = 1.0f, ob = 0.0f;
-    if (need_ln && lane < R) { og = __ldg(a.L[p.l - 1].ln_out_g + p.lo + lane); ob = __ldg(a.L[p.l - 1].ln_out_b + p.lo + lane); }
-    float4 G0 = make_float4(0.f, 0.f, 0.f, 0.f);
-    float G4 = 0.0f;
-    if (two) {
-        const float4 *ls = (const float4 *)a.fold + (int64_t)a.layers * fold_rows(D, a.FF) + 2 * p.l;
-        G0 = __ldg(ls);
-        G4 = __ldg(ls + 1).x;
-    }
-    float dw[5], hs[4];
-    if (s == 4) {
-#pragma unroll
-        for (int q = 0; q < 5; ++q) {
-            const int e = lane + 32 * q;
-            dw[q] = e < R * a.taps ? __ldg(w.dw_w + (int64_t)p.lo * a.taps + e) : 0.0f;
-        }
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-            const int e = lane + 32 * q;
-            const int h = div_q(dR, e);
-            hs[q] = e < (a.taps - 1) * R ? __ldcg(w.din + (int64_t)(p.pos - (a.taps - 1) + h) * D + p.lo + (e - h * R)) : 0.0f;
-        }
-    }
-    // the statistics (shared memory only) while the loads are in flight
-    if (fold && lane < c) fold_stats<NR>(S, lane, two, D, a.eps, G0, G4);
-#pragma unroll
-    for (int q = 0; q < QB; ++q) {
-        const int e = lane + 32 * q;
-        if (need_base && e < R * c) S.ep_base[e] = vb[q];
-    }
-    if (need_ln && lane < R) { S.ep_og[lane] = og; S.ep_ob[lane] = ob; }
-    if (s == 4) {
-#pragma unroll
-        for (int q = 0; q < 5; ++q) {
-            const int e = lane + 32 * q;
-            if (e < R * a.taps) S.ep_dw[e] = dw[q];
-        }
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-            const int e = lane + 32 * q;
-            const int h = div_q(dR, e);
-            if (e < (a.taps - 1) * R) S.ep_hist[h][e - h * R] = hs[q];
-        }
-    }
-    if (s == 0) prefetch_layer(a, p.l + 2, p.pos, p.cache_len, p.pos_rows0, p.pos_rows);
-}
-
 // NR: activation rows handled per stage (8 when c <= 8, else 16), NR / 8 MMA column tiles.
 template <int NR>
 __device__ void compute(const NbEnc1Args &a, Smem &S, uint8_t *ring, uint8_t *act) {
@@ -857,9 +769,10 @@ __device__ void compute(const NbEnc1Args &a, Smem &S, uint8_t *ring, uint8_t *ac
     slice(D, gridDim.x, blockIdx.x, dlo, dhi);  // this CTA's columns of the D-wide buffers it zeroes
     float *hA = a.h, *hB = a.h2;                // a block runs hA -> hB (FF1b) -> hA (FF2b)
     int gi = 0;                                 // projection index
-    int issued = 0, head = 0;                   // weight ring (warp ISSUE_WARP)
+    Ring rq;                                    // weight ring (warp ISSUE_WARP)
+    ring_init(S, rq);
     const uint64_t pol = evict_first_policy();
-    issue_ahead(a, S, ring, issued, head, 0, pol, 1 << 30);
+    issue_ahead(a, S, ring, rq, 0, pol, 1 << 30);
     float4 nga, nba, ngb, nbb;  // the next stage's normalisation vectors (this thread's columns)
     stage_norm(a, 0, 0, nga, nba, ngb, nbb);
     // position-table rows this chunk's attention reads: (Lmax - L) + (c - 1 - r) + j, j < L, r < c
@@ -873,7 +786,7 @@ __device__ void compute(const NbEnc1Args &a, Smem &S, uint8_t *ring, uint8_t *ac
             if (s == 3) {
                 // attention over the cache window (the QKV stage's barrier made the rows visible)
                 const int items = a.H * c;
-                for (int it = blockIdx.x; it < items; it += gridDim.x) attention_item(a, S, act, w, it % a.H, it / a.H, pos, cache_len);
+                for (int it = blockIdx.x; it < items; it += gridDim.x) attention_item<NR == 8 ? 64 : MAXL>(a, S, act, w, it % a.H, it / a.H, pos, cache_len);
                 if (!grid_sync(a, S, epoch)) break;
             }
             struct { int lo, hi, kr, krw; } g = { S.g_lo[s], S.g_hi[s], S.g_kr[s], S.g_krw[s] };
@@ -889,6 +802,43 @@ __device__ void compute(const NbEnc1Args &a, Smem &S, uint8_t *ring, uint8_t *ac
             Act<NR> A;
             gather<NR>(A, X, ldx, g.kr * g.krw, K, c);
             const bool own = 4 * tid < K;
+            // what the epilogue needs, requested with the input rows: the residual values (and
+            // LN_out vectors) of this thread's items e = tid + 256 q, output column g.lo + e % R, row
+            // e / R; for PW1 the depthwise taps and history rows of its conv item; for a fold of two
+            // LayerNorms (issue warp) the LN_out sums of the row
+            const Div dR = make_div(R);
+            const bool need_base = ((s == 1 || s == 7) && g.kr == 0) || s == 3 || s == 5, need_ln = s == 1 && g.kr == 0 && l > 0;
+            const float *resid = (s == 1) ? hA : hB;
+            float base[2] = { 0.f, 0.f }, og[2] = { 1.f, 1.f }, ob[2] = { 0.f, 0.f };
+#pragma unroll
+            for (int q = 0; q < 2; ++q) {
+                const int e = tid + CTHREADS * q;
+                if (R > 0 && e < R * c) {
+                    const int r = div_q(dR, e), col = g.lo + (e - r * R);
+                    if (need_base) base[q] = __ldcg(resid + (int64_t)r * D + col);
+                    if (need_ln) { og[q] = __ldg(a.L[l - 1].ln_out_g + col); ob[q] = __ldg(a.L[l - 1].ln_out_b + col); }
+                }
+            }
+            const bool dact = s == 4 && R > 0 && tid < R * c;
+            const int er = div_q(dR, tid), en = tid - er * R;
+            float dw[9], hist[8];
+            if (dact) {
+                const int ch = g.lo + en;
+#pragma unroll
+                for (int t = 0; t < 9; ++t) dw[t] = t < a.taps ? __ldg(w.dw_w + ch * a.taps + t) : 0.0f;
+#pragma unroll
+                for (int t = 0; t < 8; ++t) {
+                    const int row = pos - (a.taps - 1) + er + t;  // history rows precede pos
+                    hist[t] = (t < a.taps - 1 && row < pos) ? __ldcg(w.din + (int64_t)row * D + ch) : 0.0f;
+                }
+            }
+            float4 G0 = make_float4(0.f, 0.f, 0.f, 0.f);
+            float G4 = 0.0f;
+            if (mode == P_LN2 && warp == ISSUE_WARP) {
+                const float4 *ls = (const float4 *)a.fold + (int64_t)a.layers * fold_rows(D, a.FF) + 2 * l;
+                G0 = __ldg(ls);
+                G4 = __ldg(ls + 1).x;
+            }
             // the residual buffer the next FF-out stage accumulates into starts at zero
             if (s == 0 || s == 6) {
                 float *z = s == 0 ? hB : hA;
@@ -919,22 +869,21 @@ __device__ void compute(const NbEnc1Args &a, Smem &S, uint8_t *ring, uint8_t *ac
                 }
             }
             stage_store<NR>(A, act, c, K);
-            // this projection's weight rows: requested now if the ring had no room for them while
-            // the previous entry was held (everything before gi is released here); one thread
-            // waits, the others at the barrier
-            issue_ahead(a, S, ring, issued, head, gi, pol, gi + 1);
+            // the weight stream's next requests (everything before gi is released here; the
+            // current projection's rows too if the ring had no room for them while the previous
+            // entry was held), made before the MMAs, whose shared-memory traffic would slow them; then
+            // the issue warp waits for this projection's rows, the others at the CTA barrier
+            issue_ahead(a, S, ring, rq, gi, pol, 1 << 30);
+            if (s == 0) prefetch_layer(a, l + 2, pos, cache_len, pos_rows0, pos_rows);
             const int slot = gi % NB;
-            if (tid == 0 && !sm100::mbar_wait(&S.full[slot], (gi / NB) & 1, WAIT_LIMIT)) {
+            if (tid == ISSUE_WARP * 32 && !sm100::mbar_wait(&S.full[slot], (gi / NB) & 1, WAIT_LIMIT)) {
                 S.abort = 1;
                 atomicExch(&a.bar[1], 1u);
                 atomicCAS(a.err, 0, 3);
             }
             cbar();
             if (S.abort) break;
-            if (warp == ISSUE_WARP) {
-                const StagePrep p = { l, s, mode, g.lo, R, g.kr, nrows, pos, cache_len, pos_rows0, pos_rows, (s == 1) ? hA : hB };
-                stage_prep<NR>(a, S, ring, issued, head, gi, pol, p);
-            } else {
+            {
                 float acc[2][NT][4], acl[2][NT][4], acc2[2][NT][4], acl2[2][NT][4];
 #pragma unroll
                 for (int gg = 0; gg < 2; ++gg)
@@ -944,15 +893,15 @@ __device__ void compute(const NbEnc1Args &a, Smem &S, uint8_t *ring, uint8_t *ac
                         for (int q = 0; q < 4; ++q) acc[gg][nt][q] = acl[gg][nt][q] = acc2[gg][nt][q] = acl2[gg][nt][q] = 0.0f;
                 if (nrows > 0) {
                     const uint32_t actb = sm100::smem_u32(act), wb = sm100::smem_u32(ring + S.ring_off[slot]);
-                    // k-steps of this warp (the seven MMA warps share them). Software-pipelined: the
-                    // next k-step's fragments are requested before this one's MMAs, which alternate
+                    // k-steps of this warp (the eight warps share them). Software-pipelined: the next
+                    // k-step's fragments are requested before this one's MMAs, which alternate
                     // between two accumulator sets.
-                    const int T = K / 16, kb = T / (CWARPS - 1), extra = T % (CWARPS - 1);
+                    const int T = K / 16, kb = T / CWARPS, extra = T % CWARPS;
                     const int per = kb + (warp < extra ? 1 : 0), k0 = 16 * (warp * kb + min(warp, extra));
                     Frag f[2];
                     if (per > 0) frag_load<NR>(f[0], actb, wb, pitch, nrows, k0, ng, nnt);
 #pragma unroll
-                    for (int q = 0; q < KRW / 16 / (CWARPS - 1) + 1; ++q) {
+                    for (int q = 0; q < KRW / 16 / CWARPS + 1; ++q) {
                         if (q >= per) break;
                         if (q + 1 < per) frag_load<NR>(f[(q + 1) & 1], actb, wb, pitch, nrows, k0 + (q + 1) * 16, ng, nnt);
                         if (q & 1) frag_mma<NT>(f[q & 1], ng, nnt, acc2, acl2);
@@ -967,17 +916,19 @@ __device__ void compute(const NbEnc1Args &a, Smem &S, uint8_t *ring, uint8_t *ac
                         for (int q = 0; q < 4; ++q) S.red[warp][gg][nt][lane * 4 + q] = acc[gg][nt][q] + acl[gg][nt][q] + (acc2[gg][nt][q] + acl2[gg][nt][q]);
             }
             cbar();
+            // the statistics of a folded LayerNorm (issue warp, from the per-warp sums of fold_sums),
+            // beside the reduction of the per-warp accumulators
+            if (fold && warp == ISSUE_WARP && lane < c) fold_stats<NR>(S, lane, mode == P_LN2, D, a.eps, G0, G4);
             for (int e = tid; e < 2 * NT * 128; e += CTHREADS) {
                 const int gg = e / (NT * 128), nt = (e >> 7) % NT, v = e & 127, ln = v >> 2, q = v & 3;
                 float sum = 0.0f;
 #pragma unroll
-                for (int ww = 0; ww < CWARPS - 1; ++ww) sum += S.red[ww][gg][nt][v];
+                for (int ww = 0; ww < CWARPS; ++ww) sum += S.red[ww][gg][nt][v];
                 const int n = gg * 16 + (ln >> 2) + (q >= 2 ? 8 : 0), r = nt * 8 + (ln & 3) * 2 + (q & 1);
                 S.outv[n][r] = sum;
             }
             cbar();
             // epilogue: items e = tid + 256 q (q < 2), output column g.lo + e % R, row e / R
-            const Div dR = make_div(R);
 #pragma unroll
             for (int q = 0; q < 2; ++q) {
                 const int e = tid + CTHREADS * q;
@@ -994,15 +945,15 @@ __device__ void compute(const NbEnc1Args &a, Smem &S, uint8_t *ring, uint8_t *ac
                 case 1: case 7: {
                     float add = 0.5f * v;
                     if (g.kr == 0) {
-                        float b = S.ep_base[e];
-                        if (s == 1 && l > 0) b = (b - S.st[r][0]) * S.st[r][1] * S.ep_og[n] + S.ep_ob[n];  // x = LN_out_{l-1}(h)
+                        float b = base[q];
+                        if (s == 1 && l > 0) b = (b - S.st[r][0]) * S.st[r][1] * og[q] + ob[q];  // x = LN_out_{l-1}(h)
                         add += b;
                     }
                     red_add((s == 1 ? hB : hA) + (int64_t)r * D + col, add);
                     break;
                 }
                 case 2: w.kv[(int64_t)(pos + r) * 3 * D + col] = v; break;
-                case 3: case 5: hB[(int64_t)r * D + col] = S.ep_base[e] + v; break;
+                case 3: case 5: hB[(int64_t)r * D + col] = base[q] + v; break;
                 default: {  // s == 4: GLU (gate row R + n, folded likewise)
                     const float4 F = Fr[R + n];
                     const float gt = S.st[r][5] * (S.st[r][3] * (S.outv[R + n][r] - S.st[r][2] * F.x) + F.y - S.st[r][4] * F.z) + F.w;
@@ -1018,14 +969,13 @@ __device__ void compute(const NbEnc1Args &a, Smem &S, uint8_t *ring, uint8_t *ac
                 // pos - (taps - 1) .. pos + c - 1: tap t of row er reads history row er + t while that
                 // precedes pos, else the GLU output of row er + t - (taps - 1)
                 cbar();
-                if (R > 0 && tid < R * c) {
-                    const int er = div_q(dR, tid), en = tid - er * R;
+                if (dact) {
                     float x = 0.0f;
 #pragma unroll
                     for (int t = 0; t < 9; ++t) {
                         if (t >= a.taps) break;
-                        const int h = er + t;
-                        x += S.ep_dw[en * a.taps + t] * (h < a.taps - 1 ? S.ep_hist[h][en] : S.glu[en][h - (a.taps - 1)]);
+                        const int h = er + t;  // tap t of row er: history row er + t, else GLU row h - (taps - 1)
+                        x += dw[t] * (h < a.taps - 1 ? hist[t] : S.glu[en][h - (a.taps - 1)]);
                     }
                     a.att[(int64_t)er * D + g.lo + en] = x;
                 }
@@ -1068,7 +1018,7 @@ __global__ void __launch_bounds__(THREADS, 1) encoder1_kernel(const __grid_const
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t *ring = smem_raw;
     uint8_t *act = smem_raw + a.ring_bytes;
-    const int abytes = act_bytes(a.c, a.Lmax);
+    const int abytes = act_bytes(a.c, a.left + a.c);
     Smem &S = *(Smem *)(act + abytes);
     if (threadIdx.x == 0) {
         for (int s = 0; s < NB; ++s) sm100::mbar_init(&S.full[s], 1);
@@ -1099,9 +1049,10 @@ __global__ void __launch_bounds__(THREADS, 1) encoder1_kernel(const __grid_const
 }  // namespace
 
 // Bytes of the weight ring for a model of width D / FF on `grid` CTAs with `smem_optin` bytes of
-// shared memory per CTA, chunks of up to cmax rows and attention windows of up to Lmax rows; 0
-// when the ring could not hold two of the largest entries.
-extern "C" int nb_encoder1_ring_bytes(int D, int FF, int grid, size_t smem_optin, int cmax, int Lmax) {
+// shared memory per CTA, for a chunk of c rows and attention windows of up to Lw rows (the ring
+// takes what the activation area leaves; its entries live within one launch); 0 when the ring
+// could not hold two of the largest entries.
+extern "C" int nb_encoder1_ring_bytes(int D, int FF, int grid, size_t smem_optin, int c, int Lw) {
     int biggest = 0;
     const int outs[NSTAGE] = { FF, D, 3 * D, D, D, D, FF, D }, Ks[NSTAGE] = { D, FF, D, D, D, D, D, FF }, mult[NSTAGE] = { 1, 1, 1, 1, 2, 1, 1, 1 };
     for (int s = 0; s < NSTAGE; ++s) {
@@ -1112,12 +1063,12 @@ extern "C" int nb_encoder1_ring_bytes(int D, int FF, int grid, size_t smem_optin
         const int b = mult[s] * R * stage_row_bytes(s, krw);
         if (b > biggest) biggest = b;
     }
-    const long long avail = (long long)smem_optin - act_bytes(cmax, Lmax) - (long long)sizeof(Smem) - 1024;
+    const long long avail = (long long)smem_optin - act_bytes(c, Lw) - (long long)sizeof(Smem) - 1024;
     const long long ring = avail / 128 * 128;
     return ring >= 2LL * biggest ? (int)ring : 0;
 }
 
-extern "C" size_t nb_encoder1_smem(int ring_bytes, int c, int Lmax) { return (size_t)ring_bytes + act_bytes(c, Lmax) + sizeof(Smem); }
+extern "C" size_t nb_encoder1_smem(int ring_bytes, int c, int Lw) { return (size_t)ring_bytes + act_bytes(c, Lw) + sizeof(Smem); }
 
 extern "C" size_t nb_encoder1_image_bytes(int D, int FF, int layers) { return (size_t)layers * (size_t)layer_image_bytes(D, FF); }
 
@@ -1150,13 +1101,15 @@ extern "C" int nb_encoder1(const NbEnc1Args *args, int grid, void *stream) {
     if (a.D % 128 || a.D > KRW || a.FF % 128 || (a.FF > KRW && a.FF % KRW))
         return nb_set_error("persistent encoder: unsupported widths D=%d FF=%d", a.D, a.FF);
     if (a.H * 128 != a.D) return nb_set_error("persistent encoder: heads of 128 expected");
-    if (a.Lmax > MAXL) return nb_set_error("persistent encoder: attention window %d above %d rows", a.Lmax, MAXL);
+    if (a.Lmax > MAXL || a.left < 0 || a.left + a.c > MAXL) return nb_set_error("persistent encoder: attention window %d above %d rows", a.left + a.c, MAXL);
     if (a.taps < 1 || a.taps > 9) return nb_set_error("persistent encoder: depthwise kernel of %d taps (1..9)", a.taps);
     if (!a.h2 || a.h2 == a.h) return nb_set_error("persistent encoder: needs two residual buffers");
     if (!a.image || !a.fold) return nb_set_error("persistent encoder: no weight image or fold constants");
-    const size_t smem = nb_encoder1_smem(a.ring_bytes, a.c, a.Lmax);
+    if (a.ring_bytes <= 0 || a.ring_bytes % 128) return nb_set_error("persistent encoder: weight ring of %d bytes", a.ring_bytes);
+    const size_t smem = nb_encoder1_smem(a.ring_bytes, a.c, a.left + a.c);
     // rows <= 8: one MMA column tile and half the registers of the 16-row form
-    const void *fn = a.c <= 8 ? (const void *)encoder1_kernel<8> : (const void *)encoder1_kernel<16>;
+    const bool eight = act_rows(a.c, a.left + a.c) == 8;
+    const void *fn = eight ? (const void *)encoder1_kernel<8> : (const void *)encoder1_kernel<16>;
     if (nb_smem_attr(fn, smem)) return nb_set_error("persistent encoder: %s", nemo_gpu_last_error());
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
@@ -1170,7 +1123,7 @@ extern "C" int nb_encoder1(const NbEnc1Args *args, int grid, void *stream) {
     cfg.numAttrs = 1;
     if (cudaMemsetAsync(a.bar, 0, 2 * sizeof(unsigned), (cudaStream_t)stream) != cudaSuccess)
         return nb_set_error("persistent encoder: %s", cudaGetErrorString(cudaGetLastError()));
-    const cudaError_t e = a.c <= 8 ? cudaLaunchKernelEx(&cfg, encoder1_kernel<8>, a) : cudaLaunchKernelEx(&cfg, encoder1_kernel<16>, a);
+    const cudaError_t e = eight ? cudaLaunchKernelEx(&cfg, encoder1_kernel<8>, a) : cudaLaunchKernelEx(&cfg, encoder1_kernel<16>, a);
     if (e != cudaSuccess) return nb_set_error("persistent encoder: %s", cudaGetErrorString(cudaGetLastError()));
     return nb_check_launch("encoder1_kernel");
 }
