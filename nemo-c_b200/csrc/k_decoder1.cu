@@ -83,26 +83,21 @@ __device__ __forceinline__ void copy_vec(float *dst, const float *src, int n) {
     }
 }
 
-// out[r] = sum_k W[r][k] x[k] for the nr <= 4 * NWARPS rows of a bf16 [nr][K] block in shared
-// memory; x in shared memory. Warp w takes rows w, w + 8, w + 16, w + 24 at once (lanes over k in
-// float4 steps, one pass over x for all of them), then one butterfly for the four sums.
+// out[r] = sum_k W[r][k] x[k] for the nr rows of a bf16 [nr][K] block in shared memory (row r
+// handled by warp r % 8, lanes over k in float4 steps); x in shared memory.
 __device__ __forceinline__ void rows_dot(const uint16_t *W, int nr, int K, const float *x, float *out) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    float acc[4] = { 0.0f, 0.0f, 0.0f, 0.0f };
-    for (int k = lane; k < K / 4; k += 32) {
-        const float4 xx = *(const float4 *)(x + 4 * k);
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const int r = warp + NWARPS * j;
-            if (r < nr) {
-                const uint2 q = ((const uint2 *)(W + (size_t)r * K))[k];
-                acc[j] += xx.x * nb::bf16lo(q.x) + xx.y * nb::bf16hi(q.x) + xx.z * nb::bf16lo(q.y) + xx.w * nb::bf16hi(q.y);
-            }
+    for (int r = warp; r < nr; r += NWARPS) {
+        const uint2 *w = (const uint2 *)(W + (size_t)r * K);
+        float acc = 0.0f;
+        for (int k = lane; k < K / 4; k += 32) {
+            const uint2 q = w[k];
+            const float4 xx = *(const float4 *)(x + 4 * k);
+            acc += xx.x * nb::bf16lo(q.x) + xx.y * nb::bf16hi(q.x) + xx.z * nb::bf16lo(q.y) + xx.w * nb::bf16hi(q.y);
         }
+        acc = nb::warp_sum(acc);
+        if (lane == 0) out[r] = acc;
     }
-    nb::warp_fold<4>(acc);  // lane l: the sum of row warp + 8 (l >> 3)
-    const int r = warp + NWARPS * (lane >> 3);
-    if ((lane & 7) == 0 && r < nr) out[r] = acc[0];
 }
 
 __global__ void __launch_bounds__(THREADS, 1) decoder1_kernel(const __grid_constant__ NbDec1Args a) {
@@ -218,33 +213,30 @@ __global__ void __launch_bounds__(THREADS, 1) decoder1_kernel(const __grid_const
         __syncthreads();
         const int nf = c - t;
         {
-            float bv = -INFINITY;  // this lane's frame: best logit and its index
-            int bi = 0x7fffffff;
-            // every remaining frame of a vocabulary row in one pass over k, then one butterfly for
-            // the frames' sums: lane 2 f then holds frame f's logit (and keeps its running best)
-            const int f_own = lane >> 1;
+            float bv[MAXF];
+            int bi[MAXF];
+#pragma unroll
+            for (int f = 0; f < MAXF; ++f) { bv[f] = -INFINITY; bi[f] = 0x7fffffff; }
             for (int r = warp; r < Vr; r += NWARPS) {  // rows ascend per warp: strict > keeps the lowest index
                 const uint2 *w = (const uint2 *)(Wos + (size_t)r * JH);
-                float acc[MAXF];
 #pragma unroll
-                for (int f = 0; f < MAXF; ++f) acc[f] = 0.0f;
-                for (int k = lane; k < JH / 4; k += 32) {
-                    const uint2 q = w[k];
-                    const float4 pp = *(const float4 *)(S.pred + 4 * k);
-#pragma unroll
-                    for (int f = 0; f < MAXF; ++f) {
-                        if (f < nf) {
-                            const float4 ee = *(const float4 *)(encs + (size_t)(t + f) * JH + 4 * k);
-                            acc[f] += fmaxf(ee.x + pp.x, 0.0f) * nb::bf16lo(q.x) + fmaxf(ee.y + pp.y, 0.0f) * nb::bf16hi(q.x) +
-                                      fmaxf(ee.z + pp.z, 0.0f) * nb::bf16lo(q.y) + fmaxf(ee.w + pp.w, 0.0f) * nb::bf16hi(q.y);
-                        }
+                for (int f = 0; f < MAXF; ++f) {
+                    if (f >= nf) break;
+                    const float *e = encs + (size_t)(t + f) * JH;
+                    float acc = 0.0f;
+                    for (int k = lane; k < JH / 4; k += 32) {
+                        const uint2 q = w[k];
+                        const float4 ee = *(const float4 *)(e + 4 * k), pp = *(const float4 *)(S.pred + 4 * k);
+                        acc += fmaxf(ee.x + pp.x, 0.0f) * nb::bf16lo(q.x) + fmaxf(ee.y + pp.y, 0.0f) * nb::bf16hi(q.x) +
+                               fmaxf(ee.z + pp.z, 0.0f) * nb::bf16lo(q.y) + fmaxf(ee.w + pp.w, 0.0f) * nb::bf16hi(q.y);
                     }
+                    acc = nb::warp_sum(acc) + a.bo[v0 + r];
+                    if (acc > bv[f]) { bv[f] = acc; bi[f] = v0 + r; }
                 }
-                nb::warp_fold<MAXF>(acc);
-                const float v = acc[0] + a.bo[v0 + r];
-                if (f_own < nf && v > bv) { bv = v; bi = v0 + r; }
             }
-            if ((lane & 1) == 0) { S.pv[warp][f_own] = bv; S.pi[warp][f_own] = bi; }
+            if (lane == 0)
+#pragma unroll
+                for (int f = 0; f < MAXF; ++f) { S.pv[warp][f] = bv[f]; S.pi[warp][f] = bi[f]; }
         }
         __syncthreads();
         if (tid < nf) {
