@@ -72,8 +72,8 @@ struct nb_engine {
     NbEnc1Args enc1_args;      /* launch arguments (large: the layer table travels by value) */
     /* one stream: the greedy loop of a chunk runs as one persistent kernel (NEMO_PERSISTENT=0 disables) */
     int use_dec1, dec1_grid;
-    float *d_dec1;             /* H0 [2][PH] | H1 [2][PH] | PRED [JH] | part_v [grid][16] */
-    int *d_dec1_i;             /* part_i [grid][16] | err */
+    float *d_dec1;             /* H0 [2][PH] | H1 [2][PH] | PRED [JH] | part_v [16][grid] */
+    int *d_dec1_i;             /* part_i [16][grid] | err */
     unsigned *d_dec1_bar;
     /* several streams: the greedy loop as four tensor-core GEMMs with decoder epilogues and one
        step kernel per iteration (NEMO_DEC_FUSED=0 keeps the kernel-by-kernel iteration) */

@@ -61,8 +61,8 @@ typedef struct {
     const float *enc;                     /* [c][JH] joint encoder rows of the chunk */
     float *H0, *H1;                       /* [2][PH] committed / provisional hidden state (roles swap on emission) */
     float *PRED;                          /* [JH] */
-    float *part_v;                        /* [grid][16] per-CTA best logit per frame */
-    int *part_i;                          /* [grid][16] and its vocabulary index */
+    float *part_v;                        /* [16][grid] per-CTA best logit per frame */
+    int *part_i;                          /* [16][grid] and its vocabulary index */
     unsigned *bar;                        /* [2] grid-barrier arrivals, abort flag (zeroed before each launch) */
     int *err;
     int PH, JH, V, blank, max_symbols, c;

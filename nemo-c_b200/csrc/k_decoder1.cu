@@ -160,6 +160,14 @@ __global__ void __launch_bounds__(THREADS, 1) decoder1_kernel(const __grid_const
     }
     if (pred_valid)
         for (int j = p0 + tid; j < p1; j += THREADS) a.PRED[j] = d.pred[j];
+    // the biases this thread adds, held in registers for the whole launch: gates i, f, g, o of unit
+    // u0 + tid in both layers (tid < U), prediction row p0 + tid (tid < P), vocabulary row v0 + warp
+    float b0r[4] = { 0.f, 0.f, 0.f, 0.f }, b1r[4] = { 0.f, 0.f, 0.f, 0.f }, bpr = 0.0f, bor = 0.0f;
+    if (tid < U)
+#pragma unroll
+        for (int gt = 0; gt < 4; ++gt) { b0r[gt] = a.b0[gt * PH + u0 + tid]; b1r[gt] = a.b1[gt * PH + u0 + tid]; }
+    if (tid < P) bpr = a.bp[p0 + tid];
+    if (warp < Vr) bor = a.bo[v0 + warp];
     unsigned epoch = 0;
     bool ok = grid_sync(a, S, epoch);
     if (ok && tid == 0 && !sm100::mbar_wait(&S.wbar, 0, WAIT_LIMIT)) { S.abort = 1; atomicExch(&a.bar[1], 1u); atomicCAS(a.err, 0, 2); }
@@ -172,15 +180,28 @@ __global__ void __launch_bounds__(THREADS, 1) decoder1_kernel(const __grid_const
             // ---- L0: x = [embed(last) | h0 committed] ----
             float *H0c = a.H0 + cur * PH, *H0p = a.H0 + (1 - cur) * PH;
             float *H1c = a.H1 + cur * PH, *H1p = a.H1 + (1 - cur) * PH;
-            for (int k = tid; k < PH; k += THREADS) S.x[k] = last == a.blank ? 0.0f : nb::bf2f(a.embed[(size_t)last * PH + k]);
-            copy_vec(S.x + PH, H0c, PH);
+            {
+                // the embedding row (all loads in flight at once) and the committed h0
+                uint16_t ev[4];
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    const int k = tid + q * THREADS;
+                    ev[q] = (k < PH && last != a.blank) ? a.embed[(size_t)last * PH + k] : (uint16_t)0;
+                }
+                copy_vec(S.x + PH, H0c, PH);
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    const int k = tid + q * THREADS;
+                    if (k < PH) S.x[k] = nb::bf2f(ev[q]);
+                }
+            }
             __syncthreads();
             rows_dot(W0s, 4 * U, 2 * PH, S.x, S.gates);
             __syncthreads();
             if (tid < U) {
                 const int j = u0 + tid;
-                const float ig = nb::sigmoid_f(S.gates[tid] + a.b0[j]), fg = nb::sigmoid_f(S.gates[U + tid] + a.b0[PH + j]);
-                const float gg = tanhf(S.gates[2 * U + tid] + a.b0[2 * PH + j]), og = nb::sigmoid_f(S.gates[3 * U + tid] + a.b0[3 * PH + j]);
+                const float ig = nb::sigmoid_f(S.gates[tid] + b0r[0]), fg = nb::sigmoid_f(S.gates[U + tid] + b0r[1]);
+                const float gg = tanhf(S.gates[2 * U + tid] + b0r[2]), og = nb::sigmoid_f(S.gates[3 * U + tid] + b0r[3]);
                 cp0 = fg * cc0 + ig * gg;
                 H0p[j] = og * tanhf(cp0);
             }
@@ -193,8 +214,8 @@ __global__ void __launch_bounds__(THREADS, 1) decoder1_kernel(const __grid_const
             __syncthreads();
             if (tid < U) {
                 const int j = u0 + tid;
-                const float ig = nb::sigmoid_f(S.gates[tid] + a.b1[j]), fg = nb::sigmoid_f(S.gates[U + tid] + a.b1[PH + j]);
-                const float gg = tanhf(S.gates[2 * U + tid] + a.b1[2 * PH + j]), og = nb::sigmoid_f(S.gates[3 * U + tid] + a.b1[3 * PH + j]);
+                const float ig = nb::sigmoid_f(S.gates[tid] + b1r[0]), fg = nb::sigmoid_f(S.gates[U + tid] + b1r[1]);
+                const float gg = tanhf(S.gates[2 * U + tid] + b1r[2]), og = nb::sigmoid_f(S.gates[3 * U + tid] + b1r[3]);
                 cp1 = fg * cc1 + ig * gg;
                 H1p[j] = og * tanhf(cp1);
             }
@@ -204,7 +225,7 @@ __global__ void __launch_bounds__(THREADS, 1) decoder1_kernel(const __grid_const
             __syncthreads();
             rows_dot(Wps, P, PH, S.x, S.gates);
             __syncthreads();
-            if (tid < P) a.PRED[p0 + tid] = S.gates[tid] + a.bp[p0 + tid];
+            if (tid < P) a.PRED[p0 + tid] = S.gates[tid] + bpr;
             if (!(ok = grid_sync(a, S, epoch))) break;
             pred_valid = 1;
         }
@@ -230,7 +251,7 @@ __global__ void __launch_bounds__(THREADS, 1) decoder1_kernel(const __grid_const
                         acc += fmaxf(ee.x + pp.x, 0.0f) * nb::bf16lo(q.x) + fmaxf(ee.y + pp.y, 0.0f) * nb::bf16hi(q.x) +
                                fmaxf(ee.z + pp.z, 0.0f) * nb::bf16lo(q.y) + fmaxf(ee.w + pp.w, 0.0f) * nb::bf16hi(q.y);
                     }
-                    acc = nb::warp_sum(acc) + a.bo[v0 + r];
+                    acc = nb::warp_sum(acc) + (r == warp ? bor : a.bo[v0 + r]);
                     if (acc > bv[f]) { bv[f] = acc; bi[f] = v0 + r; }
                 }
             }
@@ -247,8 +268,8 @@ __global__ void __launch_bounds__(THREADS, 1) decoder1_kernel(const __grid_const
                 const int i = S.pi[w][tid];
                 if (v > best || (v == best && i < bidx)) { best = v; bidx = i; }
             }
-            a.part_v[(size_t)blockIdx.x * MAXF + tid] = best;
-            a.part_i[(size_t)blockIdx.x * MAXF + tid] = bidx;
+            a.part_v[(size_t)tid * gridDim.x + blockIdx.x] = best;  // frame-major: one frame's maxima are contiguous
+            a.part_i[(size_t)tid * gridDim.x + blockIdx.x] = bidx;
         }
         if (!(ok = grid_sync(a, S, epoch))) break;
         // ---- decision (every CTA): argmax per frame over the CTAs, first non-blank frame ----
@@ -263,8 +284,8 @@ __global__ void __launch_bounds__(THREADS, 1) decoder1_kernel(const __grid_const
                 pv[q] = -INFINITY;
                 pix[q] = 0x7fffffff;
                 if (b < (int)gridDim.x) {
-                    pv[q] = __ldcg(a.part_v + (size_t)b * MAXF + fr);
-                    pix[q] = __ldcg(a.part_i + (size_t)b * MAXF + fr);
+                    pv[q] = __ldcg(a.part_v + (size_t)fr * gridDim.x + b);
+                    pix[q] = __ldcg(a.part_i + (size_t)fr * gridDim.x + b);
                 }
             }
             float best = -INFINITY;
