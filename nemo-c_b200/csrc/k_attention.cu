@@ -6,10 +6,11 @@
 // computed once per position row r (L + c - 1 rows) and read back diagonally.
 //
 // One CTA (8 warps) per (head, stream). The stream's V rows of the head (half of the HBM traffic
-// of the kernel) are requested as the CTA starts, 16-byte loads spread over all threads, and land
-// in shared memory once the position scores are formed; the K rows are read straight into the
-// score tiles' fragments (each 32-byte sector read whole, by one thread group). Issuing one bulk
-// copy per 512-byte row instead cost more than the transfer itself. The three products (content
+// of the kernel) are requested as the CTA starts, 16-byte asynchronous copies into shared memory
+// spread over all threads (no registers held, so three CTAs fit an SM); the K rows are read
+// straight into the score tiles' fragments by warps 0-3 (each 32-byte sector read whole, by one
+// thread group) while warps 4-7 form the position scores. Issuing one bulk copy per 512-byte row
+// instead cost more than the transfer itself. The three products (content
 // and position scores, probabilities times V) run on the
 // tensor cores as mma.sync m16n8k16 tiles (the chunk's <= 16 query rows are the M side) with
 // both operands split into bf16 hi + lo parts and three products per tile (hi.hi, hi.lo, lo.hi;
@@ -118,9 +119,15 @@ __device__ __forceinline__ void score_tile(const uint16_t *qhi, const uint16_t *
 __host__ __device__ __forceinline__ int smem_floats(int Lmax) {
     return Lmax * VP + MAXC * Lmax + MAXC * (Lmax + MAXC) + 4 * MAXC * QP / 2;
 }
-constexpr int VLOADS = (MAXL * DH / 4 + THREADS - 1) / THREADS;  // 16-byte V loads per thread
 
-__global__ void __launch_bounds__(THREADS) attention_kernel(const float *__restrict__ Q, int64_t ldq, int64_t q_sstride, const float *__restrict__ K,
+// 16-byte global -> shared copy through L2 (the rows were written by the projection just before),
+// completed by cp_async_wait_all.
+__device__ __forceinline__ void cp_async16(void *dst, const void *src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(sm100::smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory"); }
+
+__global__ void __launch_bounds__(THREADS, 3) attention_kernel(const float *__restrict__ Q, int64_t ldq, int64_t q_sstride, const float *__restrict__ K,
                                                             const float *__restrict__ V, int64_t ldk, int64_t kv_sstride, const int *pos_p,
                                                             const int *cache_len_p, const float *__restrict__ P, const float *__restrict__ bias_u,
                                                             const float *__restrict__ bias_v, void *O, int o_fmt, int64_t o_plane, int64_t o_sstride,
@@ -148,13 +155,11 @@ __global__ void __launch_bounds__(THREADS) attention_kernel(const float *__restr
         bu2[r] = *(const float2 *)(bias_u + off + k);
         bv2[r] = *(const float2 *)(bias_v + off + k);
     }
-    // the window's V rows: every load in flight now, stored to shared memory after the position
-    // scores (element e: row e / 32, columns 4 (e % 32) .. +3)
-    float4 vr[VLOADS];
-#pragma unroll
-    for (int u = 0; u < VLOADS; ++u) {
-        const int e = tid + u * THREADS, r = e >> 5;
-        vr[u] = r < L ? __ldg((const float4 *)(Vb + (int64_t)r * ldk) + (e & 31)) : make_float4(0.f, 0.f, 0.f, 0.f);
+    // the window's V rows: asynchronous 16-byte copies into shared memory, every one in flight now
+    // (element e: row e / 32, columns 4 (e % 32) .. +3), no registers held
+    for (int e = tid; e < L * 32; e += THREADS) {
+        const int r = e >> 5, c4 = 4 * (e & 31);
+        cp_async16(Vs + r * VP + c4, Vb + (int64_t)r * ldk + c4);
     }
 #pragma unroll
     for (int r = 0; r < 4; ++r) {
@@ -169,29 +174,29 @@ __global__ void __launch_bounds__(THREADS) attention_kernel(const float *__restr
         *(uint32_t *)(qul + i * QP + k) = l;
     }
     __syncthreads();
-    // position scores (q + v) . P from P (shared by all streams, L2-resident) while K and V arrive
+    // the two score products side by side: warps 0-3 the content scores (q + u) . k from the K
+    // rows, read straight from global memory (their HBM latency passes while warps 4-7 form the
+    // position scores (q + v) . P from the L2-resident table)
     const float *Pb = P + (int64_t)prow0 * D + off;
     const int ntP = (NP + 7) >> 3, ntK = (L + 7) >> 3;
-    for (int nt = warp; nt < ntP; nt += THREADS / 32) {
-        float d[4];
-        score_tile(qvh, qvl, Pb, D, nt * 8, NP, lane, d);
-        const int col = nt * 8 + 2 * t;
-        if (g < c) { if (col < NP) gp[g * gpl + col] = d[0]; if (col + 1 < NP) gp[g * gpl + col + 1] = d[1]; }
-        if (g + 8 < c) { if (col < NP) gp[(g + 8) * gpl + col] = d[2]; if (col + 1 < NP) gp[(g + 8) * gpl + col + 1] = d[3]; }
+    if (warp < 4) {
+        for (int nt = warp; nt < ntK; nt += 4) {
+            float d[4];
+            score_tile(quh, qul, Kb, ldk, nt * 8, L, lane, d);
+            const int col = nt * 8 + 2 * t;
+            if (g < c) { if (col < L) sk[g * Lmax + col] = d[0]; if (col + 1 < L) sk[g * Lmax + col + 1] = d[1]; }
+            if (g + 8 < c) { if (col < L) sk[(g + 8) * Lmax + col] = d[2]; if (col + 1 < L) sk[(g + 8) * Lmax + col + 1] = d[3]; }
+        }
+    } else {
+        for (int nt = warp - 4; nt < ntP; nt += 4) {
+            float d[4];
+            score_tile(qvh, qvl, Pb, D, nt * 8, NP, lane, d);
+            const int col = nt * 8 + 2 * t;
+            if (g < c) { if (col < NP) gp[g * gpl + col] = d[0]; if (col + 1 < NP) gp[g * gpl + col + 1] = d[1]; }
+            if (g + 8 < c) { if (col < NP) gp[(g + 8) * gpl + col] = d[2]; if (col + 1 < NP) gp[(g + 8) * gpl + col + 1] = d[3]; }
+        }
     }
-#pragma unroll
-    for (int u = 0; u < VLOADS; ++u) {
-        const int e = tid + u * THREADS, r = e >> 5;
-        if (r < L) *(float4 *)(Vs + r * VP + 4 * (e & 31)) = vr[u];
-    }
-    // content scores (q + u) . k from the K rows, read straight from global memory
-    for (int nt = warp; nt < ntK; nt += THREADS / 32) {
-        float d[4];
-        score_tile(quh, qul, Kb, ldk, nt * 8, L, lane, d);
-        const int col = nt * 8 + 2 * t;
-        if (g < c) { if (col < L) sk[g * Lmax + col] = d[0]; if (col + 1 < L) sk[g * Lmax + col + 1] = d[1]; }
-        if (g + 8 < c) { if (col < L) sk[(g + 8) * Lmax + col] = d[2]; if (col + 1 < L) sk[(g + 8) * Lmax + col + 1] = d[3]; }
-    }
+    cp_async_wait_all();
     __syncthreads();
     // softmax of each query row (one warp per row); rows c..15 become zero probabilities
     for (int i = warp; i < MAXC; i += THREADS / 32) {
