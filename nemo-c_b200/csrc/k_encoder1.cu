@@ -460,15 +460,12 @@ __device__ __forceinline__ void attention_item(const NbEnc1Args &a, Smem &S, uin
             p4[i] = ld4g(Pb + (int64_t)j * D + 4 * lane);
         }
     }
-    // value rows: element e = row e / 32, columns 4 (e % 32) .. +3; every load in flight at once,
-    // stored to shared memory after the scores
-    constexpr int VIT = LM * 32 / CTHREADS;
-    float4 vv[VIT];
-#pragma unroll
-    for (int q = 0; q < VIT; ++q) {
-        const int e = tid + q * CTHREADS;
-        if (e < L * 32) vv[q] = __ldcg((const float4 *)(Vb + (int64_t)(e >> 5) * ld) + (e & 31));
-    }
+    // value rows: element e = row e / 32, columns 4 (e % 32) .. +3, 16-byte asynchronous copies
+    // straight into shared memory (no registers held), every one in flight at once, waited for
+    // before the weighted sum
+    for (int e = tid; e < L * 32; e += CTHREADS)
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(sm100::smem_u32(Vs + 4 * e)), "l"((const float4 *)(Vb + (int64_t)(e >> 5) * ld) + (e & 31))
+                     : "memory");
     const float4 qu = make_float4(q4.x + u4.x, q4.y + u4.y, q4.z + u4.z, q4.w + u4.w);
     const float4 qv = make_float4(q4.x + v4.x, q4.y + v4.y, q4.z + v4.z, q4.w + v4.w);
     // this lane's part of the KI scores (q + u).k_j + (q + v).p_j, all reduced over the warp by one
@@ -487,11 +484,7 @@ __device__ __forceinline__ void attention_item(const NbEnc1Args &a, Smem &S, uin
         const int i = lane >> 1, j = warp + CWARPS * i;
         if ((lane & 1) == 0 && i < KI && j < L) S.sc[j] = sv[0] * a.scale;
     }
-#pragma unroll
-    for (int q = 0; q < VIT; ++q) {
-        const int e = tid + q * CTHREADS;
-        if (e < L * 32) ((float4 *)Vs)[e] = vv[q];
-    }
+    asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");  // this thread's value copies
     cbar();
     if (warp == 0) {
         float sv[3], mx = -INFINITY;
