@@ -63,6 +63,8 @@ struct Smem {
     float rs[2][CWARPS][2 * MAXC]; // per-warp row sums (two buffers)
     float fs[CWARPS][128];         // per-warp row sums of a folded LayerNorm
     float glu[16][MAXC];           // conv-module GLU outputs of this CTA's channels
+    float cdw[16][9];              // depthwise taps of this CTA's channels (flat: channel * taps + tap)
+    float chist[8][16];            // conv history rows [h][channel]
     float sc[MAXL];                // attention scores / probabilities
     float vpart[2][128];           // attention value halves
     uint64_t full[NB];
@@ -814,15 +816,17 @@ __device__ void compute(const NbEnc1Args &a, Smem &S, uint8_t *ring, uint8_t *ac
             }
             const bool dact = s == 4 && R > 0 && tid < R * c;
             const int er = div_q(dR, tid), en = tid - er * R;
-            float dw[9], hist[8];
-            if (dact) {
-                const int ch = g.lo + en;
-#pragma unroll
-                for (int t = 0; t < 9; ++t) dw[t] = t < a.taps ? __ldg(w.dw_w + ch * a.taps + t) : 0.0f;
-#pragma unroll
-                for (int t = 0; t < 8; ++t) {
-                    const int row = pos - (a.taps - 1) + er + t;  // history rows precede pos
-                    hist[t] = (t < a.taps - 1 && row < pos) ? __ldcg(w.din + (int64_t)row * D + ch) : 0.0f;
+            if (s == 4 && R > 0) {
+                // the depthwise taps [channel][tap] and history rows [h][channel] (h < taps - 1: row
+                // pos - (taps - 1) + h, which precedes pos) of this CTA's channels: 4-byte asynchronous
+                // copies into shared memory, waited for before the conv (both are read-only during the
+                // launch: the taps are weights, the history rows were written by earlier chunks)
+                for (int e = tid; e < R * a.taps; e += CTHREADS)
+                    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(sm100::smem_u32(&S.cdw[0][0] + e)), "l"(w.dw_w + (int64_t)g.lo * a.taps + e) : "memory");
+                for (int e = tid; e < (a.taps - 1) * R; e += CTHREADS) {
+                    const int h = div_q(dR, e), n = e - h * R;
+                    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(sm100::smem_u32(&S.chist[h][n])),
+                                 "l"(w.din + (int64_t)(pos - (a.taps - 1) + h) * D + g.lo + n) : "memory");
                 }
             }
             float4 G0 = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -961,6 +965,7 @@ __device__ void compute(const NbEnc1Args &a, Smem &S, uint8_t *ring, uint8_t *ac
                 // causal depthwise conv of this CTA's channels (src/kernels.metal:361-380) over rows
                 // pos - (taps - 1) .. pos + c - 1: tap t of row er reads history row er + t while that
                 // precedes pos, else the GLU output of row er + t - (taps - 1)
+                asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");  // the taps and history
                 cbar();
                 if (dact) {
                     float x = 0.0f;
@@ -968,7 +973,7 @@ __device__ void compute(const NbEnc1Args &a, Smem &S, uint8_t *ring, uint8_t *ac
                     for (int t = 0; t < 9; ++t) {
                         if (t >= a.taps) break;
                         const int h = er + t;  // tap t of row er: history row er + t, else GLU row h - (taps - 1)
-                        x += dw[t] * (h < a.taps - 1 ? hist[t] : S.glu[en][h - (a.taps - 1)]);
+                        x += (&S.cdw[0][0])[en * a.taps + t] * (h < a.taps - 1 ? S.chist[h][en] : S.glu[en][h - (a.taps - 1)]);
                     }
                     a.att[(int64_t)er * D + g.lo + en] = x;
                 }
