@@ -145,10 +145,10 @@ def test_gemm_row_mapping_and_dynamic_rows():
     assert rel_err(got[:4], orc.gemm(A[:4], W)) < FP32_TOL and np.all(got[4:] == 0)
 
 
-@pytest.mark.parametrize("D", [256, 1024])
-def test_layernorms(D):
-    rng = np.random.default_rng(D)
-    M = 9
+@pytest.mark.parametrize("D,M", [(256, 9), (1024, 9), (1024, 1795)])
+def test_layernorms(D, M):
+    # M = 1795: the several-rows-per-block form for large batches, with a last, partly filled block
+    rng = np.random.default_rng(D + M)
     X = (rng.standard_normal((M, D)) * 3 + 1).astype(np.float32)
     g1, b1, g2, b2 = (rng.standard_normal(D).astype(np.float32) for _ in range(4))
     dX, dY1, dY2 = dev(X), dev(np.zeros_like(X)), dev(np.zeros_like(X))
