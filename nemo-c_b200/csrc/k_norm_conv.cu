@@ -494,66 +494,6 @@ __global__ void __launch_bounds__(256) layernorm_row_kernel(const float *__restr
     store4(Y, y_fmt, y_plane, base, v);
 }
 
-// The same for LN_RPB rows per block: every row's load in flight at once and one pair of barriers
-// for all of them, so a block keeps LN_RPB x 4 KB in flight instead of 4 KB. Per row the arithmetic
-// (and its order) is ln_block1024's.
-constexpr int LN_RPB = 4;
-__global__ void __launch_bounds__(256) layernorm_rows_kernel(const float *__restrict__ X, const float *__restrict__ g, const float *__restrict__ b,
-                                                             const float *__restrict__ g2, const float *__restrict__ b2, float *Y1, void *Y, int y_fmt,
-                                                             int64_t y_plane, float eps, int M) {
-    __shared__ float red[2][LN_RPB][8];
-    nb::pdl_wait();
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, r0 = blockIdx.x * LN_RPB;
-    float4 v[LN_RPB];
-#pragma unroll
-    for (int r = 0; r < LN_RPB; ++r)
-        v[r] = r0 + r < M ? *(const float4 *)(X + (int64_t)(r0 + r) * 1024 + 4 * threadIdx.x) : make_float4(0.f, 0.f, 0.f, 0.f);
-    const float4 gg = __ldg((const float4 *)(g + 4 * threadIdx.x)), bb = __ldg((const float4 *)(b + 4 * threadIdx.x));
-    float4 gg2 = make_float4(0.f, 0.f, 0.f, 0.f), bb2 = gg2;
-    if (g2) { gg2 = __ldg((const float4 *)(g2 + 4 * threadIdx.x)); bb2 = __ldg((const float4 *)(b2 + 4 * threadIdx.x)); }
-    for (int pass = 0; pass < (g2 ? 2 : 1); ++pass) {
-        const float4 G = pass ? gg2 : gg, Bv = pass ? bb2 : bb;
-        float s[LN_RPB];
-#pragma unroll
-        for (int r = 0; r < LN_RPB; ++r) s[r] = nb::warp_sum(v[r].x + v[r].y + v[r].z + v[r].w);
-        if (lane == 0)
-#pragma unroll
-            for (int r = 0; r < LN_RPB; ++r) red[0][r][warp] = s[r];
-        __syncthreads();
-        float q[LN_RPB];
-#pragma unroll
-        for (int r = 0; r < LN_RPB; ++r) {
-            float tot = 0.0f;
-#pragma unroll
-            for (int i = 0; i < 8; ++i) tot += red[0][r][i];
-            const float mean = tot / 1024.0f;
-            v[r] = make_float4(v[r].x - mean, v[r].y - mean, v[r].z - mean, v[r].w - mean);
-            q[r] = nb::warp_sum(v[r].x * v[r].x + v[r].y * v[r].y + v[r].z * v[r].z + v[r].w * v[r].w);
-        }
-        if (lane == 0)
-#pragma unroll
-            for (int r = 0; r < LN_RPB; ++r) red[1][r][warp] = q[r];
-        __syncthreads();
-#pragma unroll
-        for (int r = 0; r < LN_RPB; ++r) {
-            float qt = 0.0f;
-#pragma unroll
-            for (int i = 0; i < 8; ++i) qt += red[1][r][i];
-            const float inv = 1.0f / sqrtf(qt / 1024.0f + eps);
-            v[r] = make_float4(v[r].x * inv * G.x + Bv.x, v[r].y * inv * G.y + Bv.y, v[r].z * inv * G.z + Bv.z, v[r].w * inv * G.w + Bv.w);
-        }
-        if (g2 && pass == 0) {
-#pragma unroll
-            for (int r = 0; r < LN_RPB; ++r)
-                if (r0 + r < M) *(float4 *)(Y1 + (int64_t)(r0 + r) * 1024 + 4 * threadIdx.x) = v[r];
-            __syncthreads();  // every warp has read red before the second pass rewrites it
-        }
-    }
-#pragma unroll
-    for (int r = 0; r < LN_RPB; ++r)
-        if (r0 + r < M) store4(Y, y_fmt, y_plane, (int64_t)(r0 + r) * 1024 + 4 * threadIdx.x, v[r]);
-}
-
 // Causal depthwise conv + LN + SiLU (src/kernels.metal:361-409), one warp per (stream, row).
 __global__ void __launch_bounds__(WROWS * 32) dwconv_ln_silu_warp_kernel(const float *__restrict__ din, int64_t din_sstride, const int *pos_p,
                                                                          const float *__restrict__ W, const float *__restrict__ g,
@@ -624,10 +564,6 @@ static int grid_for(int64_t total) {
 extern "C" int nemo_layernorm(const float *X, const float *g, const float *b, void *Y, int y_fmt, int64_t y_plane, int M, int D, float eps, void *stream) {
     if (D > LNT * LN_MAXV) return nb_set_error("nemo_layernorm: D=%d too large", D);
     if (M <= 0) return 0;
-    if (D == 1024 && warp_rows_ok(X, Y, y_fmt, y_plane, D) && M >= 148 * LN_RPB) {
-        nb::launch(layernorm_rows_kernel, (M + LN_RPB - 1) / LN_RPB, 256, 0, (cudaStream_t)stream, X, g, b, nullptr, nullptr, nullptr, Y, y_fmt, y_plane, eps, M);
-        return nb_check_launch("layernorm_rows_kernel");
-    }
     if (D == 1024 && warp_rows_ok(X, Y, y_fmt, y_plane, D)) {
         nb::launch(layernorm_row_kernel, M, 256, 0, (cudaStream_t)stream, X, g, b, nullptr, nullptr, nullptr, Y, y_fmt, y_plane, eps);
         return nb_check_launch("layernorm_row_kernel");
@@ -645,10 +581,6 @@ extern "C" int nemo_layernorm2(const float *X, const float *g1, const float *b1,
                                int y2_fmt, int64_t y2_plane, int M, int D, float eps, void *stream) {
     if (D > LNT * LN_MAXV) return nb_set_error("nemo_layernorm2: D=%d too large", D);
     if (M <= 0) return 0;
-    if (D == 1024 && warp_rows_ok(X, Y2, y2_fmt, y2_plane, D) && !((uintptr_t)Y1 & 15) && M >= 148 * LN_RPB) {
-        nb::launch(layernorm_rows_kernel, (M + LN_RPB - 1) / LN_RPB, 256, 0, (cudaStream_t)stream, X, g1, b1, g2, b2, Y1, Y2, y2_fmt, y2_plane, eps, M);
-        return nb_check_launch("layernorm_rows_kernel");
-    }
     if (D == 1024 && warp_rows_ok(X, Y2, y2_fmt, y2_plane, D) && !((uintptr_t)Y1 & 15)) {
         nb::launch(layernorm_row_kernel, M, 256, 0, (cudaStream_t)stream, X, g1, b1, g2, b2, Y1, Y2, y2_fmt, y2_plane, eps);
         return nb_check_launch("layernorm_row_kernel");

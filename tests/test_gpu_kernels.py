@@ -147,7 +147,7 @@ def test_gemm_row_mapping_and_dynamic_rows():
 
 @pytest.mark.parametrize("D,M", [(256, 9), (1024, 9), (1024, 1795)])
 def test_layernorms(D, M):
-    # M = 1795: the several-rows-per-block form for large batches, with a last, partly filled block
+    # M = 1795: a batch-sized row count (one block per row)
     rng = np.random.default_rng(D + M)
     X = (rng.standard_normal((M, D)) * 3 + 1).astype(np.float32)
     g1, b1, g2, b2 = (rng.standard_normal(D).astype(np.float32) for _ in range(4))
