@@ -370,20 +370,29 @@ struct CfgR {
     static constexpr int SMEM = 1024 + STAGES * STAGE + 1024;    // stages | barriers
 };
 
+// Global operands of one 16-column chunk of the activation-major epilogue, requested a chunk ahead
+// (the first chunk's before the accumulator is complete), so that their latency overlaps the MMAs
+// and the previous chunk's math instead of adding an L2 round trip to every chunk:
+//   plain / GLU tiles: a = bias, b = GLU gate bias, or the fp32 output being accumulated into;
+//   argmax (decoder mode 3): a = bias (the columns that exist);
+//   LSTM (mode 1): a = the stream's gate-table row, c = the cell state of the chunk's 4 units;
+//   joint input (mode 2): a = bias, b = the encoder row; aux columns: a = aux bias.
+struct EpiIn { float4 a[4], b[4], c; };
+
+__device__ __forceinline__ void set4(float4 &v, int j, float f) {
+    if (j == 0) v.x = f; else if (j == 1) v.y = f; else if (j == 2) v.z = f; else v.w = f;
+}
+
 // 16 consecutive output columns of one activation row (activation-major epilogue):
 // bias -> activation (ACT: NEMO_ACT_*, GLU pairs value and gate) -> x alpha -> (+= C) -> store as
 // fp32 or bf16 hi/lo planes (BF16 = true), plus the optional fp32 copy. 16-byte accesses.
 template <int ACT, bool BF16>
-__device__ __forceinline__ void epi16(const TcArgs &p, int64_t rowbase, int64_t brow, int m, int n0, const float (&va)[16], const float (&vg)[16]) {
+__device__ __forceinline__ void epi16(const TcArgs &p, int64_t rowbase, int m, int n0, const float (&va)[16], const float (&vg)[16], const EpiIn &in) {
     float *__restrict__ C32 = (float *)p.e.C;
     float o[16], bv[16], bg[16];
 #pragma unroll
     for (int x = 0; x < 16; x += 4) {
-        float4 b4 = make_float4(0.f, 0.f, 0.f, 0.f), g4 = b4;
-        if (p.e.bias) {
-            b4 = __ldg((const float4 *)(p.e.bias + brow + n0 + x));
-            if (ACT == NEMO_ACT_GLU) g4 = __ldg((const float4 *)(p.e.bias + brow + n0 + x + p.N / 2));
-        }
+        const float4 b4 = in.a[x >> 2], g4 = ACT == NEMO_ACT_GLU ? in.b[x >> 2] : make_float4(0.f, 0.f, 0.f, 0.f);
         bv[x] = b4.x; bv[x + 1] = b4.y; bv[x + 2] = b4.z; bv[x + 3] = b4.w;
         bg[x] = g4.x; bg[x + 1] = g4.y; bg[x + 2] = g4.z; bg[x + 3] = g4.w;
     }
@@ -399,9 +408,11 @@ __device__ __forceinline__ void epi16(const TcArgs &p, int64_t rowbase, int64_t 
     const int64_t idx = rowbase + n0;
     if (!BF16) {
         if (p.e.accumulate) {
+            // the accumulated output came with the operands, except for GLU tiles (whose b holds
+            // the gate bias)
 #pragma unroll
             for (int x = 0; x < 16; x += 4) {
-                const float4 c4 = *(const float4 *)(C32 + idx + x);
+                const float4 c4 = ACT == NEMO_ACT_GLU ? *(const float4 *)(C32 + idx + x) : in.b[x >> 2];
                 o[x] += c4.x; o[x + 1] += c4.y; o[x + 2] += c4.z; o[x + 3] += c4.w;
             }
         }
@@ -431,16 +442,16 @@ __device__ __forceinline__ void epi16(const TcArgs &p, int64_t rowbase, int64_t 
 // Batched greedy decoder epilogues: 16 output columns of GEMM row m, whose stream is b.
 // LSTM cell (src/kernels.metal:475-486) on gate-interleaved columns: columns n0 .. n0 + 15 are
 // gates i, f, g, o of units n0 / 4 .. n0 / 4 + 3; `row` is the stream's gate row (bias included).
-__device__ __forceinline__ void dec_lstm16(const NbDecEpi &de, const float *__restrict__ row, int m, int b, int n0, const float (&va)[16]) {
+__device__ __forceinline__ void dec_lstm16(const NbDecEpi &de, int m, int b, int n0, const float (&va)[16], const EpiIn &in) {
     const int u0 = n0 >> 2, ph = de.n_split >> 2;
     float g[16];
 #pragma unroll
     for (int x = 0; x < 16; x += 4) {
-        const float4 b4 = *(const float4 *)(row + n0 + x);
+        const float4 b4 = in.a[x >> 2];
         g[x] = va[x] + b4.x; g[x + 1] = va[x + 1] + b4.y; g[x + 2] = va[x + 2] + b4.z; g[x + 3] = va[x + 3] + b4.w;
     }
     float *cp = de.c + (int64_t)b * ph + u0;
-    const float4 c4 = *(const float4 *)cp;
+    const float4 c4 = in.c;
     const float cold[4] = { c4.x, c4.y, c4.z, c4.w };
     float cc[4], hh[4];
 #pragma unroll
@@ -465,13 +476,13 @@ __device__ __forceinline__ void dec_lstm16(const NbDecEpi &de, const float *__re
 
 // Prediction projection row of stream b (pred = bias + acc, n_split columns) and its joint input
 // X[b] = relu(enc[er] + pred) as bf16 hi/lo planes.
-__device__ __forceinline__ void dec_joint16(const NbDecEpi &de, const float *__restrict__ bias, int b, int er, int n0, const float (&va)[16]) {
+__device__ __forceinline__ void dec_joint16(const NbDecEpi &de, int b, int n0, const float (&va)[16], const EpiIn &in) {
     const int N = de.n_split;
     float v[16], x[16];
 #pragma unroll
     for (int q = 0; q < 16; q += 4) {
-        const float4 b4 = __ldg((const float4 *)(bias + n0 + q));
-        const float4 e4 = *(const float4 *)(de.enc + (int64_t)er * N + n0 + q);
+        const float4 b4 = in.a[q >> 2];
+        const float4 e4 = in.b[q >> 2];
         v[q] = va[q] + b4.x; v[q + 1] = va[q + 1] + b4.y; v[q + 2] = va[q + 2] + b4.z; v[q + 3] = va[q + 3] + b4.w;
         x[q] = fmaxf(e4.x + v[q], 0.0f); x[q + 1] = fmaxf(e4.y + v[q + 1], 0.0f);
         x[q + 2] = fmaxf(e4.z + v[q + 2], 0.0f); x[q + 3] = fmaxf(e4.w + v[q + 3], 0.0f);
@@ -494,15 +505,61 @@ __device__ __forceinline__ void dec_joint16(const NbDecEpi &de, const float *__r
 }
 
 // Columns at or past n_split: the stream's aux row (product plus aux_bias).
-__device__ __forceinline__ void dec_aux16(const NbDecEpi &de, int N, int b, int n0, const float (&va)[16]) {
+__device__ __forceinline__ void dec_aux16(const NbDecEpi &de, int N, int b, int n0, const float (&va)[16], const EpiIn &in) {
     const int w = N - de.n_split, col = n0 - de.n_split;
     float *dst = de.aux + (int64_t)b * w + col;
 #pragma unroll
     for (int q = 0; q < 16; q += 4) {
-        float4 b4 = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (de.aux_bias) b4 = __ldg((const float4 *)(de.aux_bias + col + q));
+        const float4 b4 = in.a[q >> 2];
         *(float4 *)(dst + q) = make_float4(va[q] + b4.x, va[q + 1] + b4.y, va[q + 2] + b4.z, va[q + 3] + b4.w);
     }
+}
+
+// Requests the operands of the chunk at output column n0 (see EpiIn), with the same conditions
+// under which the chunk's epilogue reads them; everything else is zero.
+__device__ __forceinline__ void epi_in(const TcArgs &p, bool row_ok, int n0, int nout, int64_t rowbase, int64_t brow, int ds, int der,
+                                       const float *dbias, EpiIn &in) {
+    const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int x = 0; x < 4; ++x) in.a[x] = in.b[x] = z;
+    in.c = z;
+    if (!row_ok || n0 >= nout) return;
+    const int cnt = min(16, nout - n0);
+    if (p.de.mode == 3) {
+#pragma unroll
+        for (int x = 0; x < 16; ++x)
+            if (x < cnt) set4(in.a[x >> 2], x & 3, __ldg(p.e.bias + n0 + x));
+        return;
+    }
+    if (p.de.mode) {
+        const NbDecEpi &de = p.de;
+        if (n0 >= de.n_split) {
+            if (de.aux_bias)
+#pragma unroll
+                for (int q = 0; q < 4; ++q) in.a[q] = __ldg((const float4 *)(de.aux_bias + (n0 - de.n_split) + 4 * q));
+        } else if (de.mode == 1) {
+#pragma unroll
+            for (int q = 0; q < 4; ++q) in.a[q] = *(const float4 *)(dbias + n0 + 4 * q);
+            in.c = *(const float4 *)(de.c + (int64_t)ds * (de.n_split >> 2) + (n0 >> 2));
+        } else {
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                in.a[q] = __ldg((const float4 *)(dbias + n0 + 4 * q));
+                in.b[q] = *(const float4 *)(de.enc + (int64_t)der * de.n_split + n0 + 4 * q);
+            }
+        }
+        return;
+    }
+    if (!p.vec || cnt != 16) return;  // the scalar path loads its own operands
+    if (p.e.bias)
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            in.a[q] = __ldg((const float4 *)(p.e.bias + brow + n0 + 4 * q));
+            if (p.glu) in.b[q] = __ldg((const float4 *)(p.e.bias + brow + n0 + 4 * q + p.N / 2));
+        }
+    if (!p.glu && p.e.accumulate && p.e.c_fmt == NEMO_FMT_F32)
+#pragma unroll
+        for (int q = 0; q < 4; ++q) in.b[q] = *(const float4 *)((const float *)p.e.C + rowbase + n0 + 4 * q);
 }
 
 template <int BW>
@@ -628,16 +685,19 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tcr_kernel(const __grid_const
                     if (p.de.mode == 2) der = p.de.erow[ds];
                 }
             }
-            if (!sm100::mbar_wait(&acc_full[b], (t >> 1) & 1)) { flags[2] = 1; flags[0] = 1; atomicExch(&g_tc_error, 8); }
-            sm100::named_barrier(1, 256);
-            const bool ok = !flags[2];
-            sm100::tc_fence_after();
-            const uint32_t tacc = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(b * BW);
             // columns of this thread: GLU -> value cols [half*BW/4, +BW/4) and their gates at +BW/2;
             // plain -> [half*BW/2, +BW/2)
             const int span = p.glu ? BW / 4 : BW / 2;
             const int j0 = half * span;
             const int n_base = p.glu ? wt * (BW / 2) : wt * OUT_COLS;
+            // the first chunk's operands, in flight while the MMAs finish
+            EpiIn cur;
+            epi_in(p, row_ok, n_base + j0, nout, rowbase, brow, ds, der, dbias, cur);
+            if (!sm100::mbar_wait(&acc_full[b], (t >> 1) & 1)) { flags[2] = 1; flags[0] = 1; atomicExch(&g_tc_error, 8); }
+            sm100::named_barrier(1, 256);
+            const bool ok = !flags[2];
+            sm100::tc_fence_after();
+            const uint32_t tacc = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(b * BW);
             float *wsb = p.ws + (int64_t)tile * p.slots * 128 * BW;
             bool finish = ok;
             if (ok && w.parts > 1) {
@@ -681,76 +741,77 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tcr_kernel(const __grid_const
                                 }
                             }
                     }
-                    if (!row_ok) continue;
+                    // the next chunk's operands, in flight during this chunk's math
+                    EpiIn nxt;
+                    epi_in(p, row_ok && jj0 + 16 < j0 + span, n_base + jj0 + 16, nout, rowbase, brow, ds, der, dbias, nxt);
                     const int n0 = n_base + jj0;
-                    if (n0 >= nout) continue;
-                    const int cnt = min(16, nout - n0);
-                    if (p.de.mode == 3) {
+                    if (row_ok && n0 < nout) {
+                        const int cnt = min(16, nout - n0);
+                        if (p.de.mode == 3) {
 #pragma unroll
-                        for (int x = 0; x < 16; ++x) {
-                            if (x >= cnt) break;
-                            const float v = va[x] + __ldg(p.e.bias + n0 + x);
-                            if (v > amax) { amax = v; aidx = n0 + x; }
-                        }
-                        continue;
-                    }
-                    if (p.de.mode) {
-                        if (n0 >= p.de.n_split) dec_aux16(p.de, p.N, ds, n0, va);
-                        else if (p.de.mode == 1) dec_lstm16(p.de, dbias, m, ds, n0, va);
-                        else dec_joint16(p.de, dbias, ds, der, n0, va);
-                        continue;
-                    }
-                    if (p.vec && cnt == 16) {
-                        // 16-byte accesses (alignment of every pointer and stride checked on the host),
-                        // the activation / output format resolved at compile time
-                        const int mode = (p.glu ? 3 : p.e.act) | (p.e.c_fmt == NEMO_FMT_F32 ? 0 : 4);
-                        switch (mode) {
-                        case 0: epi16<0, false>(p, rowbase, brow, m, n0, va, vg); break;
-                        case 1: epi16<1, false>(p, rowbase, brow, m, n0, va, vg); break;
-                        case 2: epi16<2, false>(p, rowbase, brow, m, n0, va, vg); break;
-                        case 3: epi16<3, false>(p, rowbase, brow, m, n0, va, vg); break;
-                        case 4: epi16<0, true>(p, rowbase, brow, m, n0, va, vg); break;
-                        case 5: epi16<1, true>(p, rowbase, brow, m, n0, va, vg); break;
-                        case 6: epi16<2, true>(p, rowbase, brow, m, n0, va, vg); break;
-                        default: epi16<3, true>(p, rowbase, brow, m, n0, va, vg); break;
-                        }
-                        continue;
-                    }
-                    float cin[16], bv[16], bg[16];
+                            for (int x = 0; x < 16; ++x) {
+                                if (x >= cnt) break;
+                                const float4 b4 = cur.a[x >> 2];
+                                const float v = va[x] + ((x & 3) == 0 ? b4.x : (x & 3) == 1 ? b4.y : (x & 3) == 2 ? b4.z : b4.w);
+                                if (v > amax) { amax = v; aidx = n0 + x; }
+                            }
+                        } else if (p.de.mode) {
+                            if (n0 >= p.de.n_split) dec_aux16(p.de, p.N, ds, n0, va, cur);
+                            else if (p.de.mode == 1) dec_lstm16(p.de, m, ds, n0, va, cur);
+                            else dec_joint16(p.de, ds, n0, va, cur);
+                        } else if (p.vec && cnt == 16) {
+                            // 16-byte accesses (alignment of every pointer and stride checked on the
+                            // host), the activation / output format resolved at compile time
+                            const int mode = (p.glu ? 3 : p.e.act) | (p.e.c_fmt == NEMO_FMT_F32 ? 0 : 4);
+                            switch (mode) {
+                            case 0: epi16<0, false>(p, rowbase, m, n0, va, vg, cur); break;
+                            case 1: epi16<1, false>(p, rowbase, m, n0, va, vg, cur); break;
+                            case 2: epi16<2, false>(p, rowbase, m, n0, va, vg, cur); break;
+                            case 3: epi16<3, false>(p, rowbase, m, n0, va, vg, cur); break;
+                            case 4: epi16<0, true>(p, rowbase, m, n0, va, vg, cur); break;
+                            case 5: epi16<1, true>(p, rowbase, m, n0, va, vg, cur); break;
+                            case 6: epi16<2, true>(p, rowbase, m, n0, va, vg, cur); break;
+                            default: epi16<3, true>(p, rowbase, m, n0, va, vg, cur); break;
+                            }
+                        } else {
+                            float cin[16], bv[16], bg[16];
 #pragma unroll
-                    for (int x = 0; x < 16; ++x) {
-                        cin[x] = bv[x] = bg[x] = 0.0f;
-                        if (x < cnt) {
-                            if (p.e.accumulate) cin[x] = C32[rowbase + n0 + x];
-                            if (p.e.bias) {
-                                bv[x] = p.e.bias[brow + n0 + x];
-                                if (p.glu) bg[x] = p.e.bias[brow + n0 + x + p.N / 2];
+                            for (int x = 0; x < 16; ++x) {
+                                cin[x] = bv[x] = bg[x] = 0.0f;
+                                if (x < cnt) {
+                                    if (p.e.accumulate) cin[x] = C32[rowbase + n0 + x];
+                                    if (p.e.bias) {
+                                        bv[x] = p.e.bias[brow + n0 + x];
+                                        if (p.glu) bg[x] = p.e.bias[brow + n0 + x + p.N / 2];
+                                    }
+                                }
+                            }
+#pragma unroll
+                            for (int x = 0; x < 16; ++x) {
+                                if (x >= cnt) break;
+                                float v;
+                                if (p.glu) {
+                                    v = (va[x] + bv[x]) * fast_sigmoid(vg[x] + bg[x]) * p.e.alpha;
+                                } else {
+                                    v = va[x] + bv[x];
+                                    if (p.e.act == NEMO_ACT_SILU) v = v * fast_sigmoid(v);
+                                    else if (p.e.act == NEMO_ACT_RELU) v = fmaxf(v, 0.0f);
+                                    v *= p.e.alpha;
+                                }
+                                v += cin[x];
+                                const int64_t idx = rowbase + n0 + x;
+                                if (p.e.c_fmt == NEMO_FMT_F32) {
+                                    C32[idx] = v;
+                                } else {
+                                    const uint16_t hi = nb::f2bf(v);
+                                    C16[idx] = hi;
+                                    C16[idx + p.e.c_plane] = nb::f2bf(v - nb::bf2f(hi));
+                                }
+                                if (p.e.c32) p.e.c32[(int64_t)m * p.e.ldc32 + n0 + x] = v;
                             }
                         }
                     }
-#pragma unroll
-                    for (int x = 0; x < 16; ++x) {
-                        if (x >= cnt) break;
-                        float v;
-                        if (p.glu) {
-                            v = (va[x] + bv[x]) * fast_sigmoid(vg[x] + bg[x]) * p.e.alpha;
-                        } else {
-                            v = va[x] + bv[x];
-                            if (p.e.act == NEMO_ACT_SILU) v = v * fast_sigmoid(v);
-                            else if (p.e.act == NEMO_ACT_RELU) v = fmaxf(v, 0.0f);
-                            v *= p.e.alpha;
-                        }
-                        v += cin[x];
-                        const int64_t idx = rowbase + n0 + x;
-                        if (p.e.c_fmt == NEMO_FMT_F32) {
-                            C32[idx] = v;
-                        } else {
-                            const uint16_t hi = nb::f2bf(v);
-                            C16[idx] = hi;
-                            C16[idx + p.e.c_plane] = nb::f2bf(v - nb::bf2f(hi));
-                        }
-                        if (p.e.c32) p.e.c32[(int64_t)m * p.e.ldc32 + n0 + x] = v;
-                    }
+                    cur = nxt;
                 }
                 if (p.de.mode == 3 && row_ok) {
                     p.de.part_v[(int64_t)m * p.de.part_ld + 2 * wt + half] = amax;
