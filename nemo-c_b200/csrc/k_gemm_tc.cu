@@ -562,7 +562,10 @@ __device__ __forceinline__ void epi_in(const TcArgs &p, bool row_ok, int n0, int
         for (int q = 0; q < 4; ++q) in.b[q] = *(const float4 *)((const float *)p.e.C + rowbase + n0 + 4 * q);
 }
 
-template <int BW>
+// DEC: the batched greedy decoder's epilogues (one tile per CTA, exposed): operands requested a
+// full chunk ahead, in a second register set; otherwise each chunk's operands are requested at the
+// end of the previous chunk (one register set, the register budget of the pipelined tile loop).
+template <int BW, bool DEC>
 __global__ void __launch_bounds__(THREADS, 1) gemm_tcr_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmAh,
                                                             const __grid_constant__ CUtensorMap tmAl, const __grid_constant__ TcArgs p) {
     using C = CfgR<BW>;
@@ -741,9 +744,9 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tcr_kernel(const __grid_const
                                 }
                             }
                     }
-                    // the next chunk's operands, in flight during this chunk's math
+                    // decoder epilogues: the next chunk's operands, in flight during this chunk's math
                     EpiIn nxt;
-                    epi_in(p, row_ok && jj0 + 16 < j0 + span, n_base + jj0 + 16, nout, rowbase, brow, ds, der, dbias, nxt);
+                    if (DEC) epi_in(p, row_ok && jj0 + 16 < j0 + span, n_base + jj0 + 16, nout, rowbase, brow, ds, der, dbias, nxt);
                     const int n0 = n_base + jj0;
                     if (row_ok && n0 < nout) {
                         const int cnt = min(16, nout - n0);
@@ -811,7 +814,8 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tcr_kernel(const __grid_const
                             }
                         }
                     }
-                    cur = nxt;
+                    if (DEC) cur = nxt;
+                    else epi_in(p, row_ok && jj0 + 16 < j0 + span, n_base + jj0 + 16, nout, rowbase, brow, ds, der, dbias, cur);
                 }
                 if (p.de.mode == 3 && row_ok) {
                     p.de.part_v[(int64_t)m * p.de.part_ld + 2 * wt + half] = amax;
@@ -868,8 +872,10 @@ int init_once() {
     cudaFuncSetAttribute(gemm_tc_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<64>::SMEM);
     cudaFuncSetAttribute(gemm_tc_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<128>::SMEM);
     cudaFuncSetAttribute(gemm_tc_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<256>::SMEM);
-    cudaFuncSetAttribute(gemm_tcr_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, CfgR<128>::SMEM);
-    cudaFuncSetAttribute(gemm_tcr_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize, CfgR<256>::SMEM);
+    cudaFuncSetAttribute(gemm_tcr_kernel<128, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, CfgR<128>::SMEM);
+    cudaFuncSetAttribute(gemm_tcr_kernel<256, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, CfgR<256>::SMEM);
+    cudaFuncSetAttribute(gemm_tcr_kernel<128, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, CfgR<128>::SMEM);
+    cudaFuncSetAttribute(gemm_tcr_kernel<256, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, CfgR<256>::SMEM);
     g_encode = (EncodeTiled)fn;
     return 0;
 }
@@ -1030,7 +1036,8 @@ int launch_r(const nemo_gemm_args_t *a, const PlanR &pl, cudaStream_t st, const 
     p.sk_q = pl.sk_q;
     p.slots = pl.slots;
     const int grid = pl.grid;
-    nb::launch(gemm_tcr_kernel<BW>, grid, THREADS, CfgR<BW>::SMEM, st, mw, mh, ml, p);
+    if (de) nb::launch(gemm_tcr_kernel<BW, true>, grid, THREADS, CfgR<BW>::SMEM, st, mw, mh, ml, p);
+    else nb::launch(gemm_tcr_kernel<BW, false>, grid, THREADS, CfgR<BW>::SMEM, st, mw, mh, ml, p);
     return nb_check_launch("gemm_tcr_kernel");
 }
 
