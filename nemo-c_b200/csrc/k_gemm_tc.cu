@@ -355,7 +355,9 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
 
 // ---- activation-major tiles for batches -------------------------------------------------------
 // For many rows the roles swap: 128 activation rows are the MMA's M side (TMEM lanes) and BW
-// weight rows (128 or 256) its N side (TMEM columns). One k-step stages 2 x 16 KB of activation
+// weight rows (128, 224 or 256) its N side (TMEM columns). The 224-row tile (plain tiles only)
+// exists for wave quantisation: at 1792 x 4096 it makes 266 tiles, 1.8 rounds of 148 SMs, where
+// 256-row tiles make 224 (1.5 rounds: half the SMs idle through the second). One k-step stages 2 x 16 KB of activation
 // planes and BW x 128 B of weights for 128 x BW x 64 x 2 multiply-adds, 1.5x fewer bytes per
 // MMA than the weight-major tile at BW = 256. Each epilogue thread owns one activation row and
 // reads 16 consecutive output columns per TMEM load; a GLU tile holds the value half in TMEM
@@ -363,10 +365,10 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
 template <int BW>
 struct CfgR {
     static constexpr int A_PLANE = 128 * BK * 2;                 // 16 KB
-    static constexpr int W_BYTES = BW * BK * 2;                  // 16 / 32 KB
-    static constexpr int STAGE = 2 * A_PLANE + W_BYTES;
-    static constexpr int STAGES = BW == 256 ? 3 : 4;
-    static constexpr int TMEM_COLS = 2 * BW;                     // two accumulator buffers
+    static constexpr int W_BYTES = BW * BK * 2;                  // 16 / 28 / 32 KB
+    static constexpr int STAGE = 2 * A_PLANE + W_BYTES;          // a multiple of 1 KB (128-byte swizzle)
+    static constexpr int STAGES = BW > 128 ? 3 : 4;
+    static constexpr int TMEM_COLS = BW > 128 ? 512 : 256;       // two accumulator buffers (a power of 2)
     static constexpr int SMEM = 1024 + STAGES * STAGE + 1024;    // stages | barriers
 };
 
@@ -876,6 +878,8 @@ int init_once() {
     cudaFuncSetAttribute(gemm_tcr_kernel<256, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, CfgR<256>::SMEM);
     cudaFuncSetAttribute(gemm_tcr_kernel<128, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, CfgR<128>::SMEM);
     cudaFuncSetAttribute(gemm_tcr_kernel<256, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, CfgR<256>::SMEM);
+    cudaFuncSetAttribute(gemm_tcr_kernel<224, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, CfgR<224>::SMEM);
+    cudaFuncSetAttribute(gemm_tcr_kernel<224, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, CfgR<224>::SMEM);
     g_encode = (EncodeTiled)fn;
     return 0;
 }
@@ -1046,11 +1050,13 @@ int launch_rows(const nemo_gemm_args_t *a, cudaStream_t st, const NbDecEpi *de =
     const bool glu = a->act == NEMO_ACT_GLU;
     const bool ok256 = !glu || (a->N / 2) % 128 == 0;
     PlanR best = plan_r(a, 128, false);
-    const PlanR cand[3] = { plan_r(a, 256, false), plan_r(a, 128, true), plan_r(a, 256, true) };
+    // (224-row tiles without k-splits: with them the 1024 x 4096 FF-out shape measured 38 us per
+    // CTA against 31 us with unsplit 128-row tiles)
+    const PlanR cand[4] = { plan_r(a, 256, false), plan_r(a, 128, true), plan_r(a, 256, true), plan_r(a, 224, false) };
     const int pol = sched == 1 ? 0 : sched == 2 ? 1 : sk_policy();
     if (pol != 1)
         for (const PlanR &p : cand)
-            if ((p.bw == 128 || ok256) && p.est_us < best.est_us) best = p;
+            if ((p.bw == 128 || (p.bw == 256 && ok256) || (p.bw == 224 && !glu)) && p.est_us < best.est_us) best = p;
     if (pol != 0) {
         int ok128 = 0, ok2 = 0;
         const PlanR s128 = plan_sk(a, 128, &ok128), s256 = plan_sk(a, 256, &ok2);
@@ -1059,6 +1065,7 @@ int launch_rows(const nemo_gemm_args_t *a, cudaStream_t st, const NbDecEpi *de =
         if (ok2 && ok256 && s256.est_us < best.est_us) best = s256;
     }
     if (best.bw == 256) return launch_r<256>(a, best, st, de);
+    if (best.bw == 224) return launch_r<224>(a, best, st, de);
     return launch_r<128>(a, best, st, de);
 }
 

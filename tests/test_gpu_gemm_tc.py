@@ -83,6 +83,21 @@ def test_tcr_gemm_epilogues(M, act):
     assert rel_err(got, ref) < BF16X2_TOL
 
 
+@pytest.mark.parametrize("act", [0, 1, 2])
+def test_tcr_gemm_224_wide_tiles(act):
+    # 1792 x 4096 picks the 224-row weight tiles (266 tiles: 1.8 rounds of 148 SMs); the last tile
+    # holds 64 real weight rows; bias, activation, alpha and accumulation on every chunk
+    rng = np.random.default_rng(51 + act)
+    M, N, K = 1792, 4096, 320
+    A = rng.standard_normal((M, K)).astype(np.float32)
+    W = bf16(rng, (N, K))
+    b = (rng.standard_normal(N) * 0.1).astype(np.float32)
+    C0 = rng.standard_normal((M, N)).astype(np.float32)
+    got = run_gemm(A, W, b, C0, act=act, acc=1, alpha=0.5, kind=5, a_fmt=1)
+    ref = orc.gemm(A, W, b, C0=C0, act=act, accumulate=True, alpha=0.5)
+    assert rel_err(got, ref) < BF16X2_TOL
+
+
 @pytest.mark.parametrize("shape", [(3072, 1024), (4096, 1024), (1024, 4096), (2048, 1024), (640, 1024), (1025, 640), (1024, 4352)])
 def test_tcr_gemm_model_shapes(shape):
     rng = np.random.default_rng(11 + sum(shape))
