@@ -355,9 +355,13 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
 
 // ---- activation-major tiles for batches -------------------------------------------------------
 // For many rows the roles swap: 128 activation rows are the MMA's M side (TMEM lanes) and BW
-// weight rows (128, 224 or 256) its N side (TMEM columns). The 224-row tile (plain tiles only)
-// exists for wave quantisation: at 1792 x 4096 it makes 266 tiles, 1.8 rounds of 148 SMs, where
-// 256-row tiles make 224 (1.5 rounds: half the SMs idle through the second). One k-step stages 2 x 16 KB of activation
+// weight rows (112, 128, 160, 224 or 256) its N side (TMEM columns). The widths other than 128
+// and 256 (plain tiles only, no k-splits) exist for wave quantisation on 148 SMs: at 1792 rows,
+// N = 4096 makes 266 tiles of 224 (1.8 rounds; 256-row tiles make 224, 1.5 rounds: half the SMs
+// idle through the second), N = 3072 makes 280 tiles of 160 (1.9 rounds) and N = 1024 makes 140
+// tiles of 112 (one round; 128-row tiles leave 36 SMs idle). Accumulator buffer 1 starts at TMEM
+// column 128 or 256 whatever the width; the epilogue splits a 112-column tile 64 + 48 between its
+// two thread halves, so every 16-column TMEM load starts on a 16-column boundary. One k-step stages 2 x 16 KB of activation
 // planes and BW x 128 B of weights for 128 x BW x 64 x 2 multiply-adds, 1.5x fewer bytes per
 // MMA than the weight-major tile at BW = 256. Each epilogue thread owns one activation row and
 // reads 16 consecutive output columns per TMEM load; a GLU tile holds the value half in TMEM
@@ -368,7 +372,8 @@ struct CfgR {
     static constexpr int W_BYTES = BW * BK * 2;                  // 16 / 28 / 32 KB
     static constexpr int STAGE = 2 * A_PLANE + W_BYTES;          // a multiple of 1 KB (128-byte swizzle)
     static constexpr int STAGES = BW > 128 ? 3 : 4;
-    static constexpr int TMEM_COLS = BW > 128 ? 512 : 256;       // two accumulator buffers (a power of 2)
+    static constexpr int ACC_STRIDE = BW > 128 ? 256 : 128;     // TMEM column of accumulator buffer 1
+    static constexpr int TMEM_COLS = 2 * ACC_STRIDE;              // two accumulator buffers (a power of 2)
     static constexpr int SMEM = 1024 + STAGES * STAGE + 1024;    // stages | barriers
 };
 
@@ -641,7 +646,7 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tcr_kernel(const __grid_const
             const int b = t & 1;
             if (t >= 2 && !sm100::mbar_wait(&acc_empty[b], ((t >> 1) - 1) & 1)) { flags[0] = 1; atomicExch(&g_tc_error, 6); break; }
             sm100::tc_fence_after();
-            const uint32_t dacc = tmem + (uint32_t)(b * BW);
+            const uint32_t dacc = tmem + (uint32_t)(b * C::ACC_STRIDE);
             for (int kb = kb0; kb < kb1; ++kb, ++i) {
                 const int s = i % C::STAGES;
                 if (!sm100::mbar_wait(&full[s], (i / C::STAGES) & 1)) { flags[0] = 1; atomicExch(&g_tc_error, 7); break; }
@@ -692,8 +697,10 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tcr_kernel(const __grid_const
             }
             // columns of this thread: GLU -> value cols [half*BW/4, +BW/4) and their gates at +BW/2;
             // plain -> [half*BW/2, +BW/2)
-            const int span = p.glu ? BW / 4 : BW / 2;
-            const int j0 = half * span;
+            // (a 112-column tile splits 64 + 48, so every chunk starts on a 16-column boundary)
+            const int hs = p.glu ? BW / 4 : (BW / 2 + 15) / 16 * 16;
+            const int span = p.glu ? BW / 4 : half ? BW - hs : hs;
+            const int j0 = half * hs;
             const int n_base = p.glu ? wt * (BW / 2) : wt * OUT_COLS;
             // the first chunk's operands, in flight while the MMAs finish
             EpiIn cur;
@@ -702,7 +709,7 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tcr_kernel(const __grid_const
             sm100::named_barrier(1, 256);
             const bool ok = !flags[2];
             sm100::tc_fence_after();
-            const uint32_t tacc = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(b * BW);
+            const uint32_t tacc = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(b * C::ACC_STRIDE);
             float *wsb = p.ws + (int64_t)tile * p.slots * 128 * BW;
             bool finish = ok;
             if (ok && w.parts > 1) {
@@ -880,6 +887,10 @@ int init_once() {
     cudaFuncSetAttribute(gemm_tcr_kernel<256, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, CfgR<256>::SMEM);
     cudaFuncSetAttribute(gemm_tcr_kernel<224, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, CfgR<224>::SMEM);
     cudaFuncSetAttribute(gemm_tcr_kernel<224, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, CfgR<224>::SMEM);
+    cudaFuncSetAttribute(gemm_tcr_kernel<160, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, CfgR<160>::SMEM);
+    cudaFuncSetAttribute(gemm_tcr_kernel<160, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, CfgR<160>::SMEM);
+    cudaFuncSetAttribute(gemm_tcr_kernel<112, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, CfgR<112>::SMEM);
+    cudaFuncSetAttribute(gemm_tcr_kernel<112, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, CfgR<112>::SMEM);
     g_encode = (EncodeTiled)fn;
     return 0;
 }
@@ -962,7 +973,7 @@ PlanR plan_r(const nemo_gemm_args_t *a, int bw, bool allow_split) {
     r.slots = r.splits;
     r.grid = r.units < g_sms ? r.units : g_sms;
     const int rounds = (r.units + g_sms - 1) / g_sms;
-    r.est_us = rounds * (0.27f * (bw / 128) * r.kb_per_split + 4.0f) + (r.splits > 1 ? 6.0f : 0.0f);
+    r.est_us = rounds * (0.27f * ((float)bw / 128.0f) * r.kb_per_split + 4.0f) + (r.splits > 1 ? 6.0f : 0.0f);
     return r;
 }
 
@@ -1040,6 +1051,9 @@ int launch_r(const nemo_gemm_args_t *a, const PlanR &pl, cudaStream_t st, const 
     p.sk_q = pl.sk_q;
     p.slots = pl.slots;
     const int grid = pl.grid;
+    // the widths other than 128 and 256: no k-splits (their partial tiles are laid out by halves
+    // of BW / 2 columns) and no GLU (value and gate halves of BW / 4 columns per thread half)
+    if (BW != 128 && BW != 256 && (pl.splits > 1 || pl.sk_q || glu)) return nb_set_error("tensor-core GEMM: %d-row tiles take unsplit plain GEMMs only", BW);
     if (de) nb::launch(gemm_tcr_kernel<BW, true>, grid, THREADS, CfgR<BW>::SMEM, st, mw, mh, ml, p);
     else nb::launch(gemm_tcr_kernel<BW, false>, grid, THREADS, CfgR<BW>::SMEM, st, mw, mh, ml, p);
     return nb_check_launch("gemm_tcr_kernel");
@@ -1052,11 +1066,13 @@ int launch_rows(const nemo_gemm_args_t *a, cudaStream_t st, const NbDecEpi *de =
     PlanR best = plan_r(a, 128, false);
     // (224-row tiles without k-splits: with them the 1024 x 4096 FF-out shape measured 38 us per
     // CTA against 31 us with unsplit 128-row tiles)
-    const PlanR cand[4] = { plan_r(a, 256, false), plan_r(a, 128, true), plan_r(a, 256, true), plan_r(a, 224, false) };
+    const PlanR cand[6] = { plan_r(a, 256, false), plan_r(a, 128, true), plan_r(a, 256, true), plan_r(a, 224, false), plan_r(a, 160, false), plan_r(a, 112, false) };
     const int pol = sched == 1 ? 0 : sched == 2 ? 1 : sk_policy();
     if (pol != 1)
-        for (const PlanR &p : cand)
-            if ((p.bw == 128 || (p.bw == 256 && ok256) || (p.bw == 224 && !glu)) && p.est_us < best.est_us) best = p;
+        for (const PlanR &p : cand) {
+            const bool fits = p.bw == 128 || (p.bw == 256 && ok256) || ((p.bw == 224 || p.bw == 160 || p.bw == 112) && !glu);
+            if (fits && p.est_us < best.est_us) best = p;
+        }
     if (pol != 0) {
         int ok128 = 0, ok2 = 0;
         const PlanR s128 = plan_sk(a, 128, &ok128), s256 = plan_sk(a, 256, &ok2);
@@ -1066,6 +1082,8 @@ int launch_rows(const nemo_gemm_args_t *a, cudaStream_t st, const NbDecEpi *de =
     }
     if (best.bw == 256) return launch_r<256>(a, best, st, de);
     if (best.bw == 224) return launch_r<224>(a, best, st, de);
+    if (best.bw == 160) return launch_r<160>(a, best, st, de);
+    if (best.bw == 112) return launch_r<112>(a, best, st, de);
     return launch_r<128>(a, best, st, de);
 }
 

@@ -83,12 +83,15 @@ def test_tcr_gemm_epilogues(M, act):
     assert rel_err(got, ref) < BF16X2_TOL
 
 
+@pytest.mark.parametrize("N", [4096, 3072, 1024])
 @pytest.mark.parametrize("act", [0, 1, 2])
-def test_tcr_gemm_224_wide_tiles(act):
-    # 1792 x 4096 picks the 224-row weight tiles (266 tiles: 1.8 rounds of 148 SMs); the last tile
-    # holds 64 real weight rows; bias, activation, alpha and accumulation on every chunk
-    rng = np.random.default_rng(51 + act)
-    M, N, K = 1792, 4096, 320
+def test_tcr_gemm_odd_width_tiles(N, act):
+    # at 1792 rows the planner takes 224-row weight tiles for N = 4096 (266 tiles: 1.8 rounds of
+    # 148 SMs; the last tile holds 64 real rows), 160-row tiles for N = 3072 (280 tiles) and
+    # 112-row tiles for N = 1024 (140 tiles, epilogue halves of 64 + 48 columns); bias,
+    # activation, alpha and accumulation on every chunk
+    rng = np.random.default_rng(51 + act + N)
+    M, K = 1792, 320
     A = rng.standard_normal((M, K)).astype(np.float32)
     W = bf16(rng, (N, K))
     b = (rng.standard_normal(N) * 0.1).astype(np.float32)
