@@ -66,6 +66,7 @@ struct nb_engine {
     int use_graphs;
     /* one stream: the conformer blocks run as one persistent kernel (NEMO_PERSISTENT=0 disables) */
     int use_enc1, enc1_grid, enc1_optin;
+    int enc1_tail;             /* the prompt and joint encoder projections run as the launch's last stages */
     NbEnc1Layer *enc1_layers;  /* host copy, passed by value at each launch */
     uint8_t *enc1_image;       /* the model's weights laid out per CTA of the persistent grid (owned by the model) */
     float *enc1_fold;          /* and its LayerNorm fold constants (owned by the model) */
@@ -144,6 +145,11 @@ static int enc1_setup(nb_engine_t *e, char *err, size_t errlen) {
         o->din = e->din + (size_t)l * din_s;
     }
     e->enc1_layers = L;
+    /* the encoder's tail (prompt projections, joint encoder projection) as three more stages when
+       its widths fit the stage shapes: K <= 1024 or a multiple of 1024, at most 32 rows per CTA */
+    const int PRH = g->prompt_hidden, JH = g->joint_hidden, NP = g->num_prompts;
+    const int tail = PRH % 128 == 0 && (PRH <= 1024 || PRH % 1024 == 0) && JH % 16 == 0 && (D + NP) % 8 == 0 && (PRH + sms - 1) / sms <= 32 &&
+                     (JH + sms - 1) / sms <= 32 && (PRH <= 1024 || (D + sms / (PRH / 1024) - 1) / (sms / (PRH / 1024)) <= 32);
     /* the weights re-laid out in the order the persistent grid reads them (one bulk copy per CTA
        and projection), built once per model; without room for the copy the blocks run kernel by
        kernel */
@@ -154,7 +160,8 @@ static int enc1_setup(nb_engine_t *e, char *err, size_t errlen) {
         mm->enc1_image = NULL;
         mm->enc1_fold = NULL;
         mm->enc1_grid = 0;
-        const size_t img = nb_encoder1_image_bytes(D, FF, g->n_layers), fb = nb_encoder1_fold_bytes(D, FF, g->n_layers);
+        const size_t img = nb_encoder1_image_bytes(D, FF, g->n_layers) + (tail ? nb_encoder1_tail_image_bytes(D, PRH, JH) : 0),
+                     fb = nb_encoder1_fold_bytes(D, FF, g->n_layers);
         if (cudaMalloc((void **)&mm->enc1_image, img) != cudaSuccess || cudaMalloc((void **)&mm->enc1_fold, fb) != cudaSuccess) {
             cudaGetLastError();
             if (mm->enc1_image) cudaFree(mm->enc1_image);
@@ -166,6 +173,8 @@ static int enc1_setup(nb_engine_t *e, char *err, size_t errlen) {
         memset(q, 0, sizeof *q);
         memcpy(q->L, L, (size_t)g->n_layers * sizeof *L);
         q->layers = g->n_layers; q->D = D; q->FF = FF;
+        q->tail = tail; q->PRH = PRH; q->JH = JH; q->pw0_ld = D + NP;
+        q->pw0 = m->prompt_w0; q->pw2 = m->prompt_w2; q->jw = m->joint_enc_w;
         if (nb_encoder1_repack(q, sms, mm->enc1_image, mm->enc1_fold, e->st) || cudaStreamSynchronize(e->st) != cudaSuccess) {
             snprintf(err, errlen, "persistent encoder set-up: %s", nemo_gpu_last_error());
             return -1;
@@ -178,6 +187,7 @@ static int enc1_setup(nb_engine_t *e, char *err, size_t errlen) {
                    cudaMemset(e->d_enc1_err, 0, sizeof(int)) != cudaSuccess;
     if (rc) { snprintf(err, errlen, "persistent encoder set-up: %s", cudaGetErrorString(cudaGetLastError())); return -1; }
     e->use_enc1 = 1;
+    e->enc1_tail = tail;
     e->enc1_grid = sms;
     e->enc1_optin = optin;
     return 0;
@@ -701,7 +711,12 @@ static int launch_encoder(nb_engine_t *e, int nwin, int c) {
         q->h = h; q->h2 = hn; q->ff = e->ff; q->att = e->att; q->image = e->enc1_image; q->fold = e->enc1_fold;
         q->xout = (uint16_t *)e->xin; q->xout_plane = plD;
         q->bar = e->d_enc1_bar; q->err = e->d_enc1_err;
+        q->tail = e->enc1_tail; q->PRH = PRH; q->JH = JH; q->pw0_ld = D + NP;
+        q->pw0 = m->prompt_w0; q->pw2 = m->prompt_w2; q->jw = m->joint_enc_w;
+        q->pb0 = e->b_eff; q->pb2 = m->prompt_b2; q->jb = m->joint_enc_b;  /* one stream: its prompt bias row */
+        q->ph = e->ph; q->prompted = e->prompted; q->joint = e->joint_enc;
         if (nb_encoder1(q, e->enc1_grid, st)) return -1;
+        if (e->enc1_tail) return 0;  /* prompted and joint_enc came out of the launch */
     }
     for (int l = 0; l < (e->use_enc1 ? 0 : g->n_layers); ++l) {
         const nb_layer_t *W = &m->L[l];

@@ -51,6 +51,14 @@ typedef struct {
     int64_t xout_plane;
     unsigned *bar;              /* [2] grid-barrier arrivals, abort flag (zeroed before each launch) */
     int *err;                   /* nonzero after a bounded wait gave up */
+    /* the encoder's tail as three more stages of the launch (tail = 1; src/encoder.c:189-194):
+       ph = relu(LN_out(h) pw0^T + pb0) [c][PRH], prompted = ph pw2^T + pb2 [c][D] (fp32),
+       joint = prompted jw^T + jb [c][JH]; pw0 rows are pw0_ld bf16 apart (its language columns are
+       folded into pb0). With tail = 0 the launch ends with xout and these are unused. */
+    int tail, PRH, JH, pw0_ld;
+    const uint16_t *pw0, *pw2, *jw;
+    const float *pb0, *pb2, *jb;
+    float *ph, *prompted, *joint;
 } NbEnc1Args;
 
 /* Persistent single-stream greedy decoder (k_decoder1.cu). */
@@ -76,6 +84,7 @@ int nb_encoder1(const NbEnc1Args *args, int grid, void *stream);
 int nb_encoder1_ring_bytes(int D, int FF, int grid, size_t smem_optin, int c, int Lw);
 size_t nb_encoder1_smem(int ring_bytes, int c, int Lw);
 size_t nb_encoder1_image_bytes(int D, int FF, int layers);
+size_t nb_encoder1_tail_image_bytes(int D, int PRH, int JH);
 size_t nb_encoder1_fold_bytes(int D, int FF, int layers);
 int nb_encoder1_repack(const NbEnc1Args *args, int grid, uint8_t *image, float *fold, void *stream);
 

@@ -54,6 +54,8 @@ constexpr int NB = 8;                    // projections in flight in the weight 
 constexpr int MAXL = 72;                 // attention window rows (56 history + 16 new)
 constexpr int MAXR = 32;                 // weight rows of one CTA in one projection
 constexpr int NSTAGE = 8;                // projections per block
+constexpr int NTAIL = 3;                 // projections of the encoder's tail (prompt and joint encoder)
+constexpr int NALL = NSTAGE + NTAIL;     // projection types
 constexpr long long WAIT_LIMIT = 2000000000LL;  // clock cycles (~1 s)
 
 struct Smem {
@@ -70,8 +72,9 @@ struct Smem {
     float vpart[2][128];           // attention value halves
     uint64_t full[NB];
     int ring_off[NB];              // byte offset of projection i's rows in the ring (slot i % NB)
-    int g_lo[NSTAGE], g_hi[NSTAGE], g_kr[NSTAGE], g_krw[NSTAGE], g_rows[NSTAGE], g_pitch[NSTAGE], g_bytes[NSTAGE];
-    long long g_img[NSTAGE];       // byte offset of this CTA's block of projection s in block 0 of the image
+    int g_lo[NALL], g_hi[NALL], g_kr[NALL], g_krw[NALL], g_rows[NALL], g_pitch[NALL], g_bytes[NALL];
+    long long g_img[NALL];         // byte offset of this CTA's block of projection s in block 0 of the image
+                                   // (for the tail: in the tail, which follows the blocks)
     long long g_layer;             // image bytes of one block
     int consumed;                  // projections taken by the compute warps (set when they stop)
     int issued;                    // projections requested so far
@@ -132,7 +135,7 @@ __device__ __forceinline__ void cbar() { sm100::named_barrier(1, CTHREADS); }
 // wider than KRW is split two ways: KT / KRW k-ranges x (grid / ranges) column groups.
 struct Geo {
     const uint16_t *W;
-    int N, K, krw, kr, lo, hi;
+    int N, K, ldw, krw, kr, lo, hi;  // ldw: elements between weight rows
     bool glu;
 };
 
@@ -154,8 +157,13 @@ __device__ __forceinline__ Geo stage_geo(const NbEnc1Args &a, int l, int s, int 
     case 4: g.W = w.pw1; g.N = 2 * D; g.K = D; g.glu = true; break;
     case 5: g.W = w.pw2; g.N = D; g.K = D; break;
     case 6: g.W = w.ff2_w1; g.N = FF; g.K = D; break;
-    default: g.W = w.ff2_w2; g.N = D; g.K = FF; break;
+    case 7: g.W = w.ff2_w2; g.N = D; g.K = FF; break;
+    // the tail (one each per launch): prompt projections and joint encoder projection
+    case 8: g.W = a.pw0; g.N = a.PRH; g.K = D; break;
+    case 9: g.W = a.pw2; g.N = D; g.K = a.PRH; break;
+    default: g.W = a.jw; g.N = a.JH; g.K = D; break;
     }
+    g.ldw = s == 8 ? a.pw0_ld : g.K;
     const int nout = g.glu ? g.N / 2 : g.N;
     if (g.K <= KRW) {
         g.krw = g.K;
@@ -191,9 +199,9 @@ __host__ __device__ inline void stage_shape(int s, int D, int FF, int &nout, int
     mult = m[s];
 }
 // Image bytes per weight row of projection s: the padded row, plus for a projection that follows a
-// folded LayerNorm (FF1a, QKV, PW1, FF2a: s even) its float4 of fold constants, stored after all
-// rows of the CTA's block (one bulk copy brings both).
-__host__ __device__ inline int stage_row_bytes(int s, int krw) { return krw * 2 + 16 + ((s & 1) ? 0 : 16); }
+// folded LayerNorm (FF1a, QKV, PW1, FF2a: s even, below NSTAGE) its float4 of fold constants, stored
+// after all rows of the CTA's block (one bulk copy brings both).
+__host__ __device__ inline int stage_row_bytes(int s, int krw) { return krw * 2 + 16 + ((s & 1) || s >= NSTAGE ? 0 : 16); }
 __host__ __device__ inline long long stage_image_bytes(int s, int D, int FF) {
     int nout, K, mult;
     stage_shape(s, D, FF, nout, K, mult);
@@ -205,9 +213,31 @@ __host__ __device__ inline long long layer_image_bytes(int D, int FF) {
     for (int s = 0; s < NSTAGE; ++s) b += stage_image_bytes(s, D, FF);
     return b;
 }
+// The tail follows the blocks: projection NSTAGE + t, t < NTAIL, all CTAs' rows in turn.
+__host__ __device__ inline void tail_shape(int t, int D, int PRH, int JH, int &nout, int &K) {
+    nout = t == 0 ? PRH : t == 1 ? D : JH;
+    K = t == 1 ? PRH : D;
+}
+__host__ __device__ inline long long tail_stage_bytes(int t, int D, int PRH, int JH) {
+    int nout, K;
+    tail_shape(t, D, PRH, JH, nout, K);
+    const int krw = K <= KRW ? K : KRW;
+    return (long long)stage_row_bytes(NSTAGE + t, krw) * nout * (K / krw);
+}
+__host__ __device__ inline long long tail_image_bytes(int D, int PRH, int JH) {
+    long long b = 0;
+    for (int t = 0; t < NTAIL; ++t) b += tail_stage_bytes(t, D, PRH, JH);
+    return b;
+}
 __device__ __forceinline__ long long image_offset(const NbEnc1Args &a, int l, int s, const Geo &g, int cta, int grid) {
-    long long off = (long long)l * layer_image_bytes(a.D, a.FF);
-    for (int t = 0; t < s; ++t) off += stage_image_bytes(t, a.D, a.FF);
+    long long off = 0;
+    if (s >= NSTAGE) {
+        off = (long long)a.layers * layer_image_bytes(a.D, a.FF);
+        for (int t = 0; t < s - NSTAGE; ++t) off += tail_stage_bytes(t, a.D, a.PRH, a.JH);
+    } else {
+        off = (long long)l * layer_image_bytes(a.D, a.FF);
+        for (int t = 0; t < s; ++t) off += stage_image_bytes(t, a.D, a.FF);
+    }
     const int nout = g.glu ? g.N / 2 : g.N, mult = g.glu ? 2 : 1;
     long long rows_before = (long long)mult * g.lo;
     if (g.K > KRW) rows_before += (long long)g.kr * nout;
@@ -220,8 +250,8 @@ __host__ __device__ inline int fold_off(int s, int D, int FF);
 
 // Set-up: one CTA per (CTA of the persistent grid, projection, block) copies that CTA's rows (and
 // for s even their fold constants, from a.fold, computed before).
-__global__ void encoder1_repack_kernel(const __grid_constant__ NbEnc1Args a, uint8_t *image) {
-    const int cta = blockIdx.x, s = blockIdx.y, l = blockIdx.z;
+__global__ void encoder1_repack_kernel(const __grid_constant__ NbEnc1Args a, uint8_t *image, int s_base) {
+    const int cta = blockIdx.x, s = s_base + blockIdx.y, l = blockIdx.z;
     const Geo g = stage_geo(a, l, s, cta, gridDim.x);
     const int rows = geo_rows(g), pitch = geo_pitch(g), R = g.hi - g.lo, vec = g.krw / 8;  // 16-byte pieces per row
     uint8_t *dst = image + image_offset(a, l, s, g, cta, gridDim.x);
@@ -230,11 +260,11 @@ __global__ void encoder1_repack_kernel(const __grid_constant__ NbEnc1Args a, uin
         uint4 x = make_uint4(0u, 0u, 0u, 0u);
         if (v < vec) {
             const int wrow = j < R ? g.lo + j : g.N / 2 + g.lo + (j - R);
-            x = *(const uint4 *)(g.W + (int64_t)wrow * g.K + (int64_t)g.kr * g.krw + v * 8);
+            x = *(const uint4 *)(g.W + (int64_t)wrow * g.ldw + (int64_t)g.kr * g.krw + v * 8);
         }
         *(uint4 *)(dst + (size_t)j * pitch + v * 16) = x;
     }
-    if (!(s & 1))
+    if (!(s & 1) && s < NSTAGE)
         for (int j = threadIdx.x; j < rows; j += blockDim.x) {
             const int wrow = j < R ? g.lo + j : g.N / 2 + g.lo + (j - R);
             ((float4 *)(dst + (size_t)rows * pitch))[j] = ((const float4 *)a.fold)[(int64_t)l * fold_rows(a.D, a.FF) + fold_off(s, a.D, a.FF) + wrow];
@@ -253,25 +283,26 @@ __global__ void encoder1_repack_kernel(const __grid_constant__ NbEnc1Args a, uin
 // latency-critical accesses.
 struct Ring {
     int o, z, j;     // lane's slot: byte offset, bytes, projection (-1: none)
-    int bytes;       // lane s < NSTAGE: bytes of projection type s
-    long long img;   // and its offset in block 0 of the image
+    int bytes;       // lane s < NALL: bytes of projection type s
+    long long img;   // and its offset in block 0 of the image (the tail's: in the tail)
     int issued, head;
 };
-__device__ __forceinline__ void ring_init(const Smem &S, Ring &q) {
+__device__ __forceinline__ void ring_init(const NbEnc1Args &a, const Smem &S, Ring &q) {
     const int lane = threadIdx.x & 31;
     q.o = q.z = 0;
     q.j = -1;
-    q.bytes = lane < NSTAGE ? S.g_bytes[lane] : 0;
-    q.img = lane < NSTAGE ? S.g_img[lane] : 0;
+    q.bytes = lane < (a.tail ? NALL : NSTAGE) ? S.g_bytes[lane] : 0;
+    q.img = lane < (a.tail ? NALL : NSTAGE) ? S.g_img[lane] : 0;
     q.issued = q.head = 0;
 }
 __device__ void issue_ahead(const NbEnc1Args &a, Smem &S, uint8_t *ring, Ring &q, int consumed, uint64_t pol, int limit) {
     if ((threadIdx.x >> 5) != ISSUE_WARP) return;
     const int lane = threadIdx.x & 31, RB = a.ring_bytes;
     const long long layer_bytes = S.g_layer;
-    limit = min(limit, a.layers * NSTAGE);
+    const int blocks = a.layers * NSTAGE;  // projections of the blocks; the tail's follow
+    limit = min(limit, blocks + (a.tail ? NTAIL : 0));
     while (q.issued < limit && q.issued - consumed < NB) {
-        const int i = q.issued, st = i % NSTAGE, slot = i % NB;
+        const int i = q.issued, st = i < blocks ? i % NSTAGE : NSTAGE + (i - blocks), slot = i % NB;
         const int sz = __shfl_sync(0xffffffffu, q.bytes, st);
         const long long img = __shfl_sync(0xffffffffu, q.img, st);
         const int off = q.head + sz > RB ? 0 : q.head;
@@ -282,7 +313,8 @@ __device__ void issue_ahead(const NbEnc1Args &a, Smem &S, uint8_t *ring, Ring &q
             S.ring_off[slot] = off;
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // the bytes' earlier generic reads before the copies
             sm100::mbar_arrive_expect_tx(&S.full[slot], (uint32_t)sz);
-            if (sz > 0) bulk_g2s_stream(ring + off, a.image + (long long)(i / NSTAGE) * layer_bytes + img, (uint32_t)sz, &S.full[slot], pol);
+            const long long src = (i < blocks ? (long long)(i / NSTAGE) : (long long)a.layers) * layer_bytes + img;
+            if (sz > 0) bulk_g2s_stream(ring + off, a.image + src, (uint32_t)sz, &S.full[slot], pol);
         }
         q.head = off + sz;
         q.issued = i + 1;
@@ -331,7 +363,7 @@ struct Div { int R, m; };
 __device__ __forceinline__ Div make_div(int R) { R = max(R, 1); return { R, (65536 + R - 1) / R }; }
 __device__ __forceinline__ int div_q(const Div &d, int e) { return (e * d.m) >> 16; }
 
-enum { P_PLAIN = 0, P_LN = 1, P_LN2 = 2, P_DWLN = 3 };
+enum { P_PLAIN = 0, P_LN = 1, P_LN2 = 2, P_DWLN = 3, P_LNX = 4 };  // P_LNX: LayerNorm applied in the gather, no SiLU
 
 // The stage's input rows in registers: thread t holds columns 4t .. 4t+3 of every row (t < K/4).
 template <int NR> struct Act { float4 x[NR]; };
@@ -564,11 +596,14 @@ __device__ __forceinline__ void stage_input(const NbEnc1Args &a, int l, int s, c
     case 1: case 7: X = a.ff; ldx = a.FF; mode = P_PLAIN; break;
     case 2: case 4: case 6: X = hB; mode = P_LN; break;
     case 3: X = a.att; mode = P_PLAIN; break;
-    default: X = a.att; mode = P_DWLN; break;  // att holds the depthwise-conv output
+    case 5: X = a.att; mode = P_DWLN; break;  // att holds the depthwise-conv output
+    case 8: X = hA; mode = P_LNX; break;      // LN_out of the last block, then the prompt projection
+    case 9: X = a.ph; ldx = a.PRH; mode = P_PLAIN; break;
+    default: X = a.prompted; mode = P_PLAIN; break;
     }
 }
 __device__ __forceinline__ void stage_norm(const NbEnc1Args &a, int l, int s, float4 &ga, float4 &ba, float4 &gb, float4 &bb) {
-    const NbEnc1Layer &w = a.L[l];
+    const NbEnc1Layer &w = a.L[s >= NSTAGE ? a.layers - 1 : l];
     const float *g1 = nullptr, *b1 = nullptr, *g2 = nullptr, *b2 = nullptr;
     switch (s) {
     case 0:
@@ -579,6 +614,7 @@ __device__ __forceinline__ void stage_norm(const NbEnc1Args &a, int l, int s, fl
     case 4: g1 = w.ln_conv_g; b1 = w.ln_conv_b; break;
     case 5: g1 = w.bn_g; b1 = w.bn_b; break;
     case 6: g1 = w.ln_ff2_g; b1 = w.ln_ff2_b; break;
+    case 8: g1 = w.ln_out_g; b1 = w.ln_out_b; break;  // the last block's output norm, before the prompt
     default: break;
     }
     const int k = 4 * threadIdx.x;
@@ -767,7 +803,7 @@ __device__ void compute(const NbEnc1Args &a, Smem &S, uint8_t *ring, uint8_t *ac
     float *hA = a.h, *hB = a.h2;                // a block runs hA -> hB (FF1b) -> hA (FF2b)
     int gi = 0;                                 // projection index
     Ring rq;                                    // weight ring (warp ISSUE_WARP)
-    ring_init(S, rq);
+    ring_init(a, S, rq);
     const uint64_t pol = evict_first_policy();
     issue_ahead(a, S, ring, rq, 0, pol, 1 << 30);
     float4 nga, nba, ngb, nbb;  // the next stage's normalisation vectors (this thread's columns)
@@ -776,10 +812,14 @@ __device__ void compute(const NbEnc1Args &a, Smem &S, uint8_t *ring, uint8_t *ac
     const int L_att = cache_len + c, pos_rows0 = a.Lmax - L_att, pos_rows = L_att + c - 1;
     prefetch_layer(a, 0, pos, cache_len, pos_rows0, pos_rows);
     prefetch_layer(a, 1, pos, cache_len, pos_rows0, pos_rows);
-    for (int l = 0; l < a.layers && !S.abort; ++l) {
-        const NbEnc1Layer &w = a.L[l];
+    // the blocks, then (tail) one more pass for the prompt and joint encoder projections
+    const int passes = a.layers + (a.tail ? 1 : 0);
+    for (int l = 0; l < passes && !S.abort; ++l) {
+        const bool tl = l == a.layers;
+        const NbEnc1Layer &w = a.L[tl ? a.layers - 1 : l];
+        const int s_end = tl ? NALL : NSTAGE;
 #pragma unroll 1
-        for (int s = 0; s < NSTAGE; ++s, ++gi) {
+        for (int s = tl ? NSTAGE : 0; s < s_end; ++s, ++gi) {
             if (s == 3) {
                 // attention over the cache window (the QKV stage's barrier made the rows visible)
                 const int items = a.H * c;
@@ -838,9 +878,10 @@ __device__ void compute(const NbEnc1Args &a, Smem &S, uint8_t *ring, uint8_t *ac
                 G0 = __ldg(ls);
                 G4 = __ldg(ls + 1).x;
             }
-            // the residual buffer the next FF-out stage accumulates into starts at zero
-            if (s == 0 || s == 6) {
-                float *z = s == 0 ? hB : hA;
+            // the residual buffer the next FF-out stage accumulates into starts at zero (and the
+            // prompt output the tail's second projection accumulates into)
+            if (s == 0 || s == 6 || s == 8) {
+                float *z = s == 0 ? hB : s == 6 ? hA : a.prompted;
                 for (int e = tid; e < (dhi - dlo) * c; e += CTHREADS) z[(int64_t)(e / (dhi - dlo)) * D + dlo + e % (dhi - dlo)] = 0.0f;
             }
             // A compute warp whose projection was requested in an earlier stage waits for its weight
@@ -863,9 +904,10 @@ __device__ void compute(const NbEnc1Args &a, Smem &S, uint8_t *ring, uint8_t *ac
                     float4 &x = A.x[u];
                     x = own ? make_float4(x.x * gp.x, x.y * gp.y, x.z * gp.z, x.w * gp.w) : make_float4(0.f, 0.f, 0.f, 0.f);
                 }
-            } else if (mode == P_DWLN) {
+            } else if (mode == P_DWLN || mode == P_LNX) {
                 float mean[NR], inv[NR];
                 row_stats<NR>(A, S, rbuf, K, a.eps, mean, inv);
+                const bool silu = mode == P_DWLN;
 #pragma unroll
                 for (int u = 0; u < NR; ++u) {
                     float4 &x = A.x[u];
@@ -873,7 +915,7 @@ __device__ void compute(const NbEnc1Args &a, Smem &S, uint8_t *ring, uint8_t *ac
                     x.y = (x.y - mean[u]) * inv[u] * ga.y + ba.y;
                     x.z = (x.z - mean[u]) * inv[u] * ga.z + ba.z;
                     x.w = (x.w - mean[u]) * inv[u] * ga.w + ba.w;
-                    x.x *= sigm(x.x); x.y *= sigm(x.y); x.z *= sigm(x.z); x.w *= sigm(x.w);
+                    if (silu) { x.x *= sigm(x.x); x.y *= sigm(x.y); x.z *= sigm(x.z); x.w *= sigm(x.w); }
                     if (!own) x = make_float4(0.f, 0.f, 0.f, 0.f);
                 }
             }
@@ -977,6 +1019,9 @@ __device__ void compute(const NbEnc1Args &a, Smem &S, uint8_t *ring, uint8_t *ac
                 }
                 case 2: w.kv[(int64_t)(pos + r) * 3 * D + col] = v; break;
                 case 3: case 5: hB[(int64_t)r * D + col] = base[q] + v; break;
+                case 8: a.ph[(int64_t)r * a.PRH + col] = fmaxf(v + __ldg(a.pb0 + col), 0.0f); break;  // relu(x pw0^T + b_eff)
+                case 9: red_add(a.prompted + (int64_t)r * D + col, v + (g.kr == 0 ? __ldg(a.pb2 + col) : 0.0f)); break;
+                case 10: a.joint[(int64_t)r * a.JH + col] = v + __ldg(a.jb + col); break;
                 default: {  // s == 4: GLU (gate row R + n, folded likewise)
                     const float4 F = Fr[R + n];
                     const float gt = S.st[r][5] * (S.st[r][3] * (S.outv[R + n][r] - S.st[r][2] * F.x) + F.y - S.st[r][4] * F.z) + F.w;
@@ -1004,15 +1049,16 @@ __device__ void compute(const NbEnc1Args &a, Smem &S, uint8_t *ring, uint8_t *ac
                     a.att[(int64_t)er * D + g.lo + en] = x;
                 }
             }
-            if (s + 1 < NSTAGE) stage_norm(a, l, s + 1, nga, nba, ngb, nbb);
-            else if (l + 1 < a.layers) stage_norm(a, l + 1, 0, nga, nba, ngb, nbb);
+            if (s + 1 < s_end) stage_norm(a, l, s + 1, nga, nba, ngb, nbb);
+            else if (l + 1 < passes) stage_norm(a, l + 1, l + 1 == a.layers ? NSTAGE : 0, nga, nba, ngb, nbb);
+            if (s + 1 == NALL) break;  // the joint encoder projection ends the launch: nothing reads it here
             if (!grid_sync(a, S, epoch)) break;
         }
     }
     if (tid == 0) S.consumed = gi;
     // output LayerNorm of the last block, as bf16 hi/lo planes for the prompt projection (one CTA:
     // 16 KB of stores after the last barrier)
-    if (!S.abort && blockIdx.x == 0) {
+    if (!S.abort && !a.tail && blockIdx.x == 0) {
         const NbEnc1Layer &w = a.L[a.layers - 1];
         Act<NR> A;
         gather<NR>(A, hA, D, 0, D, c);
@@ -1052,12 +1098,12 @@ __global__ void __launch_bounds__(THREADS, 1) encoder1_kernel(const __grid_const
         sm100::fence_mbar_init();
     }
     // this CTA's part of each projection type (the same in every block)
-    if (threadIdx.x < NSTAGE) {
+    if (threadIdx.x < (a.tail ? NALL : NSTAGE)) {
         const int st = threadIdx.x;
         const Geo g = stage_geo(a, 0, st, blockIdx.x, gridDim.x);
         S.g_lo[st] = g.lo; S.g_hi[st] = g.hi; S.g_kr[st] = g.kr; S.g_krw[st] = g.krw;
         S.g_rows[st] = geo_rows(g); S.g_pitch[st] = geo_pitch(g); S.g_bytes[st] = geo_rows(g) * stage_row_bytes(st, g.krw);
-        S.g_img[st] = image_offset(a, 0, st, g, blockIdx.x, gridDim.x);
+        S.g_img[st] = image_offset(a, 0, st, g, blockIdx.x, gridDim.x) - (st >= NSTAGE ? (long long)a.layers * layer_image_bytes(a.D, a.FF) : 0);
     }
     // activation rows past c stay zero for the whole launch (the MMAs read 8 or 16 rows)
     for (int i = threadIdx.x; i < abytes / 16; i += THREADS) ((uint4 *)act)[i] = make_uint4(0u, 0u, 0u, 0u);
@@ -1096,6 +1142,7 @@ extern "C" int nb_encoder1_ring_bytes(int D, int FF, int grid, size_t smem_optin
 extern "C" size_t nb_encoder1_smem(int ring_bytes, int c, int Lw) { return (size_t)ring_bytes + act_bytes(c, Lw) + sizeof(Smem); }
 
 extern "C" size_t nb_encoder1_image_bytes(int D, int FF, int layers) { return (size_t)layers * (size_t)layer_image_bytes(D, FF); }
+extern "C" size_t nb_encoder1_tail_image_bytes(int D, int PRH, int JH) { return (size_t)tail_image_bytes(D, PRH, JH); }
 
 // Bytes of the LayerNorm fold constants: per block one float4 per row of the folded projections,
 // then two float4 of LN_out sums per block.
@@ -1116,7 +1163,12 @@ extern "C" int nb_encoder1_repack(const NbEnc1Args *args, int grid, uint8_t *ima
     if (nb_check_launch("encoder1_fold_kernel")) return -1;
     encoder1_lnsum_kernel<<<a.layers, 32, 0, st>>>(a, (float4 *)fold + (size_t)a.layers * fold_rows(a.D, a.FF));
     if (nb_check_launch("encoder1_lnsum_kernel")) return -1;
-    encoder1_repack_kernel<<<dim3(grid, NSTAGE, a.layers), 256, 0, st>>>(a, image);
+    encoder1_repack_kernel<<<dim3(grid, NSTAGE, a.layers), 256, 0, st>>>(a, image, 0);
+    if (nb_check_launch("encoder1_repack_kernel")) return -1;
+    if (!a.tail) return 0;
+    if (!a.pw0 || !a.pw2 || !a.jw || a.PRH % 128 || (a.PRH > KRW && a.PRH % KRW) || a.JH % 16 || a.pw0_ld < a.D || a.pw0_ld % 8)
+        return nb_set_error("persistent encoder: unsupported tail (prompt %d, joint %d)", a.PRH, a.JH);
+    encoder1_repack_kernel<<<dim3(grid, NTAIL, 1), 256, 0, st>>>(a, image, NSTAGE);
     return nb_check_launch("encoder1_repack_kernel");
 }
 
@@ -1131,6 +1183,9 @@ extern "C" int nb_encoder1(const NbEnc1Args *args, int grid, void *stream) {
     if (!a.h2 || a.h2 == a.h) return nb_set_error("persistent encoder: needs two residual buffers");
     if (!a.image || !a.fold) return nb_set_error("persistent encoder: no weight image or fold constants");
     if (a.ring_bytes <= 0 || a.ring_bytes % 128) return nb_set_error("persistent encoder: weight ring of %d bytes", a.ring_bytes);
+    if (a.tail && (!a.pw0 || !a.pw2 || !a.jw || !a.pb0 || !a.pb2 || !a.jb || !a.ph || !a.prompted || !a.joint || a.PRH % 128 || (a.PRH > KRW && a.PRH % KRW) ||
+                   a.JH % 16))
+        return nb_set_error("persistent encoder: incomplete tail (prompt %d, joint %d)", a.PRH, a.JH);
     const size_t smem = nb_encoder1_smem(a.ring_bytes, a.c, a.left + a.c);
     // rows <= 8: one MMA column tile and half the registers of the 16-row form
     const bool eight = act_rows(a.c, a.left + a.c) == 8;
