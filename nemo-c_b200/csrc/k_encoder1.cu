@@ -259,12 +259,8 @@ __global__ void encoder1_repack_kernel(const __grid_constant__ NbEnc1Args a, uin
         const int j = e / (vec + 1), v = e % (vec + 1);
         uint4 x = make_uint4(0u, 0u, 0u, 0u);
         if (v < vec) {
-            // within every 16 columns the order the MMA's activation fragments take (see
-            // k_columns): image piece 0 holds column pairs 0, 2, 4, 6 of the 16, piece 1 pairs 1, 3, 5, 7
             const int wrow = j < R ? g.lo + j : g.N / 2 + g.lo + (j - R);
-            const uint4 *grp = (const uint4 *)(g.W + (int64_t)wrow * g.ldw + (int64_t)g.kr * g.krw + (v >> 1) * 16);
-            const uint4 p0 = grp[0], p1 = grp[1];
-            x = (v & 1) ? make_uint4(p0.y, p0.w, p1.y, p1.w) : make_uint4(p0.x, p0.z, p1.x, p1.z);
+            x = *(const uint4 *)(g.W + (int64_t)wrow * g.ldw + (int64_t)g.kr * g.krw + v * 8);
         }
         *(uint4 *)(dst + (size_t)j * pitch + v * 16) = x;
     }
@@ -414,12 +410,7 @@ __device__ __forceinline__ void row_stats(const Act<NR> &A, Smem &S, int &buf, i
     }
 }
 
-// k_columns: the order of the K columns within every 16. The MMA (m16n8k16) gives lane 4r + q of a
-// warp the k-positions 2q, 2q + 1, 2q + 8, 2q + 9 of activation row r; the weight image stores the
-// columns of every 16 in the order 0 1 4 5 8 9 12 13 2 3 6 7 10 11 14 15, so that those four
-// positions are the contiguous input columns 4q .. 4q + 3 (one 16-byte load per lane and row in
-// the 8-row form, which builds its fragments in registers). Sums over k are unchanged.
-// Store the (normalised) rows as bf16 hi / lo planes of the activation tile (16-row form).
+// Store the (normalised) rows as bf16 hi / lo planes of the activation tile.
 template <int NR>
 __device__ __forceinline__ void stage_store(const Act<NR> &A, uint8_t *act, int c, int K) {
     const int t = threadIdx.x;
@@ -436,13 +427,9 @@ __device__ __forceinline__ void stage_store(const Act<NR> &A, uint8_t *act, int 
             const float r2 = v.z - __uint_as_float(h1 << 16), r3 = v.w - __uint_as_float(h1 & 0xffff0000u);
             asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(l0) : "f"(r1), "f"(r0));
             asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(l1) : "f"(r3), "f"(r2));
-            // columns 4t .. 4t + 3 are the pairs at k-positions 2q and 8 + 2q of their 16 (q = t % 4;
-            // see k_columns)
-            uint8_t *hp = act + u * APITCH + (t >> 2) * 32 + (t & 3) * 4;
-            *(uint32_t *)hp = h0;
-            *(uint32_t *)(hp + 16) = h1;
-            *(uint32_t *)(hp + NR * APITCH) = l0;
-            *(uint32_t *)(hp + NR * APITCH + 16) = l1;
+            uint8_t *hp = act + u * APITCH + t * 8;
+            *(uint2 *)hp = make_uint2(h0, h1);
+            *(uint2 *)(hp + NR * APITCH) = make_uint2(l0, l1);
         }
     }
 }
