@@ -101,11 +101,22 @@ class ClockSampler:
             self.p = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "-i", str(self.index), "--format=csv,noheader,nounits", "-lms", "200"],
                                       stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             threading.Thread(target=lambda: [self.lines.append(l.strip()) for l in self.p.stdout], daemon=True).start()
+            # nvidia-smi takes a moment to print its first line: wait for it (bounded) so that the
+            # samples from here on fall into the timed region, which may last only ~0.1 s
+            t0 = time.time()
+            while not self.lines and time.time() - t0 < 3.0 and self.p.poll() is None:
+                time.sleep(0.01)
+            self.n0 = len(self.lines)
         except OSError:
             self.p = None
 
     def stop(self):
         if self.p:
+            # at least one sample taken after the timed region began (bounded wait)
+            t0 = time.time()
+            while len(self.lines) <= getattr(self, "n0", 0) and time.time() - t0 < 1.0 and self.p.poll() is None:
+                time.sleep(0.01)
+            self.lines = self.lines[getattr(self, "n0", 0):] or self.lines
             self.p.terminate()
             try:
                 self.p.wait(timeout=5)
