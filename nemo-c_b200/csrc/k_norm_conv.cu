@@ -644,10 +644,77 @@ __global__ void __launch_bounds__(256) dwconv_ln_silu_row_kernel(const float *__
     store4(Y, y_fmt, y_plane, (int64_t)item * D + ch, o);
 }
 
+// The same for all c <= 8 rows of a stream at once: one block per stream, thread = four channels.
+// The stream's c + 8 input rows are read once (the row kernel reads 9 rows for each output row,
+// ~9x the L2 traffic), the taps once per block; both LayerNorm passes reduce all rows together
+// (two CTA barriers per block instead of two per row).
+constexpr int DW_CM = 8;  // rows per stream at most
+__global__ void __launch_bounds__(256) dwconv_ln_silu_stream_kernel(const float *__restrict__ din, int64_t din_sstride, const int *pos_p,
+                                                                    const float *__restrict__ W, const float *__restrict__ g, const float *__restrict__ b,
+                                                                    void *Y, int y_fmt, int64_t y_plane, int c, float eps) {
+    constexpr int D = 1024, TAPS = 9, R = DW_CM + TAPS - 1;
+    __shared__ float red[2][8][DW_CM];
+    nb::pdl_wait();
+    const int s = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31, ch = 4 * threadIdx.x;
+    const float *x = din + (int64_t)s * din_sstride + (int64_t)(*pos_p - (TAPS - 1)) * D + ch;
+    float4 xv[R], wv[TAPS];
+#pragma unroll
+    for (int r = 0; r < R; ++r) xv[r] = r < c + TAPS - 1 ? *(const float4 *)(x + (int64_t)r * D) : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int q = 0; q < TAPS; ++q) wv[q] = __ldg((const float4 *)(W + ch * TAPS) + q);  // the 4 channels' 36 taps, [ch][9]
+    const float4 gg = __ldg((const float4 *)(g + ch)), bv = __ldg((const float4 *)(b + ch));
+    const float *w = (const float *)wv;
+    float4 acc[DW_CM];
+#pragma unroll
+    for (int t = 0; t < DW_CM; ++t) {
+        acc[t] = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int tap = 0; tap < TAPS; ++tap) {  // output row t reads input rows t .. t + 8
+            acc[t].x += w[tap] * xv[t + tap].x;
+            acc[t].y += w[9 + tap] * xv[t + tap].y;
+            acc[t].z += w[18 + tap] * xv[t + tap].z;
+            acc[t].w += w[27 + tap] * xv[t + tap].w;
+        }
+        const float sum = nb::warp_sum((acc[t].x + acc[t].y) + (acc[t].z + acc[t].w));
+        if (lane == 0) red[0][warp][t] = sum;
+    }
+    __syncthreads();
+    float q[DW_CM];
+#pragma unroll
+    for (int t = 0; t < DW_CM; ++t) {
+        float tot = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) tot += red[0][i][t];
+        const float mean = tot / (float)D;
+        acc[t].x -= mean; acc[t].y -= mean; acc[t].z -= mean; acc[t].w -= mean;
+        q[t] = nb::warp_sum(acc[t].x * acc[t].x + acc[t].y * acc[t].y + acc[t].z * acc[t].z + acc[t].w * acc[t].w);
+        if (lane == 0) red[1][warp][t] = q[t];
+    }
+    __syncthreads();
+#pragma unroll
+    for (int t = 0; t < DW_CM; ++t) {
+        if (t >= c) break;
+        float qt = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) qt += red[1][i][t];
+        const float inv = 1.0f / sqrtf(qt / (float)D + eps);
+        float4 o;
+        o.x = nb::silu_f(acc[t].x * inv * gg.x + bv.x);
+        o.y = nb::silu_f(acc[t].y * inv * gg.y + bv.y);
+        o.z = nb::silu_f(acc[t].z * inv * gg.z + bv.z);
+        o.w = nb::silu_f(acc[t].w * inv * gg.w + bv.w);
+        store4(Y, y_fmt, y_plane, ((int64_t)s * c + t) * D + ch, o);
+    }
+}
+
 extern "C" int nemo_dwconv_ln_silu(const float *din, int64_t din_sstride, const int *pos, const float *W, const float *g, const float *b, void *Y,
                                    int y_fmt, int64_t y_plane, int streams, int c, int D, int taps, float eps, void *stream) {
     if (D > LNT * LN_MAXV) return nb_set_error("nemo_dwconv_ln_silu: D=%d too large", D);
     if (streams <= 0 || c <= 0) return 0;
+    if (D == 1024 && taps == 9 && c <= DW_CM && warp_rows_ok(din, Y, y_fmt, y_plane, D) && din_sstride % 4 == 0 && !((uintptr_t)W & 15)) {
+        nb::launch(dwconv_ln_silu_stream_kernel, streams, 256, 0, (cudaStream_t)stream, din, din_sstride, pos, W, g, b, Y, y_fmt, y_plane, c, eps);
+        return nb_check_launch("dwconv_ln_silu_stream_kernel");
+    }
     if (D == 1024 && taps == 9 && warp_rows_ok(din, Y, y_fmt, y_plane, D) && din_sstride % 4 == 0 && !((uintptr_t)W & 15)) {
         nb::launch(dwconv_ln_silu_row_kernel, streams * c, 256, 0, (cudaStream_t)stream, din, din_sstride, pos, W, g, b, Y, y_fmt, y_plane, c, eps);
         return nb_check_launch("dwconv_ln_silu_row_kernel");

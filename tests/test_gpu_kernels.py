@@ -185,9 +185,10 @@ def test_attention_over_cache(c, cache_len):
         assert rel_err(got[s], ref) < BF16X2_TOL
 
 
-def test_dwconv_ln_silu():
-    rng = np.random.default_rng(4)
-    streams, c, D, cap, pos = 2, 7, 1024, 40, 20
+@pytest.mark.parametrize("c", [1, 7, 8, 14])  # c <= 8: one block per stream; 14: one block per row
+def test_dwconv_ln_silu(c):
+    rng = np.random.default_rng(4 + c)
+    streams, D, cap, pos = 3, 1024, 40, 20
     din = rng.standard_normal((streams, cap, D)).astype(np.float32)
     W = rng.standard_normal((D, 9)).astype(np.float32) * 0.3
     g, b = rng.standard_normal(D).astype(np.float32), rng.standard_normal(D).astype(np.float32)
