@@ -69,6 +69,7 @@ def parse():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-single", action="store_true", help="skip the single-stream (config #1) chunk latency")
     ap.add_argument("--kernel-only", action="store_true", help="time only the dominant GEMM (small device footprint, for ncu captures)")
+    ap.add_argument("--attention-only", action="store_true", help="time only the attention launch at the step's shape (1.6 GB on the device, for ncu captures)")
     ap.add_argument("--session48k", type=float, default=0, metavar="SECONDS",
                     help="BASELINE config #3 only: one stream, 80 ms chunks, SECONDS of 48 kHz audio through the public API, GPU vs host resampler")
     ap.add_argument("--resample-only", type=int, default=0, metavar="RATE",
@@ -200,6 +201,49 @@ def dominant_gemm(nb, torch, a, B, c):
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / 20
     return ms, 2.0 * M * N * K
+
+
+def attention_kernel(nb, torch, peaks, B, c):
+    """CUDA-event time of one nemo_attention_rel launch at the step's shape (B streams, c rows,
+    full cache of att_left rows, the synthetic model's window bound att_left + 16), averaged over
+    40 launches that rotate over 4 K/V caches (1.6 GB: the window rows come from HBM, as in the
+    step), with the HBM bytes it must move: the window's K and V rows of every head plus the
+    query rows and the output."""
+    import ctypes as C
+    H, D, dh = 8, 1024, 128
+    left = nb.synth_default().att_left
+    Lmax, L, cap = left + 16, left + c, 128
+    pos = left + 8
+    kvs = [torch.randn(B, cap, 3 * D, device="cuda") for _ in range(4)]
+    P = torch.randn(2 * Lmax - 1, D, device="cuda")
+    bu, bv = torch.randn(D, device="cuda") * 0.1, torch.randn(D, device="cuda") * 0.1
+    dpos, dcl = torch.tensor([pos], dtype=torch.int32, device="cuda"), torch.tensor([left], dtype=torch.int32, device="cuda")
+    O = torch.empty(B * c, D, device="cuda")
+    st = torch.cuda.current_stream()
+    f = nb.api().nemo_attention_rel
+    f.restype = C.c_int
+
+    def run(kv):
+        b = kv.data_ptr()
+        nb.check(f(C.c_void_p(b), C.c_int64(3 * D), C.c_int64(cap * 3 * D), C.c_void_p(b + 4 * D), C.c_void_p(b + 8 * D), C.c_int64(3 * D),
+                   C.c_int64(cap * 3 * D), C.c_void_p(dpos.data_ptr()), C.c_void_p(dcl.data_ptr()), C.c_void_p(P.data_ptr()), C.c_void_p(bu.data_ptr()),
+                   C.c_void_p(bv.data_ptr()), C.c_void_p(O.data_ptr()), 0, C.c_int64(0), C.c_int64(c * D), B, c, Lmax, H, dh, D,
+                   C.c_float(dh ** -0.5), C.c_void_p(st.cuda_stream)))
+    for i in range(4):
+        run(kvs[i])
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record(st)
+    for i in range(40):
+        run(kvs[i % 4])
+    e1.record(st)
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) / 40 * 1e3
+    nbytes = B * (2 * L * D + 2 * c * D) * 4
+    peak = peaks.get("hbm_gbs", 6650.0)
+    del kvs
+    return {"kernel": "nemo_attention_rel (streams=%d, rows=%d, keys=%d, heads=%d)" % (B, c, L, H), "us_per_launch": us, "hbm_bytes": nbytes,
+            "achieved_gbs": nbytes / (us * 1e-6) / 1e9, "peak_gbs": peak, "frac": nbytes / (us * 1e-6) / 1e9 / peak}
 
 
 def resample_kernel(nb, torch, a, rate):
@@ -599,6 +643,11 @@ def main():
         ms, flops = dominant_gemm(nb, torch, a, a.streams, c)
         print(json.dumps({"kernel": "nemo_gemm FF-in", "M": a.streams * c, "N": 4096, "K": 1024, "us": ms * 1e3, "tflops": flops / ms / 1e9}))
         return
+    if a.attention_only:
+        import torch
+        import nemoasr_b200 as nb
+        print(json.dumps(attention_kernel(nb, torch, peaks, a.streams, a.latency // 80)))
+        return
     if a.session48k:
         import torch  # noqa: F401 (CUDA context as in the other modes)
         import nemoasr_b200 as nb
@@ -699,6 +748,7 @@ def main():
     # ---- dominant kernel roofline ------------------------------------------------------------
     c = a.latency // 80
     ms, flops = dominant_gemm(nb, torch, a, B, c)
+    att = attention_kernel(nb, torch, peaks, B, c) if c <= 16 else None
     single = None if a.no_single or rank != 0 else single_stream(nb, torch, peaks)
     cfg5 = None if a.no_config5 else config5(nb, torch, a, rank, world, dist, barrier)
     peak = peaks.get("bf16_tflops", 1590.0)
@@ -719,7 +769,7 @@ def main():
                 "operands": "bf16 weights x bf16 hi/lo activation planes (16 significant bits), fp32 accumulate and fp32 elsewhere",
                 "data": "synthetic (seeded chirps + noise + pauses; random-init bf16 weights of the published shape)",
                 "config": config_dict(a, world), "e2e": e2e, "gpu_launches": int(launches), "tokens_in_timed_region": toks, "decode": decode,
-                "roofline": roof, "cpu_baseline": cpu, "clocks": clk, "single_stream": single, "config5": cfg5}
+                "roofline": roof, "attention": att, "cpu_baseline": cpu, "clocks": clk, "single_stream": single, "config5": cfg5}
         print(json.dumps(line), flush=True)
     if dist:
         dist.barrier()
