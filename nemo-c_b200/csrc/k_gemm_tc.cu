@@ -355,10 +355,11 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
 
 // ---- activation-major tiles for batches -------------------------------------------------------
 // For many rows the roles swap: 128 activation rows are the MMA's M side (TMEM lanes) and BW
-// weight rows (112, 128, 160, 224 or 256) its N side (TMEM columns). The widths other than 128
-// and 256 (plain tiles only, no k-splits) exist for wave quantisation on 148 SMs: at 1792 rows,
-// N = 4096 makes 266 tiles of 224 (1.8 rounds; 256-row tiles make 224, 1.5 rounds: half the SMs
-// idle through the second), N = 3072 makes 280 tiles of 160 (1.9 rounds) and N = 1024 makes 140
+// weight rows (112, 128, 160, 208, 224 or 256) its N side (TMEM columns). The widths other than
+// 128 and 256 (plain tiles only, no k-splits) exist for wave quantisation on 148 SMs: at 1792
+// rows, N = 4096 makes 280 tiles of 208 (1.9 rounds: 416 weight rows on the busiest SM, against
+// 448 with 266 tiles of 224 and 512 with 224 tiles of 256, 1.5 rounds: half the SMs idle through
+// the second), N = 3072 makes 280 tiles of 160 (1.9 rounds) and N = 1024 makes 140
 // tiles of 112 (one round; 128-row tiles leave 36 SMs idle). Accumulator buffer 1 starts at TMEM
 // column 128 or 256 whatever the width; the epilogue splits a 112-column tile 64 + 48 between its
 // two thread halves, so every 16-column TMEM load starts on a 16-column boundary. One k-step stages 2 x 16 KB of activation
@@ -887,6 +888,8 @@ int init_once() {
     cudaFuncSetAttribute(gemm_tcr_kernel<256, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, CfgR<256>::SMEM);
     cudaFuncSetAttribute(gemm_tcr_kernel<224, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, CfgR<224>::SMEM);
     cudaFuncSetAttribute(gemm_tcr_kernel<224, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, CfgR<224>::SMEM);
+    cudaFuncSetAttribute(gemm_tcr_kernel<208, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, CfgR<208>::SMEM);
+    cudaFuncSetAttribute(gemm_tcr_kernel<208, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, CfgR<208>::SMEM);
     cudaFuncSetAttribute(gemm_tcr_kernel<160, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, CfgR<160>::SMEM);
     cudaFuncSetAttribute(gemm_tcr_kernel<160, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, CfgR<160>::SMEM);
     cudaFuncSetAttribute(gemm_tcr_kernel<112, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, CfgR<112>::SMEM);
@@ -1066,11 +1069,12 @@ int launch_rows(const nemo_gemm_args_t *a, cudaStream_t st, const NbDecEpi *de =
     PlanR best = plan_r(a, 128, false);
     // (224-row tiles without k-splits: with them the 1024 x 4096 FF-out shape measured 38 us per
     // CTA against 31 us with unsplit 128-row tiles)
-    const PlanR cand[6] = { plan_r(a, 256, false), plan_r(a, 128, true), plan_r(a, 256, true), plan_r(a, 224, false), plan_r(a, 160, false), plan_r(a, 112, false) };
+    const PlanR cand[7] = { plan_r(a, 256, false), plan_r(a, 128, true), plan_r(a, 256, true), plan_r(a, 224, false), plan_r(a, 208, false), plan_r(a, 160, false),
+                            plan_r(a, 112, false) };
     const int pol = sched == 1 ? 0 : sched == 2 ? 1 : sk_policy();
     if (pol != 1)
         for (const PlanR &p : cand) {
-            const bool fits = p.bw == 128 || (p.bw == 256 && ok256) || ((p.bw == 224 || p.bw == 160 || p.bw == 112) && !glu);
+            const bool fits = p.bw == 128 || (p.bw == 256 && ok256) || ((p.bw == 224 || p.bw == 208 || p.bw == 160 || p.bw == 112) && !glu);
             if (fits && p.est_us < best.est_us) best = p;
         }
     if (pol != 0) {
@@ -1082,6 +1086,7 @@ int launch_rows(const nemo_gemm_args_t *a, cudaStream_t st, const NbDecEpi *de =
     }
     if (best.bw == 256) return launch_r<256>(a, best, st, de);
     if (best.bw == 224) return launch_r<224>(a, best, st, de);
+    if (best.bw == 208) return launch_r<208>(a, best, st, de);
     if (best.bw == 160) return launch_r<160>(a, best, st, de);
     if (best.bw == 112) return launch_r<112>(a, best, st, de);
     return launch_r<128>(a, best, st, de);

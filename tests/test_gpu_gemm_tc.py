@@ -86,8 +86,8 @@ def test_tcr_gemm_epilogues(M, act):
 @pytest.mark.parametrize("N", [4096, 3072, 1024])
 @pytest.mark.parametrize("act", [0, 1, 2])
 def test_tcr_gemm_odd_width_tiles(N, act):
-    # at 1792 rows the planner takes 224-row weight tiles for N = 4096 (266 tiles: 1.8 rounds of
-    # 148 SMs; the last tile holds 64 real rows), 160-row tiles for N = 3072 (280 tiles) and
+    # at 1792 rows the planner takes 208-row weight tiles for N = 4096 (280 tiles: 1.9 rounds of
+    # 148 SMs; the last tile holds 144 real rows), 160-row tiles for N = 3072 (280 tiles) and
     # 112-row tiles for N = 1024 (140 tiles, epilogue halves of 64 + 48 columns); bias,
     # activation, alpha and accumulation on every chunk
     rng = np.random.default_rng(51 + act + N)
