@@ -160,10 +160,13 @@ def test_layernorms(D, M):
     assert rel_err(host(dY1), r1) < FP32_TOL and rel_err(host(dY2), r2) < FP32_TOL
 
 
-@pytest.mark.parametrize("c,cache_len", [(7, 56), (1, 0), (14, 40), (16, 56), (3, 5)])
-def test_attention_over_cache(c, cache_len):
+# c <= 8: keys as the MMA's 16-row side (attention8_kernel); c > 8: queries as the 16-row side.
+# (8, 64, 72): the window fills Lmax (position rows from 0); (8, 88, 96) and (16, 80, 96): the
+# largest window (96 keys; 103 position rows, so the key warps also form position tiles 4-6)
+@pytest.mark.parametrize("c,cache_len,Lmax", [(7, 56, 72), (1, 0, 72), (14, 40, 72), (16, 56, 72), (3, 5, 72), (8, 64, 72), (8, 88, 96), (16, 80, 96)])
+def test_attention_over_cache(c, cache_len, Lmax):
     rng = np.random.default_rng(c * 100 + cache_len)
-    H, dh, Lmax, streams = 8, 128, 72, 2
+    H, dh, streams = 8, 128, 2
     D = H * dh
     cap, pos = 120, cache_len + 11
     kv = rng.standard_normal((streams, cap, 3 * D)).astype(np.float32)
