@@ -452,47 +452,50 @@ __global__ void __launch_bounds__(WROWS * 32) layernorm_warp_kernel(const float 
     for (int j = 0; j < 8; ++j) if (j < nv) store4(Y, y_fmt, y_plane, (int64_t)row * D + 4 * (lane + 32 * j), v[j]);
 }
 
-// Two-pass LayerNorm of one 1024-wide row held as one float4 per thread of a 256-thread block
-// (thread i owns columns 4i .. 4i + 3); the warps' partial sums meet in shared memory.
-__device__ __forceinline__ float4 ln_block1024(float4 v, float4 gg, float4 bb, float eps, float (&red)[2][8]) {
+// Two-pass LayerNorm of one 1024-wide row over a 128-thread block: thread t holds dims 4t .. 4t + 3
+// (v0) and 512 + 4t .. + 3 (v1); the four warps' partial sums meet in shared memory.
+__device__ __forceinline__ void ln_block1024x2(float4 &v0, float4 &v1, float4 g0, float4 g1, float4 b0, float4 b1, float eps, float (&red)[2][4]) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const float s = nb::warp_sum(v.x + v.y + v.z + v.w);
+    const float s = nb::warp_sum((v0.x + v0.y + v0.z + v0.w) + (v1.x + v1.y + v1.z + v1.w));
     if (lane == 0) red[0][warp] = s;
     __syncthreads();
-    float tot = 0.0f;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) tot += red[0][i];
-    const float mean = tot / 1024.0f;
-    const float a0 = v.x - mean, a1 = v.y - mean, a2 = v.z - mean, a3 = v.w - mean;
-    const float q = nb::warp_sum(a0 * a0 + a1 * a1 + a2 * a2 + a3 * a3);
+    const float mean = (red[0][0] + red[0][1] + red[0][2] + red[0][3]) / 1024.0f;
+    const float a0 = v0.x - mean, a1 = v0.y - mean, a2 = v0.z - mean, a3 = v0.w - mean;
+    const float c0 = v1.x - mean, c1 = v1.y - mean, c2 = v1.z - mean, c3 = v1.w - mean;
+    const float q = nb::warp_sum((a0 * a0 + a1 * a1 + a2 * a2 + a3 * a3) + (c0 * c0 + c1 * c1 + c2 * c2 + c3 * c3));
     if (lane == 0) red[1][warp] = q;
     __syncthreads();
-    float qt = 0.0f;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) qt += red[1][i];
-    const float inv = 1.0f / sqrtf(qt / 1024.0f + eps);
-    return make_float4(a0 * inv * gg.x + bb.x, a1 * inv * gg.y + bb.y, a2 * inv * gg.z + bb.z, a3 * inv * gg.w + bb.w);
+    const float inv = 1.0f / sqrtf((red[1][0] + red[1][1] + red[1][2] + red[1][3]) / 1024.0f + eps);
+    v0 = make_float4(a0 * inv * g0.x + b0.x, a1 * inv * g0.y + b0.y, a2 * inv * g0.z + b0.z, a3 * inv * g0.w + b0.w);
+    v1 = make_float4(c0 * inv * g1.x + b1.x, c1 * inv * g1.y + b1.y, c2 * inv * g1.z + b1.z, c3 * inv * g1.w + b1.w);
 }
 
-// LayerNorm (and the paired second LayerNorm of layernorm2) for D = 1024 with one block per row:
-// 8x the warps of the warp-per-row kernel, one load per thread.
-__global__ void __launch_bounds__(256) layernorm_row_kernel(const float *__restrict__ X, const float *__restrict__ g, const float *__restrict__ b,
-                                                            const float *__restrict__ g2, const float *__restrict__ b2, float *Y1, void *Y, int y_fmt,
-                                                            int64_t y_plane, float eps) {
-    __shared__ float red[2][8];
+// LayerNorm (and the paired second LayerNorm of layernorm2) for D = 1024, one 128-thread block per
+// row: every row of a 1792-row batch resident at once (16 blocks per SM), two barriers per LayerNorm
+// among four warps. (One 256-thread block per row took 1.5 rounds of the SMs and 0.15 ms more per
+// config #4 step over its 96 launches.)
+__global__ void __launch_bounds__(128) layernorm_row128_kernel(const float *__restrict__ X, const float *__restrict__ g, const float *__restrict__ b,
+                                                               const float *__restrict__ g2, const float *__restrict__ b2, float *Y1, void *Y, int y_fmt,
+                                                               int64_t y_plane, float eps) {
+    __shared__ float red[2][4];
     nb::pdl_wait();
-    const int64_t base = (int64_t)blockIdx.x * 1024 + 4 * threadIdx.x;
-    const float4 x = *(const float4 *)(X + base);
-    const float4 gg = __ldg((const float4 *)(g + 4 * threadIdx.x)), bb = __ldg((const float4 *)(b + 4 * threadIdx.x));
-    float4 gg2 = make_float4(0.f, 0.f, 0.f, 0.f), bb2 = gg2;
-    if (g2) { gg2 = __ldg((const float4 *)(g2 + 4 * threadIdx.x)); bb2 = __ldg((const float4 *)(b2 + 4 * threadIdx.x)); }
-    float4 v = ln_block1024(x, gg, bb, eps, red);
+    const int t4 = 4 * threadIdx.x;
+    const int64_t base = (int64_t)blockIdx.x * 1024 + t4;
+    float4 v0 = *(const float4 *)(X + base), v1 = *(const float4 *)(X + base + 512);
+    const float4 ga = __ldg((const float4 *)(g + t4)), gb = __ldg((const float4 *)(g + t4 + 512));
+    const float4 ba = __ldg((const float4 *)(b + t4)), bb = __ldg((const float4 *)(b + t4 + 512));
+    ln_block1024x2(v0, v1, ga, gb, ba, bb, eps, red);
     if (g2) {
-        *(float4 *)(Y1 + base) = v;
-        v = ln_block1024(v, gg2, bb2, eps, red);  // red is free again: every warp read it before the last barrier
+        *(float4 *)(Y1 + base) = v0;
+        *(float4 *)(Y1 + base + 512) = v1;
+        const float4 g2a = __ldg((const float4 *)(g2 + t4)), g2b = __ldg((const float4 *)(g2 + t4 + 512));
+        const float4 b2a = __ldg((const float4 *)(b2 + t4)), b2b = __ldg((const float4 *)(b2 + t4 + 512));
+        ln_block1024x2(v0, v1, g2a, g2b, b2a, b2b, eps, red);  // red is free again: every warp read it before the last barrier
     }
-    store4(Y, y_fmt, y_plane, base, v);
+    store4(Y, y_fmt, y_plane, base, v0);
+    store4(Y, y_fmt, y_plane, base + 512, v1);
 }
+
 
 // Causal depthwise conv + LN + SiLU (src/kernels.metal:361-409), one warp per (stream, row).
 __global__ void __launch_bounds__(WROWS * 32) dwconv_ln_silu_warp_kernel(const float *__restrict__ din, int64_t din_sstride, const int *pos_p,
@@ -565,8 +568,8 @@ extern "C" int nemo_layernorm(const float *X, const float *g, const float *b, vo
     if (D > LNT * LN_MAXV) return nb_set_error("nemo_layernorm: D=%d too large", D);
     if (M <= 0) return 0;
     if (D == 1024 && warp_rows_ok(X, Y, y_fmt, y_plane, D)) {
-        nb::launch(layernorm_row_kernel, M, 256, 0, (cudaStream_t)stream, X, g, b, nullptr, nullptr, nullptr, Y, y_fmt, y_plane, eps);
-        return nb_check_launch("layernorm_row_kernel");
+        nb::launch(layernorm_row128_kernel, M, 128, 0, (cudaStream_t)stream, X, g, b, nullptr, nullptr, nullptr, Y, y_fmt, y_plane, eps);
+        return nb_check_launch("layernorm_row128_kernel");
     }
     if (warp_rows_ok(X, Y, y_fmt, y_plane, D)) {
         nb::launch(layernorm_warp_kernel, (M + WROWS - 1) / WROWS, WROWS * 32, 0, (cudaStream_t)stream, X, g, b, nullptr, nullptr, nullptr, Y, y_fmt, y_plane, M, D,
@@ -582,8 +585,8 @@ extern "C" int nemo_layernorm2(const float *X, const float *g1, const float *b1,
     if (D > LNT * LN_MAXV) return nb_set_error("nemo_layernorm2: D=%d too large", D);
     if (M <= 0) return 0;
     if (D == 1024 && warp_rows_ok(X, Y2, y2_fmt, y2_plane, D) && !((uintptr_t)Y1 & 15)) {
-        nb::launch(layernorm_row_kernel, M, 256, 0, (cudaStream_t)stream, X, g1, b1, g2, b2, Y1, Y2, y2_fmt, y2_plane, eps);
-        return nb_check_launch("layernorm_row_kernel");
+        nb::launch(layernorm_row128_kernel, M, 128, 0, (cudaStream_t)stream, X, g1, b1, g2, b2, Y1, Y2, y2_fmt, y2_plane, eps);
+        return nb_check_launch("layernorm_row128_kernel");
     }
     if (warp_rows_ok(X, Y2, y2_fmt, y2_plane, D) && !((uintptr_t)Y1 & 15)) {
         nb::launch(layernorm_warp_kernel, (M + WROWS - 1) / WROWS, WROWS * 32, 0, (cudaStream_t)stream, X, g1, b1, g2, b2, Y1, Y2, y2_fmt, y2_plane, M, D, eps);
