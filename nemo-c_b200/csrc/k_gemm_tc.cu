@@ -355,8 +355,9 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
 
 // ---- activation-major tiles for batches -------------------------------------------------------
 // For many rows the roles swap: 128 activation rows are the MMA's M side (TMEM lanes) and BW
-// weight rows (112, 128, 160, 208, 224 or 256) its N side (TMEM columns). The widths other than
-// 128 and 256 (plain tiles only, no k-splits) exist for wave quantisation on 148 SMs: at 1792
+// weight rows (80, 112, 128, 160, 208, 224 or 256) its N side (TMEM columns); 80 only for the
+// greedy decoder's GEMMs. The widths other than 128 and 256 (plain tiles only, no k-splits) exist
+// for wave quantisation on 148 SMs: at 1792
 // rows, N = 4096 makes 280 tiles of 208 (1.9 rounds: 416 weight rows on the busiest SM, against
 // 448 with 266 tiles of 224 and 512 with 224 tiles of 256, 1.5 rounds: half the SMs idle through
 // the second), N = 3072 makes 280 tiles of 160 (1.9 rounds) and N = 1024 makes 140
@@ -890,6 +891,8 @@ int init_once() {
     cudaFuncSetAttribute(gemm_tcr_kernel<224, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, CfgR<224>::SMEM);
     cudaFuncSetAttribute(gemm_tcr_kernel<208, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, CfgR<208>::SMEM);
     cudaFuncSetAttribute(gemm_tcr_kernel<208, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, CfgR<208>::SMEM);
+    cudaFuncSetAttribute(gemm_tcr_kernel<80, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, CfgR<80>::SMEM);
+    cudaFuncSetAttribute(gemm_tcr_kernel<80, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, CfgR<80>::SMEM);
     cudaFuncSetAttribute(gemm_tcr_kernel<160, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, CfgR<160>::SMEM);
     cudaFuncSetAttribute(gemm_tcr_kernel<160, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, CfgR<160>::SMEM);
     cudaFuncSetAttribute(gemm_tcr_kernel<112, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, CfgR<112>::SMEM);
@@ -1139,7 +1142,12 @@ extern "C" int nb_gemm_dec(const nemo_gemm_args_t *a, const NbDecEpi *de, void *
     if (de->mode == 2 && (!a->bias || ((uintptr_t)a->bias & 15) || !de->enc || !de->erow || !de->pred || !de->X ||
                           (((uintptr_t)de->enc | (uintptr_t)de->pred | (uintptr_t)de->X) & 15) || de->x_plane % 8))
         return nb_set_error("decoder GEMM: joint epilogue operands misaligned or missing");
-    return launch_rows(a, (cudaStream_t)stream, de);
+    // 80-row weight tiles: each CTA's time is its 128 rows of activation planes (K x 4 bytes per
+    // row, the same for every width) plus its weight rows and an epilogue that grow with the width,
+    // so more, narrower tiles finish sooner (256 streams, greedy decoder per config #4 step:
+    // 4.39 / 3.94 / 3.47 / 3.15 / 3.12 / 2.93 / 2.83 ms with 256- / 208- / 160- / 128- / 112- /
+    // 96- / 80-row tiles; 1024 streams: 8.57 ms with 112, 8.06 with 80)
+    return launch_r<80>(a, plan_r(a, 80, false), (cudaStream_t)stream, de);
 }
 
 extern "C" int nb_attention_device_error(void);
