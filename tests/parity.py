@@ -35,9 +35,15 @@ def tokens_match(got, ref_tokens, dec_token=None, dec_margin=None, blank=None):
     k = next((i for i, (a, b) in enumerate(zip(got, ref_tokens)) if a != b), min(len(got), len(ref_tokens)))
     if dec_token is None:
         return False, f"tokens differ at {k}"
-    # decisions of the oracle between emitted token k-1 and emitted token k (inclusive)
+    # decisions of the oracle between emitted token k-1 and emitted token k (inclusive); when the
+    # token inserted or dropped at k repeats the tokens just before it, the flipped decision may sit
+    # anywhere in that run of equal tokens, so the window starts where the run starts
     emitted = np.nonzero(np.asarray(dec_token) != blank)[0]
-    lo = emitted[k - 1] + 1 if k >= 1 and k - 1 < len(emitted) else 0
+    moved = {t for t in (got[k] if k < len(got) else None, ref_tokens[k] if k < len(ref_tokens) else None) if t is not None}
+    s0 = k
+    while s0 >= 1 and ref_tokens[s0 - 1] in moved:
+        s0 -= 1
+    lo = emitted[s0 - 1] + 1 if s0 >= 1 and s0 - 1 < len(emitted) else 0
     hi = emitted[k] + 1 if k < len(emitted) else len(dec_token)
     window = np.asarray(dec_margin)[lo:hi]
     if window.size and window.min() < MARGIN:

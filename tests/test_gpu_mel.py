@@ -10,8 +10,9 @@ import pytest
 import torch
 
 import nemoasr_b200 as nb
-from parity import REL_TOL, per_chunk_rel
-from test_gpu_stream import run_session
+import oracle as orc
+from parity import REL_TOL, per_chunk_rel, tokens_match
+from test_gpu_stream import run_session, tiny_oracle  # noqa: F401 (fixture)
 
 pytestmark = pytest.mark.gpu
 MEL_TOL = 1e-5
@@ -90,19 +91,34 @@ def _batch(host_mel, B, ckpt, lat):
             os.environ["NEMO_HOST_MEL"] = old
 
 
-def test_batch_gpu_mel_grouped_staging_matches_host_mel(tiny_ckpt):
-    # 64 streams: the spans are staged and uploaded in groups
+def test_batch_gpu_mel_grouped_staging_matches_host_mel(tiny_ckpt, tiny_oracle):
+    # 64 streams: the spans are staged and uploaded in groups. The GPU log-mel agrees with the host
+    # transform to MEL_TOL (not bit for bit), so the two runs' encoder outputs must agree per chunk
+    # within REL_TOL, and their tokens must be identical except in a stream whose decisions meet a
+    # near-tie: where a stream's tokens differ, both runs must match the oracle's under the
+    # near-tie rule.
     B, lat, block = 64, 560, 8960
     audio = np.stack([nb.synth_audio(300 + i, 16000, seconds=3.0, pauses=True) for i in range(B)])
-    out = []
+    out, taps = [], []
     for host in (False, True):
         b = _batch(host, B, tiny_ckpt, lat)
+        b.set_taps(B * 64, 256, 128)
         toks = [[] for _ in range(B)]
         for q in range(0, audio.shape[1], block):
             o = b.feed(audio[:, q:q + block], final=q + block >= audio.shape[1])
             for i in range(B):
                 toks[i] += o[i]
+        taps.append((b.tc[:np.count_nonzero(b.tc)].copy(), b.tp.copy()))
         b.close()
         out.append(toks)
     assert sum(len(t) for t in out[0]) > 0
-    assert out[0] == out[1]
+    rows = taps[0][0]
+    np.testing.assert_array_equal(rows, taps[1][0])
+    n = int(rows.sum()) * B  # taps are [chunk][stream][row]
+    assert max(per_chunk_rel(taps[0][1][:n], taps[1][1][:n], rows * B)) < REL_TOL
+    for i in range(B):
+        if out[0][i] != out[1][i]:
+            o = orc.run_stream(tiny_oracle, audio[i], 16000, lat, block=block)
+            for k in range(2):
+                ok, note = tokens_match(out[k][i], o["tokens"], o["dec_token"], o["dec_margin"], blank=64)
+                assert ok, f"stream {i}, {'host' if k else 'GPU'} log-mel: {note}"
