@@ -85,7 +85,7 @@ struct nb_engine {
     float *dec_b1i;              /* interleaved b1 */
     float *dec_table;            /* [vocab + 1][4PH]: b0 + W0x . embed[v], interleaved */
     float *dec_r0, *dec_r1;      /* [B][4PH]: W0h . h0 and b1 + W1h . h1 of each stream's committed state */
-    float *dec_pv;               /* [B][dec_np]: joint argmax partials (value, column) per 128-column tile half */
+    float *dec_pv;               /* [B][dec_np]: joint argmax partials (value, column) per column tile half */
     int *dec_pi, dec_np;
     unsigned *d_enc1_bar;
     int *d_enc1_err;
@@ -203,7 +203,7 @@ static int dec_fused_setup(nb_engine_t *e, char *err, size_t errlen) {
     const nb_config_t *g = &m->g;
     const size_t PH = (size_t)g->pred_hidden, JH = (size_t)g->joint_hidden, NV = (size_t)g->vocab_size + 1;
     if (g->pred_layers != 2 || PH % 16 || JH % 16 || g->num_classes > (int)NV || g->blank_id < 0 || g->blank_id >= (int)NV) return 0;
-    if (2 * ((g->num_classes + 127) / 128) > 32) return 0;  /* the step kernel reduces the argmax partials within one warp */
+    if (nb_dec_joint_parts(g->num_classes) > 32) return 0;  /* the step kernel reduces the argmax partials within one warp */
     int fail = 0;
     uint16_t *w0i = dalloc(4 * PH * 2 * PH * 2, &fail), *w1i = dalloc(4 * PH * 2 * PH * 2, &fail);
     float *b0i = dalloc(4 * PH * 4, &fail);
@@ -213,7 +213,7 @@ static int dec_fused_setup(nb_engine_t *e, char *err, size_t errlen) {
     e->dec_wg2 = dalloc((JH + 4 * PH) * PH * 2, &fail);
     e->dec_r0 = dalloc((size_t)e->B * 4 * PH * 4, &fail);
     e->dec_r1 = dalloc((size_t)e->B * 4 * PH * 4, &fail);
-    e->dec_np = 2 * ((g->num_classes + 127) / 128);
+    e->dec_np = nb_dec_joint_parts(g->num_classes);
     e->dec_pv = dalloc((size_t)e->B * e->dec_np * 4, &fail);
     e->dec_pi = dalloc((size_t)e->B * e->dec_np * 4, &fail);
     int rc = fail ? -1 : 0;

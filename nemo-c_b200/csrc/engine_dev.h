@@ -158,6 +158,8 @@ typedef struct {
 
 /* Tensor-core GEMM (activation-major tiles) with a decoder epilogue instead of the plain one. */
 int nb_gemm_dec(const nemo_gemm_args_t *a, const NbDecEpi *de, void *stream);
+/* Argmax partials per row of the mode-3 (joint output) GEMM over n columns: two per column tile. */
+int nb_dec_joint_parts(int n);
 
 typedef struct {
     const float *logits;      /* [streams][ldl] */

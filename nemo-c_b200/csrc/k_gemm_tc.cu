@@ -1120,16 +1120,25 @@ int nb_gemm_tc_layout(const nemo_gemm_args_t *a, int layout, void *stream) {
 
 int nb_gemm_tc(const nemo_gemm_args_t *a, void *stream) { return nb_gemm_tc_layout(a, 0, stream); }
 
+// Column-tile width of the joint GEMM with the argmax epilogue: 80 (faster, see below) while its
+// partials (two per tile) fit the step kernel's one-warp reduction, else 128.
+static int dec_joint_bw(int n) { return 2 * ((n + 79) / 80) <= 32 ? 80 : 128; }
+extern "C" int nb_dec_joint_parts(int n) {
+    const int bw = dec_joint_bw(n);
+    return 2 * ((n + bw - 1) / bw);
+}
+
 extern "C" int nb_gemm_dec(const nemo_gemm_args_t *a, const NbDecEpi *de, void *stream) {
     if (init_once()) return -1;
     if (!de || de->mode < 1 || de->mode > 3) return nb_set_error("decoder GEMM: unknown epilogue mode");
     if (de->mode == 3) {
-        // rows are streams (no row list); partials per (column tile of 128, half): 2 * ceil(N / 128) <= part_ld
+        // rows are streams (no row list); partials per (column tile, half): nb_dec_joint_parts(N) <= part_ld
+        const int bw = dec_joint_bw(a->N);
         if (a->a_fmt != NEMO_FMT_BF16X2 || a->act != NEMO_ACT_NONE || a->accumulate || a->K % 8 || !a->bias || !de->part_v || !de->part_i ||
-            de->part_ld < 2 * ((a->N + 127) / 128) || a->dynM)
-            return nb_set_error("decoder GEMM: argmax epilogue needs bf16 hi/lo activations, a bias, partial buffers of %d columns", 2 * ((a->N + 127) / 128));
-        const PlanR pl = plan_r(a, 128, false);
-        return launch_r<128>(a, pl, (cudaStream_t)stream, de);  // 128-column tiles: the partial layout above
+            de->part_ld < nb_dec_joint_parts(a->N) || a->dynM)
+            return nb_set_error("decoder GEMM: argmax epilogue needs bf16 hi/lo activations, a bias, partial buffers of %d columns", nb_dec_joint_parts(a->N));
+        if (bw == 80) return launch_r<80>(a, plan_r(a, 80, false), (cudaStream_t)stream, de);
+        return launch_r<128>(a, plan_r(a, 128, false), (cudaStream_t)stream, de);
     }
     if (a->a_fmt != NEMO_FMT_BF16X2 || a->act != NEMO_ACT_NONE || a->accumulate || a->K % 8 || a->N % 16)
         return nb_set_error("decoder GEMM: needs bf16 hi/lo activations, no activation or accumulation, K %% 8 == 0 and N %% 16 == 0");
