@@ -90,7 +90,9 @@ int nemo_layernorm2(const float *X, const float *g1, const float *b1, const floa
    Per stream s: queries are rows [*pos, *pos + c) of Q + s*q_sstride ([.][ldq]); keys/values
    rows [*pos - *cache_len, *pos + c) of K + s*kv_sstride / V + s*kv_sstride ([.][ldk]), so
    L = *cache_len + c (<= Lmax); pos and cache_len are read from device ints. P: [2*Lmax-1][D] position table. Output
-   O + s*o_sstride ([c][D]) as fp32 or BF16X2 planes (o_plane apart). */
+   O + s*o_sstride ([c][D]) as fp32 or BF16X2 planes (o_plane apart). Limits: head dim 128, c <= 16,
+   Lmax <= 96; Q, K, V, P, bias_u and bias_v 16-byte aligned; ldq, ldk, q_sstride, kv_sstride and D
+   multiples of 4 floats (an error otherwise). */
 int nemo_attention_rel(const float *Q, int64_t ldq, int64_t q_sstride, const float *K, const float *V, int64_t ldk,
                        int64_t kv_sstride, const int *pos, const int *cache_len, const float *P, const float *bias_u,
                        const float *bias_v, void *O, int o_fmt, int64_t o_plane, int64_t o_sstride,
