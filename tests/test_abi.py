@@ -106,3 +106,35 @@ def test_resample_rejects_bad_arguments():
     assert lib.nemo_resample(None, 1 << 20, 0, 1 << 20, 1 << 20, 0, 8, 1000000, 16000, None, 64, 1, None) == -1
     assert b"shared memory" in lib.nemo_gpu_last_error()
     assert lib.nemo_resample(None, 64, 0, 64, 64, 0, 0, 48000, 16000, None, 64, 1, None) == 0  # nothing to do
+
+
+def test_decoder_joint_partials():
+    """Argmax partials per stream of the joint GEMM (two per column tile): 80-column tiles while
+    the partials fit the step kernel's one-warp reduction, else 128-column tiles."""
+    f = nb.api().nb_dec_joint_parts
+    f.argtypes, f.restype = [C.c_int], C.c_int
+    assert f(1025) == 26  # the vocabulary + blank of the published model: 13 tiles of 80
+    assert f(65) == 2
+    assert f(1280) == 32
+    assert f(1281) == 22  # 17 tiles of 80 would be 34 partials: 11 tiles of 128
+    assert f(2048) == 32
+    assert f(2049) == 34  # over 32: the engine then keeps the separate argmax kernel
+
+
+def test_attention_rejects_bad_arguments():
+    """Checked on the host before any launch: head dim, chunk rows, window, 16-byte alignment."""
+    lib = nb.api()
+    f = lib.nemo_attention_rel
+    p, i64 = C.c_void_p, C.c_int64
+    f.argtypes = [p, i64, i64, p, p, i64, i64, p, p, p, p, p, p, C.c_int, i64, i64, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_float, p]
+    f.restype = C.c_int
+    A = 0x10000  # never dereferenced: every case below returns before a launch
+
+    def call(dh=128, c=7, Lmax=72, bias=A, ldk=3072):
+        return f(A, 3072, 3072 * 128, A, A, ldk, 3072 * 128, A, A, A, bias, A, A, 0, 0, c * 1024, 2, c, Lmax, 8, dh, 1024, 0.088, None)
+    assert call(dh=64) == -1 and b"head dim" in lib.nemo_gpu_last_error()
+    assert call(c=17) == -1 and b"too large" in lib.nemo_gpu_last_error()
+    assert call(Lmax=97) == -1 and b"too large" in lib.nemo_gpu_last_error()
+    assert call(bias=A + 8) == -1 and b"16-byte aligned" in lib.nemo_gpu_last_error()
+    assert call(ldk=3070) == -1 and b"16-byte aligned" in lib.nemo_gpu_last_error()
+    assert call(c=0) == 0  # nothing to do
