@@ -414,9 +414,6 @@ __global__ void __launch_bounds__(THREADS, 2) attention8_kernel(const float *__r
     // ldmatrix row addresses of a query (or probability) plane pair: matrix lane / 8 = (hi, cols
     // 0-7), (hi, 8-15), (lo, 0-7), (lo, 8-15) of the k-step, row lane % 8
     const int mi = lane >> 3, mr = lane & 7;
-    // position scores (q + v) . P[prow0 + r], r < NP, of row tile m (rows 16 m .. + 15), the
-    // tile's P rows read from L2 all at once
-    const uint32_t qva = sm100::smem_u32((mi < 2 ? qvh : qvl) + mr * QP8 + 8 * (mi & 1));
     auto issue_v = [&]() {  // warps 4-7: the window's V rows, after their first position tile's loads
         for (int e = tid - 128; e < L * 32; e += 128) {
             const int r = e >> 5, c4 = 4 * (e & 31);
@@ -424,6 +421,9 @@ __global__ void __launch_bounds__(THREADS, 2) attention8_kernel(const float *__r
         }
         asm volatile("cp.async.commit_group;" ::: "memory");
     };
+    // position scores (q + v) . P[prow0 + r], r < NP, of row tile m (rows 16 m .. + 15), the
+    // tile's P rows read from L2 all at once
+    const uint32_t qva = sm100::smem_u32((mi < 2 ? qvh : qvl) + mr * QP8 + 8 * (mi & 1));
     auto pos_tile = [&](int m) {
         const int r0 = 16 * m + g, r1 = r0 + 8;
         const float *p0 = P + (int64_t)(prow0 + (r0 < NP ? r0 : 0)) * D + off + 4 * t;
